@@ -1,0 +1,266 @@
+#!/usr/bin/env python3
+"""Batch-1 greedy decode throughput on B200 (BASELINE.json metric), one JSON line on stdout.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config NAME]
+
+Workload (default): SmolLM2-135M-shaped GQA Llama in q8_0 (the largest
+decode configuration; seeded synthetic N(0, 0.02) weights), KV ctx 256, the 4 seeded benchmark
+prompt ids, greedy until the context is full: 256 forward passes per step, which is one
+l3m_generate call. tok/s counts forward passes, prompt included, as the reference's `l3m bench`.
+
+  value      forward passes / device time of the decode kernel (CUDA events around each launch,
+             inputs resident in HBM), summed over ranks / max over ranks
+  e2e        the same through the public API (l3m_generate: host prompt in, host tokens out via
+             on_token), host wall clock around each call
+  roofline   HBM: algorithmic bytes per launch (weights once per token + KV reads and writes) over
+             the kernel's duration, against MEASURED_PEAKS.json
+  cpu_baseline  the reference itself (oracle/_ref/l3m bench, built from its sources) on this host's cores
+
+The L2 is flushed (a 256 MiB write) between timed steps. --impl reference times the reference's
+own CPU engine on the same model and context instead (rank 0 only).
+"""
+import argparse
+import ctypes as C
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+from l3m_b200 import synth  # noqa: E402
+
+REF_CLI = ROOT / "oracle" / "_ref" / "l3m"
+PUBLISHED = {"SmolLM2-135M-q8_0": 530.0, "stories15M-bf16": 15300.0, "stories42M-q8_0": 10700.0, "stories110M-q4_0": 5800.0}
+MODEL_DIR = Path(os.environ.get("L3M_BENCH_DIR", "/tmp/l3m_bench"))
+
+
+def rank_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+class Clocks:
+    """nvidia-smi sampled every 200 ms while the timed region runs."""
+    Q = "clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown," \
+        "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, gpu):
+        self.gpu, self.rows, self.proc = gpu, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=lambda: self.rows.extend(self.proc.stdout), daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            self.proc.wait()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            f = [v.strip() for v in r.split(",")]
+            if len(f) < 6 or not f[0].replace(".", "").isdigit():
+                continue
+            sm.append(float(f[0]))
+            mx = max(mx, float(f[1]))
+            reasons |= {n for n, v in zip(names, f[2:6]) if v.lower() == "active"}
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+class L2Flush:
+    """A 256 MiB device buffer written between steps (larger than the 126 MB L2)."""
+
+    def __init__(self):
+        self.rt = C.CDLL("/usr/local/cuda/lib64/libcudart.so.12")
+        self.rt.cudaMalloc.argtypes = [C.POINTER(C.c_void_p), C.c_size_t]
+        self.rt.cudaMemset.argtypes = [C.c_void_p, C.c_int, C.c_size_t]
+        self.p, self.n = C.c_void_p(), 256 << 20
+        assert self.rt.cudaMalloc(C.byref(self.p), self.n) == 0
+
+    def __call__(self, v=0):
+        self.rt.cudaMemset(self.p, v & 0xFF, self.n)
+        self.rt.cudaDeviceSynchronize()
+
+
+def algorithmic_bytes(name, ctx, n_prompt):
+    """Weights once per forward pass plus KV traffic: 2*L*(pos+1)*kv*2 bytes read and 2*L*kv*2 written per position."""
+    shape = synth.CONFIGS[name][0]
+    L, kvd = shape["n_layers"], shape["dim"] // shape["n_heads"] * shape["n_kv_heads"]
+    w = synth.weight_bytes(name)
+    positions = ctx
+    kv = sum(2 * L * (p + 1) * kvd * 2 + 2 * L * kvd * 2 for p in range(positions))
+    return positions * w + kv, positions
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], "measured"
+    return 6650.0, "fallback"
+
+
+def reference_cpu(path, ctx, n_tokens):
+    """The reference's own CLI bench on this host (all its default cores), median of 3."""
+    if not REF_CLI.exists():
+        return None
+    vals, desc = [], ""
+    for _ in range(3):
+        out = subprocess.run([str(REF_CLI), "bench", str(path), "--ctx", str(ctx), "-n", str(n_tokens), "--force", "--md"],
+                             capture_output=True, text=True, timeout=900)
+        if out.returncode:
+            return {"unavailable": out.stderr.strip()[:200]}
+        row = out.stdout.splitlines()[2].split("|")
+        desc = row[1].strip()
+        vals.append(float(row[2]))
+    m = re.search(r"on (\d+) cores? \((\w+)\)", desc)
+    return {"value": statistics.median(vals), "unit": "tok/s", "cores": int(m.group(1)) if m else None,
+            "kind": "reference", "table": m.group(2) if m else None,
+            "sample": f"reference `l3m bench --ctx {ctx} -n {n_tokens} --force`, median of 3 (16 warm-up tokens each)"}
+
+
+def bench_ours(a):
+    rank, world, local = rank_env()
+    import l3m_b200
+    name = a.config
+    _, dtype, _, ctx = synth.CONFIGS[name]
+    path = synth.make(name, MODEL_DIR)
+    prompt = synth.prompt(4, seed=1, vocab=32000)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("gloo", timeout=__import__("datetime").timedelta(seconds=600))
+    m = l3m_b200.Model(path, cpus=[local], ctx=ctx, force=True)
+    flush = L2Flush()
+    sink = []
+    for _ in range(a.warmup):
+        m.generate(prompt, 256, temperature=0, on_token=sink.append)
+    m.perf()
+    if dist:
+        dist.barrier()
+    dev_ns, wall_ns, positions = [], [], 0
+    with Clocks(local) as clk:
+        for _ in range(a.steps):
+            flush()
+            t0 = time.perf_counter_ns()
+            toks = m.generate(prompt, 256, temperature=0, on_token=sink.append)
+            wall_ns.append(time.perf_counter_ns() - t0)
+            p = m.perf()
+            dev_ns.append(p["ns_compute"] * p["tokens"])
+            positions += int(p["tokens"])
+    n_gen = len(toks)
+    t_dev, t_wall = sum(dev_ns), sum(wall_ns)
+    if dist:
+        import torch
+        t = torch.tensor([t_dev, t_wall, positions], dtype=torch.float64)
+        tmax = t.clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        tsum = t.clone()
+        dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
+        t_dev, t_wall, total = tmax[0].item(), tmax[1].item(), tsum[2].item()
+        dist.barrier()
+        dist.destroy_process_group()
+    else:
+        total = positions
+    if rank:
+        return
+    value = total / (t_dev * 1e-9)
+    e2e = total / (t_wall * 1e-9)
+    alg, per_launch_pos = algorithmic_bytes(name, ctx, len(prompt))
+    launch_s = (t_dev / a.steps) * 1e-9
+    peak, peak_kind = measured_peaks()
+    achieved = alg / launch_s / 1e9
+    traffic = None
+    prof = ROOT / "profiles" / "decode_kernel_traffic.json"
+    if prof.exists():
+        traffic = json.loads(prof.read_text()).get(name)
+    out = {
+        "metric": "batch-1 decode tok/s", "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": round(t_dev / a.steps * 1e-6, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": round(value / PUBLISHED[name], 3) if name in PUBLISHED else None,
+        "dtype": {"q8_0": "int8 dot / fp32", "q4_0": "int4 dot / fp32", "mxfp4": "e2m1 dot / fp32", "bf16": "bf16 x bf16 / fp32"}[dtype],
+        "data": "synthetic (seeded N(0,0.02) weights, 4 seeded prompt ids)",
+        "config": {"workload": f"{name} batch-1 greedy decode, ctx {ctx}, {per_launch_pos} forward passes per step "
+                               f"({len(prompt)}-token prompt, {n_gen} generated)", "ctx": ctx, "l2_flush_between_steps": True,
+                   "parallelism": f"replica x{world}" if world > 1 else "1 GPU", "table": "sm100a (bit-exact with the reference's scalar path)"},
+        "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * len(prompt), "d2h_bytes_per_step": 4 * n_gen,
+                "timing": "host wall clock around l3m_generate"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "traffic": traffic, "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_launch": alg},
+        "gpu_launches": a.steps,
+        "clocks": clk.summary(),
+    }
+    if not a.no_cpu:
+        out["cpu_baseline"] = reference_cpu(path, ctx, 256)
+    print(json.dumps(out), flush=True)
+
+
+def bench_reference(a):
+    rank, world, _ = rank_env()
+    if rank:
+        return
+    name = a.config
+    _, dtype, _, ctx = synth.CONFIGS[name]
+    path = synth.make(name, MODEL_DIR)
+    if not REF_CLI.exists():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/l3m was not built (needs the reference sources)"}))
+        return
+    vals = []
+    desc = ""
+    for i in range(a.warmup + a.steps):
+        out = subprocess.run([str(REF_CLI), "bench", str(path), "--ctx", str(ctx), "-n", "256", "--force", "--md"],
+                             capture_output=True, text=True, timeout=900)
+        if out.returncode:
+            print(json.dumps({"impl": "reference", "unavailable": out.stderr.strip()[:200]}))
+            return
+        row = out.stdout.splitlines()[2].split("|")
+        desc = row[1].strip()
+        if i >= a.warmup:
+            vals.append(float(row[2]))
+    m = re.search(r"on (\d+) cores? \((\w+)\)", desc)
+    value = statistics.median(vals)
+    print(json.dumps({
+        "impl": "reference", "metric": "batch-1 decode tok/s", "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": round(value / PUBLISHED[name], 3) if name in PUBLISHED else None, "dtype": dtype, "data": "synthetic",
+        "config": {"workload": f"{name} batch-1 greedy decode, ctx {ctx}", "ctx": ctx},
+        "cpu_baseline": {"value": round(value, 1), "unit": "tok/s", "cores": int(m.group(1)) if m else None, "kind": "reference",
+                         "sample": f"reference `l3m bench --ctx {ctx} -n 256 --force` ({m.group(2) if m else '?'} table), median over steps"},
+        "e2e": {"value": round(value, 1), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default="SmolLM2-135M-q8_0", choices=list(synth.CONFIGS))
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    a = ap.parse_args()
+    if a.warmup < 3:
+        ap.error("--warmup must be at least 3")
+    (bench_reference if a.impl == "reference" else bench_ours)(a)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,630 @@
+// The B200 decode engine behind include/l3m.h. Replaces the reference's sharded CPU engine
+// (src/engine.c:1-603) with a device-resident one:
+//   load      validate the file, pack every matrix into 16-output tiles in one device arena (the
+//             streamed weights first, so one persisting-L2 window covers them), give each CTA its
+//             share of every phase, refuse when the weights exceed the L2 persisting budget unless
+//             forced (the reference's cache-budget refusal, src/engine.c:496-525);
+//   generate  one cooperative launch of the persistent decode kernel per call; tokens stream back
+//             through host-mapped memory to on_token on the caller's thread, and a stop request
+//             streams in the other way.
+#include <cuda_runtime.h>
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <ctime>
+#include <string>
+#include <vector>
+#include <x86intrin.h>
+#include "file.h"
+#include "numerics.h"
+#include "ops.cuh"
+#include "decode.cuh"
+#include "../../include/l3m.h"
+#include "../../include/l3m_kernels.h"
+
+extern "C" int l3m_decode_launch(const l3m::DecodeArgs *a, void *stream);
+extern "C" int l3m_decode_occupancy(int smem_bytes);
+extern "C" int l3m_expf_tables(const uint32_t **list, const uint32_t **index);
+
+namespace {
+
+constexpr int kMaxGpus = 8;
+constexpr int kDefaultCtx = 512;
+constexpr double MiB = 1024.0 * 1024.0;
+
+double now_ns() {
+    timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return ts.tv_sec * 1e9 + ts.tv_nsec;
+}
+
+int tiles_of(int n) { return (n + L3M_TILE - 1) / L3M_TILE; }
+
+struct Gpu {
+    int dev = -1, sms = 0;
+    cudaStream_t stream = nullptr, side = nullptr;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    uint8_t *arena = nullptr;
+    size_t arena_bytes = 0, weight_bytes = 0;
+    uint16_t *kv = nullptr;
+    size_t kv_bytes = 0;
+    float2 *rope = nullptr;
+    l3m::LayerDev *layers = nullptr;
+    l3m::Role *roles = nullptr;
+    uint64_t *ex = nullptr;
+    size_t ex_bytes = 0;
+    int32_t *prompt = nullptr;
+    float *logits = nullptr;
+    int *abort_flag = nullptr;
+    l3m::DecodeArgs args{};
+    size_t l2_bytes = 0, persist_max = 0, window_max = 0, prev_limit = 0;
+    bool limit_set = false;
+    std::string name;
+};
+
+}  // namespace
+
+struct l3m_model {
+    l3m_file f;
+    int n_gpus = 0;
+    Gpu g[kMaxGpus];
+    int dim = 0, hd = 0, ffn = 0, vocab = 0, ctx = 0, n_heads = 0, n_kv = 0, hpk = 0, n_layers = 0;
+    unsigned flags = 0;
+    int reference = 0, cold = 0;
+    l3m::Ctrl *ctrl = nullptr;
+    int32_t *tokens = nullptr;
+    l3m::Ctrl *ctrl_dev = nullptr;
+    int32_t *tokens_dev = nullptr;
+    std::vector<float> host_logits;
+    int logits_pos = -1, cached_pos = -2;
+    double tok_count = 0, ns = 0, dev_ns = 0;
+    size_t weight_bytes = 0;
+    const l3m_kernels *kk = nullptr;
+    char desc[256] = {0};
+};
+
+namespace {
+
+l3m_model *fail(l3m_model *m, const char *msg) {
+    fprintf(stderr, "l3m: %s\n", msg);
+    l3m_free(m);
+    return nullptr;
+}
+
+bool cuda_ok(cudaError_t e, const char *what) {
+    if (e == cudaSuccess) return true;
+    fprintf(stderr, "l3m: %s: %s\n", what, cudaGetErrorString(e));
+    return false;
+}
+
+// Host staging of one GPU's arena; every part starts 256-byte aligned.
+struct Stage {
+    std::vector<uint8_t> buf;
+    size_t put(const void *src, size_t n) {
+        size_t off = (buf.size() + 255) & ~(size_t)255;
+        buf.resize(off + n);
+        if (src) memcpy(buf.data() + off, src, n);
+        return off;
+    }
+    size_t reserve(size_t n) { return put(nullptr, n); }
+};
+
+const void *row_ptr(const l3m_file *f, const l3m_tensor *t, int r) {
+    return (const uint8_t *)l3m_file_data(f, t) + (size_t)r * l3m_row_bytes((int)t->dtype, (int)t->shape[1]);
+}
+
+// Rows of one matrix to pack, as file rows (dtype of the tensor) or, on the reference path,
+// dequantised f32 copies (the fp32 reference dequantises every matrix, src/ref.c:24-32).
+struct Rows {
+    int dtype = 0, k = 0;
+    std::vector<const void *> ptr;
+    std::vector<std::vector<float>> f32;
+    void add(const l3m_file *f, const l3m_tensor *t, int r, bool to_f32) {
+        k = (int)t->shape[1];
+        if (!to_f32) {
+            dtype = (int)t->dtype;
+            ptr.push_back(row_ptr(f, t, r));
+            return;
+        }
+        dtype = L3M_F32;
+        f32.emplace_back(k);
+        l3m_dequant_row(f32.back().data(), (int)t->dtype, row_ptr(f, t, r), k);
+    }
+    void finish() {
+        if (!f32.empty()) for (auto &v : f32) ptr.push_back(v.data());
+    }
+};
+
+size_t pack(Stage &s, Rows &rows) {
+    rows.finish();
+    const int n = (int)rows.ptr.size(), nt = tiles_of(n);
+    const size_t tb = l3m_tile_bytes(rows.dtype, rows.k);
+    size_t off = s.reserve((size_t)nt * tb);
+    for (int t = 0; t < nt; t++) {
+        const void *tr[L3M_TILE];
+        for (int j = 0; j < L3M_TILE; j++) tr[j] = t * L3M_TILE + j < n ? rows.ptr[t * L3M_TILE + j] : nullptr;
+        l3m_pack_tile(s.buf.data() + off + (size_t)t * tb, rows.dtype, tr, rows.k);
+    }
+    return off;
+}
+
+size_t pack_matrix(Stage &s, const l3m_file *f, const l3m_tensor *t, bool to_f32, int *dtype) {
+    Rows r;
+    for (int i = 0; i < (int)t->shape[0]; i++) r.add(f, t, i, to_f32);
+    *dtype = r.dtype;
+    return pack(s, r);
+}
+
+// RoPE coefficients with the reference's exact expressions and this host's libm (src/ops.c:29-33).
+std::vector<float2> rope_table(int ctx, int hd, float theta) {
+    std::vector<float2> t((size_t)ctx * (hd / 2));
+    for (int pos = 0; pos < ctx; pos++)
+        for (int i = 0; i < hd / 2; i++) {
+            volatile float e = -2.0f * (float)i / (float)hd;
+            float angle = (float)pos * powf(theta, e);
+            t[(size_t)pos * (hd / 2) + i] = make_float2(cosf(angle), sinf(angle));
+        }
+    return t;
+}
+
+void split(int n, int parts, int r, int *lo, int *hi) {   // reference src/engine.c:88-91
+    *lo = (int)((long)n * r / parts);
+    *hi = (int)((long)n * (r + 1) / parts);
+}
+
+int align16(int x) { return (x + 15) & ~15; }
+
+// Build everything one GPU holds and fill its decode arguments.
+bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
+    const l3m_file *f = &m->f;
+    const bool ref = m->reference;
+    if (!cuda_ok(cudaSetDevice(g.dev), "cudaSetDevice")) return false;
+    cudaDeviceProp prop;
+    if (!cuda_ok(cudaGetDeviceProperties(&prop, g.dev), "cudaGetDeviceProperties")) return false;
+    g.name = prop.name;
+    g.sms = prop.multiProcessorCount;
+    g.l2_bytes = (size_t)prop.l2CacheSize;
+    g.persist_max = (size_t)prop.persistingL2CacheMaxSize;
+    g.window_max = (size_t)prop.accessPolicyMaxWindowSize;
+    if (prop.major != 10) {
+        char msg[160];
+        snprintf(msg, sizeof msg, "GPU %d (%s) is compute capability %d.%d; this build runs on B200 (sm_100a)", g.dev, prop.name, prop.major, prop.minor);
+        fprintf(stderr, "l3m: %s\n", msg);
+        return false;
+    }
+    const int G = g.sms, dim = m->dim, hd = m->hd, ffn = m->ffn, V = m->vocab, L = m->n_layers;
+    if (m->n_heads > G) { fprintf(stderr, "l3m: %d heads exceed the %d SMs of GPU %d\n", m->n_heads, G, g.dev); return false; }
+
+    // Streamed weights first (one contiguous range for the persisting window), then the rest.
+    Stage s;
+    std::vector<l3m::LayerDev> layers(L);
+    std::vector<size_t> off_qkv(L), off_wo(L), off_gate(L), off_up(L), off_down(L);
+    const int unit_rows = 3 * hd, unit_tiles = tiles_of(unit_rows);
+    for (int l = 0; l < L; l++) {
+        const l3m_tensor *wq = l3m_file_blk(f, l, "wq"), *wk = l3m_file_blk(f, l, "wk"), *wv = l3m_file_blk(f, l, "wv");
+        for (int h = 0; h < m->n_heads; h++) {                                      // one unit per query head
+            Rows r;
+            const int kvh = h / m->hpk;
+            for (int i = 0; i < hd; i++) r.add(f, wq, h * hd + i, ref);
+            for (int i = 0; i < hd; i++) r.add(f, wk, kvh * hd + i, ref);
+            for (int i = 0; i < hd; i++) r.add(f, wv, kvh * hd + i, ref);
+            size_t off = pack(s, r);
+            if (h == 0) { off_qkv[l] = off; layers[l].dt_qkv = r.dtype; }
+        }
+        off_wo[l] = pack_matrix(s, f, l3m_file_blk(f, l, "wo"), ref, &layers[l].dt_wo);
+        off_up[l] = pack_matrix(s, f, l3m_file_blk(f, l, "w_up"), ref, &layers[l].dt_up);
+        off_gate[l] = pack_matrix(s, f, l3m_file_blk(f, l, "w_gate"), ref, &layers[l].dt_gate);
+        off_down[l] = pack_matrix(s, f, l3m_file_blk(f, l, "w_down"), ref, &layers[l].dt_down);
+    }
+    const l3m_tensor *head = l3m_file_tensor(f, (m->flags & L3M_F_TIED) ? "embed" : "lm_head");
+    int dt_head = 0;
+    size_t off_head = pack_matrix(s, f, head, ref, &dt_head);
+    g.weight_bytes = s.buf.size();
+    // Per-head units repeat the kv rows of a GQA group: the streamed bytes include that.
+    const l3m_tensor *emb = l3m_file_tensor(f, "embed");
+    int dt_embed = (int)emb->dtype;
+    size_t emb_row = l3m_row_bytes(dt_embed, dim), off_embed;
+    if (ref && dt_embed != L3M_F32) {
+        std::vector<float> rowf((size_t)dim);
+        off_embed = s.reserve((size_t)V * dim * 4);
+        for (int r = 0; r < V; r++) {
+            l3m_dequant_row(rowf.data(), dt_embed, row_ptr(f, emb, r), dim);
+            memcpy(s.buf.data() + off_embed + (size_t)r * dim * 4, rowf.data(), (size_t)dim * 4);
+        }
+        dt_embed = L3M_F32;
+        emb_row = (size_t)dim * 4;
+    } else {
+        off_embed = s.put(l3m_file_data(f, emb), (size_t)V * emb_row);
+    }
+    auto put_vec = [&](const l3m_tensor *t) -> long long {
+        return t ? (long long)s.put(l3m_file_data(f, t), (size_t)t->nbytes) : -1;
+    };
+    struct VecOffs { long long an, fn, bq, bk, bv, bo, bu, bd; };
+    std::vector<VecOffs> vo(L);
+    for (int l = 0; l < L; l++) {
+        vo[l] = {put_vec(l3m_file_blk(f, l, "attn_norm")), put_vec(l3m_file_blk(f, l, "ffn_norm")), put_vec(l3m_file_blk(f, l, "bq")),
+                 put_vec(l3m_file_blk(f, l, "bk")), put_vec(l3m_file_blk(f, l, "bv")), put_vec(l3m_file_blk(f, l, "bo")),
+                 put_vec(l3m_file_blk(f, l, "b_up")), put_vec(l3m_file_blk(f, l, "b_down"))};
+    }
+    long long off_norm = put_vec(l3m_file_tensor(f, "norm"));
+    g.arena_bytes = s.buf.size();
+
+    if (!cuda_ok(cudaMalloc(&g.arena, g.arena_bytes), "weights")) return false;
+    if (!cuda_ok(cudaMemcpy(g.arena, s.buf.data(), g.arena_bytes, cudaMemcpyHostToDevice), "weights upload")) return false;
+    std::vector<uint8_t>().swap(s.buf);
+
+    g.kv_bytes = (size_t)L * 2 * m->n_kv * m->ctx * hd * 2;
+    if (!cuda_ok(cudaMalloc(&g.kv, g.kv_bytes), "KV cache")) return false;
+    cudaMemset(g.kv, 0, g.kv_bytes);
+    auto A = [&](long long off) -> const float * { return off < 0 ? nullptr : (const float *)(g.arena + off); };
+    for (int l = 0; l < L; l++) {
+        l3m::LayerDev &d = layers[l];
+        d.qkv = g.arena + off_qkv[l];
+        d.wo = g.arena + off_wo[l];
+        d.up = g.arena + off_up[l];
+        d.gate = g.arena + off_gate[l];
+        d.down = g.arena + off_down[l];
+        d.attn_norm = A(vo[l].an); d.ffn_norm = A(vo[l].fn);
+        d.bq = A(vo[l].bq); d.bk = A(vo[l].bk); d.bv = A(vo[l].bv); d.bo = A(vo[l].bo); d.b_up = A(vo[l].bu); d.b_down = A(vo[l].bd);
+        const size_t per = (size_t)m->n_kv * m->ctx * hd;
+        d.kc = g.kv + (size_t)l * 2 * per;
+        d.vc = d.kc + per;
+    }
+    if (!cuda_ok(cudaMalloc(&g.layers, sizeof(l3m::LayerDev) * L), "layers")) return false;
+    cudaMemcpy(g.layers, layers.data(), sizeof(l3m::LayerDev) * L, cudaMemcpyHostToDevice);
+
+    auto rope = rope_table(m->ctx, hd, m->f.h->rope_theta);
+    if (!cuda_ok(cudaMalloc(&g.rope, rope.size() * sizeof(float2)), "rope")) return false;
+    cudaMemcpy(g.rope, rope.data(), rope.size() * sizeof(float2), cudaMemcpyHostToDevice);
+
+    // Each CTA's share of every phase: contiguous tile ranges, the reference's split (engine.c:471-476).
+    const int Td = tiles_of(dim), Tf = tiles_of(ffn), Tv = tiles_of(V);
+    std::vector<l3m::Role> roles(G);
+    int max_ffn_tiles = 0;
+    for (int c = 0; c < G; c++) {
+        l3m::Role &r = roles[c];
+        r.head = -1;
+        r.kv_writer = 0;
+        split(Td, G, c, &r.wo0, &r.wo1);
+        split(Tf, G, c, &r.ffn0, &r.ffn1);
+        split(Td, G, c, &r.dn0, &r.dn1);
+        split(Tv, G, c, &r.voc0, &r.voc1);
+        max_ffn_tiles = std::max(max_ffn_tiles, r.ffn1 - r.ffn0);
+    }
+    for (int h = 0; h < m->n_heads; h++) {
+        l3m::Role &r = roles[(long)h * G / m->n_heads];
+        r.head = h;
+        r.kv_writer = h % m->hpk == 0;
+    }
+    if (!cuda_ok(cudaMalloc(&g.roles, sizeof(l3m::Role) * G), "roles")) return false;
+    cudaMemcpy(g.roles, roles.data(), sizeof(l3m::Role) * G, cudaMemcpyHostToDevice);
+
+    l3m::DecodeArgs &a = g.args;
+    a.dim = dim; a.hd = hd; a.ffn = ffn; a.vocab = V; a.ctx = m->ctx; a.n_heads = m->n_heads; a.n_kv = m->n_kv; a.hpk = m->hpk;
+    a.n_layers = L; a.unit_tiles = unit_tiles; a.grid = G; a.eps = m->f.h->norm_eps;
+    a.layers = g.layers;
+    a.head = g.arena + off_head; a.dt_head = dt_head;
+    a.embed = g.arena + off_embed; a.dt_embed = dt_embed; a.embed_row_bytes = (long long)emb_row;
+    a.norm = A(off_norm);
+    a.rope = (m->flags & L3M_F_LEARNED_POS) ? nullptr : g.rope;
+    if (l3m_expf_tables(&a.elist, &a.eindex)) { fprintf(stderr, "l3m: %s\n", l3m_cuda_error()); return false; }
+    a.roles = g.roles;
+    a.off_attn = 0; a.off_proj = dim; a.off_h = 2 * dim; a.off_down = 2 * dim + ffn; a.off_pres = 3 * dim + ffn;
+    a.off_tok = a.off_pres + G;
+    a.ex_half = (a.off_tok + 3 * G + 31) & ~31;
+    g.ex_bytes = (size_t)a.ex_half * 2 * sizeof(uint64_t);
+    if (!cuda_ok(cudaMalloc(&g.ex, g.ex_bytes), "exchange")) return false;
+    a.ex = g.ex;
+    if (!cuda_ok(cudaMalloc(&g.prompt, (size_t)m->ctx * 4), "prompt")) return false;
+    if (!cuda_ok(cudaMalloc(&g.logits, (size_t)m->ctx * V * 4), "logits")) return false;
+    cudaMemset(g.logits, 0, (size_t)m->ctx * V * 4);
+    if (!cuda_ok(cudaMalloc(&g.abort_flag, 4), "flag")) return false;
+    a.prompt = g.prompt;
+    a.eos = m->f.tok.eos; a.bos = m->f.tok.bos;
+    a.logits = g.logits;
+    a.abort_flag = g.abort_flag;
+    const char *tmo = getenv("L3M_TIMEOUT_MS");
+    a.timeout_ns = (unsigned long long)(tmo ? atof(tmo) : 5000.0) * 1000000ull;
+
+    // Shared memory layout.
+    const int mx = std::max(dim, ffn), nb = (mx + 31) / 32;
+    int off = 0;
+    auto take = [&](int bytes) { int o2 = off; off = align16(off + bytes); return o2; };
+    a.sm_x = take(dim * 4);
+    a.sm_xb = take(mx * 4);
+    a.sm_tmp = take(mx * 4);
+    a.sm_q8 = take(mx);
+    a.sm_scale = take(nb * 4);
+    a.sm_sum = take(nb * 4);
+    a.sm_xf = take(mx * 4);
+    a.sm_y = take(std::max(unit_tiles, max_ffn_tiles) * L3M_TILE * 4);
+    a.sm_scores = take(std::max(m->ctx, 3 * G) * 4);
+    a.sm_kv = take(2 * hd * 2);
+    a.sm_att = take(hd * 4);
+    a.sm_red = take(64 * 4);
+    a.sm_scratch = take(0);
+    const int budget = 200 * 1024;
+    a.scratch_pairs = std::min(8192, (budget - off) / 8);
+    const int need_pairs = (mx / 32) * L3M_TILE;
+    if (a.scratch_pairs < need_pairs) {
+        fprintf(stderr, "l3m: dim %d / ffn %d need more shared memory than a B200 SM has for this kernel\n", dim, ffn);
+        return false;
+    }
+    a.smem_bytes = off + a.scratch_pairs * 8;
+    if (l3m_decode_occupancy(a.smem_bytes) < 1) {
+        fprintf(stderr, "l3m: the decode kernel does not fit on an SM of GPU %d\n", g.dev);
+        return false;
+    }
+    a.ctrl = m->ctrl_dev;
+    a.tokens = m->tokens_dev;
+    if (!cuda_ok(cudaStreamCreateWithFlags(&g.stream, cudaStreamNonBlocking), "stream")) return false;
+    if (!cuda_ok(cudaStreamCreateWithFlags(&g.side, cudaStreamNonBlocking), "stream")) return false;
+    cudaEventCreate(&g.ev0);
+    cudaEventCreate(&g.ev1);
+    (void)o;
+    return true;
+}
+
+// Keep the streamed weights in L2 with a persisting access-policy window (the GPU form of the
+// reference's cache residency). Returns false when over budget and not forced.
+bool place_in_l2(l3m_model *m, Gpu &g, const l3m_opts &o, bool *over) {
+    *over = g.weight_bytes > g.persist_max;
+    if (o.verbose || (*over && !o.force))
+        fprintf(stderr, "l3m: gpu %d (%s)  heads [0, %d)  weights %.2f + kv %.2f MiB, persisting L2 budget %.2f of %.2f MiB L2%s\n",
+                g.dev, g.name.c_str(), m->n_heads, g.weight_bytes / MiB, g.kv_bytes / MiB, g.persist_max / MiB, g.l2_bytes / MiB,
+                *over ? "  OVER" : "");
+    if (*over && !o.force) return false;
+    if (m->cold || !g.persist_max || !g.window_max) return true;
+    cudaSetDevice(g.dev);
+    size_t setaside = std::min(g.weight_bytes, g.persist_max);
+    if (cudaDeviceGetLimit(&g.prev_limit, cudaLimitPersistingL2CacheSize) == cudaSuccess &&
+        cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, setaside) == cudaSuccess) {
+        g.limit_set = true;
+        cudaStreamAttrValue attr = {};
+        attr.accessPolicyWindow.base_ptr = g.arena;
+        attr.accessPolicyWindow.num_bytes = std::min(g.weight_bytes, g.window_max);
+        attr.accessPolicyWindow.hitRatio = (float)std::min(1.0, (double)setaside / attr.accessPolicyWindow.num_bytes);
+        attr.accessPolicyWindow.hitProp = cudaAccessPropertyPersisting;
+        attr.accessPolicyWindow.missProp = cudaAccessPropertyStreaming;
+        cudaStreamSetAttribute(g.stream, cudaStreamAttributeAccessPolicyWindow, &attr);
+    }
+    cudaGetLastError();   // the window is best effort
+    return true;
+}
+
+}  // namespace
+
+extern "C" {
+
+L3M_API l3m_model *l3m_load(const char *path, const l3m_opts *opts) {
+    l3m_opts o = opts ? *opts : l3m_opts{};
+    l3m_model *m = new l3m_model();
+    if (l3m_file_open(&m->f, path)) { delete m; return nullptr; }
+    const l3m_header *h = m->f.h;
+    m->flags = h->flags;
+    if (m->flags & (L3M_F_LAYERNORM | L3M_F_GELU | L3M_F_LEARNED_POS))
+        return fail(m, "this GPU build runs Llama-family files (RMSNorm, RoPE, SiLU gate); LayerNorm, GELU and learned positions are not built");
+    m->dim = (int)h->dim; m->n_heads = (int)h->n_heads; m->n_kv = (int)h->n_kv_heads; m->hpk = m->n_heads / m->n_kv;
+    m->hd = m->dim / m->n_heads; m->ffn = (int)h->ffn_dim; m->vocab = (int)h->vocab; m->n_layers = (int)h->n_layers;
+    m->ctx = std::min((int)h->ctx, o.ctx > 0 ? o.ctx : kDefaultCtx);
+    m->reference = o.reference;
+    m->cold = o.cold;
+    m->kk = l3m_kernels_pick();
+    if (m->kk != &l3m_kernels_sm100a) return fail(m, "the decode engine runs the sm100a (exact) table; unset L3M_ISA");
+    int devices = 0;
+    if (cudaGetDeviceCount(&devices) != cudaSuccess || devices < 1) return fail(m, "no CUDA device: this build runs on B200 GPUs only");
+    int list[kMaxGpus], n = o.cpus ? o.n_cpus : 1;
+    if (n < 1 || n > kMaxGpus) return fail(m, "bad GPU list");
+    for (int i = 0; i < n; i++) {
+        list[i] = o.cpus ? o.cpus[i] : 0;
+        if (list[i] < 0 || list[i] >= devices) return fail(m, "bad GPU list: no such device");
+        for (int j = 0; j < i; j++) if (list[j] == list[i]) return fail(m, "a GPU appears twice in the list");
+    }
+    if (n > 1) return fail(m, "sharding one model over several GPUs in one process is not built; run one process per GPU");
+    m->n_gpus = n;
+    cudaSetDevice(list[0]);
+    if (!cuda_ok(cudaHostAlloc((void **)&m->ctrl, sizeof(l3m::Ctrl), cudaHostAllocMapped), "control block") ||
+        !cuda_ok(cudaHostAlloc((void **)&m->tokens, (size_t)m->ctx * 4, cudaHostAllocMapped), "token ring"))
+        return fail(m, "host-mapped memory unavailable");
+    cudaHostGetDevicePointer((void **)&m->ctrl_dev, m->ctrl, 0);
+    cudaHostGetDevicePointer((void **)&m->tokens_dev, m->tokens, 0);
+    bool over_any = false;
+    for (int i = 0; i < n; i++) {
+        m->g[i].dev = list[i];
+        if (!build_gpu(m, m->g[i], o)) { l3m_free(m); return nullptr; }
+        bool over;
+        if (!place_in_l2(m, m->g[i], o, &over)) {
+            over_any = true;
+        }
+        m->weight_bytes += m->g[i].weight_bytes;
+    }
+    if (over_any) {
+        char msg[256];
+        snprintf(msg, sizeof msg, "the weights will not stay resident in the persisting L2 window on %d GPU%s: use more GPUs, "
+                 "a smaller --dtype at export, or --force", n, n > 1 ? "s" : "");
+        return fail(m, msg);
+    }
+    m->host_logits.assign((size_t)m->vocab, 0.0f);
+    const char *base = strrchr(path, '/');
+    base = base ? base + 1 : path;
+    const int dtype = (int)l3m_file_blk(&m->f, 0, "w_up")->dtype;
+    if (m->reference)
+        snprintf(m->desc, sizeof m->desc, "%s: %s, %d layers, reference fp32 on %d GPU%s (%s)", base, l3m_dtype_name(dtype), m->n_layers, n,
+                 n > 1 ? "s" : "", m->kk->name);
+    else
+        snprintf(m->desc, sizeof m->desc, "%s: %s, %d layers, %.1f MiB on %d GPU%s (%s)", base, l3m_dtype_name(dtype), m->n_layers,
+                 m->weight_bytes / MiB, n, n > 1 ? "s" : "", m->kk->name);
+    if (o.verbose) fprintf(stderr, "l3m: %s, ctx %d\n", m->desc, m->ctx);
+    return m;
+}
+
+L3M_API void l3m_free(l3m_model *m) {
+    if (!m) return;
+    for (int i = 0; i < kMaxGpus; i++) {
+        Gpu &g = m->g[i];
+        if (g.dev < 0) continue;
+        cudaSetDevice(g.dev);
+        if (g.stream) cudaStreamSynchronize(g.stream);
+        if (g.limit_set) {
+            cudaCtxResetPersistingL2Cache();
+            cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, g.prev_limit);
+        }
+        cudaFree(g.arena); cudaFree(g.kv); cudaFree(g.rope); cudaFree(g.layers); cudaFree(g.roles); cudaFree(g.ex);
+        cudaFree(g.prompt); cudaFree(g.logits); cudaFree(g.abort_flag);
+        if (g.ev0) cudaEventDestroy(g.ev0);
+        if (g.ev1) cudaEventDestroy(g.ev1);
+        if (g.stream) cudaStreamDestroy(g.stream);
+        if (g.side) cudaStreamDestroy(g.side);
+    }
+    if (m->ctrl) cudaFreeHost(m->ctrl);
+    if (m->tokens) cudaFreeHost(m->tokens);
+    l3m_file_close(&m->f);
+    delete m;
+}
+
+L3M_API int l3m_generate(l3m_model *m, const int32_t *prompt, int n_prompt, int max_new, float temperature, uint64_t seed,
+                         int (*on_token)(int32_t, void *), void *user) {
+    (void)seed;
+    if (n_prompt < 1 || n_prompt >= m->ctx) return 0;
+    for (int i = 0; i < n_prompt; i++)
+        if (prompt[i] < 0 || prompt[i] >= m->vocab) { fprintf(stderr, "l3m: token %d out of range\n", prompt[i]); return -1; }
+    if (temperature > 0) { fprintf(stderr, "l3m: temperature sampling is not built on the GPU yet; use temperature 0\n"); return -1; }
+    Gpu &g = m->g[0];
+    cudaSetDevice(g.dev);
+    memset((void *)m->ctrl, 0, sizeof *m->ctrl);
+    l3m::DecodeArgs a = g.args;
+    a.n_prompt = n_prompt;
+    a.max_new = max_new;
+    const double t0 = now_ns();
+    cudaMemcpyAsync(g.prompt, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, g.stream);
+    cudaMemsetAsync(g.ex, 0, g.ex_bytes, g.stream);
+    cudaMemsetAsync(g.abort_flag, 0, 4, g.stream);
+    cudaEventRecord(g.ev0, g.stream);
+    if (l3m_decode_launch(&a, g.stream)) return -1;
+    cudaEventRecord(g.ev1, g.stream);
+    int seen = 0, n_gen = 0, stopped = -1;
+    if (on_token) {
+        for (;;) {
+            const int done = m->ctrl->done;
+            const int np = m->ctrl->n_published;
+            for (; seen < np; seen++) {
+                if (stopped >= 0) continue;
+                n_gen++;
+                m->logits_pos = n_prompt - 1 + seen;                 // l3m_logits inside on_token: this token's logits
+                if (!on_token(m->tokens[seen], user)) {
+                    stopped = seen;
+                    m->ctrl->stop_request = 1;
+                }
+            }
+            if (done) break;
+            if (cudaEventQuery(g.ev1) == cudaSuccess && !m->ctrl->done) break;   // the kernel ended without finishing
+            _mm_pause();
+        }
+    }
+    cudaError_t e = cudaStreamSynchronize(g.stream);
+    const double t1 = now_ns();
+    if (!cuda_ok(e, "decode")) return -1;
+    if (!m->ctrl->done || m->ctrl->error) {
+        fprintf(stderr, "l3m: decode kernel %s (code %d)\n", m->ctrl->done ? "reported an error" : "did not finish", m->ctrl->error);
+        return -1;
+    }
+    int last_pos;
+    if (stopped >= 0) {
+        last_pos = n_prompt - 1 + stopped;
+    } else {
+        n_gen = m->ctrl->n_gen;
+        last_pos = m->ctrl->final_pos;
+    }
+    m->logits_pos = last_pos;
+    m->cached_pos = -2;
+    float ms = 0;
+    cudaEventElapsedTime(&ms, g.ev0, g.ev1);
+    m->tok_count += last_pos + 1;
+    m->ns += t1 - t0;
+    m->dev_ns += ms * 1e6;
+    return n_gen;
+}
+
+L3M_API const float *l3m_logits(const l3m_model *cm) {
+    l3m_model *m = const_cast<l3m_model *>(cm);
+    if (m->logits_pos >= 0 && m->cached_pos != m->logits_pos) {
+        Gpu &g = m->g[0];
+        cudaSetDevice(g.dev);
+        cudaMemcpyAsync(m->host_logits.data(), g.logits + (size_t)m->logits_pos * m->vocab, (size_t)m->vocab * 4, cudaMemcpyDeviceToHost, g.side);
+        cudaStreamSynchronize(g.side);
+        m->cached_pos = m->logits_pos;
+    }
+    return m->host_logits.data();
+}
+
+L3M_API int l3m_vocab(const l3m_model *m) { return m->vocab; }
+L3M_API int l3m_ctx(const l3m_model *m) { return m->ctx; }
+L3M_API const char *l3m_describe(const l3m_model *m) { return m->desc; }
+L3M_API int l3m_bos(const l3m_model *m) { return m->f.tok.bos; }
+L3M_API int l3m_eos(const l3m_model *m) { return m->f.tok.eos; }
+L3M_API const char *l3m_chatml(const l3m_model *m, int32_t *im_start) {
+    *im_start = m->f.im_start;
+    return m->f.system;
+}
+L3M_API int l3m_encode(const l3m_model *m, const char *text, int add_bos, int32_t *out, int max) {
+    return l3m_tokenizer_encode(&m->f.tok, text, add_bos, out, max);
+}
+L3M_API const char *l3m_decode(const l3m_model *m, int32_t tok, int *len) {
+    return (const char *)l3m_tokenizer_decode(&m->f.tok, tok, len);
+}
+
+L3M_API int l3m_perf_read(l3m_model *m, l3m_perf *out) {
+    memset(out, 0, sizeof *out);
+    out->l3_miss = out->dram_bytes = out->energy_j = out->llc_occupancy = NAN;
+    const double tokens = m->tok_count, ns = m->ns, dev = m->dev_ns;
+    m->tok_count = m->ns = m->dev_ns = 0;
+    if (tokens <= 0) return -1;
+    out->tokens = tokens;
+    out->ns_token = ns / tokens;
+    out->ns_compute = std::min(dev / tokens, out->ns_token);
+    out->ns_wait = out->ns_token - out->ns_compute;          // outside the kernel: launch and host
+    out->bytes_token = (double)m->weight_bytes;
+    for (int i = 0; i < m->n_gpus; i++) out->l2_bytes += (double)m->g[i].l2_bytes;
+    return 0;
+}
+
+L3M_API int l3m_parse_cpus(const char *list, int *cpus, int max) {
+    int n = 0;
+    const char *p = list;
+    if (!p || !*p) return -1;
+    for (;;) {
+        char *end;
+        long a = strtol(p, &end, 10);
+        if (end == p || a < 0 || a > 4095) return -1;
+        long b = a;
+        p = end;
+        if (*p == '-') {
+            b = strtol(p + 1, &end, 10);
+            if (end == p + 1 || b < a || b > 4095) return -1;
+            p = end;
+        }
+        for (long c = a; c <= b; c++) {
+            if (n == max) return -1;
+            cpus[n++] = (int)c;
+        }
+        if (!*p) return n;
+        if (*p != ',' || !p[1]) return -1;
+        p++;
+    }
+}
+
+L3M_API void l3m_print_hw(FILE *out) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) { fprintf(out, "no CUDA devices\n"); return; }
+    for (int d = 0; d < n; d++) {
+        cudaDeviceProp p;
+        if (cudaGetDeviceProperties(&p, d) != cudaSuccess) continue;
+        fprintf(out, "GPU %d: %s, sm_%d%d, %d SMs, L2 %.1f MiB, persisting budget %.1f MiB, window %.1f MiB, %.1f GiB\n", d, p.name,
+                p.major, p.minor, p.multiProcessorCount, p.l2CacheSize / MiB, p.persistingL2CacheMaxSize / MiB,
+                p.accessPolicyMaxWindowSize / MiB, p.totalGlobalMem / (MiB * 1024));
+    }
+}
+
+}  // extern "C"

@@ -73,7 +73,10 @@ def encode(x, dtype):
         return to_bf16(x).tobytes()
     if x.shape[-1] % 32:
         raise ValueError(f"{dtype}: inputs {x.shape[-1]} not a multiple of 32")
-    return {"q8_0": q8_0, "q4_0": q4_0, "mxfp4": mxfp4}[dtype](x).tobytes()
+    fn = {"q8_0": q8_0, "q4_0": q4_0, "mxfp4": mxfp4}[dtype]
+    flat = x.reshape(-1, 32)
+    step = 1 << 18                                        # blocks per chunk: bounded temporaries
+    return b"".join(fn(flat[i:i + step]).tobytes() for i in range(0, len(flat), step))
 
 
 # ---- the container

@@ -252,12 +252,16 @@ static float *dequant_matrix(const tensor *t) {
     return out;
 }
 
-// reference ref.c:35-42: out[i] = Σ_j w[i][j] x[j] by sequential fma, then + bias.
+// reference ref.c:35-42: out[i] = Σ_j w[i][j] x[j] in input order, then + bias. As in the f32
+// kernel, the compiler vectorises the products 8 (then 4) wide and adds them one by one; the
+// inputs past o_rmsnorm_fused_from(k) each take one fused multiply-add.
 static void matvec(float *out, const float *w, const float *x, const float *bias, int n, int k) {
+    int split = o_rmsnorm_fused_from(k);
     for (int i = 0; i < n; i++) {
         const float *r = w + (size_t)i * k;
         float acc = 0.0f;
-        for (int j = 0; j < k; j++) acc = fmaf(r[j], x[j], acc);
+        for (int j = 0; j < split; j++) acc = acc + r[j] * x[j];
+        for (int j = split; j < k; j++) acc = fmaf(r[j], x[j], acc);
         out[i] = acc + (bias ? bias[i] : 0.0f);
     }
 }

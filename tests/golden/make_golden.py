@@ -1,0 +1,128 @@
+"""Regenerate the golden fixtures in this directory from the reference (fpedd/l3m) itself.
+
+Run where the reference checkout and its compiled library exist (oracle/_ref, built by
+oracle/Makefile):  python tests/golden/make_golden.py [/root/reference]
+
+  ggml.json       ggml block bytes for the reference's own known-answer inputs (its
+                  tests/unit/test_export.py:19-59), recomputed with its exporter and checked
+                  against the hex strings in that test file.
+  models.json     sha256 of small .l3m files written by the reference's exporter from the same
+                  fp32 tensors as l3m_b200.synth builds (the tests' `models` fixture).
+  engine.npz      the reference engine's greedy tokens and logits on those files: its scalar
+                  kernel table on 1 and 3 cores (L3M_ISA=scalar), and its fp32 reference path.
+"""
+import ctypes as C
+import hashlib
+import json
+import os
+import re
+import sys
+import tempfile
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parents[1]
+REF = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+sys.path.insert(0, str(REF / "python"))
+sys.path.insert(0, str(ROOT))
+
+from l3m import archs, export  # noqa: E402  (the reference's exporter)
+
+from l3m_b200 import synth  # noqa: E402
+
+PROMPT = [5, 77, 200, 3]
+STEPS = 40
+SPECS = {   # must match tests/conftest.py `models`
+    "gqa": dict(dim=64, n_layers=2, n_heads=4, n_kv_heads=2, ffn_dim=128, vocab=300, ctx=96, tied=False, seed=1),
+    "mha40": dict(dim=160, n_layers=2, n_heads=4, n_kv_heads=4, ffn_dim=96, vocab=320, ctx=96, tied=True, seed=2),
+}
+DTYPES = ["f32", "bf16", "q8_0", "q4_0", "mxfp4"]
+
+
+def ggml_golden():
+    src = (REF / "tests/unit/test_export.py").read_text()
+    halves = np.arange(-16, 16, dtype=np.float32) / 2
+    ties = np.float32([127, 0.49999997, -0.49999997, 0.5, -0.5, 1.5, -2.5] + [0] * 25)
+    cases = re.findall(r'\("(q8_0|q4_0|mxfp4)", (HALVES|TIES), "([0-9a-f]+)"\)', src)
+    assert len(cases) == 6, cases
+    out = {"halves": halves.tolist(), "ties": ties.tolist(), "blocks": []}
+    for dtype, which, hexs in cases:
+        x = halves if which == "HALVES" else ties
+        assert getattr(export, dtype)(x).tobytes().hex() == hexs
+        out["blocks"].append({"dtype": dtype, "input": which.lower(), "hex": hexs})
+    bf = np.array([1.0, 1 + 2**-8, 1 + 3 * 2**-8, 1 + 2**-7 + 2**-9, -2.5], dtype=np.float32)
+    out["bf16_in"] = bf.tolist()
+    out["bf16_out"] = ((export.to_bf16(bf).astype(np.uint32) << 16).view(np.float32)).tolist()
+    m = re.search(r"def test_q8_0_rounds_like_ggml\(\):.*?x = np.array\(\[(.*?)\], dtype", src, re.S)
+    xs = [float(v) for v in m.group(1).replace("\n", " ").split(",")]
+    q = export.q8_0(np.array(xs, dtype=np.float32))[0, 2:].view(np.int8)
+    assert q[21] == 75
+    out["q8_rounding_in"] = xs
+    out["q8_rounding_q"] = q.tolist()
+    return out
+
+
+def ref_model(m):
+    return archs.Model(m.arch, m.flags, m.dim, m.n_layers, m.n_heads, m.n_kv_heads, m.ffn_dim, m.vocab, m.ctx, m.rope_theta,
+                       m.norm_eps, tensors=m.tensors, tokens=m.tokens, bos=m.bos, eos=m.eos)
+
+
+class Opts(C.Structure):
+    _fields_ = [("cpus", C.POINTER(C.c_int)), ("n_cpus", C.c_int), ("ctx", C.c_int), ("reference", C.c_int),
+                ("force", C.c_int), ("verbose", C.c_int), ("cold", C.c_int)]
+
+
+def run_ref(lib, path, cores, reference):
+    """Greedy tokens and the logits at every sampling position, by feeding prefixes (the reference
+    exposes only the last position's logits)."""
+    cb_t = C.CFUNCTYPE(C.c_int, C.c_int32, C.c_void_p)
+    cpus = (C.c_int * cores)(*range(cores))
+    o = Opts(cpus=None if reference else cpus, n_cpus=0 if reference else cores, reference=int(reference), force=1)
+    m = lib.l3m_load(os.fsencode(str(path)), C.byref(o))
+    assert m
+    V = lib.l3m_vocab(m)
+    toks = []
+    cb = cb_t(lambda t, u: toks.append(t) or 1)
+    pr = (C.c_int32 * len(PROMPT))(*PROMPT)
+    lib.l3m_generate(m, pr, len(PROMPT), STEPS, 0.0, 0, cb, None)
+    logits = []
+    for i in range(len(toks) + 1):
+        seq = PROMPT + toks[:i]
+        pr = (C.c_int32 * len(seq))(*seq)
+        lib.l3m_generate(m, pr, len(seq), 0, 0.0, 0, cb_t(lambda t, u: 1), None)
+        logits.append(np.ctypeslib.as_array(lib.l3m_logits(m), shape=(V,)).copy())
+    lib.l3m_free(m)
+    return toks, np.stack(logits)
+
+
+def main():
+    (HERE / "ggml.json").write_text(json.dumps(ggml_golden(), indent=1))
+    os.environ["L3M_ISA"] = "scalar"
+    lib = C.CDLL(str(ROOT / "oracle/_ref/libl3m.so"))
+    lib.l3m_load.restype, lib.l3m_load.argtypes = C.c_void_p, [C.c_char_p, C.POINTER(Opts)]
+    lib.l3m_generate.argtypes = [C.c_void_p, C.POINTER(C.c_int32), C.c_int, C.c_int, C.c_float, C.c_uint64, C.c_void_p, C.c_void_p]
+    lib.l3m_logits.restype, lib.l3m_logits.argtypes = C.POINTER(C.c_float), [C.c_void_p]
+    lib.l3m_vocab.argtypes = lib.l3m_free.argtypes = [C.c_void_p]
+    hashes, arrays = {}, {}
+    with tempfile.TemporaryDirectory() as tmp:
+        for name, shape in SPECS.items():
+            m = synth.llama(**shape, std="fan_in", stop_tokens=False)
+            for dt in DTYPES:
+                path = Path(tmp) / f"{name}-{dt}.l3m"
+                export.write(ref_model(m), dt, dt, path)
+                hashes[f"{name}-{dt}"] = hashlib.sha256(path.read_bytes()).hexdigest()
+                for label, cores, reference in (("scalar1", 1, 0), ("scalar3", 3, 0), ("ref", 1, 1)):
+                    toks, lg = run_ref(lib, path, cores, reference)
+                    arrays[f"{name}-{dt}-{label}-tokens"] = np.array(toks, np.int32)
+                    arrays[f"{name}-{dt}-{label}-logits"] = lg
+                assert np.array_equal(arrays[f"{name}-{dt}-scalar1-logits"], arrays[f"{name}-{dt}-scalar3-logits"])
+                del arrays[f"{name}-{dt}-scalar3-logits"], arrays[f"{name}-{dt}-scalar3-tokens"]
+    (HERE / "models.json").write_text(json.dumps({"prompt": PROMPT, "steps": STEPS, "sha256": hashes}, indent=1))
+    np.savez_compressed(HERE / "engine.npz", **arrays)
+    print("wrote", ", ".join(p.name for p in HERE.iterdir() if p.suffix in (".json", ".npz")))
+
+
+if __name__ == "__main__":
+    main()

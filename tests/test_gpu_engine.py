@@ -1,0 +1,128 @@
+"""The decode engine behind l3m.h on a B200, against the oracle: greedy tokens and the logits of
+every sampled position bit for bit, on the engine path (the reference's scalar table) and on the
+fp32 reference path (reference=True); plus the generate contract (stops, callbacks, errors)
+that the reference's tests/integration/test_engine.py checks."""
+import ctypes as C
+import json
+
+import numpy as np
+import pytest
+
+import l3m_b200
+from conftest import DTYPES, GOLDEN, OracleRun
+from l3m_b200 import synth
+
+pytestmark = pytest.mark.gpu
+MJ = json.loads((GOLDEN / "models.json").read_text())
+PROMPT = MJ["prompt"]
+
+
+def gpu_run(path, prompt, max_new, **kw):
+    """Tokens and the logits behind each one (read inside on_token), then the final logits."""
+    m = l3m_b200.Model(path, force=True, **kw)
+    rows = []
+    toks = m.generate(prompt, max_new, temperature=0, on_token=lambda t: rows.append(m.logits) or True)
+    rows.append(m.logits)
+    return m, toks, np.stack(rows)
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+@pytest.mark.parametrize("name", ["gqa", "mha40"])
+@pytest.mark.parametrize("reference", [False, True])
+def test_logits_bit_exact(gpu, oracle, models, name, dt, reference):
+    path = models[(name, dt)]
+    want = OracleRun(oracle, path, PROMPT, MJ["steps"], reference=reference)
+    m, toks, lg = gpu_run(path, PROMPT, MJ["steps"], reference=reference)
+    assert toks == want.tokens
+    assert lg.shape == want.logits.shape
+    bad = np.nonzero((lg.view(np.uint32) != want.logits.view(np.uint32)).any(axis=1))[0]
+    assert bad.size == 0, f"first differing position {bad[0]}, max |diff| {np.abs(lg - want.logits).max()}"
+
+
+def test_max_new_zero_gives_prompt_logits(gpu, oracle, models):
+    path = models[("gqa", "q8_0")]
+    m = l3m_b200.Model(path, force=True)
+    assert m.generate(PROMPT, 0, temperature=0) == []
+    want = OracleRun(oracle, path, PROMPT, 0)
+    assert np.array_equal(m.logits.view(np.uint32), want.logits[0].view(np.uint32))
+
+
+def test_ctx_limits_generation(gpu, oracle, models):
+    """pos + 1 >= ctx stops the stream (reference engine.c:322; test_engine.py:319-324)."""
+    path = models[("mha40", "bf16")]
+    m = l3m_b200.Model(path, ctx=16, force=True)
+    assert m.ctx == 16
+    toks = m.generate(PROMPT, 100, temperature=0)
+    assert len(toks) == 16 - len(PROMPT)
+    want = OracleRun(oracle, path, PROMPT, 100, ctx=16)
+    assert toks == want.tokens
+    assert np.array_equal(m.logits.view(np.uint32), want.logits[-1].view(np.uint32))
+    with pytest.raises(ValueError):
+        m.generate([1] * 16, 4, temperature=0)
+
+
+def test_stops_at_eos_and_bos(gpu, oracle, models, tmp_path):
+    """EOS and BOS end the stream and are not returned (reference engine.c:323-324)."""
+    path = models[("gqa", "f32")]
+    free = OracleRun(oracle, path, PROMPT, 24).tokens
+    base = synth.llama(dim=64, n_layers=2, n_heads=4, n_kv_heads=2, ffn_dim=128, vocab=300, ctx=96, tied=False, seed=1,
+                       std="fan_in", stop_tokens=False)
+    for attr in ("eos", "bos"):
+        stop = free[8]
+        if stop in free[:8]:
+            continue
+        m = base
+        m.bos, m.eos = (-1, stop) if attr == "eos" else (stop, -1)
+        p = tmp_path / f"{attr}.l3m"
+        synth.write(m, "f32", "f32", p)
+        got = l3m_b200.Model(p, force=True).generate(PROMPT, 24, temperature=0)
+        assert got == free[:8]
+        assert OracleRun(oracle, p, PROMPT, 24).tokens == free[:8]
+
+
+def test_callback_stops_and_perf_counts(gpu, models):
+    """on_token returning False stops after that token (reference test_engine.py:279-287)."""
+    m = l3m_b200.Model(models[("gqa", "q8_0")], force=True)
+    seen = []
+    out = m.generate(PROMPT, 30, temperature=0, on_token=lambda t: seen.append(t) or len(seen) < 5)
+    assert out == seen and len(out) == 5
+    p = m.perf()
+    assert p["tokens"] == len(PROMPT) + len(out) - 1 and p["ns_token"] > 0 and p["bytes_token"] > 0
+    assert 0 <= p["ns_wait"] < p["ns_token"]
+    assert all(np.isnan(v) for v in m.perf().values())
+    full = m.generate(PROMPT, 30, temperature=0)
+    assert full[:5] == out
+
+
+def test_c_api_contracts(gpu, models):
+    """What the Python wrapper guards, refused by the C API too (reference test_engine.py:290-302)."""
+    m = l3m_b200.Model(models[("gqa", "f32")], ctx=16, force=True)
+    lib, h, cb = m._lib, m._m, l3m_b200._CB(lambda t, u: 1)
+    assert lib.l3m_generate(h, (C.c_int32 * 1)(m.vocab), 1, 2, 0.0, 0, cb, None) == -1
+    assert lib.l3m_generate(h, (C.c_int32 * 16)(*[1] * 16), 16, 2, 0.0, 0, cb, None) == 0
+    assert lib.l3m_generate(h, (C.c_int32 * 0)(), 0, 2, 0.0, 0, cb, None) == 0
+    buf = (C.c_int32 * 3)()
+    assert lib.l3m_encode(h, b"hello", 1, buf, 2) == -1
+    n = C.c_int(7)
+    lib.l3m_decode(h, 99999, C.byref(n))
+    assert n.value == 0
+    assert lib.l3m_perf_read(h, C.byref(l3m_b200.Perf())) == -1
+
+
+def test_repeat_generate_is_deterministic(gpu, models):
+    m = l3m_b200.Model(models[("mha40", "q4_0")], force=True)
+    a = m.generate(PROMPT, 30, temperature=0)
+    la = m.logits
+    b = m.generate(PROMPT, 30, temperature=0)
+    assert a == b and np.array_equal(la.view(np.uint32), m.logits.view(np.uint32))
+
+
+def test_describe_and_python_api(gpu, models):
+    path = models[("gqa", "f32")]
+    with l3m_b200.Model(path, force=True, verbose=True) as m:
+        assert "GPU" in m.describe() and "sm100a" in m.describe()
+        assert m.generate(PROMPT, 3, temperature=0)
+    with pytest.raises(ValueError):
+        m.describe()
+    with pytest.raises(ValueError):
+        l3m_b200.Model(path, ctx=1)

@@ -1,0 +1,268 @@
+"""Host side of the library, no GPU: the exported C ABI, tile packing and activation prepare
+against the oracle, the loader's validation messages (the reference's robustness cases,
+tests/integration/test_robustness.py:23-46), GPU-list parsing, and the tokenizer (its tests,
+tests/unit/test_tokenizer.py), through a small harness linked against the loader and tokenizer."""
+import ctypes as C
+import re
+import struct
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from conftest import ROOT, P, Vec
+from l3m_b200 import synth
+from test_oracle import random_rows
+
+LIB = ROOT / "l3m_b200" / "libl3m.so"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not LIB.exists():
+        subprocess.run(["make", "-s", "-C", str(ROOT / "l3m_b200")], check=True)
+    import l3m_b200
+    return l3m_b200.lib()
+
+
+def declared_symbols():
+    names = set()
+    for h in (ROOT / "include").glob("*.h"):
+        text = re.sub(r"#define L3M_API.*", "", h.read_text())
+        for decl in re.findall(r"L3M_API[^;]*?;", text, re.S):
+            fn = re.findall(r"\b(l3m_\w+)\s*\(", decl)
+            if fn:
+                names.add(fn[0])                                      # a function: the name before (
+            else:
+                names.update(re.findall(r"\b(l3m_\w+)\s*(?:,|;)", decl))   # data: the declarators
+    return names
+
+
+def test_exports_every_declared_symbol(lib):
+    out = subprocess.run(["nm", "-D", "--defined-only", str(LIB)], capture_output=True, text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines()}
+    declared = declared_symbols()
+    assert len(declared) >= 30
+    missing = declared - exported
+    assert not missing, missing
+    assert not any(s.startswith("o_") for s in exported)   # nothing of the oracle is in the product
+
+
+@pytest.mark.parametrize("dtype", range(5))
+def test_host_layout_matches_oracle(lib, oracle, dtype):
+    rng = np.random.default_rng(dtype)
+    for k in ([2, 18, 288] if dtype <= 1 else [32, 288, 1376]):
+        rb, tb = lib.l3m_row_bytes(dtype, k), lib.l3m_tile_bytes(dtype, k)
+        assert (rb, tb) == (oracle.o_row_bytes(dtype, k), oracle.o_tile_bytes(dtype, k))
+        rows = random_rows(rng, dtype, 16, k, rb, edge=dtype >= 2)
+        ptrs = (C.c_void_p * 16)(*[rows[c].ctypes.data if c < 11 else None for c in range(16)])
+        a, b = np.zeros(tb, np.uint8), np.zeros(tb, np.uint8)
+        lib.l3m_pack_tile(P(a), dtype, ptrs, k)
+        oracle.o_pack_tile(P(b), dtype, ptrs, k)
+        assert np.array_equal(a, b)
+        da, db = np.zeros(k, np.float32), np.zeros(k, np.float32)
+        lib.l3m_dequant_row(P(da), dtype, P(rows[0]), k)
+        oracle.o_dequant_row(P(db), dtype, P(rows[0]), k)
+        assert np.array_equal(da.view(np.uint32), db.view(np.uint32))
+        if dtype >= 1 and k % 32 == 0 or dtype == 1:
+            x = (rng.standard_normal(k) * 3).astype(np.float32)
+            sa, sb = np.zeros(4 * k + 64, np.uint8), np.zeros(4 * k + 64, np.uint8)
+            lib.l3m_vec_prepare(C.byref(Vec()), dtype, P(x), k, P(sa))
+            oracle.o_vec_prepare(C.byref(Vec()), dtype, P(x), k, P(sb))
+            assert np.array_equal(sa, sb)
+
+
+def test_parse_cpus(lib):
+    buf = (C.c_int * 8)()
+    assert lib.l3m_parse_cpus(b"0-3,6", buf, 8) == 5 and list(buf[:5]) == [0, 1, 2, 3, 6]
+    for bad in (b"", b"0,", b"3-1", b"a", b"0-9"):
+        assert lib.l3m_parse_cpus(bad, buf, 8) == -1, bad
+
+
+# ---- loader validation, in a child process so the library's stderr can be read
+
+def toc(data):
+    n, _, off, _ = struct.unpack_from("<IIQQ", data, 64)
+    return {bytes(data[e:e + 64]).split(b"\0")[0].decode(): e for e in range(off, off + 120 * n, 120)}
+
+
+def patched(src, dst, edits):
+    b = bytearray(Path(src).read_bytes())
+    base = toc(b) | {"tok": struct.unpack_from("<Q", b, 80)[0]}
+    for fmt, where, v in edits:
+        struct.pack_into(fmt, b, base[where[0]] + where[1] if isinstance(where, tuple) else where, v)
+    Path(dst).write_bytes(b)
+    return dst
+
+
+CASES = {   # header: n_heads at 36, vocab 48, n_tensors 64, toc 72, chat 88 (reference test_robustness.py:23-38)
+    "n_tensors": ([("<I", 64, 0xFFFFFFFF)], "truncated file"),
+    "toc_offset": ([("<Q", 72, 1 << 63)], "truncated file"),
+    "heads": ([("<I", 36, 3)], "bad config"),
+    "dtype": ([("<I", ("blk.0.w_up", 64), 9)], "bad dtype"),
+    "shape": ([("<Q", ("blk.0.wk", 72), 1)], "nbytes does not match"),
+    "offset": ([("<Q", ("blk.0.wq", 104), 1)], "misaligned"),
+    "offset_wrap": ([("<Q", ("blk.0.wq", 104), (1 << 64) - 64)], "past the end"),
+    "missing": ([("<2s", ("blk.1.w_down", 0), b"zz")], "blk.1.w_down missing"),
+    "norm_dtype": ([("<I", ("norm", 64), 1), ("<Q", ("norm", 112), 128)], "tensor norm: expected f32"),
+    "tok_count": ([("<I", ("tok", 0), 0x7FFFFFFF)], "bad tokenizer"),
+    "tok_len": ([("<H", ("tok", 20), 65535)], "bad tokenizer"),
+    "tok_bos": ([("<i", ("tok", 4), 99999)], "bad tokenizer"),
+    "tok_vocab": ([("<I", 48, 100)], "tensor embed: expected"),
+    "chat_offset": ([("<Q", 88, 1 << 40)], "bad chat section"),
+}
+
+LOAD = """
+import ctypes as C, sys
+sys.path.insert(0, {root!r})
+import l3m_b200
+lib = l3m_b200.lib()
+m = lib.l3m_load({path!r}.encode(), None)
+sys.exit(0 if m else 1)
+"""
+
+
+def load_stderr(path):
+    r = subprocess.run([sys.executable, "-c", LOAD.format(root=str(ROOT), path=str(path))], capture_output=True, text=True, timeout=120)
+    return r.returncode, r.stderr
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_malformed_file_is_a_clean_error(lib, models, tmp_path, case):
+    edits, msg = CASES[case]
+    path = patched(models[("gqa", "q4_0")], tmp_path / f"{case}.l3m", edits)
+    rc, err = load_stderr(path)
+    assert rc == 1 and msg in err, err
+
+
+def test_qkv_biases_come_together(lib, tmp_path):
+    m = synth.llama(64, 2, 4, 4, 128, 260, 64, seed=3)
+    m.tensors["blk.1.bq"] = np.zeros(64, np.float32)
+    synth.write(m, "f32", "f32", tmp_path / "bq.l3m")
+    rc, err = load_stderr(tmp_path / "bq.l3m")
+    assert rc == 1 and "come together" in err, err
+
+
+def test_truncated_file(lib, models, tmp_path):
+    data = Path(models[("gqa", "q8_0")]).read_bytes()
+    toc_off, tok_off = struct.unpack_from("<QQ", data, 72)
+    for cut in (0, 100, 1024, toc_off + 10, tok_off + 3, len(data) - 1):
+        p = tmp_path / f"cut{cut}.l3m"
+        p.write_bytes(data[:cut])
+        rc, err = load_stderr(p)
+        assert rc == 1 and err.startswith("l3m: "), (cut, err)
+
+
+# ---- tokenizer, through a harness linked against the loader and tokenizer objects
+
+HARNESS = r"""
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include "file.h"
+int main(int argc, char **argv) {   /* file, add_bos, then one text per line on stdin: ids out */
+    l3m_file f;
+    if (l3m_file_open(&f, argv[1])) return 1;
+    static char line[1 << 22];
+    static int32_t out[1 << 22];
+    while (fgets(line, sizeof line, stdin)) {
+        size_t n = strlen(line);
+        if (n && line[n - 1] == '\n') line[--n] = 0;
+        for (size_t i = 0; i < n; i++) if (line[i] == 1) line[i] = '\n';   /* \x01 stands for a newline */
+        int k = l3m_tokenizer_encode(&f.tok, line, atoi(argv[2]), out, 1 << 22);
+        for (int i = 0; i < k; i++) printf("%d ", out[i]);
+        printf("\n");
+    }
+    l3m_file_close(&f);
+    return 0;
+}
+"""
+
+
+@pytest.fixture(scope="module")
+def tok_bin(tmp_path_factory):
+    d = tmp_path_factory.mktemp("tok")
+    (d / "h.c").write_text(HARNESS)
+    src = ROOT / "l3m_b200" / "csrc"
+    exe = d / "tok"
+    subprocess.run(["gcc", "-O2", "-std=c11", "-D_GNU_SOURCE", f"-I{src}", "-o", str(exe), str(d / "h.c"),
+                    str(src / "file.c"), str(src / "tokenizer.c"), str(src / "pack.c"), "-lm"], check=True)
+    return exe
+
+
+def encode(exe, path, texts, bos=False):
+    inp = "".join(t.replace("\n", "\x01") + "\n" for t in texts)
+    r = subprocess.run([str(exe), str(path), str(int(bos))], input=inp.encode(), capture_output=True, check=True)
+    return [[int(v) for v in line.split()] for line in r.stdout.decode().splitlines()]
+
+
+def with_tokens(path, tokens, flags=0):
+    m = synth.llama(64, 2, 4, 2, 128, len(tokens), 64, seed=1)
+    m.tokens, m.flags = tokens, m.flags | flags
+    m.bos, m.eos = 256, 257
+    synth.write(m, "f32", "f32", path)
+    return path
+
+
+BYTES = synth.byte_tokens(258)
+
+
+def test_byte_round_trip(tok_bin, tmp_path):
+    p = with_tokens(tmp_path / "b.l3m", BYTES)
+    texts = ["Once upon a time, there was a little girl named Lily.", "tabs\tand newlines", "ünïcödé 🐍 bytes"]
+    for t, ids in zip(texts, encode(tok_bin, p, texts)):
+        assert ids == list(t.encode())
+    assert encode(tok_bin, p, ["a"], bos=True)[0] == [256, 97]
+
+
+def test_byte_level_pieces(tok_bin, tmp_path):
+    """Merges stay inside GPT-2 pre-tokenizer pieces (reference test_tokenizer.py:31-39)."""
+    for digits in (False, True):
+        p = with_tokens(tmp_path / f"bpe{digits}.l3m", BYTES + [(b"\n\n", -1.0), (b"'s", -2.0)], synth.DIGITS if digits else 0)
+        got = encode(tok_bin, p, ["a\n\nb", "a\n\n", "it's '", "x='s", "\n\n1"])
+        assert got[0] == [97, 10, 10, 98]
+        assert got[1] == [97, 258]
+        assert got[2] == [105, 116, 259, 32, 39]
+        assert got[3] == [120, 61, 39, 115]
+        assert got[4] == ([258, 49] if digits else [10, 10, 49])
+
+
+MERGES = [(b"ab", -3.0), (b"bc", -1.0), (b"xy", -1.0), (b"xyz", -2.0), (b"aa", -4.0), (b" a", -5.0), ("ü".encode(), synth.NO_MERGE), (b",", 0.0)]
+
+
+def test_merges(tok_bin, tmp_path):
+    """Highest score first, leftmost on ties, whole characters, duplicates by score (reference test_tokenizer.py:42-61)."""
+    p = with_tokens(tmp_path / "m.l3m", BYTES + MERGES)
+    got = encode(tok_bin, p, ["abc", "xyz", "aaa", "üé", ","])
+    assert got == [[97, 259], [261], [262, 97], [264, 0xC3, 0xA9], [265]]
+    sp = with_tokens(tmp_path / "sp.l3m", BYTES + MERGES, synth.SP_PREFIX)
+    got = encode(tok_bin, sp, ["a", "", "b"]) + encode(tok_bin, sp, ["b"], bos=True)
+    assert got == [[263], [], [32, 98], [256, 32, 98]]
+
+
+def test_merges_match_quadratic_reference(tok_bin, tmp_path):
+    import random
+    p = with_tokens(tmp_path / "q.l3m", BYTES + MERGES)
+    vocab = {b: i for i, (b, _) in enumerate(BYTES)} | {b: 258 + i for i, (b, _) in enumerate(MERGES)}
+    score = {258 + i: s for i, (_, s) in enumerate(MERGES)}
+    rng = random.Random(1)
+    texts, wants = [], []
+    for _ in range(50):
+        text = "".join(rng.choices("abcxyz", k=rng.randrange(1, 300)))
+        syms = [bytes([c]) for c in text.encode()]
+        while cands := [(score[vocab[a + b]], -i) for i, (a, b) in enumerate(zip(syms, syms[1:])) if a + b in vocab]:
+            i = -max(cands)[1]
+            syms[i:i + 2] = [syms[i] + syms[i + 1]]
+        texts.append(text)
+        wants.append([vocab[s] for s in syms])
+    assert encode(tok_bin, p, texts) == wants
+
+
+def test_long_piece_is_not_quadratic(tok_bin, tmp_path):
+    import time
+    p = with_tokens(tmp_path / "l.l3m", BYTES + MERGES)
+    t = time.perf_counter()
+    assert encode(tok_bin, p, ["a" * (1 << 20)])[0] == [262] * (1 << 19)
+    assert time.perf_counter() - t < 10
