@@ -14,6 +14,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <ctime>
+#include <deque>
 #include <string>
 #include <vector>
 #include <x86intrin.h>
@@ -116,11 +117,12 @@ const void *row_ptr(const l3m_file *f, const l3m_tensor *t, int r) {
 }
 
 // Rows of one matrix to pack, as file rows (dtype of the tensor) or, on the reference path,
-// dequantised f32 copies (the fp32 reference dequantises every matrix, src/ref.c:24-32).
+// dequantised f32 copies (the fp32 reference dequantises every matrix, src/ref.c:24-32). A NULL
+// row packs as zeros.
 struct Rows {
     int dtype = 0, k = 0;
     std::vector<const void *> ptr;
-    std::vector<std::vector<float>> f32;
+    std::deque<std::vector<float>> f32;          // stable addresses as it grows
     void add(const l3m_file *f, const l3m_tensor *t, int r, bool to_f32) {
         k = (int)t->shape[1];
         if (!to_f32) {
@@ -131,14 +133,12 @@ struct Rows {
         dtype = L3M_F32;
         f32.emplace_back(k);
         l3m_dequant_row(f32.back().data(), (int)t->dtype, row_ptr(f, t, r), k);
+        ptr.push_back(f32.back().data());
     }
-    void finish() {
-        if (!f32.empty()) for (auto &v : f32) ptr.push_back(v.data());
-    }
+    void pad_to(size_t n) { while (ptr.size() < n) ptr.push_back(nullptr); }
 };
 
 size_t pack(Stage &s, Rows &rows) {
-    rows.finish();
     const int n = (int)rows.ptr.size(), nt = tiles_of(n);
     const size_t tb = l3m_tile_bytes(rows.dtype, rows.k);
     size_t off = s.reserve((size_t)nt * tb);
@@ -204,15 +204,16 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     const int unit_rows = 3 * hd, unit_tiles = tiles_of(unit_rows);
     for (int l = 0; l < L; l++) {
         const l3m_tensor *wq = l3m_file_blk(f, l, "wq"), *wk = l3m_file_blk(f, l, "wk"), *wv = l3m_file_blk(f, l, "wv");
-        for (int h = 0; h < m->n_heads; h++) {                                      // one unit per query head
-            Rows r;
+        Rows r;                                                                     // one unit per query head,
+        for (int h = 0; h < m->n_heads; h++) {                                      // each whole tiles, back to back
             const int kvh = h / m->hpk;
             for (int i = 0; i < hd; i++) r.add(f, wq, h * hd + i, ref);
             for (int i = 0; i < hd; i++) r.add(f, wk, kvh * hd + i, ref);
             for (int i = 0; i < hd; i++) r.add(f, wv, kvh * hd + i, ref);
-            size_t off = pack(s, r);
-            if (h == 0) { off_qkv[l] = off; layers[l].dt_qkv = r.dtype; }
+            r.pad_to((size_t)(h + 1) * unit_tiles * L3M_TILE);
         }
+        off_qkv[l] = pack(s, r);
+        layers[l].dt_qkv = r.dtype;
         off_wo[l] = pack_matrix(s, f, l3m_file_blk(f, l, "wo"), ref, &layers[l].dt_wo);
         off_up[l] = pack_matrix(s, f, l3m_file_blk(f, l, "w_up"), ref, &layers[l].dt_up);
         off_gate[l] = pack_matrix(s, f, l3m_file_blk(f, l, "w_gate"), ref, &layers[l].dt_gate);
