@@ -32,6 +32,13 @@ struct Ctrl {
 };
 
 enum { kErrNone = 0, kErrTimeout = 1, kErrEpoch = 2 };
+constexpr int kDecodeThreads = 256;   // 8 warps: the register file holds every live value without spilling
+
+// Exchanges between phases. Each has a float data buffer and an arrival counter, both in two halves
+// by step parity. A producer writes its outputs and adds 1 (release) to the counter; a consumer's
+// thread 0 polls the counter (acquire) until every expected arrival of this step is in, then the CTA
+// reads the data once. Counters sit on their own 128-byte lines.
+enum { kXAttn, kXProj, kXH, kXDown, kXTok, kXCount };
 
 struct DecodeArgs {
     int dim, hd, ffn, vocab, ctx, n_heads, n_kv, hpk, n_layers, unit_tiles, grid;
@@ -46,9 +53,11 @@ struct DecodeArgs {
     const float2 *rope;                 // [ctx][hd/2] {cos, sin}; NULL: learned positions
     const uint32_t *elist, *eindex;     // libm expf exception list
     const Role *roles;
-    uint64_t *ex;                       // exchange slots: two halves by parity
-    long long ex_half;                  // slots per half
-    int off_attn, off_proj, off_h, off_down, off_pres, off_tok;
+    float *xd;                          // exchange data, two halves of xd_half floats
+    long long xd_half;
+    int d_attn, d_proj, d_h, d_down, d_tok;   // float offsets within a half
+    uint32_t *ctr;                      // [kXCount][2] counters, 32 words apart
+    int arrivals[kXCount];              // per use: producers (+ every CTA's presence for kXDown)
     const int32_t *prompt;
     int n_prompt, max_new, eos, bos;
     float *logits;                      // [ctx][vocab]
@@ -56,9 +65,11 @@ struct DecodeArgs {
     int32_t *tokens;                    // host-mapped, ctx entries
     int *abort_flag;                    // device: first error code
     unsigned long long timeout_ns;      // per wait
+    unsigned long long *trace;          // optional: [4][ctx][n_layers + 1][16] globaltimer stamps
+    int trace_cta[4];
     // shared memory layout, byte offsets
-    int sm_x, sm_xb, sm_tmp, sm_q8, sm_scale, sm_sum, sm_xf, sm_y, sm_scores, sm_kv, sm_att, sm_red, sm_scratch;
-    int scratch_pairs, smem_bytes;
+    int sm_x, sm_xb, sm_tmp, sm_q8, sm_scale, sm_sum, sm_xf, sm_y, sm_y2, sm_scores, sm_kv, sm_att, sm_red, sm_kvbuf, sm_scratch;
+    int scratch_pairs, smem_bytes, attn_chunk;
 };
 
 }  // namespace l3m

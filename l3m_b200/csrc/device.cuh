@@ -10,39 +10,16 @@ constexpr int kTile = 16;
 constexpr int kQB = 32;
 
 // ---- loads
-// Weights are read-only for a kernel's lifetime: the non-coherent path.
-__device__ __forceinline__ uint4 ld_nc_v4(const void *p) {
-    uint4 v;
-    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
-    return v;
-}
-__device__ __forceinline__ uint32_t ld_nc_u32(const void *p) {
-    uint32_t v;
-    asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(v) : "l"(p));
-    return v;
-}
-__device__ __forceinline__ uint16_t ld_nc_u16(const void *p) {
-    uint16_t v;
-    asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(v) : "l"(p));
-    return v;
-}
-__device__ __forceinline__ uint8_t ld_nc_u8(const void *p) {
-    uint16_t v;
-    asm volatile("ld.global.nc.u8 %0, [%1];" : "=h"(v) : "l"(p));
-    return (uint8_t)v;
-}
+// Weights are read-only for a kernel's lifetime: the non-coherent path, as plain intrinsics so the
+// compiler is free to hoist and batch them.
+__device__ __forceinline__ uint4 ld_nc_v4(const void *p) { return __ldg((const uint4 *)p); }
+__device__ __forceinline__ uint32_t ld_nc_u32(const void *p) { return __ldg((const unsigned int *)p); }
+__device__ __forceinline__ uint16_t ld_nc_u16(const void *p) { return __ldg((const unsigned short *)p); }
+__device__ __forceinline__ uint8_t ld_nc_u8(const void *p) { return __ldg((const unsigned char *)p); }
 // Data other CTAs write during the kernel (KV cache rows): cached in L2 only, never in L1, so a
 // line fetched before a neighbouring row was written cannot be served stale.
-__device__ __forceinline__ uint4 ld_cg_v4(const void *p) {
-    uint4 v;
-    asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
-    return v;
-}
-__device__ __forceinline__ uint16_t ld_cg_u16(const void *p) {
-    uint16_t v;
-    asm volatile("ld.global.cg.u16 %0, [%1];" : "=h"(v) : "l"(p));
-    return v;
-}
+__device__ __forceinline__ uint4 ld_cg_v4(const void *p) { return __ldcg((const uint4 *)p); }
+__device__ __forceinline__ uint16_t ld_cg_u16(const void *p) { return __ldcg((const unsigned short *)p); }
 
 // ---- integer dot of 4 bytes: unsigned weights times signed activations, plus c
 __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {

@@ -25,7 +25,7 @@
 #include "../../include/l3m.h"
 #include "../../include/l3m_kernels.h"
 
-extern "C" int l3m_decode_launch(const l3m::DecodeArgs *a, void *stream);
+extern "C" int l3m_decode_launch(const l3m::DecodeArgs *a, const l3m::DecodeArgs *a_dev, void *stream);
 extern "C" int l3m_decode_occupancy(int smem_bytes);
 extern "C" int l3m_expf_tables(const uint32_t **list, const uint32_t **index);
 
@@ -54,8 +54,13 @@ struct Gpu {
     float2 *rope = nullptr;
     l3m::LayerDev *layers = nullptr;
     l3m::Role *roles = nullptr;
-    uint64_t *ex = nullptr;
-    size_t ex_bytes = 0;
+    l3m::DecodeArgs *args_dev = nullptr;
+    float *xd = nullptr;
+    size_t xd_bytes = 0;
+    uint32_t *flags = nullptr;
+    size_t flags_bytes = 0;
+    unsigned long long *trace = nullptr;
+    size_t trace_bytes = 0;
     int32_t *prompt = nullptr;
     float *logits = nullptr;
     int *abort_flag = nullptr;
@@ -196,6 +201,7 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     }
     const int G = g.sms, dim = m->dim, hd = m->hd, ffn = m->ffn, V = m->vocab, L = m->n_layers;
     if (m->n_heads > G) { fprintf(stderr, "l3m: %d heads exceed the %d SMs of GPU %d\n", m->n_heads, G, g.dev); return false; }
+    if (hd > l3m::kDecodeThreads) { fprintf(stderr, "l3m: head_dim %d above %d is not built\n", hd, l3m::kDecodeThreads); return false; }
 
     // Streamed weights first (one contiguous range for the persisting window), then the rest.
     Stage s;
@@ -312,12 +318,36 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     a.rope = (m->flags & L3M_F_LEARNED_POS) ? nullptr : g.rope;
     if (l3m_expf_tables(&a.elist, &a.eindex)) { fprintf(stderr, "l3m: %s\n", l3m_cuda_error()); return false; }
     a.roles = g.roles;
-    a.off_attn = 0; a.off_proj = dim; a.off_h = 2 * dim; a.off_down = 2 * dim + ffn; a.off_pres = 3 * dim + ffn;
-    a.off_tok = a.off_pres + G;
-    a.ex_half = (a.off_tok + 3 * G + 31) & ~31;
-    g.ex_bytes = (size_t)a.ex_half * 2 * sizeof(uint64_t);
-    if (!cuda_ok(cudaMalloc(&g.ex, g.ex_bytes), "exchange")) return false;
-    a.ex = g.ex;
+    // Exchange buffers: floats in two halves by step parity, one flag per (exchange, parity, CTA).
+    a.d_attn = 0; a.d_proj = dim; a.d_h = 2 * dim; a.d_down = 2 * dim + ffn; a.d_tok = 3 * dim + ffn;
+    a.xd_half = ((long long)a.d_tok + 3 * G + 63) & ~63LL;
+    g.xd_bytes = (size_t)a.xd_half * 2 * sizeof(float);
+    g.flags_bytes = (size_t)l3m::kXCount * 2 * 32 * sizeof(uint32_t);
+    if (!cuda_ok(cudaMalloc(&g.xd, g.xd_bytes), "exchange") || !cuda_ok(cudaMalloc(&g.flags, g.flags_bytes), "counters")) return false;
+    a.xd = g.xd;
+    a.ctr = g.flags;
+    auto count = [&](auto pred) { int n = 0; for (int c = 0; c < G; c++) n += pred(roles[c]); return n; };
+    a.arrivals[l3m::kXAttn] = m->n_heads;
+    a.arrivals[l3m::kXProj] = count([](const l3m::Role &r) { return r.wo0 < r.wo1; });
+    a.arrivals[l3m::kXH] = count([](const l3m::Role &r) { return r.ffn0 < r.ffn1; });
+    a.arrivals[l3m::kXDown] = count([](const l3m::Role &r) { return r.dn0 < r.dn1; }) + G;   // + every CTA's presence
+    a.arrivals[l3m::kXTok] = G;
+    std::vector<int> plist;                                           // CTA ids by role, for the trace picks
+    for (int c = 0; c < G; c++) if (roles[c].head >= 0) plist.push_back(c);
+    for (int i = 0; i < 4; i++) a.trace_cta[i] = -1;
+    if (getenv("L3M_TRACE")) {                                         // phase timestamps of four CTAs
+        int pick[4] = {plist[0], -1, -1, -1};
+        for (int c = 0; c < G; c++) {
+            if (pick[1] < 0 && roles[c].wo0 < roles[c].wo1 && roles[c].head < 0) pick[1] = c;
+            if (pick[2] < 0 && roles[c].ffn0 < roles[c].ffn1 && roles[c].head < 0 && roles[c].wo0 == roles[c].wo1) pick[2] = c;
+            if (pick[3] < 0 && roles[c].head < 0 && roles[c].wo0 == roles[c].wo1 && roles[c].ffn0 == roles[c].ffn1) pick[3] = c;
+        }
+        for (int i = 0; i < 4; i++) a.trace_cta[i] = pick[i];
+        g.trace_bytes = (size_t)4 * m->ctx * (L + 1) * 16 * sizeof(unsigned long long);
+        if (!cuda_ok(cudaMalloc(&g.trace, g.trace_bytes), "trace")) return false;
+        cudaMemset(g.trace, 0, g.trace_bytes);
+        a.trace = g.trace;
+    }
     if (!cuda_ok(cudaMalloc(&g.prompt, (size_t)m->ctx * 4), "prompt")) return false;
     if (!cuda_ok(cudaMalloc(&g.logits, (size_t)m->ctx * V * 4), "logits")) return false;
     cudaMemset(g.logits, 0, (size_t)m->ctx * V * 4);
@@ -340,11 +370,17 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     a.sm_scale = take(nb * 4);
     a.sm_sum = take(nb * 4);
     a.sm_xf = take(mx * 4);
-    a.sm_y = take(std::max(unit_tiles, max_ffn_tiles) * L3M_TILE * 4);
+    int max_tiles = std::max(unit_tiles, max_ffn_tiles);
+    for (int c = 0; c < G; c++)
+        max_tiles = std::max({max_tiles, roles[c].wo1 - roles[c].wo0, roles[c].dn1 - roles[c].dn0, roles[c].voc1 - roles[c].voc0});
+    a.sm_y = take(max_tiles * L3M_TILE * 4);
+    a.sm_y2 = take(max_ffn_tiles * L3M_TILE * 4);
     a.sm_scores = take(std::max(m->ctx, 3 * G) * 4);
     a.sm_kv = take(2 * hd * 2);
     a.sm_att = take(hd * 4);
     a.sm_red = take(64 * 4);
+    a.attn_chunk = std::min(m->ctx, 128);
+    a.sm_kvbuf = take(a.attn_chunk * (hd + 8) * 2);
     a.sm_scratch = take(0);
     const int budget = 200 * 1024;
     a.scratch_pairs = std::min(8192, (budget - off) / 8);
@@ -362,6 +398,7 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     a.tokens = m->tokens_dev;
     if (!cuda_ok(cudaStreamCreateWithFlags(&g.stream, cudaStreamNonBlocking), "stream")) return false;
     if (!cuda_ok(cudaStreamCreateWithFlags(&g.side, cudaStreamNonBlocking), "stream")) return false;
+    if (!cuda_ok(cudaMalloc(&g.args_dev, sizeof(l3m::DecodeArgs)), "args")) return false;
     cudaEventCreate(&g.ev0);
     cudaEventCreate(&g.ev1);
     (void)o;
@@ -472,7 +509,7 @@ L3M_API void l3m_free(l3m_model *m) {
             cudaCtxResetPersistingL2Cache();
             cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, g.prev_limit);
         }
-        cudaFree(g.arena); cudaFree(g.kv); cudaFree(g.rope); cudaFree(g.layers); cudaFree(g.roles); cudaFree(g.ex);
+        cudaFree(g.arena); cudaFree(g.kv); cudaFree(g.rope); cudaFree(g.layers); cudaFree(g.roles); cudaFree(g.args_dev); cudaFree(g.xd); cudaFree(g.flags); cudaFree(g.trace);
         cudaFree(g.prompt); cudaFree(g.logits); cudaFree(g.abort_flag);
         if (g.ev0) cudaEventDestroy(g.ev0);
         if (g.ev1) cudaEventDestroy(g.ev1);
@@ -500,10 +537,11 @@ L3M_API int l3m_generate(l3m_model *m, const int32_t *prompt, int n_prompt, int 
     a.max_new = max_new;
     const double t0 = now_ns();
     cudaMemcpyAsync(g.prompt, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, g.stream);
-    cudaMemsetAsync(g.ex, 0, g.ex_bytes, g.stream);
+    cudaMemsetAsync(g.flags, 0, g.flags_bytes, g.stream);
     cudaMemsetAsync(g.abort_flag, 0, 4, g.stream);
+    cudaMemcpyAsync(g.args_dev, &a, sizeof a, cudaMemcpyHostToDevice, g.stream);
     cudaEventRecord(g.ev0, g.stream);
-    if (l3m_decode_launch(&a, g.stream)) return -1;
+    if (l3m_decode_launch(&a, g.args_dev, g.stream)) return -1;
     cudaEventRecord(g.ev1, g.stream);
     int seen = 0, n_gen = 0, stopped = -1;
     if (on_token) {
@@ -540,6 +578,16 @@ L3M_API int l3m_generate(l3m_model *m, const int32_t *prompt, int n_prompt, int 
     }
     m->logits_pos = last_pos;
     m->cached_pos = -2;
+    if (g.trace) {                                                      // L3M_TRACE: raw stamps for offline analysis
+        std::vector<unsigned long long> t(g.trace_bytes / 8);
+        cudaMemcpy(t.data(), g.trace, g.trace_bytes, cudaMemcpyDeviceToHost);
+        if (FILE *tf = fopen(getenv("L3M_TRACE"), "wb")) {
+            int hdr[8] = {m->ctx, m->n_layers, n_prompt, last_pos, g.args.trace_cta[0], g.args.trace_cta[1], g.args.trace_cta[2], g.args.trace_cta[3]};
+            fwrite(hdr, sizeof hdr, 1, tf);
+            fwrite(t.data(), 8, t.size(), tf);
+            fclose(tf);
+        }
+    }
     float ms = 0;
     cudaEventElapsedTime(&ms, g.ev0, g.ev1);
     m->tok_count += last_pos + 1;

@@ -31,6 +31,7 @@ int fail_msg(const char *msg) {
 
 constexpr int kThreads = 512;
 constexpr int kScratchPairs = 4096;                 // 32 KB of block results per chunk
+constexpr int kAttnChunk = 128;                     // KV rows staged in shared memory at a time
 
 struct VecArg { const float *f32; const uint16_t *bf16; const int8_t *q8; const float *scale; const int32_t *sum; };
 
@@ -67,8 +68,9 @@ __global__ void __launch_bounds__(kThreads) gemv_exact_kernel(int dtype, float *
     float2 *scratch = (float2 *)(smem + prep_smem(k));
     load_prep(dtype, x, k, p);
     const int t0 = (int)((long long)blockIdx.x * ntiles / gridDim.x), t1 = (int)((long long)(blockIdx.x + 1) * ntiles / gridDim.x);
-    float *yo = y + (size_t)t0 * kTile;
-    matvec_exact(dtype, tiles, k, t0, t1, p, scratch, kScratchPairs, [&](int o, float v) { yo[o] = v; });
+    float *ys = (float *)(scratch + kScratchPairs);                    // this CTA's outputs, then to global
+    matvec_exact(dtype, tiles, k, t0, t1, p, scratch, kScratchPairs, ys);
+    for (int o = threadIdx.x; o < (t1 - t0) * kTile; o += blockDim.x) y[(size_t)t0 * kTile + o] = ys[o];
 }
 
 // Fast f32/bf16: one warp per tile; each half warp walks alternate 16-input chunks for its 16 outputs.
@@ -97,30 +99,26 @@ __global__ void __launch_bounds__(kThreads) gemv_fast_kernel(int dtype, float *y
 }
 
 // Exact integer block dots, one warp (q8) or half warp (q4, mxfp4) per (tile, block).
-__global__ void block_dots_kernel(int dtype, int32_t *dots, const uint8_t *tiles, int ntiles, int k, VecArg x) {
-    const int lane = threadIdx.x & 31, nb = k / kQB, items = ntiles * nb, bb = block_bytes(dtype);
+template <int DT>
+__device__ void block_dots_items(int32_t *dots, const uint8_t *tiles, int ntiles, int k, const VecArg &x) {
+    const int nb = k / kQB, bb = block_bytes(DT);
     const size_t tb = (size_t)nb * bb;
-    const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), nw = gridDim.x * (blockDim.x >> 5);
+    const long long n = (long long)ntiles * kTile, items = n * nb;
     const uint32_t *xw = (const uint32_t *)x.q8;
-    if (dtype == DT_Q8) {
-        for (int it = gw; it < items; it += nw) {
-            const int t = it / nb, b = it % nb;
-            const uint8_t *blk = tiles + (size_t)t * tb + (size_t)b * bb;
-            int c;
-            const int d = q8_dot(ld_nc_v4(blk + 32 + lane * 16), lane, xw[b * 8 + (lane >> 2)], x.sum[b], &c);
-            if (!(lane & 4)) dots[((size_t)t * kTile + c) * nb + b] = d;
-        }
-    } else {
-        for (int base = 2 * gw; base < items; base += 2 * nw) {
-            const int it = base + (lane >> 4), itc = it < items ? it : base;
-            const int t = itc / nb, b = itc % nb;
-            const uint8_t *blk = tiles + (size_t)t * tb + (size_t)b * bb;
-            const uint4 w = ld_nc_v4(blk + (dtype == DT_MX ? 16 : 32) + (lane & 15) * 16);
-            int c;
-            const int d = dtype == DT_MX ? q4_dot<true>(w, lane & 15, xw + b * 8, x.sum[b], &c) : q4_dot<false>(w, lane & 15, xw + b * 8, x.sum[b], &c);
-            if (it < items) dots[((size_t)t * kTile + c) * nb + b] = d;
-        }
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < items; i += (long long)gridDim.x * blockDim.x) {
+        const int b = (int)(i / n);
+        const long long o = i - (long long)b * n;
+        QLoad q;
+        qload<DT>(q, tiles + (size_t)(o >> 4) * tb + (size_t)b * bb, (int)(o & 15));
+        dots[o * nb + b] = qdot<DT>(q, xw + 8 * b, x.sum[b]);
     }
+}
+
+// Exact integer block dots: one thread per (output, block).
+__global__ void block_dots_kernel(int dtype, int32_t *dots, const uint8_t *tiles, int ntiles, int k, VecArg x) {
+    if (dtype == DT_Q8) block_dots_items<DT_Q8>(dots, tiles, ntiles, k, x);
+    else if (dtype == DT_Q4) block_dots_items<DT_Q4>(dots, tiles, ntiles, k, x);
+    else block_dots_items<DT_MX>(dots, tiles, ntiles, k, x);
 }
 
 // Unpack: one thread per (output, block).
@@ -172,14 +170,14 @@ __global__ void __launch_bounds__(kThreads) attend_kernel(float *out, const floa
                                                           int stride, const uint32_t *elist, const uint32_t *eindex) {
     extern __shared__ __align__(16) unsigned char smem[];
     float *qs = (float *)smem, *o = qs + hd, *red = o + hd, *scores = red + 64;
-    uint16_t *kcur = (uint16_t *)(scores + ((pos + 4) & ~3)), *vcur = kcur + hd;
+    uint16_t *kcur = (uint16_t *)(scores + ((pos + 4) & ~3)), *vcur = kcur + hd, *kvbuf = vcur + hd;
     for (int i = threadIdx.x; i < hd; i += blockDim.x) {
         qs[i] = q[i];
         kcur[i] = k[(size_t)pos * stride + i];
         vcur[i] = v[(size_t)pos * stride + i];
     }
     __syncthreads();
-    attend_exact(qs, k, v, stride, kcur, vcur, pos, hd, scores, o, red, elist, eindex);
+    attend_exact(qs, k, v, stride, kcur, vcur, pos, hd, scores, o, red, elist, eindex, kvbuf, kAttnChunk);
     for (int i = threadIdx.x; i < hd; i += blockDim.x) out[i] = o[i];
 }
 
@@ -236,7 +234,8 @@ L3M_API int l3m_gemv_dev(int exact, int dtype, float *y, const void *tiles, int 
     if (!exact && dtype <= DT_BF16) {
         gemv_fast_kernel<<<grid_for((ntiles + 15) / 16), kThreads, 0, s>>>(dtype, y, (const uint8_t *)tiles, ntiles, k, vec_arg(x));
     } else {
-        size_t smem = prep_smem(k) + (dtype >= DT_Q8 ? (size_t)kScratchPairs * sizeof(float2) : 0);
+        const int per_cta = (ntiles + grid_for(ntiles) - 1) / grid_for(ntiles);
+        size_t smem = prep_smem(k) + (size_t)kScratchPairs * sizeof(float2) + (size_t)per_cta * kTile * 4;
         if (dtype >= DT_Q8 && (size_t)(k / kQB) * kTile > (size_t)kScratchPairs) return fail_msg("l3m_gemv_dev: k too large");
         cudaError_t e = cudaFuncSetAttribute(gemv_exact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return fail(e, "l3m_gemv_dev");
@@ -287,7 +286,8 @@ L3M_API int l3m_attend_dev(float *out, const float *q, const uint16_t *k, const 
     if (head_dim % 8 || head_dim <= 0 || pos < 0 || stride < head_dim) return fail_msg("l3m_attend_dev: bad arguments");
     const uint32_t *list, *index;
     if (l3m_expf_tables(&list, &index)) return -1;
-    size_t smem = (size_t)head_dim * 8 + 64 * 4 + (size_t)((pos + 4) & ~3) * 4 + (size_t)head_dim * 4 + 16;
+    size_t smem = (size_t)head_dim * 8 + 64 * 4 + (size_t)((pos + 4) & ~3) * 4 + (size_t)head_dim * 4 + 16 +
+                  (size_t)kAttnChunk * (head_dim + 8) * 2;
     cudaError_t e = cudaFuncSetAttribute(attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return fail(e, "l3m_attend_dev");
     attend_kernel<<<1, kThreads, smem, (cudaStream_t)stream>>>(out, q, k, v, pos, head_dim, stride, list, index);

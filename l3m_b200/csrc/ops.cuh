@@ -4,7 +4,7 @@
 // path rounds (its compiled arithmetic is restated and pinned in the oracle; the same order is
 // written here):
 //   matvec, quantised:  acc = fma(RN(sx[b] * d[c]), (float)dot[b][c], acc) over blocks b in order,
-//                       where dot is the exact integer block dot (any order);
+//                       where dot is the exact integer block dot (computed by any thread);
 //   matvec, bf16:       acc = fma(w_i, x_i, acc) over inputs in order (products are exact);
 //   matvec, f32:        acc = acc + RN(w_i x_i) up to split(K), then fma — split(n) = n & ~7, plus 4
 //                       more when n % 8 >= 4 (the reference compiler's 8- then 4-wide vector loop);
@@ -41,7 +41,7 @@ struct Prep {
 };
 
 // ---- prepare (reference src/pack.c:101-122)
-__device__ inline void prepare(int dtype, const float *x, int n, const Prep &p) {
+static __device__ __noinline__ void prepare(int dtype, const float *x, int n, const Prep p) {
     const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31, warp = tid >> 5, nw = nth >> 5;
     if (dtype == DT_F32) {
         for (int i = tid; i < n; i += nth) p.xf[i] = x[i];
@@ -66,33 +66,13 @@ __device__ inline void prepare(int dtype, const float *x, int n, const Prep &p) 
 }
 
 // ---- quantised block dots. Tile layout per 32-input block (reference src/kernels.h:1-10):
-// q8: d[16] f16 then q[8 groups][16 lanes][4] (value + 128); q4/mxfp4: scales then
-// q[4 groups][16 lanes][4 bytes], byte j of a lane holding inputs 8g+j (low) and 8g+4+j (high).
-// Each result is written as {RN(sx[b] * d[c]), (float)dot} for the fp32 chain.
-
-// One q8 block of one tile by a whole warp: lane l loads 16 bytes = group l/4, outputs 4(l%4)..+3.
-// Returns the exact integer dot of output *c (offset removed); lanes with bit 2 clear hold each
-// output once.
-__device__ __forceinline__ int q8_dot(uint4 w, int lane, uint32_t xw, int32_t xsum, int *c) {
-    int p0 = dp4a_us(w.x, xw, 0), p1 = dp4a_us(w.y, xw, 0), p2 = dp4a_us(w.z, xw, 0), p3 = dp4a_us(w.w, xw, 0);
-    const bool b4 = lane & 16, b3 = lane & 8;
-    // Reduce the 8 groups (lane bits 4,3,2) while spreading the 4 outputs over those bits.
-    int k0 = (b4 ? p2 : p0) + __shfl_xor_sync(0xffffffffu, b4 ? p0 : p2, 16);
-    int k1 = (b4 ? p3 : p1) + __shfl_xor_sync(0xffffffffu, b4 ? p1 : p3, 16);
-    int k = (b3 ? k1 : k0) + __shfl_xor_sync(0xffffffffu, b3 ? k0 : k1, 8);
-    k += __shfl_xor_sync(0xffffffffu, k, 4);
-    *c = 4 * (lane & 3) + (b4 ? 2 : 0) + (b3 ? 1 : 0);
-    return k - 128 * xsum;
-}
-
-__device__ __forceinline__ void q8_block(uint4 w, const uint8_t *blk, int lane, uint32_t xw, int32_t xsum, float xscale, float2 *dst) {
-    int c;
-    const int dot = q8_dot(w, lane, xw, xsum, &c);
-    if (!(lane & 4)) {
-        float d = l3m_f16_to_f32(ld_nc_u16(blk + 2 * c));
-        dst[c] = make_float2(__fmul_rn(xscale, d), __int2float_rn(dot));
-    }
-}
+//   q8:    d[16] f16, then q[8 groups][16 rows][4] u8 (value + 128): group g holds inputs 4g..4g+3
+//   q4:    d[16] f16, then q[4 groups][16 rows][4] bytes: byte j of group g holds inputs 8g+j (low
+//          nibble) and 8g+4+j (high nibble)
+//   mxfp4: e[16] e8m0, then codes as q4
+// One row's block is 8 (q8) or 4 (q4, mxfp4) words 64 bytes apart, so one thread computes a whole
+// exact block dot with dp4a and no cross-lane traffic, and the 16 rows of a tile read one 64-byte
+// run per group.
 
 // The 16-entry mxfp4 table (doubled e2m1 + 16) applied to 4 nibble selectors in s[15:0].
 __device__ __forceinline__ uint32_t mx_lut16(uint32_t s) {
@@ -103,154 +83,164 @@ __device__ __forceinline__ uint32_t mx_lut16(uint32_t s) {
     return (pos & ~m) | (neg & m);
 }
 
-// One 4-bit block of one tile by a half warp: t = lane % 16 loads 16 bytes = group t/4, outputs
-// 4(t%4)..+3. Returns the exact integer dot of output *c (offset removed); every t holds a distinct output.
-template <bool MX>
-__device__ __forceinline__ int q4_dot(uint4 w, int t, const uint32_t *xw, int32_t xsum, int *c) {
-    const int g = t >> 2;
-    const uint32_t xl = xw[2 * g], xh = xw[2 * g + 1];
-    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-    int p[4];
-    if (MX) {
-        const uint32_t xa = prmt(xl, xh, 0x5140u), xb = prmt(xl, xh, 0x7362u);   // inputs 0 4 1 5 and 2 6 3 7
+// One row's block, loaded ahead of use: its words and its scale bits.
+struct QLoad { uint32_t w[8]; uint32_t d; };
+
+template <int DT>
+__device__ __forceinline__ void qload(QLoad &q, const uint8_t *blk, int c) {
+    if (DT == DT_Q8) {
+        const uint32_t *g = (const uint32_t *)(blk + 32) + c;
 #pragma unroll
-        for (int j = 0; j < 4; j++) p[j] = dp4a_us(mx_lut16(ww[j]), xa, dp4a_us(mx_lut16(ww[j] >> 16), xb, 0));
+        for (int j = 0; j < 8; j++) q.w[j] = __ldg(g + 16 * j);
+        q.d = ld_nc_u16(blk + 2 * c);
+    } else if (DT == DT_Q4) {
+        const uint32_t *g = (const uint32_t *)(blk + 32) + c;
+#pragma unroll
+        for (int j = 0; j < 4; j++) q.w[j] = __ldg(g + 16 * j);
+        q.d = ld_nc_u16(blk + 2 * c);
+    } else {
+        const uint32_t *g = (const uint32_t *)(blk + 16) + c;
+#pragma unroll
+        for (int j = 0; j < 4; j++) q.w[j] = __ldg(g + 16 * j);
+        q.d = ld_nc_u8(blk + c);
+    }
+}
+
+// Exact integer dot of a loaded block with the block's 8 prepared activation words xw[0..7], offset
+// removed (the reference's acc_i - offset * sum, src/kernels_scalar.c:37-43, 57-71).
+template <int DT>
+__device__ __forceinline__ int qdot(const QLoad &q, const uint32_t *xw, int32_t xsum) {
+    int s = 0, t = 0;
+    if (DT == DT_Q8) {
+#pragma unroll
+        for (int j = 0; j < 8; j += 2) { s = dp4a_us(q.w[j], xw[j], s); t = dp4a_us(q.w[j + 1], xw[j + 1], t); }
+        return s + t - 128 * xsum;
+    } else if (DT == DT_Q4) {
+#pragma unroll
+        for (int g = 0; g < 4; g++) {
+            s = dp4a_us(q.w[g] & 0x0F0F0F0Fu, xw[2 * g], s);
+            t = dp4a_us((q.w[g] >> 4) & 0x0F0F0F0Fu, xw[2 * g + 1], t);
+        }
+        return s + t - 8 * xsum;
     } else {
 #pragma unroll
-        for (int j = 0; j < 4; j++) p[j] = dp4a_us(ww[j] & 0x0F0F0F0Fu, xl, dp4a_us((ww[j] >> 4) & 0x0F0F0F0Fu, xh, 0));
-    }
-    const bool b3 = t & 8, b2 = t & 4;
-    int k0 = (b3 ? p[2] : p[0]) + __shfl_xor_sync(0xffffffffu, b3 ? p[0] : p[2], 8);
-    int k1 = (b3 ? p[3] : p[1]) + __shfl_xor_sync(0xffffffffu, b3 ? p[1] : p[3], 8);
-    int k = (b2 ? k1 : k0) + __shfl_xor_sync(0xffffffffu, b2 ? k0 : k1, 4);
-    *c = 4 * (t & 3) + (b3 ? 2 : 0) + (b2 ? 1 : 0);
-    return k - (MX ? 16 : 8) * xsum;
-}
-
-template <bool MX>
-__device__ __forceinline__ void q4_block(uint4 w, const uint8_t *blk, int t, const uint32_t *xw, int32_t xsum, float xscale,
-                                         float2 *dst, bool valid) {
-    int c;
-    const int dot = q4_dot<MX>(w, t, xw, xsum, &c);
-    if (valid) {
-        float d = MX ? l3m_e8m0_half(ld_nc_u8(blk + c)) : l3m_f16_to_f32(ld_nc_u16(blk + 2 * c));
-        dst[c] = make_float2(__fmul_rn(xscale, d), __int2float_rn(dot));
+        for (int g = 0; g < 4; g++) {
+            const uint32_t xl = xw[2 * g], xh = xw[2 * g + 1];
+            // bytes 0,1 of the word select inputs 0 4 1 5 of the group; bytes 2,3 select 2 6 3 7
+            s = dp4a_us(mx_lut16(q.w[g]), prmt(xl, xh, 0x5140u), s);
+            t = dp4a_us(mx_lut16(q.w[g] >> 16), prmt(xl, xh, 0x7362u), t);
+        }
+        return s + t - 16 * xsum;
     }
 }
 
-// Block dots of tiles [c0, c0 + ntl) into scratch[(tile * nb + b) * 16 + c]; four blocks in flight per warp.
-__device__ inline void block_dots(int dtype, const uint8_t *tiles, int k, int c0, int ntl, const Prep &p, float2 *scratch) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    const int nb = k / kQB, items = ntl * nb, bb = block_bytes(dtype);
+template <int DT>
+__device__ __forceinline__ float qscale(uint32_t d) { return DT == DT_MX ? l3m_e8m0_half((uint8_t)d) : l3m_f16_to_f32((uint16_t)d); }
+
+// Outputs [0, n_out) of the tiles at `tiles`, exact. The (output, block) items of a chunk of outputs
+// are dealt to threads output-fastest, kQU blocks in flight per thread; each stores {RN(sx[b] * d),
+// (float)dot} at scratch[b * m + o]. Then one thread per output runs the fp32 chain in block order.
+constexpr int kQU = 4;
+template <int DT>
+__device__ void qmatvec(const uint8_t *tiles, int k, int n_out, const Prep &p, float2 *scratch, int scratch_pairs, float *y) {
+    const int tid = threadIdx.x, nth = blockDim.x, nb = k / kQB, bb = block_bytes(DT);
     const size_t tb = (size_t)nb * bb;
     const uint32_t *xw = (const uint32_t *)p.q8;
-    if (dtype == DT_Q8) {
-        for (int base = warp; base < items; base += 4 * nw) {
-            uint4 w[4];
-            const uint8_t *blk[4];
+    int chunk = scratch_pairs / nb;
+    if (chunk > n_out) chunk = n_out;
+    for (int o0 = 0; o0 < n_out; o0 += chunk) {
+        const int m = min(chunk, n_out - o0), items = m * nb;
+        // item i = b * m + o; this thread starts at i = tid and steps by nth
+        int b = tid / m, o = tid - b * m;
+        const int db = nth / m, dor = nth - db * m;
+        const uint8_t *base = tiles + (size_t)o0 / kTile * tb;   // o0 is a multiple of 16 unless chunk is not
+        const int oc = o0 % kTile;
+        for (int i = tid; i < items; i += kQU * nth) {
+            QLoad q[kQU];
+            int bs[kQU], os[kQU];
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
-                int it = base + u * nw;
-                if (it < items) {
-                    int ti = it / nb, b = it - ti * nb;
-                    blk[u] = tiles + (size_t)(c0 + ti) * tb + (size_t)b * bb;
-                    w[u] = ld_nc_v4(blk[u] + 32 + lane * 16);
+            for (int u = 0; u < kQU; u++) {
+                bs[u] = b; os[u] = o;
+                if (i + u * nth < items) {
+                    const int oo = o + oc;
+                    qload<DT>(q[u], base + (size_t)(oo >> 4) * tb + (size_t)b * bb, oo & 15);
                 }
+                o += dor; b += db;
+                if (o >= m) { o -= m; b++; }
             }
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
-                int it = base + u * nw;
-                if (it < items) {
-                    int ti = it / nb, b = it - ti * nb;
-                    q8_block(w[u], blk[u], lane, xw[b * 8 + (lane >> 2)], p.sum[b], p.scale[b], scratch + ((size_t)ti * nb + b) * kTile);
+            for (int u = 0; u < kQU; u++) {
+                if (i + u * nth < items) {
+                    const int dot = qdot<DT>(q[u], xw + 8 * bs[u], p.sum[bs[u]]);
+                    scratch[(size_t)bs[u] * m + os[u]] = make_float2(__fmul_rn(p.scale[bs[u]], qscale<DT>(q[u].d)), __int2float_rn(dot));
                 }
             }
         }
-    } else {
-        const int half = lane >> 4, t = lane & 15, sb = dtype == DT_MX ? 16 : 32;
-        for (int base = 2 * warp; base < items; base += 8 * nw) {
-            uint4 w[4];
-            const uint8_t *blk[4];
-            int bs[4], tis[4];
-            bool ok[4];
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                int it0 = base + 2 * u * nw;                  // both halves agree on whether to run
-                int it = it0 + half;
-                ok[u] = it < items;
-                int itc = ok[u] ? it : (it0 < items ? it0 : 0);
-                tis[u] = itc / nb;
-                bs[u] = itc - tis[u] * nb;
-                blk[u] = tiles + (size_t)(c0 + tis[u]) * tb + (size_t)bs[u] * bb;
-                if (it0 < items) w[u] = ld_nc_v4(blk[u] + sb + t * 16);
+        __syncthreads();
+        for (int oo = tid; oo < m; oo += nth) {
+            const float2 *r = scratch + oo;
+            float acc = 0.0f;
+#pragma unroll 6
+            for (int bb2 = 0; bb2 < nb; bb2++) {
+                const float2 v = r[(size_t)bb2 * m];
+                acc = __fmaf_rn(v.x, v.y, acc);
             }
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                if (base + 2 * u * nw >= items) continue;     // uniform across the warp
-                float2 *dst = scratch + ((size_t)tis[u] * nb + bs[u]) * kTile;
-                if (dtype == DT_MX) q4_block<true>(w[u], blk[u], t, xw + bs[u] * 8, p.sum[bs[u]], p.scale[bs[u]], dst, ok[u]);
-                else q4_block<false>(w[u], blk[u], t, xw + bs[u] * 8, p.sum[bs[u]], p.scale[bs[u]], dst, ok[u]);
-            }
+            y[o0 + oo] = acc;
         }
+        __syncthreads();
     }
 }
 
-// y = tiles[t0, t1) . x for one CTA, exact. out(o, value) receives output o in [0, 16 (t1 - t0)).
-// scratch holds scratch_pairs float2 (quantised dtypes; at least k/32 * 16).
-template <class Out>
-__device__ void matvec_exact(int dtype, const uint8_t *tiles, int k, int t0, int t1, const Prep &p, float2 *scratch,
-                             int scratch_pairs, Out out) {
+// y = tiles[t0, t1) . x for one CTA, exact: y[o] for o in [0, 16 (t1 - t0)) (shared memory).
+// scratch holds scratch_pairs float2 (quantised dtypes; at least k/32).
+static __device__ __noinline__ void matvec_exact(int dtype, const uint8_t *tiles, int k, int t0, int t1, const Prep p, float2 *scratch,
+                                                 int scratch_pairs, float *y) {
     const int tid = threadIdx.x, nth = blockDim.x;
     if (t1 <= t0) return;
-    if (dtype == DT_F32 || dtype == DT_BF16) {
-        const size_t tb = tile_bytes(dtype, k);
-        const int n = (t1 - t0) * kTile, split = fused_from(k);
-        for (int o = tid; o < n; o += nth) {
-            const uint8_t *tile = tiles + (size_t)(t0 + (o >> 4)) * tb;
-            const int c = o & 15;
-            float acc = 0.0f;
-            if (dtype == DT_BF16) {
-                const uint32_t *w = (const uint32_t *)tile + c;
-#pragma unroll 8
-                for (int q = 0; q < k / 2; q++) {
-                    uint32_t v = ld_nc_u32(w + (size_t)q * kTile);
-                    acc = __fmaf_rn(l3m_bits_f32(v << 16), p.xf[2 * q], acc);
-                    acc = __fmaf_rn(l3m_bits_f32(v & 0xFFFF0000u), p.xf[2 * q + 1], acc);
+    const size_t tb = tile_bytes(dtype, k);
+    const uint8_t *base = tiles + (size_t)t0 * tb;
+    const int n = (t1 - t0) * kTile;
+    if (dtype == DT_Q8) { qmatvec<DT_Q8>(base, k, n, p, scratch, scratch_pairs, y); return; }
+    if (dtype == DT_Q4) { qmatvec<DT_Q4>(base, k, n, p, scratch, scratch_pairs, y); return; }
+    if (dtype == DT_MX) { qmatvec<DT_MX>(base, k, n, p, scratch, scratch_pairs, y); return; }
+    // f32 / bf16 (tiles [K][16] f32, [K/2][16][2] bf16): one thread per output walks its row in input
+    // order, the reference's chain.
+    const int split = fused_from(k);
+    for (int o = tid; o < n; o += nth) {
+        const uint8_t *tile = base + (size_t)(o >> 4) * tb;
+        const int c = o & 15;
+        float acc = 0.0f;
+        if (dtype == DT_BF16) {
+            const uint32_t *w = (const uint32_t *)tile + c;
+            int q = 0;
+            for (; q + 8 <= k / 2; q += 8) {
+                uint32_t v[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) v[j] = __ldg(w + (size_t)(q + j) * kTile);
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    acc = __fmaf_rn(l3m_bits_f32(v[j] << 16), p.xf[2 * (q + j)], acc);
+                    acc = __fmaf_rn(l3m_bits_f32(v[j] & 0xFFFF0000u), p.xf[2 * (q + j) + 1], acc);
                 }
-            } else {
-                const float *w = (const float *)tile + c;
+            }
+            for (; q < k / 2; q++) {
+                const uint32_t v = __ldg(w + (size_t)q * kTile);
+                acc = __fmaf_rn(l3m_bits_f32(v << 16), p.xf[2 * q], acc);
+                acc = __fmaf_rn(l3m_bits_f32(v & 0xFFFF0000u), p.xf[2 * q + 1], acc);
+            }
+        } else {
+            const float *w = (const float *)tile + c;
 #pragma unroll 8
-                for (int i = 0; i < split; i++) acc = __fadd_rn(acc, __fmul_rn(__ldg(w + (size_t)i * kTile), p.xf[i]));
-                for (int i = split; i < k; i++) acc = __fmaf_rn(__ldg(w + (size_t)i * kTile), p.xf[i], acc);
-            }
-            out(o, acc);
+            for (int i = 0; i < split; i++) acc = __fadd_rn(acc, __fmul_rn(__ldg(w + (size_t)i * kTile), p.xf[i]));
+            for (int i = split; i < k; i++) acc = __fmaf_rn(__ldg(w + (size_t)i * kTile), p.xf[i], acc);
         }
-        __syncthreads();
-        return;
+        y[o] = acc;
     }
-    const int nb = k / kQB;
-    int chunk = scratch_pairs / (nb * kTile);
-    if (chunk < 1) chunk = 1;
-    for (int c0 = t0; c0 < t1; c0 += chunk) {
-        const int ntl = min(t1 - c0, chunk);
-        block_dots(dtype, tiles, k, c0, ntl, p, scratch);
-        __syncthreads();
-        for (int o = tid; o < ntl * kTile; o += nth) {
-            const float2 *s = scratch + (size_t)(o >> 4) * nb * kTile + (o & 15);
-            float acc = 0.0f;
-#pragma unroll 4
-            for (int b = 0; b < nb; b++) {
-                float2 v = s[(size_t)b * kTile];
-                acc = __fmaf_rn(v.x, v.y, acc);
-            }
-            out((c0 - t0) * kTile + o, acc);
-        }
-        __syncthreads();
-    }
+    __syncthreads();
 }
 
 // ---- rmsnorm (reference src/ops.c:13-18). tmp: n floats of shared scratch; red: one float.
-__device__ inline void rmsnorm_exact(const float *x, const float *w, int n, float eps, float *y, float *tmp, float *red) {
+static __device__ __noinline__ void rmsnorm_exact(const float *x, const float *w, int n, float eps, float *y, float *tmp, float *red) {
     const int tid = threadIdx.x, nth = blockDim.x, split = fused_from(n);
     for (int i = tid; i < split; i += nth) tmp[i] = __fmul_rn(x[i], x[i]);
     __syncthreads();
@@ -296,26 +286,40 @@ __device__ __forceinline__ uint4 ld_row8(const uint16_t *p, bool vec) {
     return make_uint4(h[0] | (uint32_t)h[1] << 16, h[2] | (uint32_t)h[3] << 16, h[4] | (uint32_t)h[5] << 16, h[6] | (uint32_t)h[7] << 16);
 }
 
-__device__ inline void attend_exact(const float *q, const uint16_t *kc, const uint16_t *vc, int stride, const uint16_t *kcur,
+static __device__ __noinline__ void attend_exact(const float *q, const uint16_t *kc, const uint16_t *vc, int stride, const uint16_t *kcur,
                                     const uint16_t *vcur, int pos, int hd, float *scores, float *out, float *red,
-                                    const uint32_t *elist, const uint32_t *eindex) {
+                                    const uint32_t *elist, const uint32_t *eindex, uint16_t *kvbuf, int chunk) {
     const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31, warp = tid >> 5;
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
-    const bool vec = stride % 8 == 0 && ((uintptr_t)kc & 15) == 0;
-    for (int t = tid; t <= pos; t += nth) {
-        float dot = 0.0f;
-        for (int i = 0; i < hd; i += 8) {
-            uint4 v = t == pos ? *(const uint4 *)(kcur + i) : ld_row8(kc + (size_t)t * stride + i, vec);
-            const uint32_t u[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                dot = __fadd_rn(dot, __fmul_rn(q[i + 2 * j], l3m_bits_f32(u[j] << 16)));
-                dot = __fadd_rn(dot, __fmul_rn(q[i + 2 * j + 1], l3m_bits_f32(u[j] & 0xFFFF0000u)));
-            }
+    const bool vec = stride % 8 == 0 && ((uintptr_t)kc & 15) == 0 && ((uintptr_t)vc & 15) == 0;
+    const int rs = hd + 8;                                   // padded row stride in the staging buffer (elements)
+    // Rows 0..pos-1 come through shared memory in chunks: coalesced 16-byte loads, then each thread
+    // walks its own row (scores) or its own column (value mix) out of the staging buffer.
+    for (int c0 = 0; c0 <= pos; c0 += chunk) {
+        const int n = min(chunk, pos + 1 - c0);
+#pragma unroll 4
+        for (int e = tid; e < n * (hd / 8); e += nth) {
+            const int r = e / (hd / 8), i = (e - r * (hd / 8)) * 8, t = c0 + r;
+            const uint4 v = t == pos ? *(const uint4 *)(kcur + i) : ld_row8(kc + (size_t)t * stride + i, vec);
+            *(uint4 *)(kvbuf + r * rs + i) = v;
         }
-        scores[t] = __fmul_rn(dot, scale);
+        __syncthreads();
+        for (int r = tid; r < n; r += nth) {
+            const uint16_t *row = kvbuf + r * rs;
+            float dot = 0.0f;
+            for (int i = 0; i < hd; i += 8) {
+                const uint4 v = *(const uint4 *)(row + i);
+                const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    dot = __fadd_rn(dot, __fmul_rn(q[i + 2 * j], l3m_bits_f32(u[j] << 16)));
+                    dot = __fadd_rn(dot, __fmul_rn(q[i + 2 * j + 1], l3m_bits_f32(u[j] & 0xFFFF0000u)));
+                }
+            }
+            scores[c0 + r] = __fmul_rn(dot, scale);
+        }
+        __syncthreads();
     }
-    __syncthreads();
     // The reference takes the running maximum from scores[0] with a strict >: NaN scores after the
     // first are skipped, a NaN first score stays. The maximum of the rest is order-free.
     float m = -INFINITY;
@@ -341,12 +345,23 @@ __device__ inline void attend_exact(const float *q, const uint16_t *kc, const ui
     const float sum = red[32];
     for (int t = tid; t <= pos; t += nth) scores[t] = __fdiv_rn(scores[t], sum);
     __syncthreads();
-    for (int i = tid; i < hd; i += nth) {
-        float acc = 0.0f;
+    float acc = 0.0f;                                        // thread i < hd: output element i
+    for (int c0 = 0; c0 <= pos; c0 += chunk) {
+        const int n = min(chunk, pos + 1 - c0);
+#pragma unroll 4
+        for (int e = tid; e < n * (hd / 8); e += nth) {
+            const int r = e / (hd / 8), i = (e - r * (hd / 8)) * 8, t = c0 + r;
+            const uint4 v = t == pos ? *(const uint4 *)(vcur + i) : ld_row8(vc + (size_t)t * stride + i, vec);
+            *(uint4 *)(kvbuf + r * rs + i) = v;
+        }
+        __syncthreads();
+        if (tid < hd) {
 #pragma unroll 8
-        for (int t = 0; t < pos; t++) acc = __fmaf_rn(scores[t], l3m_bf16_to_f32(ld_cg_u16(vc + (size_t)t * stride + i)), acc);
-        out[i] = __fmaf_rn(scores[pos], l3m_bf16_to_f32(vcur[i]), acc);
+            for (int r = 0; r < n; r++) acc = __fmaf_rn(scores[c0 + r], l3m_bf16_to_f32(kvbuf[r * rs + tid]), acc);
+        }
+        __syncthreads();
     }
+    for (int i = tid; i < hd; i += nth) out[i] = acc;
     __syncthreads();
 }
 
