@@ -66,6 +66,15 @@ L3M_API void   l3m_vec_prepare(l3m_vec *v, int dtype, const float *x, int n, voi
 
 // y = tiles . x on the device. exact 1: the sm100a table's order; 0: sm100a-fast.
 L3M_API int l3m_gemv_dev(int exact, int dtype, float *y, const void *tiles, int ntiles, int k, const l3m_vec *x, void *stream);
+// The exact quantised matvec (the same y as l3m_gemv_dev with exact = 1, bit for bit) for callers
+// that must not allocate device memory, such as a host whose framework owns the device's memory
+// pool, or a decode loop where the implicit device synchronisation of cudaMalloc/cudaFree would
+// stall other streams. No counterpart in the reference. K is split across every SM through one
+// fixed 4 MiB device buffer inside this library: q8_0/q4_0/mxfp4 only, at most 524,288 block
+// results per call (ntiles*16*k/32), larger calls return -1 and launch nothing. The buffer is
+// shared by all calls on a device, so overlapping calls (two streams or threads) race and must be
+// serialised. The first call on each device looks the buffer up; make it before any stream capture.
+L3M_API int l3m_gemv_splitk_dev(int dtype, float *y, const void *tiles, int ntiles, int k, const l3m_vec *x, void *stream);
 // Prepare x[0..n) for dtype on the device, as l3m_vec_prepare. scratch (device) >= 2n + n/4 bytes.
 L3M_API int l3m_vec_prepare_dev(int dtype, l3m_vec *out, const float *x, int n, void *scratch, void *stream);
 // The exact integer part of each quantised kernel: dots[(t*16 + c)*(k/32) + b] = sum_i w*q8_x over block b

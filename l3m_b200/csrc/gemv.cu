@@ -221,6 +221,10 @@ extern "C" int l3m_expf_tables(const uint32_t **list, const uint32_t **index) {
     return 0;
 }
 
+// Error text for the other entry-point files of this library (not exported).
+extern "C" int l3m_error_msg(const char *msg) { return fail_msg(msg); }
+extern "C" int l3m_error_cuda(int e, const char *what) { return fail((cudaError_t)e, what); }
+
 extern "C" {
 
 L3M_API const char *l3m_cuda_error(void) { return g_err; }
