@@ -25,8 +25,9 @@
 namespace l3m {
 
 struct Smem {
-    float *x, *xb, *tmp, *y, *att2, *scores, *att, *red;
-    uint16_t *kcur, *vcur, *kvbuf;
+    float *x, *xb, *tmp, *y, *att2, *scores, *att, *red, *wa, *wf, *wh;
+    float2 *rope;
+    uint16_t *kcur, *vcur, *kvbuf, *vtbuf;
     float2 *scratch;
     Prep prep;
 };
@@ -41,9 +42,14 @@ __device__ __forceinline__ Smem carve(unsigned char *base, const DecodeArgs &a) 
     s.scores = (float *)(base + a.sm_scores);
     s.att = (float *)(base + a.sm_att);
     s.red = (float *)(base + a.sm_red);
+    s.wa = (float *)(base + a.sm_wa);
+    s.wf = (float *)(base + a.sm_wf);
+    s.wh = (float *)(base + a.sm_wh);
+    s.rope = (float2 *)(base + a.sm_rope);
     s.kcur = (uint16_t *)(base + a.sm_kv);
     s.vcur = s.kcur + a.hd;
     s.kvbuf = (uint16_t *)(base + a.sm_kvbuf);
+    s.vtbuf = (uint16_t *)(base + a.sm_vt);
     s.scratch = (float2 *)(base + a.sm_scratch);
     s.prep.q8 = (int8_t *)(base + a.sm_q8);
     s.prep.scale = (float *)(base + a.sm_scale);
@@ -167,7 +173,7 @@ __device__ __noinline__ void embed_row(const DecodeArgs &a, int tok, float *x) {
 __device__ __noinline__ void phase_attention(const DecodeArgs &a, const LayerDev &L, const Role &role, int pos, float *attn, Smem &s,
                                              int tslot, int l) {
     const int tid = threadIdx.x, nth = blockDim.x, hd = a.hd, h = role.head, kvh = h / a.hpk;
-    rmsnorm_exact(s.x, L.attn_norm, a.dim, a.eps, s.xb, s.tmp, s.red);
+    rmsnorm_exact(s.x, s.wa, a.dim, a.eps, s.xb, s.tmp, s.red);
     trace(a, tslot, pos, l, 8);
     prepare(L.dt_qkv, s.xb, a.dim, s.prep);
     trace(a, tslot, pos, l, 9);
@@ -184,32 +190,49 @@ __device__ __noinline__ void phase_attention(const DecodeArgs &a, const LayerDev
         __syncthreads();
     }
     if (a.rope) {
-        rope_exact(y, hd, a.rope + (size_t)pos * (hd / 2));
-        rope_exact(y + hd, hd, a.rope + (size_t)pos * (hd / 2));
+        rope_exact(y, hd, s.rope);
+        rope_exact(y + hd, hd, s.rope);
     }
-    uint16_t *kc = L.kc + (size_t)kvh * a.ctx * hd, *vc = L.vc + (size_t)kvh * a.ctx * hd;
+    uint16_t *kc = L.kc + (size_t)kvh * a.ctx * hd, *vc = L.vc + (size_t)kvh * hd * a.vstride;
     for (int i = tid; i < hd; i += nth) {
         const uint16_t kb = l3m_f32_to_bf16(y[hd + i]), vb = l3m_f32_to_bf16(y[2 * hd + i]);
         s.kcur[i] = kb;
         s.vcur[i] = vb;
         if (role.kv_writer) {
             kc[(size_t)pos * hd + i] = kb;
-            vc[(size_t)pos * hd + i] = vb;
+            vc[(size_t)i * a.vstride + pos] = vb;
         }
     }
     __syncthreads();
     trace(a, tslot, pos, l, 11);
-    attend_exact(y, kc, vc, hd, s.kcur, s.vcur, pos, hd, s.scores, s.att, s.red, a.elist, a.eindex, s.kvbuf, a.attn_chunk);
+    attend_exact<true>(y, kc, vc, hd, a.vstride, s.kcur, s.vcur, pos, hd, s.scores, s.att, s.red, a.elist, a.eindex, s.kvbuf, s.vtbuf,
+                       a.attn_chunk);
     trace(a, tslot, pos, l, 12);
     for (int i = tid; i < hd; i += nth) attn[h * hd + i] = s.att[i];
 }
 
 __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeArgs *__restrict__ ap) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    const DecodeArgs &a = *ap;                                      // in global memory: no local copy
+    // The arguments, this CTA's role and every layer's pointers live in shared memory for the whole
+    // launch: reading them never waits on L1 misses behind the streamed weights.
+    __shared__ DecodeArgs sh_args;
+    __shared__ Role sh_role;
+    if (threadIdx.x == 0) {
+        sh_args = *ap;
+        sh_role = ap->roles[blockIdx.x];
+    }
+    __syncthreads();
+    const DecodeArgs &a = sh_args;
+    {
+        const uint32_t *src = (const uint32_t *)ap->layers;
+        uint32_t *dst = (uint32_t *)(smem_raw + a.sm_layers);
+        for (int i = threadIdx.x; i < a.n_layers * (int)(sizeof(LayerDev) / 4); i += blockDim.x) dst[i] = src[i];
+    }
+    const LayerDev *layers = (const LayerDev *)(smem_raw + a.sm_layers);
+    __syncthreads();
     Smem s = carve(smem_raw, a);
     const int cta = blockIdx.x, tid = threadIdx.x, nth = blockDim.x;
-    const Role role = a.roles[cta];
+    const Role &role = sh_role;
     int tslot = -1;
     for (int i = 0; i < 4; i++) if (a.trace_cta[i] == cta) tslot = i;
     uint32_t step = 0, tcount = 0;
@@ -223,21 +246,30 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
         embed_row(a, tok, s.x);
         for (int l = 0; l < a.n_layers && ok; l++) {
             ++step;
-            const LayerDev &L = a.layers[l];
-            if (l + 1 < a.n_layers) prefetch_layer(a, a.layers[l + 1], role);
+            const LayerDev &L = layers[l];
+            if (l + 1 < a.n_layers) prefetch_layer(a, layers[l + 1], role);
             else {
-                prefetch_layer(a, a.layers[0], role);
+                prefetch_layer(a, layers[0], role);
                 if (last && role.voc0 < role.voc1 && threadIdx.x == 0) {
                     const size_t th = tile_bytes(a.dt_head, a.dim);
                     prefetch_l2(a.head + role.voc0 * th, (size_t)(role.voc1 - role.voc0) * th);
                 }
             }
+            // This layer's small vectors into shared memory while the exchange below is awaited.
+            if (role.head >= 0) {
+                stage_f32(s.wa, L.attn_norm, a.dim);
+                if (a.rope) stage_f32((float *)s.rope, (const float *)(a.rope + (size_t)pos * (a.hd / 2)), a.hd);
+            }
+            if (role.ffn0 < role.ffn1) stage_f32(s.wf, L.ffn_norm, a.dim);
+            if (l + 1 == a.n_layers && last && role.voc0 < role.voc1) stage_f32(s.wh, a.norm, a.dim);
+            cp_async_commit();
             if (l > 0) {
                 if (!(ok = wait_x(a, kXDown, step - 1))) break;
                 read_x(xbuf(a, a.d_down, step - 1), a.dim, s.tmp);
                 for (int i = tid; i < a.dim; i += nth) s.x[i] = __fadd_rn(s.x[i], s.tmp[i]);
-                __syncthreads();
             }
+            cp_async_wait_all();
+            __syncthreads();
             trace(a, tslot, pos, l, 0);
             if (role.head >= 0) {                                            // A
                 phase_attention(a, L, role, pos, xbuf(a, a.d_attn, step), s, tslot, l);
@@ -261,7 +293,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
             for (int i = tid; i < a.dim; i += nth) s.x[i] = __fadd_rn(s.x[i], s.tmp[i]);
             publish(a, kXDown, step);                                       // presence: done reading step - 1
             if (role.ffn0 < role.ffn1) {
-                rmsnorm_exact(s.x, L.ffn_norm, a.dim, a.eps, s.xb, s.tmp, s.red);
+                rmsnorm_exact(s.x, s.wf, a.dim, a.eps, s.xb, s.tmp, s.red);
                 trace(a, tslot, pos, l, 13);
                 prepare(L.dt_up, s.xb, a.dim, s.prep);
                 matvec_exact(L.dt_up, L.up, a.dim, role.ffn0, role.ffn1, s.prep, s.scratch, a.scratch_pairs, s.y);
@@ -306,7 +338,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
         float best = -INFINITY;
         int best_i = -1;
         if (role.voc0 < role.voc1) {
-            rmsnorm_exact(s.x, a.norm, a.dim, a.eps, s.xb, s.tmp, s.red);
+            rmsnorm_exact(s.x, s.wh, a.dim, a.eps, s.xb, s.tmp, s.red);
             prepare(a.dt_head, s.xb, a.dim, s.prep);
             matvec_exact(a.dt_head, a.head, a.dim, role.voc0, role.voc1, s.prep, s.scratch, a.scratch_pairs, s.y);
             float *lg = a.logits + (size_t)pos * a.vocab;
@@ -363,6 +395,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
         }
         if (stop_req) break;
     }
+    cp_async_wait_all();                                                    // no copy outlives the CTA
     if (!ok) err = *(volatile int *)a.abort_flag;
     if (cta == 0 && tid == 0) {
         a.ctrl->final_pos = pos;

@@ -4,12 +4,12 @@
 
 namespace l3m {
 
-struct LayerDev {
+struct alignas(16) LayerDev {
     const uint8_t *qkv;                 // one unit per query head: its q rows, then its kv head's k and v rows
     const uint8_t *wo, *gate, *up, *down;
     const float *attn_norm, *ffn_norm;
     const float *bq, *bk, *bv, *bo, *b_up, *b_down;   // NULL when absent
-    uint16_t *kc, *vc;                  // [n_kv][ctx][hd] bf16
+    uint16_t *kc, *vc;                  // K [n_kv][ctx][hd], V [n_kv][hd][vstride] bf16
     int dt_qkv, dt_wo, dt_gate, dt_up, dt_down;
 };
 
@@ -68,7 +68,10 @@ struct DecodeArgs {
     unsigned long long *trace;          // optional: [4][ctx][n_layers + 1][16] globaltimer stamps
     int trace_cta[4];
     // shared memory layout, byte offsets
-    int sm_x, sm_xb, sm_tmp, sm_q8, sm_scale, sm_sum, sm_xf, sm_y, sm_y2, sm_scores, sm_kv, sm_att, sm_red, sm_kvbuf, sm_scratch;
+    int sm_x, sm_xb, sm_tmp, sm_q8, sm_scale, sm_sum, sm_xf, sm_y, sm_y2, sm_scores, sm_kv, sm_att, sm_red, sm_kvbuf, sm_vt, sm_scratch;
+    int sm_wa, sm_wf, sm_wh, sm_rope;   // this layer's norm weights, the final norm, this position's RoPE row
+    int sm_layers;                      // a copy of layers[0 .. n_layers)
+    int vstride;                        // V cache: element i of position t at vc[i * vstride + t]
     int scratch_pairs, smem_bytes, attn_chunk;
 };
 

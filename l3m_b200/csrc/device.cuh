@@ -19,6 +19,28 @@ __device__ __forceinline__ uint8_t ld_nc_u8(const void *p) { return __ldg((const
 // Data other CTAs write during the kernel (KV cache rows): cached in L2 only, never in L1, so a
 // line fetched before a neighbouring row was written cannot be served stale.
 __device__ __forceinline__ uint4 ld_cg_v4(const void *p) { return __ldcg((const uint4 *)p); }
+// Streamed read-only data (weights): not allocated in L1, so it does not evict what the kernel reuses.
+__device__ __forceinline__ uint4 ld_stream_v4(const void *p) {
+    uint4 v;
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint2 ld_stream_v2(const void *p) {
+    uint2 v;
+    asm("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint32_t ld_stream_u32(const void *p) {
+    uint32_t v;
+    asm("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+// 16-byte asynchronous copy global -> shared through L2 (both addresses 16-byte aligned).
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((unsigned)__cvta_generic_to_shared(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 __device__ __forceinline__ uint16_t ld_cg_u16(const void *p) { return __ldcg((const unsigned short *)p); }
 
 // ---- integer dot of 4 bytes: unsigned weights times signed activations, plus c

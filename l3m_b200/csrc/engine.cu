@@ -262,7 +262,11 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     if (!cuda_ok(cudaMemcpy(g.arena, s.buf.data(), g.arena_bytes, cudaMemcpyHostToDevice), "weights upload")) return false;
     std::vector<uint8_t>().swap(s.buf);
 
-    g.kv_bytes = (size_t)L * 2 * m->n_kv * m->ctx * hd * 2;
+    // Per layer: K [n_kv][ctx][hd] (a row per position) and V transposed, [n_kv][hd][vstride] (a
+    // column per position), both bf16.
+    const int vstride = (m->ctx + 7) & ~7;
+    const size_t k_per = (size_t)m->n_kv * m->ctx * hd, v_per = (size_t)m->n_kv * hd * vstride;
+    g.kv_bytes = (size_t)L * (k_per + v_per) * 2;
     if (!cuda_ok(cudaMalloc(&g.kv, g.kv_bytes), "KV cache")) return false;
     cudaMemset(g.kv, 0, g.kv_bytes);
     auto A = [&](long long off) -> const float * { return off < 0 ? nullptr : (const float *)(g.arena + off); };
@@ -275,9 +279,8 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
         d.down = g.arena + off_down[l];
         d.attn_norm = A(vo[l].an); d.ffn_norm = A(vo[l].fn);
         d.bq = A(vo[l].bq); d.bk = A(vo[l].bk); d.bv = A(vo[l].bv); d.bo = A(vo[l].bo); d.b_up = A(vo[l].bu); d.b_down = A(vo[l].bd);
-        const size_t per = (size_t)m->n_kv * m->ctx * hd;
-        d.kc = g.kv + (size_t)l * 2 * per;
-        d.vc = d.kc + per;
+        d.kc = g.kv + (size_t)l * (k_per + v_per);
+        d.vc = d.kc + k_per;
     }
     if (!cuda_ok(cudaMalloc(&g.layers, sizeof(l3m::LayerDev) * L), "layers")) return false;
     cudaMemcpy(g.layers, layers.data(), sizeof(l3m::LayerDev) * L, cudaMemcpyHostToDevice);
@@ -379,8 +382,15 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     a.sm_kv = take(2 * hd * 2);
     a.sm_att = take(hd * 4);
     a.sm_red = take(64 * 4);
-    a.attn_chunk = std::min(m->ctx, 128);
+    a.sm_wa = take(dim * 4);
+    a.sm_wf = take(dim * 4);
+    a.sm_wh = take(dim * 4);
+    a.sm_rope = take(hd / 2 * 8);
+    a.sm_layers = take(L * (int)sizeof(l3m::LayerDev));
+    a.attn_chunk = std::min(m->ctx, 256);
     a.sm_kvbuf = take(a.attn_chunk * (hd + 8) * 2);
+    a.sm_vt = take(hd * l3m::attn_vt_stride(a.attn_chunk) * 2);
+    a.vstride = vstride;
     a.sm_scratch = take(0);
     const int budget = 200 * 1024;
     a.scratch_pairs = std::min(8192, (budget - off) / 8);

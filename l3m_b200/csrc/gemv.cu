@@ -1,9 +1,9 @@
 // Standalone matvec kernels behind include/l3m_kernels.h: y = tiles . x on the device, with the
 // reference's tile layout (src/kernels.h:1-10) and its scalar table's results (src/kernels_scalar.c).
 //
-// Exact table, quantised dtypes: every CTA takes a contiguous run of tiles; warps compute the exact
-// integer dot of each (tile, 32-input block) with dp4a from 16-byte coalesced loads (four blocks in
-// flight per warp), then one thread per output runs the fp32 epilogue over the blocks in order.
+// Exact table, quantised dtypes: every CTA takes a contiguous run of tiles; each thread computes the
+// exact integer dots of 4 outputs x one 32-input block with dp4a from 16-byte loads (two such items
+// in flight), then one thread per output runs the fp32 epilogue over the blocks in order.
 // Exact table, f32/bf16: one thread per output runs the sequential chain over K (the order the
 // reference rounds in). Fast table, f32/bf16: the chain is split over K across a warp and reduced
 // with shuffles (reassociated, like the reference's AVX tables; tolerance-checked).
@@ -177,7 +177,7 @@ __global__ void __launch_bounds__(kThreads) attend_kernel(float *out, const floa
         vcur[i] = v[(size_t)pos * stride + i];
     }
     __syncthreads();
-    attend_exact(qs, k, v, stride, kcur, vcur, pos, hd, scores, o, red, elist, eindex, kvbuf, kAttnChunk);
+    attend_exact<false>(qs, k, v, stride, stride, kcur, vcur, pos, hd, scores, o, red, elist, eindex, kvbuf, nullptr, kAttnChunk);
     for (int i = threadIdx.x; i < hd; i += blockDim.x) out[i] = o[i];
 }
 

@@ -42,27 +42,52 @@ struct Prep {
 
 // ---- prepare (reference src/pack.c:101-122)
 static __device__ __noinline__ void prepare(int dtype, const float *x, int n, const Prep p) {
-    const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31, warp = tid >> 5, nw = nth >> 5;
+    const int tid = threadIdx.x, nth = blockDim.x;
     if (dtype == DT_F32) {
         for (int i = tid; i < n; i += nth) p.xf[i] = x[i];
     } else if (dtype == DT_BF16) {
         for (int i = tid; i < n; i += nth) p.xf[i] = l3m_bf16_to_f32(l3m_f32_to_bf16(x[i]));
     } else {
-        for (int b = warp; b < n / kQB; b += nw) {
-            float v = x[b * kQB + lane];
-            float a = fabsf(v);
-            float amax = warp_max_f32(a > 0.0f ? a : 0.0f);          // a NaN never raises the maximum
-            float inv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-            int8_t q = (int8_t)__float2int_rn(__fmul_rn(v, inv));
-            p.q8[b * kQB + lane] = q;
-            int s = warp_sum_i32((int)q);
-            if (lane == 0) {
-                p.scale[b] = __fdiv_rn(amax, 127.0f);
-                p.sum[b] = s;
+        // 8 threads per 32-input block, 4 inputs each (x 16-byte aligned in shared memory); a warp takes
+        // 4 blocks per step and every lane of it runs every step, so the shuffles always see the whole warp.
+        const int j = tid & 7, sub = (tid & 31) >> 3, nblk = n / kQB;
+        for (int b0 = (tid >> 5) * 4; b0 < nblk; b0 += (nth >> 5) * 4) {
+            const int b = b0 + sub;
+            const bool ok = b < nblk;
+            const float4 v = ok ? ((const float4 *)(x + b * kQB))[j] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            const float a0 = fabsf(v.x), a1 = fabsf(v.y), a2 = fabsf(v.z), a3 = fabsf(v.w);
+            // a NaN never raises the maximum; the maximum of the rest is order-free
+            float m = fmaxf(fmaxf(a0 > 0.0f ? a0 : 0.0f, a1 > 0.0f ? a1 : 0.0f), fmaxf(a2 > 0.0f ? a2 : 0.0f, a3 > 0.0f ? a3 : 0.0f));
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+            const float inv = m > 0.0f ? __fdiv_rn(127.0f, m) : 0.0f;
+            const int q0 = (int8_t)__float2int_rn(__fmul_rn(v.x, inv)), q1 = (int8_t)__float2int_rn(__fmul_rn(v.y, inv));
+            const int q2 = (int8_t)__float2int_rn(__fmul_rn(v.z, inv)), q3 = (int8_t)__float2int_rn(__fmul_rn(v.w, inv));
+            int sm = q0 + q1 + q2 + q3;
+            sm += __shfl_xor_sync(0xffffffffu, sm, 4);
+            sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+            sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+            if (ok) {
+                ((uint32_t *)(p.q8 + b * kQB))[j] = (uint32_t)(q0 & 0xFF) | (uint32_t)(q1 & 0xFF) << 8 | (uint32_t)(q2 & 0xFF) << 16 | (uint32_t)(q3 & 0xFF) << 24;
+                if (j == 0) {
+                    p.scale[b] = __fdiv_rn(m, 127.0f);
+                    p.sum[b] = sm;
+                }
             }
         }
     }
     __syncthreads();
+}
+
+// Copy n floats global -> shared: asynchronous 16-byte copies when both sides allow (the caller
+// commits, then waits with cp_async_wait_all + __syncthreads), else plain loads.
+__device__ __forceinline__ void stage_f32(float *dst, const float *src, int n) {
+    if ((n & 3) == 0 && ((uintptr_t)src & 15) == 0 && ((uintptr_t)dst & 15) == 0) {
+        for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4) cp_async16(dst + i, src + i);
+    } else {
+        for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = __ldg(src + i);
+    }
 }
 
 // ---- quantised block dots. Tile layout per 32-input block (reference src/kernels.h:1-10):
@@ -83,7 +108,65 @@ __device__ __forceinline__ uint32_t mx_lut16(uint32_t s) {
     return (pos & ~m) | (neg & m);
 }
 
-// One row's block, loaded ahead of use: its words and its scale bits.
+// Four consecutive rows' block (rows 4r4..4r4+3 of a tile), loaded ahead of use: 16 bytes per group
+// (q8: 8 groups, q4/mxfp4: 4) and the four scales.
+struct QLoad4 { uint4 w[8]; uint2 d; };
+
+template <int DT>
+__device__ __forceinline__ void qload4(QLoad4 &q, const uint8_t *blk, int r4) {
+    if (DT == DT_Q8) {
+        const uint8_t *g = blk + 32 + 16 * r4;
+#pragma unroll
+        for (int j = 0; j < 8; j++) q.w[j] = ld_stream_v4(g + 64 * j);
+        q.d = ld_stream_v2(blk + 8 * r4);
+    } else {
+        const uint8_t *g = blk + (DT == DT_MX ? 16 : 32) + 16 * r4;
+#pragma unroll
+        for (int j = 0; j < 4; j++) q.w[j] = ld_stream_v4(g + 64 * j);
+        if (DT == DT_MX) q.d = make_uint2(ld_stream_u32(blk + 4 * r4), 0);
+        else q.d = ld_stream_v2(blk + 8 * r4);
+    }
+}
+
+__device__ __forceinline__ uint32_t u4_at(const uint4 &v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
+
+// Exact integer dot of row c (0..3) of a QLoad4 with the block's prepared activation words xw[0..7],
+// offset removed (the reference's acc_i - offset * sum, src/kernels_scalar.c:37-43, 57-71).
+template <int DT>
+__device__ __forceinline__ int qdot4(const QLoad4 &q, int c, const uint32_t *xw, int32_t xsum) {
+    int s = 0, t = 0;
+    if (DT == DT_Q8) {
+#pragma unroll
+        for (int j = 0; j < 8; j += 2) { s = dp4a_us(u4_at(q.w[j], c), xw[j], s); t = dp4a_us(u4_at(q.w[j + 1], c), xw[j + 1], t); }
+        return s + t - 128 * xsum;
+    } else if (DT == DT_Q4) {
+#pragma unroll
+        for (int g = 0; g < 4; g++) {
+            const uint32_t w = u4_at(q.w[g], c);
+            s = dp4a_us(w & 0x0F0F0F0Fu, xw[2 * g], s);
+            t = dp4a_us((w >> 4) & 0x0F0F0F0Fu, xw[2 * g + 1], t);
+        }
+        return s + t - 8 * xsum;
+    } else {
+#pragma unroll
+        for (int g = 0; g < 4; g++) {
+            const uint32_t w = u4_at(q.w[g], c), xl = xw[2 * g], xh = xw[2 * g + 1];
+            // bytes 0,1 of the word select inputs 0 4 1 5 of the group; bytes 2,3 select 2 6 3 7
+            s = dp4a_us(mx_lut16(w), prmt(xl, xh, 0x5140u), s);
+            t = dp4a_us(mx_lut16(w >> 16), prmt(xl, xh, 0x7362u), t);
+        }
+        return s + t - 16 * xsum;
+    }
+}
+
+template <int DT>
+__device__ __forceinline__ float qscale4(const uint2 &d, int c) {
+    if (DT == DT_MX) return l3m_e8m0_half((uint8_t)(d.x >> (8 * c)));
+    const uint32_t w = c < 2 ? d.x : d.y;
+    return l3m_f16_to_f32((uint16_t)(c & 1 ? w >> 16 : w));
+}
+
+// Single-row forms (one output's block), used where one thread owns one (output, block) item.
 struct QLoad { uint32_t w[8]; uint32_t d; };
 
 template <int DT>
@@ -106,73 +189,61 @@ __device__ __forceinline__ void qload(QLoad &q, const uint8_t *blk, int c) {
     }
 }
 
-// Exact integer dot of a loaded block with the block's 8 prepared activation words xw[0..7], offset
-// removed (the reference's acc_i - offset * sum, src/kernels_scalar.c:37-43, 57-71).
 template <int DT>
 __device__ __forceinline__ int qdot(const QLoad &q, const uint32_t *xw, int32_t xsum) {
-    int s = 0, t = 0;
-    if (DT == DT_Q8) {
+    QLoad4 q4;
 #pragma unroll
-        for (int j = 0; j < 8; j += 2) { s = dp4a_us(q.w[j], xw[j], s); t = dp4a_us(q.w[j + 1], xw[j + 1], t); }
-        return s + t - 128 * xsum;
-    } else if (DT == DT_Q4) {
-#pragma unroll
-        for (int g = 0; g < 4; g++) {
-            s = dp4a_us(q.w[g] & 0x0F0F0F0Fu, xw[2 * g], s);
-            t = dp4a_us((q.w[g] >> 4) & 0x0F0F0F0Fu, xw[2 * g + 1], t);
-        }
-        return s + t - 8 * xsum;
-    } else {
-#pragma unroll
-        for (int g = 0; g < 4; g++) {
-            const uint32_t xl = xw[2 * g], xh = xw[2 * g + 1];
-            // bytes 0,1 of the word select inputs 0 4 1 5 of the group; bytes 2,3 select 2 6 3 7
-            s = dp4a_us(mx_lut16(q.w[g]), prmt(xl, xh, 0x5140u), s);
-            t = dp4a_us(mx_lut16(q.w[g] >> 16), prmt(xl, xh, 0x7362u), t);
-        }
-        return s + t - 16 * xsum;
-    }
+    for (int j = 0; j < 8; j++) q4.w[j] = make_uint4(q.w[j], 0, 0, 0);
+    q4.d = make_uint2(q.d, 0);
+    return qdot4<DT>(q4, 0, xw, xsum);
 }
 
 template <int DT>
 __device__ __forceinline__ float qscale(uint32_t d) { return DT == DT_MX ? l3m_e8m0_half((uint8_t)d) : l3m_f16_to_f32((uint16_t)d); }
 
-// Outputs [0, n_out) of the tiles at `tiles`, exact. The (output, block) items of a chunk of outputs
-// are dealt to threads output-fastest, kQU blocks in flight per thread; each stores {RN(sx[b] * d),
-// (float)dot} at scratch[b * m + o]. Then one thread per output runs the fp32 chain in block order.
-constexpr int kQU = 4;
+// Outputs [0, n_out) of the tiles at `tiles` (n_out a multiple of 16), exact. The (4 outputs, block)
+// items of a chunk of outputs are dealt to threads output-fastest, kQU items in flight per thread;
+// each output's {RN(sx[b] * d), (float)dot} goes to scratch[b * m + o]. Then one thread per output
+// runs the fp32 chain in block order.
+constexpr int kQU = 2;
 template <int DT>
 __device__ void qmatvec(const uint8_t *tiles, int k, int n_out, const Prep &p, float2 *scratch, int scratch_pairs, float *y) {
     const int tid = threadIdx.x, nth = blockDim.x, nb = k / kQB, bb = block_bytes(DT);
     const size_t tb = (size_t)nb * bb;
     const uint32_t *xw = (const uint32_t *)p.q8;
-    int chunk = scratch_pairs / nb;
+    int chunk = (scratch_pairs / nb) & ~(kTile - 1);
     if (chunk > n_out) chunk = n_out;
     for (int o0 = 0; o0 < n_out; o0 += chunk) {
-        const int m = min(chunk, n_out - o0), items = m * nb;
-        // item i = b * m + o; this thread starts at i = tid and steps by nth
-        int b = tid / m, o = tid - b * m;
-        const int db = nth / m, dor = nth - db * m;
-        const uint8_t *base = tiles + (size_t)o0 / kTile * tb;   // o0 is a multiple of 16 unless chunk is not
-        const int oc = o0 % kTile;
+        const int m = min(chunk, n_out - o0), m4 = m >> 2, items = m4 * nb;
+        const uint8_t *base = tiles + (size_t)(o0 >> 4) * tb;
+        // item i = b * m4 + quad; this thread starts at i = tid and steps by nth
+        int b = tid / m4, qd = tid - b * m4;
+        const int db = nth / m4, dq = nth - db * m4;
         for (int i = tid; i < items; i += kQU * nth) {
-            QLoad q[kQU];
-            int bs[kQU], os[kQU];
+            QLoad4 q[kQU];
+            int bs[kQU], qs[kQU];
 #pragma unroll
             for (int u = 0; u < kQU; u++) {
-                bs[u] = b; os[u] = o;
-                if (i + u * nth < items) {
-                    const int oo = o + oc;
-                    qload<DT>(q[u], base + (size_t)(oo >> 4) * tb + (size_t)b * bb, oo & 15);
-                }
-                o += dor; b += db;
-                if (o >= m) { o -= m; b++; }
+                bs[u] = b; qs[u] = qd;
+                if (i + u * nth < items) qload4<DT>(q[u], base + (size_t)(qd >> 2) * tb + (size_t)b * bb, qd & 3);
+                qd += dq; b += db;
+                if (qd >= m4) { qd -= m4; b++; }
             }
 #pragma unroll
             for (int u = 0; u < kQU; u++) {
                 if (i + u * nth < items) {
-                    const int dot = qdot<DT>(q[u], xw + 8 * bs[u], p.sum[bs[u]]);
-                    scratch[(size_t)bs[u] * m + os[u]] = make_float2(__fmul_rn(p.scale[bs[u]], qscale<DT>(q[u].d)), __int2float_rn(dot));
+                    const uint4 x0 = *(const uint4 *)(xw + 8 * bs[u]), x1 = *(const uint4 *)(xw + 8 * bs[u] + 4);
+                    const uint32_t xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                    const float sx = p.scale[bs[u]];
+                    const int32_t xs = p.sum[bs[u]];
+                    float4 r0, r1;
+                    r0.x = __fmul_rn(sx, qscale4<DT>(q[u].d, 0)); r0.y = __int2float_rn(qdot4<DT>(q[u], 0, xv, xs));
+                    r0.z = __fmul_rn(sx, qscale4<DT>(q[u].d, 1)); r0.w = __int2float_rn(qdot4<DT>(q[u], 1, xv, xs));
+                    r1.x = __fmul_rn(sx, qscale4<DT>(q[u].d, 2)); r1.y = __int2float_rn(qdot4<DT>(q[u], 2, xv, xs));
+                    r1.z = __fmul_rn(sx, qscale4<DT>(q[u].d, 3)); r1.w = __int2float_rn(qdot4<DT>(q[u], 3, xv, xs));
+                    float4 *dst = (float4 *)(scratch + (size_t)bs[u] * m + 4 * qs[u]);
+                    dst[0] = r0;
+                    dst[1] = r1;
                 }
             }
         }
@@ -216,7 +287,7 @@ static __device__ __noinline__ void matvec_exact(int dtype, const uint8_t *tiles
             for (; q + 8 <= k / 2; q += 8) {
                 uint32_t v[8];
 #pragma unroll
-                for (int j = 0; j < 8; j++) v[j] = __ldg(w + (size_t)(q + j) * kTile);
+                for (int j = 0; j < 8; j++) v[j] = ld_stream_u32(w + (size_t)(q + j) * kTile);
 #pragma unroll
                 for (int j = 0; j < 8; j++) {
                     acc = __fmaf_rn(l3m_bits_f32(v[j] << 16), p.xf[2 * (q + j)], acc);
@@ -224,7 +295,7 @@ static __device__ __noinline__ void matvec_exact(int dtype, const uint8_t *tiles
                 }
             }
             for (; q < k / 2; q++) {
-                const uint32_t v = __ldg(w + (size_t)q * kTile);
+                const uint32_t v = ld_stream_u32(w + (size_t)q * kTile);
                 acc = __fmaf_rn(l3m_bits_f32(v << 16), p.xf[2 * q], acc);
                 acc = __fmaf_rn(l3m_bits_f32(v & 0xFFFF0000u), p.xf[2 * q + 1], acc);
             }
@@ -239,24 +310,59 @@ static __device__ __noinline__ void matvec_exact(int dtype, const uint8_t *tiles
     __syncthreads();
 }
 
-// ---- rmsnorm (reference src/ops.c:13-18). tmp: n floats of shared scratch; red: one float.
-static __device__ __noinline__ void rmsnorm_exact(const float *x, const float *w, int n, float eps, float *y, float *tmp, float *red) {
-    const int tid = threadIdx.x, nth = blockDim.x, split = fused_from(n);
-    for (int i = tid; i < split; i += nth) tmp[i] = __fmul_rn(x[i], x[i]);
-    __syncthreads();
-    if (tid == 0) {
-        float ss = 0.0f;
-        const float4 *t4 = (const float4 *)tmp;
-        for (int i = 0; i < split / 4; i++) {
-            float4 v = t4[i];
-            ss = __fadd_rn(ss, v.x); ss = __fadd_rn(ss, v.y); ss = __fadd_rn(ss, v.z); ss = __fadd_rn(ss, v.w);
+// Sequential fp32 sum of v[0..n) in index order (v 16-byte aligned), by the calling thread: 32 values
+// per batch, the next batch loading while this one adds.
+// squares: add RN(v*v) instead of v.
+template <bool SQUARES>
+__device__ __forceinline__ float chain_sum(const float *v, int n, float acc) {
+    const float4 *v4 = (const float4 *)v;
+    const int nf = n & ~31;
+    if (nf) {
+        float4 r[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) r[j] = v4[j];
+        for (int i = 0; i < nf; i += 32) {
+            float4 nx[8];
+            const int in = i + 32 < nf ? i + 32 : i;
+#pragma unroll
+            for (int j = 0; j < 8; j++) nx[j] = v4[in / 4 + j];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const float e[4] = {r[j].x, r[j].y, r[j].z, r[j].w};
+#pragma unroll
+                for (int h = 0; h < 4; h++) acc = __fadd_rn(acc, SQUARES ? __fmul_rn(e[h], e[h]) : e[h]);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) r[j] = nx[j];
         }
+    }
+#pragma unroll 8
+    for (int i = nf; i < n; i++) acc = __fadd_rn(acc, SQUARES ? __fmul_rn(v[i], v[i]) : v[i]);
+    return acc;
+}
+
+// ---- rmsnorm (reference src/ops.c:13-18). x 16-byte aligned, w in shared or global memory; red: one
+// float. The sum of squares is the reference's sequential chain, run by thread 0 from registers while
+// the other threads fetch w.
+constexpr int kNormPerThread = 8;
+static __device__ __noinline__ void rmsnorm_exact(const float *x, const float *w, int n, float eps, float *y, float *tmp, float *red) {
+    const int tid = threadIdx.x, nth = blockDim.x;
+    (void)tmp;
+    float wr[kNormPerThread];
+#pragma unroll
+    for (int j = 0; j < kNormPerThread; j++) wr[j] = tid + j * nth < n ? w[tid + j * nth] : 0.0f;
+    if (tid == 0) {
+        const int split = fused_from(n);
+        float ss = chain_sum<true>(x, split, 0.0f);
         for (int i = split; i < n; i++) ss = __fmaf_rn(x[i], x[i], ss);
         *red = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
     }
     __syncthreads();
-    const float s = *red;
-    for (int i = tid; i < n; i += nth) y[i] = __fmul_rn(__fmul_rn(x[i], s), __ldg(w + i));
+    const float sc = *red;
+#pragma unroll
+    for (int j = 0; j < kNormPerThread; j++)
+        if (tid + j * nth < n) y[tid + j * nth] = __fmul_rn(__fmul_rn(x[tid + j * nth], sc), wr[j]);
+    for (int i = tid + kNormPerThread * nth; i < n; i += nth) y[i] = __fmul_rn(__fmul_rn(x[i], sc), w[i]);
     __syncthreads();
 }
 
@@ -275,9 +381,13 @@ __device__ __forceinline__ float expf_libm(float x, const uint32_t *list, const 
     return l3m_expf_exact(x, list, index);
 }
 
-// ---- one head of attention at position pos (reference src/ops.c:42-47, 58-73). Rows 0..pos-1 of
-// this head's K and V cache are in global memory, `stride` elements apart; row pos is kcur/vcur
-// (16-byte aligned). scores: >= pos + 1 floats of shared scratch; red: >= 33 floats. hd % 8 == 0.
+// ---- one head of attention at position pos (reference src/ops.c:42-47, 58-73).
+// K rows 0..pos-1 are in global memory, kstride elements apart; row pos is kcur (shared, 16-byte
+// aligned). V: with VT false, rows like K (vstride apart), row pos in vcur; with VT true, the cache
+// is transposed — element i of position t at vc[i * vstride + t], vstride >= pos + 1 rounded up to
+// 8 — and element i of row pos is vcur[i]. scores: >= pos + 1 floats of shared scratch (16-byte aligned); red: >= 33 floats.
+// kvbuf: chunk * (hd + 8) bf16 of staging; vtbuf (VT only): hd * attn_vt_stride(chunk) bf16.
+// hd % 8 == 0; chunk a multiple of 8.
 __device__ __forceinline__ uint4 ld_row8(const uint16_t *p, bool vec) {
     if (vec) return ld_cg_v4(p);
     uint16_t h[8];
@@ -286,80 +396,162 @@ __device__ __forceinline__ uint4 ld_row8(const uint16_t *p, bool vec) {
     return make_uint4(h[0] | (uint32_t)h[1] << 16, h[2] | (uint32_t)h[3] << 16, h[4] | (uint32_t)h[5] << 16, h[6] | (uint32_t)h[7] << 16);
 }
 
-static __device__ __noinline__ void attend_exact(const float *q, const uint16_t *kc, const uint16_t *vc, int stride, const uint16_t *kcur,
-                                    const uint16_t *vcur, int pos, int hd, float *scores, float *out, float *red,
-                                    const uint32_t *elist, const uint32_t *eindex, uint16_t *kvbuf, int chunk) {
+// Row stride (elements) of the transposed V staging buffer: 4 x odd words, so the 16-byte reads of 8
+// consecutive rows fall in distinct bank groups.
+__host__ __device__ constexpr int attn_vt_stride(int chunk) { return ((chunk + 15) & ~15) + 8; }
+
+template <bool VT>
+__device__ __noinline__ void attend_exact(const float *q, const uint16_t *kc, const uint16_t *vc, int kstride, int vstride, const uint16_t *kcur,
+                             const uint16_t *vcur, int pos, int hd, float *scores, float *out, float *red, const uint32_t *elist,
+                             const uint32_t *eindex, uint16_t *kvbuf, uint16_t *vtbuf, int chunk) {
     const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31, warp = tid >> 5;
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
-    const bool vec = stride % 8 == 0 && ((uintptr_t)kc & 15) == 0 && ((uintptr_t)vc & 15) == 0;
-    const int rs = hd + 8;                                   // padded row stride in the staging buffer (elements)
-    // Rows 0..pos-1 come through shared memory in chunks: coalesced 16-byte loads, then each thread
-    // walks its own row (scores) or its own column (value mix) out of the staging buffer.
-    for (int c0 = 0; c0 <= pos; c0 += chunk) {
-        const int n = min(chunk, pos + 1 - c0);
-#pragma unroll 4
-        for (int e = tid; e < n * (hd / 8); e += nth) {
-            const int r = e / (hd / 8), i = (e - r * (hd / 8)) * 8, t = c0 + r;
-            const uint4 v = t == pos ? *(const uint4 *)(kcur + i) : ld_row8(kc + (size_t)t * stride + i, vec);
-            *(uint4 *)(kvbuf + r * rs + i) = v;
+    const bool kvec = kstride % 8 == 0 && ((uintptr_t)kc & 15) == 0;
+    const bool vvec = vstride % 8 == 0 && ((uintptr_t)vc & 15) == 0;
+    const int n = pos + 1, rs = hd + 8, h8 = hd / 8, vs = attn_vt_stride(chunk);
+    // V of positions [c0, c0 + cnt) into shared memory; aligned pieces as asynchronous copies that land
+    // while the caller goes on (cp_async_wait_all + __syncthreads before reading them).
+    auto stage_v = [&](int c0, int cnt) {
+        if (VT) {                                            // vtbuf[i * vs + r], one 8-position piece per copy
+            // Positions past pos in a piece are never read; position pos itself is patched from vcur
+            // by the thread that reads its column, after the copies have landed.
+            const int p8 = (cnt + 7) >> 3, di = nth / p8, dp = nth - di * p8;
+            int i = tid / p8, pc = tid - i * p8;
+            for (int e = tid; e < hd * p8; e += nth) {
+                uint16_t *dst = vtbuf + i * vs + pc * 8;
+                const uint16_t *src = vc + (size_t)i * vstride + c0 + pc * 8;
+                if (vvec) cp_async16(dst, src);
+                else *(uint4 *)dst = ld_row8(src, false);
+                pc += dp; i += di;
+                if (pc >= p8) { pc -= p8; i++; }
+            }
+        } else {                                             // kvbuf[r * rs + i], rows as in global memory
+            const int dr = nth / h8, dj = nth - dr * h8;
+            int r = tid / h8, j = tid - r * h8;
+            for (int e = tid; e < cnt * h8; e += nth) {
+                const int i = j * 8, t = c0 + r;
+                uint16_t *dst = kvbuf + r * rs + i;
+                if (t == pos) *(uint4 *)dst = *(const uint4 *)(vcur + i);
+                else if (vvec) cp_async16(dst, vc + (size_t)t * vstride + i);
+                else *(uint4 *)dst = ld_row8(vc + (size_t)t * vstride + i, false);
+                j += dj; r += dr;
+                if (j >= h8) { j -= h8; r++; }
+            }
         }
+        cp_async_commit();
+    };
+    auto stage_k = [&](int c0, int cnt) {
+        const int dr = nth / h8, dj = nth - dr * h8;
+        int r = tid / h8, j = tid - r * h8;
+        for (int e = tid; e < cnt * h8; e += nth) {
+            const int i = j * 8, t = c0 + r;
+            uint16_t *dst = kvbuf + r * rs + i;
+            if (t == pos) *(uint4 *)dst = *(const uint4 *)(kcur + i);
+            else if (kvec) cp_async16(dst, kc + (size_t)t * kstride + i);
+            else *(uint4 *)dst = ld_row8(kc + (size_t)t * kstride + i, false);
+            j += dj; r += dr;
+            if (j >= h8) { j -= h8; r++; }
+        }
+        cp_async_commit();
+    };
+    if (VT) stage_v(0, min(chunk, n));                       // its own buffer: lands during the scores
+    // Scores: one thread per row, from K rows staged in shared memory (coalesced copies).
+    float m = -INFINITY;
+    for (int c0 = 0; c0 < n; c0 += chunk) {
+        const int cnt = min(chunk, n - c0);
+        if (c0 > 0) __syncthreads();
+        stage_k(c0, cnt);
+        cp_async_wait_all();
         __syncthreads();
-        for (int r = tid; r < n; r += nth) {
+        for (int r = tid; r < cnt; r += nth) {
             const uint16_t *row = kvbuf + r * rs;
             float dot = 0.0f;
-            for (int i = 0; i < hd; i += 8) {
-                const uint4 v = *(const uint4 *)(row + i);
-                const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+            for (int i0 = 0; i0 < hd; i0 += 64) {
+                uint4 v[8];
 #pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    dot = __fadd_rn(dot, __fmul_rn(q[i + 2 * j], l3m_bits_f32(u[j] << 16)));
-                    dot = __fadd_rn(dot, __fmul_rn(q[i + 2 * j + 1], l3m_bits_f32(u[j] & 0xFFFF0000u)));
+                for (int j = 0; j < 8; j++)
+                    if (i0 + 8 * j < hd) v[j] = *(const uint4 *)(row + i0 + 8 * j);
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    if (i0 + 8 * j >= hd) break;
+                    const uint32_t u[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+                    const float *qq = q + i0 + 8 * j;
+#pragma unroll
+                    for (int h = 0; h < 4; h++) {
+                        dot = __fadd_rn(dot, __fmul_rn(qq[2 * h], l3m_bits_f32(u[h] << 16)));
+                        dot = __fadd_rn(dot, __fmul_rn(qq[2 * h + 1], l3m_bits_f32(u[h] & 0xFFFF0000u)));
+                    }
                 }
             }
-            scores[c0 + r] = __fmul_rn(dot, scale);
+            const float sc = __fmul_rn(dot, scale);
+            scores[c0 + r] = sc;
+            m = fmaxf(m, sc);
         }
-        __syncthreads();
     }
+    __syncthreads();
+    if (!VT) stage_v(0, min(chunk, n));                      // reuses the K buffer
     // The reference takes the running maximum from scores[0] with a strict >: NaN scores after the
-    // first are skipped, a NaN first score stays. The maximum of the rest is order-free.
-    float m = -INFINITY;
-    for (int t = tid; t <= pos; t += nth) m = fmaxf(m, scores[t]);
+    // first are skipped (fmaxf drops them), a NaN first score stays. The maximum of the rest is order-free.
     m = warp_max_f32(m);
     if (lane == 0) red[warp] = m;
     __syncthreads();
-    if (tid == 0) {
-        float mm = -INFINITY;
-        for (int w = 0; w < (nth >> 5); w++) mm = fmaxf(mm, red[w]);
-        red[32] = scores[0] != scores[0] ? scores[0] : mm;
-    }
+    float mx = -INFINITY;
+    for (int w = 0; w < (nth >> 5); w++) mx = fmaxf(mx, red[w]);
+    if (scores[0] != scores[0]) mx = scores[0];
+    for (int t = tid; t < n; t += nth) scores[t] = expf_libm(__fsub_rn(scores[t], mx), elist, eindex);
     __syncthreads();
-    const float mx = red[32];
-    for (int t = tid; t <= pos; t += nth) scores[t] = expf_libm(__fsub_rn(scores[t], mx), elist, eindex);
-    __syncthreads();
-    if (tid == 0) {
-        float sum = 0.0f;
-        for (int t = 0; t <= pos; t++) sum = __fadd_rn(sum, scores[t]);
-        red[32] = sum;
-    }
+    if (tid == 0) red[32] = chain_sum<false>(scores, n, 0.0f);     // the sequential sum
     __syncthreads();
     const float sum = red[32];
-    for (int t = tid; t <= pos; t += nth) scores[t] = __fdiv_rn(scores[t], sum);
+    for (int t = tid; t < n; t += nth) scores[t] = __fdiv_rn(scores[t], sum);
+    cp_async_wait_all();
     __syncthreads();
     float acc = 0.0f;                                        // thread i < hd: output element i
-    for (int c0 = 0; c0 <= pos; c0 += chunk) {
-        const int n = min(chunk, pos + 1 - c0);
-#pragma unroll 4
-        for (int e = tid; e < n * (hd / 8); e += nth) {
-            const int r = e / (hd / 8), i = (e - r * (hd / 8)) * 8, t = c0 + r;
-            const uint4 v = t == pos ? *(const uint4 *)(vcur + i) : ld_row8(vc + (size_t)t * stride + i, vec);
-            *(uint4 *)(kvbuf + r * rs + i) = v;
+    for (int c0 = 0; c0 < n; c0 += chunk) {
+        const int cnt = min(chunk, n - c0);
+        if (c0 > 0) {
+            __syncthreads();
+            stage_v(c0, cnt);
+            cp_async_wait_all();
+            __syncthreads();
         }
-        __syncthreads();
         if (tid < hd) {
-#pragma unroll 8
-            for (int r = 0; r < n; r++) acc = __fmaf_rn(scores[c0 + r], l3m_bf16_to_f32(kvbuf[r * rs + tid]), acc);
+            const float *pp = scores + c0;                   // c0 is a multiple of 8
+            int r = 0;
+            if (VT) {
+                uint16_t *col = vtbuf + tid * vs;            // 8 positions per 16-byte read, one batch ahead
+                if (pos - c0 < cnt) col[pos - c0] = vcur[tid];
+                if (cnt >= 8) {
+                    uint4 v = *(const uint4 *)col;
+                    float4 p0 = *(const float4 *)pp, p1 = *(const float4 *)(pp + 4);
+                    for (; r + 8 <= cnt; r += 8) {
+                        const int rn = r + 16 <= cnt ? r + 8 : r;
+                        const uint4 vn = *(const uint4 *)(col + rn);
+                        const float4 q0 = *(const float4 *)(pp + rn), q1 = *(const float4 *)(pp + rn + 4);
+                        acc = __fmaf_rn(p0.x, l3m_bits_f32(v.x << 16), acc); acc = __fmaf_rn(p0.y, l3m_bits_f32(v.x & 0xFFFF0000u), acc);
+                        acc = __fmaf_rn(p0.z, l3m_bits_f32(v.y << 16), acc); acc = __fmaf_rn(p0.w, l3m_bits_f32(v.y & 0xFFFF0000u), acc);
+                        acc = __fmaf_rn(p1.x, l3m_bits_f32(v.z << 16), acc); acc = __fmaf_rn(p1.y, l3m_bits_f32(v.z & 0xFFFF0000u), acc);
+                        acc = __fmaf_rn(p1.z, l3m_bits_f32(v.w << 16), acc); acc = __fmaf_rn(p1.w, l3m_bits_f32(v.w & 0xFFFF0000u), acc);
+                        v = vn; p0 = q0; p1 = q1;
+                    }
+                }
+#pragma unroll 4
+                for (; r < cnt; r++) acc = __fmaf_rn(pp[r], l3m_bf16_to_f32(col[r]), acc);
+            } else {
+                const uint16_t *col = kvbuf + tid;
+                for (; r + 8 <= cnt; r += 8) {
+                    const float4 p0 = *(const float4 *)(pp + r), p1 = *(const float4 *)(pp + r + 4);
+                    float vv[8];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) vv[j] = l3m_bf16_to_f32(col[(r + j) * rs]);
+                    acc = __fmaf_rn(p0.x, vv[0], acc); acc = __fmaf_rn(p0.y, vv[1], acc);
+                    acc = __fmaf_rn(p0.z, vv[2], acc); acc = __fmaf_rn(p0.w, vv[3], acc);
+                    acc = __fmaf_rn(p1.x, vv[4], acc); acc = __fmaf_rn(p1.y, vv[5], acc);
+                    acc = __fmaf_rn(p1.z, vv[6], acc); acc = __fmaf_rn(p1.w, vv[7], acc);
+                }
+                for (; r < cnt; r++) acc = __fmaf_rn(pp[r], l3m_bf16_to_f32(col[r * rs]), acc);
+            }
         }
-        __syncthreads();
     }
     for (int i = tid; i < hd; i += nth) out[i] = acc;
     __syncthreads();
