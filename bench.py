@@ -99,12 +99,11 @@ class L2Flush:
         self.rt.cudaDeviceSynchronize()
 
 
-def algorithmic_bytes(name, ctx, n_prompt):
+def algorithmic_bytes(name, positions):
     """Weights once per forward pass plus KV traffic: 2*L*(pos+1)*kv*2 bytes read and 2*L*kv*2 written per position."""
     shape = synth.CONFIGS[name][0]
     L, kvd = shape["n_layers"], shape["dim"] // shape["n_heads"] * shape["n_kv_heads"]
     w = synth.weight_bytes(name)
-    positions = ctx
     kv = sum(2 * L * (p + 1) * kvd * 2 + 2 * L * kvd * 2 for p in range(positions))
     return positions * w + kv, positions
 
@@ -143,6 +142,8 @@ def bench_ours(a):
     _, dtype, _, ctx = synth.CONFIGS[name]
     path = synth.make(name, MODEL_DIR)
     prompt = synth.prompt(4, seed=1, vocab=32000)
+    positions_per_step = min(a.positions or ctx, ctx)
+    max_new = positions_per_step - len(prompt)
     dist = None
     if world > 1:
         import torch.distributed as dist
@@ -151,7 +152,7 @@ def bench_ours(a):
     flush = L2Flush()
     sink = []
     for _ in range(a.warmup):
-        m.generate(prompt, 256, temperature=0, on_token=sink.append)
+        m.generate(prompt, max_new, temperature=0, on_token=sink.append)
     m.perf()
     if dist:
         dist.barrier()
@@ -160,7 +161,7 @@ def bench_ours(a):
         for _ in range(a.steps):
             flush()
             t0 = time.perf_counter_ns()
-            toks = m.generate(prompt, 256, temperature=0, on_token=sink.append)
+            toks = m.generate(prompt, max_new, temperature=0, on_token=sink.append)
             wall_ns.append(time.perf_counter_ns() - t0)
             p = m.perf()
             dev_ns.append(p["ns_compute"] * p["tokens"])
@@ -183,14 +184,15 @@ def bench_ours(a):
         return
     value = total / (t_dev * 1e-9)
     e2e = total / (t_wall * 1e-9)
-    alg, per_launch_pos = algorithmic_bytes(name, ctx, len(prompt))
+    alg, per_launch_pos = algorithmic_bytes(name, positions_per_step)
     launch_s = (t_dev / a.steps) * 1e-9
     peak, peak_kind = measured_peaks()
     achieved = alg / launch_s / 1e9
     traffic = None
     prof = ROOT / "profiles" / "decode_kernel_traffic.json"
     if prof.exists():
-        traffic = json.loads(prof.read_text()).get(name)
+        per_pos = json.loads(prof.read_text()).get(name)               # DRAM bytes per forward pass (ncu)
+        traffic = round(per_pos * per_launch_pos) if per_pos else None
     out = {
         "metric": "batch-1 decode tok/s", "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": a.steps,
         "warmup": a.warmup, "ms_per_step": round(t_dev / a.steps * 1e-6, 4), "higher_is_better": True,
@@ -209,7 +211,7 @@ def bench_ours(a):
         "clocks": clk.summary(),
     }
     if not a.no_cpu:
-        out["cpu_baseline"] = reference_cpu(path, ctx, 256)
+        out["cpu_baseline"] = reference_cpu(path, ctx, max_new)
     print(json.dumps(out), flush=True)
 
 
@@ -256,6 +258,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="SmolLM2-135M-q8_0", choices=list(synth.CONFIGS))
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--positions", type=int, default=0,
+                    help="forward passes per step (default: the whole context); small values make a profiling case")
     a = ap.parse_args()
     if a.warmup < 3:
         ap.error("--warmup must be at least 3")
