@@ -22,7 +22,7 @@ typedef struct {
     int        reference;  // 1 = the fp32 reference path (no activation quantisation), on the GPU
     int        force;      // 1 = load even if the weights will not stay resident in the persisting L2 window
     int        verbose;    // print each GPU's shard sizes against its L2 budget, on stderr
-    int        cold;       // 1 = evict the weights from L2 before each token (not counted as token time)
+    int        cold;       // 1 = no persisting L2 window: the weights compete for L2 (per-token eviction not built)
 } l3m_opts;
 
 // Field order and types are the reference's (src/l3m.h:21-29).
