@@ -1,31 +1,37 @@
-// The persistent decode kernel: one cooperative launch runs a whole l3m_generate call (prompt feed
-// and greedy sampling) on one GPU, one CTA per SM. Replaces the reference's pinned thread pool and
-// its four barriers per layer (src/engine.c:230-281, src/pool.c:111-123): no grid-wide barrier;
-// a CTA waits only for the CTAs that produce what it reads.
+// The decode kernel: one launch runs a whole l3m_generate call (prompt feed and greedy sampling) on
+// one GPU as a single thread-block cluster of kClusterCtas CTAs. Replaces the reference's pinned
+// thread pool and its four barriers per layer (src/engine.c:230-281, src/pool.c:111-123).
 //
-// Per layer (step s, exchange buffers double-buffered by s % 2):
-//   A  head CTAs: rmsnorm, q/k/v rows of their head, RoPE, KV row, attention  -> attn
-//   B  wo CTAs:   wait attn, matvec                                           -> proj
-//   C  all CTAs:  wait proj, x += proj, presence; ffn CTAs: rmsnorm, up and
-//                 gate matvecs, SiLU gate                                      -> h
-//   D  down CTAs: wait h, matvec                                              -> down
-//   next layer / end of token: all CTAs wait down and every CTA's presence, x += down
-// Presence makes every CTA finish reading step s before anyone writes step s + 2, so two buffers
-// suffice. After the last prompt position each position ends with the head matvec, a per-CTA
-// argmax and an all-to-all exchange of (max, index) that every CTA reduces in CTA order.
-//
-// An exchange is a float buffer plus an arrival counter. A producer writes its floats and adds its
-// arrival (release); one thread of each consumer polls the counter (acquire, short sleeps) and
-// then the whole CTA reads the floats once. A single polled word per exchange keeps L2 free for
-// the CTAs doing the work. Presence is an arrival on the down counter.
+// Every CTA keeps the residual x in its shared memory. Each matrix is split into contiguous runs of
+// 16-row tiles over the CTAs (the reference's split over ranks, src/engine.c:88-91). A CTA writes
+// its slice of every produced vector straight into the shared memory of all CTAs of the cluster
+// (distributed shared memory) and a hardware cluster barrier (release/acquire) makes it visible, so
+// an exchange costs a few hundred nanoseconds and no global-memory round trip. Per layer:
+//   Q  qkv CTAs:  rmsnorm, their tiles of the q/k/v rows                   -> qkv      barrier 1
+//   A  head CTAs: RoPE, KV row, attention (K/V copies started before 1)   -> attn     barrier 2
+//   B  wo CTAs:   matvec                                                  -> proj     barrier 3
+//   C  all:       x += proj; ffn CTAs: rmsnorm, up and gate, SiLU gate    -> h        barrier 4
+//   D  down CTAs: matvec                                                  -> down     barrier 5
+//   all:          x += down
+// After the last prompt position each position ends with the head matvec (logits kept for
+// l3m_logits), a per-CTA argmax, an all-gather of (max, index, host stop) and the same global
+// argmax in every CTA, in CTA order. Each exchanged vector has one buffer: its next write comes at
+// least one barrier after every reader has finished with it. The weights of the next layer are
+// prefetched into L2 a layer ahead; each layer's norm weights and RoPE row are copied into shared
+// memory while the previous layer runs. No CTA ever spins on memory: the only waits are cluster
+// barriers, which every CTA reaches the same number of times.
 #include <cstdio>
+#include <cooperative_groups.h>
 #include "ops.cuh"
 #include "decode.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace l3m {
 
 struct Smem {
-    float *x, *xb, *tmp, *y, *att2, *scores, *att, *red, *wa, *wf, *wh;
+    float *x, *xb, *tmp, *y, *scores, *att, *red, *wa, *wf, *wh;
+    float *xq, *xa, *xp, *xh, *xd, *xt;
     float2 *rope;
     uint16_t *kcur, *vcur, *kvbuf, *vtbuf;
     float2 *scratch;
@@ -38,13 +44,18 @@ __device__ __forceinline__ Smem carve(unsigned char *base, const DecodeArgs &a) 
     s.xb = (float *)(base + a.sm_xb);
     s.tmp = (float *)(base + a.sm_tmp);
     s.y = (float *)(base + a.sm_y);
-    s.att2 = (float *)(base + a.sm_y2);
     s.scores = (float *)(base + a.sm_scores);
     s.att = (float *)(base + a.sm_att);
     s.red = (float *)(base + a.sm_red);
     s.wa = (float *)(base + a.sm_wa);
     s.wf = (float *)(base + a.sm_wf);
     s.wh = (float *)(base + a.sm_wh);
+    s.xq = (float *)(base + a.sm_xq);
+    s.xa = (float *)(base + a.sm_xa);
+    s.xp = (float *)(base + a.sm_xp);
+    s.xh = (float *)(base + a.sm_xh);
+    s.xd = (float *)(base + a.sm_xd);
+    s.xt = (float *)(base + a.sm_xt);
     s.rope = (float2 *)(base + a.sm_rope);
     s.kcur = (uint16_t *)(base + a.sm_kv);
     s.vcur = s.kcur + a.hd;
@@ -58,68 +69,39 @@ __device__ __forceinline__ Smem carve(unsigned char *base, const DecodeArgs &a) 
     return s;
 }
 
-__device__ __forceinline__ void st_release_u32(uint32_t *p, uint32_t v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t *p) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ float ld_relaxed_f32(const float *p) {
-    float v;
-    asm volatile("ld.relaxed.gpu.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
-    return v;
+// Every thread of every CTA of the cluster: writes before it (shared, distributed shared and global
+// memory) are visible to every thread of the cluster after it.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-__device__ __forceinline__ uint32_t *counter(const DecodeArgs &a, int x, uint32_t epoch) {
-    return a.ctr + (x * 2 + (epoch & 1)) * 32;
-}
-
-// This CTA's part of exchange x at `epoch` is written (or, for presence, its reads are done):
-// after the barrier one thread adds its arrival with release semantics, which covers every
-// thread's writes before the barrier.
-__device__ __forceinline__ void publish(const DecodeArgs &a, int x, uint32_t epoch) {
-    __syncthreads();
-    if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(counter(a, x, epoch)) : "memory");
-}
-
-// Wait until exchange x has every arrival of `epoch` (counters only grow within a launch: the
-// k-th use of a parity half expects k * arrivals). False on timeout or another CTA's abort.
-__device__ __noinline__ bool wait_x(const DecodeArgs &a, int x, uint32_t epoch) {
-    bool ok = true;
-    if (threadIdx.x == 0) {
-        const uint32_t *c = counter(a, x, epoch), want = ((epoch + 1) >> 1) * (uint32_t)a.arrivals[x];
-        const uint64_t t0 = globaltimer_ns();
-        for (int spins = 0;; spins++) {
-            if (ld_acquire_u32(c) >= want) break;
-            __nanosleep(32);
-            if ((spins & 255) == 255) {
-                if (globaltimer_ns() - t0 > a.timeout_ns) { atomicCAS(a.abort_flag, 0, kErrTimeout); ok = false; break; }
-                if (*(volatile int *)a.abort_flag) { ok = false; break; }
-            }
+// src[0, n) (this CTA's slice, shared memory) to dst[g0, g0 + n) in the shared memory of every CTA of
+// the cluster, this one included. Visible to the readers after the next cluster_sync.
+__device__ __noinline__ void scatter(const float *src, float *dst, int g0, int n) {
+    cg::cluster_group cl = cg::this_cluster();
+    const int tid = threadIdx.x, nth = blockDim.x, nr = (int)cl.num_blocks();
+    if (((g0 | n) & 3) == 0) {
+        const int n4 = n >> 2;
+        for (int e = tid; e < n4 * nr; e += nth) {
+            const int r = e % nr, j = e / nr;
+            float4 *d = (float4 *)cl.map_shared_rank(dst + g0, (unsigned)r);
+            d[j] = ((const float4 *)src)[j];
+        }
+    } else {
+        for (int e = tid; e < n * nr; e += nth) {
+            const int r = e % nr, j = e / nr;
+            cl.map_shared_rank(dst + g0, (unsigned)r)[j] = src[j];
         }
     }
-    return __syncthreads_and(ok);
-}
-
-// Read n exchanged floats into shared memory (after wait_x).
-__device__ __forceinline__ void read_x(const float *src, int n, float *dst) {
-    for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = ld_relaxed_f32(src + i);
-    __syncthreads();
-}
-
-__device__ __forceinline__ float *xbuf(const DecodeArgs &a, int off, uint32_t epoch) {
-    return a.xd + (epoch & 1) * a.xd_half + off;
 }
 
 __device__ __forceinline__ void trace(const DecodeArgs &a, int slot, int pos, int l, int ev) {
     if (a.trace && slot >= 0 && threadIdx.x == 0)
-        a.trace[(((size_t)slot * a.ctx + pos) * (a.n_layers + 1) + l) * 16 + ev] = globaltimer_ns();
+        a.trace[(((size_t)slot * a.ctx + pos) * (a.n_layers + 1) + l) * kTraceEvents + ev] = globaltimer_ns();
 }
 
-// Pull a CTA's weight tiles for layer l into L2 ahead of use (cp.async.bulk.prefetch: no registers,
-// no completion to wait for). Every tile range is 16-byte aligned and a multiple of 16 bytes.
+// Pull a CTA's weight tiles into L2 ahead of use (cp.async.bulk.prefetch: no registers, no
+// completion to wait for). Every tile range is 16-byte aligned and a multiple of 16 bytes.
 __device__ __forceinline__ void prefetch_l2(const void *p, size_t bytes) {
     for (size_t o = 0; o < bytes; o += (1u << 20)) {
         const uint32_t n = (uint32_t)min(bytes - o, (size_t)1 << 20);
@@ -131,13 +113,22 @@ __device__ void prefetch_layer(const DecodeArgs &a, const LayerDev &L, const Rol
     if (threadIdx.x != 0) return;
     const size_t tq = tile_bytes(L.dt_qkv, a.dim), to = tile_bytes(L.dt_wo, a.dim), tu = tile_bytes(L.dt_up, a.dim),
                  tg = tile_bytes(L.dt_gate, a.dim), td = tile_bytes(L.dt_down, a.ffn);
-    if (r.head >= 0) prefetch_l2(L.qkv + (size_t)r.head * a.unit_tiles * tq, (size_t)a.unit_tiles * tq);
+    if (r.qkv0 < r.qkv1) prefetch_l2(L.qkv + r.qkv0 * tq, (size_t)(r.qkv1 - r.qkv0) * tq);
     if (r.wo0 < r.wo1) prefetch_l2(L.wo + r.wo0 * to, (size_t)(r.wo1 - r.wo0) * to);
     if (r.ffn0 < r.ffn1) {
         prefetch_l2(L.up + r.ffn0 * tu, (size_t)(r.ffn1 - r.ffn0) * tu);
         prefetch_l2(L.gate + r.ffn0 * tg, (size_t)(r.ffn1 - r.ffn0) * tg);
     }
     if (r.dn0 < r.dn1) prefetch_l2(L.down + r.dn0 * td, (size_t)(r.dn1 - r.dn0) * td);
+}
+
+// The norm weights of layer L and the RoPE row of position pos, into shared memory (asynchronous;
+// the top of the next layer waits for them).
+__device__ void stage_vectors(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s, int pos) {
+    if (role.qkv0 < role.qkv1) stage_f32(s.wa, L.attn_norm, a.dim);
+    if (role.ffn0 < role.ffn1) stage_f32(s.wf, L.ffn_norm, a.dim);
+    if (role.head0 >= 0 && a.rope && pos < a.ctx) stage_f32((float *)s.rope, (const float *)(a.rope + (size_t)pos * (a.hd / 2)), a.hd);
+    cp_async_commit();
 }
 
 // x = embedding row of tok (reference src/engine.c:236, src/pack.c:55-62).
@@ -169,54 +160,218 @@ __device__ __noinline__ void embed_row(const DecodeArgs &a, int tok, float *x) {
     __syncthreads();
 }
 
-// Phase A for query head h of layer L at position pos: writes attn[h*hd, (h+1)*hd).
-__device__ __noinline__ void phase_attention(const DecodeArgs &a, const LayerDev &L, const Role &role, int pos, float *attn, Smem &s,
-                                             int tslot, int l) {
-    const int tid = threadIdx.x, nth = blockDim.x, hd = a.hd, h = role.head, kvh = h / a.hpk;
+// Phase Q: this CTA's tiles of the q/k/v rows (biases added) -> every CTA's xq.
+__device__ __noinline__ void phase_qkv(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s) {
     rmsnorm_exact(s.x, s.wa, a.dim, a.eps, s.xb, s.tmp, s.red);
-    trace(a, tslot, pos, l, 8);
     prepare(L.dt_qkv, s.xb, a.dim, s.prep);
-    trace(a, tslot, pos, l, 9);
-    float *y = s.y;
-    const uint8_t *unit = L.qkv + (size_t)h * a.unit_tiles * tile_bytes(L.dt_qkv, a.dim);
-    matvec_exact(L.dt_qkv, unit, a.dim, 0, a.unit_tiles, s.prep, s.scratch, a.scratch_pairs, y);
-    trace(a, tslot, pos, l, 10);
+    matvec_exact(L.dt_qkv, L.qkv, a.dim, role.qkv0, role.qkv1, s.prep, s.scratch, a.scratch_pairs, s.y);
+    const int g0 = role.qkv0 * kTile, n = min(role.qkv1 * kTile, a.n_qkv) - g0, nq = a.n_heads * a.hd, nk = a.n_kv * a.hd;
     if (L.bq) {
-        for (int i = tid; i < hd; i += nth) {
-            y[i] = __fadd_rn(y[i], __ldg(L.bq + h * hd + i));
-            y[hd + i] = __fadd_rn(y[hd + i], __ldg(L.bk + kvh * hd + i));
-            y[2 * hd + i] = __fadd_rn(y[2 * hd + i], __ldg(L.bv + kvh * hd + i));
+        for (int o = threadIdx.x; o < n; o += blockDim.x) {
+            const int r = g0 + o;
+            s.y[o] = __fadd_rn(s.y[o], __ldg(r < nq ? L.bq + r : r < nq + nk ? L.bk + (r - nq) : L.bv + (r - nq - nk)));
         }
         __syncthreads();
     }
+    scatter(s.y, s.xq, g0, n);
+}
+
+__device__ __forceinline__ const uint16_t *kcache(const DecodeArgs &a, const LayerDev &L, int h) {
+    return L.kc + (size_t)(h / a.hpk) * a.ctx * a.hd;
+}
+__device__ __forceinline__ const uint16_t *vcache(const DecodeArgs &a, const LayerDev &L, int h) {
+    return L.vc + (size_t)(h / a.hpk) * a.hd * a.vstride;
+}
+
+// Phase A for query head h at position pos (xq complete): RoPE, this position's K/V row (stored by
+// the first head of each kv group), attention -> every CTA's xa[h*hd, (h+1)*hd).
+__device__ __noinline__ void phase_attention(const DecodeArgs &a, const LayerDev &L, const Smem &s, int h, int pos, bool prestaged) {
+    const int tid = threadIdx.x, nth = blockDim.x, hd = a.hd, kvh = h / a.hpk, nq = a.n_heads * hd, nk = a.n_kv * hd;
+    float *y = s.y;                                                  // q, k, v of this head
+    for (int i = tid; i < hd; i += nth) {
+        y[i] = s.xq[h * hd + i];
+        y[hd + i] = s.xq[nq + kvh * hd + i];
+        y[2 * hd + i] = s.xq[nq + nk + kvh * hd + i];
+    }
+    __syncthreads();
     if (a.rope) {
         rope_exact(y, hd, s.rope);
         rope_exact(y + hd, hd, s.rope);
     }
-    uint16_t *kc = L.kc + (size_t)kvh * a.ctx * hd, *vc = L.vc + (size_t)kvh * hd * a.vstride;
+    uint16_t *kc = (uint16_t *)kcache(a, L, h), *vc = (uint16_t *)vcache(a, L, h);
+    const bool writer = h % a.hpk == 0;
     for (int i = tid; i < hd; i += nth) {
         const uint16_t kb = l3m_f32_to_bf16(y[hd + i]), vb = l3m_f32_to_bf16(y[2 * hd + i]);
         s.kcur[i] = kb;
         s.vcur[i] = vb;
-        if (role.kv_writer) {
+        if (writer) {
             kc[(size_t)pos * hd + i] = kb;
             vc[(size_t)i * a.vstride + pos] = vb;
         }
     }
     __syncthreads();
-    trace(a, tslot, pos, l, 11);
     attend_exact<true>(y, kc, vc, hd, a.vstride, s.kcur, s.vcur, pos, hd, s.scores, s.att, s.red, a.elist, a.eindex, s.kvbuf, s.vtbuf,
-                       a.attn_chunk);
+                       a.attn_chunk, prestaged);
+    scatter(s.att, s.xa, h * hd, hd);
+}
+
+// Phase B: this CTA's tiles of wo over attn -> every CTA's xp.
+__device__ __noinline__ void phase_wo(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s) {
+    prepare(L.dt_wo, s.xa, a.dim, s.prep);
+    matvec_exact(L.dt_wo, L.wo, a.dim, role.wo0, role.wo1, s.prep, s.scratch, a.scratch_pairs, s.y);
+    const int g0 = role.wo0 * kTile, n = min(role.wo1 * kTile, a.dim) - g0;
+    if (L.bo) {
+        for (int o = threadIdx.x; o < n; o += blockDim.x) s.y[o] = __fadd_rn(s.y[o], __ldg(L.bo + g0 + o));
+        __syncthreads();
+    }
+    scatter(s.y, s.xp, g0, n);
+}
+
+// Phase C: x += proj in every CTA; the ffn CTAs' tiles of up and gate, SiLU gate -> every CTA's xh.
+__device__ __noinline__ void phase_ffn(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s, int pos, int l, int tslot) {
+    const int tid = threadIdx.x, nth = blockDim.x;
+    for (int i = tid; i < a.dim; i += nth) s.x[i] = __fadd_rn(s.x[i], s.xp[i]);
+    __syncthreads();
+    if (role.ffn0 >= role.ffn1) return;
+    rmsnorm_exact(s.x, s.wf, a.dim, a.eps, s.xb, s.tmp, s.red);
+    trace(a, tslot, pos, l, 7);
+    const int nf = role.ffn1 - role.ffn0;
+    prepare(L.dt_up, s.xb, a.dim, s.prep);
     trace(a, tslot, pos, l, 12);
-    for (int i = tid; i < hd; i += nth) attn[h * hd + i] = s.att[i];
+    matvec_exact(L.dt_up, L.up, a.dim, role.ffn0, role.ffn1, s.prep, s.scratch, a.scratch_pairs, s.y);
+    if (L.dt_gate != L.dt_up) prepare(L.dt_gate, s.xb, a.dim, s.prep);
+    matvec_exact(L.dt_gate, L.gate, a.dim, role.ffn0, role.ffn1, s.prep, s.scratch, a.scratch_pairs, s.y + nf * kTile);
+    trace(a, tslot, pos, l, 13);
+    const int g0 = role.ffn0 * kTile, n = min(role.ffn1 * kTile, a.ffn) - g0;
+    for (int o = tid; o < n; o += nth) {
+        const float up = L.b_up ? __fadd_rn(s.y[o], __ldg(L.b_up + g0 + o)) : s.y[o];
+        s.tmp[o] = silu_mul(up, s.y[nf * kTile + o], a.elist, a.eindex);
+    }
+    __syncthreads();
+    scatter(s.tmp, s.xh, g0, n);
+}
+
+// Phase D: this CTA's tiles of down over h -> every CTA's xd.
+__device__ __noinline__ void phase_down(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s) {
+    prepare(L.dt_down, s.xh, a.ffn, s.prep);
+    matvec_exact(L.dt_down, L.down, a.ffn, role.dn0, role.dn1, s.prep, s.scratch, a.scratch_pairs, s.y);
+    const int g0 = role.dn0 * kTile, n = min(role.dn1 * kTile, a.dim) - g0;
+    if (L.b_down) {
+        for (int o = threadIdx.x; o < n; o += blockDim.x) s.y[o] = __fadd_rn(s.y[o], __ldg(L.b_down + g0 + o));
+        __syncthreads();
+    }
+    scatter(s.y, s.xd, g0, n);
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Thread 0 waits until *p >= want (or, with done_ok, *p == kHeadDone), sleeping between polls; the
+// whole CTA learns the outcome: 1 reached, 0 done, -1 timeout or another CTA's abort.
+__device__ __noinline__ int wait_word(const DecodeArgs &a, const uint32_t *p, uint32_t want, bool done_ok) {
+    __shared__ int res;
+    if (threadIdx.x == 0) {
+        const uint64_t t0 = globaltimer_ns();
+        int r = -1;
+        for (int spins = 0;; spins++) {
+            const uint32_t v = ld_acquire_u32(p);
+            if (done_ok && v == kHeadDone) { r = 0; break; }
+            if (v >= want && v != kHeadDone) { r = 1; break; }
+            __nanosleep(done_ok ? 256 : 64);
+            if ((spins & 255) == 255) {
+                if (globaltimer_ns() - t0 > a.hx.timeout_ns) { atomicCAS(a.hx.abort_flag, 0, kErrTimeout); break; }
+                if (*(volatile int *)a.hx.abort_flag) break;
+            }
+        }
+        res = r;
+    }
+    __syncthreads();
+    const int r = res;
+    __syncthreads();
+    return r;
+}
+
+// The head matvec over this CTA's vocabulary tiles of the final x in s.x (logits kept for
+// l3m_logits), this CTA's argmax -> hx.slots[cta] with an arrival on hx.count. host_stop: the
+// host's stop request (cluster 0, CTA 0 only).
+__device__ __noinline__ void head_logits(const DecodeArgs &a, const Role &role, const Smem &s, int pos, int host_stop, int tslot) {
+    const int cta = blockIdx.x, tid = threadIdx.x, nth = blockDim.x;
+    float best = -INFINITY;
+    int best_i = -1;
+    if (role.voc0 < role.voc1) {
+        rmsnorm_exact(s.x, s.wh, a.dim, a.eps, s.xb, s.tmp, s.red);
+        trace(a, tslot, pos, a.n_layers, 3);
+        prepare(a.dt_head, s.xb, a.dim, s.prep);
+        trace(a, tslot, pos, a.n_layers, 4);
+        matvec_exact(a.dt_head, a.head, a.dim, role.voc0, role.voc1, s.prep, s.scratch, a.scratch_pairs, s.y);
+        trace(a, tslot, pos, a.n_layers, 5);
+        float *lg = a.logits + (size_t)pos * a.vocab;
+        const int g0 = role.voc0 * kTile, n = min(role.voc1 * kTile, a.vocab) - g0;
+        for (int o = tid; o < n; o += nth) {
+            const float v = s.y[o];
+            lg[g0 + o] = v;
+            if (v > best) { best = v; best_i = g0 + o; }                      // this thread's outputs rise with o
+        }
+    }
+    // CTA argmax: the largest value, the lowest index among equals (reference engine.c:293-294).
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+        if (ov > best || (ov == best && oi >= 0 && (best_i < 0 || oi < best_i))) { best = ov; best_i = oi; }
+    }
+    if ((tid & 31) == 0) { s.red[tid >> 5] = best; ((int *)s.red)[32 + (tid >> 5)] = best_i; }
+    __syncthreads();
+    if (tid == 0) {
+        float m = -INFINITY;
+        int mi = -1;
+        for (int w = 0; w < nth / 32; w++) {
+            const float v = s.red[w];
+            const int vi = ((int *)s.red)[32 + w];
+            if (v > m || (v == m && vi >= 0 && (mi < 0 || vi < mi))) { m = v; mi = vi; }
+        }
+        if (mi < 0) mi = role.voc0 * kTile;                                   // an empty or all-NaN slice
+        a.hx.slots[3 * cta] = m;
+        a.hx.slots[3 * cta + 1] = __int_as_float(mi);
+        a.hx.slots[3 * cta + 2] = __int_as_float(host_stop);
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.hx.count) : "memory");
+    }
+    __syncthreads();
+}
+
+// A CTA outside cluster 0: between sampled positions it sleeps on hx.flag; for each published x it
+// computes its vocabulary tiles. Ends when cluster 0 writes kHeadDone (or on a failed wait).
+__device__ __noinline__ void head_helper(const DecodeArgs &a, const Role &role, const Smem &s) {
+    if (role.voc0 < role.voc1 && threadIdx.x == 0) {
+        const size_t th = tile_bytes(a.dt_head, a.dim);
+        prefetch_l2(a.head + role.voc0 * th, (size_t)(role.voc1 - role.voc0) * th);
+    }
+    for (uint32_t e = 1;; e++) {
+        if (wait_word(a, a.hx.flag, e, true) <= 0) return;
+        const int pos = __float_as_int(ld_cg_f32(a.hx.x + a.dim));
+        if ((a.dim & 3) == 0)
+            for (int i = threadIdx.x * 4; i < a.dim; i += blockDim.x * 4) *(float4 *)(s.x + i) = __ldcg((const float4 *)(a.hx.x + i));
+        else
+            for (int i = threadIdx.x; i < a.dim; i += blockDim.x) s.x[i] = ld_cg_f32(a.hx.x + i);
+        cp_async_wait_all();                                              // the final norm's weights
+        __syncthreads();
+        head_logits(a, role, s, pos, 0, -1);
+        if (role.voc0 < role.voc1 && threadIdx.x == 0) {                  // the next position reads the same tiles
+            const size_t th = tile_bytes(a.dt_head, a.dim);
+            prefetch_l2(a.head + role.voc0 * th, (size_t)(role.voc1 - role.voc0) * th);
+        }
+    }
 }
 
 __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeArgs *__restrict__ ap) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    // The arguments, this CTA's role and every layer's pointers live in shared memory for the whole
-    // launch: reading them never waits on L1 misses behind the streamed weights.
+    // The arguments, this CTA's role, every layer's pointers and the carved shared-memory pointers
+    // live in shared memory for the whole launch.
     __shared__ DecodeArgs sh_args;
     __shared__ Role sh_role;
+    __shared__ Smem sh_s;
     if (threadIdx.x == 0) {
         sh_args = *ap;
         sh_role = ap->roles[blockIdx.x];
@@ -229,164 +384,114 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
         for (int i = threadIdx.x; i < a.n_layers * (int)(sizeof(LayerDev) / 4); i += blockDim.x) dst[i] = src[i];
     }
     const LayerDev *layers = (const LayerDev *)(smem_raw + a.sm_layers);
+    if (threadIdx.x == 0) sh_s = carve(smem_raw, a);
     __syncthreads();
-    Smem s = carve(smem_raw, a);
-    const int cta = blockIdx.x, tid = threadIdx.x, nth = blockDim.x;
+    const Smem &s = sh_s;
     const Role &role = sh_role;
-    int tslot = -1;
-    for (int i = 0; i < 4; i++) if (a.trace_cta[i] == cta) tslot = i;
-    uint32_t step = 0, tcount = 0;
-    int n_gen = 0, tok = 0, pos = 0, err = 0;
+    const int cta = blockIdx.x, tid = threadIdx.x;
+    const int tslot = a.trace_cta[0] == cta ? 0 : a.trace_cta[1] == cta ? 1 : -1;
+    int n_gen = 0, tok = 0, pos = 0;
+    uint32_t tcount = 0;
     bool ok = true;
+    if (role.voc0 < role.voc1) stage_f32(s.wh, a.norm, a.dim);
+    if (cta >= kClusterCtas) {                                            // the other clusters: head tiles only
+        cp_async_commit();
+        head_helper(a, role, s);
+        cp_async_wait_all();
+        return;
+    }
+    stage_vectors(a, layers[0], role, s, 0);
+    cluster_sync();                                                       // every CTA of the cluster has started
 
     for (pos = 0;; pos++) {
         const bool last = pos >= a.n_prompt - 1;
         if (pos < a.n_prompt) tok = a.prompt[pos];
         const bool stop_after = last && (n_gen >= a.max_new || pos + 1 >= a.ctx);   // reference engine.c:322, 352
         embed_row(a, tok, s.x);
-        for (int l = 0; l < a.n_layers && ok; l++) {
-            ++step;
+        for (int l = 0; l < a.n_layers; l++) {
             const LayerDev &L = layers[l];
             if (l + 1 < a.n_layers) prefetch_layer(a, layers[l + 1], role);
             else {
                 prefetch_layer(a, layers[0], role);
-                if (last && role.voc0 < role.voc1 && threadIdx.x == 0) {
+                if (last && role.voc0 < role.voc1 && tid == 0) {
                     const size_t th = tile_bytes(a.dt_head, a.dim);
                     prefetch_l2(a.head + role.voc0 * th, (size_t)(role.voc1 - role.voc0) * th);
                 }
             }
-            // This layer's small vectors into shared memory while the exchange below is awaited.
-            if (role.head >= 0) {
-                stage_f32(s.wa, L.attn_norm, a.dim);
-                if (a.rope) stage_f32((float *)s.rope, (const float *)(a.rope + (size_t)pos * (a.hd / 2)), a.hd);
-            }
-            if (role.ffn0 < role.ffn1) stage_f32(s.wf, L.ffn_norm, a.dim);
-            if (l + 1 == a.n_layers && last && role.voc0 < role.voc1) stage_f32(s.wh, a.norm, a.dim);
-            cp_async_commit();
-            if (l > 0) {
-                if (!(ok = wait_x(a, kXDown, step - 1))) break;
-                read_x(xbuf(a, a.d_down, step - 1), a.dim, s.tmp);
-                for (int i = tid; i < a.dim; i += nth) s.x[i] = __fadd_rn(s.x[i], s.tmp[i]);
-            }
-            cp_async_wait_all();
+            cp_async_wait_all();                                          // this layer's norm weights and RoPE row
             __syncthreads();
             trace(a, tslot, pos, l, 0);
-            if (role.head >= 0) {                                            // A
-                phase_attention(a, L, role, pos, xbuf(a, a.d_attn, step), s, tslot, l);
-                publish(a, kXAttn, step);
-            }
+            if (role.head0 >= 0)                                          // K/V copies land during Q
+                attend_prestage<true>(kcache(a, L, role.head0), vcache(a, L, role.head0), a.hd, a.vstride, pos, a.hd, s.kvbuf, s.vtbuf,
+                                      a.attn_chunk);
+            if (role.qkv0 < role.qkv1) phase_qkv(a, L, role, s);          // Q
             trace(a, tslot, pos, l, 1);
-            if (role.wo0 < role.wo1) {                                       // B
-                if (!(ok = wait_x(a, kXAttn, step))) break;
-                trace(a, tslot, pos, l, 2);
-                read_x(xbuf(a, a.d_attn, step), a.dim, s.xb);
-                prepare(L.dt_wo, s.xb, a.dim, s.prep);
-                matvec_exact(L.dt_wo, L.wo, a.dim, role.wo0, role.wo1, s.prep, s.scratch, a.scratch_pairs, s.y);
-                float *out = xbuf(a, a.d_proj, step);
-                const int g0 = role.wo0 * kTile, n = min(role.wo1 * kTile, a.dim) - g0;
-                for (int o = tid; o < n; o += nth) out[g0 + o] = L.bo ? __fadd_rn(s.y[o], __ldg(L.bo + g0 + o)) : s.y[o];
-                publish(a, kXProj, step);
-            }
-            if (!(ok = wait_x(a, kXProj, step))) break;                      // C
+            cluster_sync();                                               // 1: qkv
+            trace(a, tslot, pos, l, 2);
+            for (int h = role.head0; h >= 0 && h < a.n_heads; h += kClusterCtas)   // A
+                phase_attention(a, L, s, h, pos, h == role.head0);
             trace(a, tslot, pos, l, 3);
-            read_x(xbuf(a, a.d_proj, step), a.dim, s.tmp);
-            for (int i = tid; i < a.dim; i += nth) s.x[i] = __fadd_rn(s.x[i], s.tmp[i]);
-            publish(a, kXDown, step);                                       // presence: done reading step - 1
-            if (role.ffn0 < role.ffn1) {
-                rmsnorm_exact(s.x, s.wf, a.dim, a.eps, s.xb, s.tmp, s.red);
-                trace(a, tslot, pos, l, 13);
-                prepare(L.dt_up, s.xb, a.dim, s.prep);
-                matvec_exact(L.dt_up, L.up, a.dim, role.ffn0, role.ffn1, s.prep, s.scratch, a.scratch_pairs, s.y);
-                trace(a, tslot, pos, l, 14);
-                if (L.dt_gate != L.dt_up) prepare(L.dt_gate, s.xb, a.dim, s.prep);
-                matvec_exact(L.dt_gate, L.gate, a.dim, role.ffn0, role.ffn1, s.prep, s.scratch, a.scratch_pairs, s.att2);
-                trace(a, tslot, pos, l, 15);
-                float *out = xbuf(a, a.d_h, step);
-                const int g0 = role.ffn0 * kTile, n = min(role.ffn1 * kTile, a.ffn) - g0;
-                for (int o = tid; o < n; o += nth) {
-                    const float up = L.b_up ? __fadd_rn(s.y[o], __ldg(L.b_up + g0 + o)) : s.y[o];
-                    out[g0 + o] = silu_mul(up, s.att2[o], a.elist, a.eindex);
-                }
-                publish(a, kXH, step);
-            }
+            cluster_sync();                                               // 2: attn
             trace(a, tslot, pos, l, 4);
-            if (role.dn0 < role.dn1) {                                       // D
-                if (!(ok = wait_x(a, kXH, step))) break;
-                trace(a, tslot, pos, l, 5);
-                read_x(xbuf(a, a.d_h, step), a.ffn, s.xb);
-                prepare(L.dt_down, s.xb, a.ffn, s.prep);
-                matvec_exact(L.dt_down, L.down, a.ffn, role.dn0, role.dn1, s.prep, s.scratch, a.scratch_pairs, s.y);
-                float *out = xbuf(a, a.d_down, step);
-                const int g0 = role.dn0 * kTile, n = min(role.dn1 * kTile, a.dim) - g0;
-                for (int o = tid; o < n; o += nth) out[g0 + o] = L.b_down ? __fadd_rn(s.y[o], __ldg(L.b_down + g0 + o)) : s.y[o];
-                publish(a, kXDown, step);
-            }
+            if (role.wo0 < role.wo1) phase_wo(a, L, role, s);             // B
+            trace(a, tslot, pos, l, 5);
+            cluster_sync();                                               // 3: proj
             trace(a, tslot, pos, l, 6);
+            phase_ffn(a, L, role, s, pos, l, tslot);                      // C
+            // The next layer's norm weights (and the next position's RoPE row) while the rest runs.
+            if (l + 1 < a.n_layers) stage_vectors(a, layers[l + 1], role, s, pos);
+            else stage_vectors(a, layers[0], role, s, pos + 1);
+            trace(a, tslot, pos, l, 8);
+            cluster_sync();                                               // 4: h
+            trace(a, tslot, pos, l, 9);
+            if (role.dn0 < role.dn1) phase_down(a, L, role, s);           // D
+            trace(a, tslot, pos, l, 10);
+            cluster_sync();                                               // 5: down
+            for (int i = tid; i < a.dim; i += blockDim.x) s.x[i] = __fadd_rn(s.x[i], s.xd[i]);
+            __syncthreads();
+            trace(a, tslot, pos, l, 11);
         }
-        if (!ok) break;
-        if (!(ok = wait_x(a, kXDown, step))) break;
-        read_x(xbuf(a, a.d_down, step), a.dim, s.tmp);
-        for (int i = tid; i < a.dim; i += nth) s.x[i] = __fadd_rn(s.x[i], s.tmp[i]);
-        __syncthreads();
-        trace(a, tslot, pos, a.n_layers, 0);
-        if (!last) continue;
-
-        // Head: logits for this position and this CTA's share of the argmax.
+        if (!last) continue;                                              // the next position starts from its embedding
         ++tcount;
+        // Publish x to every CTA of the launch (cluster 0's copies are identical), then this CTA's tiles.
+        if (cta == 0) {
+            for (int i = tid; i < a.dim; i += blockDim.x) a.hx.x[i] = s.x[i];
+            if (tid == 0) a.hx.x[a.dim] = __int_as_float(pos);
+            __syncthreads();
+            if (tid == 0) asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.hx.flag), "r"(tcount) : "memory");
+        }
+        trace(a, tslot, pos, a.n_layers, 0);
         int host_stop = 0;
         if (cta == 0 && tid == 0) host_stop = ld_relaxed_sys_i32((const int *)&a.ctrl->stop_request);
-        float best = -INFINITY;
-        int best_i = -1;
-        if (role.voc0 < role.voc1) {
-            rmsnorm_exact(s.x, s.wh, a.dim, a.eps, s.xb, s.tmp, s.red);
-            prepare(a.dt_head, s.xb, a.dim, s.prep);
-            matvec_exact(a.dt_head, a.head, a.dim, role.voc0, role.voc1, s.prep, s.scratch, a.scratch_pairs, s.y);
-            float *lg = a.logits + (size_t)pos * a.vocab;
-            const int g0 = role.voc0 * kTile, n = min(role.voc1 * kTile, a.vocab) - g0;
-            for (int o = tid; o < n; o += nth) {
-                const float v = s.y[o];
-                lg[g0 + o] = v;
-                if (v > best) { best = v; best_i = g0 + o; }                  // this thread's outputs rise with o
-            }
-        }
+        head_logits(a, role, s, pos, host_stop, tslot);
         trace(a, tslot, pos, a.n_layers, 1);
-        if (stop_after) break;                                              // logits kept, nothing sampled
-        // CTA argmax: the largest value, the lowest index among equals (reference engine.c:293-294).
-        for (int o = 16; o; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
-            if (ov > best || (ov == best && oi >= 0 && (best_i < 0 || oi < best_i))) { best = ov; best_i = oi; }
-        }
-        if ((tid & 31) == 0) { s.red[tid >> 5] = best; ((int *)s.red)[32 + (tid >> 5)] = best_i; }
-        __syncthreads();
-        float *tx = xbuf(a, a.d_tok, tcount);
-        if (tid == 0) {
-            float m = -INFINITY;
-            int mi = -1;
-            for (int w = 0; w < nth / 32; w++) {
-                const float v = s.red[w];
-                const int vi = ((int *)s.red)[32 + w];
-                if (v > m || (v == m && vi >= 0 && (mi < 0 || vi < mi))) { m = v; mi = vi; }
+        // CTA 0 waits for every CTA's (max, index) (so every slice of the logits is written, also when
+        // nothing is sampled), reduces them in CTA order (vocabulary order, reference
+        // engine.c:299-300) and hands the result to cluster 0, so all 16 decide alike.
+        if (cta == 0) {
+            const int r = wait_word(a, a.hx.count, tcount * (uint32_t)a.grid, false);
+            if (tid == 0) {
+                float gmax = -INFINITY;
+                int next = 0;
+                for (int c = 0; c < a.grid; c++) {
+                    const float v = ld_cg_f32(a.hx.slots + 3 * c);
+                    if (v > gmax) { gmax = v; next = __float_as_int(ld_cg_f32(a.hx.slots + 3 * c + 1)); }
+                }
+                s.tmp[0] = __int_as_float(next);
+                s.tmp[1] = __int_as_float(__float_as_int(ld_cg_f32(a.hx.slots + 2)));
+                s.tmp[2] = __int_as_float(r > 0 ? 1 : 0);
+                s.tmp[3] = 0.0f;
             }
-            if (mi < 0) mi = role.voc0 * kTile;                               // an empty or all-NaN slice
-            tx[3 * cta] = m;
-            tx[3 * cta + 1] = __int_as_float(mi);
-            tx[3 * cta + 2] = __int_as_float(host_stop);
+            __syncthreads();
+            scatter(s.tmp, s.xt, 0, 4);
         }
-        publish(a, kXTok, tcount);
-        if (!(ok = wait_x(a, kXTok, tcount))) break;
-        read_x(tx, 3 * a.grid, s.scores);
-        // Global argmax over the CTAs in vocabulary order (reference engine.c:299-300), same in every CTA.
-        float gmax = -INFINITY;
-        int next = 0;
-        for (int c = 0; c < a.grid; c++) {
-            if (s.scores[3 * c] > gmax) { gmax = s.scores[3 * c]; next = __float_as_int(s.scores[3 * c + 1]); }
-        }
-        const int stop_req = __float_as_int(s.scores[2]);
-        __syncthreads();
+        cluster_sync();                                                   // 6: the sampled token
+        const int next = __float_as_int(s.xt[0]), stop_req = __float_as_int(s.xt[1]);
+        if (!__float_as_int(s.xt[2])) { ok = false; break; }
         trace(a, tslot, pos, a.n_layers, 2);
+        if (stop_after) break;                                            // logits kept, nothing sampled (uniform)
         tok = next;
-        if (tok == a.eos || tok == a.bos) break;                              // reference engine.c:323-324
+        if (tok == a.eos || tok == a.bos) break;                          // reference engine.c:323-324
         n_gen++;
         if (cta == 0 && tid == 0) {
             a.tokens[n_gen - 1] = tok;
@@ -394,13 +499,17 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
             a.ctrl->n_published = n_gen;
         }
         if (stop_req) break;
+        // xt is rewritten at the next sampled position only after barriers 1-5, which every CTA
+        // reaches after reading it here.
     }
-    cp_async_wait_all();                                                    // no copy outlives the CTA
-    if (!ok) err = *(volatile int *)a.abort_flag;
+    cp_async_wait_all();                                                  // no copy outlives the CTA
+    cluster_sync();                                                       // no CTA leaves while others may write its memory
     if (cta == 0 && tid == 0) {
+        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.hx.flag), "r"(kHeadDone) : "memory");   // the helpers stop
+        const int err = *(volatile int *)a.hx.abort_flag;
         a.ctrl->final_pos = pos;
         a.ctrl->n_gen = n_gen;
-        a.ctrl->error = err ? err : (ok ? 0 : kErrTimeout);
+        a.ctrl->error = ok ? 0 : (err ? err : kErrTimeout);
         __threadfence_system();
         a.ctrl->done = 1;
     }
@@ -408,13 +517,43 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
 
 }  // namespace l3m
 
+namespace {
+
+// grid CTAs in clusters of kClusterCtas, all resident at once (cooperative): the helper clusters wait
+// on cluster 0 through global memory.
+cudaLaunchConfig_t cluster_config(int grid, int smem_bytes, cudaLaunchAttribute *at) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(l3m::kDecodeThreads);
+    cfg.dynamicSmemBytes = (size_t)smem_bytes;
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = (unsigned)l3m::kClusterCtas;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeCooperative;
+    at[1].val.cooperative = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 2;
+    return cfg;
+}
+
+cudaError_t set_attributes(int smem_bytes) {
+    cudaError_t e = cudaFuncSetAttribute(l3m::decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(l3m::decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    return e;
+}
+
+}  // namespace
+
 // a_dev: the arguments, already in device memory.
 extern "C" int l3m_decode_launch(const l3m::DecodeArgs *a, const l3m::DecodeArgs *a_dev, void *stream) {
-    void *args[] = {(void *)&a_dev};
-    cudaError_t e = cudaFuncSetAttribute(l3m::decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, a->smem_bytes);
-    if (e == cudaSuccess)
-        e = cudaLaunchCooperativeKernel((const void *)l3m::decode_kernel, dim3(a->grid), dim3(l3m::kDecodeThreads), args,
-                                        (size_t)a->smem_bytes, (cudaStream_t)stream);
+    cudaError_t e = set_attributes(a->smem_bytes);
+    if (e == cudaSuccess) {
+        cudaLaunchAttribute at[2];
+        cudaLaunchConfig_t cfg = cluster_config(a->grid, a->smem_bytes, at);
+        cfg.stream = (cudaStream_t)stream;
+        e = cudaLaunchKernelEx(&cfg, l3m::decode_kernel, a_dev);
+    }
     if (e != cudaSuccess) {
         fprintf(stderr, "l3m: decode launch: %s\n", cudaGetErrorString(e));
         return -1;
@@ -422,9 +561,14 @@ extern "C" int l3m_decode_launch(const l3m::DecodeArgs *a, const l3m::DecodeArgs
     return 0;
 }
 
+// How many clusters of kClusterCtas CTAs with smem_bytes of shared memory each can be resident on
+// the current device at once.
 extern "C" int l3m_decode_occupancy(int smem_bytes) {
+    if (set_attributes(smem_bytes) != cudaSuccess) return 0;
+    cudaLaunchAttribute at[2];
+    cudaLaunchConfig_t cfg = cluster_config(l3m::kClusterCtas, smem_bytes, at);
+    cfg.numAttrs = 1;
     int n = 0;
-    if (cudaFuncSetAttribute(l3m::decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) != cudaSuccess) return 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, l3m::decode_kernel, l3m::kDecodeThreads, smem_bytes) != cudaSuccess) return 0;
+    if (cudaOccupancyMaxActiveClusters(&n, (const void *)l3m::decode_kernel, &cfg) != cudaSuccess) return 0;
     return n;
 }

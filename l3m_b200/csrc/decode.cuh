@@ -5,7 +5,7 @@
 namespace l3m {
 
 struct alignas(16) LayerDev {
-    const uint8_t *qkv;                 // one unit per query head: its q rows, then its kv head's k and v rows
+    const uint8_t *qkv;                 // rows: q of every head, then k of every kv head, then v
     const uint8_t *wo, *gate, *up, *down;
     const float *attn_norm, *ffn_norm;
     const float *bq, *bk, *bv, *bo, *b_up, *b_down;   // NULL when absent
@@ -13,11 +13,11 @@ struct alignas(16) LayerDev {
     int dt_qkv, dt_wo, dt_gate, dt_up, dt_down;
 };
 
-// One CTA's share of every phase (output tiles are 16 rows; ranges are [lo, hi)).
+// One CTA's share of every phase (output tiles are 16 rows; ranges are [lo, hi)). Query heads
+// head0, head0 + n_ctas, ... are this CTA's.
 struct Role {
-    int head;          // query head of the attention phase, -1 for none
-    int kv_writer;     // 1: stores the KV row of its kv head
-    int wo0, wo1, ffn0, ffn1, dn0, dn1, voc0, voc1;
+    int head0;
+    int qkv0, qkv1, wo0, wo1, ffn0, ffn1, dn0, dn1, voc0, voc1;
 };
 
 // Host-mapped control block: tokens stream out, a stop request streams in.
@@ -27,21 +27,31 @@ struct Ctrl {
     volatile int32_t final_pos;      // last position run
     volatile int32_t n_gen;          // tokens the device accepted
     volatile int32_t stop_request;   // set by the host when on_token returns 0
-    volatile int32_t error;          // nonzero: see kErr*
+    volatile int32_t error;          // nonzero: a device-side failure (kErr*)
     volatile int32_t pad[2];
 };
 
-enum { kErrNone = 0, kErrTimeout = 1, kErrEpoch = 2 };
-constexpr int kDecodeThreads = 256;   // 8 warps: the register file holds every live value without spilling
+constexpr int kDecodeThreads = 256;   // 8 warps per CTA
+constexpr int kClusterCtas = 16;      // one thread-block cluster runs the whole model
+constexpr int kTraceEvents = 16;      // stamps per (position, layer); see the trace() calls in decode.cu
 
-// Exchanges between phases. Each has a float data buffer and an arrival counter, both in two halves
-// by step parity. A producer writes its outputs and adds 1 (release) to the counter; a consumer's
-// thread 0 polls the counter (acquire) until every expected arrival of this step is in, then the CTA
-// reads the data once. Counters sit on their own 128-byte lines.
-enum { kXAttn, kXProj, kXH, kXDown, kXTok, kXCount };
+// The head phase runs on every CTA of the launch (several clusters): cluster 0 publishes x in
+// global memory with a release flag, every CTA computes its vocabulary tiles and adds (max, index)
+// with an arrival count that cluster 0 waits for. Waits are bounded by timeout_ns.
+struct HeadX {
+    float *x;                           // [dim] the final residual of the sampled position
+    uint32_t *flag;                     // tcount of the published x; kHeadDone when generation ends
+    uint32_t *count;                    // arrivals: grid per sampled position
+    float *slots;                       // [grid][2] (max, index bits)
+    int *abort_flag;                    // first error code of any CTA
+    unsigned long long timeout_ns;
+};
+constexpr uint32_t kHeadDone = 0xFFFFFFFFu;
+enum { kErrNone = 0, kErrTimeout = 1 };
 
 struct DecodeArgs {
-    int dim, hd, ffn, vocab, ctx, n_heads, n_kv, hpk, n_layers, unit_tiles, grid;
+    int dim, hd, ffn, vocab, ctx, n_heads, n_kv, hpk, n_layers, n_qkv, grid;   // n_qkv = (n_heads + 2 n_kv) hd; grid: all CTAs
+    HeadX hx;
     float eps;
     const LayerDev *layers;
     const uint8_t *head;
@@ -50,27 +60,21 @@ struct DecodeArgs {
     int dt_embed;
     long long embed_row_bytes;
     const float *norm;
-    const float2 *rope;                 // [ctx][hd/2] {cos, sin}; NULL: learned positions
+    const float2 *rope;                 // [ctx][hd/2] {cos, sin}
     const uint32_t *elist, *eindex;     // libm expf exception list
     const Role *roles;
-    float *xd;                          // exchange data, two halves of xd_half floats
-    long long xd_half;
-    int d_attn, d_proj, d_h, d_down, d_tok;   // float offsets within a half
-    uint32_t *ctr;                      // [kXCount][2] counters, 32 words apart
-    int arrivals[kXCount];              // per use: producers (+ every CTA's presence for kXDown)
     const int32_t *prompt;
     int n_prompt, max_new, eos, bos;
     float *logits;                      // [ctx][vocab]
     Ctrl *ctrl;
     int32_t *tokens;                    // host-mapped, ctx entries
-    int *abort_flag;                    // device: first error code
-    unsigned long long timeout_ns;      // per wait
-    unsigned long long *trace;          // optional: [4][ctx][n_layers + 1][16] globaltimer stamps
-    int trace_cta[4];
+    unsigned long long *trace;          // optional: [2][ctx][n_layers + 1][kTraceEvents] globaltimer stamps
+    int trace_cta[2];
     // shared memory layout, byte offsets
-    int sm_x, sm_xb, sm_tmp, sm_q8, sm_scale, sm_sum, sm_xf, sm_y, sm_y2, sm_scores, sm_kv, sm_att, sm_red, sm_kvbuf, sm_vt, sm_scratch;
+    int sm_x, sm_xb, sm_tmp, sm_q8, sm_scale, sm_sum, sm_xf, sm_y, sm_scores, sm_kv, sm_att, sm_red, sm_kvbuf, sm_vt, sm_scratch;
     int sm_wa, sm_wf, sm_wh, sm_rope;   // this layer's norm weights, the final norm, this position's RoPE row
     int sm_layers;                      // a copy of layers[0 .. n_layers)
+    int sm_xq, sm_xa, sm_xp, sm_xh, sm_xd, sm_xt;   // exchanged vectors: qkv, attn, proj, h, down, (max, index, stop) per CTA
     int vstride;                        // V cache: element i of position t at vc[i * vstride + t]
     int scratch_pairs, smem_bytes, attn_chunk;
 };

@@ -19,6 +19,7 @@ __device__ __forceinline__ uint8_t ld_nc_u8(const void *p) { return __ldg((const
 // Data other CTAs write during the kernel (KV cache rows): cached in L2 only, never in L1, so a
 // line fetched before a neighbouring row was written cannot be served stale.
 __device__ __forceinline__ uint4 ld_cg_v4(const void *p) { return __ldcg((const uint4 *)p); }
+__device__ __forceinline__ float ld_cg_f32(const float *p) { return __ldcg(p); }
 // Streamed read-only data (weights): not allocated in L1, so it does not evict what the kernel reuses.
 __device__ __forceinline__ uint4 ld_stream_v4(const void *p) {
     uint4 v;

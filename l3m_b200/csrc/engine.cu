@@ -4,7 +4,7 @@
 //             streamed weights first, so one persisting-L2 window covers them), give each CTA its
 //             share of every phase, refuse when the weights exceed the L2 persisting budget unless
 //             forced (the reference's cache-budget refusal, src/engine.c:496-525);
-//   generate  one cooperative launch of the persistent decode kernel per call; tokens stream back
+//   generate  one launch of the decode kernel (a single thread-block cluster) per call; tokens stream back
 //             through host-mapped memory to on_token on the caller's thread, and a stop request
 //             streams in the other way.
 #include <cuda_runtime.h>
@@ -55,15 +55,12 @@ struct Gpu {
     l3m::LayerDev *layers = nullptr;
     l3m::Role *roles = nullptr;
     l3m::DecodeArgs *args_dev = nullptr;
-    float *xd = nullptr;
-    size_t xd_bytes = 0;
-    uint32_t *flags = nullptr;
-    size_t flags_bytes = 0;
     unsigned long long *trace = nullptr;
     size_t trace_bytes = 0;
+    void *hx = nullptr;
+    size_t hx_bytes = 0;
     int32_t *prompt = nullptr;
     float *logits = nullptr;
-    int *abort_flag = nullptr;
     l3m::DecodeArgs args{};
     size_t l2_bytes = 0, persist_max = 0, window_max = 0, prev_limit = 0;
     bool limit_set = false;
@@ -140,7 +137,6 @@ struct Rows {
         l3m_dequant_row(f32.back().data(), (int)t->dtype, row_ptr(f, t, r), k);
         ptr.push_back(f32.back().data());
     }
-    void pad_to(size_t n) { while (ptr.size() < n) ptr.push_back(nullptr); }
 };
 
 size_t pack(Stage &s, Rows &rows) {
@@ -199,25 +195,24 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
         fprintf(stderr, "l3m: %s\n", msg);
         return false;
     }
-    const int G = g.sms, dim = m->dim, hd = m->hd, ffn = m->ffn, V = m->vocab, L = m->n_layers;
-    if (m->n_heads > G) { fprintf(stderr, "l3m: %d heads exceed the %d SMs of GPU %d\n", m->n_heads, G, g.dev); return false; }
+    // One cluster of kClusterCtas CTAs runs the layers; the head runs on every CTA of as many whole
+    // clusters as there are SMs for (9 x 16 = 144 on a B200).
+    const int G = l3m::kClusterCtas, dim = m->dim, hd = m->hd, ffn = m->ffn, V = m->vocab, L = m->n_layers;
+    if (g.sms < G) { fprintf(stderr, "l3m: GPU %d has %d SMs; the decode cluster needs %d\n", g.dev, g.sms, G); return false; }
+    int GT = g.sms / G * G;
     if (hd > l3m::kDecodeThreads) { fprintf(stderr, "l3m: head_dim %d above %d is not built\n", hd, l3m::kDecodeThreads); return false; }
 
     // Streamed weights first (one contiguous range for the persisting window), then the rest.
     Stage s;
     std::vector<l3m::LayerDev> layers(L);
     std::vector<size_t> off_qkv(L), off_wo(L), off_gate(L), off_up(L), off_down(L);
-    const int unit_rows = 3 * hd, unit_tiles = tiles_of(unit_rows);
+    const int n_qkv = (m->n_heads + 2 * m->n_kv) * hd;
     for (int l = 0; l < L; l++) {
         const l3m_tensor *wq = l3m_file_blk(f, l, "wq"), *wk = l3m_file_blk(f, l, "wk"), *wv = l3m_file_blk(f, l, "wv");
-        Rows r;                                                                     // one unit per query head,
-        for (int h = 0; h < m->n_heads; h++) {                                      // each whole tiles, back to back
-            const int kvh = h / m->hpk;
-            for (int i = 0; i < hd; i++) r.add(f, wq, h * hd + i, ref);
-            for (int i = 0; i < hd; i++) r.add(f, wk, kvh * hd + i, ref);
-            for (int i = 0; i < hd; i++) r.add(f, wv, kvh * hd + i, ref);
-            r.pad_to((size_t)(h + 1) * unit_tiles * L3M_TILE);
-        }
+        Rows r;                                                                     // q of every head, then k, then v
+        for (int i = 0; i < m->n_heads * hd; i++) r.add(f, wq, i, ref);
+        for (int i = 0; i < m->n_kv * hd; i++) r.add(f, wk, i, ref);
+        for (int i = 0; i < m->n_kv * hd; i++) r.add(f, wv, i, ref);
         off_qkv[l] = pack(s, r);
         layers[l].dt_qkv = r.dtype;
         off_wo[l] = pack_matrix(s, f, l3m_file_blk(f, l, "wo"), ref, &layers[l].dt_wo);
@@ -229,7 +224,6 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     int dt_head = 0;
     size_t off_head = pack_matrix(s, f, head, ref, &dt_head);
     g.weight_bytes = s.buf.size();
-    // Per-head units repeat the kv rows of a GQA group: the streamed bytes include that.
     const l3m_tensor *emb = l3m_file_tensor(f, "embed");
     int dt_embed = (int)emb->dtype;
     size_t emb_row = l3m_row_bytes(dt_embed, dim), off_embed;
@@ -289,64 +283,44 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     if (!cuda_ok(cudaMalloc(&g.rope, rope.size() * sizeof(float2)), "rope")) return false;
     cudaMemcpy(g.rope, rope.data(), rope.size() * sizeof(float2), cudaMemcpyHostToDevice);
 
-    // Each CTA's share of every phase: contiguous tile ranges, the reference's split (engine.c:471-476).
-    const int Td = tiles_of(dim), Tf = tiles_of(ffn), Tv = tiles_of(V);
-    std::vector<l3m::Role> roles(G);
-    int max_ffn_tiles = 0;
-    for (int c = 0; c < G; c++) {
-        l3m::Role &r = roles[c];
-        r.head = -1;
-        r.kv_writer = 0;
-        split(Td, G, c, &r.wo0, &r.wo1);
-        split(Tf, G, c, &r.ffn0, &r.ffn1);
-        split(Td, G, c, &r.dn0, &r.dn1);
-        split(Tv, G, c, &r.voc0, &r.voc1);
-        max_ffn_tiles = std::max(max_ffn_tiles, r.ffn1 - r.ffn0);
-    }
-    for (int h = 0; h < m->n_heads; h++) {
-        l3m::Role &r = roles[(long)h * G / m->n_heads];
-        r.head = h;
-        r.kv_writer = h % m->hpk == 0;
-    }
-    if (!cuda_ok(cudaMalloc(&g.roles, sizeof(l3m::Role) * G), "roles")) return false;
-    cudaMemcpy(g.roles, roles.data(), sizeof(l3m::Role) * G, cudaMemcpyHostToDevice);
+    // Each CTA's share of every phase: contiguous tile ranges, the reference's split (engine.c:471-476);
+    // query heads round-robin over the CTAs.
+    const int Td = tiles_of(dim), Tf = tiles_of(ffn), Tv = tiles_of(V), Tq = tiles_of(n_qkv);
+    // Roles for a grid of gt CTAs; the shared-memory layout is sized for the largest share (gt = G).
+    auto make_roles = [&](int gt) {
+        std::vector<l3m::Role> rs(gt);
+        for (int c = 0; c < gt; c++) {
+            l3m::Role &r = rs[c];
+            r = l3m::Role{-1, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
+            if (c < G) {
+                r.head0 = c < m->n_heads ? c : -1;
+                split(Tq, G, c, &r.qkv0, &r.qkv1);
+                split(Td, G, c, &r.wo0, &r.wo1);
+                split(Tf, G, c, &r.ffn0, &r.ffn1);
+                split(Td, G, c, &r.dn0, &r.dn1);
+            }
+            split(Tv, gt, c, &r.voc0, &r.voc1);
+        }
+        return rs;
+    };
+    int max_tiles = tiles_of(3 * hd);
+    for (const l3m::Role &r : make_roles(G))
+        max_tiles = std::max({max_tiles, r.qkv1 - r.qkv0, 2 * (r.ffn1 - r.ffn0), r.wo1 - r.wo0, r.dn1 - r.dn0, r.voc1 - r.voc0});
 
     l3m::DecodeArgs &a = g.args;
     a.dim = dim; a.hd = hd; a.ffn = ffn; a.vocab = V; a.ctx = m->ctx; a.n_heads = m->n_heads; a.n_kv = m->n_kv; a.hpk = m->hpk;
-    a.n_layers = L; a.unit_tiles = unit_tiles; a.grid = G; a.eps = m->f.h->norm_eps;
+    a.n_layers = L; a.n_qkv = n_qkv; a.grid = GT; a.eps = m->f.h->norm_eps;
     a.layers = g.layers;
     a.head = g.arena + off_head; a.dt_head = dt_head;
     a.embed = g.arena + off_embed; a.dt_embed = dt_embed; a.embed_row_bytes = (long long)emb_row;
     a.norm = A(off_norm);
     a.rope = (m->flags & L3M_F_LEARNED_POS) ? nullptr : g.rope;
     if (l3m_expf_tables(&a.elist, &a.eindex)) { fprintf(stderr, "l3m: %s\n", l3m_cuda_error()); return false; }
-    a.roles = g.roles;
-    // Exchange buffers: floats in two halves by step parity, one flag per (exchange, parity, CTA).
-    a.d_attn = 0; a.d_proj = dim; a.d_h = 2 * dim; a.d_down = 2 * dim + ffn; a.d_tok = 3 * dim + ffn;
-    a.xd_half = ((long long)a.d_tok + 3 * G + 63) & ~63LL;
-    g.xd_bytes = (size_t)a.xd_half * 2 * sizeof(float);
-    g.flags_bytes = (size_t)l3m::kXCount * 2 * 32 * sizeof(uint32_t);
-    if (!cuda_ok(cudaMalloc(&g.xd, g.xd_bytes), "exchange") || !cuda_ok(cudaMalloc(&g.flags, g.flags_bytes), "counters")) return false;
-    a.xd = g.xd;
-    a.ctr = g.flags;
-    auto count = [&](auto pred) { int n = 0; for (int c = 0; c < G; c++) n += pred(roles[c]); return n; };
-    a.arrivals[l3m::kXAttn] = m->n_heads;
-    a.arrivals[l3m::kXProj] = count([](const l3m::Role &r) { return r.wo0 < r.wo1; });
-    a.arrivals[l3m::kXH] = count([](const l3m::Role &r) { return r.ffn0 < r.ffn1; });
-    a.arrivals[l3m::kXDown] = count([](const l3m::Role &r) { return r.dn0 < r.dn1; }) + G;   // + every CTA's presence
-    a.arrivals[l3m::kXTok] = G;
-    std::vector<int> plist;                                           // CTA ids by role, for the trace picks
-    for (int c = 0; c < G; c++) if (roles[c].head >= 0) plist.push_back(c);
-    for (int i = 0; i < 4; i++) a.trace_cta[i] = -1;
-    if (getenv("L3M_TRACE")) {                                         // phase timestamps of four CTAs
-        int pick[4] = {plist[0], -1, -1, -1};
-        for (int c = 0; c < G; c++) {
-            if (pick[1] < 0 && roles[c].wo0 < roles[c].wo1 && roles[c].head < 0) pick[1] = c;
-            if (pick[2] < 0 && roles[c].ffn0 < roles[c].ffn1 && roles[c].head < 0 && roles[c].wo0 == roles[c].wo1) pick[2] = c;
-            if (pick[3] < 0 && roles[c].head < 0 && roles[c].wo0 == roles[c].wo1 && roles[c].ffn0 == roles[c].ffn1) pick[3] = c;
-        }
-        for (int i = 0; i < 4; i++) a.trace_cta[i] = pick[i];
-        g.trace_bytes = (size_t)4 * m->ctx * (L + 1) * 16 * sizeof(unsigned long long);
+    a.trace_cta[0] = a.trace_cta[1] = -1;
+    if (getenv("L3M_TRACE")) {                                         // phase time stamps of two CTAs: the first and the last
+        a.trace_cta[0] = 0;
+        a.trace_cta[1] = G - 1;
+        g.trace_bytes = (size_t)2 * m->ctx * (L + 1) * l3m::kTraceEvents * sizeof(unsigned long long);
         if (!cuda_ok(cudaMalloc(&g.trace, g.trace_bytes), "trace")) return false;
         cudaMemset(g.trace, 0, g.trace_bytes);
         a.trace = g.trace;
@@ -354,13 +328,13 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     if (!cuda_ok(cudaMalloc(&g.prompt, (size_t)m->ctx * 4), "prompt")) return false;
     if (!cuda_ok(cudaMalloc(&g.logits, (size_t)m->ctx * V * 4), "logits")) return false;
     cudaMemset(g.logits, 0, (size_t)m->ctx * V * 4);
-    if (!cuda_ok(cudaMalloc(&g.abort_flag, 4), "flag")) return false;
     a.prompt = g.prompt;
     a.eos = m->f.tok.eos; a.bos = m->f.tok.bos;
     a.logits = g.logits;
-    a.abort_flag = g.abort_flag;
+    // The head exchange (allocated once the grid is known): x (+ the position), the flag, the arrival
+    // count, the slots, the abort word.
     const char *tmo = getenv("L3M_TIMEOUT_MS");
-    a.timeout_ns = (unsigned long long)(tmo ? atof(tmo) : 5000.0) * 1000000ull;
+    a.hx.timeout_ns = (unsigned long long)(tmo ? atof(tmo) : 5000.0) * 1000000ull;
 
     // Shared memory layout.
     const int mx = std::max(dim, ffn), nb = (mx + 31) / 32;
@@ -373,12 +347,8 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     a.sm_scale = take(nb * 4);
     a.sm_sum = take(nb * 4);
     a.sm_xf = take(mx * 4);
-    int max_tiles = std::max(unit_tiles, max_ffn_tiles);
-    for (int c = 0; c < G; c++)
-        max_tiles = std::max({max_tiles, roles[c].wo1 - roles[c].wo0, roles[c].dn1 - roles[c].dn0, roles[c].voc1 - roles[c].voc0});
     a.sm_y = take(max_tiles * L3M_TILE * 4);
-    a.sm_y2 = take(max_ffn_tiles * L3M_TILE * 4);
-    a.sm_scores = take(std::max(m->ctx, 3 * G) * 4);
+    a.sm_scores = take(m->ctx * 4);
     a.sm_kv = take(2 * hd * 2);
     a.sm_att = take(hd * 4);
     a.sm_red = take(64 * 4);
@@ -391,6 +361,12 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     a.sm_kvbuf = take(a.attn_chunk * (hd + 8) * 2);
     a.sm_vt = take(hd * l3m::attn_vt_stride(a.attn_chunk) * 2);
     a.vstride = vstride;
+    a.sm_xq = take(n_qkv * 4);
+    a.sm_xa = take(dim * 4);
+    a.sm_xp = take(dim * 4);
+    a.sm_xh = take(ffn * 4);
+    a.sm_xd = take(dim * 4);
+    a.sm_xt = take(4 * G * 4);
     a.sm_scratch = take(0);
     const int budget = 200 * 1024;
     a.scratch_pairs = std::min(8192, (budget - off) / 8);
@@ -400,10 +376,25 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
         return false;
     }
     a.smem_bytes = off + a.scratch_pairs * 8;
-    if (l3m_decode_occupancy(a.smem_bytes) < 1) {
-        fprintf(stderr, "l3m: the decode kernel does not fit on an SM of GPU %d\n", g.dev);
+    GT = std::min(GT, l3m_decode_occupancy(a.smem_bytes) * G);            // whole clusters resident at once
+    if (GT < G) {
+        fprintf(stderr, "l3m: a cluster of %d decode CTAs does not fit on GPU %d\n", G, g.dev);
         return false;
     }
+    a.grid = GT;
+    {
+        std::vector<l3m::Role> roles = make_roles(GT);
+        if (!cuda_ok(cudaMalloc(&g.roles, sizeof(l3m::Role) * GT), "roles")) return false;
+        cudaMemcpy(g.roles, roles.data(), sizeof(l3m::Role) * GT, cudaMemcpyHostToDevice);
+        a.roles = g.roles;
+    }
+    g.hx_bytes = (size_t)(dim + 4) * 4 + 256 + (size_t)3 * GT * 4;
+    if (!cuda_ok(cudaMalloc(&g.hx, g.hx_bytes), "head exchange")) return false;
+    a.hx.x = (float *)g.hx;
+    a.hx.flag = (uint32_t *)((char *)g.hx + (size_t)(dim + 4) * 4);
+    a.hx.count = a.hx.flag + 32;
+    a.hx.abort_flag = (int *)(a.hx.flag + 16);
+    a.hx.slots = (float *)(a.hx.flag + 64);
     a.ctrl = m->ctrl_dev;
     a.tokens = m->tokens_dev;
     if (!cuda_ok(cudaStreamCreateWithFlags(&g.stream, cudaStreamNonBlocking), "stream")) return false;
@@ -519,8 +510,8 @@ L3M_API void l3m_free(l3m_model *m) {
             cudaCtxResetPersistingL2Cache();
             cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, g.prev_limit);
         }
-        cudaFree(g.arena); cudaFree(g.kv); cudaFree(g.rope); cudaFree(g.layers); cudaFree(g.roles); cudaFree(g.args_dev); cudaFree(g.xd); cudaFree(g.flags); cudaFree(g.trace);
-        cudaFree(g.prompt); cudaFree(g.logits); cudaFree(g.abort_flag);
+        cudaFree(g.arena); cudaFree(g.kv); cudaFree(g.rope); cudaFree(g.layers); cudaFree(g.roles); cudaFree(g.args_dev); cudaFree(g.trace); cudaFree(g.hx);
+        cudaFree(g.prompt); cudaFree(g.logits);
         if (g.ev0) cudaEventDestroy(g.ev0);
         if (g.ev1) cudaEventDestroy(g.ev1);
         if (g.stream) cudaStreamDestroy(g.stream);
@@ -547,9 +538,8 @@ L3M_API int l3m_generate(l3m_model *m, const int32_t *prompt, int n_prompt, int 
     a.max_new = max_new;
     const double t0 = now_ns();
     cudaMemcpyAsync(g.prompt, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, g.stream);
-    cudaMemsetAsync(g.flags, 0, g.flags_bytes, g.stream);
-    cudaMemsetAsync(g.abort_flag, 0, 4, g.stream);
     cudaMemcpyAsync(g.args_dev, &a, sizeof a, cudaMemcpyHostToDevice, g.stream);
+    cudaMemsetAsync(g.hx, 0, g.hx_bytes, g.stream);                    // flag, count and abort word start at 0
     cudaEventRecord(g.ev0, g.stream);
     if (l3m_decode_launch(&a, g.args_dev, g.stream)) return -1;
     cudaEventRecord(g.ev1, g.stream);
@@ -592,7 +582,7 @@ L3M_API int l3m_generate(l3m_model *m, const int32_t *prompt, int n_prompt, int 
         std::vector<unsigned long long> t(g.trace_bytes / 8);
         cudaMemcpy(t.data(), g.trace, g.trace_bytes, cudaMemcpyDeviceToHost);
         if (FILE *tf = fopen(getenv("L3M_TRACE"), "wb")) {
-            int hdr[8] = {m->ctx, m->n_layers, n_prompt, last_pos, g.args.trace_cta[0], g.args.trace_cta[1], g.args.trace_cta[2], g.args.trace_cta[3]};
+            int hdr[8] = {m->ctx, m->n_layers, n_prompt, last_pos, g.args.trace_cta[0], g.args.trace_cta[1], l3m::kTraceEvents, 0};
             fwrite(hdr, sizeof hdr, 1, tf);
             fwrite(t.data(), 8, t.size(), tf);
             fclose(tf);

@@ -177,7 +177,7 @@ __global__ void __launch_bounds__(kThreads) attend_kernel(float *out, const floa
         vcur[i] = v[(size_t)pos * stride + i];
     }
     __syncthreads();
-    attend_exact<false>(qs, k, v, stride, stride, kcur, vcur, pos, hd, scores, o, red, elist, eindex, kvbuf, nullptr, kAttnChunk);
+    attend_exact<false>(qs, k, v, stride, stride, kcur, vcur, pos, hd, scores, o, red, elist, eindex, kvbuf, nullptr, kAttnChunk, false);
     for (int i = threadIdx.x; i < hd; i += blockDim.x) out[i] = o[i];
 }
 

@@ -206,16 +206,17 @@ __device__ __forceinline__ float qscale(uint32_t d) { return DT == DT_MX ? l3m_e
 // each output's {RN(sx[b] * d), (float)dot} goes to scratch[b * m + o]. Then one thread per output
 // runs the fp32 chain in block order.
 constexpr int kQU = 2;
+// Tiles [0, ntA) come from `tiles`, tiles from ntA on from tilesB (a second matrix of the same shape).
 template <int DT>
-__device__ void qmatvec(const uint8_t *tiles, int k, int n_out, const Prep &p, float2 *scratch, int scratch_pairs, float *y) {
+__device__ void qmatvec(const uint8_t *tiles, const uint8_t *tilesB, int ntA, int k, int n_out, const Prep &p, float2 *scratch,
+                        int scratch_pairs, float *y) {
     const int tid = threadIdx.x, nth = blockDim.x, nb = k / kQB, bb = block_bytes(DT);
     const size_t tb = (size_t)nb * bb;
     const uint32_t *xw = (const uint32_t *)p.q8;
-    int chunk = (scratch_pairs / nb) & ~(kTile - 1);
+    int chunk = (scratch_pairs / nb) & ~(kTile - 1);           // >= 16: callers size scratch for one tile
     if (chunk > n_out) chunk = n_out;
     for (int o0 = 0; o0 < n_out; o0 += chunk) {
-        const int m = min(chunk, n_out - o0), m4 = m >> 2, items = m4 * nb;
-        const uint8_t *base = tiles + (size_t)(o0 >> 4) * tb;
+        const int m = min(chunk, n_out - o0), m4 = m >> 2, items = m4 * nb, t0 = o0 >> 4;
         // item i = b * m4 + quad; this thread starts at i = tid and steps by nth
         int b = tid / m4, qd = tid - b * m4;
         const int db = nth / m4, dq = nth - db * m4;
@@ -225,7 +226,11 @@ __device__ void qmatvec(const uint8_t *tiles, int k, int n_out, const Prep &p, f
 #pragma unroll
             for (int u = 0; u < kQU; u++) {
                 bs[u] = b; qs[u] = qd;
-                if (i + u * nth < items) qload4<DT>(q[u], base + (size_t)(qd >> 2) * tb + (size_t)b * bb, qd & 3);
+                if (i + u * nth < items) {
+                    const int ti = t0 + (qd >> 2);
+                    const uint8_t *tile = ti < ntA ? tiles + (size_t)ti * tb : tilesB + (size_t)(ti - ntA) * tb;
+                    qload4<DT>(q[u], tile + (size_t)b * bb, qd & 3);
+                }
                 qd += dq; b += db;
                 if (qd >= m4) { qd -= m4; b++; }
             }
@@ -271,9 +276,9 @@ static __device__ __noinline__ void matvec_exact(int dtype, const uint8_t *tiles
     const size_t tb = tile_bytes(dtype, k);
     const uint8_t *base = tiles + (size_t)t0 * tb;
     const int n = (t1 - t0) * kTile;
-    if (dtype == DT_Q8) { qmatvec<DT_Q8>(base, k, n, p, scratch, scratch_pairs, y); return; }
-    if (dtype == DT_Q4) { qmatvec<DT_Q4>(base, k, n, p, scratch, scratch_pairs, y); return; }
-    if (dtype == DT_MX) { qmatvec<DT_MX>(base, k, n, p, scratch, scratch_pairs, y); return; }
+    if (dtype == DT_Q8) { qmatvec<DT_Q8>(base, base, 1 << 30, k, n, p, scratch, scratch_pairs, y); return; }
+    if (dtype == DT_Q4) { qmatvec<DT_Q4>(base, base, 1 << 30, k, n, p, scratch, scratch_pairs, y); return; }
+    if (dtype == DT_MX) { qmatvec<DT_MX>(base, base, 1 << 30, k, n, p, scratch, scratch_pairs, y); return; }
     // f32 / bf16 (tiles [K][16] f32, [K/2][16][2] bf16): one thread per output walks its row in input
     // order, the reference's chain.
     const int split = fused_from(k);
@@ -387,7 +392,7 @@ __device__ __forceinline__ float expf_libm(float x, const uint32_t *list, const 
 // is transposed — element i of position t at vc[i * vstride + t], vstride >= pos + 1 rounded up to
 // 8 — and element i of row pos is vcur[i]. scores: >= pos + 1 floats of shared scratch (16-byte aligned); red: >= 33 floats.
 // kvbuf: chunk * (hd + 8) bf16 of staging; vtbuf (VT only): hd * attn_vt_stride(chunk) bf16.
-// hd % 8 == 0; chunk a multiple of 8.
+// hd % 8 == 0; chunk a multiple of 8. prestaged: attend_prestage has run for this call.
 __device__ __forceinline__ uint4 ld_row8(const uint16_t *p, bool vec) {
     if (vec) return ld_cg_v4(p);
     uint16_t h[8];
@@ -400,10 +405,47 @@ __device__ __forceinline__ uint4 ld_row8(const uint16_t *p, bool vec) {
 // consecutive rows fall in distinct bank groups.
 __host__ __device__ constexpr int attn_vt_stride(int chunk) { return ((chunk + 15) & ~15) + 8; }
 
+// Start the copies of everything attention at pos reads that exists before row pos: K rows
+// [0, min(chunk, pos)) and, with VT, V positions [0, min(chunk, pos + 1)) (position pos itself is
+// patched later). Needs nothing of this position, so it can run before q, k and v are known.
+template <bool VT>
+__device__ __noinline__ void attend_prestage(const uint16_t *kc, const uint16_t *vc, int kstride, int vstride, int pos, int hd,
+                                             uint16_t *kvbuf, uint16_t *vtbuf, int chunk) {
+    const int tid = threadIdx.x, nth = blockDim.x, rs = hd + 8, h8 = hd / 8, vs = attn_vt_stride(chunk);
+    const bool kvec = kstride % 8 == 0 && ((uintptr_t)kc & 15) == 0;
+    const bool vvec = vstride % 8 == 0 && ((uintptr_t)vc & 15) == 0;
+    const int nk = min(chunk, pos);
+    {
+        const int dr = nth / h8, dj = nth - dr * h8;
+        int r = tid / h8, j = tid - r * h8;
+        for (int e = tid; e < nk * h8; e += nth) {
+            uint16_t *dst = kvbuf + r * rs + j * 8;
+            const uint16_t *src = kc + (size_t)r * kstride + j * 8;
+            if (kvec) cp_async16(dst, src);
+            else *(uint4 *)dst = ld_row8(src, false);
+            j += dj; r += dr;
+            if (j >= h8) { j -= h8; r++; }
+        }
+    }
+    if (VT) {
+        const int p8 = (min(chunk, pos + 1) + 7) >> 3, di = nth / p8, dp = nth - di * p8;
+        int i = tid / p8, pc = tid - i * p8;
+        for (int e = tid; e < hd * p8; e += nth) {
+            uint16_t *dst = vtbuf + i * vs + pc * 8;
+            const uint16_t *src = vc + (size_t)i * vstride + pc * 8;
+            if (vvec) cp_async16(dst, src);
+            else *(uint4 *)dst = ld_row8(src, false);
+            pc += dp; i += di;
+            if (pc >= p8) { pc -= p8; i++; }
+        }
+    }
+    cp_async_commit();
+}
+
 template <bool VT>
 __device__ __noinline__ void attend_exact(const float *q, const uint16_t *kc, const uint16_t *vc, int kstride, int vstride, const uint16_t *kcur,
                              const uint16_t *vcur, int pos, int hd, float *scores, float *out, float *red, const uint32_t *elist,
-                             const uint32_t *eindex, uint16_t *kvbuf, uint16_t *vtbuf, int chunk) {
+                             const uint32_t *eindex, uint16_t *kvbuf, uint16_t *vtbuf, int chunk, bool prestaged) {
     const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31, warp = tid >> 5;
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
     const bool kvec = kstride % 8 == 0 && ((uintptr_t)kc & 15) == 0;
@@ -454,13 +496,17 @@ __device__ __noinline__ void attend_exact(const float *q, const uint16_t *kc, co
         }
         cp_async_commit();
     };
-    if (VT) stage_v(0, min(chunk, n));                       // its own buffer: lands during the scores
+    if (!prestaged) attend_prestage<VT>(kc, vc, kstride, vstride, pos, hd, kvbuf, vtbuf, chunk);
     // Scores: one thread per row, from K rows staged in shared memory (coalesced copies).
     float m = -INFINITY;
     for (int c0 = 0; c0 < n; c0 += chunk) {
         const int cnt = min(chunk, n - c0);
-        if (c0 > 0) __syncthreads();
-        stage_k(c0, cnt);
+        if (c0 > 0) {
+            __syncthreads();
+            stage_k(c0, cnt);
+        } else if (pos < cnt) {                              // the first chunk's rows < pos are prestaged
+            for (int i = tid * 8; i < hd; i += nth * 8) *(uint4 *)(kvbuf + pos * rs + i) = *(const uint4 *)(kcur + i);
+        }
         cp_async_wait_all();
         __syncthreads();
         for (int r = tid; r < cnt; r += nth) {
