@@ -116,8 +116,11 @@ __device__ void prefetch_layer(const DecodeArgs &a, const LayerDev &L, const Rol
     if (r.qkv0 < r.qkv1) prefetch_l2(L.qkv + r.qkv0 * tq, (size_t)(r.qkv1 - r.qkv0) * tq);
     if (r.wo0 < r.wo1) prefetch_l2(L.wo + r.wo0 * to, (size_t)(r.wo1 - r.wo0) * to);
     if (r.ffn0 < r.ffn1) {
-        prefetch_l2(L.up + r.ffn0 * tu, (size_t)(r.ffn1 - r.ffn0) * tu);
-        prefetch_l2(L.gate + r.ffn0 * tg, (size_t)(r.ffn1 - r.ffn0) * tg);
+        if (!L.gate) prefetch_l2(L.up + 2 * r.ffn0 * tu, (size_t)2 * (r.ffn1 - r.ffn0) * tu);
+        else {
+            prefetch_l2(L.up + r.ffn0 * tu, (size_t)(r.ffn1 - r.ffn0) * tu);
+            prefetch_l2(L.gate + r.ffn0 * tg, (size_t)(r.ffn1 - r.ffn0) * tg);
+        }
     }
     if (r.dn0 < r.dn1) prefetch_l2(L.down + r.dn0 * td, (size_t)(r.dn1 - r.dn0) * td);
 }
@@ -238,9 +241,13 @@ __device__ __noinline__ void phase_ffn(const DecodeArgs &a, const LayerDev &L, c
     const int nf = role.ffn1 - role.ffn0;
     prepare(L.dt_up, s.xb, a.dim, s.prep);
     trace(a, tslot, pos, l, 12);
-    matvec_exact(L.dt_up, L.up, a.dim, role.ffn0, role.ffn1, s.prep, s.scratch, a.scratch_pairs, s.y);
-    if (L.dt_gate != L.dt_up) prepare(L.dt_gate, s.xb, a.dim, s.prep);
-    matvec_exact(L.dt_gate, L.gate, a.dim, role.ffn0, role.ffn1, s.prep, s.scratch, a.scratch_pairs, s.y + nf * kTile);
+    if (!L.gate) {                                                        // up and gate packed per CTA: one pass
+        matvec_exact(L.dt_up, L.up, a.dim, 2 * role.ffn0, 2 * role.ffn1, s.prep, s.scratch, a.scratch_pairs, s.y);
+    } else {
+        matvec_exact(L.dt_up, L.up, a.dim, role.ffn0, role.ffn1, s.prep, s.scratch, a.scratch_pairs, s.y);
+        if (L.dt_gate != L.dt_up) prepare(L.dt_gate, s.xb, a.dim, s.prep);
+        matvec_exact(L.dt_gate, L.gate, a.dim, role.ffn0, role.ffn1, s.prep, s.scratch, a.scratch_pairs, s.y + nf * kTile);
+    }
     trace(a, tslot, pos, l, 13);
     const int g0 = role.ffn0 * kTile, n = min(role.ffn1 * kTile, a.ffn) - g0;
     for (int o = tid; o < n; o += nth) {
@@ -470,15 +477,17 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
         // engine.c:299-300) and hands the result to cluster 0, so all 16 decide alike.
         if (cta == 0) {
             const int r = wait_word(a, a.hx.count, tcount * (uint32_t)a.grid, false);
+            float *sl = s.tmp + 4;                                        // every slot at once, then a serial scan
+            for (int i = tid; i < 3 * a.grid; i += blockDim.x) sl[i] = ld_cg_f32(a.hx.slots + i);
+            __syncthreads();
             if (tid == 0) {
                 float gmax = -INFINITY;
                 int next = 0;
                 for (int c = 0; c < a.grid; c++) {
-                    const float v = ld_cg_f32(a.hx.slots + 3 * c);
-                    if (v > gmax) { gmax = v; next = __float_as_int(ld_cg_f32(a.hx.slots + 3 * c + 1)); }
+                    if (sl[3 * c] > gmax) { gmax = sl[3 * c]; next = __float_as_int(sl[3 * c + 1]); }
                 }
                 s.tmp[0] = __int_as_float(next);
-                s.tmp[1] = __int_as_float(__float_as_int(ld_cg_f32(a.hx.slots + 2)));
+                s.tmp[1] = sl[2];
                 s.tmp[2] = __int_as_float(r > 0 ? 1 : 0);
                 s.tmp[3] = 0.0f;
             }

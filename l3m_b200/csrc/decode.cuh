@@ -6,7 +6,7 @@ namespace l3m {
 
 struct alignas(16) LayerDev {
     const uint8_t *qkv;                 // rows: q of every head, then k of every kv head, then v
-    const uint8_t *wo, *gate, *up, *down;
+    const uint8_t *wo, *gate, *up, *down;   // gate NULL: up holds, per CTA, its up tiles then its gate tiles
     const float *attn_norm, *ffn_norm;
     const float *bq, *bk, *bv, *bo, *b_up, *b_down;   // NULL when absent
     uint16_t *kc, *vc;                  // K [n_kv][ctx][hd], V [n_kv][hd][vstride] bf16

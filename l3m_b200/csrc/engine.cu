@@ -216,8 +216,27 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
         off_qkv[l] = pack(s, r);
         layers[l].dt_qkv = r.dtype;
         off_wo[l] = pack_matrix(s, f, l3m_file_blk(f, l, "wo"), ref, &layers[l].dt_wo);
-        off_up[l] = pack_matrix(s, f, l3m_file_blk(f, l, "w_up"), ref, &layers[l].dt_up);
-        off_gate[l] = pack_matrix(s, f, l3m_file_blk(f, l, "w_gate"), ref, &layers[l].dt_gate);
+        const l3m_tensor *wu = l3m_file_blk(f, l, "w_up"), *wg = l3m_file_blk(f, l, "w_gate");
+        if (ref || wu->dtype == wg->dtype) {
+            // Up and gate in one matrix, each CTA's range back to back: [its up tiles][its gate tiles].
+            Rows r;
+            for (int c = 0; c < l3m::kClusterCtas; c++) {
+                int t0, t1;
+                split(tiles_of(ffn), l3m::kClusterCtas, c, &t0, &t1);
+                for (const l3m_tensor *t : {wu, wg}) {
+                    for (int i = t0 * L3M_TILE; i < t1 * L3M_TILE; i++) {
+                        if (i < ffn) r.add(f, t, i, ref);
+                        else r.ptr.push_back(nullptr);
+                    }
+                }
+            }
+            off_up[l] = pack(s, r);
+            off_gate[l] = (size_t)-1;
+            layers[l].dt_up = layers[l].dt_gate = r.dtype;
+        } else {
+            off_up[l] = pack_matrix(s, f, wu, ref, &layers[l].dt_up);
+            off_gate[l] = pack_matrix(s, f, wg, ref, &layers[l].dt_gate);
+        }
         off_down[l] = pack_matrix(s, f, l3m_file_blk(f, l, "w_down"), ref, &layers[l].dt_down);
     }
     const l3m_tensor *head = l3m_file_tensor(f, (m->flags & L3M_F_TIED) ? "embed" : "lm_head");
@@ -269,7 +288,7 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
         d.qkv = g.arena + off_qkv[l];
         d.wo = g.arena + off_wo[l];
         d.up = g.arena + off_up[l];
-        d.gate = g.arena + off_gate[l];
+        d.gate = off_gate[l] == (size_t)-1 ? nullptr : g.arena + off_gate[l];
         d.down = g.arena + off_down[l];
         d.attn_norm = A(vo[l].an); d.ffn_norm = A(vo[l].fn);
         d.bq = A(vo[l].bq); d.bk = A(vo[l].bk); d.bv = A(vo[l].bv); d.bo = A(vo[l].bo); d.b_up = A(vo[l].bu); d.b_down = A(vo[l].bd);
