@@ -35,6 +35,8 @@ struct Smem {
     float2 *rope;
     uint16_t *kcur, *vcur, *kvbuf, *vtbuf;
     float2 *scratch;
+    uint8_t *w;                          // weight staging area
+    unsigned long long *wbar;            // its mbarrier
     Prep prep;
 };
 
@@ -62,6 +64,8 @@ __device__ __forceinline__ Smem carve(unsigned char *base, const DecodeArgs &a) 
     s.kvbuf = (uint16_t *)(base + a.sm_kvbuf);
     s.vtbuf = (uint16_t *)(base + a.sm_vt);
     s.scratch = (float2 *)(base + a.sm_scratch);
+    s.w = base + a.sm_w;
+    s.wbar = (unsigned long long *)(base + a.sm_wbar);
     s.prep.q8 = (int8_t *)(base + a.sm_q8);
     s.prep.scale = (float *)(base + a.sm_scale);
     s.prep.sum = (int32_t *)(base + a.sm_sum);
@@ -134,6 +138,67 @@ __device__ void stage_vectors(const DecodeArgs &a, const LayerDev &L, const Role
     cp_async_commit();
 }
 
+// ---- Weight staging. A CTA's quantised tiles for its next matvec phase are copied into shared
+// memory by the tensor memory accelerator (cp.async.bulk: one thread issues, no registers held,
+// completion counted in bytes on one mbarrier) while the current phase, its barrier and the next
+// norm run; the matvec then reads shared memory. One copy is outstanding at a time: the phase that
+// consumes it waits for it, and the next copy is issued only after that phase's last read.
+constexpr uint32_t kStageChunk = 32768;
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void stage_init(const Smem &s) {
+    if (threadIdx.x == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(s.wbar)) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+}
+
+// Tiles [t0, t1) of a matrix of dtype with k inputs: how many of the first ones fit in cap bytes
+// (0 for f32/bf16, which are read from global memory). Same value in every thread.
+__device__ __forceinline__ int stage_count(int dtype, int k, int t0, int t1, int cap) {
+    if (t1 <= t0 || !(dtype == DT_Q8 || dtype == DT_Q4 || dtype == DT_MX) || cap <= 0) return 0;
+    return (int)min((size_t)(t1 - t0), (size_t)cap / tile_bytes(dtype, k));
+}
+
+// Every thread, after a __syncthreads that ends every read of dst: start the copy of tiles
+// [t0, t0 + n) to dst (n = stage_count(...)); returns n.
+__device__ __noinline__ int stage_issue(const Smem &s, int dtype, const uint8_t *tiles, int k, int t0, int t1, uint8_t *dst, int cap) {
+    const int n = stage_count(dtype, k, t0, t1, cap);
+    if (n > 0 && threadIdx.x == 0) {
+        const size_t tb = tile_bytes(dtype, k);
+        const uint32_t bytes = (uint32_t)(n * tb), bar = smem_addr(s.wbar);
+        const uint8_t *src = tiles + (size_t)t0 * tb;
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+        for (uint32_t o = 0; o < bytes; o += kStageChunk) {
+            const uint32_t c = min(bytes - o, kStageChunk);
+            asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                         ::"r"(smem_addr(dst + o)), "l"(src + o), "r"(c), "r"(bar) : "memory");
+        }
+    }
+    return n;
+}
+
+// Every thread: wait for the outstanding copy (phase parity par of the mbarrier). Bounded by
+// timeout_ns; on timeout the abort word is set (the sampled position then stops the launch) and
+// the caller goes on with whatever the buffer holds.
+__device__ __noinline__ void stage_wait(const DecodeArgs &a, const Smem &s, uint32_t par) {
+    const uint32_t bar = smem_addr(s.wbar);
+    uint64_t t0 = 0;
+    for (int spins = 0;; spins++) {
+        uint32_t done;
+        asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                     : "=r"(done) : "r"(bar), "r"(par) : "memory");
+        if (done) return;
+        if (spins == 0) t0 = globaltimer_ns();
+        else if ((spins & 63) == 0 && globaltimer_ns() - t0 > a.hx.timeout_ns) {
+            atomicCAS(a.hx.abort_flag, 0, kErrTimeout);
+            return;
+        }
+    }
+}
+
 // x = embedding row of tok (reference src/engine.c:236, src/pack.c:55-62).
 __device__ __noinline__ void embed_row(const DecodeArgs &a, int tok, float *x) {
     const uint8_t *row = a.embed + (size_t)tok * a.embed_row_bytes;
@@ -163,11 +228,18 @@ __device__ __noinline__ void embed_row(const DecodeArgs &a, int tok, float *x) {
     __syncthreads();
 }
 
-// Phase Q: this CTA's tiles of the q/k/v rows (biases added) -> every CTA's xq.
-__device__ __noinline__ void phase_qkv(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s) {
+// Phase Q: this CTA's tiles of the q/k/v rows (biases added) -> s.y (the caller scatters into xq).
+// ns tiles staged at the staging area's offset w_extra (phase parity par).
+__device__ __noinline__ void phase_qkv(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s, int ns, uint32_t par, int pos,
+                                       int l, int tslot) {
     rmsnorm_exact(s.x, s.wa, a.dim, a.eps, s.xb, s.tmp, s.red);
+    trace(a, tslot, pos, l, 16);
     prepare(L.dt_qkv, s.xb, a.dim, s.prep);
-    matvec_exact(L.dt_qkv, L.qkv, a.dim, role.qkv0, role.qkv1, s.prep, s.scratch, a.scratch_pairs, s.y);
+    trace(a, tslot, pos, l, 17);
+    if (ns) stage_wait(a, s, par);
+    trace(a, tslot, pos, l, 18);
+    matvec_exact(L.dt_qkv, L.qkv, a.dim, role.qkv0, role.qkv1, s.prep, s.scratch, a.scratch_pairs, s.y, s.w + a.w_extra, ns);
+    trace(a, tslot, pos, l, 19);
     const int g0 = role.qkv0 * kTile, n = min(role.qkv1 * kTile, a.n_qkv) - g0, nq = a.n_heads * a.hd, nk = a.n_kv * a.hd;
     if (L.bq) {
         for (int o = threadIdx.x; o < n; o += blockDim.x) {
@@ -176,7 +248,6 @@ __device__ __noinline__ void phase_qkv(const DecodeArgs &a, const LayerDev &L, c
         }
         __syncthreads();
     }
-    scatter(s.y, s.xq, g0, n);
 }
 
 __device__ __forceinline__ const uint16_t *kcache(const DecodeArgs &a, const LayerDev &L, int h) {
@@ -188,7 +259,8 @@ __device__ __forceinline__ const uint16_t *vcache(const DecodeArgs &a, const Lay
 
 // Phase A for query head h at position pos (xq complete): RoPE, this position's K/V row (stored by
 // the first head of each kv group), attention -> every CTA's xa[h*hd, (h+1)*hd).
-__device__ __noinline__ void phase_attention(const DecodeArgs &a, const LayerDev &L, const Smem &s, int h, int pos, bool prestaged) {
+__device__ __noinline__ void phase_attention(const DecodeArgs &a, const LayerDev &L, const Smem &s, int h, int pos, bool prestaged, int l,
+                                             int tslot) {
     const int tid = threadIdx.x, nth = blockDim.x, hd = a.hd, kvh = h / a.hpk, nq = a.n_heads * hd, nk = a.n_kv * hd;
     float *y = s.y;                                                  // q, k, v of this head
     for (int i = tid; i < hd; i += nth) {
@@ -213,61 +285,79 @@ __device__ __noinline__ void phase_attention(const DecodeArgs &a, const LayerDev
         }
     }
     __syncthreads();
+    trace(a, tslot, pos, l, 14);
     attend_exact<true>(y, kc, vc, hd, a.vstride, s.kcur, s.vcur, pos, hd, s.scores, s.att, s.red, a.elist, a.eindex, s.kvbuf, s.vtbuf,
                        a.attn_chunk, prestaged);
+    trace(a, tslot, pos, l, 15);
     scatter(s.att, s.xa, h * hd, hd);
 }
 
-// Phase B: this CTA's tiles of wo over attn -> every CTA's xp.
-__device__ __noinline__ void phase_wo(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s) {
+// Phase B: this CTA's tiles of wo over attn -> s.y (the caller scatters into xp; ns tiles staged at
+// offset w_extra).
+__device__ __noinline__ void phase_wo(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s, int ns, uint32_t par, int pos,
+                                      int l, int tslot) {
     prepare(L.dt_wo, s.xa, a.dim, s.prep);
-    matvec_exact(L.dt_wo, L.wo, a.dim, role.wo0, role.wo1, s.prep, s.scratch, a.scratch_pairs, s.y);
+    trace(a, tslot, pos, l, 20);
+    if (ns) stage_wait(a, s, par);
+    trace(a, tslot, pos, l, 21);
+    matvec_exact(L.dt_wo, L.wo, a.dim, role.wo0, role.wo1, s.prep, s.scratch, a.scratch_pairs, s.y, s.w + a.w_extra, ns);
+    trace(a, tslot, pos, l, 22);
     const int g0 = role.wo0 * kTile, n = min(role.wo1 * kTile, a.dim) - g0;
     if (L.bo) {
         for (int o = threadIdx.x; o < n; o += blockDim.x) s.y[o] = __fadd_rn(s.y[o], __ldg(L.bo + g0 + o));
         __syncthreads();
     }
-    scatter(s.y, s.xp, g0, n);
 }
 
-// Phase C: x += proj in every CTA; the ffn CTAs' tiles of up and gate, SiLU gate -> every CTA's xh.
-__device__ __noinline__ void phase_ffn(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s, int pos, int l, int tslot) {
-    const int tid = threadIdx.x, nth = blockDim.x;
-    for (int i = tid; i < a.dim; i += nth) s.x[i] = __fadd_rn(s.x[i], s.xp[i]);
+// Phase C: x += proj in every CTA; the ffn CTAs' tiles of up and gate -> s.y (up of the CTA's
+// tiles, then gate; ns tiles of up, or of the interleaved up/gate, staged at offset 0).
+__device__ __noinline__ void phase_ffn(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s, int pos, int l, int tslot,
+                                       int ns, uint32_t par) {
+    for (int i = threadIdx.x; i < a.dim; i += blockDim.x) s.x[i] = __fadd_rn(s.x[i], s.xp[i]);
     __syncthreads();
     if (role.ffn0 >= role.ffn1) return;
     rmsnorm_exact(s.x, s.wf, a.dim, a.eps, s.xb, s.tmp, s.red);
     trace(a, tslot, pos, l, 7);
     const int nf = role.ffn1 - role.ffn0;
     prepare(L.dt_up, s.xb, a.dim, s.prep);
+    trace(a, tslot, pos, l, 26);
+    if (ns) stage_wait(a, s, par);
     trace(a, tslot, pos, l, 12);
     if (!L.gate) {                                                        // up and gate packed per CTA: one pass
-        matvec_exact(L.dt_up, L.up, a.dim, 2 * role.ffn0, 2 * role.ffn1, s.prep, s.scratch, a.scratch_pairs, s.y);
+        matvec_exact(L.dt_up, L.up, a.dim, 2 * role.ffn0, 2 * role.ffn1, s.prep, s.scratch, a.scratch_pairs, s.y, s.w, ns);
     } else {
-        matvec_exact(L.dt_up, L.up, a.dim, role.ffn0, role.ffn1, s.prep, s.scratch, a.scratch_pairs, s.y);
+        matvec_exact(L.dt_up, L.up, a.dim, role.ffn0, role.ffn1, s.prep, s.scratch, a.scratch_pairs, s.y, s.w, ns);
         if (L.dt_gate != L.dt_up) prepare(L.dt_gate, s.xb, a.dim, s.prep);
         matvec_exact(L.dt_gate, L.gate, a.dim, role.ffn0, role.ffn1, s.prep, s.scratch, a.scratch_pairs, s.y + nf * kTile);
     }
     trace(a, tslot, pos, l, 13);
-    const int g0 = role.ffn0 * kTile, n = min(role.ffn1 * kTile, a.ffn) - g0;
-    for (int o = tid; o < n; o += nth) {
+}
+
+// The SiLU gate of phase C's up/gate results in s.y -> s.tmp (the caller scatters into xh).
+__device__ __noinline__ void ffn_gate(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s) {
+    const int nf = role.ffn1 - role.ffn0, g0 = role.ffn0 * kTile, n = min(role.ffn1 * kTile, a.ffn) - g0;
+    for (int o = threadIdx.x; o < n; o += blockDim.x) {
         const float up = L.b_up ? __fadd_rn(s.y[o], __ldg(L.b_up + g0 + o)) : s.y[o];
         s.tmp[o] = silu_mul(up, s.y[nf * kTile + o], a.elist, a.eindex);
     }
     __syncthreads();
-    scatter(s.tmp, s.xh, g0, n);
 }
 
-// Phase D: this CTA's tiles of down over h -> every CTA's xd.
-__device__ __noinline__ void phase_down(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s) {
+// Phase D: this CTA's tiles of down over h -> s.y (the caller scatters into xd; ns tiles staged at
+// offset 0).
+__device__ __noinline__ void phase_down(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s, int ns, uint32_t par, int pos,
+                                        int l, int tslot) {
     prepare(L.dt_down, s.xh, a.ffn, s.prep);
-    matvec_exact(L.dt_down, L.down, a.ffn, role.dn0, role.dn1, s.prep, s.scratch, a.scratch_pairs, s.y);
+    trace(a, tslot, pos, l, 23);
+    if (ns) stage_wait(a, s, par);
+    trace(a, tslot, pos, l, 24);
+    matvec_exact(L.dt_down, L.down, a.ffn, role.dn0, role.dn1, s.prep, s.scratch, a.scratch_pairs, s.y, s.w, ns);
+    trace(a, tslot, pos, l, 25);
     const int g0 = role.dn0 * kTile, n = min(role.dn1 * kTile, a.dim) - g0;
     if (L.b_down) {
         for (int o = threadIdx.x; o < n; o += blockDim.x) s.y[o] = __fadd_rn(s.y[o], __ldg(L.b_down + g0 + o));
         __syncthreads();
     }
-    scatter(s.y, s.xd, g0, n);
 }
 
 __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t *p) {
@@ -408,6 +498,12 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
         return;
     }
     stage_vectors(a, layers[0], role, s, 0);
+    stage_init(s);
+    // The staged-weight schedule: qkv and wo into [w_extra, w_bytes) (the attention buffers are live
+    // from the layer top to the end of attention), up/gate and down from offset 0. ns: tiles of the
+    // outstanding copy; wpar: its mbarrier phase parity.
+    uint32_t wpar = 0;
+    int ns = stage_issue(s, layers[0].dt_qkv, layers[0].qkv, a.dim, role.qkv0, role.qkv1, s.w + a.w_extra, a.w_bytes - a.w_extra);
     cluster_sync();                                                       // every CTA of the cluster has started
 
     for (pos = 0;; pos++) {
@@ -431,27 +527,52 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
             if (role.head0 >= 0)                                          // K/V copies land during Q
                 attend_prestage<true>(kcache(a, L, role.head0), vcache(a, L, role.head0), a.hd, a.vstride, pos, a.hd, s.kvbuf, s.vtbuf,
                                       a.attn_chunk);
-            if (role.qkv0 < role.qkv1) phase_qkv(a, L, role, s);          // Q
+            // Each phase: its matvec, the copy of the next phase's tiles (the staging area is free from
+            // here on), then the exchange.
+            if (role.qkv0 < role.qkv1) phase_qkv(a, L, role, s, ns, wpar, pos, l, tslot);   // Q
+            if (ns) wpar ^= 1;
+            ns = stage_issue(s, L.dt_wo, L.wo, a.dim, role.wo0, role.wo1, s.w + a.w_extra, a.w_bytes - a.w_extra);
+            trace(a, tslot, pos, l, 27);
+            if (role.qkv0 < role.qkv1) scatter(s.y, s.xq, role.qkv0 * kTile, min(role.qkv1 * kTile, a.n_qkv) - role.qkv0 * kTile);
             trace(a, tslot, pos, l, 1);
             cluster_sync();                                               // 1: qkv
             trace(a, tslot, pos, l, 2);
             for (int h = role.head0; h >= 0 && h < a.n_heads; h += kClusterCtas)   // A
-                phase_attention(a, L, s, h, pos, h == role.head0);
+                phase_attention(a, L, s, h, pos, h == role.head0, l, tslot);
             trace(a, tslot, pos, l, 3);
             cluster_sync();                                               // 2: attn
             trace(a, tslot, pos, l, 4);
-            if (role.wo0 < role.wo1) phase_wo(a, L, role, s);             // B
+            if (role.wo0 < role.wo1) phase_wo(a, L, role, s, ns, wpar, pos, l, tslot);   // B
+            if (ns) wpar ^= 1;
+            if (!L.gate) ns = stage_issue(s, L.dt_up, L.up, a.dim, 2 * role.ffn0, 2 * role.ffn1, s.w, a.w_bytes);
+            else ns = stage_issue(s, L.dt_up, L.up, a.dim, role.ffn0, role.ffn1, s.w, a.w_bytes);
+            trace(a, tslot, pos, l, 28);
+            if (role.wo0 < role.wo1) scatter(s.y, s.xp, role.wo0 * kTile, min(role.wo1 * kTile, a.dim) - role.wo0 * kTile);
             trace(a, tslot, pos, l, 5);
             cluster_sync();                                               // 3: proj
             trace(a, tslot, pos, l, 6);
-            phase_ffn(a, L, role, s, pos, l, tslot);                      // C
+            phase_ffn(a, L, role, s, pos, l, tslot, ns, wpar);            // C
+            if (ns) wpar ^= 1;
+            ns = stage_issue(s, L.dt_down, L.down, a.ffn, role.dn0, role.dn1, s.w, a.w_bytes);
+            trace(a, tslot, pos, l, 29);
+            if (role.ffn0 < role.ffn1) {
+                ffn_gate(a, L, role, s);
+                scatter(s.tmp, s.xh, role.ffn0 * kTile, min(role.ffn1 * kTile, a.ffn) - role.ffn0 * kTile);
+            }
             // The next layer's norm weights (and the next position's RoPE row) while the rest runs.
             if (l + 1 < a.n_layers) stage_vectors(a, layers[l + 1], role, s, pos);
             else stage_vectors(a, layers[0], role, s, pos + 1);
             trace(a, tslot, pos, l, 8);
             cluster_sync();                                               // 4: h
             trace(a, tslot, pos, l, 9);
-            if (role.dn0 < role.dn1) phase_down(a, L, role, s);           // D
+            if (role.dn0 < role.dn1) phase_down(a, L, role, s, ns, wpar, pos, l, tslot);   // D
+            if (ns) wpar ^= 1;
+            {
+                const LayerDev &N = layers[l + 1 < a.n_layers ? l + 1 : 0];
+                ns = stage_issue(s, N.dt_qkv, N.qkv, a.dim, role.qkv0, role.qkv1, s.w + a.w_extra, a.w_bytes - a.w_extra);
+            }
+            trace(a, tslot, pos, l, 30);
+            if (role.dn0 < role.dn1) scatter(s.y, s.xd, role.dn0 * kTile, min(role.dn1 * kTile, a.dim) - role.dn0 * kTile);
             trace(a, tslot, pos, l, 10);
             cluster_sync();                                               // 5: down
             for (int i = tid; i < a.dim; i += blockDim.x) s.x[i] = __fadd_rn(s.x[i], s.xd[i]);
@@ -488,7 +609,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
                 }
                 s.tmp[0] = __int_as_float(next);
                 s.tmp[1] = sl[2];
-                s.tmp[2] = __int_as_float(r > 0 ? 1 : 0);
+                s.tmp[2] = __int_as_float(r > 0 && !*(volatile int *)a.hx.abort_flag ? 1 : 0);
                 s.tmp[3] = 0.0f;
             }
             __syncthreads();
@@ -512,6 +633,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
         // reaches after reading it here.
     }
     cp_async_wait_all();                                                  // no copy outlives the CTA
+    if (ns) stage_wait(a, s, wpar);
     cluster_sync();                                                       // no CTA leaves while others may write its memory
     if (cta == 0 && tid == 0) {
         asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.hx.flag), "r"(kHeadDone) : "memory");   // the helpers stop
@@ -568,6 +690,17 @@ extern "C" int l3m_decode_launch(const l3m::DecodeArgs *a, const l3m::DecodeArgs
         return -1;
     }
     return 0;
+}
+
+// The dynamic shared memory one decode CTA may use on the current device: the opt-in limit per block
+// less the kernel's static shared memory.
+extern "C" int l3m_decode_smem_budget(void) {
+    int dev = 0, optin = 0;
+    cudaFuncAttributes fa = {};
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+        cudaFuncGetAttributes(&fa, (const void *)l3m::decode_kernel) != cudaSuccess)
+        return 0;
+    return optin - (int)fa.sharedSizeBytes;
 }
 
 // How many clusters of kClusterCtas CTAs with smem_bytes of shared memory each can be resident on

@@ -33,7 +33,7 @@ struct Ctrl {
 
 constexpr int kDecodeThreads = 256;   // 8 warps per CTA
 constexpr int kClusterCtas = 16;      // one thread-block cluster runs the whole model
-constexpr int kTraceEvents = 16;      // stamps per (position, layer); see the trace() calls in decode.cu
+constexpr int kTraceEvents = 32;      // stamps per (position, layer); see the trace() calls in decode.cu
 
 // The head phase runs on every CTA of the launch (several clusters): cluster 0 publishes x in
 // global memory with a release flag, every CTA computes its vocabulary tiles and adds (max, index)
@@ -75,6 +75,10 @@ struct DecodeArgs {
     int sm_wa, sm_wf, sm_wh, sm_rope;   // this layer's norm weights, the final norm, this position's RoPE row
     int sm_layers;                      // a copy of layers[0 .. n_layers)
     int sm_xq, sm_xa, sm_xp, sm_xh, sm_xd, sm_xt;   // exchanged vectors: qkv, attn, proj, h, down, (max, index, stop) per CTA
+    // Weight staging area (quantised tiles of the next matvec phase, copied in by cp.async.bulk):
+    // sm_w .. sm_w + w_bytes; its first w_extra bytes overlap the attention buffers (kvbuf, vt), so
+    // the phases around attention (qkv, wo) use only [w_extra, w_bytes). sm_wbar: its mbarrier.
+    int sm_w, w_bytes, w_extra, sm_wbar;
     int vstride;                        // V cache: element i of position t at vc[i * vstride + t]
     int scratch_pairs, smem_bytes, attn_chunk;
 };

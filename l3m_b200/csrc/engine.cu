@@ -27,6 +27,7 @@
 
 extern "C" int l3m_decode_launch(const l3m::DecodeArgs *a, const l3m::DecodeArgs *a_dev, void *stream);
 extern "C" int l3m_decode_occupancy(int smem_bytes);
+extern "C" int l3m_decode_smem_budget(void);
 extern "C" int l3m_expf_tables(const uint32_t **list, const uint32_t **index);
 
 namespace {
@@ -377,8 +378,6 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     a.sm_rope = take(hd / 2 * 8);
     a.sm_layers = take(L * (int)sizeof(l3m::LayerDev));
     a.attn_chunk = std::min(m->ctx, 256);
-    a.sm_kvbuf = take(a.attn_chunk * (hd + 8) * 2);
-    a.sm_vt = take(hd * l3m::attn_vt_stride(a.attn_chunk) * 2);
     a.vstride = vstride;
     a.sm_xq = take(n_qkv * 4);
     a.sm_xa = take(dim * 4);
@@ -386,15 +385,32 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     a.sm_xh = take(ffn * 4);
     a.sm_xd = take(dim * 4);
     a.sm_xt = take(4 * G * 4);
-    a.sm_scratch = take(0);
-    const int budget = 200 * 1024;
-    a.scratch_pairs = std::min(8192, (budget - off) / 8);
-    const int need_pairs = (mx / 32) * L3M_TILE;
-    if (a.scratch_pairs < need_pairs) {
-        fprintf(stderr, "l3m: dim %d / ffn %d need more shared memory than a B200 SM has for this kernel\n", dim, ffn);
+    a.sm_wbar = take(16);
+    // Scratch: the (scale product, dot) pairs of the largest per-CTA phase of a layer, so each runs in
+    // one pass (the head runs in several).
+    int pairs = (mx / 32) * L3M_TILE;
+    for (const l3m::Role &r : make_roles(G))
+        pairs = std::max({pairs, (r.qkv1 - r.qkv0) * L3M_TILE * (dim / 32), (r.wo1 - r.wo0) * L3M_TILE * (dim / 32),
+                          2 * (r.ffn1 - r.ffn0) * L3M_TILE * (dim / 32), (r.dn1 - r.dn0) * L3M_TILE * (ffn / 32)});
+    a.scratch_pairs = pairs;
+    a.sm_scratch = take(pairs * 8);
+    // The weight staging area takes the rest; the attention buffers are its first bytes.
+    off = (off + 127) & ~127;
+    a.sm_w = off;
+    a.sm_kvbuf = take(a.attn_chunk * (hd + 8) * 2);
+    a.sm_vt = take(hd * l3m::attn_vt_stride(a.attn_chunk) * 2);
+    off = (off + 127) & ~127;
+    a.w_extra = off - a.sm_w;
+    const int budget = l3m_decode_smem_budget();
+    if (off > budget) {
+        fprintf(stderr, "l3m: dim %d / ffn %d / ctx %d need more shared memory than a B200 SM has for this kernel\n", dim, ffn, m->ctx);
         return false;
     }
-    a.smem_bytes = off + a.scratch_pairs * 8;
+    a.w_bytes = (budget - a.sm_w) & ~127;
+    a.smem_bytes = a.sm_w + a.w_bytes;
+    if (o.verbose)
+        fprintf(stderr, "l3m: shared memory %d B per CTA: vectors %d, scratch %d pairs, staging %d (attention buffers %d)\n", a.smem_bytes,
+                a.sm_scratch, a.scratch_pairs, a.w_bytes, a.w_extra);
     GT = std::min(GT, l3m_decode_occupancy(a.smem_bytes) * G);            // whole clusters resident at once
     if (GT < G) {
         fprintf(stderr, "l3m: a cluster of %d decode CTAs does not fit on GPU %d\n", G, g.dev);

@@ -33,14 +33,21 @@ L3M_HD uint16_t l3m_f32_to_bf16(float f) {
     return (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
 }
 
-// binary16 -> binary32, exact (subnormals scaled by 2^-24, inf and NaN payloads kept).
+// binary16 -> binary32, exact (subnormals scaled by 2^-24, inf and NaN payloads kept). On the
+// device the hardware widening (exact for every non-NaN input) with the NaN bits selected, no branch.
 L3M_HD float l3m_f16_to_f32(uint16_t h) {
     uint32_t sign = (uint32_t)(h & 0x8000u) << 16, e = (h >> 10) & 31u, m = h & 1023u;
+#ifdef __CUDA_ARCH__
+    float f;
+    asm("cvt.f32.f16 %0, %1;" : "=f"(f) : "h"(h));
+    return e == 31 && m ? l3m_bits_f32(sign | 0x7F800000u | m << 13) : f;
+#else
     if (e == 0) {
         float mag = (float)m * l3m_bits_f32(0x33800000u);     // m * 2^-24, exact
         return sign ? -mag : mag;
     }
     return l3m_bits_f32(e == 31 ? (sign | 0x7F800000u | m << 13) : (sign | (e + 112u) << 23 | m << 13));
+#endif
 }
 
 // The mxfp4 block scale of the reference's kernels: 2^(e-127) / 2 = 2^(e-128), subnormal for e < 2.

@@ -112,19 +112,20 @@ __device__ __forceinline__ uint32_t mx_lut16(uint32_t s) {
 // (q8: 8 groups, q4/mxfp4: 4) and the four scales.
 struct QLoad4 { uint4 w[8]; uint2 d; };
 
-template <int DT>
+// GEN: generic loads (the block may be in shared memory), else streaming global loads.
+template <int DT, bool GEN>
 __device__ __forceinline__ void qload4(QLoad4 &q, const uint8_t *blk, int r4) {
     if (DT == DT_Q8) {
         const uint8_t *g = blk + 32 + 16 * r4;
 #pragma unroll
-        for (int j = 0; j < 8; j++) q.w[j] = ld_stream_v4(g + 64 * j);
-        q.d = ld_stream_v2(blk + 8 * r4);
+        for (int j = 0; j < 8; j++) q.w[j] = GEN ? *(const uint4 *)(g + 64 * j) : ld_stream_v4(g + 64 * j);
+        q.d = GEN ? *(const uint2 *)(blk + 8 * r4) : ld_stream_v2(blk + 8 * r4);
     } else {
         const uint8_t *g = blk + (DT == DT_MX ? 16 : 32) + 16 * r4;
 #pragma unroll
-        for (int j = 0; j < 4; j++) q.w[j] = ld_stream_v4(g + 64 * j);
-        if (DT == DT_MX) q.d = make_uint2(ld_stream_u32(blk + 4 * r4), 0);
-        else q.d = ld_stream_v2(blk + 8 * r4);
+        for (int j = 0; j < 4; j++) q.w[j] = GEN ? *(const uint4 *)(g + 64 * j) : ld_stream_v4(g + 64 * j);
+        if (DT == DT_MX) q.d = make_uint2(GEN ? *(const uint32_t *)(blk + 4 * r4) : ld_stream_u32(blk + 4 * r4), 0);
+        else q.d = GEN ? *(const uint2 *)(blk + 8 * r4) : ld_stream_v2(blk + 8 * r4);
     }
 }
 
@@ -206,8 +207,9 @@ __device__ __forceinline__ float qscale(uint32_t d) { return DT == DT_MX ? l3m_e
 // each output's {RN(sx[b] * d), (float)dot} goes to scratch[b * m + o]. Then one thread per output
 // runs the fp32 chain in block order.
 constexpr int kQU = 2;
-// Tiles [0, ntA) come from `tiles`, tiles from ntA on from tilesB (a second matrix of the same shape).
-template <int DT>
+// Tiles [0, ntA) come from `tiles`, tiles from ntA on from tilesB. GEN: generic loads (tiles may be
+// a copy in shared memory), else streaming global loads.
+template <int DT, bool GEN>
 __device__ void qmatvec(const uint8_t *tiles, const uint8_t *tilesB, int ntA, int k, int n_out, const Prep &p, float2 *scratch,
                         int scratch_pairs, float *y) {
     const int tid = threadIdx.x, nth = blockDim.x, nb = k / kQB, bb = block_bytes(DT);
@@ -229,7 +231,7 @@ __device__ void qmatvec(const uint8_t *tiles, const uint8_t *tilesB, int ntA, in
                 if (i + u * nth < items) {
                     const int ti = t0 + (qd >> 2);
                     const uint8_t *tile = ti < ntA ? tiles + (size_t)ti * tb : tilesB + (size_t)(ti - ntA) * tb;
-                    qload4<DT>(q[u], tile + (size_t)b * bb, qd & 3);
+                    qload4<DT, GEN>(q[u], tile + (size_t)b * bb, qd & 3);
                 }
                 qd += dq; b += db;
                 if (qd >= m4) { qd -= m4; b++; }
@@ -268,17 +270,20 @@ __device__ void qmatvec(const uint8_t *tiles, const uint8_t *tilesB, int ntA, in
 }
 
 // y = tiles[t0, t1) . x for one CTA, exact: y[o] for o in [0, 16 (t1 - t0)) (shared memory).
-// scratch holds scratch_pairs float2 (quantised dtypes; at least k/32).
+// scratch holds scratch_pairs float2 (quantised dtypes; at least k/32). staged, ns: a copy of tiles
+// [t0, t0 + ns) in shared memory (quantised dtypes), read instead of global memory.
 static __device__ __noinline__ void matvec_exact(int dtype, const uint8_t *tiles, int k, int t0, int t1, const Prep p, float2 *scratch,
-                                                 int scratch_pairs, float *y) {
+                                                 int scratch_pairs, float *y, const uint8_t *staged = nullptr, int ns = 0) {
     const int tid = threadIdx.x, nth = blockDim.x;
     if (t1 <= t0) return;
     const size_t tb = tile_bytes(dtype, k);
     const uint8_t *base = tiles + (size_t)t0 * tb;
     const int n = (t1 - t0) * kTile;
-    if (dtype == DT_Q8) { qmatvec<DT_Q8>(base, base, 1 << 30, k, n, p, scratch, scratch_pairs, y); return; }
-    if (dtype == DT_Q4) { qmatvec<DT_Q4>(base, base, 1 << 30, k, n, p, scratch, scratch_pairs, y); return; }
-    if (dtype == DT_MX) { qmatvec<DT_MX>(base, base, 1 << 30, k, n, p, scratch, scratch_pairs, y); return; }
+    const uint8_t *ta = ns > 0 ? staged : base, *tbb = ns > 0 ? base + (size_t)ns * tb : base;
+    const int nta = ns > 0 ? ns : 1 << 30;
+    if (dtype == DT_Q8) { qmatvec<DT_Q8, true>(ta, tbb, nta, k, n, p, scratch, scratch_pairs, y); return; }
+    if (dtype == DT_Q4) { qmatvec<DT_Q4, true>(ta, tbb, nta, k, n, p, scratch, scratch_pairs, y); return; }
+    if (dtype == DT_MX) { qmatvec<DT_MX, true>(ta, tbb, nta, k, n, p, scratch, scratch_pairs, y); return; }
     // f32 / bf16 (tiles [K][16] f32, [K/2][16][2] bf16): one thread per output walks its row in input
     // order, the reference's chain.
     const int split = fused_from(k);

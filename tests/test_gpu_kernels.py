@@ -142,6 +142,28 @@ def test_block_dots_and_unpack_exact(gpu, oracle, cuda, dtype):
             cuda.free()
 
 
+def test_f16_scales_every_bit_pattern(gpu, oracle, cuda):
+    """The device's binary16 -> binary32 scale conversion on all 65536 bit patterns (subnormals,
+    infinities and NaN payloads included), through the q8_0 unpack entry: equal to the oracle's."""
+    k, nb = 8192, 256
+    tb = gpu.l3m_tile_bytes(2, k)
+    ntiles = 65536 // (16 * nb)
+    tiles = np.random.default_rng(5).integers(0, 256, ntiles * tb, dtype=np.uint8)
+    h = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    for t in range(ntiles):
+        for b in range(nb):
+            o = t * tb + b * 544
+            tiles[o:o + 32] = h[(t * nb + b) * 16:(t * nb + b + 1) * 16].view(np.uint8)
+    dt = cuda.put(tiles)
+    dq, ds = cuda.empty(ntiles * 16 * k), cuda.empty(ntiles * 16 * nb * 4)
+    assert gpu.l3m_unpack_dev(2, dq, ds, dt, ntiles, k, None) == 0, gpu.l3m_cuda_error()
+    gs = cuda.get(ds, np.zeros(ntiles * 16 * nb, np.float32))
+    wq, ws = np.zeros(ntiles * 16 * k, np.int8), np.zeros(ntiles * 16 * nb, np.float32)
+    oracle.o_unpack(2, P(wq), P(ws), P(tiles), ntiles, k)
+    assert np.array_equal(gs.view(np.uint32), ws.view(np.uint32))
+    cuda.free()
+
+
 def test_device_prepare_exact(gpu, oracle, cuda):
     rng = np.random.default_rng(3)
     for dtype in (1, 2):
