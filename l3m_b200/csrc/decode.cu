@@ -99,9 +99,11 @@ __device__ __noinline__ void scatter(const float *src, float *dst, int g0, int n
     }
 }
 
+// Diagnostics: thread 0 of the traced CTAs stamps its SM cycle counter (clock64: a few cycles to
+// read, unlike the global timer) per (position, layer, event).
 __device__ __forceinline__ void trace(const DecodeArgs &a, int slot, int pos, int l, int ev) {
     if (a.trace && slot >= 0 && threadIdx.x == 0)
-        a.trace[(((size_t)slot * a.ctx + pos) * (a.n_layers + 1) + l) * kTraceEvents + ev] = globaltimer_ns();
+        a.trace[(((size_t)slot * a.ctx + pos) * (a.n_layers + 1) + l) * kTraceEvents + ev] = (unsigned long long)clock64();
 }
 
 // Pull a CTA's weight tiles into L2 ahead of use (cp.async.bulk.prefetch: no registers, no
@@ -113,8 +115,11 @@ __device__ __forceinline__ void prefetch_l2(const void *p, size_t bytes) {
     }
 }
 
+// Issued by thread 32 (warp 1), which is idle while warp 0 runs the serial part of the rmsnorm that
+// follows: a bulk instruction can hold its thread while the copy engine takes earlier requests.
+constexpr int kPrefetchThread = 32;
 __device__ void prefetch_layer(const DecodeArgs &a, const LayerDev &L, const Role &r) {
-    if (threadIdx.x != 0) return;
+    if (threadIdx.x != kPrefetchThread) return;
     const size_t tq = tile_bytes(L.dt_qkv, a.dim), to = tile_bytes(L.dt_wo, a.dim), tu = tile_bytes(L.dt_up, a.dim),
                  tg = tile_bytes(L.dt_gate, a.dim), td = tile_bytes(L.dt_down, a.ffn);
     if (r.qkv0 < r.qkv1) prefetch_l2(L.qkv + r.qkv0 * tq, (size_t)(r.qkv1 - r.qkv0) * tq);
@@ -143,7 +148,7 @@ __device__ void stage_vectors(const DecodeArgs &a, const LayerDev &L, const Role
 // completion counted in bytes on one mbarrier) while the current phase, its barrier and the next
 // norm run; the matvec then reads shared memory. One copy is outstanding at a time: the phase that
 // consumes it waits for it, and the next copy is issued only after that phase's last read.
-constexpr uint32_t kStageChunk = 32768;
+constexpr uint32_t kStageChunk = 1u << 20;   // every stage is one copy (at most the staging area)
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -159,14 +164,14 @@ __device__ __forceinline__ void stage_init(const Smem &s) {
 // (0 for f32/bf16, which are read from global memory). Same value in every thread.
 __device__ __forceinline__ int stage_count(int dtype, int k, int t0, int t1, int cap) {
     if (t1 <= t0 || !(dtype == DT_Q8 || dtype == DT_Q4 || dtype == DT_MX) || cap <= 0) return 0;
-    return (int)min((size_t)(t1 - t0), (size_t)cap / tile_bytes(dtype, k));
+    return min(t1 - t0, cap / (int)tile_bytes(dtype, k));
 }
 
 // Every thread, after a __syncthreads that ends every read of dst: start the copy of tiles
 // [t0, t0 + n) to dst (n = stage_count(...)); returns n.
-__device__ __noinline__ int stage_issue(const Smem &s, int dtype, const uint8_t *tiles, int k, int t0, int t1, uint8_t *dst, int cap) {
+__device__ __forceinline__ int stage_issue(const Smem &s, int dtype, const uint8_t *tiles, int k, int t0, int t1, uint8_t *dst, int cap) {
     const int n = stage_count(dtype, k, t0, t1, cap);
-    if (n > 0 && threadIdx.x == 0) {
+    if (n > 0 && threadIdx.x == kPrefetchThread) {
         const size_t tb = tile_bytes(dtype, k);
         const uint32_t bytes = (uint32_t)(n * tb), bar = smem_addr(s.wbar);
         const uint8_t *src = tiles + (size_t)t0 * tb;
@@ -183,7 +188,7 @@ __device__ __noinline__ int stage_issue(const Smem &s, int dtype, const uint8_t 
 // Every thread: wait for the outstanding copy (phase parity par of the mbarrier). Bounded by
 // timeout_ns; on timeout the abort word is set (the sampled position then stops the launch) and
 // the caller goes on with whatever the buffer holds.
-__device__ __noinline__ void stage_wait(const DecodeArgs &a, const Smem &s, uint32_t par) {
+__device__ __forceinline__ void stage_wait(const DecodeArgs &a, const Smem &s, uint32_t par) {
     const uint32_t bar = smem_addr(s.wbar);
     uint64_t t0 = 0;
     for (int spins = 0;; spins++) {
@@ -513,17 +518,15 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
         embed_row(a, tok, s.x);
         for (int l = 0; l < a.n_layers; l++) {
             const LayerDev &L = layers[l];
-            if (l + 1 < a.n_layers) prefetch_layer(a, layers[l + 1], role);
-            else {
-                prefetch_layer(a, layers[0], role);
-                if (last && role.voc0 < role.voc1 && tid == 0) {
+            cp_async_wait_all();                                          // this layer's norm weights and RoPE row
+            __syncthreads();
+            trace(a, tslot, pos, l, 0);
+            if (l + 1 == a.n_layers) {
+                if (last && role.voc0 < role.voc1 && tid == kPrefetchThread) {
                     const size_t th = tile_bytes(a.dt_head, a.dim);
                     prefetch_l2(a.head + role.voc0 * th, (size_t)(role.voc1 - role.voc0) * th);
                 }
             }
-            cp_async_wait_all();                                          // this layer's norm weights and RoPE row
-            __syncthreads();
-            trace(a, tslot, pos, l, 0);
             if (role.head0 >= 0)                                          // K/V copies land during Q
                 attend_prestage<true>(kcache(a, L, role.head0), vcache(a, L, role.head0), a.hd, a.vstride, pos, a.hd, s.kvbuf, s.vtbuf,
                                       a.attn_chunk);
