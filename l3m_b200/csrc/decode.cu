@@ -235,9 +235,25 @@ __device__ __noinline__ void embed_row(const DecodeArgs &a, int tok, float *x) {
 
 // Phase Q: this CTA's tiles of the q/k/v rows (biases added) -> s.y (the caller scatters into xq).
 // ns tiles staged at the staging area's offset w_extra (phase parity par).
+__device__ __forceinline__ const uint16_t *kcache(const DecodeArgs &a, const LayerDev &L, int h) {
+    return L.kc + (size_t)(h / a.hpk) * a.ctx * a.hd;
+}
+__device__ __forceinline__ const uint16_t *vcache(const DecodeArgs &a, const LayerDev &L, int h) {
+    return L.vc + (size_t)(h / a.hpk) * a.hd * a.vstride;
+}
+
+// A head CTA's warps 1.. start the K/V copies of its attention (attend_prestage) while warp 0 runs
+// the serial part of the rmsnorm.
 __device__ __noinline__ void phase_qkv(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s, int ns, uint32_t par, int pos,
                                        int l, int tslot) {
-    rmsnorm_exact(s.x, s.wa, a.dim, a.eps, s.xb, s.tmp, s.red);
+    if (role.head0 >= 0) {
+        const uint16_t *kc = kcache(a, L, role.head0), *vc = vcache(a, L, role.head0);
+        rmsnorm_side(s.x, s.wa, a.dim, a.eps, s.xb, s.red, [&](int t, int nt) {
+            attend_prestage<true>(kc, vc, a.hd, a.vstride, pos, a.hd, s.kvbuf, s.vtbuf, a.attn_chunk, t, nt);
+        });
+    } else {
+        rmsnorm_exact(s.x, s.wa, a.dim, a.eps, s.xb, s.tmp, s.red);
+    }
     trace(a, tslot, pos, l, 16);
     prepare(L.dt_qkv, s.xb, a.dim, s.prep);
     trace(a, tslot, pos, l, 17);
@@ -253,13 +269,6 @@ __device__ __noinline__ void phase_qkv(const DecodeArgs &a, const LayerDev &L, c
         }
         __syncthreads();
     }
-}
-
-__device__ __forceinline__ const uint16_t *kcache(const DecodeArgs &a, const LayerDev &L, int h) {
-    return L.kc + (size_t)(h / a.hpk) * a.ctx * a.hd;
-}
-__device__ __forceinline__ const uint16_t *vcache(const DecodeArgs &a, const LayerDev &L, int h) {
-    return L.vc + (size_t)(h / a.hpk) * a.hd * a.vstride;
 }
 
 // Phase A for query head h at position pos (xq complete): RoPE, this position's K/V row (stored by
@@ -527,7 +536,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
                     prefetch_l2(a.head + role.voc0 * th, (size_t)(role.voc1 - role.voc0) * th);
                 }
             }
-            if (role.head0 >= 0)                                          // K/V copies land during Q
+            if (role.head0 >= 0 && role.qkv0 >= role.qkv1)               // K/V copies land during Q (else started by phase_qkv)
                 attend_prestage<true>(kcache(a, L, role.head0), vcache(a, L, role.head0), a.hd, a.vstride, pos, a.hd, s.kvbuf, s.vtbuf,
                                       a.attn_chunk);
             // Each phase: its matvec, the copy of the next phase's tiles (the staging area is free from

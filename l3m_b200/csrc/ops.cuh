@@ -355,9 +355,11 @@ __device__ __forceinline__ float chain_sum(const float *v, int n, float acc) {
 // float. The sum of squares is the reference's sequential chain, run by thread 0 from registers while
 // the other threads fetch w.
 constexpr int kNormPerThread = 8;
-static __device__ __noinline__ void rmsnorm_exact(const float *x, const float *w, int n, float eps, float *y, float *tmp, float *red) {
+struct NoSide { __device__ void operator()(int, int) const {} };
+// side(t, nt): work for threads 32.. (t = threadIdx.x - 32 of nt) while thread 0 runs the chain.
+template <class Side>
+__device__ __forceinline__ void rmsnorm_side(const float *x, const float *w, int n, float eps, float *y, float *red, const Side &side) {
     const int tid = threadIdx.x, nth = blockDim.x;
-    (void)tmp;
     float wr[kNormPerThread];
 #pragma unroll
     for (int j = 0; j < kNormPerThread; j++) wr[j] = tid + j * nth < n ? w[tid + j * nth] : 0.0f;
@@ -366,6 +368,8 @@ static __device__ __noinline__ void rmsnorm_exact(const float *x, const float *w
         float ss = chain_sum<true>(x, split, 0.0f);
         for (int i = split; i < n; i++) ss = __fmaf_rn(x[i], x[i], ss);
         *red = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
+    } else if (tid >= 32) {
+        side(tid - 32, nth - 32);
     }
     __syncthreads();
     const float sc = *red;
@@ -374,6 +378,11 @@ static __device__ __noinline__ void rmsnorm_exact(const float *x, const float *w
         if (tid + j * nth < n) y[tid + j * nth] = __fmul_rn(__fmul_rn(x[tid + j * nth], sc), wr[j]);
     for (int i = tid + kNormPerThread * nth; i < n; i += nth) y[i] = __fmul_rn(__fmul_rn(x[i], sc), w[i]);
     __syncthreads();
+}
+
+static __device__ __noinline__ void rmsnorm_exact(const float *x, const float *w, int n, float eps, float *y, float *tmp, float *red) {
+    (void)tmp;
+    rmsnorm_side(x, w, n, eps, y, red, NoSide());
 }
 
 // ---- RoPE on one head in place (reference src/ops.c:29-40): cs[i] = {cos, sin} of pair i at this position.
@@ -412,11 +421,14 @@ __host__ __device__ constexpr int attn_vt_stride(int chunk) { return ((chunk + 1
 
 // Start the copies of everything attention at pos reads that exists before row pos: K rows
 // [0, min(chunk, pos)) and, with VT, V positions [0, min(chunk, pos + 1)) (position pos itself is
-// patched later). Needs nothing of this position, so it can run before q, k and v are known.
+// patched later). Needs nothing of this position, so it can run before q, k and v are known. Run
+// by threads tid of nth (every thread of the CTA by default, or a subset); each thread waits for its
+// own copies (cp_async_wait_all) before the barrier that precedes reading them.
 template <bool VT>
 __device__ __noinline__ void attend_prestage(const uint16_t *kc, const uint16_t *vc, int kstride, int vstride, int pos, int hd,
-                                             uint16_t *kvbuf, uint16_t *vtbuf, int chunk) {
-    const int tid = threadIdx.x, nth = blockDim.x, rs = hd + 8, h8 = hd / 8, vs = attn_vt_stride(chunk);
+                                             uint16_t *kvbuf, uint16_t *vtbuf, int chunk, int tid = -1, int nth = 0) {
+    if (tid < 0) { tid = threadIdx.x; nth = blockDim.x; }
+    const int rs = hd + 8, h8 = hd / 8, vs = attn_vt_stride(chunk);
     const bool kvec = kstride % 8 == 0 && ((uintptr_t)kc & 15) == 0;
     const bool vvec = vstride % 8 == 0 && ((uintptr_t)vc & 15) == 0;
     const int nk = min(chunk, pos);
