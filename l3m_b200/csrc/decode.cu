@@ -198,7 +198,7 @@ __device__ __forceinline__ void stage_wait(const DecodeArgs &a, const Smem &s, u
         if (done) return;
         if (spins == 0) t0 = globaltimer_ns();
         else if ((spins & 63) == 0 && globaltimer_ns() - t0 > a.hx.timeout_ns) {
-            atomicCAS(a.hx.abort_flag, 0, kErrTimeout);
+            atomicCAS(a.hx.abort_flag, 0, kErrStageTimeout);
             return;
         }
     }
@@ -444,6 +444,9 @@ __device__ __noinline__ void head_logits(const DecodeArgs &a, const Role &role, 
             if (v > m || (v == m && vi >= 0 && (mi < 0 || vi < mi))) { m = v; mi = vi; }
         }
         if (mi < 0) mi = role.voc0 * kTile;                                   // an empty or all-NaN slice
+        s.tmp[0] = m;                                                         // also kept here for a one-cluster launch
+        s.tmp[1] = __int_as_float(mi);
+        s.tmp[2] = __int_as_float(host_stop);
         a.hx.slots[3 * cta] = m;
         a.hx.slots[3 * cta + 1] = __int_as_float(mi);
         a.hx.slots[3 * cta + 2] = __int_as_float(host_stop);
@@ -594,7 +597,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
         if (!last) continue;                                              // the next position starts from its embedding
         ++tcount;
         // Publish x to every CTA of the launch (cluster 0's copies are identical), then this CTA's tiles.
-        if (cta == 0) {
+        if (cta == 0 && a.grid > kClusterCtas) {
             for (int i = tid; i < a.dim; i += blockDim.x) a.hx.x[i] = s.x[i];
             if (tid == 0) a.hx.x[a.dim] = __int_as_float(pos);
             __syncthreads();
@@ -605,10 +608,16 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
         if (cta == 0 && tid == 0) host_stop = ld_relaxed_sys_i32((const int *)&a.ctrl->stop_request);
         head_logits(a, role, s, pos, host_stop, tslot);
         trace(a, tslot, pos, a.n_layers, 1);
-        // CTA 0 waits for every CTA's (max, index) (so every slice of the logits is written, also when
-        // nothing is sampled), reduces them in CTA order (vocabulary order, reference
+        // One cluster: every CTA sends (max, index, host stop, no abort seen) to every CTA's xt[4 + 4 cta],
+        // and after the barrier each reduces the same 16 slots in CTA order. Several clusters: CTA 0
+        // waits for every CTA's (max, index) in global memory (so every slice of the logits is written,
+        // also when nothing is sampled), reduces them in CTA order (vocabulary order, reference
         // engine.c:299-300) and hands the result to cluster 0, so all 16 decide alike.
-        if (cta == 0) {
+        if (a.grid == kClusterCtas) {
+            if (tid == 0) s.tmp[3] = __int_as_float(*(volatile int *)a.hx.abort_flag == 0 ? 1 : 0);
+            __syncthreads();
+            scatter(s.tmp, s.xt, 4 + 4 * cta, 4);
+        } else if (cta == 0) {
             const int r = wait_word(a, a.hx.count, tcount * (uint32_t)a.grid, false);
             float *sl = s.tmp + 4;                                        // every slot at once, then a serial scan
             for (int i = tid; i < 3 * a.grid; i += blockDim.x) sl[i] = ld_cg_f32(a.hx.slots + i);
@@ -628,6 +637,18 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
             scatter(s.tmp, s.xt, 0, 4);
         }
         cluster_sync();                                                   // 6: the sampled token
+        if (a.grid == kClusterCtas) {
+            float gmax = -INFINITY;
+            int nx = 0, all = 1;
+            for (int c = 0; c < kClusterCtas; c++) {
+                const float *sl = s.xt + 4 + 4 * c;
+                if (sl[0] > gmax) { gmax = sl[0]; nx = __float_as_int(sl[1]); }
+                all &= __float_as_int(sl[3]);
+            }
+            __syncthreads();                                              // every thread has read the slots
+            if (tid == 0) { s.xt[0] = __int_as_float(nx); s.xt[1] = s.xt[4 + 2]; s.xt[2] = __int_as_float(all); }
+            __syncthreads();
+        }
         const int next = __float_as_int(s.xt[0]), stop_req = __float_as_int(s.xt[1]);
         if (!__float_as_int(s.xt[2])) { ok = false; break; }
         trace(a, tslot, pos, a.n_layers, 2);

@@ -47,7 +47,7 @@ struct HeadX {
     unsigned long long timeout_ns;
 };
 constexpr uint32_t kHeadDone = 0xFFFFFFFFu;
-enum { kErrNone = 0, kErrTimeout = 1 };
+enum { kErrNone = 0, kErrTimeout = 1, kErrStageTimeout = 2 };   // a wait on another CTA; a wait on a weight copy
 
 struct DecodeArgs {
     int dim, hd, ffn, vocab, ctx, n_heads, n_kv, hpk, n_layers, n_qkv, grid;   // n_qkv = (n_heads + 2 n_kv) hd; grid: all CTAs
@@ -74,7 +74,8 @@ struct DecodeArgs {
     int sm_x, sm_xb, sm_tmp, sm_q8, sm_scale, sm_sum, sm_xf, sm_y, sm_scores, sm_kv, sm_att, sm_red, sm_kvbuf, sm_vt, sm_scratch;
     int sm_wa, sm_wf, sm_wh, sm_rope;   // this layer's norm weights, the final norm, this position's RoPE row
     int sm_layers;                      // a copy of layers[0 .. n_layers)
-    int sm_xq, sm_xa, sm_xp, sm_xh, sm_xd, sm_xt;   // exchanged vectors: qkv, attn, proj, h, down, (max, index, stop) per CTA
+    int sm_xq, sm_xa, sm_xp, sm_xh, sm_xd, sm_xt;   // exchanged vectors: qkv, attn, proj, h, down; xt: the sampled token
+                                                    // (next, stop, ok) and, one-cluster launch, each CTA c's slot at 4 + 4c
     // Weight staging area (quantised tiles of the next matvec phase, copied in by cp.async.bulk):
     // sm_w .. sm_w + w_bytes; its first w_extra bytes overlap the attention buffers (kvbuf, vt), so
     // the phases around attention (qkv, wo) use only [w_extra, w_bytes). sm_wbar: its mbarrier.

@@ -201,6 +201,9 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     const int G = l3m::kClusterCtas, dim = m->dim, hd = m->hd, ffn = m->ffn, V = m->vocab, L = m->n_layers;
     if (g.sms < G) { fprintf(stderr, "l3m: GPU %d has %d SMs; the decode cluster needs %d\n", g.dev, g.sms, G); return false; }
     int GT = g.sms / G * G;
+    // L3M_CLUSTERS=n caps the launch at n clusters (1: the head runs on cluster 0 alone, with no
+    // cross-cluster waits; for profilers that do not keep every cluster of a launch resident).
+    if (const char *nc = getenv("L3M_CLUSTERS")) GT = std::max(G, std::min(GT, atoi(nc) * G));
     if (hd > l3m::kDecodeThreads) { fprintf(stderr, "l3m: head_dim %d above %d is not built\n", hd, l3m::kDecodeThreads); return false; }
 
     // Streamed weights first (one contiguous range for the persisting window), then the rest.
@@ -384,7 +387,7 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     a.sm_xp = take(dim * 4);
     a.sm_xh = take(ffn * 4);
     a.sm_xd = take(dim * 4);
-    a.sm_xt = take(4 * G * 4);
+    a.sm_xt = take((4 + 4 * G) * 4);
     a.sm_wbar = take(16);
     // Scratch: the (scale product, dot) pairs of the largest per-CTA phase of a layer, so each runs in
     // one pass (the head runs in several).
@@ -617,7 +620,9 @@ L3M_API int l3m_generate(l3m_model *m, const int32_t *prompt, int n_prompt, int 
         std::vector<unsigned long long> t(g.trace_bytes / 8);
         cudaMemcpy(t.data(), g.trace, g.trace_bytes, cudaMemcpyDeviceToHost);
         if (FILE *tf = fopen(getenv("L3M_TRACE"), "wb")) {
-            int hdr[8] = {m->ctx, m->n_layers, n_prompt, last_pos, g.args.trace_cta[0], g.args.trace_cta[1], l3m::kTraceEvents, 0};
+            int khz = 0;                                                 // the stamps are SM cycles; the header carries the clock
+            cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, g.dev);
+            int hdr[8] = {m->ctx, m->n_layers, n_prompt, last_pos, g.args.trace_cta[0], g.args.trace_cta[1], l3m::kTraceEvents, khz};
             fwrite(hdr, sizeof hdr, 1, tf);
             fwrite(t.data(), 8, t.size(), tf);
             fclose(tf);

@@ -1,0 +1,79 @@
+"""Per-phase timing of the decode kernel, from the cycle stamps it writes when L3M_TRACE is set.
+
+    python -m l3m_b200.trace [--config SmolLM2-135M-q8_0] [--out /tmp/l3m_trace.bin]
+
+Runs one greedy generation (the bench workload: the config's context, a 4-token prompt, the rest
+generated) of a synthetic model through ``l3m_b200.Model`` with tracing on, then prints for the two
+traced CTAs (the first and the last of cluster 0) the median time, over layers and over the
+positions from 50 on, of every traced event after the layer's start, then the layer and token
+periods and the head phase. Times are SM cycles converted at the clock the header records (the
+maximum SM clock; the bench's clock samples show the part runs there under this load).
+"""
+import argparse
+import os
+import sys
+
+import numpy as np
+
+# Event ids as stamped in csrc/decode.cu (per position and layer; the head uses layer index n_layers).
+LAYER_EVENTS = {
+    16: "Q   rmsnorm (head CTAs: K/V copies issued meanwhile)", 17: "Q   prepare", 18: "Q   weight copy waited", 19: "Q   matvec",
+    27: "Q   next copy issued", 1: "Q   exchanged", 2: "    barrier 1",
+    14: "A   RoPE + K/V row", 15: "A   attention", 3: "A   exchanged", 4: "    barrier 2",
+    20: "B   prepare", 21: "B   weight copy waited", 22: "B   matvec", 28: "B   next copy issued", 5: "B   exchanged", 6: "    barrier 3",
+    7: "C   x += proj, rmsnorm", 26: "C   prepare", 12: "C   weight copy waited", 13: "C   up/gate matvec", 29: "C   next copy issued",
+    8: "C   SiLU gate exchanged", 9: "    barrier 4",
+    23: "D   prepare", 24: "D   weight copy waited", 25: "D   matvec", 30: "D   next copy issued", 10: "D   exchanged",
+    11: "    barrier 5, x += down (layer end)",
+}
+HEAD_EVENTS = {3: "rmsnorm", 4: "prepare", 5: "matvec", 1: "argmax slots", 2: "token agreed"}
+
+
+def summarize(path, first=50):
+    raw = open(path, "rb").read()
+    hdr = np.frombuffer(raw[:32], np.int32)
+    ctx, L, _, last, cta0, cta1, E, khz = (int(v) for v in hdr)
+    t = np.frombuffer(raw[32:], np.uint64).reshape(2, ctx, L + 1, E).astype(np.float64) / (khz / 1e6)   # ns
+    lines = [f"clock {khz / 1000:.0f} MHz; positions {first}..{last - 1}; medians in ns after the layer start"]
+    for slot, cta in enumerate((cta0, cta1)):
+        tt = t[slot, first:last]
+        lines.append(f"-- CTA {cta}")
+        rows = []
+        for ev, name in LAYER_EVENTS.items():
+            ok = (tt[:, :L, ev] > 0) & (tt[:, :L, 0] > 0)
+            if ok.any():
+                rows.append((np.median((tt[:, :L, ev] - tt[:, :L, 0])[ok]), name))
+        for v, name in sorted(rows):
+            lines.append(f"   {v:8.0f}  {name}")
+        lay = tt[:, 1:L, 0] - tt[:, :L - 1, 0]
+        tok = np.diff(tt[:, 0, 0])
+        lines.append(f"   layer period {np.median(lay):.0f} ns, token period {np.median(tok):.0f} ns")
+        h = tt[:, L]
+        parts = [f"{HEAD_EVENTS[e]} {np.median(h[:, e] - h[:, p]):.0f}" for p, e in ((0, 3), (3, 4), (4, 5), (5, 1), (1, 2))]
+        lines.append("   head (ns): " + ", ".join(parts))
+    return "\n".join(lines)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--config", default="SmolLM2-135M-q8_0")
+    ap.add_argument("--out", default="/tmp/l3m_trace.bin")
+    ap.add_argument("--models", default="/tmp/l3m_bench")
+    a = ap.parse_args()
+    os.environ["L3M_TRACE"] = a.out
+    import l3m_b200
+    from l3m_b200 import synth
+    _, _, _, ctx = synth.CONFIGS[a.config]
+    path = synth.make(a.config, a.models)
+    m = l3m_b200.Model(str(path), ctx=ctx, force=True)
+    prompt = synth.prompt(4, seed=1, vocab=32000)
+    for _ in range(2):                                   # the second run is the one summarized
+        m.generate(prompt, ctx - len(prompt), temperature=0)
+    p = m.perf()
+    print(f"{a.config}: {1e9 / p['ns_compute']:.1f} tok/s (device), {1e9 / p['ns_token']:.1f} tok/s (wall)")
+    print(summarize(a.out))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
