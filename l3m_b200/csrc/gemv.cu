@@ -8,7 +8,9 @@
 // reference rounds in). Fast table, f32/bf16: the chain is split over K across a warp and reduced
 // with shuffles (reassociated, like the reference's AVX tables; tolerance-checked).
 #include <cuda_runtime.h>
+#include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include "ops.cuh"
@@ -71,6 +73,168 @@ __global__ void __launch_bounds__(kThreads) gemv_exact_kernel(int dtype, float *
     float *ys = (float *)(scratch + kScratchPairs);                    // this CTA's outputs, then to global
     matvec_exact(dtype, tiles, k, t0, t1, p, scratch, kScratchPairs, ys);
     for (int o = threadIdx.x; o < (t1 - t0) * kTile; o += blockDim.x) y[(size_t)t0 * kTile + o] = ys[o];
+}
+
+// ---- Streamed exact matvec (q8_0, q4_0, mxfp4, bf16 with k a multiple of 32).
+// One CTA per SM takes a contiguous run of tiles [t0, t1) and handles it in waves of G tiles; a wave
+// reads its tiles' 32-input blocks in order, U blocks per chunk, through a ring of kStreamStages
+// shared-memory buffers. A producer warp starts each chunk with one cp.async.bulk per tile (global ->
+// this CTA's shared memory, no multicast; bytes complete on the buffer's "full" mbarrier) once the 8
+// compute warps have each arrived on the buffer's "empty" mbarrier for its previous chunk, so the
+// compute warps never wait for one another inside a wave. Quantised dtypes: each (4 outputs x 1
+// block) item leaves {RN(sx*d), (float)dot} in the wave's scratch; at the end of the wave one thread
+// per output runs acc = fma(RN(sx*d), dot, acc) over all blocks in order. bf16: each output's thread
+// runs the input-order chain straight from the staged words, its accumulator kept across chunks. So
+// the rounding sequence is the scalar kernel's (src/kernels_scalar.c:19-75), as in gemv_exact_kernel.
+constexpr int kStreamWarps = 8;                     // compute warps; warp 8 produces
+constexpr int kStreamThreads = 32 * (kStreamWarps + 1);
+constexpr int kStreamStages = 4;
+constexpr int kStreamChunk = 32768;                 // target weight bytes per chunk
+constexpr int kStreamScratch = 48 * 1024;           // bytes of per-wave (scale product, dot) pairs
+
+struct StreamPlan { int G, U, piece, stage_bytes, scratch_pairs; };
+
+__host__ __device__ inline int stream_unit_bytes(int dtype) { return dtype == DT_BF16 ? 1024 : block_bytes(dtype); }
+
+// tiles_per_cta: the largest run a CTA gets. G: a power of two <= 16 that fits the run (and, for the
+// quantised dtypes, whose pairs fit the scratch); U: blocks per chunk so that a chunk is about
+// kStreamChunk bytes; piece: a tile's share of a stage buffer, padded by 64 bytes so that
+// consecutive tiles start in different bank halves. G = 0: the shape does not fit this kernel.
+StreamPlan stream_plan(int dtype, int k, int tiles_per_cta) {
+    StreamPlan pl;
+    const int bb = stream_unit_bytes(dtype), nb = k / kQB;
+    const long long pair_bytes_per_tile = (long long)nb * kTile * sizeof(float2);
+    pl.G = 1;
+    while (pl.G < 16 && 2 * pl.G <= tiles_per_cta && (dtype == DT_BF16 || 2 * pl.G * pair_bytes_per_tile <= kStreamScratch)) pl.G *= 2;
+    if (dtype != DT_BF16 && pair_bytes_per_tile > kStreamScratch) pl.G = 0;
+    const int g = pl.G ? pl.G : 1;
+    pl.U = std::max(1, std::min(nb, kStreamChunk / (g * bb)));
+    pl.piece = pl.U * bb + 64;
+    pl.stage_bytes = g * pl.piece;
+    pl.scratch_pairs = dtype == DT_BF16 ? 0 : g * nb * kTile;
+    return pl;
+}
+
+size_t stream_smem(int k, const StreamPlan &pl) {
+    return ((prep_smem(k) + 127) & ~(size_t)127) + (size_t)kStreamStages * pl.stage_bytes + (size_t)pl.scratch_pairs * sizeof(float2);
+}
+
+__device__ int g_stream_timeouts;                   // diagnostics: waits that gave up (never expected)
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// Wait for phase parity `par` of the mbarrier at shared address bar (time-limited: 2 s).
+__device__ __forceinline__ void mbar_wait(uint32_t bar, uint32_t par) {
+    uint64_t start = 0;
+    for (int spin = 0;; spin++) {
+        uint32_t done;
+        asm volatile("{\n\t.reg .pred q;\n\tmbarrier.try_wait.parity.shared::cta.b64 q, [%1], %2;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+                     : "=r"(done) : "r"(bar), "r"(par) : "memory");
+        if (done) return;
+        if (spin == 0) start = globaltimer_ns();
+        else if ((spin & 63) == 0 && globaltimer_ns() - start > 2000000000ull) { atomicAdd(&g_stream_timeouts, 1); return; }
+    }
+}
+
+template <int DT>
+__global__ void __launch_bounds__(kStreamThreads, 1) gemv_stream_kernel(float *y, const uint8_t *tiles, int ntiles, int k, VecArg x,
+                                                                         StreamPlan pl) {
+    extern __shared__ __align__(16) unsigned char smem_stream[];
+    __shared__ __align__(8) unsigned long long full[kStreamStages], empty[kStreamStages];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int bb = stream_unit_bytes(DT), nb = k / kQB;
+    const size_t tb = (size_t)nb * bb;
+    Prep p = carve_prep(smem_stream, k);
+    unsigned char *stage0 = smem_stream + ((prep_smem(k) + 127) & ~(size_t)127);   // 16-byte aligned (bulk copy destinations)
+    float2 *scratch = (float2 *)(stage0 + (size_t)kStreamStages * pl.stage_bytes);
+    const int t0 = (int)((long long)blockIdx.x * ntiles / gridDim.x), t1 = (int)((long long)(blockIdx.x + 1) * ntiles / gridDim.x);
+    const int nch = (nb + pl.U - 1) / pl.U, total = (t1 - t0 + pl.G - 1) / pl.G * nch;
+    if (tid == 0) {
+        for (int i = 0; i < kStreamStages; i++) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&full[i])) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&empty[i])), "r"(kStreamWarps) : "memory");
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    load_prep(DT, x, k, p);                                                // every thread; ends with __syncthreads
+    if (warp == kStreamWarps) {                                            // the producer
+        for (int c = 0; c < total; c++) {
+            const int st = c % kStreamStages;
+            if (c >= kStreamStages) mbar_wait(smem_u32(&empty[st]), (uint32_t)(c / kStreamStages + 1) & 1u);
+            const int g0 = t0 + c / nch * pl.G, ng = min(pl.G, t1 - g0), b0 = c % nch * pl.U, nu = min(pl.U, nb - b0);
+            unsigned char *buf = stage0 + (size_t)st * pl.stage_bytes;
+            const uint32_t bar = smem_u32(&full[st]);
+            if (lane == 0) asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"((uint32_t)(ng * nu * bb)) : "memory");
+            __syncwarp();
+            for (int g = lane; g < ng; g += 32)
+                asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                             ::"r"(smem_u32(buf + (size_t)g * pl.piece)), "l"(tiles + (size_t)(g0 + g) * tb + (size_t)b0 * bb),
+                             "r"((uint32_t)(nu * bb)), "r"(bar) : "memory");
+        }
+        return;                                                            // every chunk it started is waited for by the compute warps
+    }
+    const uint32_t *xw = (const uint32_t *)p.q8;
+    float acc = 0.0f;
+    for (int c = 0; c < total; c++) {
+        const int st = c % kStreamStages, g0 = t0 + c / nch * pl.G, ng = min(pl.G, t1 - g0), cb = c % nch, b0 = cb * pl.U,
+                  nu = min(pl.U, nb - b0);
+        const unsigned char *buf = stage0 + (size_t)st * pl.stage_bytes;
+        mbar_wait(smem_u32(&full[st]), (uint32_t)(c / kStreamStages) & 1u);
+        if (DT == DT_BF16) {
+            if (tid < ng * kTile) {                                         // output (tile g, row r): its chain over the chunk's inputs
+                const int g = tid >> 4, r = tid & 15;
+                const uint32_t *w = (const uint32_t *)(buf + (size_t)g * pl.piece) + r;
+                const float *xf = p.xf + (size_t)b0 * kQB;
+                for (int q = 0; q < nu * 16; q += 8) {
+                    uint32_t v[8];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) v[j] = w[(q + j) * kTile];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        acc = __fmaf_rn(l3m_bits_f32(v[j] << 16), xf[2 * (q + j)], acc);
+                        acc = __fmaf_rn(l3m_bits_f32(v[j] & 0xFFFF0000u), xf[2 * (q + j) + 1], acc);
+                    }
+                }
+            }
+        } else {
+            const int per_u = ng * 4, items = per_u * nu;
+            for (int i = tid; i < items; i += 32 * kStreamWarps) {
+                const int u = i / per_u, rem = i - u * per_u, g = rem >> 2, r4 = rem & 3, b = b0 + u;
+                QLoad4 q;
+                qload4<DT, true>(q, buf + (size_t)g * pl.piece + (size_t)u * bb, r4);
+                const uint4 x0 = *(const uint4 *)(xw + 8 * b), x1 = *(const uint4 *)(xw + 8 * b + 4);
+                const uint32_t xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                const float sx = p.scale[b];
+                const int32_t xs = p.sum[b];
+                float4 r0, r1;
+                r0.x = __fmul_rn(sx, qscale4<DT>(q.d, 0)); r0.y = __int2float_rn(qdot4<DT>(q, 0, xv, xs));
+                r0.z = __fmul_rn(sx, qscale4<DT>(q.d, 1)); r0.w = __int2float_rn(qdot4<DT>(q, 1, xv, xs));
+                r1.x = __fmul_rn(sx, qscale4<DT>(q.d, 2)); r1.y = __int2float_rn(qdot4<DT>(q, 2, xv, xs));
+                r1.z = __fmul_rn(sx, qscale4<DT>(q.d, 3)); r1.w = __int2float_rn(qdot4<DT>(q, 3, xv, xs));
+                float4 *dst = (float4 *)(scratch + (size_t)b * pl.G * kTile + g * kTile + 4 * r4);
+                dst[0] = r0;
+                dst[1] = r1;
+            }
+        }
+        __syncwarp();                                                       // this warp is done with the stage buffer
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&empty[st])) : "memory");
+        if (cb == nch - 1) {                                                // the wave's last blocks
+            if (DT != DT_BF16) {
+                asm volatile("bar.sync 1, %0;" ::"n"(32 * kStreamWarps) : "memory");   // every pair of the wave written
+                if (tid < ng * kTile) {
+                    const float2 *r = scratch + tid;
+#pragma unroll 8
+                    for (int b = 0; b < nb; b++) {
+                        const float2 v = r[(size_t)b * pl.G * kTile];
+                        acc = __fmaf_rn(v.x, v.y, acc);
+                    }
+                }
+                asm volatile("bar.sync 1, %0;" ::"n"(32 * kStreamWarps) : "memory");   // read before the next wave writes
+            }
+            if (tid < ng * kTile) y[(size_t)(g0 + (tid >> 4)) * kTile + (tid & 15)] = acc;
+            acc = 0.0f;
+        }
+    }
 }
 
 // Fast f32/bf16: one warp per tile; each half warp walks alternate 16-input chunks for its 16 outputs.
@@ -183,6 +347,27 @@ __global__ void __launch_bounds__(kThreads) attend_kernel(float *out, const floa
 
 VecArg vec_arg(const l3m_vec *x) { return VecArg{x->f32, x->bf16, x->q8, x->scale, x->sum}; }
 
+int stream_sms() {
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (sms <= 0) sms = 148;
+    }
+    return sms;
+}
+
+size_t smem_optin() {
+    static int v = 0;
+    if (!v) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    }
+    return (size_t)v;
+}
+
 int grid_for(int ntiles) {
     static int sms = 0;
     if (!sms) {
@@ -235,8 +420,34 @@ L3M_API int l3m_gemv_dev(int exact, int dtype, float *y, const void *tiles, int 
     if (dtype == DT_BF16 && k % 2) return fail_msg("l3m_gemv_dev: bf16 k must be even");
     if (ntiles == 0) return 0;
     cudaStream_t s = (cudaStream_t)stream;
+    static const bool stream_off = getenv("L3M_GEMV_STREAM") && !strcmp(getenv("L3M_GEMV_STREAM"), "0");
     if (!exact && dtype <= DT_BF16) {
         gemv_fast_kernel<<<grid_for((ntiles + 15) / 16), kThreads, 0, s>>>(dtype, y, (const uint8_t *)tiles, ntiles, k, vec_arg(x));
+    } else if (!stream_off && dtype >= DT_BF16 && k % kQB == 0 && ((uintptr_t)tiles & 15) == 0 && stream_plan(dtype, k, 16).G &&
+               stream_smem(k, stream_plan(dtype, k, 16)) + 1024 <= smem_optin()) {
+        const int grid = std::min(ntiles, stream_sms());
+        const StreamPlan pl = stream_plan(dtype, k, (ntiles + grid - 1) / grid);
+        const size_t smem = stream_smem(k, pl);
+        cudaError_t e = cudaSuccess;
+        const uint8_t *t = (const uint8_t *)tiles;
+        switch (dtype) {
+        case DT_BF16:
+            e = cudaFuncSetAttribute(gemv_stream_kernel<DT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e == cudaSuccess) gemv_stream_kernel<DT_BF16><<<grid, kStreamThreads, smem, s>>>(y, t, ntiles, k, vec_arg(x), pl);
+            break;
+        case DT_Q8:
+            e = cudaFuncSetAttribute(gemv_stream_kernel<DT_Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e == cudaSuccess) gemv_stream_kernel<DT_Q8><<<grid, kStreamThreads, smem, s>>>(y, t, ntiles, k, vec_arg(x), pl);
+            break;
+        case DT_Q4:
+            e = cudaFuncSetAttribute(gemv_stream_kernel<DT_Q4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e == cudaSuccess) gemv_stream_kernel<DT_Q4><<<grid, kStreamThreads, smem, s>>>(y, t, ntiles, k, vec_arg(x), pl);
+            break;
+        default:
+            e = cudaFuncSetAttribute(gemv_stream_kernel<DT_MX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e == cudaSuccess) gemv_stream_kernel<DT_MX><<<grid, kStreamThreads, smem, s>>>(y, t, ntiles, k, vec_arg(x), pl);
+        }
+        if (e != cudaSuccess) return fail(e, "l3m_gemv_dev");
     } else {
         const int per_cta = (ntiles + grid_for(ntiles) - 1) / grid_for(ntiles);
         size_t smem = prep_smem(k) + (size_t)kScratchPairs * sizeof(float2) + (size_t)per_cta * kTile * 4;

@@ -8,7 +8,8 @@ tile layout with the sweep's value distributions: q8_0 int8 uniform in [-127, 12
 |N(0,1)|*0.01; q4_0 nibbles uniform in [0, 15] (value - 8) with the same scales; mxfp4 e2m1 codes
 uniform with e8m0 scales uniform in [118, 130]; bf16 weights N(0, 0.02). x ~ N(0,1) is prepared on
 the device (l3m_vec_prepare_dev). Each case runs l3m_gemv_dev (the C ABI, device pointers) in two
-regimes, timed with CUDA events on the launching stream over `iters` launches after a warm-up:
+regimes; `iters` launches are captured into a CUDA graph, which is replayed once warm and once
+timed with CUDA events (so the GPU time per launch is measured, not the host's launch rate):
 
   hbm  R copies of the matrix, at least 2.5x the L2 in total, used round robin: every launch reads
        its tiles from HBM;
@@ -99,19 +100,29 @@ def run(dtypes, shapes, iters, exact, out):
             y = torch.empty(m, dtype=torch.float32, device="cuda")
             base = buf.data_ptr()
             for regime in ("hbm", "l2"):
-                def launch(i):
+                def launch(i, st):
                     p = base + (i % reps) * stride if regime == "hbm" else base
-                    if L.l3m_gemv_dev(exact, dt, C.c_void_p(y.data_ptr()), C.c_void_p(p), m // 16, k, C.byref(v), sp):
+                    if L.l3m_gemv_dev(exact, dt, C.c_void_p(y.data_ptr()), C.c_void_p(p), m // 16, k, C.byref(v), st):
                         raise RuntimeError(L.l3m_cuda_error().decode())
                 for i in range(min(20, reps) if regime == "hbm" else 20):
-                    launch(i)
+                    launch(i, sp)
+                torch.cuda.synchronize()
+                # The launches are captured into a CUDA graph and replayed, so the GPU runs them back to
+                # back (a Python loop of single launches cannot issue faster than about one per 6 us).
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, capture_error_mode="relaxed"):
+                    cs = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+                    for i in range(iters):
+                        launch(i, cs)
+                g.replay()
+                torch.cuda.synchronize()
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
-                for i in range(iters):
-                    launch(i)
+                g.replay()
                 e1.record(stream)
                 torch.cuda.synchronize()
                 us = e0.elapsed_time(e1) * 1e3 / iters
+                del g
                 gbs = nbytes / (us * 1e-6) / 1e9
                 row = {"dtype": name, "m": m, "k": k, "regime": regime, "table": "exact" if exact else "fast",
                        "bytes": nbytes, "us_per_launch": round(us, 3), "gbs": round(gbs, 1),
