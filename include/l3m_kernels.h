@@ -75,6 +75,14 @@ L3M_API int l3m_gemv_dev(int exact, int dtype, float *y, const void *tiles, int 
 // shared by all calls on a device, so overlapping calls (two streams or threads) race and must be
 // serialised. The first call on each device looks the buffer up; make it before any stream capture.
 L3M_API int l3m_gemv_splitk_dev(int dtype, float *y, const void *tiles, int ntiles, int k, const l3m_vec *x, void *stream);
+// One draw of the reference's temperature sampler (src/engine.c:98-101, 283-287, 370-384, one
+// rank) over logits[0..vocab) on the device: weights expf((l - max) / temperature) (0 below -16),
+// the first index whose running double sum exceeds u * (the whole sum), u the next xorshift64*
+// draw of *rng_state (advanced); the last index when none does. rng_state, token: device memory;
+// scratch: vocab floats of device memory. temperature must be > 0. Tests use it; l3m_generate
+// samples inside its own kernel with the same code.
+L3M_API int l3m_sample_dev(const float *logits, int vocab, float temperature, uint64_t *rng_state, int32_t *token, float *scratch,
+                           void *stream);
 // Prepare x[0..n) for dtype on the device, as l3m_vec_prepare. scratch (device) >= 2n + n/4 bytes.
 L3M_API int l3m_vec_prepare_dev(int dtype, l3m_vec *out, const float *x, int n, void *scratch, void *stream);
 // The exact integer part of each quantised kernel: dots[(t*16 + c)*(k/32) + b] = sum_i w*q8_x over block b

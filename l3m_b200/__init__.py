@@ -79,6 +79,7 @@ def lib():
         "l3m_gemv_dev": (i, [i, i, vp, vp, i, i, C.POINTER(Vec), vp]),
         "l3m_gemv_splitk_dev": (i, [i, vp, vp, i, i, C.POINTER(Vec), vp]),
         "l3m_vec_prepare_dev": (i, [i, C.POINTER(Vec), vp, i, vp, vp]),
+        "l3m_sample_dev": (i, [vp, i, f, vp, vp, vp, vp]),
         "l3m_block_dots_dev": (i, [i, vp, vp, i, i, C.POINTER(Vec), vp]),
         "l3m_unpack_dev": (i, [i, vp, vp, vp, i, i, vp]),
         "l3m_attend_dev": (i, [vp, vp, vp, vp, i, i, i, vp]),

@@ -24,6 +24,7 @@
 #include <cooperative_groups.h>
 #include "ops.cuh"
 #include "decode.cuh"
+#include "../../include/l3m_kernels.h"
 
 namespace cg = cooperative_groups;
 
@@ -374,6 +375,166 @@ __device__ __noinline__ void phase_down(const DecodeArgs &a, const LayerDev &L, 
     }
 }
 
+// ---- Temperature sampling (reference engine.c:98-101, 283-287, 370-384, one rank): the weights
+// p_i = expf((l_i - gmax) / T) (0 below -16), z = their sequential double sum, u = the next
+// xorshift64* draw; the token is the first i whose running double sum exceeds u * z (the last
+// index when none does: a NaN sum). Every nonzero weight is a float in [2^-24, 1], an integer
+// number of 2^-47 units, so the running sums are computed exactly as 64-bit integers in parallel;
+// the sequential double sum equals them until the first step whose exact sum is not a double
+// (more than 53 significant bits: only after the sum passes 64 and only for weights below about
+// 6e-5). Without such a step the draw is found in parallel from the exact sums; with one, one
+// thread runs the reference's double chains over the stored weights (rare, slow, exact).
+struct SampleIn {
+    const float *logits;                 // [vocab], this position's
+    float *probs;                        // [vocab] scratch: the weights
+    int vocab;
+    float temp, gmax;
+    const uint32_t *elist, *eindex;      // libm expf exception list
+};
+
+__device__ __forceinline__ double rand01(unsigned long long &st) {
+    st ^= st >> 12;
+    st ^= st << 25;
+    st ^= st >> 27;
+    return (double)((st * 0x2545F4914F6CDD1DULL) >> 11) * (1.0 / 9007199254740992.0);
+}
+
+__device__ __forceinline__ unsigned long long weight_units(float p) {   // p * 2^47, exact
+    return (unsigned long long)__fmul_rn(p, 140737488355328.0f);
+}
+
+__device__ __forceinline__ bool double_exact(unsigned long long e) {     // at most 53 significant bits
+    const int bl = 64 - __clzll((long long)e);
+    return bl <= 53 || (e & ((1ull << (bl - 53)) - 1)) == 0;
+}
+
+__device__ __forceinline__ void put_u64(float *d, unsigned long long v) {
+    d[0] = __int_as_float((int)(uint32_t)v);
+    d[1] = __int_as_float((int)(uint32_t)(v >> 32));
+}
+__device__ __forceinline__ unsigned long long get_u64(const float *d) {
+    return (unsigned long long)(uint32_t)__float_as_int(d[0]) | (unsigned long long)(uint32_t)__float_as_int(d[1]) << 32;
+}
+
+// The smallest value of v over the CTA (every thread gets it); red: >= 8 ints of shared memory.
+__device__ int cta_min(int v, int *red) {
+    for (int o = 16; o; o >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, o));
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    int m = red[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); w++) m = min(m, red[w]);
+    __syncthreads();
+    return m;
+}
+
+// Every CTA of the cluster, in step; the same token returned in every CTA. xs: 3 x 16 x 4 floats of
+// shared memory, written by every CTA of the cluster (distributed shared memory); tmp: 4 floats; red:
+// 32 floats; stage: stage_n floats of shared memory for the one-thread fallback.
+__device__ __noinline__ int sample_token(const SampleIn &in, float *xs, float *tmp, float *red, float *stage, int stage_n,
+                                         unsigned long long &rng) {
+    const int rank = (int)cg::this_cluster().block_rank(), tid = threadIdx.x, nth = blockDim.x, V = in.vocab;
+    const double u = rand01(rng);
+    const int lo = (int)((long long)rank * V / kClusterCtas), hi = (int)((long long)(rank + 1) * V / kClusterCtas);
+    const int per = (hi - lo + nth - 1) / nth, i0 = min(hi, lo + tid * per), i1 = min(hi, i0 + per);
+    // 1: the weights of this CTA's slice, their exact sum, NaN seen.
+    unsigned long long tsum = 0;
+    int nan = 0;
+    for (int i = i0; i < i1; i++) {
+        const float d = __fdiv_rn(__fsub_rn(ld_cg_f32(in.logits + i), in.gmax), in.temp);
+        const float p = d < -16.0f ? 0.0f : l3m_expf_exact(d, in.elist, in.eindex);
+        in.probs[i] = p;
+        if (p != p) nan = 1;
+        else tsum += weight_units(p);
+    }
+    unsigned long long incl = tsum;                                       // exclusive scan over threads (index order)
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long n = __shfl_up_sync(0xffffffffu, incl, o);
+        if ((tid & 31) >= o) incl += n;
+    }
+    unsigned long long *wsum = (unsigned long long *)red;
+    __syncthreads();
+    if ((tid & 31) == 31) wsum[tid >> 5] = incl;
+    const int anynan_cta = __syncthreads_or(nan);
+    unsigned long long toff = incl - tsum, total = 0;
+    for (int w = 0; w < nth >> 5; w++) {
+        if (w < (tid >> 5)) toff += wsum[w];
+        total += wsum[w];
+    }
+    if (tid == 0) { put_u64(tmp, total); tmp[2] = __int_as_float(anynan_cta); tmp[3] = 0.0f; }
+    __syncthreads();
+    scatter(tmp, xs, 4 * rank, 4);
+    cluster_sync();
+    unsigned long long base = 0, Z = 0;
+    int anynan = 0;
+    for (int c = 0; c < kClusterCtas; c++) {
+        const unsigned long long t = get_u64(xs + 4 * c);
+        if (c < rank) base += t;
+        Z += t;
+        anynan |= __float_as_int(xs[4 * c + 2]);
+    }
+    if (anynan) return V - 1;                                             // the same in every CTA
+    // 2: the first step whose exact running sum is not a double.
+    int first = 0x7FFFFFFF;
+    {
+        unsigned long long e = base + toff;
+        for (int i = i0; i < i1; i++) {
+            e += weight_units(in.probs[i]);
+            if (!double_exact(e)) { first = i; break; }
+        }
+    }
+    first = cta_min(first, (int *)red);
+    if (tid == 0) { tmp[0] = __int_as_float(first); tmp[1] = tmp[2] = tmp[3] = 0.0f; }
+    __syncthreads();
+    scatter(tmp, xs + 4 * kClusterCtas, 4 * rank, 4);
+    cluster_sync();
+    int jr = 0x7FFFFFFF;
+    for (int c = 0; c < kClusterCtas; c++) jr = min(jr, __float_as_int(xs[4 * kClusterCtas + 4 * c]));
+    // 3: the draw.
+    int tok = 0x7FFFFFFF;
+    if (jr == 0x7FFFFFFF) {                                               // every running sum is a double: z = Z * 2^-47
+        const double target = u * ((double)Z * 0x1p-47);
+        unsigned long long e = base + toff;
+        for (int i = i0; i < i1; i++) {
+            e += weight_units(in.probs[i]);
+            if ((double)e * 0x1p-47 > target) { tok = i; break; }
+        }
+        tok = cta_min(tok, (int *)red);
+    } else if (rank == 0) {                                               // the reference's chains over the stored weights, by
+        double z = 0.0, target = 0.0, c = 0.0;                            // thread 0, the CTA staging them in shared memory
+        int *found = (int *)red;
+        for (int pass = 0; pass < 2; pass++) {
+            if (tid == 0) found[0] = 0x7FFFFFFF;
+            for (int b0 = 0; b0 < V; b0 += stage_n) {
+                const int n = min(stage_n, V - b0);
+                __syncthreads();
+                for (int i = tid; i < n; i += nth) stage[i] = ld_cg_f32(in.probs + b0 + i);
+                __syncthreads();
+                if (tid == 0) {
+                    if (pass == 0) {
+                        for (int i = 0; i < n; i++) z += (double)stage[i];
+                    } else if (found[0] == 0x7FFFFFFF) {
+                        for (int i = 0; i < n; i++) {
+                            c += (double)stage[i];
+                            if (c > target) { found[0] = b0 + i; break; }
+                        }
+                    }
+                }
+            }
+            if (pass == 0 && tid == 0) target = u * z;
+        }
+        __syncthreads();
+        tok = found[0];
+    }
+    if (tid == 0) { tmp[0] = __int_as_float(tok); tmp[1] = tmp[2] = tmp[3] = 0.0f; }
+    __syncthreads();
+    scatter(tmp, xs + 8 * kClusterCtas, 4 * rank, 4);
+    cluster_sync();
+    int t = 0x7FFFFFFF;
+    for (int c = 0; c < kClusterCtas; c++) t = min(t, __float_as_int(xs[8 * kClusterCtas + 4 * c]));
+    return t == 0x7FFFFFFF ? V - 1 : t;
+}
+
 __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t *p) {
     uint32_t v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -506,6 +667,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
     const int tslot = a.trace_cta[0] == cta ? 0 : a.trace_cta[1] == cta ? 1 : -1;
     int n_gen = 0, tok = 0, pos = 0;
     uint32_t tcount = 0;
+    unsigned long long rng = a.rng;                                       // advanced identically in every CTA of cluster 0
     bool ok = true;
     if (role.voc0 < role.voc1) stage_f32(s.wh, a.norm, a.dim);
     if (cta >= kClusterCtas) {                                            // the other clusters: head tiles only
@@ -631,7 +793,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
                 s.tmp[0] = __int_as_float(next);
                 s.tmp[1] = sl[2];
                 s.tmp[2] = __int_as_float(r > 0 && !*(volatile int *)a.hx.abort_flag ? 1 : 0);
-                s.tmp[3] = 0.0f;
+                s.tmp[3] = gmax;
             }
             __syncthreads();
             scatter(s.tmp, s.xt, 0, 4);
@@ -646,13 +808,19 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
                 all &= __float_as_int(sl[3]);
             }
             __syncthreads();                                              // every thread has read the slots
-            if (tid == 0) { s.xt[0] = __int_as_float(nx); s.xt[1] = s.xt[4 + 2]; s.xt[2] = __int_as_float(all); }
+            if (tid == 0) { s.xt[0] = __int_as_float(nx); s.xt[1] = s.xt[4 + 2]; s.xt[2] = __int_as_float(all); s.xt[3] = gmax; }
             __syncthreads();
         }
-        const int next = __float_as_int(s.xt[0]), stop_req = __float_as_int(s.xt[1]);
+        int next = __float_as_int(s.xt[0]);
+        const int stop_req = __float_as_int(s.xt[1]);
+        const float gmax_all = s.xt[3];
         if (!__float_as_int(s.xt[2])) { ok = false; break; }
         trace(a, tslot, pos, a.n_layers, 2);
         if (stop_after) break;                                            // logits kept, nothing sampled (uniform)
+        if (a.temp > 0.0f) {                                              // every CTA of cluster 0, in step
+            const SampleIn in{a.logits + (size_t)pos * a.vocab, a.probs, a.vocab, a.temp, gmax_all, a.elist, a.eindex};
+            next = sample_token(in, s.xt + 4 + 4 * kClusterCtas, s.tmp, s.red, (float *)s.scratch, 2 * a.scratch_pairs, rng);
+        }
         tok = next;
         if (tok == a.eos || tok == a.bos) break;                          // reference engine.c:323-324
         n_gen++;
@@ -677,6 +845,36 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
         __threadfence_system();
         a.ctrl->done = 1;
     }
+}
+
+// One draw of the sampler on its own (tests): a single 16-CTA cluster over logits already on the
+// device; the maximum is found first (every CTA its slice, then an exchange).
+__global__ void __launch_bounds__(kDecodeThreads, 1) sample_kernel(const float *logits, float *probs, int vocab, float temp,
+                                                                  unsigned long long *rng_io, int *token, const uint32_t *elist,
+                                                                  const uint32_t *eindex) {
+    __shared__ __align__(16) float xs[16 * kClusterCtas], xm[4 * kClusterCtas], tmp[4], red[64], stage[4096];
+    const int rank = (int)cg::this_cluster().block_rank(), tid = threadIdx.x;
+    const int lo = (int)((long long)rank * vocab / kClusterCtas), hi = (int)((long long)(rank + 1) * vocab / kClusterCtas);
+    float m = -INFINITY;
+    for (int i = lo + tid; i < hi; i += blockDim.x) m = fmaxf(m, ld_cg_f32(logits + i));   // a NaN never wins
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((tid & 31) == 0) red[tid >> 5] = m;
+    __syncthreads();
+    if (tid == 0) {
+        float v = -INFINITY;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) v = fmaxf(v, red[w]);
+        tmp[0] = v; tmp[1] = tmp[2] = tmp[3] = 0.0f;
+    }
+    __syncthreads();
+    scatter(tmp, xm, 4 * rank, 4);
+    cluster_sync();
+    float gmax = -INFINITY;
+    for (int c = 0; c < kClusterCtas; c++) gmax = fmaxf(gmax, xm[4 * c]);
+    unsigned long long rng = *rng_io;
+    const SampleIn in{logits, probs, vocab, temp, gmax, elist, eindex};
+    const int t = sample_token(in, xs + 4, tmp, red, stage, 4096, rng);
+    if (rank == 0 && tid == 0) { *token = t; *rng_io = rng; }
+    cluster_sync();                                                       // no CTA leaves while others may write its memory
 }
 
 }  // namespace l3m
@@ -734,6 +932,34 @@ extern "C" int l3m_decode_smem_budget(void) {
         cudaFuncGetAttributes(&fa, (const void *)l3m::decode_kernel) != cudaSuccess)
         return 0;
     return optin - (int)fa.sharedSizeBytes;
+}
+
+extern "C" int l3m_expf_tables(const uint32_t **list, const uint32_t **index);
+extern "C" int l3m_error_msg(const char *msg);
+extern "C" int l3m_error_cuda(int e, const char *what);
+
+// One draw of the reference's sampler over device logits (include/l3m_kernels.h).
+extern "C" L3M_API int l3m_sample_dev(const float *logits, int vocab, float temperature, uint64_t *rng_state, int32_t *token, float *scratch,
+                                      void *stream) {
+    if (vocab <= 0 || !(temperature > 0.0f)) return l3m_error_msg("l3m_sample_dev: vocab > 0 and temperature > 0");
+    const uint32_t *list, *index;
+    if (l3m_expf_tables(&list, &index)) return -1;
+    cudaError_t e = cudaFuncSetAttribute(l3m::sample_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e == cudaSuccess) {
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute at[1];
+        cfg.gridDim = dim3(l3m::kClusterCtas);
+        cfg.blockDim = dim3(l3m::kDecodeThreads);
+        cfg.stream = (cudaStream_t)stream;
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = (unsigned)l3m::kClusterCtas;
+        at[0].val.clusterDim.y = at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, l3m::sample_kernel, logits, scratch, vocab, temperature, (unsigned long long *)rng_state, (int *)token,
+                               list, index);
+    }
+    return e == cudaSuccess ? 0 : l3m_error_cuda((int)e, "l3m_sample_dev");
 }
 
 // How many clusters of kClusterCtas CTAs with smem_bytes of shared memory each can be resident on

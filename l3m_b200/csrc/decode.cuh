@@ -66,6 +66,9 @@ struct DecodeArgs {
     const int32_t *prompt;
     int n_prompt, max_new, eos, bos;
     float *logits;                      // [ctx][vocab]
+    float temp;                         // > 0: sample (reference engine.c:370-384); else greedy
+    unsigned long long rng;             // xorshift64* state, seeded as the reference (engine.c:555)
+    float *probs;                       // [vocab] the sampling weights of the current position
     Ctrl *ctrl;
     int32_t *tokens;                    // host-mapped, ctx entries
     unsigned long long *trace;          // optional: [2][ctx][n_layers + 1][kTraceEvents] globaltimer stamps

@@ -62,6 +62,7 @@ struct Gpu {
     size_t hx_bytes = 0;
     int32_t *prompt = nullptr;
     float *logits = nullptr;
+    float *probs = nullptr;                                            // [vocab] sampling weights
     l3m::DecodeArgs args{};
     size_t l2_bytes = 0, persist_max = 0, window_max = 0, prev_limit = 0;
     bool limit_set = false;
@@ -350,6 +351,7 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     }
     if (!cuda_ok(cudaMalloc(&g.prompt, (size_t)m->ctx * 4), "prompt")) return false;
     if (!cuda_ok(cudaMalloc(&g.logits, (size_t)m->ctx * V * 4), "logits")) return false;
+    if (!cuda_ok(cudaMalloc(&g.probs, (size_t)V * 4), "sampling weights")) return false;
     cudaMemset(g.logits, 0, (size_t)m->ctx * V * 4);
     a.prompt = g.prompt;
     a.eos = m->f.tok.eos; a.bos = m->f.tok.bos;
@@ -387,7 +389,7 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     a.sm_xp = take(dim * 4);
     a.sm_xh = take(ffn * 4);
     a.sm_xd = take(dim * 4);
-    a.sm_xt = take((4 + 4 * G) * 4);
+    a.sm_xt = take((4 + 16 * G) * 4);                                  // token, argmax slots, 3 sampling exchanges
     a.sm_wbar = take(16);
     // Scratch: the (scale product, dot) pairs of the largest per-CTA phase of a layer, so each runs in
     // one pass (the head runs in several).
@@ -549,7 +551,7 @@ L3M_API void l3m_free(l3m_model *m) {
             cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, g.prev_limit);
         }
         cudaFree(g.arena); cudaFree(g.kv); cudaFree(g.rope); cudaFree(g.layers); cudaFree(g.roles); cudaFree(g.args_dev); cudaFree(g.trace); cudaFree(g.hx);
-        cudaFree(g.prompt); cudaFree(g.logits);
+        cudaFree(g.prompt); cudaFree(g.logits); cudaFree(g.probs);
         if (g.ev0) cudaEventDestroy(g.ev0);
         if (g.ev1) cudaEventDestroy(g.ev1);
         if (g.stream) cudaStreamDestroy(g.stream);
@@ -563,17 +565,18 @@ L3M_API void l3m_free(l3m_model *m) {
 
 L3M_API int l3m_generate(l3m_model *m, const int32_t *prompt, int n_prompt, int max_new, float temperature, uint64_t seed,
                          int (*on_token)(int32_t, void *), void *user) {
-    (void)seed;
     if (n_prompt < 1 || n_prompt >= m->ctx) return 0;
     for (int i = 0; i < n_prompt; i++)
         if (prompt[i] < 0 || prompt[i] >= m->vocab) { fprintf(stderr, "l3m: token %d out of range\n", prompt[i]); return -1; }
-    if (temperature > 0) { fprintf(stderr, "l3m: temperature sampling is not built on the GPU yet; use temperature 0\n"); return -1; }
     Gpu &g = m->g[0];
     cudaSetDevice(g.dev);
     memset((void *)m->ctrl, 0, sizeof *m->ctrl);
     l3m::DecodeArgs a = g.args;
     a.n_prompt = n_prompt;
     a.max_new = max_new;
+    a.temp = temperature > 0 ? temperature : 0.0f;                     // NaN and <= 0: greedy (reference engine.c:301)
+    a.rng = seed * 0x9E3779B97F4A7C15ULL + 1;                           // reference engine.c:555
+    a.probs = g.probs;
     const double t0 = now_ns();
     cudaMemcpyAsync(g.prompt, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, g.stream);
     cudaMemcpyAsync(g.args_dev, &a, sizeof a, cudaMemcpyHostToDevice, g.stream);

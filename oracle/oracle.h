@@ -62,6 +62,12 @@ const float *o_ref_forward(o_model *m, int32_t tok, int pos);
 // Returns the number generated; *n_pos gets the positions run (prompt included).
 int          o_generate(o_model *m, const int32_t *prompt, int n_prompt, int max_new, int32_t *out,
                         float *logits_out, int *n_pos, int reference);
+// The same with temperature sampling (temp > 0; seed as l3m_generate's).
+int          o_generate_t(o_model *m, const int32_t *prompt, int n_prompt, int max_new, float temp, uint64_t seed,
+                          int32_t *out, float *logits_out, int *n_pos, int reference);
+// One draw of the reference's sampler over logits[0..n) (reference engine.c:283-287, 370-384):
+// argmax when temp is not > 0; advances *rng only when it samples.
+int32_t      o_sample(const float *logits, int n, float temp, uint64_t *rng);
 
 // ---- libm expf, as the reference calls it (softmax, SiLU); exposed so tests can compare.
 float o_expf(float x);

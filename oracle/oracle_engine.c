@@ -330,9 +330,48 @@ static int32_t argmax(const float *logits, int n) {
     return idx;
 }
 
+// reference engine.c:98-101: xorshift64*, a double in [0, 1).
+static double rand01(uint64_t *s) {
+    *s ^= *s >> 12;
+    *s ^= *s << 25;
+    *s ^= *s >> 27;
+    return (double)((*s * 0x2545F4914F6CDD1DULL) >> 11) * (1.0 / 9007199254740992.0);
+}
+
+// reference engine.c:283-287: the unnormalised weight of a logit, 0 below e^-16 of the maximum.
+static float prob(float logit, float gmax, float temp) {
+    float d = (logit - gmax) / temp;
+    return d < -16 ? 0 : o_expf(d);
+}
+
+// reference engine.c:370-384 (and 290-330 with one rank): the greedy choice when temp is not > 0;
+// else the first index whose running double sum of weights exceeds u * z (z the whole sum, u the
+// next draw), the last index when none does (a NaN sum).
+int32_t o_sample(const float *logits, int n, float temp, uint64_t *rng) {
+    float gmax = -INFINITY;
+    int32_t best = 0;
+    for (int i = 0; i < n; i++) if (logits[i] > gmax) { gmax = logits[i]; best = i; }
+    if (!(temp > 0)) return best;
+    float *probs = malloc((size_t)n * sizeof(float));
+    double z = 0;
+    for (int i = 0; i < n; i++) z += probs[i] = prob(logits[i], gmax, temp);
+    double target = rand01(rng) * z, c = 0;
+    int32_t tok = n - 1;
+    for (int i = 0; i < n; i++) if ((c += probs[i]) > target) { tok = i; break; }
+    free(probs);
+    return tok;
+}
+
 // reference engine.c:322-327, 342-362 (and 364-386 for the reference path), temperature 0.
 int o_generate(o_model *m, const int32_t *prompt, int n_prompt, int max_new, int32_t *out, float *logits_out,
                int *n_pos, int reference) {
+    return o_generate_t(m, prompt, n_prompt, max_new, 0.0f, 0, out, logits_out, n_pos, reference);
+}
+
+// The same with temperature sampling (reference engine.c:549-555 seeds the generator).
+int o_generate_t(o_model *m, const int32_t *prompt, int n_prompt, int max_new, float temp, uint64_t seed, int32_t *out,
+                 float *logits_out, int *n_pos, int reference) {
+    uint64_t rng = seed * 0x9E3779B97F4A7C15ULL + 1;
     if (n_prompt < 1 || n_prompt >= m->ctx) { if (n_pos) *n_pos = 0; return 0; }
     int n_gen = 0, pos = 0, rows = 0;
     int32_t tok = 0;
@@ -351,7 +390,7 @@ int o_generate(o_model *m, const int32_t *prompt, int n_prompt, int max_new, int
         if (logits_out) memcpy(logits_out + (size_t)rows * m->vocab, lg, (size_t)m->vocab * 4);
         rows++;
         if (stop) break;
-        tok = argmax(lg, m->vocab);
+        tok = temp > 0 ? o_sample(lg, m->vocab, temp, &rng) : argmax(lg, m->vocab);
         if (tok == m->eos || tok == m->bos) break;
         out[n_gen++] = tok;
     }

@@ -55,6 +55,8 @@ def load_oracle():
         "o_eos": (i, [vp]), "o_bos": (i, [vp]),
         "o_forward": (C.POINTER(C.c_float), [vp, C.c_int32, i, i]),
         "o_generate": (i, [vp, C.POINTER(C.c_int32), i, i, vp, vp, C.POINTER(i), i]),
+        "o_generate_t": (i, [vp, C.POINTER(C.c_int32), i, i, C.c_float, C.c_uint64, vp, vp, C.POINTER(i), i]),
+        "o_sample": (C.c_int32, [vp, i, C.c_float, C.POINTER(C.c_uint64)]),
         "o_row_bytes": (C.c_size_t, [i, i]), "o_tile_bytes": (C.c_size_t, [i, i]),
         "o_pack_tile": (None, [vp, i, C.POINTER(vp), i]), "o_dequant_row": (None, [vp, i, vp, i]),
         "o_vec_prepare": (None, [C.POINTER(Vec), i, vp, i, vp]),
@@ -72,9 +74,10 @@ def load_oracle():
 
 
 class OracleRun:
-    """Greedy generate on the oracle: tokens, logits of every sampled position, positions run."""
+    """Generate on the oracle (greedy, or sampled at temperature > 0): tokens, logits of every
+    sampled position, positions run."""
 
-    def __init__(self, oracle, path, prompt, max_new, ctx=0, reference=False):
+    def __init__(self, oracle, path, prompt, max_new, ctx=0, reference=False, temperature=0.0, seed=0):
         m = oracle.o_load(os.fsencode(str(path)), ctx)
         assert m, f"oracle could not load {path}"
         try:
@@ -83,7 +86,7 @@ class OracleRun:
             lg = np.zeros((max_new + 1, V), np.float32)
             npos = C.c_int()
             pr = (C.c_int32 * len(prompt))(*prompt)
-            n = oracle.o_generate(m, pr, len(prompt), max_new, out, P(lg), C.byref(npos), int(reference))
+            n = oracle.o_generate_t(m, pr, len(prompt), max_new, temperature, seed, out, P(lg), C.byref(npos), int(reference))
             self.tokens = list(out[:n])
             self.n_pos = npos.value
             rows = self.n_pos - (len(prompt) - 1)

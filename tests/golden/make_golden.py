@@ -9,7 +9,9 @@ oracle/Makefile):  python tests/golden/make_golden.py [/root/reference]
   models.json     sha256 of small .l3m files written by the reference's exporter from the same
                   fp32 tensors as l3m_b200.synth builds (the tests' `models` fixture).
   engine.npz      the reference engine's greedy tokens and logits on those files: its scalar
-                  kernel table on 1 and 3 cores (L3M_ISA=scalar), and its fp32 reference path.
+                  kernel table on 1 and 3 cores (L3M_ISA=scalar), and its fp32 reference path;
+                  and its sampled tokens (temperature 0.8 seed 7, 1.7 seed 123) on 1 core and
+                  on the reference path.
 """
 import ctypes as C
 import hashlib
@@ -97,6 +99,24 @@ def run_ref(lib, path, cores, reference):
     return toks, np.stack(logits)
 
 
+SAMPLED = ((0.8, 7), (1.7, 123))                 # (temperature, seed) of the sampled golden runs
+
+
+def run_ref_sampled(lib, path, cores, reference, temp, seed):
+    """Tokens of one sampled generation (the reference's sampler; one core = one rank)."""
+    cb_t = C.CFUNCTYPE(C.c_int, C.c_int32, C.c_void_p)
+    cpus = (C.c_int * cores)(*range(cores))
+    o = Opts(cpus=None if reference else cpus, n_cpus=0 if reference else cores, reference=int(reference), force=1)
+    m = lib.l3m_load(os.fsencode(str(path)), C.byref(o))
+    assert m
+    toks = []
+    cb = cb_t(lambda t, u: toks.append(t) or 1)
+    pr = (C.c_int32 * len(PROMPT))(*PROMPT)
+    lib.l3m_generate(m, pr, len(PROMPT), STEPS, temp, seed, cb, None)
+    lib.l3m_free(m)
+    return toks
+
+
 def main():
     (HERE / "ggml.json").write_text(json.dumps(ggml_golden(), indent=1))
     os.environ["L3M_ISA"] = "scalar"
@@ -117,6 +137,10 @@ def main():
                     toks, lg = run_ref(lib, path, cores, reference)
                     arrays[f"{name}-{dt}-{label}-tokens"] = np.array(toks, np.int32)
                     arrays[f"{name}-{dt}-{label}-logits"] = lg
+                for label, cores, reference in (("scalar1", 1, 0), ("ref", 1, 1)):
+                    for temp, seed in SAMPLED:
+                        toks = run_ref_sampled(lib, path, cores, reference, temp, seed)
+                        arrays[f"{name}-{dt}-{label}-t{temp}-s{seed}-tokens"] = np.array(toks, np.int32)
                 assert np.array_equal(arrays[f"{name}-{dt}-scalar1-logits"], arrays[f"{name}-{dt}-scalar3-logits"])
                 del arrays[f"{name}-{dt}-scalar3-logits"], arrays[f"{name}-{dt}-scalar3-tokens"]
     (HERE / "models.json").write_text(json.dumps({"prompt": PROMPT, "steps": STEPS, "sha256": hashes}, indent=1))

@@ -39,6 +39,59 @@ def test_logits_bit_exact(gpu, oracle, models, name, dt, reference):
     assert bad.size == 0, f"first differing position {bad[0]}, max |diff| {np.abs(lg - want.logits).max()}"
 
 
+ENGINE = np.load(GOLDEN / "engine.npz")
+SAMPLED = ((0.8, 7), (1.7, 123))
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+@pytest.mark.parametrize("name", ["gqa", "mha40"])
+@pytest.mark.parametrize("reference", [False, True])
+def test_sampling_matches_reference(gpu, oracle, models, name, dt, reference):
+    """Temperature sampling (reference engine.c:370-384, one rank): the reference's own token streams
+    (tests/golden, its 1-core table and its fp32 path) and the oracle's, token for token."""
+    path = models[(name, dt)]
+    m = l3m_b200.Model(path, force=True, reference=reference)
+    for temp, seed in SAMPLED:
+        got = m.generate(PROMPT, MJ["steps"], temperature=temp, seed=seed)
+        want = OracleRun(oracle, path, PROMPT, MJ["steps"], reference=reference, temperature=temp, seed=seed)
+        assert got == want.tokens, (temp, seed)
+        label = "ref" if reference else "scalar1"
+        assert got == ENGINE[f"{name}-{dt}-{label}-t{temp}-s{seed}-tokens"].tolist(), (temp, seed)
+
+
+def test_sampler_draws_match_oracle(gpu, oracle):
+    """l3m_sample_dev (the device sampler l3m_generate runs) against the oracle's sampler, draw by
+    draw with the generator state carried along: random logits at three temperatures; a flat
+    distribution with a tail of tiny weights over a 49152 vocabulary, whose double running sum
+    rounds (the one-thread fallback); a NaN logit (the last index); a 7-entry vocabulary."""
+    import torch
+    lib = l3m_b200.lib()
+    lib.l3m_sample_dev.restype = C.c_int
+    lib.l3m_sample_dev.argtypes = [C.c_void_p, C.c_int, C.c_float, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
+    rng = np.random.default_rng(4)
+    V = 49152
+    flat = np.zeros(V, np.float32)
+    flat[rng.integers(0, V, 20000)] = -15.9          # e^-15.9: weights far below the running sum's last bit
+    flat[rng.integers(0, V, 5000)] = -11.3
+    nan = rng.standard_normal(V).astype(np.float32)
+    nan[V // 3] = np.nan
+    cases = [(rng.standard_normal(V).astype(np.float32) * 3, t) for t in (0.5, 1.0, 2.0)]
+    cases += [(flat, 1.0), (nan, 1.0), (rng.standard_normal(7).astype(np.float32), 0.9)]
+    for lg, temp in cases:
+        dl = torch.from_numpy(lg).cuda()
+        scratch = torch.empty(lg.size, dtype=torch.float32, device="cuda")
+        st = torch.tensor([12345], dtype=torch.int64, device="cuda")
+        tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+        ost = C.c_uint64(12345)
+        for _ in range(6):
+            assert lib.l3m_sample_dev(C.c_void_p(dl.data_ptr()), lg.size, temp, C.c_void_p(st.data_ptr()), C.c_void_p(tok.data_ptr()),
+                                      C.c_void_p(scratch.data_ptr()), None) == 0, lib.l3m_cuda_error()
+            torch.cuda.synchronize()
+            want = oracle.o_sample(lg.ctypes.data_as(C.c_void_p), lg.size, temp, C.byref(ost))
+            assert int(tok.item()) == want, (lg.size, temp)
+            assert int(st.item()) & 0xFFFFFFFFFFFFFFFF == ost.value
+
+
 def test_max_new_zero_gives_prompt_logits(gpu, oracle, models):
     path = models[("gqa", "q8_0")]
     m = l3m_b200.Model(path, force=True)

@@ -58,6 +58,40 @@ def test_oracle_matches_reference_engine(oracle, models, name, dt, path_kind):
     assert np.array_equal(run.logits.view(np.uint32), want_l.view(np.uint32))
 
 
+SAMPLED = ((0.8, 7), (1.7, 123))
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+@pytest.mark.parametrize("name", ["gqa", "mha40"])
+@pytest.mark.parametrize("path_kind", ["scalar1", "ref"])
+def test_oracle_sampling_matches_reference_engine(oracle, models, name, dt, path_kind):
+    """Temperature sampling: the reference's token streams (one rank; its fp32 path) for two
+    (temperature, seed) pairs, token for token."""
+    for temp, seed in SAMPLED:
+        run = OracleRun(oracle, models[(name, dt)], MJ["prompt"], MJ["steps"], reference=path_kind == "ref", temperature=temp, seed=seed)
+        assert run.tokens == ENGINE[f"{name}-{dt}-{path_kind}-t{temp}-s{seed}-tokens"].tolist(), (temp, seed)
+
+
+def test_oracle_sampler_edges(oracle):
+    """The sampler alone: greedy below temperature 0 and for NaN (no draw), the last index for a NaN
+    sum, and the xorshift64* draws of the reference (engine.c:98-101)."""
+    lg = np.array([0.5, 2.0, 2.0, -30.0], np.float32)
+    st = C.c_uint64(5)
+    assert oracle.o_sample(P(lg), 4, 0.0, C.byref(st)) == 1 and st.value == 5
+    assert oracle.o_sample(P(lg), 4, float("nan"), C.byref(st)) == 1 and st.value == 5
+    lg2 = np.array([1.0, np.nan, 3.0], np.float32)
+    assert oracle.o_sample(P(lg2), 3, 1.0, C.byref(st)) == 2 and st.value != 5
+    s = 5
+    for _ in range(3):
+        s ^= s >> 12
+        s ^= (s << 25) & 0xFFFFFFFFFFFFFFFF
+        s ^= s >> 27
+    st = C.c_uint64(5)
+    got = [oracle.o_sample(P(np.zeros(1000, np.float32)), 1000, 1.0, C.byref(st)) for _ in range(3)]
+    u = ((s * 0x2545F4914F6CDD1D) & 0xFFFFFFFFFFFFFFFF) >> 11
+    assert st.value == s and got[2] == int(u / 2**53 * 1000)
+
+
 # ---- function by function against the compiled reference (when oracle/_ref is present)
 
 @pytest.fixture(scope="module")
