@@ -87,7 +87,8 @@ def test_oracle_sampler_edges(oracle):
         s ^= (s << 25) & 0xFFFFFFFFFFFFFFFF
         s ^= s >> 27
     st = C.c_uint64(5)
-    got = [oracle.o_sample(P(np.zeros(1000, np.float32)), 1000, 1.0, C.byref(st)) for _ in range(3)]
+    zeros = np.zeros(1000, np.float32)                 # kept alive while the C code reads it
+    got = [oracle.o_sample(P(zeros), 1000, 1.0, C.byref(st)) for _ in range(3)]
     u = ((s * 0x2545F4914F6CDD1D) & 0xFFFFFFFFFFFFFFFF) >> 11
     assert st.value == s and got[2] == int(u / 2**53 * 1000)
 
