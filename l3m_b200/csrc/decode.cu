@@ -38,6 +38,7 @@ struct Smem {
     float2 *scratch;
     uint8_t *w;                          // weight staging area
     unsigned long long *wbar;            // its mbarrier
+    unsigned long long *xbar;            // exchanges 1-5 (async_x)
     Prep prep;
 };
 
@@ -67,6 +68,7 @@ __device__ __forceinline__ Smem carve(unsigned char *base, const DecodeArgs &a) 
     s.scratch = (float2 *)(base + a.sm_scratch);
     s.w = base + a.sm_w;
     s.wbar = (unsigned long long *)(base + a.sm_wbar);
+    s.xbar = (unsigned long long *)(base + a.sm_xbar);
     s.prep.q8 = (int8_t *)(base + a.sm_q8);
     s.prep.scale = (float *)(base + a.sm_scale);
     s.prep.sum = (int32_t *)(base + a.sm_sum);
@@ -102,6 +104,35 @@ __device__ __noinline__ void scatter(const float *src, float *dst, int g0, int n
 
 // Diagnostics: thread 0 of the traced CTAs stamps its SM cycle counter (clock64: a few cycles to
 // read, unlike the global timer) per (position, layer, event).
+// The same with st.async: each 16- (or 4-) byte store completes its bytes on the receiving CTA's
+// mbarrier bar (this CTA's address of it, mapped per rank), so the receivers wait for their bytes
+// instead of a cluster barrier, and the sender does not wait for its stores to land.
+__device__ __noinline__ void scatter_tx(const float *src, float *dst, int g0, int n, unsigned long long *bar) {
+    const int tid = threadIdx.x, nth = blockDim.x;
+    const uint32_t ld = (uint32_t)__cvta_generic_to_shared(dst + g0), lb = (uint32_t)__cvta_generic_to_shared(bar);
+    if (((g0 | n) & 3) == 0) {
+        const int n4 = n >> 2;
+        for (int e = tid; e < n4 * kClusterCtas; e += nth) {
+            const int r = e % kClusterCtas, j = e / kClusterCtas;
+            uint32_t ra, rb;
+            asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(ld + 16 * j), "r"(r));
+            asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rb) : "r"(lb), "r"(r));
+            const float4 v = ((const float4 *)src)[j];
+            asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];"
+                         ::"r"(ra), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(rb) : "memory");
+        }
+    } else {
+        for (int e = tid; e < n * kClusterCtas; e += nth) {
+            const int r = e % kClusterCtas, j = e / kClusterCtas;
+            uint32_t ra, rb;
+            asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(ld + 4 * j), "r"(r));
+            asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rb) : "r"(lb), "r"(r));
+            asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(ra), "r"(__float_as_uint(src[j])), "r"(rb)
+                         : "memory");
+        }
+    }
+}
+
 __device__ __forceinline__ void trace(const DecodeArgs &a, int slot, int pos, int l, int ev) {
     if (a.trace && slot >= 0 && threadIdx.x == 0)
         a.trace[(((size_t)slot * a.ctx + pos) * (a.n_layers + 1) + l) * kTraceEvents + ev] = (unsigned long long)clock64();
@@ -205,6 +236,26 @@ __device__ __forceinline__ void stage_wait(const DecodeArgs &a, const Smem &s, u
     }
 }
 
+// Exchange k (0-4) of the current layer has fully arrived in this CTA (phase parity par; every
+// thread, time-limited), then it is armed for the next layer: one arrival expecting `bytes`.
+__device__ __noinline__ void xwait(const DecodeArgs &a, const Smem &s, int k, uint32_t par, uint32_t bytes) {
+    const uint32_t bar = smem_addr(s.xbar + k);
+    uint64_t t0 = 0;
+    for (int spins = 0;; spins++) {
+        uint32_t done;
+        asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                     : "=r"(done) : "r"(bar), "r"(par) : "memory");
+        if (done) break;
+        if (spins == 0) t0 = globaltimer_ns();
+        else if ((spins & 63) == 0 && globaltimer_ns() - t0 > a.hx.timeout_ns) {
+            atomicCAS(a.hx.abort_flag, 0, kErrTimeout);
+            break;
+        }
+    }
+    __syncthreads();                                                      // every thread has seen this phase complete
+    if (threadIdx.x == 0) asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
 // x = embedding row of tok (reference src/engine.c:236, src/pack.c:55-62).
 __device__ __noinline__ void embed_row(const DecodeArgs &a, int tok, float *x) {
     const uint8_t *row = a.embed + (size_t)tok * a.embed_row_bytes;
@@ -304,7 +355,8 @@ __device__ __noinline__ void phase_attention(const DecodeArgs &a, const LayerDev
     attend_exact<true>(y, kc, vc, hd, a.vstride, s.kcur, s.vcur, pos, hd, s.scores, s.att, s.red, a.elist, a.eindex, s.kvbuf, s.vtbuf,
                        a.attn_chunk, prestaged);
     trace(a, tslot, pos, l, 15);
-    scatter(s.att, s.xa, h * hd, hd);
+    if (a.async_x) scatter_tx(s.att, s.xa, h * hd, hd, s.xbar + 1);
+    else scatter(s.att, s.xa, h * hd, hd);
 }
 
 // Phase B: this CTA's tiles of wo over attn -> s.y (the caller scatters into xp; ns tiles staged at
@@ -678,6 +730,14 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
     }
     stage_vectors(a, layers[0], role, s, 0);
     stage_init(s);
+    uint32_t xpar = 0;                                                    // the exchanges' phase parity (one phase per layer)
+    if (a.async_x && tid == 0) {
+        const uint32_t bytes[5] = {(uint32_t)a.n_qkv * 4, (uint32_t)a.dim * 4, (uint32_t)a.dim * 4, (uint32_t)a.ffn * 4, (uint32_t)a.dim * 4};
+        for (int k = 0; k < 5; k++) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(s.xbar + k)) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int k = 0; k < 5; k++)
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(s.xbar + k)), "r"(bytes[k]) : "memory");
+    }
     // The staged-weight schedule: qkv and wo into [w_extra, w_bytes) (the attention buffers are live
     // from the layer top to the end of attention), up/gate and down from offset 0. ns: tiles of the
     // outstanding copy; wpar: its mbarrier phase parity.
@@ -710,23 +770,34 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
             if (ns) wpar ^= 1;
             ns = stage_issue(s, L.dt_wo, L.wo, a.dim, role.wo0, role.wo1, s.w + a.w_extra, a.w_bytes - a.w_extra);
             trace(a, tslot, pos, l, 27);
-            if (role.qkv0 < role.qkv1) scatter(s.y, s.xq, role.qkv0 * kTile, min(role.qkv1 * kTile, a.n_qkv) - role.qkv0 * kTile);
+            if (role.qkv0 < role.qkv1) {
+                const int g0 = role.qkv0 * kTile, n = min(role.qkv1 * kTile, a.n_qkv) - g0;
+                if (a.async_x) scatter_tx(s.y, s.xq, g0, n, s.xbar);
+                else scatter(s.y, s.xq, g0, n);
+            }
             trace(a, tslot, pos, l, 1);
-            cluster_sync();                                               // 1: qkv
+            if (a.async_x) xwait(a, s, 0, xpar, (uint32_t)a.n_qkv * 4);   // 1: qkv
+            else cluster_sync();
             trace(a, tslot, pos, l, 2);
             for (int h = role.head0; h >= 0 && h < a.n_heads; h += kClusterCtas)   // A
                 phase_attention(a, L, s, h, pos, h == role.head0, l, tslot);
             trace(a, tslot, pos, l, 3);
-            cluster_sync();                                               // 2: attn
+            if (a.async_x) xwait(a, s, 1, xpar, (uint32_t)a.dim * 4);     // 2: attn
+            else cluster_sync();
             trace(a, tslot, pos, l, 4);
             if (role.wo0 < role.wo1) phase_wo(a, L, role, s, ns, wpar, pos, l, tslot);   // B
             if (ns) wpar ^= 1;
             if (!L.gate) ns = stage_issue(s, L.dt_up, L.up, a.dim, 2 * role.ffn0, 2 * role.ffn1, s.w, a.w_bytes);
             else ns = stage_issue(s, L.dt_up, L.up, a.dim, role.ffn0, role.ffn1, s.w, a.w_bytes);
             trace(a, tslot, pos, l, 28);
-            if (role.wo0 < role.wo1) scatter(s.y, s.xp, role.wo0 * kTile, min(role.wo1 * kTile, a.dim) - role.wo0 * kTile);
+            if (role.wo0 < role.wo1) {
+                const int g0 = role.wo0 * kTile, n = min(role.wo1 * kTile, a.dim) - g0;
+                if (a.async_x) scatter_tx(s.y, s.xp, g0, n, s.xbar + 2);
+                else scatter(s.y, s.xp, g0, n);
+            }
             trace(a, tslot, pos, l, 5);
-            cluster_sync();                                               // 3: proj
+            if (a.async_x) xwait(a, s, 2, xpar, (uint32_t)a.dim * 4);     // 3: proj
+            else cluster_sync();
             trace(a, tslot, pos, l, 6);
             phase_ffn(a, L, role, s, pos, l, tslot, ns, wpar);            // C
             if (ns) wpar ^= 1;
@@ -734,13 +805,16 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
             trace(a, tslot, pos, l, 29);
             if (role.ffn0 < role.ffn1) {
                 ffn_gate(a, L, role, s);
-                scatter(s.tmp, s.xh, role.ffn0 * kTile, min(role.ffn1 * kTile, a.ffn) - role.ffn0 * kTile);
+                const int g0 = role.ffn0 * kTile, n = min(role.ffn1 * kTile, a.ffn) - g0;
+                if (a.async_x) scatter_tx(s.tmp, s.xh, g0, n, s.xbar + 3);
+                else scatter(s.tmp, s.xh, g0, n);
             }
             // The next layer's norm weights (and the next position's RoPE row) while the rest runs.
             if (l + 1 < a.n_layers) stage_vectors(a, layers[l + 1], role, s, pos);
             else stage_vectors(a, layers[0], role, s, pos + 1);
             trace(a, tslot, pos, l, 8);
-            cluster_sync();                                               // 4: h
+            if (a.async_x) xwait(a, s, 3, xpar, (uint32_t)a.ffn * 4);     // 4: h
+            else cluster_sync();
             trace(a, tslot, pos, l, 9);
             if (role.dn0 < role.dn1) phase_down(a, L, role, s, ns, wpar, pos, l, tslot);   // D
             if (ns) wpar ^= 1;
@@ -749,9 +823,18 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
                 ns = stage_issue(s, N.dt_qkv, N.qkv, a.dim, role.qkv0, role.qkv1, s.w + a.w_extra, a.w_bytes - a.w_extra);
             }
             trace(a, tslot, pos, l, 30);
-            if (role.dn0 < role.dn1) scatter(s.y, s.xd, role.dn0 * kTile, min(role.dn1 * kTile, a.dim) - role.dn0 * kTile);
+            if (role.dn0 < role.dn1) {
+                const int g0 = role.dn0 * kTile, n = min(role.dn1 * kTile, a.dim) - g0;
+                if (a.async_x) scatter_tx(s.y, s.xd, g0, n, s.xbar + 4);
+                else scatter(s.y, s.xd, g0, n);
+            }
             trace(a, tslot, pos, l, 10);
-            cluster_sync();                                               // 5: down
+            if (a.async_x) {                                              // 5: down
+                xwait(a, s, 4, xpar, (uint32_t)a.dim * 4);
+                xpar ^= 1u;
+            } else {
+                cluster_sync();
+            }
             for (int i = tid; i < a.dim; i += blockDim.x) s.x[i] = __fadd_rn(s.x[i], s.xd[i]);
             __syncthreads();
             trace(a, tslot, pos, l, 11);

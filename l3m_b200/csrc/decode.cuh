@@ -83,6 +83,10 @@ struct DecodeArgs {
     // sm_w .. sm_w + w_bytes; its first w_extra bytes overlap the attention buffers (kvbuf, vt), so
     // the phases around attention (qkv, wo) use only [w_extra, w_bytes). sm_wbar: its mbarrier.
     int sm_w, w_bytes, w_extra, sm_wbar;
+    // Exchanges 1-5 of a layer through st.async + per-CTA mbarriers (sm_xbar: 5 of them) instead of
+    // cluster barriers; set when every CTA of the cluster produces qkv rows, which orders every
+    // buffer's next write after all its reads (see decode.cu).
+    int async_x, sm_xbar;
     int vstride;                        // V cache: element i of position t at vc[i * vstride + t]
     int scratch_pairs, smem_bytes, attn_chunk;
 };

@@ -391,6 +391,7 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     a.sm_xd = take(dim * 4);
     a.sm_xt = take((4 + 16 * G) * 4);                                  // token, argmax slots, 3 sampling exchanges
     a.sm_wbar = take(16);
+    a.sm_xbar = take(5 * 8);
     // Scratch: the (scale product, dot) pairs of the largest per-CTA phase of a layer, so each runs in
     // one pass (the head runs in several).
     int pairs = (mx / 32) * L3M_TILE;
@@ -422,6 +423,12 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
         return false;
     }
     a.grid = GT;
+    a.async_x = !getenv("L3M_CLUSTER_BARRIERS");                        // every CTA of cluster 0 must produce qkv rows
+    {
+        std::vector<l3m::Role> rs0 = make_roles(GT);
+        for (int c = 0; c < G; c++)
+            if (rs0[c].qkv0 >= rs0[c].qkv1) a.async_x = 0;
+    }
     {
         std::vector<l3m::Role> roles = make_roles(GT);
         if (!cuda_ok(cudaMalloc(&g.roles, sizeof(l3m::Role) * GT), "roles")) return false;
