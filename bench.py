@@ -135,6 +135,20 @@ def reference_cpu(path, ctx, n_tokens):
             "sample": f"reference `l3m bench --ctx {ctx} -n {n_tokens} --force`, median of 3 (16 warm-up tokens each)"}
 
 
+def combine_ranks(dist, t_dev, t_wall, positions):
+    """The whole job's (device time, wall time, positions): the times as the maximum over ranks, the
+    positions summed (replicas: every rank runs the same workload on its own GPU)."""
+    if not dist:
+        return t_dev, t_wall, positions
+    import torch
+    t = torch.tensor([t_dev, t_wall, positions], dtype=torch.float64)
+    tmax = t.clone()
+    dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+    tsum = t.clone()
+    dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
+    return tmax[0].item(), tmax[1].item(), tsum[2].item()
+
+
 def bench_ours(a):
     rank, world, local = rank_env()
     import l3m_b200
@@ -167,19 +181,10 @@ def bench_ours(a):
             dev_ns.append(p["ns_compute"] * p["tokens"])
             positions += int(p["tokens"])
     n_gen = len(toks)
-    t_dev, t_wall = sum(dev_ns), sum(wall_ns)
+    t_dev, t_wall, total = combine_ranks(dist, sum(dev_ns), sum(wall_ns), positions)
     if dist:
-        import torch
-        t = torch.tensor([t_dev, t_wall, positions], dtype=torch.float64)
-        tmax = t.clone()
-        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
-        tsum = t.clone()
-        dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
-        t_dev, t_wall, total = tmax[0].item(), tmax[1].item(), tsum[2].item()
         dist.barrier()
         dist.destroy_process_group()
-    else:
-        total = positions
     if rank:
         return
     value = total / (t_dev * 1e-9)
