@@ -146,6 +146,43 @@ def byte_tokens(vocab):
     return toks + [(b"", NO_MERGE)] * (vocab - len(toks))
 
 
+def gpt2(dim, n_layers, n_heads, ffn_dim, vocab, ctx, seed=0, std=0.02, stop_tokens=True):
+    """A GPT-2-shaped model (LayerNorm with biases, learned positions, GELU MLP, biases on every
+    projection, tied head; the reference's "gpt2" arch flags) with N(0, std) weights (std "fan_in":
+    1/sqrt(inputs)); norm gains 1 + N(0, 0.1), every bias N(0, 0.02). Drawn in this order: embed,
+    pos_embed, norm, norm_b, then per layer attn_norm, attn_norm_b, ffn_norm, ffn_norm_b, wq, wk, wv,
+    bq, bk, bv, wo, bo, w_up, b_up, w_down, b_down."""
+    rng = np.random.default_rng(seed)
+    m = Model("gpt2", LAYERNORM | LEARNED_POS | GELU | TIED, dim, n_layers, n_heads, n_heads, ffn_dim, vocab, ctx, 10000.0, 1e-5)
+
+    def mat(rows, cols):
+        scale = np.float32(1 / np.sqrt(cols)) if std == "fan_in" else np.float32(std)
+        return (rng.standard_normal((rows, cols), dtype=np.float32) * scale).astype(np.float32)
+
+    def gain(n):
+        return (1 + rng.standard_normal(n, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
+
+    def bias(n):
+        return (rng.standard_normal(n, dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+
+    t = m.tensors
+    t["embed"] = mat(vocab, dim)
+    t["pos_embed"] = mat(ctx, dim)
+    t["norm"], t["norm_b"] = gain(dim), bias(dim)
+    for i in range(n_layers):
+        b = f"blk.{i}."
+        t[b + "attn_norm"], t[b + "attn_norm_b"] = gain(dim), bias(dim)
+        t[b + "ffn_norm"], t[b + "ffn_norm_b"] = gain(dim), bias(dim)
+        t[b + "wq"], t[b + "wk"], t[b + "wv"] = mat(dim, dim), mat(dim, dim), mat(dim, dim)
+        t[b + "bq"], t[b + "bk"], t[b + "bv"] = bias(dim), bias(dim), bias(dim)
+        t[b + "wo"], t[b + "bo"] = mat(dim, dim), bias(dim)
+        t[b + "w_up"], t[b + "b_up"] = mat(ffn_dim, dim), bias(ffn_dim)
+        t[b + "w_down"], t[b + "b_down"] = mat(dim, ffn_dim), bias(dim)
+    m.tokens = byte_tokens(vocab)
+    m.bos, m.eos = (256, 257) if stop_tokens else (-1, -1)
+    return m
+
+
 def llama(dim, n_layers, n_heads, n_kv_heads, ffn_dim, vocab, ctx, theta=10000.0, tied=True, seed=0, std=0.02,
           stop_tokens=True):
     """A Llama-shaped model with N(0, std) weights (std "fan_in": 1/sqrt(inputs)) drawn in this order:

@@ -69,6 +69,10 @@ int          o_generate_t(o_model *m, const int32_t *prompt, int n_prompt, int m
 // argmax when temp is not > 0; advances *rng only when it samples.
 int32_t      o_sample(const float *logits, int n, float temp, uint64_t *rng);
 
+// reference src/ops.c:20-27 and 53-56, exposed so tests can compare them with the reference's.
+void o_layernorm(float *y, const float *x, const float *w, const float *b, int n, float eps);
+void o_gelu(float *x, int n);
+
 // ---- libm expf, as the reference calls it (softmax, SiLU); exposed so tests can compare.
 float o_expf(float x);
 // The correctly rounded double evaluation used to build the GPU's exception list: returns the

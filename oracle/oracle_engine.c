@@ -176,18 +176,25 @@ int o_bos(const o_model *m) { return m->bos; }
 
 static void add(float *x, const float *y, int n) { for (int i = 0; i < n; i++) x[i] += y[i]; }
 
-// reference src/ops.c:20-27: sequential mean, sequential variance (fma), then (d*s)*w + b as one fma.
-static void layernorm(float *y, const float *x, const float *w, const float *b, int n, float eps) {
+// reference src/ops.c:20-27: sequential mean; sequential variance, its squares rounded on their own
+// over the part of the row the reference build vectorises (o_rmsnorm_fused_from, as in rmsnorm) and fused into
+// the sum in the tail; then (d*s)*w + b as one fma.
+void o_layernorm(float *y, const float *x, const float *w, const float *b, int n, float eps) {
     float mean = 0.0f, var = 0.0f;
     for (int i = 0; i < n; i++) mean += x[i];
     mean /= (float)n;
-    for (int i = 0; i < n; i++) { float d = x[i] - mean; var = fmaf(d, d, var); }
+    const int split = o_rmsnorm_fused_from(n);
+    for (int i = 0; i < n; i++) {
+        const float d = x[i] - mean;
+        if (i < split) { const float sq = d * d; var += sq; }
+        else var = fmaf(d, d, var);
+    }
     float s = 1.0f / sqrtf(var / (float)n + eps);
     for (int i = 0; i < n; i++) y[i] = fmaf((x[i] - mean) * s, w[i], b[i]);
 }
 
 // reference src/ops.c:53-56 (tanh approximation): x + 0.044715 x^3 contracts to one fma.
-static void gelu(float *x, int n) {
+void o_gelu(float *x, int n) {
     for (int i = 0; i < n; i++) {
         float v = x[i];
         float inner = fmaf((0.044715f * v) * v, v, v);
@@ -196,7 +203,7 @@ static void gelu(float *x, int n) {
 }
 
 static void norm(const o_model *m, float *y, const float *x, const float *w, const float *b) {
-    if (m->flags & F_LAYERNORM) layernorm(y, x, w, b, m->dim, m->eps);
+    if (m->flags & F_LAYERNORM) o_layernorm(y, x, w, b, m->dim, m->eps);
     else o_rmsnorm(y, x, w, m->dim, m->eps);
 }
 
@@ -231,7 +238,7 @@ const float *o_forward(o_model *m, int32_t tok, int pos, int want_logits) {
         norm(m, m->xb, m->x, L->ffn_norm, L->ffn_norm_b);
         gemv(m, m->h, &L->up, m->xb);
         if (L->b_up) add(m->h, L->b_up, m->ffn);
-        if (m->flags & F_GELU) gelu(m->h, m->ffn);
+        if (m->flags & F_GELU) o_gelu(m->h, m->ffn);
         else { gemv(m, m->gate, &L->gate, m->xb); o_silu_mul(m->h, m->gate, m->ffn); }
 
         gemv(m, m->down, &L->down, m->h);
@@ -313,7 +320,7 @@ const float *o_ref_forward(o_model *m, int32_t tok, int pos) {
         add(x, xb, dim);
         norm(m, xb, x, L->ffn_norm, L->ffn_norm_b);
         matvec(m->rhb, L->up_f, xb, L->b_up, ffn, dim);
-        if (m->flags & F_GELU) gelu(m->rhb, ffn);
+        if (m->flags & F_GELU) o_gelu(m->rhb, ffn);
         else { matvec(m->rg, L->gate_f, xb, NULL, ffn, dim); o_silu_mul(m->rhb, m->rg, ffn); }
         matvec(xb, L->down_f, m->rhb, L->b_down, dim, ffn);
         add(x, xb, dim);

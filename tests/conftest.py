@@ -57,6 +57,8 @@ def load_oracle():
         "o_generate": (i, [vp, C.POINTER(C.c_int32), i, i, vp, vp, C.POINTER(i), i]),
         "o_generate_t": (i, [vp, C.POINTER(C.c_int32), i, i, C.c_float, C.c_uint64, vp, vp, C.POINTER(i), i]),
         "o_sample": (C.c_int32, [vp, i, C.c_float, C.POINTER(C.c_uint64)]),
+        "o_layernorm": (None, [vp, vp, vp, vp, i, C.c_float]),
+        "o_gelu": (None, [vp, i]),
         "o_row_bytes": (C.c_size_t, [i, i]), "o_tile_bytes": (C.c_size_t, [i, i]),
         "o_pack_tile": (None, [vp, i, C.POINTER(vp), i]), "o_dequant_row": (None, [vp, i, vp, i]),
         "o_vec_prepare": (None, [C.POINTER(Vec), i, vp, i, vp]),
@@ -97,17 +99,18 @@ class OracleRun:
 
 @pytest.fixture(scope="session")
 def models(tmp_path_factory):
-    """Small seeded models: a GQA Llama with an untied head (head_dim 16) and an MHA Llama with a
-    tied head (head_dim 40), each in every dtype; weights scaled 1/sqrt(inputs) so activations
-    cover a wide range."""
+    """Small seeded models: a GQA Llama with an untied head (head_dim 16), an MHA Llama with a tied
+    head (head_dim 40) and a GPT-2 (LayerNorm, learned positions, GELU, biases; head_dim 24), each
+    in every dtype; weights scaled 1/sqrt(inputs) so activations cover a wide range."""
     out = tmp_path_factory.mktemp("models")
     specs = {
         "gqa": dict(dim=64, n_layers=2, n_heads=4, n_kv_heads=2, ffn_dim=128, vocab=300, ctx=96, tied=False, seed=1),
         "mha40": dict(dim=160, n_layers=2, n_heads=4, n_kv_heads=4, ffn_dim=96, vocab=320, ctx=96, tied=True, seed=2),
+        "gpt2s": dict(arch="gpt2", dim=96, n_layers=2, n_heads=4, ffn_dim=192, vocab=310, ctx=96, seed=3),
     }
     paths = {}
     for name, shape in specs.items():
-        m = synth.llama(**shape, std="fan_in", stop_tokens=False)
+        m = (synth.gpt2 if shape.get("arch") == "gpt2" else synth.llama)(**{k: v for k, v in shape.items() if k != "arch"}, std="fan_in", stop_tokens=False)
         for dt in DTYPES:
             p = out / f"{name}-{dt}.l3m"
             synth.write(m, dt, dt, p)

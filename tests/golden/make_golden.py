@@ -39,6 +39,7 @@ STEPS = 40
 SPECS = {   # must match tests/conftest.py `models`
     "gqa": dict(dim=64, n_layers=2, n_heads=4, n_kv_heads=2, ffn_dim=128, vocab=300, ctx=96, tied=False, seed=1),
     "mha40": dict(dim=160, n_layers=2, n_heads=4, n_kv_heads=4, ffn_dim=96, vocab=320, ctx=96, tied=True, seed=2),
+    "gpt2s": dict(arch="gpt2", dim=96, n_layers=2, n_heads=4, ffn_dim=192, vocab=310, ctx=96, seed=3),
 }
 DTYPES = ["f32", "bf16", "q8_0", "q4_0", "mxfp4"]
 
@@ -128,7 +129,7 @@ def main():
     hashes, arrays = {}, {}
     with tempfile.TemporaryDirectory() as tmp:
         for name, shape in SPECS.items():
-            m = synth.llama(**shape, std="fan_in", stop_tokens=False)
+            m = (synth.gpt2 if shape.get("arch") == "gpt2" else synth.llama)(**{k: v for k, v in shape.items() if k != "arch"}, std="fan_in", stop_tokens=False)
             for dt in DTYPES:
                 path = Path(tmp) / f"{name}-{dt}.l3m"
                 export.write(ref_model(m), dt, dt, path)

@@ -45,7 +45,7 @@ def test_writer_matches_reference_exporter(models):
 # ---- the oracle engine against the reference engine's recorded output
 
 @pytest.mark.parametrize("dt", DTYPES)
-@pytest.mark.parametrize("name", ["gqa", "mha40"])
+@pytest.mark.parametrize("name", ["gqa", "mha40", "gpt2s"])
 @pytest.mark.parametrize("path_kind", ["scalar1", "ref"])
 def test_oracle_matches_reference_engine(oracle, models, name, dt, path_kind):
     """Greedy tokens and the logits of every sampled position, bit for bit: the reference's scalar
@@ -62,7 +62,7 @@ SAMPLED = ((0.8, 7), (1.7, 123))
 
 
 @pytest.mark.parametrize("dt", DTYPES)
-@pytest.mark.parametrize("name", ["gqa", "mha40"])
+@pytest.mark.parametrize("name", ["gqa", "mha40", "gpt2s"])
 @pytest.mark.parametrize("path_kind", ["scalar1", "ref"])
 def test_oracle_sampling_matches_reference_engine(oracle, models, name, dt, path_kind):
     """Temperature sampling: the reference's token streams (one rank; its fp32 path) for two
@@ -186,7 +186,8 @@ def test_kernels_match_reference_scalar_table(ref, oracle, dtype):
 
 
 def test_ops_match_reference(ref, oracle):
-    """rmsnorm at every n % 8, RoPE, SiLU and attention, bit for bit (reference src/ops.c)."""
+    """rmsnorm and LayerNorm at every n % 8, RoPE, GELU, SiLU and attention, bit for bit (reference
+    src/ops.c)."""
     rng = np.random.default_rng(7)
     for n in list(range(1, 41)) + [288, 512, 576, 768]:
         for _ in range(20):
@@ -203,6 +204,20 @@ def test_ops_match_reference(ref, oracle):
             ref.l3m_rope(P(a), 9, hd, pos, C.c_float(10000.0))
             oracle.o_rope(P(b), 9, hd, pos, C.c_float(10000.0))
             assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    for n in list(range(1, 41)) + [96, 288, 576, 768]:
+        for _ in range(20):
+            x = (rng.standard_normal(n) * rng.uniform(0.01, 3)).astype(np.float32)
+            w = (1 + 0.1 * rng.standard_normal(n)).astype(np.float32)
+            bb = (0.02 * rng.standard_normal(n)).astype(np.float32)
+            a, b = np.zeros(n, np.float32), np.zeros(n, np.float32)
+            ref.l3m_layernorm(P(a), P(x), P(w), P(bb), n, C.c_float(1e-5))
+            oracle.o_layernorm(P(b), P(x), P(w), P(bb), n, C.c_float(1e-5))
+            assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), n
+    u = (rng.standard_normal(100000) * 3).astype(np.float32)
+    a, b = u.copy(), u.copy()
+    ref.l3m_gelu(P(a), 100000)
+    oracle.o_gelu(P(b), 100000)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
     g = (rng.standard_normal(50000) * 4).astype(np.float32)
     h = rng.standard_normal(50000).astype(np.float32)
     a, b = h.copy(), h.copy()
