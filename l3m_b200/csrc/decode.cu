@@ -31,7 +31,7 @@ namespace cg = cooperative_groups;
 namespace l3m {
 
 struct Smem {
-    float *x, *xb, *tmp, *y, *scores, *att, *red, *wa, *wf, *wh;
+    float *x, *xb, *tmp, *y, *scores, *att, *red, *wa, *wf, *wh, *wab, *wfb, *whb;
     float *xq, *xa, *xp, *xh, *xd, *xt;
     float2 *rope;
     uint16_t *kcur, *vcur, *kvbuf, *vtbuf;
@@ -54,6 +54,9 @@ __device__ __forceinline__ Smem carve(unsigned char *base, const DecodeArgs &a) 
     s.wa = (float *)(base + a.sm_wa);
     s.wf = (float *)(base + a.sm_wf);
     s.wh = (float *)(base + a.sm_wh);
+    s.wab = (float *)(base + a.sm_wab);
+    s.wfb = (float *)(base + a.sm_wfb);
+    s.whb = (float *)(base + a.sm_whb);
     s.xq = (float *)(base + a.sm_xq);
     s.xa = (float *)(base + a.sm_xa);
     s.xp = (float *)(base + a.sm_xp);
@@ -169,8 +172,14 @@ __device__ void prefetch_layer(const DecodeArgs &a, const LayerDev &L, const Rol
 // The norm weights of layer L and the RoPE row of position pos, into shared memory (asynchronous;
 // the top of the next layer waits for them).
 __device__ void stage_vectors(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s, int pos) {
-    if (role.qkv0 < role.qkv1) stage_f32(s.wa, L.attn_norm, a.dim);
-    if (role.ffn0 < role.ffn1) stage_f32(s.wf, L.ffn_norm, a.dim);
+    if (role.qkv0 < role.qkv1) {
+        stage_f32(s.wa, L.attn_norm, a.dim);
+        if (a.layernorm) stage_f32(s.wab, L.attn_norm_b, a.dim);
+    }
+    if (role.ffn0 < role.ffn1) {
+        stage_f32(s.wf, L.ffn_norm, a.dim);
+        if (a.layernorm) stage_f32(s.wfb, L.ffn_norm_b, a.dim);
+    }
     if (role.head0 >= 0 && a.rope && pos < a.ctx) stage_f32((float *)s.rope, (const float *)(a.rope + (size_t)pos * (a.hd / 2)), a.hd);
     cp_async_commit();
 }
@@ -256,8 +265,9 @@ __device__ __noinline__ void xwait(const DecodeArgs &a, const Smem &s, int k, ui
     if (threadIdx.x == 0) asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
 
-// x = embedding row of tok (reference src/engine.c:236, src/pack.c:55-62).
-__device__ __noinline__ void embed_row(const DecodeArgs &a, int tok, float *x) {
+// x = embedding row of tok, plus the learned position row when the file has one (reference
+// src/engine.c:236-237, src/pack.c:55-62).
+__device__ __noinline__ void embed_row(const DecodeArgs &a, int tok, int pos, float *x) {
     const uint8_t *row = a.embed + (size_t)tok * a.embed_row_bytes;
     for (int i = threadIdx.x; i < a.dim; i += blockDim.x) {
         float v;
@@ -280,6 +290,7 @@ __device__ __noinline__ void embed_row(const DecodeArgs &a, int tok, float *x) {
                 v = __fmul_rn(l3m_e8m0_half(ld_nc_u8(blk)), (float)l3m_mxfp4_value(nib));
             }
         }
+        if (a.pos_embed) v = __fadd_rn(v, __ldg(a.pos_embed + (size_t)pos * a.dim + i));
         x[i] = v;
     }
     __syncthreads();
@@ -300,9 +311,11 @@ __device__ __noinline__ void phase_qkv(const DecodeArgs &a, const LayerDev &L, c
                                        int l, int tslot) {
     if (role.head0 >= 0) {
         const uint16_t *kc = kcache(a, L, role.head0), *vc = vcache(a, L, role.head0);
-        rmsnorm_side(s.x, s.wa, a.dim, a.eps, s.xb, s.red, [&](int t, int nt) {
-            attend_prestage<true>(kc, vc, a.hd, a.vstride, pos, a.hd, s.kvbuf, s.vtbuf, a.attn_chunk, t, nt);
-        });
+        auto pre = [&](int t, int nt) { attend_prestage<true>(kc, vc, a.hd, a.vstride, pos, a.hd, s.kvbuf, s.vtbuf, a.attn_chunk, t, nt); };
+        if (a.layernorm) layernorm_side(s.x, s.wa, s.wab, a.dim, a.eps, s.xb, s.red, pre);
+        else rmsnorm_side(s.x, s.wa, a.dim, a.eps, s.xb, s.red, pre);
+    } else if (a.layernorm) {
+        layernorm_exact(s.x, s.wa, s.wab, a.dim, a.eps, s.xb, s.red);
     } else {
         rmsnorm_exact(s.x, s.wa, a.dim, a.eps, s.xb, s.tmp, s.red);
     }
@@ -383,14 +396,17 @@ __device__ __noinline__ void phase_ffn(const DecodeArgs &a, const LayerDev &L, c
     for (int i = threadIdx.x; i < a.dim; i += blockDim.x) s.x[i] = __fadd_rn(s.x[i], s.xp[i]);
     __syncthreads();
     if (role.ffn0 >= role.ffn1) return;
-    rmsnorm_exact(s.x, s.wf, a.dim, a.eps, s.xb, s.tmp, s.red);
+    if (a.layernorm) layernorm_exact(s.x, s.wf, s.wfb, a.dim, a.eps, s.xb, s.red);
+    else rmsnorm_exact(s.x, s.wf, a.dim, a.eps, s.xb, s.tmp, s.red);
     trace(a, tslot, pos, l, 7);
     const int nf = role.ffn1 - role.ffn0;
     prepare(L.dt_up, s.xb, a.dim, s.prep);
     trace(a, tslot, pos, l, 26);
     if (ns) stage_wait(a, s, par);
     trace(a, tslot, pos, l, 12);
-    if (!L.gate) {                                                        // up and gate packed per CTA: one pass
+    if (a.gelu) {                                                         // GPT-2: up only
+        matvec_exact(L.dt_up, L.up, a.dim, role.ffn0, role.ffn1, s.prep, s.scratch, a.scratch_pairs, s.y, s.w, ns);
+    } else if (!L.gate) {                                                 // up and gate packed per CTA: one pass
         matvec_exact(L.dt_up, L.up, a.dim, 2 * role.ffn0, 2 * role.ffn1, s.prep, s.scratch, a.scratch_pairs, s.y, s.w, ns);
     } else {
         matvec_exact(L.dt_up, L.up, a.dim, role.ffn0, role.ffn1, s.prep, s.scratch, a.scratch_pairs, s.y, s.w, ns);
@@ -405,7 +421,7 @@ __device__ __noinline__ void ffn_gate(const DecodeArgs &a, const LayerDev &L, co
     const int nf = role.ffn1 - role.ffn0, g0 = role.ffn0 * kTile, n = min(role.ffn1 * kTile, a.ffn) - g0;
     for (int o = threadIdx.x; o < n; o += blockDim.x) {
         const float up = L.b_up ? __fadd_rn(s.y[o], __ldg(L.b_up + g0 + o)) : s.y[o];
-        s.tmp[o] = silu_mul(up, s.y[nf * kTile + o], a.elist, a.eindex);
+        s.tmp[o] = a.gelu ? gelu_tanh(up) : silu_mul(up, s.y[nf * kTile + o], a.elist, a.eindex);
     }
     __syncthreads();
 }
@@ -626,7 +642,8 @@ __device__ __noinline__ void head_logits(const DecodeArgs &a, const Role &role, 
     float best = -INFINITY;
     int best_i = -1;
     if (role.voc0 < role.voc1) {
-        rmsnorm_exact(s.x, s.wh, a.dim, a.eps, s.xb, s.tmp, s.red);
+        if (a.layernorm) layernorm_exact(s.x, s.wh, s.whb, a.dim, a.eps, s.xb, s.red);
+        else rmsnorm_exact(s.x, s.wh, a.dim, a.eps, s.xb, s.tmp, s.red);
         trace(a, tslot, pos, a.n_layers, 3);
         prepare(a.dt_head, s.xb, a.dim, s.prep);
         trace(a, tslot, pos, a.n_layers, 4);
@@ -721,7 +738,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
     uint32_t tcount = 0;
     unsigned long long rng = a.rng;                                       // advanced identically in every CTA of cluster 0
     bool ok = true;
-    if (role.voc0 < role.voc1) stage_f32(s.wh, a.norm, a.dim);
+    if (role.voc0 < role.voc1) {
+        stage_f32(s.wh, a.norm, a.dim);
+        if (a.layernorm) stage_f32(s.whb, a.norm_b, a.dim);
+    }
     if (cta >= kClusterCtas) {                                            // the other clusters: head tiles only
         cp_async_commit();
         head_helper(a, role, s);
@@ -749,7 +769,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
         const bool last = pos >= a.n_prompt - 1;
         if (pos < a.n_prompt) tok = a.prompt[pos];
         const bool stop_after = last && (n_gen >= a.max_new || pos + 1 >= a.ctx);   // reference engine.c:322, 352
-        embed_row(a, tok, s.x);
+        embed_row(a, tok, pos, s.x);
         for (int l = 0; l < a.n_layers; l++) {
             const LayerDev &L = layers[l];
             cp_async_wait_all();                                          // this layer's norm weights and RoPE row
@@ -787,7 +807,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
             trace(a, tslot, pos, l, 4);
             if (role.wo0 < role.wo1) phase_wo(a, L, role, s, ns, wpar, pos, l, tslot);   // B
             if (ns) wpar ^= 1;
-            if (!L.gate) ns = stage_issue(s, L.dt_up, L.up, a.dim, 2 * role.ffn0, 2 * role.ffn1, s.w, a.w_bytes);
+            if (!L.gate && !a.gelu) ns = stage_issue(s, L.dt_up, L.up, a.dim, 2 * role.ffn0, 2 * role.ffn1, s.w, a.w_bytes);
             else ns = stage_issue(s, L.dt_up, L.up, a.dim, role.ffn0, role.ffn1, s.w, a.w_bytes);
             trace(a, tslot, pos, l, 28);
             if (role.wo0 < role.wo1) {

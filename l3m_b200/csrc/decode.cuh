@@ -8,6 +8,7 @@ struct alignas(16) LayerDev {
     const uint8_t *qkv;                 // rows: q of every head, then k of every kv head, then v
     const uint8_t *wo, *gate, *up, *down;   // gate NULL: up holds, per CTA, its up tiles then its gate tiles
     const float *attn_norm, *ffn_norm;
+    const float *attn_norm_b, *ffn_norm_b;  // LayerNorm biases (NULL for RMSNorm files)
     const float *bq, *bk, *bv, *bo, *b_up, *b_down;   // NULL when absent
     uint16_t *kc, *vc;                  // K [n_kv][ctx][hd], V [n_kv][hd][vstride] bf16
     int dt_qkv, dt_wo, dt_gate, dt_up, dt_down;
@@ -59,7 +60,9 @@ struct DecodeArgs {
     const uint8_t *embed;
     int dt_embed;
     long long embed_row_bytes;
-    const float *norm;
+    const float *norm, *norm_b;         // final norm gain (and LayerNorm bias)
+    int layernorm, gelu;                // GPT-2 family: LayerNorm instead of RMSNorm; GELU(up) instead of SiLU(gate) * up
+    const float *pos_embed;             // [ctx][dim] learned positions (NULL: RoPE)
     const float2 *rope;                 // [ctx][hd/2] {cos, sin}
     const uint32_t *elist, *eindex;     // libm expf exception list
     const Role *roles;
@@ -76,6 +79,7 @@ struct DecodeArgs {
     // shared memory layout, byte offsets
     int sm_x, sm_xb, sm_tmp, sm_q8, sm_scale, sm_sum, sm_xf, sm_y, sm_scores, sm_kv, sm_att, sm_red, sm_kvbuf, sm_vt, sm_scratch;
     int sm_wa, sm_wf, sm_wh, sm_rope;   // this layer's norm weights, the final norm, this position's RoPE row
+    int sm_wab, sm_wfb, sm_whb;         // the same norms' LayerNorm biases
     int sm_layers;                      // a copy of layers[0 .. n_layers)
     int sm_xq, sm_xa, sm_xp, sm_xh, sm_xd, sm_xt;   // exchanged vectors: qkv, attn, proj, h, down; xt: the sampled token
                                                     // (next, stop, ok) and, one-cluster launch, each CTA c's slot at 4 + 4c

@@ -222,7 +222,11 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
         layers[l].dt_qkv = r.dtype;
         off_wo[l] = pack_matrix(s, f, l3m_file_blk(f, l, "wo"), ref, &layers[l].dt_wo);
         const l3m_tensor *wu = l3m_file_blk(f, l, "w_up"), *wg = l3m_file_blk(f, l, "w_gate");
-        if (ref || wu->dtype == wg->dtype) {
+        if (!wg) {                                                                  // GELU MLP: up only
+            off_up[l] = pack_matrix(s, f, wu, ref, &layers[l].dt_up);
+            off_gate[l] = (size_t)-1;
+            layers[l].dt_gate = layers[l].dt_up;
+        } else if (ref || wu->dtype == wg->dtype) {
             // Up and gate in one matrix, each CTA's range back to back: [its up tiles][its gate tiles].
             Rows r;
             for (int c = 0; c < l3m::kClusterCtas; c++) {
@@ -266,14 +270,16 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     auto put_vec = [&](const l3m_tensor *t) -> long long {
         return t ? (long long)s.put(l3m_file_data(f, t), (size_t)t->nbytes) : -1;
     };
-    struct VecOffs { long long an, fn, bq, bk, bv, bo, bu, bd; };
+    struct VecOffs { long long an, fn, bq, bk, bv, bo, bu, bd, anb, fnb; };
     std::vector<VecOffs> vo(L);
     for (int l = 0; l < L; l++) {
         vo[l] = {put_vec(l3m_file_blk(f, l, "attn_norm")), put_vec(l3m_file_blk(f, l, "ffn_norm")), put_vec(l3m_file_blk(f, l, "bq")),
                  put_vec(l3m_file_blk(f, l, "bk")), put_vec(l3m_file_blk(f, l, "bv")), put_vec(l3m_file_blk(f, l, "bo")),
-                 put_vec(l3m_file_blk(f, l, "b_up")), put_vec(l3m_file_blk(f, l, "b_down"))};
+                 put_vec(l3m_file_blk(f, l, "b_up")), put_vec(l3m_file_blk(f, l, "b_down")), put_vec(l3m_file_blk(f, l, "attn_norm_b")),
+                 put_vec(l3m_file_blk(f, l, "ffn_norm_b"))};
     }
-    long long off_norm = put_vec(l3m_file_tensor(f, "norm"));
+    long long off_norm = put_vec(l3m_file_tensor(f, "norm")), off_norm_b = put_vec(l3m_file_tensor(f, "norm_b"));
+    long long off_pos = put_vec(l3m_file_tensor(f, "pos_embed"));           // f32 [ctx][dim] (GPT-2 family)
     g.arena_bytes = s.buf.size();
 
     if (!cuda_ok(cudaMalloc(&g.arena, g.arena_bytes), "weights")) return false;
@@ -296,6 +302,7 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
         d.gate = off_gate[l] == (size_t)-1 ? nullptr : g.arena + off_gate[l];
         d.down = g.arena + off_down[l];
         d.attn_norm = A(vo[l].an); d.ffn_norm = A(vo[l].fn);
+        d.attn_norm_b = A(vo[l].anb); d.ffn_norm_b = A(vo[l].fnb);
         d.bq = A(vo[l].bq); d.bk = A(vo[l].bk); d.bv = A(vo[l].bv); d.bo = A(vo[l].bo); d.b_up = A(vo[l].bu); d.b_down = A(vo[l].bd);
         d.kc = g.kv + (size_t)l * (k_per + v_per);
         d.vc = d.kc + k_per;
@@ -338,6 +345,10 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     a.head = g.arena + off_head; a.dt_head = dt_head;
     a.embed = g.arena + off_embed; a.dt_embed = dt_embed; a.embed_row_bytes = (long long)emb_row;
     a.norm = A(off_norm);
+    a.norm_b = A(off_norm_b);
+    a.layernorm = (m->flags & L3M_F_LAYERNORM) ? 1 : 0;
+    a.gelu = (m->flags & L3M_F_GELU) ? 1 : 0;
+    a.pos_embed = (m->flags & L3M_F_LEARNED_POS) ? A(off_pos) : nullptr;
     a.rope = (m->flags & L3M_F_LEARNED_POS) ? nullptr : g.rope;
     if (l3m_expf_tables(&a.elist, &a.eindex)) { fprintf(stderr, "l3m: %s\n", l3m_cuda_error()); return false; }
     a.trace_cta[0] = a.trace_cta[1] = -1;
@@ -380,6 +391,9 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     a.sm_wa = take(dim * 4);
     a.sm_wf = take(dim * 4);
     a.sm_wh = take(dim * 4);
+    a.sm_wab = take(dim * 4);
+    a.sm_wfb = take(dim * 4);
+    a.sm_whb = take(dim * 4);
     a.sm_rope = take(hd / 2 * 8);
     a.sm_layers = take(L * (int)sizeof(l3m::LayerDev));
     a.attn_chunk = std::min(m->ctx, 256);
@@ -490,8 +504,6 @@ L3M_API l3m_model *l3m_load(const char *path, const l3m_opts *opts) {
     if (l3m_file_open(&m->f, path)) { delete m; return nullptr; }
     const l3m_header *h = m->f.h;
     m->flags = h->flags;
-    if (m->flags & (L3M_F_LAYERNORM | L3M_F_GELU | L3M_F_LEARNED_POS))
-        return fail(m, "this GPU build runs Llama-family files (RMSNorm, RoPE, SiLU gate); LayerNorm, GELU and learned positions are not built");
     m->dim = (int)h->dim; m->n_heads = (int)h->n_heads; m->n_kv = (int)h->n_kv_heads; m->hpk = m->n_heads / m->n_kv;
     m->hd = m->dim / m->n_heads; m->ffn = (int)h->ffn_dim; m->vocab = (int)h->vocab; m->n_layers = (int)h->n_layers;
     m->ctx = std::min((int)h->ctx, o.ctx > 0 ? o.ctx : kDefaultCtx);

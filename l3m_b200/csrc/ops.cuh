@@ -380,6 +380,59 @@ __device__ __forceinline__ void rmsnorm_side(const float *x, const float *w, int
     __syncthreads();
 }
 
+// The variance chain of LayerNorm (reference src/ops.c:24 as built): d = x[i] - mean; the squares
+// rounded on their own up to split (the vectorised part of the reference build), fused after.
+__device__ __forceinline__ float chain_var(const float *v, float mean, int n, int split) {
+    float acc = 0.0f;
+    int i = 0;
+    const float4 *v4 = (const float4 *)v;
+    const int nf = split & ~3;
+    for (; i < nf; i += 4) {
+        const float4 r = v4[i >> 2];
+        const float e[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int h = 0; h < 4; h++) {
+            const float d = __fsub_rn(e[h], mean);
+            acc = __fadd_rn(acc, __fmul_rn(d, d));
+        }
+    }
+    for (; i < split; i++) { const float d = __fsub_rn(v[i], mean); acc = __fadd_rn(acc, __fmul_rn(d, d)); }
+    for (; i < n; i++) { const float d = __fsub_rn(v[i], mean); acc = __fmaf_rn(d, d, acc); }
+    return acc;
+}
+
+// LayerNorm (reference src/ops.c:20-27): sequential mean, the variance chain above, s = 1/sqrt(var/n
+// + eps), y = fma((x - mean) * s, w, b). Thread 0 runs the chains; side(t, nt) as in rmsnorm_side.
+template <class Side>
+__device__ __forceinline__ void layernorm_side(const float *x, const float *w, const float *b, int n, float eps, float *y, float *red,
+                                               const Side &side) {
+    const int tid = threadIdx.x, nth = blockDim.x;
+    if (tid == 0) {
+        const float mean = __fdiv_rn(chain_sum<false>(x, n, 0.0f), (float)n);
+        const float var = chain_var(x, mean, n, fused_from(n));
+        red[0] = mean;
+        red[1] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(var, (float)n), eps)));
+    } else if (tid >= 32) {
+        side(tid - 32, nth - 32);
+    }
+    __syncthreads();
+    const float mean = red[0], sc = red[1];
+    for (int i = tid; i < n; i += nth) y[i] = __fmaf_rn(__fmul_rn(__fsub_rn(x[i], mean), sc), w[i], b[i]);
+    __syncthreads();
+}
+
+static __device__ __noinline__ void layernorm_exact(const float *x, const float *w, const float *b, int n, float eps, float *y, float *red) {
+    layernorm_side(x, w, b, n, eps, y, red, NoSide());
+}
+
+// GELU, tanh form (reference src/ops.c:53-56 as built: x + 0.044715 x^3 is one fma). tanhf is the
+// device's: within a few ulp of the host libm's (which follows fdlibm's expm1f-based formulation),
+// so GELU outputs, unlike every other step, are not bit-identical to the reference's.
+__device__ __forceinline__ float gelu_tanh(float v) {
+    const float inner = __fmaf_rn(__fmul_rn(__fmul_rn(0.044715f, v), v), v, v);
+    return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, tanhf(__fmul_rn(0.7978845608f, inner))));
+}
+
 static __device__ __noinline__ void rmsnorm_exact(const float *x, const float *w, int n, float eps, float *y, float *tmp, float *red) {
     (void)tmp;
     rmsnorm_side(x, w, n, eps, y, red, NoSide());
