@@ -64,6 +64,12 @@ L3M_API int          l3m_perf_read(l3m_model *m, l3m_perf *out);   // since the 
 L3M_API int          l3m_parse_cpus(const char *list, int *cpus, int max);   // "0-7,12" -> count, -1 on error
 L3M_API void         l3m_print_hw(FILE *out);                        // the GPUs, their L2 and persisting budgets
 
+// No counterpart in the reference: copy the .l3m file `in` to `out` with a packed section appended
+// (every matrix the GPU streams, already in its tile order, as extra tensors named "b200v1.*" that a
+// v1 reader ignores), so that l3m_load copies those bytes instead of repacking rows. Host only (no
+// GPU); 0 on success, -1 with the reason on stderr.
+L3M_API int          l3m_write_packed(const char *in, const char *out);
+
 #ifdef __cplusplus
 }
 #endif

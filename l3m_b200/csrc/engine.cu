@@ -153,13 +153,6 @@ size_t pack(Stage &s, Rows &rows) {
     return off;
 }
 
-size_t pack_matrix(Stage &s, const l3m_file *f, const l3m_tensor *t, bool to_f32, int *dtype) {
-    Rows r;
-    for (int i = 0; i < (int)t->shape[0]; i++) r.add(f, t, i, to_f32);
-    *dtype = r.dtype;
-    return pack(s, r);
-}
-
 // RoPE coefficients with the reference's exact expressions and this host's libm (src/ops.c:29-33).
 std::vector<float2> rope_table(int ctx, int hd, float theta) {
     std::vector<float2> t((size_t)ctx * (hd / 2));
@@ -178,6 +171,93 @@ void split(int n, int parts, int r, int *lo, int *hi) {   // reference src/engin
 }
 
 int align16(int x) { return (x + 15) & ~15; }
+
+// The matrices the decode kernel streams, packed into 16-row tiles in the order and grouping the
+// kernel reads them: per layer the flat q|k|v rows, wo, up and gate (one matrix holding, per CTA of
+// the cluster, its up tiles then its gate tiles, when they share a dtype; up alone for a GELU MLP),
+// down; then the head. A file may carry any of them already packed ("b200v1." + the name below,
+// written by l3m_write_packed): those bytes are copied instead of packed from rows.
+struct Streamed {
+    std::vector<size_t> off_qkv, off_wo, off_up, off_gate, off_down;   // off_gate (size_t)-1: none (in up, or GELU)
+    std::vector<int> dt_qkv, dt_wo, dt_up, dt_gate, dt_down;
+    size_t off_head = 0;
+    int dt_head = 0;
+    struct Entry { std::string name; size_t off, rows; int dtype, k; };
+    std::vector<Entry> entries;                  // every packed matrix, for the writer
+};
+constexpr const char *kPackedPrefix = "b200v1.";
+
+size_t pack_rows(Stage &s, Rows &r, const l3m_file *f, const std::string &name, Streamed &out, bool ref, int *dtype) {
+    const size_t rows = (size_t)tiles_of((int)r.ptr.size()) * L3M_TILE, tb = l3m_tile_bytes(r.dtype, r.k);
+    *dtype = r.dtype;
+    const l3m_tensor *pt = ref ? nullptr : l3m_file_tensor(f, (kPackedPrefix + name).c_str());
+    size_t off;
+    if (pt && (int)pt->dtype == r.dtype && pt->ndim == 2 && pt->shape[0] == rows && (int)pt->shape[1] == r.k && pt->nbytes == rows / L3M_TILE * tb)
+        off = s.put(l3m_file_data(f, pt), (size_t)pt->nbytes);
+    else
+        off = pack(s, r);
+    out.entries.push_back({name, off, rows, r.dtype, r.k});
+    return off;
+}
+
+void pack_streamed(const l3m_file *f, bool ref, int n_heads, int n_kv, int hd, Stage &s, Streamed &out) {
+    const int L = (int)f->h->n_layers, ffn = (int)f->h->ffn_dim;
+    for (auto *v : {&out.off_qkv, &out.off_wo, &out.off_up, &out.off_gate, &out.off_down}) v->assign(L, 0);
+    for (auto *v : {&out.dt_qkv, &out.dt_wo, &out.dt_up, &out.dt_gate, &out.dt_down}) v->assign(L, 0);
+    for (int l = 0; l < L; l++) {
+        const std::string b = "blk." + std::to_string(l) + ".";
+        const l3m_tensor *wq = l3m_file_blk(f, l, "wq"), *wk = l3m_file_blk(f, l, "wk"), *wv = l3m_file_blk(f, l, "wv");
+        Rows r;                                                                     // q of every head, then k, then v
+        for (int i = 0; i < n_heads * hd; i++) r.add(f, wq, i, ref);
+        for (int i = 0; i < n_kv * hd; i++) r.add(f, wk, i, ref);
+        for (int i = 0; i < n_kv * hd; i++) r.add(f, wv, i, ref);
+        out.off_qkv[l] = pack_rows(s, r, f, b + "qkv", out, ref, &out.dt_qkv[l]);
+        {
+            Rows ro;
+            const l3m_tensor *wo = l3m_file_blk(f, l, "wo");
+            for (int i = 0; i < (int)wo->shape[0]; i++) ro.add(f, wo, i, ref);
+            out.off_wo[l] = pack_rows(s, ro, f, b + "wo", out, ref, &out.dt_wo[l]);
+        }
+        const l3m_tensor *wu = l3m_file_blk(f, l, "w_up"), *wg = l3m_file_blk(f, l, "w_gate");
+        if (!wg) {                                                                  // GELU MLP: up only
+            Rows ru;
+            for (int i = 0; i < ffn; i++) ru.add(f, wu, i, ref);
+            out.off_up[l] = pack_rows(s, ru, f, b + "up", out, ref, &out.dt_up[l]);
+            out.off_gate[l] = (size_t)-1;
+            out.dt_gate[l] = out.dt_up[l];
+        } else if (ref || wu->dtype == wg->dtype) {
+            // Up and gate in one matrix, each CTA's range back to back: [its up tiles][its gate tiles].
+            Rows ru;
+            for (int c = 0; c < l3m::kClusterCtas; c++) {
+                int t0, t1;
+                split(tiles_of(ffn), l3m::kClusterCtas, c, &t0, &t1);
+                for (const l3m_tensor *t : {wu, wg}) {
+                    for (int i = t0 * L3M_TILE; i < t1 * L3M_TILE; i++) {
+                        if (i < ffn) ru.add(f, t, i, ref);
+                        else ru.ptr.push_back(nullptr);
+                    }
+                }
+            }
+            out.off_up[l] = pack_rows(s, ru, f, b + "upgate16", out, ref, &out.dt_up[l]);
+            out.off_gate[l] = (size_t)-1;
+            out.dt_gate[l] = out.dt_up[l];
+        } else {
+            Rows ru, rg;
+            for (int i = 0; i < ffn; i++) ru.add(f, wu, i, ref);
+            for (int i = 0; i < ffn; i++) rg.add(f, wg, i, ref);
+            out.off_up[l] = pack_rows(s, ru, f, b + "up", out, ref, &out.dt_up[l]);
+            out.off_gate[l] = pack_rows(s, rg, f, b + "gate", out, ref, &out.dt_gate[l]);
+        }
+        Rows rd;
+        const l3m_tensor *wd = l3m_file_blk(f, l, "w_down");
+        for (int i = 0; i < (int)wd->shape[0]; i++) rd.add(f, wd, i, ref);
+        out.off_down[l] = pack_rows(s, rd, f, b + "down", out, ref, &out.dt_down[l]);
+    }
+    const l3m_tensor *head = l3m_file_tensor(f, (f->h->flags & L3M_F_TIED) ? "embed" : "lm_head");
+    Rows rh;
+    for (int i = 0; i < (int)head->shape[0]; i++) rh.add(f, head, i, ref);
+    out.off_head = pack_rows(s, rh, f, "head", out, ref, &out.dt_head);
+}
 
 // Build everything one GPU holds and fill its decode arguments.
 bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
@@ -210,47 +290,16 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     // Streamed weights first (one contiguous range for the persisting window), then the rest.
     Stage s;
     std::vector<l3m::LayerDev> layers(L);
-    std::vector<size_t> off_qkv(L), off_wo(L), off_gate(L), off_up(L), off_down(L);
+    Streamed sw;
+    pack_streamed(f, ref, m->n_heads, m->n_kv, hd, s, sw);
     const int n_qkv = (m->n_heads + 2 * m->n_kv) * hd;
+    const std::vector<size_t> &off_qkv = sw.off_qkv, &off_wo = sw.off_wo, &off_gate = sw.off_gate, &off_up = sw.off_up, &off_down = sw.off_down;
     for (int l = 0; l < L; l++) {
-        const l3m_tensor *wq = l3m_file_blk(f, l, "wq"), *wk = l3m_file_blk(f, l, "wk"), *wv = l3m_file_blk(f, l, "wv");
-        Rows r;                                                                     // q of every head, then k, then v
-        for (int i = 0; i < m->n_heads * hd; i++) r.add(f, wq, i, ref);
-        for (int i = 0; i < m->n_kv * hd; i++) r.add(f, wk, i, ref);
-        for (int i = 0; i < m->n_kv * hd; i++) r.add(f, wv, i, ref);
-        off_qkv[l] = pack(s, r);
-        layers[l].dt_qkv = r.dtype;
-        off_wo[l] = pack_matrix(s, f, l3m_file_blk(f, l, "wo"), ref, &layers[l].dt_wo);
-        const l3m_tensor *wu = l3m_file_blk(f, l, "w_up"), *wg = l3m_file_blk(f, l, "w_gate");
-        if (!wg) {                                                                  // GELU MLP: up only
-            off_up[l] = pack_matrix(s, f, wu, ref, &layers[l].dt_up);
-            off_gate[l] = (size_t)-1;
-            layers[l].dt_gate = layers[l].dt_up;
-        } else if (ref || wu->dtype == wg->dtype) {
-            // Up and gate in one matrix, each CTA's range back to back: [its up tiles][its gate tiles].
-            Rows r;
-            for (int c = 0; c < l3m::kClusterCtas; c++) {
-                int t0, t1;
-                split(tiles_of(ffn), l3m::kClusterCtas, c, &t0, &t1);
-                for (const l3m_tensor *t : {wu, wg}) {
-                    for (int i = t0 * L3M_TILE; i < t1 * L3M_TILE; i++) {
-                        if (i < ffn) r.add(f, t, i, ref);
-                        else r.ptr.push_back(nullptr);
-                    }
-                }
-            }
-            off_up[l] = pack(s, r);
-            off_gate[l] = (size_t)-1;
-            layers[l].dt_up = layers[l].dt_gate = r.dtype;
-        } else {
-            off_up[l] = pack_matrix(s, f, wu, ref, &layers[l].dt_up);
-            off_gate[l] = pack_matrix(s, f, wg, ref, &layers[l].dt_gate);
-        }
-        off_down[l] = pack_matrix(s, f, l3m_file_blk(f, l, "w_down"), ref, &layers[l].dt_down);
+        layers[l].dt_qkv = sw.dt_qkv[l]; layers[l].dt_wo = sw.dt_wo[l]; layers[l].dt_up = sw.dt_up[l];
+        layers[l].dt_gate = sw.dt_gate[l]; layers[l].dt_down = sw.dt_down[l];
     }
-    const l3m_tensor *head = l3m_file_tensor(f, (m->flags & L3M_F_TIED) ? "embed" : "lm_head");
-    int dt_head = 0;
-    size_t off_head = pack_matrix(s, f, head, ref, &dt_head);
+    const int dt_head = sw.dt_head;
+    const size_t off_head = sw.off_head;
     g.weight_bytes = s.buf.size();
     const l3m_tensor *emb = l3m_file_tensor(f, "embed");
     int dt_embed = (int)emb->dtype;
@@ -497,6 +546,63 @@ bool place_in_l2(l3m_model *m, Gpu &g, const l3m_opts &o, bool *over) {
 }  // namespace
 
 extern "C" {
+
+// Write `out`: the file `in` unchanged, then every streamed matrix packed as the decode kernel reads
+// it ("b200v1." tensors, whose bytes equal a row-major matrix of the same shape and dtype, so a v1
+// reader accepts and ignores them), then a new table of contents; the header's tensor count and
+// table offset are updated. The written file is read back and must pack to the same bytes.
+L3M_API int l3m_write_packed(const char *in, const char *out) {
+    l3m_file f;
+    if (l3m_file_open(&f, in)) return -1;
+    const l3m_header *h = f.h;
+    const int hd = (int)(h->dim / h->n_heads);
+    Stage s;
+    Streamed sw;
+    pack_streamed(&f, false, (int)h->n_heads, (int)h->n_kv_heads, hd, s, sw);
+    std::vector<l3m_tensor> toc;
+    for (uint32_t i = 0; i < h->n_tensors; i++)
+        if (strncmp(f.toc[i].name, kPackedPrefix, strlen(kPackedPrefix))) toc.push_back(f.toc[i]);
+    FILE *o = fopen(out, "wb");
+    bool ok = o && fwrite(f.map, 1, f.size, o) == f.size;
+    size_t pos = f.size;
+    auto pad = [&](size_t a) {
+        static const uint8_t z[64] = {0};
+        const size_t n = (a - pos % a) % a;
+        ok = ok && fwrite(z, 1, n, o) == n;
+        pos += n;
+    };
+    for (const Streamed::Entry &e : sw.entries) {
+        pad(64);
+        l3m_tensor t = {};
+        snprintf(t.name, sizeof t.name, "%s%s", kPackedPrefix, e.name.c_str());
+        t.dtype = (uint32_t)e.dtype;
+        t.ndim = 2;
+        t.shape[0] = e.rows;
+        t.shape[1] = (uint64_t)e.k;
+        t.offset = pos;
+        t.nbytes = e.rows / L3M_TILE * l3m_tile_bytes(e.dtype, e.k);
+        ok = ok && fwrite(s.buf.data() + e.off, 1, t.nbytes, o) == t.nbytes;
+        pos += t.nbytes;
+        toc.push_back(t);
+    }
+    pad(8);
+    l3m_header nh = *h;
+    nh.n_tensors = (uint32_t)toc.size();
+    nh.toc_offset = pos;
+    ok = ok && fwrite(toc.data(), sizeof(l3m_tensor), toc.size(), o) == toc.size();
+    ok = ok && fseek(o, 0, SEEK_SET) == 0 && fwrite(&nh, sizeof nh, 1, o) == 1;
+    if (o) ok = fclose(o) == 0 && ok;
+    l3m_file_close(&f);
+    if (!ok) { fprintf(stderr, "l3m: %s: write failed\n", out); return -1; }
+    l3m_file g;                                                       // read back: the packed tensors must be taken as they are
+    if (l3m_file_open(&g, out)) return -1;
+    Stage s2;
+    Streamed sw2;
+    pack_streamed(&g, false, (int)g.h->n_heads, (int)g.h->n_kv_heads, hd, s2, sw2);
+    l3m_file_close(&g);
+    if (s2.buf != s.buf) { fprintf(stderr, "l3m: %s: the packed section does not read back as written\n", out); return -1; }
+    return 0;
+}
 
 L3M_API l3m_model *l3m_load(const char *path, const l3m_opts *opts) {
     l3m_opts o = opts ? *opts : l3m_opts{};

@@ -109,6 +109,17 @@ def test_gpt2_family_within_tolerance(gpu, oracle, models, dt, reference):
     assert (err <= tol).all(), f"max |diff| {err.max()} at position {np.argmax(err.max(axis=1))}"
 
 
+@pytest.mark.parametrize("name,dt", [("gqa", "q8_0"), ("mha40", "bf16"), ("gpt2s", "q4_0")])
+def test_packed_section_loads_the_same(gpu, models, tmp_path, name, dt):
+    """l3m_load of a file with the packed section (l3m_write_packed) copies those tiles: the same
+    tokens and logits as from the rows."""
+    src, dst = models[(name, dt)], tmp_path / "packed.l3m"
+    assert l3m_b200.lib().l3m_write_packed(str(src).encode(), str(dst).encode()) == 0
+    _, t0, l0 = gpu_run(src, PROMPT, 24)
+    _, t1, l1 = gpu_run(dst, PROMPT, 24)
+    assert t0 == t1 and np.array_equal(l0.view(np.uint32), l1.view(np.uint32))
+
+
 def test_max_new_zero_gives_prompt_logits(gpu, oracle, models):
     path = models[("gqa", "q8_0")]
     m = l3m_b200.Model(path, force=True)

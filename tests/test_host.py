@@ -266,3 +266,55 @@ def test_long_piece_is_not_quadratic(tok_bin, tmp_path):
     t = time.perf_counter()
     assert encode(tok_bin, p, ["a" * (1 << 20)])[0] == [262] * (1 << 19)
     assert time.perf_counter() - t < 10
+
+
+# ---- the packed section (l3m_write_packed)
+
+REF_LIB = ROOT / "oracle" / "_ref" / "libl3m.so"
+
+
+def _ref_generate(path, n):
+    """Greedy tokens and last logits from the reference's own library (one core), or None."""
+    if not REF_LIB.exists():
+        pytest.skip("oracle/_ref not built")
+    lib = C.CDLL(str(REF_LIB))
+
+    class Opts(C.Structure):
+        _fields_ = [("cpus", C.POINTER(C.c_int)), ("n_cpus", C.c_int), ("ctx", C.c_int), ("reference", C.c_int),
+                    ("force", C.c_int), ("verbose", C.c_int), ("cold", C.c_int)]
+    lib.l3m_load.restype, lib.l3m_load.argtypes = C.c_void_p, [C.c_char_p, C.POINTER(Opts)]
+    lib.l3m_generate.argtypes = [C.c_void_p, C.POINTER(C.c_int32), C.c_int, C.c_int, C.c_float, C.c_uint64, C.c_void_p, C.c_void_p]
+    lib.l3m_logits.restype, lib.l3m_logits.argtypes = C.POINTER(C.c_float), [C.c_void_p]
+    lib.l3m_vocab.argtypes = lib.l3m_free.argtypes = [C.c_void_p]
+    one = (C.c_int * 1)(0)
+    m = lib.l3m_load(str(path).encode(), C.byref(Opts(cpus=one, n_cpus=1, force=1)))
+    assert m, f"the reference could not load {path}"
+    toks = []
+    cb = C.CFUNCTYPE(C.c_int, C.c_int32, C.c_void_p)(lambda t, u: toks.append(t) or 1)
+    pr = (C.c_int32 * 4)(5, 77, 200, 3)
+    lib.l3m_generate(m, pr, 4, n, 0.0, 0, cb, None)
+    lg = np.ctypeslib.as_array(lib.l3m_logits(m), shape=(lib.l3m_vocab(m),)).copy()
+    lib.l3m_free(m)
+    return toks, lg
+
+
+@pytest.mark.parametrize("name", ["gqa", "gpt2s"])
+@pytest.mark.parametrize("dt", ["f32", "q8_0", "mxfp4"])
+def test_packed_section_is_v1_compatible(lib, models, tmp_path, name, dt):
+    """A file with the packed section still reads as v1: the reference's own loader takes it and
+    generates the same tokens and logits; packing it again replaces the section (read back checked
+    by the writer itself)."""
+    src, dst, again = models[(name, dt)], tmp_path / "packed.l3m", tmp_path / "again.l3m"
+    assert lib.l3m_write_packed(str(src).encode(), str(dst).encode()) == 0
+    assert dst.stat().st_size > src.stat().st_size
+    t0, l0 = _ref_generate(src, 12)
+    t1, l1 = _ref_generate(dst, 12)
+    assert t0 == t1 and np.array_equal(l0.view(np.uint32), l1.view(np.uint32))
+    assert lib.l3m_write_packed(str(dst).encode(), str(again).encode()) == 0
+    assert again.stat().st_size > dst.stat().st_size          # the old section stays as dead bytes
+
+
+def test_packed_writer_refuses_bad_input(lib, tmp_path):
+    bad = tmp_path / "bad.l3m"
+    bad.write_bytes(b"not a model")
+    assert lib.l3m_write_packed(str(bad).encode(), str(tmp_path / "o.l3m").encode()) == -1
