@@ -20,6 +20,7 @@
 // prefetched into L2 a layer ahead; each layer's norm weights and RoPE row are copied into shared
 // memory while the previous layer runs. No CTA ever spins on memory: the only waits are cluster
 // barriers, which every CTA reaches the same number of times.
+#include <algorithm>
 #include <cstdio>
 #include <cooperative_groups.h>
 #include "ops.cuh"
@@ -170,15 +171,16 @@ __device__ void prefetch_layer(const DecodeArgs &a, const LayerDev &L, const Rol
 }
 
 // The norm weights of layer L and the RoPE row of position pos, into shared memory (asynchronous;
-// the top of the next layer waits for them).
+// the top of the next layer waits for them). GPT2: the LayerNorm biases too (GPT-2 family).
+template <bool GPT2>
 __device__ void stage_vectors(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s, int pos) {
     if (role.qkv0 < role.qkv1) {
         stage_f32(s.wa, L.attn_norm, a.dim);
-        if (a.layernorm) stage_f32(s.wab, L.attn_norm_b, a.dim);
+        if (GPT2 && a.layernorm) stage_f32(s.wab, L.attn_norm_b, a.dim);
     }
     if (role.ffn0 < role.ffn1) {
         stage_f32(s.wf, L.ffn_norm, a.dim);
-        if (a.layernorm) stage_f32(s.wfb, L.ffn_norm_b, a.dim);
+        if (GPT2 && a.layernorm) stage_f32(s.wfb, L.ffn_norm_b, a.dim);
     }
     if (role.head0 >= 0 && a.rope && pos < a.ctx) stage_f32((float *)s.rope, (const float *)(a.rope + (size_t)pos * (a.hd / 2)), a.hd);
     cp_async_commit();
@@ -209,18 +211,25 @@ __device__ __forceinline__ int stage_count(int dtype, int k, int t0, int t1, int
 }
 
 // Every thread, after a __syncthreads that ends every read of dst: start the copy of tiles
-// [t0, t0 + n) to dst (n = stage_count(...)); returns n.
-__device__ __forceinline__ int stage_issue(const Smem &s, int dtype, const uint8_t *tiles, int k, int t0, int t1, uint8_t *dst, int cap) {
+// [t0, t0 + n) to dst (n = stage_count(...)); returns n. cold: with an L2 evict-first policy.
+__device__ __forceinline__ int stage_issue(const Smem &s, int dtype, const uint8_t *tiles, int k, int t0, int t1, uint8_t *dst, int cap,
+                                           int cold = 0) {
     const int n = stage_count(dtype, k, t0, t1, cap);
     if (n > 0 && threadIdx.x == kPrefetchThread) {
         const size_t tb = tile_bytes(dtype, k);
         const uint32_t bytes = (uint32_t)(n * tb), bar = smem_addr(s.wbar);
         const uint8_t *src = tiles + (size_t)t0 * tb;
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+        uint64_t policy = 0;
+        if (cold) asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
         for (uint32_t o = 0; o < bytes; o += kStageChunk) {
             const uint32_t c = min(bytes - o, kStageChunk);
-            asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                         ::"r"(smem_addr(dst + o)), "l"(src + o), "r"(c), "r"(bar) : "memory");
+            if (cold)
+                asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+                             ::"r"(smem_addr(dst + o)), "l"(src + o), "r"(c), "r"(bar), "l"(policy) : "memory");
+            else
+                asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                             ::"r"(smem_addr(dst + o)), "l"(src + o), "r"(c), "r"(bar) : "memory");
         }
     }
     return n;
@@ -267,6 +276,7 @@ __device__ __noinline__ void xwait(const DecodeArgs &a, const Smem &s, int k, ui
 
 // x = embedding row of tok, plus the learned position row when the file has one (reference
 // src/engine.c:236-237, src/pack.c:55-62).
+template <bool GPT2>
 __device__ __noinline__ void embed_row(const DecodeArgs &a, int tok, int pos, float *x) {
     const uint8_t *row = a.embed + (size_t)tok * a.embed_row_bytes;
     for (int i = threadIdx.x; i < a.dim; i += blockDim.x) {
@@ -290,7 +300,7 @@ __device__ __noinline__ void embed_row(const DecodeArgs &a, int tok, int pos, fl
                 v = __fmul_rn(l3m_e8m0_half(ld_nc_u8(blk)), (float)l3m_mxfp4_value(nib));
             }
         }
-        if (a.pos_embed) v = __fadd_rn(v, __ldg(a.pos_embed + (size_t)pos * a.dim + i));
+        if (GPT2 && a.pos_embed) v = __fadd_rn(v, __ldg(a.pos_embed + (size_t)pos * a.dim + i));
         x[i] = v;
     }
     __syncthreads();
@@ -306,15 +316,16 @@ __device__ __forceinline__ const uint16_t *vcache(const DecodeArgs &a, const Lay
 }
 
 // A head CTA's warps 1.. start the K/V copies of its attention (attend_prestage) while warp 0 runs
-// the serial part of the rmsnorm.
+// the serial part of the rmsnorm (GPT2: the LayerNorm).
+template <bool GPT2>
 __device__ __noinline__ void phase_qkv(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s, int ns, uint32_t par, int pos,
                                        int l, int tslot) {
     if (role.head0 >= 0) {
         const uint16_t *kc = kcache(a, L, role.head0), *vc = vcache(a, L, role.head0);
         auto pre = [&](int t, int nt) { attend_prestage<true>(kc, vc, a.hd, a.vstride, pos, a.hd, s.kvbuf, s.vtbuf, a.attn_chunk, t, nt); };
-        if (a.layernorm) layernorm_side(s.x, s.wa, s.wab, a.dim, a.eps, s.xb, s.red, pre);
+        if (GPT2 && a.layernorm) layernorm_side(s.x, s.wa, s.wab, a.dim, a.eps, s.xb, s.red, pre);
         else rmsnorm_side(s.x, s.wa, a.dim, a.eps, s.xb, s.red, pre);
-    } else if (a.layernorm) {
+    } else if (GPT2 && a.layernorm) {
         layernorm_exact(s.x, s.wa, s.wab, a.dim, a.eps, s.xb, s.red);
     } else {
         rmsnorm_exact(s.x, s.wa, a.dim, a.eps, s.xb, s.tmp, s.red);
@@ -391,12 +402,13 @@ __device__ __noinline__ void phase_wo(const DecodeArgs &a, const LayerDev &L, co
 
 // Phase C: x += proj in every CTA; the ffn CTAs' tiles of up and gate -> s.y (up of the CTA's
 // tiles, then gate; ns tiles of up, or of the interleaved up/gate, staged at offset 0).
+template <bool GPT2>
 __device__ __noinline__ void phase_ffn(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s, int pos, int l, int tslot,
                                        int ns, uint32_t par) {
     for (int i = threadIdx.x; i < a.dim; i += blockDim.x) s.x[i] = __fadd_rn(s.x[i], s.xp[i]);
     __syncthreads();
     if (role.ffn0 >= role.ffn1) return;
-    if (a.layernorm) layernorm_exact(s.x, s.wf, s.wfb, a.dim, a.eps, s.xb, s.red);
+    if (GPT2 && a.layernorm) layernorm_exact(s.x, s.wf, s.wfb, a.dim, a.eps, s.xb, s.red);
     else rmsnorm_exact(s.x, s.wf, a.dim, a.eps, s.xb, s.tmp, s.red);
     trace(a, tslot, pos, l, 7);
     const int nf = role.ffn1 - role.ffn0;
@@ -404,7 +416,7 @@ __device__ __noinline__ void phase_ffn(const DecodeArgs &a, const LayerDev &L, c
     trace(a, tslot, pos, l, 26);
     if (ns) stage_wait(a, s, par);
     trace(a, tslot, pos, l, 12);
-    if (a.gelu) {                                                         // GPT-2: up only
+    if (GPT2 && a.gelu) {                                                 // GPT-2: up only
         matvec_exact(L.dt_up, L.up, a.dim, role.ffn0, role.ffn1, s.prep, s.scratch, a.scratch_pairs, s.y, s.w, ns);
     } else if (!L.gate) {                                                 // up and gate packed per CTA: one pass
         matvec_exact(L.dt_up, L.up, a.dim, 2 * role.ffn0, 2 * role.ffn1, s.prep, s.scratch, a.scratch_pairs, s.y, s.w, ns);
@@ -416,12 +428,14 @@ __device__ __noinline__ void phase_ffn(const DecodeArgs &a, const LayerDev &L, c
     trace(a, tslot, pos, l, 13);
 }
 
-// The SiLU gate of phase C's up/gate results in s.y -> s.tmp (the caller scatters into xh).
+// The SiLU gate of phase C's up/gate results in s.y -> s.tmp (the caller scatters into xh); GPT2:
+// GELU of up.
+template <bool GPT2>
 __device__ __noinline__ void ffn_gate(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s) {
     const int nf = role.ffn1 - role.ffn0, g0 = role.ffn0 * kTile, n = min(role.ffn1 * kTile, a.ffn) - g0;
     for (int o = threadIdx.x; o < n; o += blockDim.x) {
         const float up = L.b_up ? __fadd_rn(s.y[o], __ldg(L.b_up + g0 + o)) : s.y[o];
-        s.tmp[o] = a.gelu ? gelu_tanh(up) : silu_mul(up, s.y[nf * kTile + o], a.elist, a.eindex);
+        s.tmp[o] = GPT2 && a.gelu ? gelu_tanh(up) : silu_mul(up, s.y[nf * kTile + o], a.elist, a.eindex);
     }
     __syncthreads();
 }
@@ -636,13 +650,14 @@ __device__ __noinline__ int wait_word(const DecodeArgs &a, const uint32_t *p, ui
 
 // The head matvec over this CTA's vocabulary tiles of the final x in s.x (logits kept for
 // l3m_logits), this CTA's argmax -> hx.slots[cta] with an arrival on hx.count. host_stop: the
-// host's stop request (cluster 0, CTA 0 only).
+// host's stop request (cluster 0, CTA 0 only). GPT2: the final LayerNorm.
+template <bool GPT2>
 __device__ __noinline__ void head_logits(const DecodeArgs &a, const Role &role, const Smem &s, int pos, int host_stop, int tslot) {
     const int cta = blockIdx.x, tid = threadIdx.x, nth = blockDim.x;
     float best = -INFINITY;
     int best_i = -1;
     if (role.voc0 < role.voc1) {
-        if (a.layernorm) layernorm_exact(s.x, s.wh, s.whb, a.dim, a.eps, s.xb, s.red);
+        if (GPT2 && a.layernorm) layernorm_exact(s.x, s.wh, s.whb, a.dim, a.eps, s.xb, s.red);
         else rmsnorm_exact(s.x, s.wh, a.dim, a.eps, s.xb, s.tmp, s.red);
         trace(a, tslot, pos, a.n_layers, 3);
         prepare(a.dt_head, s.xb, a.dim, s.prep);
@@ -687,6 +702,7 @@ __device__ __noinline__ void head_logits(const DecodeArgs &a, const Role &role, 
 
 // A CTA outside cluster 0: between sampled positions it sleeps on hx.flag; for each published x it
 // computes its vocabulary tiles. Ends when cluster 0 writes kHeadDone (or on a failed wait).
+template <bool GPT2>
 __device__ __noinline__ void head_helper(const DecodeArgs &a, const Role &role, const Smem &s) {
     if (role.voc0 < role.voc1 && threadIdx.x == 0) {
         const size_t th = tile_bytes(a.dt_head, a.dim);
@@ -701,7 +717,7 @@ __device__ __noinline__ void head_helper(const DecodeArgs &a, const Role &role, 
             for (int i = threadIdx.x; i < a.dim; i += blockDim.x) s.x[i] = ld_cg_f32(a.hx.x + i);
         cp_async_wait_all();                                              // the final norm's weights
         __syncthreads();
-        head_logits(a, role, s, pos, 0, -1);
+        head_logits<GPT2>(a, role, s, pos, 0, -1);
         if (role.voc0 < role.voc1 && threadIdx.x == 0) {                  // the next position reads the same tiles
             const size_t th = tile_bytes(a.dt_head, a.dim);
             prefetch_l2(a.head + role.voc0 * th, (size_t)(role.voc1 - role.voc0) * th);
@@ -709,6 +725,10 @@ __device__ __noinline__ void head_helper(const DecodeArgs &a, const Role &role, 
     }
 }
 
+// One instance per model family and cache mode, so that neither costs the other registers or
+// branches: GPT2 (LayerNorm, learned positions, GELU: the GPT-2 family's layers), COLD (every weight
+// copy with an L2 evict-first policy).
+template <bool GPT2, bool COLD>
 __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeArgs *__restrict__ ap) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     // The arguments, this CTA's role, every layer's pointers and the carved shared-memory pointers
@@ -740,15 +760,15 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
     bool ok = true;
     if (role.voc0 < role.voc1) {
         stage_f32(s.wh, a.norm, a.dim);
-        if (a.layernorm) stage_f32(s.whb, a.norm_b, a.dim);
+        if (GPT2 && a.layernorm) stage_f32(s.whb, a.norm_b, a.dim);
     }
     if (cta >= kClusterCtas) {                                            // the other clusters: head tiles only
         cp_async_commit();
-        head_helper(a, role, s);
+        head_helper<GPT2>(a, role, s);
         cp_async_wait_all();
         return;
     }
-    stage_vectors(a, layers[0], role, s, 0);
+    stage_vectors<GPT2>(a, layers[0], role, s, 0);
     stage_init(s);
     uint32_t xpar = 0;                                                    // the exchanges' phase parity (one phase per layer)
     if (a.async_x && tid == 0) {
@@ -762,14 +782,14 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
     // from the layer top to the end of attention), up/gate and down from offset 0. ns: tiles of the
     // outstanding copy; wpar: its mbarrier phase parity.
     uint32_t wpar = 0;
-    int ns = stage_issue(s, layers[0].dt_qkv, layers[0].qkv, a.dim, role.qkv0, role.qkv1, s.w + a.w_extra, a.w_bytes - a.w_extra);
+    int ns = stage_issue(s, layers[0].dt_qkv, layers[0].qkv, a.dim, role.qkv0, role.qkv1, s.w + a.w_extra, a.w_bytes - a.w_extra, COLD);
     cluster_sync();                                                       // every CTA of the cluster has started
 
     for (pos = 0;; pos++) {
         const bool last = pos >= a.n_prompt - 1;
         if (pos < a.n_prompt) tok = a.prompt[pos];
         const bool stop_after = last && (n_gen >= a.max_new || pos + 1 >= a.ctx);   // reference engine.c:322, 352
-        embed_row(a, tok, pos, s.x);
+        embed_row<GPT2>(a, tok, pos, s.x);
         for (int l = 0; l < a.n_layers; l++) {
             const LayerDev &L = layers[l];
             cp_async_wait_all();                                          // this layer's norm weights and RoPE row
@@ -786,9 +806,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
                                       a.attn_chunk);
             // Each phase: its matvec, the copy of the next phase's tiles (the staging area is free from
             // here on), then the exchange.
-            if (role.qkv0 < role.qkv1) phase_qkv(a, L, role, s, ns, wpar, pos, l, tslot);   // Q
+            if (role.qkv0 < role.qkv1) phase_qkv<GPT2>(a, L, role, s, ns, wpar, pos, l, tslot);   // Q
             if (ns) wpar ^= 1;
-            ns = stage_issue(s, L.dt_wo, L.wo, a.dim, role.wo0, role.wo1, s.w + a.w_extra, a.w_bytes - a.w_extra);
+            ns = stage_issue(s, L.dt_wo, L.wo, a.dim, role.wo0, role.wo1, s.w + a.w_extra, a.w_bytes - a.w_extra, COLD);
             trace(a, tslot, pos, l, 27);
             if (role.qkv0 < role.qkv1) {
                 const int g0 = role.qkv0 * kTile, n = min(role.qkv1 * kTile, a.n_qkv) - g0;
@@ -807,8 +827,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
             trace(a, tslot, pos, l, 4);
             if (role.wo0 < role.wo1) phase_wo(a, L, role, s, ns, wpar, pos, l, tslot);   // B
             if (ns) wpar ^= 1;
-            if (!L.gate && !a.gelu) ns = stage_issue(s, L.dt_up, L.up, a.dim, 2 * role.ffn0, 2 * role.ffn1, s.w, a.w_bytes);
-            else ns = stage_issue(s, L.dt_up, L.up, a.dim, role.ffn0, role.ffn1, s.w, a.w_bytes);
+            if (!L.gate && !(GPT2 && a.gelu)) ns = stage_issue(s, L.dt_up, L.up, a.dim, 2 * role.ffn0, 2 * role.ffn1, s.w, a.w_bytes, COLD);
+            else ns = stage_issue(s, L.dt_up, L.up, a.dim, role.ffn0, role.ffn1, s.w, a.w_bytes, COLD);
             trace(a, tslot, pos, l, 28);
             if (role.wo0 < role.wo1) {
                 const int g0 = role.wo0 * kTile, n = min(role.wo1 * kTile, a.dim) - g0;
@@ -819,19 +839,19 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
             if (a.async_x) xwait(a, s, 2, xpar, (uint32_t)a.dim * 4);     // 3: proj
             else cluster_sync();
             trace(a, tslot, pos, l, 6);
-            phase_ffn(a, L, role, s, pos, l, tslot, ns, wpar);            // C
+            phase_ffn<GPT2>(a, L, role, s, pos, l, tslot, ns, wpar);      // C
             if (ns) wpar ^= 1;
-            ns = stage_issue(s, L.dt_down, L.down, a.ffn, role.dn0, role.dn1, s.w, a.w_bytes);
+            ns = stage_issue(s, L.dt_down, L.down, a.ffn, role.dn0, role.dn1, s.w, a.w_bytes, COLD);
             trace(a, tslot, pos, l, 29);
             if (role.ffn0 < role.ffn1) {
-                ffn_gate(a, L, role, s);
+                ffn_gate<GPT2>(a, L, role, s);
                 const int g0 = role.ffn0 * kTile, n = min(role.ffn1 * kTile, a.ffn) - g0;
                 if (a.async_x) scatter_tx(s.tmp, s.xh, g0, n, s.xbar + 3);
                 else scatter(s.tmp, s.xh, g0, n);
             }
             // The next layer's norm weights (and the next position's RoPE row) while the rest runs.
-            if (l + 1 < a.n_layers) stage_vectors(a, layers[l + 1], role, s, pos);
-            else stage_vectors(a, layers[0], role, s, pos + 1);
+            if (l + 1 < a.n_layers) stage_vectors<GPT2>(a, layers[l + 1], role, s, pos);
+            else stage_vectors<GPT2>(a, layers[0], role, s, pos + 1);
             trace(a, tslot, pos, l, 8);
             if (a.async_x) xwait(a, s, 3, xpar, (uint32_t)a.ffn * 4);     // 4: h
             else cluster_sync();
@@ -840,7 +860,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
             if (ns) wpar ^= 1;
             {
                 const LayerDev &N = layers[l + 1 < a.n_layers ? l + 1 : 0];
-                ns = stage_issue(s, N.dt_qkv, N.qkv, a.dim, role.qkv0, role.qkv1, s.w + a.w_extra, a.w_bytes - a.w_extra);
+                ns = stage_issue(s, N.dt_qkv, N.qkv, a.dim, role.qkv0, role.qkv1, s.w + a.w_extra, a.w_bytes - a.w_extra, COLD);
             }
             trace(a, tslot, pos, l, 30);
             if (role.dn0 < role.dn1) {
@@ -871,7 +891,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
         trace(a, tslot, pos, a.n_layers, 0);
         int host_stop = 0;
         if (cta == 0 && tid == 0) host_stop = ld_relaxed_sys_i32((const int *)&a.ctrl->stop_request);
-        head_logits(a, role, s, pos, host_stop, tslot);
+        head_logits<GPT2>(a, role, s, pos, host_stop, tslot);
         trace(a, tslot, pos, a.n_layers, 1);
         // One cluster: every CTA sends (max, index, host stop, no abort seen) to every CTA's xt[4 + 4 cta],
         // and after the barrier each reduces the same 16 slots in CTA order. Several clusters: CTA 0
@@ -1002,9 +1022,21 @@ cudaLaunchConfig_t cluster_config(int grid, int smem_bytes, cudaLaunchAttribute 
     return cfg;
 }
 
-cudaError_t set_attributes(int smem_bytes) {
-    cudaError_t e = cudaFuncSetAttribute(l3m::decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(l3m::decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+using DecodeFn = void (*)(const l3m::DecodeArgs *);
+
+// The kernel instance for a's model family and cache mode.
+DecodeFn decode_instance(const l3m::DecodeArgs &a) {
+    const bool gpt2 = a.layernorm || a.gelu || a.pos_embed != nullptr;
+    if (gpt2) return a.cold ? l3m::decode_kernel<true, true> : l3m::decode_kernel<true, false>;
+    return a.cold ? l3m::decode_kernel<false, true> : l3m::decode_kernel<false, false>;
+}
+
+constexpr DecodeFn kDecodeInstances[4] = {l3m::decode_kernel<false, false>, l3m::decode_kernel<false, true>,
+                                           l3m::decode_kernel<true, false>, l3m::decode_kernel<true, true>};
+
+cudaError_t set_attributes(DecodeFn fn, int smem_bytes) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     return e;
 }
 
@@ -1012,12 +1044,13 @@ cudaError_t set_attributes(int smem_bytes) {
 
 // a_dev: the arguments, already in device memory.
 extern "C" int l3m_decode_launch(const l3m::DecodeArgs *a, const l3m::DecodeArgs *a_dev, void *stream) {
-    cudaError_t e = set_attributes(a->smem_bytes);
+    const DecodeFn fn = decode_instance(*a);
+    cudaError_t e = set_attributes(fn, a->smem_bytes);
     if (e == cudaSuccess) {
         cudaLaunchAttribute at[2];
         cudaLaunchConfig_t cfg = cluster_config(a->grid, a->smem_bytes, at);
         cfg.stream = (cudaStream_t)stream;
-        e = cudaLaunchKernelEx(&cfg, l3m::decode_kernel, a_dev);
+        e = cudaLaunchKernelEx(&cfg, fn, a_dev);
     }
     if (e != cudaSuccess) {
         fprintf(stderr, "l3m: decode launch: %s\n", cudaGetErrorString(e));
@@ -1030,11 +1063,15 @@ extern "C" int l3m_decode_launch(const l3m::DecodeArgs *a, const l3m::DecodeArgs
 // less the kernel's static shared memory.
 extern "C" int l3m_decode_smem_budget(void) {
     int dev = 0, optin = 0;
-    cudaFuncAttributes fa = {};
-    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
-        cudaFuncGetAttributes(&fa, (const void *)l3m::decode_kernel) != cudaSuccess)
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
         return 0;
-    return optin - (int)fa.sharedSizeBytes;
+    int budget = optin;
+    for (DecodeFn fn : kDecodeInstances) {                                // the least over the instances
+        cudaFuncAttributes fa = {};
+        if (cudaFuncGetAttributes(&fa, (const void *)fn) != cudaSuccess) return 0;
+        budget = std::min(budget, optin - (int)fa.sharedSizeBytes);
+    }
+    return budget;
 }
 
 extern "C" int l3m_expf_tables(const uint32_t **list, const uint32_t **index);
@@ -1068,11 +1105,15 @@ extern "C" L3M_API int l3m_sample_dev(const float *logits, int vocab, float temp
 // How many clusters of kClusterCtas CTAs with smem_bytes of shared memory each can be resident on
 // the current device at once.
 extern "C" int l3m_decode_occupancy(int smem_bytes) {
-    if (set_attributes(smem_bytes) != cudaSuccess) return 0;
-    cudaLaunchAttribute at[2];
-    cudaLaunchConfig_t cfg = cluster_config(l3m::kClusterCtas, smem_bytes, at);
-    cfg.numAttrs = 1;
-    int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, (const void *)l3m::decode_kernel, &cfg) != cudaSuccess) return 0;
-    return n;
+    int least = -1;
+    for (DecodeFn fn : kDecodeInstances) {                                // the least over the instances
+        if (set_attributes(fn, smem_bytes) != cudaSuccess) return 0;
+        cudaLaunchAttribute at[2];
+        cudaLaunchConfig_t cfg = cluster_config(l3m::kClusterCtas, smem_bytes, at);
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, (const void *)fn, &cfg) != cudaSuccess) return 0;
+        least = least < 0 ? n : std::min(least, n);
+    }
+    return least;
 }

@@ -91,6 +91,8 @@ struct DecodeArgs {
     // cluster barriers; set when every CTA of the cluster produces qkv rows, which orders every
     // buffer's next write after all its reads (see decode.cu).
     int async_x, sm_xbar;
+    int cold;                           // reference --cold: the weight copies carry an L2 evict-first policy, so
+                                        // every token streams its weights from HBM (engine.c:330-338 flushes them)
     int vstride;                        // V cache: element i of position t at vc[i * vstride + t]
     int scratch_pairs, smem_bytes, attn_chunk;
 };

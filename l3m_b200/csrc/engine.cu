@@ -395,6 +395,7 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     a.embed = g.arena + off_embed; a.dt_embed = dt_embed; a.embed_row_bytes = (long long)emb_row;
     a.norm = A(off_norm);
     a.norm_b = A(off_norm_b);
+    a.cold = m->cold ? 1 : 0;
     a.layernorm = (m->flags & L3M_F_LAYERNORM) ? 1 : 0;
     a.gelu = (m->flags & L3M_F_GELU) ? 1 : 0;
     a.pos_embed = (m->flags & L3M_F_LEARNED_POS) ? A(off_pos) : nullptr;
@@ -440,9 +441,10 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     a.sm_wa = take(dim * 4);
     a.sm_wf = take(dim * 4);
     a.sm_wh = take(dim * 4);
-    a.sm_wab = take(dim * 4);
-    a.sm_wfb = take(dim * 4);
-    a.sm_whb = take(dim * 4);
+    const bool ln = (m->flags & L3M_F_LAYERNORM) != 0;                   // LayerNorm biases: GPT-2 family only
+    a.sm_wab = take(ln ? dim * 4 : 0);
+    a.sm_wfb = take(ln ? dim * 4 : 0);
+    a.sm_whb = take(ln ? dim * 4 : 0);
     a.sm_rope = take(hd / 2 * 8);
     a.sm_layers = take(L * (int)sizeof(l3m::LayerDev));
     a.attn_chunk = std::min(m->ctx, 256);

@@ -120,6 +120,16 @@ def test_packed_section_loads_the_same(gpu, models, tmp_path, name, dt):
     assert t0 == t1 and np.array_equal(l0.view(np.uint32), l1.view(np.uint32))
 
 
+def test_cold_matches_warm(gpu, models):
+    """cold=True (every token streams its weights from HBM: the copies carry an L2 evict-first
+    policy) gives the same tokens and logits (reference test_engine.py:231-237)."""
+    path = models[("gqa", "q8_0")]
+    _, a, la = gpu_run(path, PROMPT, 24)
+    _, b, lb = gpu_run(path, PROMPT, 24, cold=True)
+    assert a == b and len(a) == 24
+    assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
+
+
 def test_max_new_zero_gives_prompt_logits(gpu, oracle, models):
     path = models[("gqa", "q8_0")]
     m = l3m_b200.Model(path, force=True)
