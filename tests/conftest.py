@@ -1,7 +1,9 @@
 """Shared fixtures. `-m "not gpu"` runs the oracle, format, tokenizer and ABI checks on the CPU;
 `-m gpu` runs the parity tests of the CUDA path against the oracle on a B200."""
+import copy
 import ctypes as C
 import os
+import re
 import subprocess
 import sys
 from pathlib import Path
@@ -17,6 +19,15 @@ from l3m_b200 import synth  # noqa: E402
 ORACLE_DIR = ROOT / "oracle"
 GOLDEN = ROOT / "tests" / "golden"
 DTYPES = ["f32", "bf16", "q8_0", "q4_0", "mxfp4"]
+# Files beyond one dtype per model (the same table as tests/golden/make_golden.py): a body dtype with
+# another head dtype (reference tests/integration/test_engine.py:187-191) and a GPT-2 without q, k,
+# v biases (its GPT-Neo case, :194-201). (model, label) -> (body dtype, head dtype, drop qkv biases)
+VARIANTS = {
+    ("gqa", "q4_0+q8_0"): ("q4_0", "q8_0", False), ("gqa", "mxfp4+q8_0"): ("mxfp4", "q8_0", False),
+    ("gqa", "q8_0+bf16"): ("q8_0", "bf16", False), ("gpt2s", "q4_0+q8_0"): ("q4_0", "q8_0", False),
+    ("gpt2s", "mxfp4+q8_0"): ("mxfp4", "q8_0", False), ("gpt2s", "q8_0+bf16"): ("q8_0", "bf16", False),
+    ("gpt2s", "neo-q8_0"): ("q8_0", "q8_0", True),
+}
 
 
 def pytest_configure(config):
@@ -101,7 +112,8 @@ class OracleRun:
 def models(tmp_path_factory):
     """Small seeded models: a GQA Llama with an untied head (head_dim 16), an MHA Llama with a tied
     head (head_dim 40) and a GPT-2 (LayerNorm, learned positions, GELU, biases; head_dim 24), each
-    in every dtype; weights scaled 1/sqrt(inputs) so activations cover a wide range."""
+    in every dtype, plus the VARIANTS files; weights scaled 1/sqrt(inputs) so activations cover a
+    wide range."""
     out = tmp_path_factory.mktemp("models")
     specs = {
         "gqa": dict(dim=64, n_layers=2, n_heads=4, n_kv_heads=2, ffn_dim=128, vocab=300, ctx=96, tied=False, seed=1),
@@ -115,6 +127,14 @@ def models(tmp_path_factory):
             p = out / f"{name}-{dt}.l3m"
             synth.write(m, dt, dt, p)
             paths[(name, dt)] = p
+        for (spec, label), (body, head, no_qkv_bias) in VARIANTS.items():
+            if spec == name:
+                v = copy.copy(m)
+                if no_qkv_bias:
+                    v.tensors = {k: t for k, t in m.tensors.items() if not re.fullmatch(r"blk\.\d+\.b[qkv]", k)}
+                p = out / f"{name}-{label}.l3m"
+                synth.write(v, body, head, p)
+                paths[(name, label)] = p
     return paths
 
 

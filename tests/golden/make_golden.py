@@ -42,6 +42,15 @@ SPECS = {   # must match tests/conftest.py `models`
     "gpt2s": dict(arch="gpt2", dim=96, n_layers=2, n_heads=4, ffn_dim=192, vocab=310, ctx=96, seed=3),
 }
 DTYPES = ["f32", "bf16", "q8_0", "q4_0", "mxfp4"]
+# Files beyond one dtype per spec (must match tests/conftest.py `VARIANTS`): a body dtype with another
+# head dtype (reference tests/integration/test_engine.py:187-191), and a GPT-2 without q, k, v
+# biases (its GPT-Neo case, :194-201). key: (spec, label) -> (body dtype, head dtype, drop qkv biases)
+VARIANTS = {
+    ("gqa", "q4_0+q8_0"): ("q4_0", "q8_0", False), ("gqa", "mxfp4+q8_0"): ("mxfp4", "q8_0", False),
+    ("gqa", "q8_0+bf16"): ("q8_0", "bf16", False), ("gpt2s", "q4_0+q8_0"): ("q4_0", "q8_0", False),
+    ("gpt2s", "mxfp4+q8_0"): ("mxfp4", "q8_0", False), ("gpt2s", "q8_0+bf16"): ("q8_0", "bf16", False),
+    ("gpt2s", "neo-q8_0"): ("q8_0", "q8_0", True),
+}
 
 
 def ggml_golden():
@@ -144,6 +153,19 @@ def main():
                         arrays[f"{name}-{dt}-{label}-t{temp}-s{seed}-tokens"] = np.array(toks, np.int32)
                 assert np.array_equal(arrays[f"{name}-{dt}-scalar1-logits"], arrays[f"{name}-{dt}-scalar3-logits"])
                 del arrays[f"{name}-{dt}-scalar3-logits"], arrays[f"{name}-{dt}-scalar3-tokens"]
+            for (spec, label), (body, head, no_qkv_bias) in VARIANTS.items():
+                if spec != name:
+                    continue
+                v = ref_model(m)
+                if no_qkv_bias:
+                    v.tensors = {k: t for k, t in m.tensors.items() if not re.fullmatch(r"blk\.\d+\.b[qkv]", k)}
+                path = Path(tmp) / f"{name}-{label}.l3m"
+                export.write(v, body, head, path)
+                hashes[f"{name}-{label}"] = hashlib.sha256(path.read_bytes()).hexdigest()
+                for lab, cores, reference in (("scalar1", 1, 0), ("ref", 1, 1)):
+                    toks, lg = run_ref(lib, path, cores, reference)
+                    arrays[f"{name}-{label}-{lab}-tokens"] = np.array(toks, np.int32)
+                    arrays[f"{name}-{label}-{lab}-logits"] = lg
     (HERE / "models.json").write_text(json.dumps({"prompt": PROMPT, "steps": STEPS, "sha256": hashes}, indent=1))
     np.savez_compressed(HERE / "engine.npz", **arrays)
     print("wrote", ", ".join(p.name for p in HERE.iterdir() if p.suffix in (".json", ".npz")))

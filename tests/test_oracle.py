@@ -8,7 +8,7 @@ import json
 import numpy as np
 import pytest
 
-from conftest import DTYPES, GOLDEN, ORACLE_DIR, P, OracleRun, Vec
+from conftest import DTYPES, GOLDEN, ORACLE_DIR, VARIANTS, P, OracleRun, Vec
 from l3m_b200 import synth
 
 GG = json.loads((GOLDEN / "ggml.json").read_text())
@@ -54,6 +54,19 @@ def test_oracle_matches_reference_engine(oracle, models, name, dt, path_kind):
     want_t = ENGINE[f"{name}-{dt}-{path_kind}-tokens"].tolist()
     want_l = ENGINE[f"{name}-{dt}-{path_kind}-logits"]
     assert run.tokens == want_t
+    assert run.logits.shape == want_l.shape
+    assert np.array_equal(run.logits.view(np.uint32), want_l.view(np.uint32))
+
+
+@pytest.mark.parametrize("variant", sorted(VARIANTS))
+@pytest.mark.parametrize("path_kind", ["scalar1", "ref"])
+def test_oracle_variants_match_reference_engine(oracle, models, variant, path_kind):
+    """The same, on a head dtype other than the body's and on a GPT-2 without q, k, v biases
+    (reference tests/integration/test_engine.py:187-201)."""
+    name, label = variant
+    run = OracleRun(oracle, models[variant], MJ["prompt"], MJ["steps"], reference=path_kind == "ref")
+    assert run.tokens == ENGINE[f"{name}-{label}-{path_kind}-tokens"].tolist()
+    want_l = ENGINE[f"{name}-{label}-{path_kind}-logits"]
     assert run.logits.shape == want_l.shape
     assert np.array_equal(run.logits.view(np.uint32), want_l.view(np.uint32))
 
