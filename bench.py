@@ -18,6 +18,14 @@ l3m_generate call. tok/s counts forward passes, prompt included, as the referenc
 
 The L2 is flushed (a 256 MiB write) between timed steps. --impl reference times the reference's
 own CPU engine on the same model and context instead (rank 0 only).
+
+    python bench.py --sweep [--dtypes bf16,q8_0,q4_0,mxfp4] [--no-cpu]
+
+The matvec half of the metric: one JSON line per sweep case (M x K x dtype, BASELINE.json's sweep
+shapes): the device matvec's GB/s with its tiles in HBM and in L2 (l3m_b200.sweep, when a GPU is
+present), and as cpu_baseline the reference's own kernel table on the same tiles at 1 core and at
+every core of this host (oracle/_ref/libsweep_ref.so: tiles split over an l3m_pool, one l3m_sync
+per matvec, as the reference engine runs a sharded matvec).
 """
 import argparse
 import ctypes as C
@@ -133,6 +141,63 @@ def reference_cpu(path, ctx, n_tokens):
     return {"value": statistics.median(vals), "unit": "tok/s", "cores": int(m.group(1)) if m else None,
             "kind": "reference", "table": m.group(2) if m else None,
             "sample": f"reference `l3m bench --ctx {ctx} -n {n_tokens} --force`, median of 3 (16 warm-up tokens each)"}
+
+
+SWEEP_REF = ROOT / "oracle" / "_ref" / "libsweep_ref.so"
+
+
+def reference_sweep_cpu(lib, dtype, tiles, ntiles, k, x, cpus, seconds=0.25):
+    """GB/s of the reference's kernel table on `tiles` over cores `cpus` (tile bytes per matvec over
+    the mean time of a calibrated number of matvecs, about `seconds` in all), and the table's name."""
+    y = np.zeros(ntiles * 16, np.float32)
+    arr = (C.c_int * len(cpus))(*cpus)
+    name = C.c_char_p()
+    args = (dtype, C.c_void_p(tiles.ctypes.data), ntiles, k, C.c_void_p(x.ctypes.data), C.c_void_p(y.ctypes.data), arr, len(cpus))
+    ns = lib.sweep_ref_gemv(*args, 3, C.byref(name))
+    if ns <= 0:
+        return None, None
+    ns = lib.sweep_ref_gemv(*args, max(3, int(seconds * 1e9 / ns)), C.byref(name))
+    return tiles.size / ns, name.value.decode()
+
+
+def bench_sweep(a):
+    from l3m_b200 import sweep
+    dtypes = a.dtypes.split(",")
+    gpu = {}
+    try:
+        import torch
+        have_gpu = torch.cuda.is_available()
+    except ImportError:
+        have_gpu = False
+    if have_gpu:
+        for r in sweep.run(dtypes, sweep.SHAPES, 200, 1, None, echo=False):
+            gpu[(r["dtype"], r["m"], r["k"], r["regime"])] = r
+    lib = None
+    if not a.no_cpu and SWEEP_REF.exists():
+        lib = C.CDLL(str(SWEEP_REF))
+        lib.sweep_ref_gemv.restype = C.c_double
+        lib.sweep_ref_gemv.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.POINTER(C.c_int), C.c_int,
+                                       C.c_int, C.POINTER(C.c_char_p)]
+    every = sorted(os.sched_getaffinity(0))
+    peak, peak_kind = measured_peaks()
+    for name in dtypes:
+        for m, k in sweep.SHAPES:
+            rng = np.random.default_rng([m, k, sweep.DTYPES[name]])
+            tiles = sweep.make_tiles(rng, name, m, k)
+            line = {"metric": "matvec GB/s", "dtype": name, "m": m, "k": k, "bytes": int(tiles.size), "unit": "GB/s",
+                    "higher_is_better": True, "data": "synthetic", "peak_hbm_gbs": peak, "peak_kind": peak_kind}
+            h, l2 = gpu.get((name, m, k, "hbm")), gpu.get((name, m, k, "l2"))
+            if h:
+                line.update(value=h["gbs"], frac_hbm=h["frac_hbm"], us_hbm=h["us_per_launch"], value_l2=l2["gbs"],
+                            us_l2=l2["us_per_launch"], l2_copy_gbs=l2["l2_copy_gbs"])
+            if lib is not None:
+                x = rng.standard_normal(k).astype(np.float32)
+                g1, table = reference_sweep_cpu(lib, sweep.DTYPES[name], tiles, m // 16, k, x, every[:1])
+                gn, _ = reference_sweep_cpu(lib, sweep.DTYPES[name], tiles, m // 16, k, x, every)
+                line["cpu_baseline"] = {"value_1core": g1, "value": gn, "unit": "GB/s", "cores": len(every), "kind": "reference",
+                                        "table": table, "sample": "reference kernel table, tiles split over an l3m_pool, "
+                                        "one l3m_sync per matvec, about 0.25 s of matvecs per core count"}
+            print(json.dumps(line), flush=True)
 
 
 def combine_ranks(dist, t_dev, t_wall, positions):
@@ -264,9 +329,14 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--positions", type=int, default=0,
                     help="forward passes per step (default: the whole context); small values make a profiling case")
+    ap.add_argument("--sweep", action="store_true", help="the matvec sweep instead of decode (one JSON line per case)")
+    ap.add_argument("--dtypes", default="bf16,q8_0,q4_0,mxfp4", help="--sweep: the dtypes")
     a = ap.parse_args()
     if a.warmup < 3:
         ap.error("--warmup must be at least 3")
+    if a.sweep:
+        bench_sweep(a)
+        return
     (bench_reference if a.impl == "reference" else bench_ours)(a)
 
 

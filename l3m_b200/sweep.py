@@ -68,7 +68,7 @@ def l2_copy_gbs(torch, iters=200):
     return 2 * a.numel() * 4 * iters / (e0.elapsed_time(e1) * 1e-3) / 1e9
 
 
-def run(dtypes, shapes, iters, exact, out):
+def run(dtypes, shapes, iters, exact, out, echo=True):
     import torch
     from . import Vec, lib
     L = lib()
@@ -129,7 +129,8 @@ def run(dtypes, shapes, iters, exact, out):
                        "frac_hbm": round(gbs / hbm_peak, 4), "frac_l2_copy": round(gbs / l2_ref, 4),
                        "hbm_peak": hbm_peak, "hbm_peak_kind": peak_kind, "l2_copy_gbs": round(l2_ref, 1), "copies": reps}
                 rows.append(row)
-                print(json.dumps(row), flush=True)
+                if echo:
+                    print(json.dumps(row), flush=True)
                 if out:
                     out.write(json.dumps(row) + "\n")
             del buf, one

@@ -248,3 +248,36 @@ def test_ops_match_reference(ref, oracle):
                 ref.l3m_attend(P(a), P(q), P(k), P(v), pos, hd, stride)
                 oracle.o_attend(P(b), P(q), P(k), P(v), pos, hd, stride)
                 assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), (hd, pos, qscale)
+
+
+@pytest.mark.parametrize("dtype", range(1, 5))
+def test_sweep_harness_computes_the_matvec(ref, dtype):
+    """The matvec sweep's CPU baseline (oracle/sweep_ref.c) runs the reference's picked kernel table
+    over a pool of cores: its y equals one call of that table over every tile, bit for bit."""
+    import os
+    so = ORACLE_DIR / "_ref" / "libsweep_ref.so"
+    if not so.exists():
+        pytest.skip("oracle/_ref/libsweep_ref.so not built")
+    h = C.CDLL(str(so))
+    h.sweep_ref_gemv.restype = C.c_double
+    h.sweep_ref_gemv.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.POINTER(C.c_int), C.c_int, C.c_int,
+                                 C.POINTER(C.c_char_p)]
+    ref.l3m_kernels_pick.restype = C.POINTER(RefTable)
+    table = ref.l3m_kernels_pick().contents
+    rng = np.random.default_rng(dtype)
+    ntiles, k = 13, 288
+    tiles = random_rows(rng, dtype, ntiles * 16, k, ref.l3m_row_bytes(dtype, k), False)
+    packed = np.zeros(ntiles * ref.l3m_tile_bytes(dtype, k), np.uint8)
+    for t in range(ntiles):
+        ptrs = (C.c_void_p * 16)(*[tiles[t * 16 + c].ctypes.data for c in range(16)])
+        ref.l3m_pack_tile(C.c_void_p(packed.ctypes.data + t * ref.l3m_tile_bytes(dtype, k)), dtype, ptrs, k)
+    x = rng.standard_normal(k).astype(np.float32)
+    cpus = sorted(os.sched_getaffinity(0))[:3]
+    y = np.zeros(ntiles * 16, np.float32)
+    name = C.c_char_p()
+    ns = h.sweep_ref_gemv(dtype, P(packed), ntiles, k, P(x), P(y), (C.c_int * len(cpus))(*cpus), len(cpus), 2, C.byref(name))
+    assert ns > 0 and name.value == table.name
+    s, v, want = np.zeros(4 * k + 64, np.uint8), Vec(), np.zeros(ntiles * 16, np.float32)
+    ref.l3m_vec_prepare(C.byref(v), dtype, P(x), k, P(s))
+    table.gemv[dtype](P(want), P(packed), ntiles, k, C.byref(v))
+    assert np.array_equal(y.view(np.uint32), want.view(np.uint32))
