@@ -62,7 +62,8 @@ struct DecodeArgs {
     long long embed_row_bytes;
     const float *norm, *norm_b;         // final norm gain (and LayerNorm bias)
     int layernorm, gelu;                // GPT-2 family: LayerNorm instead of RMSNorm; GELU(up) instead of SiLU(gate) * up
-    const float *pos_embed;             // [ctx][dim] learned positions (NULL: RoPE)
+    const float *pos_embed;             // [ctx][dim] learned positions (NULL: RoPE). Any of the three set: the
+                                        // launch takes the kernel's GPT2 instance (only it reads them)
     const float2 *rope;                 // [ctx][hd/2] {cos, sin}
     const uint32_t *elist, *eindex;     // libm expf exception list
     const Role *roles;
@@ -91,8 +92,9 @@ struct DecodeArgs {
     // cluster barriers; set when every CTA of the cluster produces qkv rows, which orders every
     // buffer's next write after all its reads (see decode.cu).
     int async_x, sm_xbar;
-    int cold;                           // reference --cold: the weight copies carry an L2 evict-first policy, so
-                                        // every token streams its weights from HBM (engine.c:330-338 flushes them)
+    int cold;                           // reference --cold (engine.c:330-338 flushes the weights after each token):
+                                        // the launch takes the kernel's COLD instance, whose weight copies carry an
+                                        // L2 evict-first policy
     int vstride;                        // V cache: element i of position t at vc[i * vstride + t]
     int scratch_pairs, smem_bytes, attn_chunk;
 };
