@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 
 import l3m_b200
-from conftest import DTYPES, GOLDEN, OracleRun
+from conftest import DTYPES, GOLDEN, VARIANTS, OracleRun
 from l3m_b200 import synth
 
 pytestmark = pytest.mark.gpu
@@ -217,3 +217,123 @@ def test_describe_and_python_api(gpu, models):
         m.describe()
     with pytest.raises(ValueError):
         l3m_b200.Model(path, ctx=1)
+
+
+@pytest.mark.parametrize("variant", sorted(VARIANTS))
+def test_mixed_head_dtype_and_no_qkv_biases(gpu, oracle, models, variant):
+    """A head dtype other than the body's, and a GPT-2 without q, k, v biases (reference
+    tests/integration/test_engine.py:187-201), against the oracle (pinned to the reference on the
+    same files): Llama bit for bit; the GPT-2 family's logits within 1e-4 of the largest |logit|."""
+    path = models[variant]
+    want = OracleRun(oracle, path, PROMPT, MJ["steps"])
+    _, toks, lg = gpu_run(path, PROMPT, MJ["steps"])
+    assert toks == want.tokens and lg.shape == want.logits.shape
+    if variant[0] == "gpt2s":
+        assert (np.abs(lg - want.logits) <= 1e-4 * np.abs(want.logits).max(axis=1, keepdims=True)).all()
+    else:
+        assert np.array_equal(lg.view(np.uint32), want.logits.view(np.uint32))
+
+
+@pytest.mark.parametrize("name,dt", [("gqa", "q8_0"), ("mha40", "mxfp4"), ("gpt2s", "bf16")])
+def test_cluster_counts_give_identical_logits(gpu, models, monkeypatch, name, dt):
+    """The vocabulary split over one cluster (16 CTAs) and over every cluster the GPU holds gives the
+    same tokens and logits (the reference's core-count invariance, test_engine.py:217-228)."""
+    _, t0, l0 = gpu_run(models[(name, dt)], PROMPT, 24)
+    monkeypatch.setenv("L3M_CLUSTERS", "1")
+    _, t1, l1 = gpu_run(models[(name, dt)], PROMPT, 24)
+    assert t0 == t1 and np.array_equal(l0.view(np.uint32), l1.view(np.uint32))
+
+
+def test_api_misuse_raises(gpu, models):
+    """Reference tests/integration/test_robustness.py:94-114: bad prompts, an exception from
+    on_token, generate or close from on_token, use after close."""
+    m = l3m_b200.Model(models[("gqa", "q8_0")], force=True)
+    for bad in ([], [-1], [m.vocab], [2**40]):
+        with pytest.raises(ValueError):
+            m.generate(bad, 2)
+
+    def boom(t):
+        raise KeyError("stop")
+    with pytest.raises(KeyError):
+        m.generate([1], 5, on_token=boom)
+    for reenter in (lambda t: m.generate([1], 1), lambda t: m.close()):
+        with pytest.raises(RuntimeError):
+            m.generate([1], 5, on_token=reenter)
+    streamed = []
+    out = m.generate([1], 5, on_token=lambda t: streamed.append(m.decode_bytes([t])))
+    assert b"".join(streamed) == m.decode_bytes(out)
+    m.close()
+    m.close()
+    for f in (m.describe, lambda: m.generate([1], 2), lambda: m.encode("a")):
+        with pytest.raises(ValueError):
+            f()
+
+
+def test_bad_gpu_lists_are_refused(gpu, models):
+    """cpus is the GPU ordinal list: a repeated, missing or negative ordinal is a clean error
+    (reference test_robustness.py:117-125, for cores)."""
+    path = models[("gqa", "f32")]
+    for cpus in ([0, 0], [100000], [-1]):
+        with pytest.raises(RuntimeError):
+            l3m_b200.Model(path, cpus=cpus, force=True)
+    assert l3m_b200.Model(path, cpus=[0], force=True).generate(PROMPT, 3, temperature=0)
+
+
+def test_threads_share_a_model(gpu, models):
+    """Calls from several threads are serialised; a close from another thread ends theirs cleanly
+    (reference test_robustness.py:128-146)."""
+    import contextlib
+    import threading
+    m = l3m_b200.Model(models[("gpt2s", "bf16")], force=True)
+    want, got = m.generate([1, 5], 12, temperature=0), []
+
+    def worker():
+        with contextlib.suppress(ValueError):
+            for _ in range(5):
+                got.append(m.generate([1, 5], 12, temperature=0))
+
+    def together(*fns):
+        threads = [threading.Thread(target=f) for f in fns]
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join()
+    together(worker, worker, worker)
+    assert got == [want] * 15
+    together(worker, worker, worker, m.close)
+    assert got == [want] * len(got)
+
+
+def test_model_without_bos(gpu, models):
+    """A file whose bos is -1: no BOS in front of an encoded prompt (reference test_robustness.py:81-83)."""
+    m = l3m_b200.Model(models[("gqa", "f32")], force=True)
+    assert m.bos == -1 and m.encode("ab") == [97, 98]
+
+
+def test_sampling_distribution(gpu, models):
+    """Chi-square of the first sampled token over 2000 seeds against softmax(logits / T)
+    (reference test_engine.py:251-265)."""
+    m = l3m_b200.Model(models[("gpt2s", "f32")], force=True)
+    ids, temp, n = PROMPT[:1], 0.5, 2000
+    assert m.generate(ids, 0, temperature=0) == []
+    z = m.logits.astype(np.float64) / temp
+    p = np.exp(z - z.max())
+    p /= p.sum()
+    counts = np.zeros(m.vocab)
+    for seed in range(n):
+        out = m.generate(ids, 1, temperature=temp, seed=seed)
+        counts[out[0]] += 1
+    big = p * n >= 5
+    obs, exp = np.append(counts[big], counts[~big].sum()), np.append(p[big], p[~big].sum()) * n
+    df = len(obs) - 1
+    assert ((obs - exp) ** 2 / exp).sum() < df + 5 * np.sqrt(2 * df)
+
+
+def test_load_refuses_over_budget(gpu, tmp_path):
+    """Weights larger than the GPU's persisting L2 window are refused unless force (reference
+    test_engine.py:112-119): here 160 MiB of f32 against a 126 MB L2."""
+    m = synth.llama(dim=512, n_layers=10, n_heads=8, n_kv_heads=8, ffn_dim=2048, vocab=300, ctx=64, seed=4)
+    synth.write(m, "f32", "f32", tmp_path / "big.l3m")
+    with pytest.raises(RuntimeError):
+        l3m_b200.Model(tmp_path / "big.l3m", cpus=[0])
+    assert "on 1 GPU " in l3m_b200.Model(tmp_path / "big.l3m", cpus=[0], force=True).describe()
