@@ -156,21 +156,28 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gemv_stream_kernel(float *y
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    __syncthreads();                                                       // the barriers are initialised
+    // The producer: chunk c of this CTA's tiles into stage c % kStreamStages, once the compute warps
+    // have released that stage (from the second round of the ring on).
+    auto issue = [&](int c) {
+        const int st = c % kStreamStages;
+        if (c >= kStreamStages) mbar_wait(smem_u32(&empty[st]), (uint32_t)(c / kStreamStages + 1) & 1u);
+        const int g0 = t0 + c / nch * pl.G, ng = min(pl.G, t1 - g0), b0 = c % nch * pl.U, nu = min(pl.U, nb - b0);
+        unsigned char *buf = stage0 + (size_t)st * pl.stage_bytes;
+        const uint32_t bar = smem_u32(&full[st]);
+        if (lane == 0) asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"((uint32_t)(ng * nu * bb)) : "memory");
+        __syncwarp();
+        for (int g = lane; g < ng; g += 32)
+            asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                         ::"r"(smem_u32(buf + (size_t)g * pl.piece)), "l"(tiles + (size_t)(g0 + g) * tb + (size_t)b0 * bb),
+                         "r"((uint32_t)(nu * bb)), "r"(bar) : "memory");
+    };
+    const int early = min(total, kStreamStages);                           // the first ring needs no release
+    if (warp == kStreamWarps)
+        for (int c = 0; c < early; c++) issue(c);                          // the weights stream in while x is loaded
     load_prep(DT, x, k, p);                                                // every thread; ends with __syncthreads
-    if (warp == kStreamWarps) {                                            // the producer
-        for (int c = 0; c < total; c++) {
-            const int st = c % kStreamStages;
-            if (c >= kStreamStages) mbar_wait(smem_u32(&empty[st]), (uint32_t)(c / kStreamStages + 1) & 1u);
-            const int g0 = t0 + c / nch * pl.G, ng = min(pl.G, t1 - g0), b0 = c % nch * pl.U, nu = min(pl.U, nb - b0);
-            unsigned char *buf = stage0 + (size_t)st * pl.stage_bytes;
-            const uint32_t bar = smem_u32(&full[st]);
-            if (lane == 0) asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"((uint32_t)(ng * nu * bb)) : "memory");
-            __syncwarp();
-            for (int g = lane; g < ng; g += 32)
-                asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                             ::"r"(smem_u32(buf + (size_t)g * pl.piece)), "l"(tiles + (size_t)(g0 + g) * tb + (size_t)b0 * bb),
-                             "r"((uint32_t)(nu * bb)), "r"(bar) : "memory");
-        }
+    if (warp == kStreamWarps) {
+        for (int c = early; c < total; c++) issue(c);
         return;                                                            // every chunk it started is waited for by the compute warps
     }
     const uint32_t *xw = (const uint32_t *)p.q8;
