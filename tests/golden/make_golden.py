@@ -1,7 +1,7 @@
 """Regenerate the golden fixtures in this directory from the reference (fpedd/l3m) itself.
 
 Run where the reference checkout and its compiled library exist (oracle/_ref, built by
-oracle/Makefile):  python tests/golden/make_golden.py [/root/reference]
+oracle/Makefile):  python tests/golden/make_golden.py [REFERENCE_CHECKOUT]
 
   ggml.json       ggml block bytes for the reference's own known-answer inputs (its
                   tests/unit/test_export.py:19-59), recomputed with its exporter and checked
