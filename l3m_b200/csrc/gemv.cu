@@ -426,6 +426,7 @@ L3M_API int l3m_gemv_dev(int exact, int dtype, float *y, const void *tiles, int 
     if (dtype >= DT_Q8 && k % kQB) return fail_msg("l3m_gemv_dev: quantised k must be a multiple of 32");
     if (dtype == DT_BF16 && k % 2) return fail_msg("l3m_gemv_dev: bf16 k must be even");
     if (ntiles == 0) return 0;
+    if (!y || !tiles || !x) return fail_msg("l3m_gemv_dev: y, tiles and x are required");
     cudaStream_t s = (cudaStream_t)stream;
     static const bool stream_off = getenv("L3M_GEMV_STREAM") && !strcmp(getenv("L3M_GEMV_STREAM"), "0");
     if (!exact && dtype <= DT_BF16) {

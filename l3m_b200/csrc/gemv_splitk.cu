@@ -110,6 +110,8 @@ extern "C" L3M_API int l3m_gemv_splitk_dev(int dtype, float *y, const void *tile
         return l3m_error_msg(msg);
     }
     if (ntiles == 0) return 0;
+    if (!y || !tiles || !x || !x->q8 || !x->scale || !x->sum)
+        return l3m_error_msg("l3m_gemv_splitk_dev: y, tiles and a prepared x (q8, scale, sum) are required");
     DeviceSlot slot;
     if (setup(&slot)) return -1;
     cudaStream_t s = (cudaStream_t)stream;

@@ -40,6 +40,29 @@ def declared_symbols():
     return names
 
 
+def test_device_matvec_entries_refuse_bad_arguments(lib):
+    """l3m_gemv_dev and l3m_gemv_splitk_dev check their arguments before touching the GPU: -1 and a
+    message from l3m_cuda_error for a wrong dtype, k, size or missing pointer (no GPU needed)."""
+    v, buf = Vec(), (C.c_char * 64)()
+    y, t = C.cast(buf, C.c_void_p), C.cast(buf, C.c_void_p)
+    cases = [
+        (lambda: lib.l3m_gemv_dev(1, 7, y, t, 1, 32, C.byref(v), None), "bad arguments"),
+        (lambda: lib.l3m_gemv_dev(1, 2, y, t, 1, 48, C.byref(v), None), "multiple of 32"),
+        (lambda: lib.l3m_gemv_dev(1, 1, y, t, 1, 33, C.byref(v), None), "even"),
+        (lambda: lib.l3m_gemv_dev(1, 2, y, t, 1, 32, None, None), "required"),
+        (lambda: lib.l3m_gemv_splitk_dev(1, y, t, 1, 32, C.byref(v), None), "quantised dtypes only"),
+        (lambda: lib.l3m_gemv_splitk_dev(2, y, t, 1, 48, C.byref(v), None), "bad arguments"),
+        (lambda: lib.l3m_gemv_splitk_dev(2, y, t, 2049, 512, C.byref(v), None), "exceed the static scratch"),
+        (lambda: lib.l3m_gemv_splitk_dev(2, y, t, 1, 32, C.byref(v), None), "required"),
+        (lambda: lib.l3m_gemv_splitk_dev(2, y, t, 1, 32, None, None), "required"),
+    ]
+    for call, text in cases:
+        assert call() == -1
+        assert text in lib.l3m_cuda_error().decode(), text
+    assert lib.l3m_gemv_dev(1, 2, y, t, 0, 32, C.byref(v), None) == 0        # nothing to do
+    assert lib.l3m_gemv_splitk_dev(2, y, t, 0, 32, C.byref(v), None) == 0
+
+
 def test_exports_every_declared_symbol(lib):
     out = subprocess.run(["nm", "-D", "--defined-only", str(LIB)], capture_output=True, text=True, check=True).stdout
     exported = {line.split()[-1] for line in out.splitlines()}
