@@ -1082,6 +1082,7 @@ extern "C" int l3m_error_cuda(int e, const char *what);
 extern "C" L3M_API int l3m_sample_dev(const float *logits, int vocab, float temperature, uint64_t *rng_state, int32_t *token, float *scratch,
                                       void *stream) {
     if (vocab <= 0 || !(temperature > 0.0f)) return l3m_error_msg("l3m_sample_dev: vocab > 0 and temperature > 0");
+    if (!logits || !rng_state || !token || !scratch) return l3m_error_msg("l3m_sample_dev: logits, rng_state, token and scratch are required");
     const uint32_t *list, *index;
     if (l3m_expf_tables(&list, &index)) return -1;
     cudaError_t e = cudaFuncSetAttribute(l3m::sample_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);

@@ -469,7 +469,9 @@ L3M_API int l3m_gemv_dev(int exact, int dtype, float *y, const void *tiles, int 
 }
 
 L3M_API int l3m_vec_prepare_dev(int dtype, l3m_vec *out, const float *x, int n, void *scratch, void *stream) {
+    if (dtype < 0 || dtype >= L3M_DT_COUNT || n <= 0) return fail_msg("l3m_vec_prepare_dev: bad arguments (dtype, n > 0)");
     if (dtype >= DT_Q8 && n % kQB) return fail_msg("l3m_vec_prepare_dev: n must be a multiple of 32");
+    if (!out || !x || (dtype != DT_F32 && !scratch)) return fail_msg("l3m_vec_prepare_dev: out, x and (but for f32) scratch are required");
     memset(out, 0, sizeof *out);
     out->f32 = x;
     if (dtype == DT_F32) return 0;
@@ -490,16 +492,20 @@ L3M_API int l3m_vec_prepare_dev(int dtype, l3m_vec *out, const float *x, int n, 
 }
 
 L3M_API int l3m_block_dots_dev(int dtype, int32_t *dots, const void *tiles, int ntiles, int k, const l3m_vec *x, void *stream) {
-    if (dtype < DT_Q8 || dtype > DT_MX || k % kQB) return fail_msg("l3m_block_dots_dev: quantised dtypes, k a multiple of 32");
+    if (dtype < DT_Q8 || dtype > DT_MX || k <= 0 || k % kQB || ntiles < 0)
+        return fail_msg("l3m_block_dots_dev: quantised dtypes, k a positive multiple of 32, ntiles >= 0");
     if (ntiles == 0) return 0;
+    if (!dots || !tiles || !x || !x->q8 || !x->sum) return fail_msg("l3m_block_dots_dev: dots, tiles and a prepared x are required");
     block_dots_kernel<<<grid_for(ntiles), 256, 0, (cudaStream_t)stream>>>(dtype, dots, (const uint8_t *)tiles, ntiles, k, vec_arg(x));
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : fail(e, "l3m_block_dots_dev");
 }
 
 L3M_API int l3m_unpack_dev(int dtype, int8_t *q, float *d, const void *tiles, int ntiles, int k, void *stream) {
-    if (dtype < DT_Q8 || dtype > DT_MX || k % kQB) return fail_msg("l3m_unpack_dev: quantised dtypes, k a multiple of 32");
+    if (dtype < DT_Q8 || dtype > DT_MX || k <= 0 || k % kQB || ntiles < 0)
+        return fail_msg("l3m_unpack_dev: quantised dtypes, k a positive multiple of 32, ntiles >= 0");
     if (ntiles == 0) return 0;
+    if (!q || !d || !tiles) return fail_msg("l3m_unpack_dev: q, d and tiles are required");
     unpack_kernel<<<grid_for(ntiles), 256, 0, (cudaStream_t)stream>>>(dtype, q, d, (const uint8_t *)tiles, ntiles, k);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : fail(e, "l3m_unpack_dev");
@@ -507,6 +513,7 @@ L3M_API int l3m_unpack_dev(int dtype, int8_t *q, float *d, const void *tiles, in
 
 L3M_API int l3m_attend_dev(float *out, const float *q, const uint16_t *k, const uint16_t *v, int pos, int head_dim, int stride, void *stream) {
     if (head_dim % 8 || head_dim <= 0 || pos < 0 || stride < head_dim) return fail_msg("l3m_attend_dev: bad arguments");
+    if (!out || !q || !k || !v) return fail_msg("l3m_attend_dev: out, q, k and v are required");
     const uint32_t *list, *index;
     if (l3m_expf_tables(&list, &index)) return -1;
     size_t smem = (size_t)head_dim * 8 + 64 * 4 + (size_t)((pos + 4) & ~3) * 4 + (size_t)head_dim * 4 + 16 +

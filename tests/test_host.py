@@ -40,9 +40,9 @@ def declared_symbols():
     return names
 
 
-def test_device_matvec_entries_refuse_bad_arguments(lib):
-    """l3m_gemv_dev and l3m_gemv_splitk_dev check their arguments before touching the GPU: -1 and a
-    message from l3m_cuda_error for a wrong dtype, k, size or missing pointer (no GPU needed)."""
+def test_device_entries_refuse_bad_arguments(lib):
+    """Every *_dev entry checks its arguments before touching the GPU: -1 and a message from
+    l3m_cuda_error for a wrong dtype, size or missing pointer (no GPU needed)."""
     v, buf = Vec(), (C.c_char * 64)()
     y, t = C.cast(buf, C.c_void_p), C.cast(buf, C.c_void_p)
     cases = [
@@ -56,11 +56,30 @@ def test_device_matvec_entries_refuse_bad_arguments(lib):
         (lambda: lib.l3m_gemv_splitk_dev(2, y, t, 1, 32, C.byref(v), None), "required"),
         (lambda: lib.l3m_gemv_splitk_dev(2, y, t, 1, 32, None, None), "required"),
     ]
+    p = y
+    cases += [
+        (lambda: lib.l3m_vec_prepare_dev(9, C.byref(v), p, 32, p, None), "bad arguments"),
+        (lambda: lib.l3m_vec_prepare_dev(2, C.byref(v), p, 0, p, None), "bad arguments"),
+        (lambda: lib.l3m_vec_prepare_dev(2, C.byref(v), p, 40, p, None), "multiple of 32"),
+        (lambda: lib.l3m_vec_prepare_dev(2, C.byref(v), p, 32, None, None), "required"),
+        (lambda: lib.l3m_vec_prepare_dev(1, None, p, 32, p, None), "required"),
+        (lambda: lib.l3m_block_dots_dev(1, p, t, 1, 32, C.byref(v), None), "quantised dtypes"),
+        (lambda: lib.l3m_block_dots_dev(2, p, t, -1, 32, C.byref(v), None), "ntiles >= 0"),
+        (lambda: lib.l3m_block_dots_dev(2, p, t, 1, 32, C.byref(v), None), "required"),
+        (lambda: lib.l3m_unpack_dev(4, p, p, t, 1, 0, None), "positive multiple of 32"),
+        (lambda: lib.l3m_unpack_dev(3, None, p, t, 1, 32, None), "required"),
+        (lambda: lib.l3m_attend_dev(p, p, p, p, 0, 12, 12, None), "bad arguments"),
+        (lambda: lib.l3m_attend_dev(p, p, None, p, 0, 16, 16, None), "required"),
+        (lambda: lib.l3m_sample_dev(p, 0, 1.0, p, p, p, None), "vocab > 0"),
+        (lambda: lib.l3m_sample_dev(p, 10, 0.0, p, p, p, None), "temperature > 0"),
+        (lambda: lib.l3m_sample_dev(p, 10, 1.0, None, p, p, None), "required"),
+    ]
     for call, text in cases:
         assert call() == -1
         assert text in lib.l3m_cuda_error().decode(), text
     assert lib.l3m_gemv_dev(1, 2, y, t, 0, 32, C.byref(v), None) == 0        # nothing to do
     assert lib.l3m_gemv_splitk_dev(2, y, t, 0, 32, C.byref(v), None) == 0
+    assert lib.l3m_block_dots_dev(2, p, t, 0, 32, C.byref(v), None) == 0
 
 
 def test_exports_every_declared_symbol(lib):
