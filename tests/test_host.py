@@ -82,6 +82,29 @@ def test_device_entries_refuse_bad_arguments(lib):
     assert lib.l3m_block_dots_dev(2, p, t, 0, 32, C.byref(v), None) == 0
 
 
+def test_host_table_fails_loudly_without_a_gpu(lib, capfd):
+    """The kernel table's void entries (the reference's l3m_gemv_fn contract) cannot return an error:
+    when the device is unusable they say why on stderr and fill the output with NaN."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present: the failure path is not reached")
+    import l3m_b200
+    table = l3m_b200.kernels("sm100a")
+    k, ntiles = 64, 2
+    tiles = np.zeros(ntiles * lib.l3m_tile_bytes(2, k), np.uint8)
+    x = np.ones(k, np.float32)
+    scratch, v = np.zeros(4 * k + 64, np.uint8), Vec()
+    lib.l3m_vec_prepare(C.byref(v), 2, P(x), k, P(scratch))
+    y = np.zeros(ntiles * 16, np.float32)
+    table.gemv[2](P(y), P(tiles), ntiles, k, C.byref(v))
+    assert np.isnan(y).all()
+    q, kv, out = np.ones(16, np.float32), np.zeros(64, np.uint16), np.zeros(16, np.float32)
+    table.attend(P(out), P(q), P(kv), P(kv), 1, 16, 16)
+    assert np.isnan(out).all()
+    err = capfd.readouterr().err
+    assert "l3m: gemv:" in err and "l3m: attend:" in err
+
+
 def test_exports_every_declared_symbol(lib):
     out = subprocess.run(["nm", "-D", "--defined-only", str(LIB)], capture_output=True, text=True, check=True).stdout
     exported = {line.split()[-1] for line in out.splitlines()}
