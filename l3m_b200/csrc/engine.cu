@@ -720,7 +720,10 @@ L3M_API int l3m_generate(l3m_model *m, const int32_t *prompt, int n_prompt, int 
                 if (stopped >= 0) continue;
                 n_gen++;
                 m->logits_pos = n_prompt - 1 + seen;                 // l3m_logits inside on_token: this token's logits
-                if (!on_token(m->tokens[seen], user)) {
+                // A volatile read, after the volatile read of n_published: the compiler keeps the
+                // order and x86 does not reorder loads, so the token is the one the kernel published.
+                const int32_t tok = ((volatile const int32_t *)m->tokens)[seen];
+                if (!on_token(tok, user)) {
                     stopped = seen;
                     m->ctrl->stop_request = 1;
                 }
