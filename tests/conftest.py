@@ -108,6 +108,14 @@ class OracleRun:
             oracle.o_free(m)
 
 
+def oracle_stream(path, prompt, max_new, ctx):
+    """OracleRun's (tokens, logits) for one file, as a picklable call for a spawned worker process
+    (spawned, so it inherits no CUDA state): the oracle is single-threaded, and independent runs
+    go faster side by side."""
+    run = OracleRun(load_oracle(), path, prompt, max_new, ctx=ctx)
+    return run.tokens, run.logits
+
+
 @pytest.fixture(scope="session")
 def models(tmp_path_factory):
     """Small seeded models: a GQA Llama with an untied head (head_dim 16), an MHA Llama with a tied
