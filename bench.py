@@ -169,9 +169,12 @@ def bench_sweep(a):
         have_gpu = torch.cuda.is_available()
     except ImportError:
         have_gpu = False
+    clocks = None
     if have_gpu:
-        for r in sweep.run(dtypes, sweep.SHAPES, 200, 1, None, echo=False):
-            gpu[(r["dtype"], r["m"], r["k"], r["regime"])] = r
+        with Clocks(int(os.environ.get("LOCAL_RANK", 0))) as clk:
+            for r in sweep.run(dtypes, sweep.SHAPES, 200, 1, None, echo=False):
+                gpu[(r["dtype"], r["m"], r["k"], r["regime"])] = r
+        clocks = clk.summary()
     lib = None
     if not a.no_cpu and SWEEP_REF.exists():
         lib = C.CDLL(str(SWEEP_REF))
@@ -189,7 +192,7 @@ def bench_sweep(a):
             h, l2 = gpu.get((name, m, k, "hbm")), gpu.get((name, m, k, "l2"))
             if h:
                 line.update(value=h["gbs"], frac_hbm=h["frac_hbm"], us_hbm=h["us_per_launch"], value_l2=l2["gbs"],
-                            us_l2=l2["us_per_launch"], l2_copy_gbs=l2["l2_copy_gbs"])
+                            us_l2=l2["us_per_launch"], l2_copy_gbs=l2["l2_copy_gbs"], clocks=clocks)
             if lib is not None:
                 x = rng.standard_normal(k).astype(np.float32)
                 g1, table = reference_sweep_cpu(lib, sweep.DTYPES[name], tiles, m // 16, k, x, every[:1])
@@ -198,6 +201,29 @@ def bench_sweep(a):
                                         "table": table, "sample": "reference kernel table, tiles split over an l3m_pool, "
                                         "one l3m_sync per matvec, about 0.25 s of matvecs per core count"}
             print(json.dumps(line), flush=True)
+
+
+# DRAM traffic of one decode launch per forward pass, from an ncu capture of a short case of the same
+# kernel and model (dram__bytes_read.sum + dram__bytes_write.sum over the launch, divided by its
+# forward passes), scaled by the bench's forward passes per launch.
+DECODE_TRAFFIC = {}
+
+
+def matvec_line():
+    """The matvec half of the metric on this GPU: q8_0 32000x768 (BASELINE's largest sweep shape) through
+    l3m_gemv_dev, tiles read from HBM (copies cycled, 2.5x the L2) and from L2 (one copy), with the
+    SM clocks sampled while it runs."""
+    from l3m_b200 import sweep
+    with Clocks(int(os.environ.get("LOCAL_RANK", 0))) as clk:
+        rows = sweep.run(["q8_0"], [(32000, 768)], 400, 1, None, echo=False)
+    by = {r["regime"]: r for r in rows}
+    h, l2 = by["hbm"], by["l2"]
+    return {"case": "q8_0 32000x768 l3m_gemv_dev (exact)", "bytes": h["bytes"], "unit": "GB/s",
+            "hbm": {"value": h["gbs"], "us": h["us_per_launch"], "frac": h["frac_hbm"]},
+            "l2": {"value": l2["gbs"], "us": l2["us_per_launch"], "frac_of_hbm_peak": round(l2["gbs"] / h["hbm_peak"], 4),
+                   "l2_copy_gbs": l2["l2_copy_gbs"]},
+            "peak": h["hbm_peak"], "peak_kind": h["hbm_peak_kind"], "timing": "400 launches in a CUDA graph, CUDA events",
+            "clocks": clk.summary()}
 
 
 def combine_ranks(dist, t_dev, t_wall, positions):
@@ -258,9 +284,7 @@ def bench_ours(a):
     launch_s = (t_dev / a.steps) * 1e-9
     peak, peak_kind = measured_peaks()
     achieved = alg / launch_s / 1e9
-    # DRAM bytes per launch are not measured: ncu's profiled replay of the 16-CTA cluster launch loses
-    # its distributed-shared-memory exchanges (profiles/decode_kernel_ncu_SmolLM2-135M-q8_0.md).
-    traffic = None
+    traffic = DECODE_TRAFFIC.get(name)
     out = {
         "metric": "batch-1 decode tok/s", "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": a.steps,
         "warmup": a.warmup, "ms_per_step": round(t_dev / a.steps * 1e-6, 4), "higher_is_better": True,
@@ -269,16 +293,21 @@ def bench_ours(a):
         "data": "synthetic (seeded N(0,0.02) weights, 4 seeded prompt ids)",
         "config": {"workload": f"{name} batch-1 greedy decode, ctx {ctx}, {per_launch_pos} forward passes per step "
                                f"({len(prompt)}-token prompt, {n_gen} generated)", "ctx": ctx, "l2_flush_between_steps": True,
-                   "parallelism": f"replica x{world}" if world > 1 else "1 GPU", "table": "sm100a (bit-exact with the reference's scalar path)"},
+                   "parallelism": (f"{world} independent replicas: value and e2e are the aggregate of {world} batch-1 streams, "
+                                   "not one batch-1 stream on {world} GPUs") if world > 1 else "1 GPU",
+                   "table": "sm100a (bit-exact with the reference's scalar path)"},
         "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * len(prompt), "d2h_bytes_per_step": 4 * n_gen,
                 "timing": "host wall clock around l3m_generate"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                     "traffic": traffic, "traffic_note": "not measured: ncu cannot profile the cluster launch (see profiles/)",
+                     "traffic": traffic and round(traffic["dram_bytes_per_position"] * per_launch_pos),
+                     "traffic_note": traffic["note"] if traffic else "not measured for this config",
                      "peak_kind": peak_kind,
                      "algorithmic_bytes_per_launch": alg},
         "gpu_launches": a.steps,
         "clocks": clk.summary(),
     }
+    if not a.no_matvec:
+        out["matvec"] = matvec_line()
     if not a.no_cpu:
         out["cpu_baseline"] = reference_cpu(path, ctx, max_new)
     print(json.dumps(out), flush=True)
@@ -327,6 +356,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="SmolLM2-135M-q8_0", choices=list(synth.CONFIGS))
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--no-matvec", action="store_true", help="skip the matvec line of the decode bench")
     ap.add_argument("--positions", type=int, default=0,
                     help="forward passes per step (default: the whole context); small values make a profiling case")
     ap.add_argument("--sweep", action="store_true", help="the matvec sweep instead of decode (one JSON line per case)")

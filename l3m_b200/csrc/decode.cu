@@ -5,21 +5,31 @@
 // Every CTA keeps the residual x in its shared memory. Each matrix is split into contiguous runs of
 // 16-row tiles over the CTAs (the reference's split over ranks, src/engine.c:88-91). A CTA writes
 // its slice of every produced vector straight into the shared memory of all CTAs of the cluster
-// (distributed shared memory) and a hardware cluster barrier (release/acquire) makes it visible, so
-// an exchange costs a few hundred nanoseconds and no global-memory round trip. Per layer:
-//   Q  qkv CTAs:  rmsnorm, their tiles of the q/k/v rows                   -> qkv      barrier 1
-//   A  head CTAs: RoPE, KV row, attention (K/V copies started before 1)   -> attn     barrier 2
-//   B  wo CTAs:   matvec                                                  -> proj     barrier 3
-//   C  all:       x += proj; ffn CTAs: rmsnorm, up and gate, SiLU gate    -> h        barrier 4
-//   D  down CTAs: matvec                                                  -> down     barrier 5
+// (distributed shared memory) with st.async, each store completing its bytes on the receiver's
+// mbarrier for that exchange, so an exchange costs a few hundred nanoseconds and no global-memory
+// round trip (when some CTA has no qkv rows, hardware cluster barriers order the exchanges
+// instead). Per layer:
+//   Q  qkv CTAs:  rmsnorm, their tiles of the q/k/v rows                   -> qkv      exchange 1
+//   A  head CTAs: RoPE, KV row, attention (K/V copies started during Q)   -> attn     exchange 2
+//   B  wo CTAs:   matvec                                                  -> proj     exchange 3
+//   C  all:       x += proj; ffn CTAs: rmsnorm, up and gate, SiLU gate    -> h        exchange 4
+//   D  down CTAs: matvec                                                  -> down     exchange 5
 //   all:          x += down
 // After the last prompt position each position ends with the head matvec (logits kept for
-// l3m_logits), a per-CTA argmax, an all-gather of (max, index, host stop) and the same global
-// argmax in every CTA, in CTA order. Each exchanged vector has one buffer: its next write comes at
-// least one barrier after every reader has finished with it. The weights of the next layer are
-// prefetched into L2 a layer ahead; each layer's norm weights and RoPE row are copied into shared
-// memory while the previous layer runs. No CTA ever spins on memory: the only waits are cluster
-// barriers, which every CTA reaches the same number of times.
+// l3m_logits) on every CTA of the launch, a per-CTA argmax, and the same global argmax in every CTA
+// of cluster 0, in CTA order. Each exchanged vector has one buffer: its next write comes after every
+// reader has finished with it. The quantised weight tiles of the next matvec phase are copied into
+// shared memory by the tensor memory accelerator while the current phase runs; each layer's norm
+// weights and RoPE row are copied into shared memory while the previous layer runs.
+//
+// Waits. Cluster barriers are reached the same number of times by every CTA of the cluster. Every
+// other wait (an exchange's mbarrier, a weight copy's mbarrier, the head job flag and arrival count
+// in global memory) polls with a time limit; a wait that gives up records an error code and where it
+// was (CTA, position, layer, which wait) in the abort word, and every later wait of the launch stops
+// as soon as it sees that word set, so the launch ends at the next sampled position instead of
+// running every remaining wait to its limit. At entry every CTA checks that the launch has the shape
+// this code assumes (kClusterCtas CTAs per cluster, whole clusters, the grid of the arguments) and
+// ends at once with kErrShape otherwise, before any distributed-shared-memory access.
 #include <algorithm>
 #include <cstdio>
 #include <cooperative_groups.h>
@@ -235,43 +245,59 @@ __device__ __forceinline__ int stage_issue(const Smem &s, int dtype, const uint8
     return n;
 }
 
-// Every thread: wait for the outstanding copy (phase parity par of the mbarrier). Bounded by
-// timeout_ns; on timeout the abort word is set (the sampled position then stops the launch) and
-// the caller goes on with whatever the buffer holds.
-__device__ __forceinline__ void stage_wait(const DecodeArgs &a, const Smem &s, uint32_t par) {
-    const uint32_t bar = smem_addr(s.wbar);
+// The first failure of the launch: its code, and where it happened (the first CTA to record wins).
+__device__ __noinline__ void record_abort(const DecodeArgs &a, int code, int pos, int layer, int wait) {
+    if (atomicCAS(a.hx.abort_flag, 0, code) == 0) {
+        volatile int *w = a.hx.abort_flag;
+        w[1] = blockIdx.x;
+        w[2] = pos;
+        w[3] = layer;
+        w[4] = wait;
+    }
+}
+__device__ __forceinline__ bool aborted(const DecodeArgs &a) { return *(volatile int *)a.hx.abort_flag != 0; }
+
+// Poll phase parity par of the mbarrier at shared address bar until it completes (true), the time
+// limit passes (false, the failure recorded as code/where) or, with abortable, another CTA has
+// recorded a failure (false).
+__device__ __forceinline__ bool mbar_wait_bounded(const DecodeArgs &a, uint32_t bar, uint32_t par, bool abortable, int code, int pos, int layer,
+                                                  int wait) {
     uint64_t t0 = 0;
     for (int spins = 0;; spins++) {
         uint32_t done;
         asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
                      : "=r"(done) : "r"(bar), "r"(par) : "memory");
-        if (done) return;
-        if (spins == 0) t0 = globaltimer_ns();
-        else if ((spins & 63) == 0 && globaltimer_ns() - t0 > a.hx.timeout_ns) {
-            atomicCAS(a.hx.abort_flag, 0, kErrStageTimeout);
-            return;
+        if (done) return true;
+        if (spins == 0) {
+            t0 = globaltimer_ns();
+        } else if ((spins & 63) == 0) {
+            if (abortable && aborted(a)) return false;
+            if (globaltimer_ns() - t0 > a.hx.timeout_ns) {
+                record_abort(a, code, pos, layer, wait);
+                return false;
+            }
         }
     }
 }
 
+// Every thread: wait for the outstanding copy (phase parity par of the mbarrier). Time-limited, and
+// it stops early once a failure is recorded; the caller then goes on with whatever the buffer
+// holds (the sampled position ends the launch). final: the wait before the CTA exits, which must
+// see its own copy land (or its own limit pass) whatever other CTAs recorded.
+__device__ __forceinline__ void stage_wait(const DecodeArgs &a, const Smem &s, uint32_t par, int pos, int layer, bool final = false) {
+    mbar_wait_bounded(a, smem_addr(s.wbar), par, !final, kErrStageTimeout, pos, layer, kWaitStage);
+}
+
 // Exchange k (0-4) of the current layer has fully arrived in this CTA (phase parity par; every
-// thread, time-limited), then it is armed for the next layer: one arrival expecting `bytes`.
-__device__ __noinline__ void xwait(const DecodeArgs &a, const Smem &s, int k, uint32_t par, uint32_t bytes) {
+// thread, time-limited, stopping early once a failure is recorded), then it is armed for the next
+// layer: one arrival expecting `bytes`.
+__device__ __noinline__ void xwait(const DecodeArgs &a, const Smem &s, int k, uint32_t par, uint32_t bytes, int pos, int layer) {
     const uint32_t bar = smem_addr(s.xbar + k);
-    uint64_t t0 = 0;
-    for (int spins = 0;; spins++) {
-        uint32_t done;
-        asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-                     : "=r"(done) : "r"(bar), "r"(par) : "memory");
-        if (done) break;
-        if (spins == 0) t0 = globaltimer_ns();
-        else if ((spins & 63) == 0 && globaltimer_ns() - t0 > a.hx.timeout_ns) {
-            atomicCAS(a.hx.abort_flag, 0, kErrTimeout);
-            break;
-        }
-    }
+    const bool done = mbar_wait_bounded(a, bar, par, true, kErrTimeout, pos, layer, kWaitQkv + k);
     __syncthreads();                                                      // every thread has seen this phase complete
-    if (threadIdx.x == 0) asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+    // Re-armed only when thread 0 saw the phase complete (an arrival on a phase that still has its
+    // arrival is not allowed; after a failure the launch is ending anyway).
+    if (threadIdx.x == 0 && done) asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
 
 // x = embedding row of tok, plus the learned position row when the file has one (reference
@@ -333,7 +359,7 @@ __device__ __noinline__ void phase_qkv(const DecodeArgs &a, const LayerDev &L, c
     trace(a, tslot, pos, l, 16);
     prepare(L.dt_qkv, s.xb, a.dim, s.prep);
     trace(a, tslot, pos, l, 17);
-    if (ns) stage_wait(a, s, par);
+    if (ns) stage_wait(a, s, par, pos, l);
     trace(a, tslot, pos, l, 18);
     matvec_exact(L.dt_qkv, L.qkv, a.dim, role.qkv0, role.qkv1, s.prep, s.scratch, a.scratch_pairs, s.y, s.w + a.w_extra, ns);
     trace(a, tslot, pos, l, 19);
@@ -389,7 +415,7 @@ __device__ __noinline__ void phase_wo(const DecodeArgs &a, const LayerDev &L, co
                                       int l, int tslot) {
     prepare(L.dt_wo, s.xa, a.dim, s.prep);
     trace(a, tslot, pos, l, 20);
-    if (ns) stage_wait(a, s, par);
+    if (ns) stage_wait(a, s, par, pos, l);
     trace(a, tslot, pos, l, 21);
     matvec_exact(L.dt_wo, L.wo, a.dim, role.wo0, role.wo1, s.prep, s.scratch, a.scratch_pairs, s.y, s.w + a.w_extra, ns);
     trace(a, tslot, pos, l, 22);
@@ -414,7 +440,7 @@ __device__ __noinline__ void phase_ffn(const DecodeArgs &a, const LayerDev &L, c
     const int nf = role.ffn1 - role.ffn0;
     prepare(L.dt_up, s.xb, a.dim, s.prep);
     trace(a, tslot, pos, l, 26);
-    if (ns) stage_wait(a, s, par);
+    if (ns) stage_wait(a, s, par, pos, l);
     trace(a, tslot, pos, l, 12);
     if (GPT2 && a.gelu) {                                                 // GPT-2: up only
         matvec_exact(L.dt_up, L.up, a.dim, role.ffn0, role.ffn1, s.prep, s.scratch, a.scratch_pairs, s.y, s.w, ns);
@@ -446,7 +472,7 @@ __device__ __noinline__ void phase_down(const DecodeArgs &a, const LayerDev &L, 
                                         int l, int tslot) {
     prepare(L.dt_down, s.xh, a.ffn, s.prep);
     trace(a, tslot, pos, l, 23);
-    if (ns) stage_wait(a, s, par);
+    if (ns) stage_wait(a, s, par, pos, l);
     trace(a, tslot, pos, l, 24);
     matvec_exact(L.dt_down, L.down, a.ffn, role.dn0, role.dn1, s.prep, s.scratch, a.scratch_pairs, s.y, s.w, ns);
     trace(a, tslot, pos, l, 25);
@@ -625,7 +651,7 @@ __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t *p) {
 
 // Thread 0 waits until *p >= want (or, with done_ok, *p == kHeadDone), sleeping between polls; the
 // whole CTA learns the outcome: 1 reached, 0 done, -1 timeout or another CTA's abort.
-__device__ __noinline__ int wait_word(const DecodeArgs &a, const uint32_t *p, uint32_t want, bool done_ok) {
+__device__ __noinline__ int wait_word(const DecodeArgs &a, const uint32_t *p, uint32_t want, bool done_ok, int pos, int wait) {
     __shared__ int res;
     if (threadIdx.x == 0) {
         const uint64_t t0 = globaltimer_ns();
@@ -636,8 +662,8 @@ __device__ __noinline__ int wait_word(const DecodeArgs &a, const uint32_t *p, ui
             if (v >= want && v != kHeadDone) { r = 1; break; }
             __nanosleep(done_ok ? 256 : 64);
             if ((spins & 255) == 255) {
-                if (globaltimer_ns() - t0 > a.hx.timeout_ns) { atomicCAS(a.hx.abort_flag, 0, kErrTimeout); break; }
-                if (*(volatile int *)a.hx.abort_flag) break;
+                if (globaltimer_ns() - t0 > a.hx.timeout_ns) { record_abort(a, kErrTimeout, pos, -1, wait); break; }
+                if (aborted(a)) break;
             }
         }
         res = r;
@@ -709,7 +735,7 @@ __device__ __noinline__ void head_helper(const DecodeArgs &a, const Role &role, 
         prefetch_l2(a.head + role.voc0 * th, (size_t)(role.voc1 - role.voc0) * th);
     }
     for (uint32_t e = 1;; e++) {
-        if (wait_word(a, a.hx.flag, e, true) <= 0) return;
+        if (wait_word(a, a.hx.flag, e, true, -1, kWaitHeadFlag) <= 0) return;
         const int pos = __float_as_int(ld_cg_f32(a.hx.x + a.dim));
         if ((a.dim & 3) == 0)
             for (int i = threadIdx.x * 4; i < a.dim; i += blockDim.x * 4) *(float4 *)(s.x + i) = __ldcg((const float4 *)(a.hx.x + i));
@@ -736,6 +762,28 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
     __shared__ DecodeArgs sh_args;
     __shared__ Role sh_role;
     __shared__ Smem sh_s;
+    {
+        // The launch shape this code assumes; anything else ends every CTA here, before any access
+        // to another CTA's shared memory (which a cluster of another size would not have).
+        uint32_t ncta, ncl;
+        asm("mov.u32 %0, %%cluster_nctarank;" : "=r"(ncta));
+        asm("mov.u32 %0, %%nclusterid.x;" : "=r"(ncl));
+        const int grid = ap->grid;
+        if (ncta != (uint32_t)kClusterCtas || ncl * (uint32_t)kClusterCtas != gridDim.x || (int)gridDim.x != grid || gridDim.y != 1 ||
+            gridDim.z != 1 || blockDim.x != (uint32_t)kDecodeThreads || blockDim.y != 1 || blockDim.z != 1) {
+            if (blockIdx.x == 0 && threadIdx.x == 0) {
+                Ctrl *c = ap->ctrl;
+                c->where[0] = (int)ncta;
+                c->where[1] = (int)ncl;
+                c->where[2] = (int)gridDim.x;
+                c->where[3] = (int)blockDim.x;
+                c->error = kErrShape;
+                __threadfence_system();
+                c->done = 1;
+            }
+            return;
+        }
+    }
     if (threadIdx.x == 0) {
         sh_args = *ap;
         sh_role = ap->roles[blockIdx.x];
@@ -816,13 +864,13 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
                 else scatter(s.y, s.xq, g0, n);
             }
             trace(a, tslot, pos, l, 1);
-            if (a.async_x) xwait(a, s, 0, xpar, (uint32_t)a.n_qkv * 4);   // 1: qkv
+            if (a.async_x) xwait(a, s, 0, xpar, (uint32_t)a.n_qkv * 4, pos, l);   // 1: qkv
             else cluster_sync();
             trace(a, tslot, pos, l, 2);
             for (int h = role.head0; h >= 0 && h < a.n_heads; h += kClusterCtas)   // A
                 phase_attention(a, L, s, h, pos, h == role.head0, l, tslot);
             trace(a, tslot, pos, l, 3);
-            if (a.async_x) xwait(a, s, 1, xpar, (uint32_t)a.dim * 4);     // 2: attn
+            if (a.async_x) xwait(a, s, 1, xpar, (uint32_t)a.dim * 4, pos, l);     // 2: attn
             else cluster_sync();
             trace(a, tslot, pos, l, 4);
             if (role.wo0 < role.wo1) phase_wo(a, L, role, s, ns, wpar, pos, l, tslot);   // B
@@ -836,7 +884,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
                 else scatter(s.y, s.xp, g0, n);
             }
             trace(a, tslot, pos, l, 5);
-            if (a.async_x) xwait(a, s, 2, xpar, (uint32_t)a.dim * 4);     // 3: proj
+            if (a.async_x) xwait(a, s, 2, xpar, (uint32_t)a.dim * 4, pos, l);     // 3: proj
             else cluster_sync();
             trace(a, tslot, pos, l, 6);
             phase_ffn<GPT2>(a, L, role, s, pos, l, tslot, ns, wpar);      // C
@@ -853,7 +901,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
             if (l + 1 < a.n_layers) stage_vectors<GPT2>(a, layers[l + 1], role, s, pos);
             else stage_vectors<GPT2>(a, layers[0], role, s, pos + 1);
             trace(a, tslot, pos, l, 8);
-            if (a.async_x) xwait(a, s, 3, xpar, (uint32_t)a.ffn * 4);     // 4: h
+            if (a.async_x) xwait(a, s, 3, xpar, (uint32_t)a.ffn * 4, pos, l);     // 4: h
             else cluster_sync();
             trace(a, tslot, pos, l, 9);
             if (role.dn0 < role.dn1) phase_down(a, L, role, s, ns, wpar, pos, l, tslot);   // D
@@ -870,7 +918,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
             }
             trace(a, tslot, pos, l, 10);
             if (a.async_x) {                                              // 5: down
-                xwait(a, s, 4, xpar, (uint32_t)a.dim * 4);
+                xwait(a, s, 4, xpar, (uint32_t)a.dim * 4, pos, l);
                 xpar ^= 1u;
             } else {
                 cluster_sync();
@@ -903,7 +951,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
             __syncthreads();
             scatter(s.tmp, s.xt, 4 + 4 * cta, 4);
         } else if (cta == 0) {
-            const int r = wait_word(a, a.hx.count, tcount * (uint32_t)a.grid, false);
+            const int r = wait_word(a, a.hx.count, tcount * (uint32_t)a.grid, false, pos, kWaitHeadCount);
             float *sl = s.tmp + 4;                                        // every slot at once, then a serial scan
             for (int i = tid; i < 3 * a.grid; i += blockDim.x) sl[i] = ld_cg_f32(a.hx.slots + i);
             __syncthreads();
@@ -938,6 +986,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
         const int stop_req = __float_as_int(s.xt[1]);
         const float gmax_all = s.xt[3];
         if (!__float_as_int(s.xt[2])) { ok = false; break; }
+        if (next < 0 || next >= a.vocab) {                                // never expected: the same in every CTA
+            if (tid == 0) record_abort(a, kErrToken, pos, -1, next);
+            ok = false;
+            break;
+        }
         trace(a, tslot, pos, a.n_layers, 2);
         if (stop_after) break;                                            // logits kept, nothing sampled (uniform)
         if (a.temp > 0.0f) {                                              // every CTA of cluster 0, in step
@@ -957,13 +1010,14 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
         // reaches after reading it here.
     }
     cp_async_wait_all();                                                  // no copy outlives the CTA
-    if (ns) stage_wait(a, s, wpar);
+    if (ns) stage_wait(a, s, wpar, pos, -1, true);
     cluster_sync();                                                       // no CTA leaves while others may write its memory
     if (cta == 0 && tid == 0) {
         asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.hx.flag), "r"(kHeadDone) : "memory");   // the helpers stop
         const int err = *(volatile int *)a.hx.abort_flag;
         a.ctrl->final_pos = pos;
         a.ctrl->n_gen = n_gen;
+        for (int i = 0; i < 4; i++) a.ctrl->where[i] = ((volatile int *)a.hx.abort_flag)[1 + i];
         a.ctrl->error = ok ? 0 : (err ? err : kErrTimeout);
         __threadfence_system();
         a.ctrl->done = 1;

@@ -29,6 +29,8 @@ struct Ctrl {
     volatile int32_t n_gen;          // tokens the device accepted
     volatile int32_t stop_request;   // set by the host when on_token returns 0
     volatile int32_t error;          // nonzero: a device-side failure (kErr*)
+    volatile int32_t where[4];       // the first failure: CTA, position, layer, wait (kWait*); for kErrShape
+                                     // the launch shape seen: CTAs per cluster, clusters, grid, block
     volatile int32_t pad[2];
 };
 
@@ -44,11 +46,17 @@ struct HeadX {
     uint32_t *flag;                     // tcount of the published x; kHeadDone when generation ends
     uint32_t *count;                    // arrivals: grid per sampled position
     float *slots;                       // [grid][2] (max, index bits)
-    int *abort_flag;                    // first error code of any CTA
+    int *abort_flag;                    // [0]: first error code of any CTA; [1..4]: where (as Ctrl::where)
     unsigned long long timeout_ns;
 };
 constexpr uint32_t kHeadDone = 0xFFFFFFFFu;
-enum { kErrNone = 0, kErrTimeout = 1, kErrStageTimeout = 2 };   // a wait on another CTA; a wait on a weight copy
+// Error codes: a wait on another CTA gave up; a wait on a weight copy gave up; the launch does not
+// have the shape the kernel was built for (cluster size, cluster count, grid, block); a sampled token
+// outside the vocabulary.
+enum { kErrNone = 0, kErrTimeout = 1, kErrStageTimeout = 2, kErrShape = 3, kErrToken = 4 };
+// Which wait gave up (Ctrl::where[3]): exchanges 1-5 of a layer, the weight copy, the head job flag
+// (helper clusters), the head arrival count (CTA 0).
+enum { kWaitQkv = 1, kWaitAttn = 2, kWaitProj = 3, kWaitH = 4, kWaitDown = 5, kWaitStage = 8, kWaitHeadFlag = 9, kWaitHeadCount = 10 };
 
 struct DecodeArgs {
     int dim, hd, ffn, vocab, ctx, n_heads, n_kv, hpk, n_layers, n_qkv, grid;   // n_qkv = (n_heads + 2 n_kv) hd; grid: all CTAs

@@ -545,6 +545,29 @@ bool place_in_l2(l3m_model *m, Gpu &g, const l3m_opts &o, bool *over) {
     return true;
 }
 
+// What the decode kernel recorded about the first failure of a launch.
+void report_decode_error(const l3m::Ctrl *c) {
+    const int e = c->error;
+    if (!c->done) {
+        fprintf(stderr, "l3m: decode kernel did not finish\n");
+    } else if (e == l3m::kErrShape) {
+        fprintf(stderr, "l3m: decode kernel launched with %d CTAs per cluster, %d clusters, grid %d, block %d; it needs clusters of %d "
+                "CTAs of %d threads (code %d)\n", c->where[0], c->where[1], c->where[2], c->where[3], l3m::kClusterCtas,
+                l3m::kDecodeThreads, e);
+    } else {
+        static const char *waits[] = {"?", "exchange 1 (qkv)", "exchange 2 (attention)", "exchange 3 (wo)", "exchange 4 (ffn gate)",
+                                      "exchange 5 (down)", "?", "?", "a weight copy", "the head job flag", "the head arrivals"};
+        const int w = c->where[3];
+        const char *what = e == l3m::kErrTimeout ? "a wait on another CTA gave up" : e == l3m::kErrStageTimeout ? "a weight copy wait gave up"
+                           : e == l3m::kErrToken ? "a sampled token outside the vocabulary" : "unknown error";
+        if (e == l3m::kErrToken)
+            fprintf(stderr, "l3m: decode kernel: %s (token %d at position %d, code %d)\n", what, w, c->where[1], e);
+        else
+            fprintf(stderr, "l3m: decode kernel: %s: CTA %d, position %d, layer %d, waiting for %s (code %d)\n", what, c->where[0],
+                    c->where[1], c->where[2], w >= 0 && w <= 10 ? waits[w] : "?", e);
+    }
+}
+
 }  // namespace
 
 extern "C" {
@@ -737,7 +760,7 @@ L3M_API int l3m_generate(l3m_model *m, const int32_t *prompt, int n_prompt, int 
     const double t1 = now_ns();
     if (!cuda_ok(e, "decode")) return -1;
     if (!m->ctrl->done || m->ctrl->error) {
-        fprintf(stderr, "l3m: decode kernel %s (code %d)\n", m->ctrl->done ? "reported an error" : "did not finish", m->ctrl->error);
+        report_decode_error(m->ctrl);
         return -1;
     }
     int last_pos;

@@ -119,12 +119,12 @@ size_t stream_smem(int k, const StreamPlan &pl) {
     return ((prep_smem(k) + 127) & ~(size_t)127) + (size_t)kStreamStages * pl.stage_bytes + (size_t)pl.scratch_pairs * sizeof(float2);
 }
 
-__device__ int g_stream_timeouts;                   // diagnostics: waits that gave up (never expected)
-
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
-// Wait for phase parity `par` of the mbarrier at shared address bar (time-limited: 2 s).
-__device__ __forceinline__ void mbar_wait(uint32_t bar, uint32_t par) {
+// Wait for phase parity `par` of the mbarrier at shared address bar (time-limited: 2 s). A wait that
+// gives up (never expected) marks the CTA failed (*fail: its outputs are written as NaN) and counts
+// itself in *timeouts, host-mapped memory that the next l3m_gemv_dev call reports as an error.
+__device__ __forceinline__ void mbar_wait(uint32_t bar, uint32_t par, int *fail, int *timeouts) {
     uint64_t start = 0;
     for (int spin = 0;; spin++) {
         uint32_t done;
@@ -132,15 +132,20 @@ __device__ __forceinline__ void mbar_wait(uint32_t bar, uint32_t par) {
                      : "=r"(done) : "r"(bar), "r"(par) : "memory");
         if (done) return;
         if (spin == 0) start = globaltimer_ns();
-        else if ((spin & 63) == 0 && globaltimer_ns() - start > 2000000000ull) { atomicAdd(&g_stream_timeouts, 1); return; }
+        else if ((spin & 63) == 0 && globaltimer_ns() - start > 2000000000ull) {
+            *(volatile int *)fail = 1;
+            atomicAdd_system(timeouts, 1);
+            return;
+        }
     }
 }
 
 template <int DT>
 __global__ void __launch_bounds__(kStreamThreads, 1) gemv_stream_kernel(float *y, const uint8_t *tiles, int ntiles, int k, VecArg x,
-                                                                         StreamPlan pl) {
+                                                                         StreamPlan pl, int *timeouts) {
     extern __shared__ __align__(16) unsigned char smem_stream[];
     __shared__ __align__(8) unsigned long long full[kStreamStages], empty[kStreamStages];
+    __shared__ int fail;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int bb = stream_unit_bytes(DT), nb = k / kQB;
     const size_t tb = (size_t)nb * bb;
@@ -150,6 +155,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gemv_stream_kernel(float *y
     const int t0 = (int)((long long)blockIdx.x * ntiles / gridDim.x), t1 = (int)((long long)(blockIdx.x + 1) * ntiles / gridDim.x);
     const int nch = (nb + pl.U - 1) / pl.U, total = (t1 - t0 + pl.G - 1) / pl.G * nch;
     if (tid == 0) {
+        fail = 0;
         for (int i = 0; i < kStreamStages; i++) {
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&full[i])) : "memory");
             asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&empty[i])), "r"(kStreamWarps) : "memory");
@@ -161,7 +167,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gemv_stream_kernel(float *y
     // have released that stage (from the second round of the ring on).
     auto issue = [&](int c) {
         const int st = c % kStreamStages;
-        if (c >= kStreamStages) mbar_wait(smem_u32(&empty[st]), (uint32_t)(c / kStreamStages + 1) & 1u);
+        if (c >= kStreamStages) mbar_wait(smem_u32(&empty[st]), (uint32_t)(c / kStreamStages + 1) & 1u, &fail, timeouts);
         const int g0 = t0 + c / nch * pl.G, ng = min(pl.G, t1 - g0), b0 = c % nch * pl.U, nu = min(pl.U, nb - b0);
         unsigned char *buf = stage0 + (size_t)st * pl.stage_bytes;
         const uint32_t bar = smem_u32(&full[st]);
@@ -186,7 +192,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gemv_stream_kernel(float *y
         const int st = c % kStreamStages, g0 = t0 + c / nch * pl.G, ng = min(pl.G, t1 - g0), cb = c % nch, b0 = cb * pl.U,
                   nu = min(pl.U, nb - b0);
         const unsigned char *buf = stage0 + (size_t)st * pl.stage_bytes;
-        mbar_wait(smem_u32(&full[st]), (uint32_t)(c / kStreamStages) & 1u);
+        mbar_wait(smem_u32(&full[st]), (uint32_t)(c / kStreamStages) & 1u, &fail, timeouts);
         if (DT == DT_BF16) {
             if (tid < ng * kTile) {                                         // output (tile g, row r): its chain over the chunk's inputs
                 const int g = tid >> 4, r = tid & 15;
@@ -238,7 +244,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gemv_stream_kernel(float *y
                 }
                 asm volatile("bar.sync 1, %0;" ::"n"(32 * kStreamWarps) : "memory");   // read before the next wave writes
             }
-            if (tid < ng * kTile) y[(size_t)(g0 + (tid >> 4)) * kTile + (tid & 15)] = acc;
+            if (tid < ng * kTile) y[(size_t)(g0 + (tid >> 4)) * kTile + (tid & 15)] = *(volatile int *)&fail ? __int_as_float(0x7FC00000) : acc;
             acc = 0.0f;
         }
     }
@@ -354,6 +360,38 @@ __global__ void __launch_bounds__(kThreads) attend_kernel(float *out, const floa
 
 VecArg vec_arg(const l3m_vec *x) { return VecArg{x->f32, x->bf16, x->q8, x->scale, x->sum}; }
 
+// The kernels read tiles with 16-byte (and 4-byte) loads and x, y as 4-byte words: a misaligned
+// pointer would fault the caller's context, so it is refused before anything launches.
+bool misaligned_args(int dtype, const void *y, const void *tiles, const l3m_vec *x) {
+    uintptr_t w = (uintptr_t)y | (uintptr_t)tiles;
+    if (dtype == DT_F32) w |= (uintptr_t)x->f32;
+    else if (dtype == DT_BF16) w |= (uintptr_t)x->bf16 & 1;
+    else w |= (uintptr_t)x->q8 | (uintptr_t)x->scale | (uintptr_t)x->sum | ((uintptr_t)tiles & 15);
+    return (w & 3) != 0 || (dtype >= DT_Q8 && ((uintptr_t)tiles & 15) != 0);
+}
+
+// The streamed kernel's count of waits that gave up, in host-mapped memory (one counter for every
+// device: the host pointer is the device pointer under unified addressing). A count that changed
+// since the last call means an earlier launch wrote NaN outputs: this call reports it and fails.
+int stream_timeouts(int **dev_ptr) {
+    static std::mutex mu;
+    static int *host = nullptr, seen = 0;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!host) {
+        cudaError_t e = cudaHostAlloc((void **)&host, sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable);
+        if (e != cudaSuccess) { host = nullptr; return fail(e, "l3m_gemv_dev: host-mapped timeout counter"); }
+        *host = 0;
+    }
+    const int now = *(volatile int *)host;
+    if (now != seen) {
+        snprintf(g_err, sizeof g_err, "l3m_gemv_dev: %d weight-copy wait(s) of an earlier launch gave up; its y holds NaN", now - seen);
+        seen = now;
+        return -1;
+    }
+    *dev_ptr = host;
+    return 0;
+}
+
 int stream_sms() {
     static int sms = 0;
     if (!sms) {
@@ -427,6 +465,9 @@ L3M_API int l3m_gemv_dev(int exact, int dtype, float *y, const void *tiles, int 
     if (dtype == DT_BF16 && k % 2) return fail_msg("l3m_gemv_dev: bf16 k must be even");
     if (ntiles == 0) return 0;
     if (!y || !tiles || !x) return fail_msg("l3m_gemv_dev: y, tiles and x are required");
+    if (misaligned_args(dtype, y, tiles, x)) return fail_msg("l3m_gemv_dev: misaligned pointer (y, f32/q8/scale/sum and bf16/f32 tiles 4-byte, quantised tiles 16-byte, bf16 x 2-byte)");
+    int *tmo = nullptr;
+    if (stream_timeouts(&tmo)) return -1;
     cudaStream_t s = (cudaStream_t)stream;
     static const bool stream_off = getenv("L3M_GEMV_STREAM") && !strcmp(getenv("L3M_GEMV_STREAM"), "0");
     if (!exact && dtype <= DT_BF16) {
@@ -441,19 +482,19 @@ L3M_API int l3m_gemv_dev(int exact, int dtype, float *y, const void *tiles, int 
         switch (dtype) {
         case DT_BF16:
             e = cudaFuncSetAttribute(gemv_stream_kernel<DT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (e == cudaSuccess) gemv_stream_kernel<DT_BF16><<<grid, kStreamThreads, smem, s>>>(y, t, ntiles, k, vec_arg(x), pl);
+            if (e == cudaSuccess) gemv_stream_kernel<DT_BF16><<<grid, kStreamThreads, smem, s>>>(y, t, ntiles, k, vec_arg(x), pl, tmo);
             break;
         case DT_Q8:
             e = cudaFuncSetAttribute(gemv_stream_kernel<DT_Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (e == cudaSuccess) gemv_stream_kernel<DT_Q8><<<grid, kStreamThreads, smem, s>>>(y, t, ntiles, k, vec_arg(x), pl);
+            if (e == cudaSuccess) gemv_stream_kernel<DT_Q8><<<grid, kStreamThreads, smem, s>>>(y, t, ntiles, k, vec_arg(x), pl, tmo);
             break;
         case DT_Q4:
             e = cudaFuncSetAttribute(gemv_stream_kernel<DT_Q4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (e == cudaSuccess) gemv_stream_kernel<DT_Q4><<<grid, kStreamThreads, smem, s>>>(y, t, ntiles, k, vec_arg(x), pl);
+            if (e == cudaSuccess) gemv_stream_kernel<DT_Q4><<<grid, kStreamThreads, smem, s>>>(y, t, ntiles, k, vec_arg(x), pl, tmo);
             break;
         default:
             e = cudaFuncSetAttribute(gemv_stream_kernel<DT_MX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (e == cudaSuccess) gemv_stream_kernel<DT_MX><<<grid, kStreamThreads, smem, s>>>(y, t, ntiles, k, vec_arg(x), pl);
+            if (e == cudaSuccess) gemv_stream_kernel<DT_MX><<<grid, kStreamThreads, smem, s>>>(y, t, ntiles, k, vec_arg(x), pl, tmo);
         }
         if (e != cudaSuccess) return fail(e, "l3m_gemv_dev");
     } else {

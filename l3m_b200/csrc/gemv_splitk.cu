@@ -18,7 +18,12 @@
 //  - the scratch is one buffer per device and per process: calls that overlap on one device (two
 //    streams, two host threads) race on it and must be serialised by the caller;
 //  - the first call on each device looks up the buffer's address (cudaGetSymbolAddress, which may
-//    load this library's device code); make that first call before any stream capture.
+//    load this library's device code); make that first call before any stream capture;
+//  - that address is kept for the life of the process: it belongs to the device's context of the
+//    first call, so a device reset (cudaDeviceReset, or a reset of the primary context) while this
+//    library is loaded leaves it stale; do not reset a device that this entry point has used;
+//  - misaligned pointers (tiles, y, and x's q8, scale and sum must be 4-byte aligned) are refused
+//    before anything launches, like every other bad argument.
 #include <cuda_runtime.h>
 #include <cstdio>
 #include <mutex>
@@ -112,6 +117,8 @@ extern "C" L3M_API int l3m_gemv_splitk_dev(int dtype, float *y, const void *tile
     if (ntiles == 0) return 0;
     if (!y || !tiles || !x || !x->q8 || !x->scale || !x->sum)
         return l3m_error_msg("l3m_gemv_splitk_dev: y, tiles and a prepared x (q8, scale, sum) are required");
+    if (((uintptr_t)tiles | (uintptr_t)y | (uintptr_t)x->q8 | (uintptr_t)x->scale | (uintptr_t)x->sum) & 3)
+        return l3m_error_msg("l3m_gemv_splitk_dev: tiles, y, q8, scale and sum must be 4-byte aligned");
     DeviceSlot slot;
     if (setup(&slot)) return -1;
     cudaStream_t s = (cudaStream_t)stream;

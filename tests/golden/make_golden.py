@@ -26,7 +26,10 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-REF = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+_ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("L3M_REF_SRC")
+if not _ref:
+    sys.exit("usage: make_golden.py <reference checkout> (or set L3M_REF_SRC)")
+REF = Path(_ref)
 sys.path.insert(0, str(REF / "python"))
 sys.path.insert(0, str(ROOT))
 
