@@ -3,6 +3,7 @@
 logits and perf, with `cpus` read as a list of GPU ordinals. The library is the in-tree
 l3m_b200/libl3m.so (override with L3M_LIB); there is no CPU fallback.
 """
+import contextlib
 import ctypes as C
 import functools
 import os
@@ -98,41 +99,69 @@ def kernels(name="sm100a"):
     return Kernels.in_dll(lib(), sym)
 
 
+class _TokenSink:
+    """The C on_token callback of one generate call: collects ids, forwards each to the user's
+    callback, and turns its False (or an exception, kept for re-raising) into a stop request."""
+
+    def __init__(self, user):
+        self.ids, self.user, self.error = [], user, None
+        self.cfunc = _CB(self._on_token)        # referenced until the call returns
+
+    def _on_token(self, tok, _user):
+        self.ids.append(tok)
+        if self.user is None:
+            return 1
+        try:
+            return 0 if self.user(tok) is False else 1
+        except BaseException as e:              # noqa: BLE001 -- re-raised on the caller's thread
+            self.error = e
+            return 0
+
+
 class Model:
-    """A loaded .l3m file on one or more GPUs (cpus: GPU ordinals, default GPU 0) with a KV cache
-    of ctx (default min(model, 512)). Thread-safe; on_token may read the model but not generate
-    or close it."""
-    _m = None
+    """A .l3m model loaded on GPUs (cpus: GPU ordinals, default GPU 0) with a KV cache of ctx entries
+    (default min(model, 512)); the reference binding's interface (python/l3m/__init__.py:53-157).
+
+    Calls on one model are serialised. Inside on_token the model can be read (logits, decode,
+    describe, perf) but generate and close raise RuntimeError; every call on a closed model raises
+    ValueError. A negative return from the library raises RuntimeError (its reason is on stderr)."""
 
     def __init__(self, path, cpus=None, ctx=0, reference=False, force=False, verbose=False, cold=False):
-        self._lock, self._generating = threading.RLock(), False
         if ctx and ctx < 2:
             raise ValueError(f"ctx {ctx}: needs room for a prompt token and one more")
-        self._lib = lib()
-        opts = Opts(ctx=ctx, reference=int(reference), force=int(force), verbose=int(verbose), cold=int(cold))
-        if cpus:
-            self._cpus = (C.c_int * len(cpus))(*cpus)
-            opts.cpus, opts.n_cpus = self._cpus, len(cpus)
-        self._m = self._lib.l3m_load(os.fsencode(path), C.byref(opts))
-        if not self._m:
+        self._lib, self._lock, self._in_callback, self._ptr = lib(), threading.RLock(), False, None
+        gpus = list(cpus or [])
+        self._gpu_array = (C.c_int * max(1, len(gpus)))(*gpus)
+        opts = Opts(cpus=self._gpu_array if gpus else None, n_cpus=len(gpus), ctx=ctx, reference=int(bool(reference)),
+                    force=int(bool(force)), verbose=int(bool(verbose)), cold=int(bool(cold)))
+        ptr = self._lib.l3m_load(os.fsencode(path), C.byref(opts))
+        if not ptr:
             raise RuntimeError(f"l3m_load failed for {path} (the reason is on stderr)")
-        self.vocab, self.ctx = self._lib.l3m_vocab(self._m), self._lib.l3m_ctx(self._m)
-        self.bos, self.eos = self._lib.l3m_bos(self._m), self._lib.l3m_eos(self._m)
+        self._ptr = ptr
+        L = self._lib
+        self.vocab, self.ctx, self.bos, self.eos = L.l3m_vocab(ptr), L.l3m_ctx(ptr), L.l3m_bos(ptr), L.l3m_eos(ptr)
 
-    def _handle(self, writing=False):
-        if writing and self._generating:
-            raise RuntimeError("l3m: on_token cannot call generate or close")
-        if not self._m:
-            raise ValueError("l3m: model is closed")
-        return self._m
+    @contextlib.contextmanager
+    def _using(self, mutates=False):
+        """The model's pointer, with the lock held; refuses what the current state does not allow."""
+        with self._lock:
+            if mutates and self._in_callback:
+                raise RuntimeError("l3m: on_token cannot call generate or close")
+            if not self._ptr:
+                raise ValueError("l3m: model is closed")
+            yield self._ptr
 
     def close(self):
         with self._lock:
-            if self._m:
-                self._lib.l3m_free(self._handle(writing=True))
-                self._m = None
+            if self._ptr is None:
+                return
+            with self._using(mutates=True) as ptr:
+                self._ptr = None
+                self._lib.l3m_free(ptr)
 
-    __del__ = close
+    def __del__(self):
+        if getattr(self, "_ptr", None):
+            self.close()
 
     def __enter__(self):
         return self
@@ -141,68 +170,57 @@ class Model:
         self.close()
 
     def describe(self):
-        with self._lock:
-            return self._lib.l3m_describe(self._handle()).decode()
+        with self._using() as ptr:
+            return self._lib.l3m_describe(ptr).decode()
 
     def encode(self, text, bos=True):
         if "\0" in text:
             raise ValueError("l3m: text contains a NUL")
-        data = text.encode()
-        buf = (C.c_int32 * (len(data) + 8))()
-        with self._lock:
-            n = self._lib.l3m_encode(self._handle(), data, int(bos), buf, len(buf))
-        return list(buf[:n])
+        raw = text.encode()
+        ids = (C.c_int32 * (len(raw) + 8))()          # one id per byte at most, plus BOS and the SentencePiece space
+        with self._using() as ptr:
+            n = self._lib.l3m_encode(ptr, raw, int(bool(bos)), ids, len(ids))
+        return ids[:max(n, 0)]
 
     def decode_bytes(self, ids):
-        out, n = bytearray(), C.c_int()
-        with self._lock:
-            for t in ids:
-                if not 0 <= t < self.vocab:
-                    raise ValueError(f"token {t} is outside vocab {self.vocab}")
-                out += C.string_at(self._lib.l3m_decode(self._handle(), t, C.byref(n)), n.value)
-        return bytes(out)
+        bad = [t for t in ids if not 0 <= t < self.vocab]
+        if bad:
+            raise ValueError(f"token {bad[0]} is outside vocab {self.vocab}")
+        size = C.c_int()
+        with self._using() as ptr:
+            return b"".join(C.string_at(self._lib.l3m_decode(ptr, t, C.byref(size)), size.value) for t in ids)
 
     def decode(self, ids):
         return self.decode_bytes(ids).decode("utf-8", errors="replace")
 
     def generate(self, prompt, max_new, temperature=0.8, seed=0, on_token=None):
         """Up to max_new token ids after prompt, stopping at EOS or BOS; on_token(id) returning False stops."""
-        if not 0 < len(prompt) < self.ctx or not all(0 <= t < self.vocab for t in prompt):
+        prompt = list(prompt)
+        if not (0 < len(prompt) < self.ctx and all(0 <= t < self.vocab for t in prompt)):
             raise ValueError(f"prompt of {len(prompt)} ids: needs 1 to {self.ctx - 1} ids, each below vocab {self.vocab}")
-        out, err = [], []
-
-        def cb(tok, _):
-            out.append(tok)
+        sink = _TokenSink(on_token)
+        ids = (C.c_int32 * len(prompt))(*prompt)
+        with self._using(mutates=True) as ptr:
+            self._in_callback = True
             try:
-                return 0 if on_token is not None and on_token(tok) is False else 1
-            except BaseException as e:
-                err.append(e)
-                return 0
-
-        buf = (C.c_int32 * len(prompt))(*prompt)
-        with self._lock:
-            m = self._handle(writing=True)
-            self._generating = True
-            try:
-                rc = self._lib.l3m_generate(m, buf, len(prompt), min(max_new, self.ctx), temperature, seed % 2**64, _CB(cb), None)
+                rc = self._lib.l3m_generate(ptr, ids, len(ids), min(max_new, self.ctx), temperature, seed % 2**64, sink.cfunc, None)
             finally:
-                self._generating = False
-        if err:
-            raise err[0]
+                self._in_callback = False
+        if sink.error is not None:
+            raise sink.error
         if rc < 0:
             raise RuntimeError("l3m_generate failed (the reason is on stderr)")
-        return out
+        return sink.ids
 
     @property
     def logits(self):
-        """The last position's logits."""
-        with self._lock:
-            return np.ctypeslib.as_array(self._lib.l3m_logits(self._handle()), shape=(self.vocab,)).copy()
+        """The logits of the last position run (during on_token: of the token just produced)."""
+        with self._using() as ptr:
+            return np.ctypeslib.as_array(self._lib.l3m_logits(ptr), shape=(self.vocab,)).copy()
 
     def perf(self):
         """Per-token counters since the previous call; NaN where unavailable."""
-        p = Perf()
-        with self._lock:
-            if self._lib.l3m_perf_read(self._handle(), C.byref(p)):
-                return {f: float("nan") for f, _ in Perf._fields_}
-        return {f: getattr(p, f) for f, _ in Perf._fields_}
+        counters = Perf()
+        with self._using() as ptr:
+            ok = self._lib.l3m_perf_read(ptr, C.byref(counters)) == 0
+        return {name: getattr(counters, name) if ok else float("nan") for name, _ in Perf._fields_}

@@ -754,8 +754,12 @@ __device__ __noinline__ void head_helper(const DecodeArgs &a, const Role &role, 
 // One instance per model family and cache mode, so that neither costs the other registers or
 // branches: GPT2 (LayerNorm, learned positions, GELU: the GPT-2 family's layers), COLD (every weight
 // copy with an L2 evict-first policy).
+// The cluster shape is part of the kernel (__cluster_dims__), not only of the launch: a launch
+// attribute alone is dropped by some launch paths (a profiler's replay ran this kernel as clusters of
+// one CTA, which the entry check reports as kErrShape), while a compile-time shape holds for every
+// launch of the function.
 template <bool GPT2, bool COLD>
-__global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeArgs *__restrict__ ap) {
+__global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeArgs *__restrict__ ap) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     // The arguments, this CTA's role, every layer's pointers and the carved shared-memory pointers
     // live in shared memory for the whole launch.
@@ -1058,21 +1062,22 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) sample_kernel(const float *
 
 namespace {
 
-// grid CTAs in clusters of kClusterCtas, all resident at once (cooperative): the helper clusters wait
-// on cluster 0 through global memory.
+// grid CTAs in clusters of kClusterCtas (the kernel's compile-time cluster shape), all resident at
+// once (cooperative): the helper clusters wait on cluster 0 through global memory. at[1] carries the
+// cluster shape for the occupancy query only (numAttrs 2); the launch itself uses numAttrs 1.
 cudaLaunchConfig_t cluster_config(int grid, int smem_bytes, cudaLaunchAttribute *at) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(l3m::kDecodeThreads);
     cfg.dynamicSmemBytes = (size_t)smem_bytes;
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = (unsigned)l3m::kClusterCtas;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = 1;
-    at[1].id = cudaLaunchAttributeCooperative;
-    at[1].val.cooperative = 1;
+    at[0].id = cudaLaunchAttributeCooperative;
+    at[0].val.cooperative = 1;
+    at[1].id = cudaLaunchAttributeClusterDimension;
+    at[1].val.clusterDim.x = (unsigned)l3m::kClusterCtas;
+    at[1].val.clusterDim.y = 1;
+    at[1].val.clusterDim.z = 1;
     cfg.attrs = at;
-    cfg.numAttrs = 2;
+    cfg.numAttrs = 1;
     return cfg;
 }
 
@@ -1165,6 +1170,7 @@ extern "C" int l3m_decode_occupancy(int smem_bytes) {
         if (set_attributes(fn, smem_bytes) != cudaSuccess) return 0;
         cudaLaunchAttribute at[2];
         cudaLaunchConfig_t cfg = cluster_config(l3m::kClusterCtas, smem_bytes, at);
+        cfg.attrs = at + 1;                                               // the cluster shape, not cooperative
         cfg.numAttrs = 1;
         int n = 0;
         if (cudaOccupancyMaxActiveClusters(&n, (const void *)fn, &cfg) != cudaSuccess) return 0;

@@ -15,10 +15,12 @@ typedef struct {
     l3m_tokenizer     tok;
     int               im_start;       // ChatML, when system is not NULL
     const char       *system;
+    uint32_t         *index;          // hashed table-of-contents names (entry + 1; 0 empty)
+    uint32_t          index_slots;    // a power of two
 } l3m_file;
 
 // 0 on success; otherwise -1 with "l3m: <path>: <reason>" on stderr (the reference's messages,
-// src/file.c:14-139, so callers that match on them keep working).
+// src/file.c:14-139, so callers that match on them keep working). Replaces src/file.h:1-22.
 int               l3m_file_open(l3m_file *f, const char *path);
 void              l3m_file_close(l3m_file *f);
 const l3m_tensor *l3m_file_tensor(const l3m_file *f, const char *name);     // NULL if absent

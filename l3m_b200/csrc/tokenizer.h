@@ -1,5 +1,5 @@
-// The tokenizer section of a .l3m file: byte-table decoder and greedy merge encoder
-// (the reference's tokenizer semantics, src/tokenizer.c:1-177).
+// The tokenizer section of a .l3m file: byte-table decoder and best-pair merge encoder, with the
+// reference's observable behaviour (src/tokenizer.h:1-19 is the interface this replaces).
 #pragma once
 #ifdef __cplusplus
 extern "C" {
@@ -13,7 +13,8 @@ typedef struct {
     const uint8_t **bytes;                    // into the file mapping
     const uint16_t *len;
     const float    *score;
-    int            *order;                    // ids by (bytes, length, higher score first, id)
+    uint32_t       *slots;                    // hash table bytes -> id + 1 (0: empty), nslots a power of two
+    uint32_t        nslots;
 } l3m_tokenizer;
 
 int            l3m_tokenizer_init(l3m_tokenizer *t, const void *section, size_t size, unsigned flags);   // -1 if malformed

@@ -325,6 +325,51 @@ def test_merges_match_quadratic_reference(tok_bin, tmp_path):
     assert encode(tok_bin, p, texts) == wants
 
 
+def reference_encoder(path):
+    """The compiled reference's encoder (oracle/_ref, its public l3m_load + l3m_encode on the CPU)."""
+    from l3m_b200 import Opts
+    so = ROOT / "oracle" / "_ref" / "libl3m.so"
+    if not so.exists():
+        pytest.skip("oracle/_ref not built (make -C oracle ref needs the reference sources)")
+    lib = C.CDLL(str(so))
+    lib.l3m_load.restype = C.c_void_p
+    lib.l3m_load.argtypes = [C.c_char_p, C.POINTER(Opts)]
+    lib.l3m_encode.argtypes = [C.c_void_p, C.c_char_p, C.c_int, C.POINTER(C.c_int32), C.c_int]
+    lib.l3m_free.argtypes = [C.c_void_p]
+    one = (C.c_int * 1)(0)
+    m = lib.l3m_load(str(path).encode(), C.byref(Opts(cpus=one, n_cpus=1, force=1)))
+    assert m
+
+    def enc(text, bos=False):
+        data = text.encode()
+        buf = (C.c_int32 * (len(data) + 8))()
+        n = lib.l3m_encode(m, data, int(bos), buf, len(buf))
+        return list(buf[:n])
+    return enc, lambda: lib.l3m_free(m)
+
+
+@pytest.mark.parametrize("flags", ["bpe", "digits", "sp"])
+def test_tokenizer_matches_compiled_reference(tok_bin, tmp_path, flags):
+    """The encoder against the reference's own (compiled from its sources) on random texts over
+    letters, digits, apostrophes, whitespace runs and UTF-8, with a vocabulary of overlapping merges."""
+    import random
+    rng = random.Random(7)
+    alphabet = "abcxyz 019',.\n\t" + "üé🐍"
+    merges = [(b"ab", -3.0), (b"bc", -1.0), (b"xy", -1.0), (b"xyz", -2.0), (b"aa", -4.0), (b" a", -5.0), (b" ab", -2.5),
+              (b"\n\n", -1.5), (b"'s", -2.0), (b"01", -0.5), (b" 0", -0.7), (b"  ", -0.2), ("ü".encode(), -9.0),
+              ("üé".encode(), -0.1), (b"ab", -0.05), (b"c,", -1.0), (b" x", -0.3)]
+    flag = {"bpe": 0, "digits": synth.DIGITS, "sp": synth.SP_PREFIX}[flags]
+    p = with_tokens(tmp_path / f"r{flags}.l3m", BYTES + merges, flag)
+    texts = ["".join(rng.choices(alphabet, k=rng.randrange(0, 80))) for _ in range(300)]
+    texts = [t for t in texts if "\0" not in t]
+    enc, close = reference_encoder(p)
+    try:
+        want = [enc(t) for t in texts] + [enc(t, True) for t in texts[:20]]
+    finally:
+        close()
+    assert encode(tok_bin, p, texts) + encode(tok_bin, p, texts[:20], bos=True) == want
+
+
 def test_long_piece_is_not_quadratic(tok_bin, tmp_path):
     import time
     p = with_tokens(tmp_path / "l.l3m", BYTES + MERGES)
@@ -383,3 +428,51 @@ def test_packed_writer_refuses_bad_input(lib, tmp_path):
     bad = tmp_path / "bad.l3m"
     bad.write_bytes(b"not a model")
     assert lib.l3m_write_packed(str(bad).encode(), str(tmp_path / "o.l3m").encode()) == -1
+
+
+# ---- the reference's own Python binding over this library
+
+def reference_checkout():
+    """The reference checkout (L3M_REF_SRC, else a `reference` directory beside this repository)."""
+    import os
+    for cand in (os.environ.get("L3M_REF_SRC"), ROOT.parent / "reference"):
+        if cand and (Path(cand) / "python" / "l3m" / "__init__.py").exists():
+            return Path(cand)
+    return None
+
+
+def test_reference_binding_binds_this_library():
+    """The reference's python/l3m (imported from its checkout, unchanged) finds libl3m.so through
+    L3M_LIB, binds every symbol of its signature table (python/l3m/__init__.py:23-50) and drives
+    l3m_load: on a host without a B200 the load is refused with the library's message and the
+    binding raises its RuntimeError. Its Opts and Perf structures have this library's layout."""
+    import os
+    ref = reference_checkout()
+    if ref is None:
+        pytest.skip("the reference checkout is not on this host")
+    probe = r"""
+import ctypes as C, sys
+sys.path.insert(0, sys.argv[1])
+import l3m
+lib = l3m._lib()
+print("LIB", lib._name)
+sys.path.insert(0, sys.argv[2])
+import l3m_b200
+assert C.sizeof(l3m.Opts) == C.sizeof(l3m_b200.Opts) and C.sizeof(l3m.Perf) == C.sizeof(l3m_b200.Perf)
+assert [f for f, _ in l3m.Opts._fields_] == [f for f, _ in l3m_b200.Opts._fields_]
+assert [f for f, _ in l3m.Perf._fields_] == [f for f, _ in l3m_b200.Perf._fields_]
+try:
+    l3m.Model(sys.argv[3], force=True)
+    print("LOADED")
+except RuntimeError as e:
+    print("REFUSED", e)
+"""
+    p = synth.llama(64, 2, 4, 2, 128, 300, 64, seed=1)
+    path = Path(os.environ.get("TMPDIR", "/tmp")) / "l3m_binding_probe.l3m"
+    synth.write(p, "q8_0", "q8_0", path)
+    env = dict(os.environ, L3M_LIB=str(ROOT / "l3m_b200" / "libl3m.so"), CUDA_VISIBLE_DEVICES="")
+    r = subprocess.run([sys.executable, "-c", probe, str(ref / "python"), str(ROOT), str(path)], capture_output=True, text=True, env=env,
+                       timeout=300)
+    assert r.returncode == 0, r.stderr
+    assert f"LIB {ROOT / 'l3m_b200' / 'libl3m.so'}" in r.stdout
+    assert "REFUSED" in r.stdout and "l3m: no CUDA device" in r.stderr, (r.stdout, r.stderr)
