@@ -188,7 +188,7 @@ def test_callback_stops_and_perf_counts(gpu, models):
 def test_c_api_contracts(gpu, models):
     """What the Python wrapper guards, refused by the C API too (reference test_engine.py:290-302)."""
     m = l3m_b200.Model(models[("gqa", "f32")], ctx=16, force=True)
-    lib, h, cb = m._lib, m._m, l3m_b200._CB(lambda t, u: 1)
+    lib, h, cb = m._lib, m._ptr, l3m_b200._CB(lambda t, u: 1)
     assert lib.l3m_generate(h, (C.c_int32 * 1)(m.vocab), 1, 2, 0.0, 0, cb, None) == -1
     assert lib.l3m_generate(h, (C.c_int32 * 16)(*[1] * 16), 16, 2, 0.0, 0, cb, None) == 0
     assert lib.l3m_generate(h, (C.c_int32 * 0)(), 0, 2, 0.0, 0, cb, None) == 0
