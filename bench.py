@@ -9,7 +9,8 @@ prompt ids, greedy until the context is full: 256 forward passes per step, which
 l3m_generate call. tok/s counts forward passes, prompt included, as the reference's `l3m bench`.
 
   value      forward passes / device time of the decode kernel (CUDA events around each launch,
-             inputs resident in HBM), summed over ranks / max over ranks
+             inputs resident in HBM), max over ranks. With --gpus N (torchrun) one model is split over
+             N GPUs and rank 0 drives them all: one batch-1 stream, so scaling is strong
   e2e        the same through the public API (l3m_generate: host prompt in, host tokens out via
              on_token), host wall clock around each call
   roofline   HBM: algorithmic bytes per launch (weights once per token + KV reads and writes) over
@@ -206,7 +207,12 @@ def bench_sweep(a):
 # DRAM traffic of one decode launch per forward pass, from an ncu capture of a short case of the same
 # kernel and model (dram__bytes_read.sum + dram__bytes_write.sum over the launch, divided by its
 # forward passes), scaled by the bench's forward passes per launch.
-DECODE_TRAFFIC = {}
+DECODE_TRAFFIC = {
+    "SmolLM2-135M-q8_0": {"dram_bytes_per_position": 138925084,
+                          "note": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one 64-position decode_kernel launch of this "
+                                  "model (8,853,367,552 + 37,837,824 B; the 4 prompt positions skip the head), divided by 64 and "
+                                  "scaled to this launch's positions"},
+}
 
 
 def matvec_line():
@@ -228,7 +234,7 @@ def matvec_line():
 
 def combine_ranks(dist, t_dev, t_wall, positions):
     """The whole job's (device time, wall time, positions): the times as the maximum over ranks, the
-    positions summed (replicas: every rank runs the same workload on its own GPU)."""
+    positions summed (a rank that drives no model reports zeros)."""
     if not dist:
         return t_dev, t_wall, positions
     import torch
@@ -253,17 +259,21 @@ def bench_ours(a):
     if world > 1:
         import torch.distributed as dist
         dist.init_process_group("gloo", timeout=__import__("datetime").timedelta(seconds=600))
-    m = l3m_b200.Model(path, cpus=[local], ctx=ctx, force=True)
-    flush = L2Flush()
-    sink = []
-    for _ in range(a.warmup):
-        m.generate(prompt, max_new, temperature=0, on_token=sink.append)
-    m.perf()
+    # One batch-1 stream on all `world` GPUs: rank 0 loads the model split over GPUs 0..world-1 and
+    # drives every GPU (one host thread per model, as the reference's one process per model); the
+    # other ranks only join the barriers and report no work.
+    dev_ns, wall_ns, positions, toks = [], [], 0, []
+    if rank == 0:
+        m = l3m_b200.Model(path, cpus=list(range(world)), ctx=ctx, force=True)
+        flush = L2Flush()
+        sink = []
+        for _ in range(a.warmup):
+            m.generate(prompt, max_new, temperature=0, on_token=sink.append)
+        m.perf()
     if dist:
         dist.barrier()
-    dev_ns, wall_ns, positions = [], [], 0
     with Clocks(local) as clk:
-        for _ in range(a.steps):
+        for _ in range(a.steps if rank == 0 else 0):
             flush()
             t0 = time.perf_counter_ns()
             toks = m.generate(prompt, max_new, temperature=0, on_token=sink.append)
@@ -288,13 +298,13 @@ def bench_ours(a):
     out = {
         "metric": "batch-1 decode tok/s", "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": a.steps,
         "warmup": a.warmup, "ms_per_step": round(t_dev / a.steps * 1e-6, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": round(value / PUBLISHED[name], 3) if name in PUBLISHED else None,
+        "scaling": "strong", "vs_baseline": round(value / PUBLISHED[name], 3) if name in PUBLISHED else None,
         "dtype": {"q8_0": "int8 dot / fp32", "q4_0": "int4 dot / fp32", "mxfp4": "e2m1 dot / fp32", "bf16": "bf16 x bf16 / fp32"}[dtype],
         "data": "synthetic (seeded N(0,0.02) weights, 4 seeded prompt ids)",
         "config": {"workload": f"{name} batch-1 greedy decode, ctx {ctx}, {per_launch_pos} forward passes per step "
                                f"({len(prompt)}-token prompt, {n_gen} generated)", "ctx": ctx, "l2_flush_between_steps": True,
-                   "parallelism": (f"{world} independent replicas: value and e2e are the aggregate of {world} batch-1 streams, "
-                                   "not one batch-1 stream on {world} GPUs") if world > 1 else "1 GPU",
+                   "parallelism": (f"one batch-1 stream, output channels split over {world} GPUs (activations exchanged "
+                                   "over NVLink 4 times per layer)") if world > 1 else "1 GPU",
                    "table": "sm100a (bit-exact with the reference's scalar path)"},
         "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * len(prompt), "d2h_bytes_per_step": 4 * n_gen,
                 "timing": "host wall clock around l3m_generate"},
@@ -306,9 +316,9 @@ def bench_ours(a):
         "gpu_launches": a.steps,
         "clocks": clk.summary(),
     }
-    if not a.no_matvec:
+    if not a.no_matvec and world == 1:
         out["matvec"] = matvec_line()
-    if not a.no_cpu:
+    if not a.no_cpu and world == 1:
         out["cpu_baseline"] = reference_cpu(path, ctx, max_new)
     print(json.dumps(out), flush=True)
 

@@ -246,6 +246,7 @@ __device__ __forceinline__ int stage_issue(const Smem &s, int dtype, const uint8
 }
 
 // The first failure of the launch: its code, and where it happened (the first CTA to record wins).
+// With several GPUs the code is also stored into every other GPU's abort word, so their waits stop too.
 __device__ __noinline__ void record_abort(const DecodeArgs &a, int code, int pos, int layer, int wait) {
     if (atomicCAS(a.hx.abort_flag, 0, code) == 0) {
         volatile int *w = a.hx.abort_flag;
@@ -253,6 +254,8 @@ __device__ __noinline__ void record_abort(const DecodeArgs &a, int code, int pos
         w[2] = pos;
         w[3] = layer;
         w[4] = wait;
+        for (int g = 0; g < a.sh.n_gpus; g++)
+            if (g != a.sh.gpu) asm volatile("st.relaxed.sys.global.s32 [%0], %1;" ::"l"(a.sh.abort[g]), "r"(code) : "memory");
     }
 }
 __device__ __forceinline__ bool aborted(const DecodeArgs &a) { return *(volatile int *)a.hx.abort_flag != 0; }
@@ -300,6 +303,69 @@ __device__ __noinline__ void xwait(const DecodeArgs &a, const Smem &s, int k, ui
     if (threadIdx.x == 0 && done) asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
 
+// ---- Exchanges between GPUs (a model split over n_gpus > 1). Every layer step (position pos, layer
+// l) has its own epoch; each element travels as one 8-byte word {value bits, epoch}, written with a
+// single store, so a reader that sees the epoch it waits for has the value of that step, with no flag
+// and no fence between them. Receive buffers alternate halves by step parity: a GPU writes step s + 2
+// into a half only after every GPU has produced its part of step s + 1, which each produced after
+// reading step s.
+__device__ __forceinline__ uint32_t layer_step(const DecodeArgs &a, int pos, int l) { return (uint32_t)pos * (uint32_t)a.n_layers + (uint32_t)l; }
+__device__ __forceinline__ int xlen(const DecodeArgs &a, int k) { return k == kXH ? a.ffn : a.dim; }
+// The bytes of exchange k (-1: qkv) that this GPU's own CTAs deliver to each of its CTAs.
+__device__ __forceinline__ uint32_t xbytes(const DecodeArgs &a, int k) {
+    return 4u * (uint32_t)(k < 0 ? a.sh.n_qkv_g : a.sh.len[k][a.sh.gpu]);
+}
+
+// This CTA's part src[0, n) of exchanged vector k (elements [g0, g0 + n)) into every other GPU's
+// receive buffer.
+__device__ __noinline__ void peer_send(const DecodeArgs &a, int k, const float *src, int g0, int n, uint32_t step) {
+    const int G = a.sh.n_gpus, me = a.sh.gpu;
+    const uint64_t e = (uint64_t)(a.sh.epoch0 + step) << 32;
+    const size_t half = (size_t)(step & 1u) * (size_t)xlen(a, k);
+    for (int j = threadIdx.x; j < n * (G - 1); j += blockDim.x) {
+        const int p = j / n, i = j - p * n, g = p < me ? p : p + 1;
+        unsigned long long *dst = a.sh.rx[g][k] + half + g0 + i;
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst), "l"(e | __float_as_uint(src[i])) : "memory");
+    }
+}
+
+// The other GPUs' slices of exchanged vector k into dst (shared memory), from this GPU's receive
+// buffer: every thread polls its elements until their epoch is this step's (time-limited; stops
+// early once a failure is recorded), then a barrier.
+__device__ __noinline__ void peer_recv(const DecodeArgs &a, int k, float *dst, uint32_t step, int pos, int l) {
+    const int G = a.sh.n_gpus, me = a.sh.gpu;
+    const uint32_t e = a.sh.epoch0 + step;
+    const unsigned long long *buf = a.sh.rx[me][k] + (size_t)(step & 1u) * (size_t)xlen(a, k);
+    bool gave_up = false;
+    uint64_t t0 = 0;
+    int spins = 0;
+    for (int g = 0; g < G && !gave_up; g++) {
+        if (g == me) continue;
+        const int lo = a.sh.lo[k][g], hi = lo + a.sh.len[k][g];
+        for (int i = lo + threadIdx.x; i < hi && !gave_up; i += blockDim.x) {
+            for (;;) {
+                uint64_t w;
+                asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(buf + i) : "memory");
+                if ((uint32_t)(w >> 32) == e) {
+                    dst[i] = __uint_as_float((uint32_t)w);
+                    break;
+                }
+                if (spins++ == 0) {
+                    t0 = globaltimer_ns();
+                } else if ((spins & 63) == 0) {
+                    if (aborted(a)) { gave_up = true; break; }
+                    if (globaltimer_ns() - t0 > a.hx.timeout_ns) {
+                        record_abort(a, kErrTimeout, pos, l, kWaitPeerAttn + k);
+                        gave_up = true;
+                        break;
+                    }
+                }
+            }
+        }
+    }
+    __syncthreads();
+}
+
 // x = embedding row of tok, plus the learned position row when the file has one (reference
 // src/engine.c:236-237, src/pack.c:55-62).
 template <bool GPT2>
@@ -334,11 +400,12 @@ __device__ __noinline__ void embed_row(const DecodeArgs &a, int tok, int pos, fl
 
 // Phase Q: this CTA's tiles of the q/k/v rows (biases added) -> s.y (the caller scatters into xq).
 // ns tiles staged at the staging area's offset w_extra (phase parity par).
+// The KV cache of (global) query head h: this GPU holds kv heads [kv_lo, kv_lo + n_kv_g).
 __device__ __forceinline__ const uint16_t *kcache(const DecodeArgs &a, const LayerDev &L, int h) {
-    return L.kc + (size_t)(h / a.hpk) * a.ctx * a.hd;
+    return L.kc + (size_t)(h / a.hpk - a.sh.kv_lo) * a.ctx * a.hd;
 }
 __device__ __forceinline__ const uint16_t *vcache(const DecodeArgs &a, const LayerDev &L, int h) {
-    return L.vc + (size_t)(h / a.hpk) * a.hd * a.vstride;
+    return L.vc + (size_t)(h / a.hpk - a.sh.kv_lo) * a.hd * a.vstride;
 }
 
 // A head CTA's warps 1.. start the K/V copies of its attention (attend_prestage) while warp 0 runs
@@ -363,26 +430,29 @@ __device__ __noinline__ void phase_qkv(const DecodeArgs &a, const LayerDev &L, c
     trace(a, tslot, pos, l, 18);
     matvec_exact(L.dt_qkv, L.qkv, a.dim, role.qkv0, role.qkv1, s.prep, s.scratch, a.scratch_pairs, s.y, s.w + a.w_extra, ns);
     trace(a, tslot, pos, l, 19);
-    const int g0 = role.qkv0 * kTile, n = min(role.qkv1 * kTile, a.n_qkv) - g0, nq = a.n_heads * a.hd, nk = a.n_kv * a.hd;
+    // This GPU's qkv rows: q of its heads, then k and v of its kv heads (biases of the same rows).
+    const int g0 = role.qkv0 * kTile, n = min(role.qkv1 * kTile, a.sh.n_qkv_g) - g0, nq = a.sh.n_heads_g * a.hd, nk = a.sh.n_kv_g * a.hd;
     if (L.bq) {
+        const int q0 = a.sh.head_lo * a.hd, k0 = a.sh.kv_lo * a.hd;
         for (int o = threadIdx.x; o < n; o += blockDim.x) {
             const int r = g0 + o;
-            s.y[o] = __fadd_rn(s.y[o], __ldg(r < nq ? L.bq + r : r < nq + nk ? L.bk + (r - nq) : L.bv + (r - nq - nk)));
+            s.y[o] = __fadd_rn(s.y[o], __ldg(r < nq ? L.bq + q0 + r : r < nq + nk ? L.bk + k0 + (r - nq) : L.bv + k0 + (r - nq - nk)));
         }
         __syncthreads();
     }
 }
 
 // Phase A for query head h at position pos (xq complete): RoPE, this position's K/V row (stored by
-// the first head of each kv group), attention -> every CTA's xa[h*hd, (h+1)*hd).
+// the first head of each kv group this GPU holds), attention -> every CTA's xa[h*hd, (h+1)*hd).
 __device__ __noinline__ void phase_attention(const DecodeArgs &a, const LayerDev &L, const Smem &s, int h, int pos, bool prestaged, int l,
                                              int tslot) {
-    const int tid = threadIdx.x, nth = blockDim.x, hd = a.hd, kvh = h / a.hpk, nq = a.n_heads * hd, nk = a.n_kv * hd;
+    const int tid = threadIdx.x, nth = blockDim.x, hd = a.hd, hl = h - a.sh.head_lo, kvl = h / a.hpk - a.sh.kv_lo;
+    const int nq = a.sh.n_heads_g * hd, nk = a.sh.n_kv_g * hd;
     float *y = s.y;                                                  // q, k, v of this head
     for (int i = tid; i < hd; i += nth) {
-        y[i] = s.xq[h * hd + i];
-        y[hd + i] = s.xq[nq + kvh * hd + i];
-        y[2 * hd + i] = s.xq[nq + nk + kvh * hd + i];
+        y[i] = s.xq[hl * hd + i];
+        y[hd + i] = s.xq[nq + kvl * hd + i];
+        y[2 * hd + i] = s.xq[nq + nk + kvl * hd + i];
     }
     __syncthreads();
     if (a.rope) {
@@ -390,7 +460,7 @@ __device__ __noinline__ void phase_attention(const DecodeArgs &a, const LayerDev
         rope_exact(y + hd, hd, s.rope);
     }
     uint16_t *kc = (uint16_t *)kcache(a, L, h), *vc = (uint16_t *)vcache(a, L, h);
-    const bool writer = h % a.hpk == 0;
+    const bool writer = h % a.hpk == 0 || h == a.sh.head_lo;
     for (int i = tid; i < hd; i += nth) {
         const uint16_t kb = l3m_f32_to_bf16(y[hd + i]), vb = l3m_f32_to_bf16(y[2 * hd + i]);
         s.kcur[i] = kb;
@@ -419,7 +489,7 @@ __device__ __noinline__ void phase_wo(const DecodeArgs &a, const LayerDev &L, co
     trace(a, tslot, pos, l, 21);
     matvec_exact(L.dt_wo, L.wo, a.dim, role.wo0, role.wo1, s.prep, s.scratch, a.scratch_pairs, s.y, s.w + a.w_extra, ns);
     trace(a, tslot, pos, l, 22);
-    const int g0 = role.wo0 * kTile, n = min(role.wo1 * kTile, a.dim) - g0;
+    const int g0 = (a.sh.d_off + role.wo0) * kTile, n = min((a.sh.d_off + role.wo1) * kTile, a.dim) - g0;
     if (L.bo) {
         for (int o = threadIdx.x; o < n; o += blockDim.x) s.y[o] = __fadd_rn(s.y[o], __ldg(L.bo + g0 + o));
         __syncthreads();
@@ -458,7 +528,7 @@ __device__ __noinline__ void phase_ffn(const DecodeArgs &a, const LayerDev &L, c
 // GELU of up.
 template <bool GPT2>
 __device__ __noinline__ void ffn_gate(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s) {
-    const int nf = role.ffn1 - role.ffn0, g0 = role.ffn0 * kTile, n = min(role.ffn1 * kTile, a.ffn) - g0;
+    const int nf = role.ffn1 - role.ffn0, g0 = (a.sh.f_off + role.ffn0) * kTile, n = min((a.sh.f_off + role.ffn1) * kTile, a.ffn) - g0;
     for (int o = threadIdx.x; o < n; o += blockDim.x) {
         const float up = L.b_up ? __fadd_rn(s.y[o], __ldg(L.b_up + g0 + o)) : s.y[o];
         s.tmp[o] = GPT2 && a.gelu ? gelu_tanh(up) : silu_mul(up, s.y[nf * kTile + o], a.elist, a.eindex);
@@ -476,7 +546,7 @@ __device__ __noinline__ void phase_down(const DecodeArgs &a, const LayerDev &L, 
     trace(a, tslot, pos, l, 24);
     matvec_exact(L.dt_down, L.down, a.ffn, role.dn0, role.dn1, s.prep, s.scratch, a.scratch_pairs, s.y, s.w, ns);
     trace(a, tslot, pos, l, 25);
-    const int g0 = role.dn0 * kTile, n = min(role.dn1 * kTile, a.dim) - g0;
+    const int g0 = (a.sh.d_off + role.dn0) * kTile, n = min((a.sh.d_off + role.dn1) * kTile, a.dim) - g0;
     if (L.b_down) {
         for (int o = threadIdx.x; o < n; o += blockDim.x) s.y[o] = __fadd_rn(s.y[o], __ldg(L.b_down + g0 + o));
         __syncthreads();
@@ -691,11 +761,19 @@ __device__ __noinline__ void head_logits(const DecodeArgs &a, const Role &role, 
         matvec_exact(a.dt_head, a.head, a.dim, role.voc0, role.voc1, s.prep, s.scratch, a.scratch_pairs, s.y);
         trace(a, tslot, pos, a.n_layers, 5);
         float *lg = a.logits + (size_t)pos * a.vocab;
-        const int g0 = role.voc0 * kTile, n = min(role.voc1 * kTile, a.vocab) - g0;
+        const int g0 = (a.sh.v_off + role.voc0) * kTile, n = min((a.sh.v_off + role.voc1) * kTile, a.vocab) - g0;
         for (int o = tid; o < n; o += nth) {
             const float v = s.y[o];
             lg[g0 + o] = v;
             if (v > best) { best = v; best_i = g0 + o; }                      // this thread's outputs rise with o
+        }
+        if (a.sh.n_gpus > 1) {                                            // GPU 0 keeps every logit (l3m_logits); with
+            for (int t = 0; t < a.sh.n_gpus; t++) {                       // temperature sampling every GPU does
+                if (t == a.sh.gpu || (t != 0 && !a.sh.all_logits)) continue;
+                float *pl = a.sh.logits[t] + (size_t)pos * a.vocab + g0;
+                for (int o = tid; o < n; o += nth) pl[o] = s.y[o];
+            }
+            __threadfence_system();                                       // before the arrival that the vote follows
         }
     }
     // CTA argmax: the largest value, the lowest index among equals (reference engine.c:293-294).
@@ -714,7 +792,7 @@ __device__ __noinline__ void head_logits(const DecodeArgs &a, const Role &role, 
             const int vi = ((int *)s.red)[32 + w];
             if (v > m || (v == m && vi >= 0 && (mi < 0 || vi < mi))) { m = v; mi = vi; }
         }
-        if (mi < 0) mi = role.voc0 * kTile;                                   // an empty or all-NaN slice
+        if (mi < 0) mi = (a.sh.v_off + role.voc0) * kTile;                   // an empty or all-NaN slice
         s.tmp[0] = m;                                                         // also kept here for a one-cluster launch
         s.tmp[1] = __int_as_float(mi);
         s.tmp[2] = __int_as_float(host_stop);
@@ -724,6 +802,59 @@ __device__ __noinline__ void head_logits(const DecodeArgs &a, const Role &role, 
         asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.hx.count) : "memory");
     }
     __syncthreads();
+}
+
+// Several GPUs: CTA 0 of each has its GPU's agreed (max, index, host stop, ok) in xt[0..3]. Its thread 0
+// stores them into every GPU's vote buffer (two words, each with the sampled position's epoch, after
+// a release that orders this GPU's logits stores before them), waits for every GPU's (acquire,
+// time-limited), and reduces them in GPU order, the largest maximum and the first GPU among equals
+// (the vocabulary order, reference src/engine.c:299-300); the host stop is GPU 0's, ok is all of
+// them. The result goes to every CTA of cluster 0's xt[0..3] (the caller's cluster barrier follows).
+__device__ __noinline__ void gpu_vote(const DecodeArgs &a, const Smem &s, uint32_t tcount, int pos) {
+    if (threadIdx.x == 0) {
+        const int G = a.sh.n_gpus, me = a.sh.gpu;
+        const uint32_t e = a.sh.epoch0 + 0x40000000u + tcount;             // apart from the layer steps' epochs
+        const size_t half = (size_t)(tcount & 1u) * kMaxShardGpus * 2;
+        const uint32_t flags = (uint32_t)__float_as_int(s.xt[0]) & 0xFFFFFFu;
+        const uint32_t word1 = flags | (__float_as_int(s.xt[1]) ? 1u << 24 : 0u) | (__float_as_int(s.xt[2]) ? 1u << 25 : 0u);
+        const uint64_t w0 = (uint64_t)e << 32 | __float_as_uint(s.xt[3]), w1 = (uint64_t)e << 32 | word1;
+        for (int g = 0; g < G; g++) {
+            unsigned long long *v = a.sh.vote[g] + half + 2 * me;
+            asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(v + 1), "l"(w1) : "memory");
+            asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(v), "l"(w0) : "memory");
+        }
+        float gmax = -INFINITY;
+        int next = 0, stop = 0, ok = 1;
+        const uint64_t t0 = globaltimer_ns();
+        for (int g = 0; g < G; g++) {
+            const unsigned long long *v = a.sh.vote[me] + half + 2 * g;
+            uint64_t r0 = 0, r1 = 0;
+            for (int spins = 0;; spins++) {
+                asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(r0) : "l"(v) : "memory");
+                if ((uint32_t)(r0 >> 32) == e) {
+                    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(r1) : "l"(v + 1) : "memory");
+                    if ((uint32_t)(r1 >> 32) == e) break;
+                }
+                if ((spins & 63) == 63 && (aborted(a) || globaltimer_ns() - t0 > a.hx.timeout_ns)) {
+                    if (!aborted(a)) record_abort(a, kErrTimeout, pos, -1, kWaitPeerToken);
+                    r0 = (uint64_t)e << 32 | __float_as_uint(-INFINITY);
+                    r1 = 0;                                               // not ok
+                    break;
+                }
+            }
+            const float m = __uint_as_float((uint32_t)r0);
+            const uint32_t f = (uint32_t)r1;
+            if (m > gmax) { gmax = m; next = (int)(f & 0xFFFFFFu); }
+            if (g == 0) stop = (f >> 24) & 1;
+            ok &= (f >> 25) & 1;
+        }
+        s.tmp[0] = __int_as_float(next);
+        s.tmp[1] = __int_as_float(stop);
+        s.tmp[2] = __int_as_float(ok);
+        s.tmp[3] = gmax;
+    }
+    __syncthreads();
+    scatter(s.tmp, s.xt, 0, 4);
 }
 
 // A CTA outside cluster 0: between sampled positions it sleeps on hx.flag; for each published x it
@@ -805,6 +936,7 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
     const Smem &s = sh_s;
     const Role &role = sh_role;
     const int cta = blockIdx.x, tid = threadIdx.x;
+    const bool multi = a.sh.n_gpus > 1;
     const int tslot = a.trace_cta[0] == cta ? 0 : a.trace_cta[1] == cta ? 1 : -1;
     int n_gen = 0, tok = 0, pos = 0;
     uint32_t tcount = 0;
@@ -824,7 +956,7 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
     stage_init(s);
     uint32_t xpar = 0;                                                    // the exchanges' phase parity (one phase per layer)
     if (a.async_x && tid == 0) {
-        const uint32_t bytes[5] = {(uint32_t)a.n_qkv * 4, (uint32_t)a.dim * 4, (uint32_t)a.dim * 4, (uint32_t)a.ffn * 4, (uint32_t)a.dim * 4};
+        const uint32_t bytes[5] = {xbytes(a, -1), xbytes(a, kXAttn), xbytes(a, kXProj), xbytes(a, kXH), xbytes(a, kXDown)};
         for (int k = 0; k < 5; k++) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(s.xbar + k)) : "memory");
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         for (int k = 0; k < 5; k++)
@@ -863,19 +995,23 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
             ns = stage_issue(s, L.dt_wo, L.wo, a.dim, role.wo0, role.wo1, s.w + a.w_extra, a.w_bytes - a.w_extra, COLD);
             trace(a, tslot, pos, l, 27);
             if (role.qkv0 < role.qkv1) {
-                const int g0 = role.qkv0 * kTile, n = min(role.qkv1 * kTile, a.n_qkv) - g0;
+                const int g0 = role.qkv0 * kTile, n = min(role.qkv1 * kTile, a.sh.n_qkv_g) - g0;
                 if (a.async_x) scatter_tx(s.y, s.xq, g0, n, s.xbar);
                 else scatter(s.y, s.xq, g0, n);
             }
             trace(a, tslot, pos, l, 1);
-            if (a.async_x) xwait(a, s, 0, xpar, (uint32_t)a.n_qkv * 4, pos, l);   // 1: qkv
+            if (a.async_x) xwait(a, s, 0, xpar, xbytes(a, -1), pos, l);   // 1: qkv (this GPU's heads)
             else cluster_sync();
             trace(a, tslot, pos, l, 2);
-            for (int h = role.head0; h >= 0 && h < a.n_heads; h += kClusterCtas)   // A
+            const uint32_t step = layer_step(a, pos, l);
+            for (int h = role.head0; h >= 0 && h < a.sh.head_lo + a.sh.n_heads_g; h += kClusterCtas) {   // A
                 phase_attention(a, L, s, h, pos, h == role.head0, l, tslot);
+                if (multi) peer_send(a, kXAttn, s.att, h * a.hd, a.hd, step);
+            }
             trace(a, tslot, pos, l, 3);
-            if (a.async_x) xwait(a, s, 1, xpar, (uint32_t)a.dim * 4, pos, l);     // 2: attn
+            if (a.async_x) xwait(a, s, 1, xpar, xbytes(a, kXAttn), pos, l);     // 2: attn
             else cluster_sync();
+            if (multi) peer_recv(a, kXAttn, s.xa, step, pos, l);
             trace(a, tslot, pos, l, 4);
             if (role.wo0 < role.wo1) phase_wo(a, L, role, s, ns, wpar, pos, l, tslot);   // B
             if (ns) wpar ^= 1;
@@ -883,13 +1019,15 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
             else ns = stage_issue(s, L.dt_up, L.up, a.dim, role.ffn0, role.ffn1, s.w, a.w_bytes, COLD);
             trace(a, tslot, pos, l, 28);
             if (role.wo0 < role.wo1) {
-                const int g0 = role.wo0 * kTile, n = min(role.wo1 * kTile, a.dim) - g0;
+                const int g0 = (a.sh.d_off + role.wo0) * kTile, n = min((a.sh.d_off + role.wo1) * kTile, a.dim) - g0;
                 if (a.async_x) scatter_tx(s.y, s.xp, g0, n, s.xbar + 2);
                 else scatter(s.y, s.xp, g0, n);
+                if (multi) peer_send(a, kXProj, s.y, g0, n, step);
             }
             trace(a, tslot, pos, l, 5);
-            if (a.async_x) xwait(a, s, 2, xpar, (uint32_t)a.dim * 4, pos, l);     // 3: proj
+            if (a.async_x) xwait(a, s, 2, xpar, xbytes(a, kXProj), pos, l);     // 3: proj
             else cluster_sync();
+            if (multi) peer_recv(a, kXProj, s.xp, step, pos, l);
             trace(a, tslot, pos, l, 6);
             phase_ffn<GPT2>(a, L, role, s, pos, l, tslot, ns, wpar);      // C
             if (ns) wpar ^= 1;
@@ -897,16 +1035,18 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
             trace(a, tslot, pos, l, 29);
             if (role.ffn0 < role.ffn1) {
                 ffn_gate<GPT2>(a, L, role, s);
-                const int g0 = role.ffn0 * kTile, n = min(role.ffn1 * kTile, a.ffn) - g0;
+                const int g0 = (a.sh.f_off + role.ffn0) * kTile, n = min((a.sh.f_off + role.ffn1) * kTile, a.ffn) - g0;
                 if (a.async_x) scatter_tx(s.tmp, s.xh, g0, n, s.xbar + 3);
                 else scatter(s.tmp, s.xh, g0, n);
+                if (multi) peer_send(a, kXH, s.tmp, g0, n, step);
             }
             // The next layer's norm weights (and the next position's RoPE row) while the rest runs.
             if (l + 1 < a.n_layers) stage_vectors<GPT2>(a, layers[l + 1], role, s, pos);
             else stage_vectors<GPT2>(a, layers[0], role, s, pos + 1);
             trace(a, tslot, pos, l, 8);
-            if (a.async_x) xwait(a, s, 3, xpar, (uint32_t)a.ffn * 4, pos, l);     // 4: h
+            if (a.async_x) xwait(a, s, 3, xpar, xbytes(a, kXH), pos, l);     // 4: h
             else cluster_sync();
+            if (multi) peer_recv(a, kXH, s.xh, step, pos, l);
             trace(a, tslot, pos, l, 9);
             if (role.dn0 < role.dn1) phase_down(a, L, role, s, ns, wpar, pos, l, tslot);   // D
             if (ns) wpar ^= 1;
@@ -916,17 +1056,19 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
             }
             trace(a, tslot, pos, l, 30);
             if (role.dn0 < role.dn1) {
-                const int g0 = role.dn0 * kTile, n = min(role.dn1 * kTile, a.dim) - g0;
+                const int g0 = (a.sh.d_off + role.dn0) * kTile, n = min((a.sh.d_off + role.dn1) * kTile, a.dim) - g0;
                 if (a.async_x) scatter_tx(s.y, s.xd, g0, n, s.xbar + 4);
                 else scatter(s.y, s.xd, g0, n);
+                if (multi) peer_send(a, kXDown, s.y, g0, n, step);
             }
             trace(a, tslot, pos, l, 10);
             if (a.async_x) {                                              // 5: down
-                xwait(a, s, 4, xpar, (uint32_t)a.dim * 4, pos, l);
+                xwait(a, s, 4, xpar, xbytes(a, kXDown), pos, l);
                 xpar ^= 1u;
             } else {
                 cluster_sync();
             }
+            if (multi) peer_recv(a, kXDown, s.xd, step, pos, l);
             for (int i = tid; i < a.dim; i += blockDim.x) s.x[i] = __fadd_rn(s.x[i], s.xd[i]);
             __syncthreads();
             trace(a, tslot, pos, l, 11);
@@ -986,6 +1128,11 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
             if (tid == 0) { s.xt[0] = __int_as_float(nx); s.xt[1] = s.xt[4 + 2]; s.xt[2] = __int_as_float(all); s.xt[3] = gmax; }
             __syncthreads();
         }
+        if (multi) {                                                      // every GPU's (max, index): one agreed token
+            cluster_sync();                                               // every CTA has its GPU's result in xt[0..3]
+            if (cta == 0) gpu_vote(a, s, tcount, pos);
+            cluster_sync();
+        }
         int next = __float_as_int(s.xt[0]);
         const int stop_req = __float_as_int(s.xt[1]);
         const float gmax_all = s.xt[3];
@@ -1004,7 +1151,7 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
         tok = next;
         if (tok == a.eos || tok == a.bos) break;                          // reference engine.c:323-324
         n_gen++;
-        if (cta == 0 && tid == 0) {
+        if (cta == 0 && tid == 0 && a.sh.gpu == 0) {                      // GPU 0 streams the tokens
             a.tokens[n_gen - 1] = tok;
             __threadfence_system();
             a.ctrl->n_published = n_gen;

@@ -35,6 +35,7 @@ struct Ctrl {
 };
 
 constexpr int kDecodeThreads = 256;   // 8 warps per CTA
+constexpr int kMaxShardGpus = 8;      // GPUs one model can be split over
 constexpr int kClusterCtas = 16;      // one thread-block cluster runs the whole model
 constexpr int kTraceEvents = 32;      // stamps per (position, layer); see the trace() calls in decode.cu
 
@@ -56,11 +57,40 @@ constexpr uint32_t kHeadDone = 0xFFFFFFFFu;
 enum { kErrNone = 0, kErrTimeout = 1, kErrStageTimeout = 2, kErrShape = 3, kErrToken = 4 };
 // Which wait gave up (Ctrl::where[3]): exchanges 1-5 of a layer, the weight copy, the head job flag
 // (helper clusters), the head arrival count (CTA 0).
-enum { kWaitQkv = 1, kWaitAttn = 2, kWaitProj = 3, kWaitH = 4, kWaitDown = 5, kWaitStage = 8, kWaitHeadFlag = 9, kWaitHeadCount = 10 };
+enum { kWaitQkv = 1, kWaitAttn = 2, kWaitProj = 3, kWaitH = 4, kWaitDown = 5, kWaitStage = 8, kWaitHeadFlag = 9, kWaitHeadCount = 10,
+       kWaitPeerAttn = 12, kWaitPeerProj = 13, kWaitPeerH = 14, kWaitPeerDown = 15, kWaitPeerToken = 16 };
+
+// The vectors GPUs exchange each layer when a model is split over several (the reference's four
+// all-gathers per layer, src/engine.c:254-274): attention output, wo output, gate output, down output.
+enum { kXAttn = 0, kXProj = 1, kXH = 2, kXDown = 3, kXKinds = 4 };
+
+// This GPU's share of an output-channel split over n_gpus GPUs (the reference's split over ranks,
+// src/engine.c:467-476, at tile granularity, then over the CTAs of the GPU): query heads
+// [head_lo, head_lo + n_heads_g) and kv heads [kv_lo, kv_lo + n_kv_g) (a kv head whose query heads
+// straddle two GPUs is held by both, as src/engine.c:135-152), and the tile runs of wo and down
+// (d_off..), up and gate (f_off..) and the head (v_off..). One GPU: the whole of everything.
+struct Shard {
+    int n_gpus, gpu;
+    int head_lo, n_heads_g, kv_lo, n_kv_g, n_qkv_g;   // n_qkv_g = (n_heads_g + 2 n_kv_g) hd: this GPU's qkv rows
+    int d_off, f_off, v_off;                           // first dim / ffn / vocab tile held
+    int lo[kXKinds][kMaxShardGpus], len[kXKinds][kMaxShardGpus];   // every GPU's slice of each exchanged vector
+    // n_gpus > 1: every GPU's receive buffers (peer-accessible device memory). rx[g][k]: 2 x the vector's
+    // length of 8-byte words {value bits, epoch}, one half per layer parity; written by the GPUs that
+    // produce the slices, polled by GPU g's CTAs. vote[g]: kMaxShardGpus words per sampled-position
+    // parity {max bits, index | flags << 24} with the epoch in the second word. logits[g]: GPU g's logits
+    // history. abort[g]: GPU g's abort word.
+    unsigned long long *rx[kMaxShardGpus][kXKinds];
+    unsigned long long *vote[kMaxShardGpus];
+    float *logits[kMaxShardGpus];
+    int *abort[kMaxShardGpus];
+    uint32_t epoch0;                                   // the first epoch of this launch
+    int all_logits;                                    // every GPU gets every logit (temperature sampling)
+};
 
 struct DecodeArgs {
     int dim, hd, ffn, vocab, ctx, n_heads, n_kv, hpk, n_layers, n_qkv, grid;   // n_qkv = (n_heads + 2 n_kv) hd; grid: all CTAs
     HeadX hx;
+    Shard sh;
     float eps;
     const LayerDev *layers;
     const uint8_t *head;

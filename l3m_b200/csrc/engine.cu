@@ -45,7 +45,7 @@ double now_ns() {
 int tiles_of(int n) { return (n + L3M_TILE - 1) / L3M_TILE; }
 
 struct Gpu {
-    int dev = -1, sms = 0;
+    int dev = -1, sms = 0, rank = 0;
     cudaStream_t stream = nullptr, side = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     uint8_t *arena = nullptr;
@@ -63,6 +63,8 @@ struct Gpu {
     int32_t *prompt = nullptr;
     float *logits = nullptr;
     float *probs = nullptr;                                            // [vocab] sampling weights
+    unsigned long long *rx = nullptr, *vote = nullptr;                 // receive buffers and votes from other GPUs
+    size_t rx_bytes = 0, vote_bytes = 0;
     l3m::DecodeArgs args{};
     size_t l2_bytes = 0, persist_max = 0, window_max = 0, prev_limit = 0;
     bool limit_set = false;
@@ -78,9 +80,10 @@ struct l3m_model {
     int dim = 0, hd = 0, ffn = 0, vocab = 0, ctx = 0, n_heads = 0, n_kv = 0, hpk = 0, n_layers = 0;
     unsigned flags = 0;
     int reference = 0, cold = 0;
-    l3m::Ctrl *ctrl = nullptr;
+    l3m::Ctrl *ctrl = nullptr;                                         // one per GPU, host-mapped; GPU 0 streams the tokens
     int32_t *tokens = nullptr;
     l3m::Ctrl *ctrl_dev = nullptr;
+    uint32_t epoch_next = 1;                                           // the next launch's first exchange epoch
     int32_t *tokens_dev = nullptr;
     std::vector<float> host_logits;
     int logits_pos = -1, cached_pos = -2;
@@ -200,29 +203,63 @@ size_t pack_rows(Stage &s, Rows &r, const l3m_file *f, const std::string &name, 
     return off;
 }
 
-void pack_streamed(const l3m_file *f, bool ref, int n_heads, int n_kv, int hd, Stage &s, Streamed &out) {
-    const int L = (int)f->h->n_layers, ffn = (int)f->h->ffn_dim;
+// The rows one GPU holds of an output-channel split over n GPUs (the reference's split over ranks,
+// src/engine.c:467-476, with the kv heads of src/engine.c:135-152; vocabulary tiles split evenly, as
+// the reference's greedy deal comes out with equal budgets): query heads [head_lo, head_hi), kv heads
+// [kv_lo, kv_hi), and tile runs of the dim (wo, down), ffn (up, gate) and vocabulary (head) rows.
+struct ShardRange {
+    int head_lo, head_hi, kv_lo, kv_hi, d_lo, d_hi, f_lo, f_hi, v_lo, v_hi;
+    bool whole;                                                   // one GPU: the packed section of the file applies
+};
+
+ShardRange shard_range(const l3m_header *h, int n, int r) {
+    ShardRange s;
+    const int hpk = (int)(h->n_heads / h->n_kv_heads);
+    split((int)h->n_heads, n, r, &s.head_lo, &s.head_hi);
+    s.kv_lo = s.head_lo / hpk;
+    s.kv_hi = s.head_hi > s.head_lo ? (s.head_hi - 1) / hpk + 1 : s.kv_lo;
+    split(tiles_of((int)h->dim), n, r, &s.d_lo, &s.d_hi);
+    split(tiles_of((int)h->ffn_dim), n, r, &s.f_lo, &s.f_hi);
+    split(tiles_of((int)h->vocab), n, r, &s.v_lo, &s.v_hi);
+    s.whole = n == 1;
+    return s;
+}
+
+// Rows [lo, hi) of t that exist (rows past the matrix pack as zeros).
+void add_rows(Rows &r, const l3m_file *f, const l3m_tensor *t, int lo, int hi, bool ref) {
+    for (int i = lo; i < hi; i++) {
+        if (i < (int)t->shape[0]) r.add(f, t, i, ref);
+        else r.ptr.push_back(nullptr);
+    }
+}
+
+void pack_streamed(const l3m_file *f, bool ref, const ShardRange &sr, int hd, Stage &s, Streamed &out) {
+    const int L = (int)f->h->n_layers;
+    const bool packed_ok = sr.whole && !ref;                                        // the file's b200v1 section is for one GPU
     for (auto *v : {&out.off_qkv, &out.off_wo, &out.off_up, &out.off_gate, &out.off_down}) v->assign(L, 0);
     for (auto *v : {&out.dt_qkv, &out.dt_wo, &out.dt_up, &out.dt_gate, &out.dt_down}) v->assign(L, 0);
+    const int T = L3M_TILE, ftiles = sr.f_hi - sr.f_lo;
     for (int l = 0; l < L; l++) {
         const std::string b = "blk." + std::to_string(l) + ".";
         const l3m_tensor *wq = l3m_file_blk(f, l, "wq"), *wk = l3m_file_blk(f, l, "wk"), *wv = l3m_file_blk(f, l, "wv");
-        Rows r;                                                                     // q of every head, then k, then v
-        for (int i = 0; i < n_heads * hd; i++) r.add(f, wq, i, ref);
-        for (int i = 0; i < n_kv * hd; i++) r.add(f, wk, i, ref);
-        for (int i = 0; i < n_kv * hd; i++) r.add(f, wv, i, ref);
-        out.off_qkv[l] = pack_rows(s, r, f, b + "qkv", out, ref, &out.dt_qkv[l]);
+        Rows r;                                                                     // q of the heads, then k, then v
+        add_rows(r, f, wq, sr.head_lo * hd, sr.head_hi * hd, ref);
+        add_rows(r, f, wk, sr.kv_lo * hd, sr.kv_hi * hd, ref);
+        add_rows(r, f, wv, sr.kv_lo * hd, sr.kv_hi * hd, ref);
+        if (r.ptr.empty()) r.k = (int)wq->shape[1], r.dtype = ref ? L3M_F32 : (int)wq->dtype;
+        out.off_qkv[l] = pack_rows(s, r, f, b + "qkv", out, !packed_ok, &out.dt_qkv[l]);
         {
             Rows ro;
             const l3m_tensor *wo = l3m_file_blk(f, l, "wo");
-            for (int i = 0; i < (int)wo->shape[0]; i++) ro.add(f, wo, i, ref);
-            out.off_wo[l] = pack_rows(s, ro, f, b + "wo", out, ref, &out.dt_wo[l]);
+            add_rows(ro, f, wo, sr.d_lo * T, std::min(sr.d_hi * T, (int)wo->shape[0]), ref);
+            out.off_wo[l] = pack_rows(s, ro, f, b + "wo", out, !packed_ok, &out.dt_wo[l]);
         }
         const l3m_tensor *wu = l3m_file_blk(f, l, "w_up"), *wg = l3m_file_blk(f, l, "w_gate");
+        const int ffn_hi = std::min(sr.f_hi * T, (int)wu->shape[0]);
         if (!wg) {                                                                  // GELU MLP: up only
             Rows ru;
-            for (int i = 0; i < ffn; i++) ru.add(f, wu, i, ref);
-            out.off_up[l] = pack_rows(s, ru, f, b + "up", out, ref, &out.dt_up[l]);
+            add_rows(ru, f, wu, sr.f_lo * T, ffn_hi, ref);
+            out.off_up[l] = pack_rows(s, ru, f, b + "up", out, !packed_ok, &out.dt_up[l]);
             out.off_gate[l] = (size_t)-1;
             out.dt_gate[l] = out.dt_up[l];
         } else if (ref || wu->dtype == wg->dtype) {
@@ -230,33 +267,28 @@ void pack_streamed(const l3m_file *f, bool ref, int n_heads, int n_kv, int hd, S
             Rows ru;
             for (int c = 0; c < l3m::kClusterCtas; c++) {
                 int t0, t1;
-                split(tiles_of(ffn), l3m::kClusterCtas, c, &t0, &t1);
-                for (const l3m_tensor *t : {wu, wg}) {
-                    for (int i = t0 * L3M_TILE; i < t1 * L3M_TILE; i++) {
-                        if (i < ffn) ru.add(f, t, i, ref);
-                        else ru.ptr.push_back(nullptr);
-                    }
-                }
+                split(ftiles, l3m::kClusterCtas, c, &t0, &t1);
+                for (const l3m_tensor *t : {wu, wg}) add_rows(ru, f, t, (sr.f_lo + t0) * T, (sr.f_lo + t1) * T, ref);
             }
-            out.off_up[l] = pack_rows(s, ru, f, b + "upgate16", out, ref, &out.dt_up[l]);
+            out.off_up[l] = pack_rows(s, ru, f, b + "upgate16", out, !packed_ok, &out.dt_up[l]);
             out.off_gate[l] = (size_t)-1;
             out.dt_gate[l] = out.dt_up[l];
         } else {
             Rows ru, rg;
-            for (int i = 0; i < ffn; i++) ru.add(f, wu, i, ref);
-            for (int i = 0; i < ffn; i++) rg.add(f, wg, i, ref);
-            out.off_up[l] = pack_rows(s, ru, f, b + "up", out, ref, &out.dt_up[l]);
-            out.off_gate[l] = pack_rows(s, rg, f, b + "gate", out, ref, &out.dt_gate[l]);
+            add_rows(ru, f, wu, sr.f_lo * T, ffn_hi, ref);
+            add_rows(rg, f, wg, sr.f_lo * T, ffn_hi, ref);
+            out.off_up[l] = pack_rows(s, ru, f, b + "up", out, !packed_ok, &out.dt_up[l]);
+            out.off_gate[l] = pack_rows(s, rg, f, b + "gate", out, !packed_ok, &out.dt_gate[l]);
         }
         Rows rd;
         const l3m_tensor *wd = l3m_file_blk(f, l, "w_down");
-        for (int i = 0; i < (int)wd->shape[0]; i++) rd.add(f, wd, i, ref);
-        out.off_down[l] = pack_rows(s, rd, f, b + "down", out, ref, &out.dt_down[l]);
+        add_rows(rd, f, wd, sr.d_lo * T, std::min(sr.d_hi * T, (int)wd->shape[0]), ref);
+        out.off_down[l] = pack_rows(s, rd, f, b + "down", out, !packed_ok, &out.dt_down[l]);
     }
     const l3m_tensor *head = l3m_file_tensor(f, (f->h->flags & L3M_F_TIED) ? "embed" : "lm_head");
     Rows rh;
-    for (int i = 0; i < (int)head->shape[0]; i++) rh.add(f, head, i, ref);
-    out.off_head = pack_rows(s, rh, f, "head", out, ref, &out.dt_head);
+    add_rows(rh, f, head, sr.v_lo * T, std::min(sr.v_hi * T, (int)head->shape[0]), ref);
+    out.off_head = pack_rows(s, rh, f, "head", out, !packed_ok, &out.dt_head);
 }
 
 // Build everything one GPU holds and fill its decode arguments.
@@ -291,8 +323,10 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     Stage s;
     std::vector<l3m::LayerDev> layers(L);
     Streamed sw;
-    pack_streamed(f, ref, m->n_heads, m->n_kv, hd, s, sw);
+    const ShardRange sr = shard_range(f->h, m->n_gpus, g.rank);
+    pack_streamed(f, ref, sr, hd, s, sw);
     const int n_qkv = (m->n_heads + 2 * m->n_kv) * hd;
+    const int heads_g = sr.head_hi - sr.head_lo, kv_g = sr.kv_hi - sr.kv_lo, n_qkv_g = (heads_g + 2 * kv_g) * hd;
     const std::vector<size_t> &off_qkv = sw.off_qkv, &off_wo = sw.off_wo, &off_gate = sw.off_gate, &off_up = sw.off_up, &off_down = sw.off_down;
     for (int l = 0; l < L; l++) {
         layers[l].dt_qkv = sw.dt_qkv[l]; layers[l].dt_wo = sw.dt_wo[l]; layers[l].dt_up = sw.dt_up[l];
@@ -338,9 +372,9 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     // Per layer: K [n_kv][ctx][hd] (a row per position) and V transposed, [n_kv][hd][vstride] (a
     // column per position), both bf16.
     const int vstride = (m->ctx + 7) & ~7;
-    const size_t k_per = (size_t)m->n_kv * m->ctx * hd, v_per = (size_t)m->n_kv * hd * vstride;
+    const size_t k_per = (size_t)kv_g * m->ctx * hd, v_per = (size_t)kv_g * hd * vstride;   // this GPU's kv heads
     g.kv_bytes = (size_t)L * (k_per + v_per) * 2;
-    if (!cuda_ok(cudaMalloc(&g.kv, g.kv_bytes), "KV cache")) return false;
+    if (!cuda_ok(cudaMalloc(&g.kv, std::max(g.kv_bytes, (size_t)256)), "KV cache")) return false;
     cudaMemset(g.kv, 0, g.kv_bytes);
     auto A = [&](long long off) -> const float * { return off < 0 ? nullptr : (const float *)(g.arena + off); };
     for (int l = 0; l < L; l++) {
@@ -365,7 +399,7 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
 
     // Each CTA's share of every phase: contiguous tile ranges, the reference's split (engine.c:471-476);
     // query heads round-robin over the CTAs.
-    const int Td = tiles_of(dim), Tf = tiles_of(ffn), Tv = tiles_of(V), Tq = tiles_of(n_qkv);
+    const int Td = sr.d_hi - sr.d_lo, Tf = sr.f_hi - sr.f_lo, Tv = sr.v_hi - sr.v_lo, Tq = tiles_of(n_qkv_g);   // this GPU's tiles
     // Roles for a grid of gt CTAs; the shared-memory layout is sized for the largest share (gt = G).
     auto make_roles = [&](int gt) {
         std::vector<l3m::Role> rs(gt);
@@ -373,7 +407,7 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
             l3m::Role &r = rs[c];
             r = l3m::Role{-1, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
             if (c < G) {
-                r.head0 = c < m->n_heads ? c : -1;
+                r.head0 = c < heads_g ? sr.head_lo + c : -1;
                 split(Tq, G, c, &r.qkv0, &r.qkv1);
                 split(Td, G, c, &r.wo0, &r.wo1);
                 split(Tf, G, c, &r.ffn0, &r.ffn1);
@@ -390,6 +424,23 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     l3m::DecodeArgs &a = g.args;
     a.dim = dim; a.hd = hd; a.ffn = ffn; a.vocab = V; a.ctx = m->ctx; a.n_heads = m->n_heads; a.n_kv = m->n_kv; a.hpk = m->hpk;
     a.n_layers = L; a.n_qkv = n_qkv; a.grid = GT; a.eps = m->f.h->norm_eps;
+    {
+        l3m::Shard &h = a.sh;
+        h = l3m::Shard{};
+        h.n_gpus = m->n_gpus;
+        h.gpu = g.rank;
+        h.head_lo = sr.head_lo; h.n_heads_g = heads_g; h.kv_lo = sr.kv_lo; h.n_kv_g = kv_g; h.n_qkv_g = n_qkv_g;
+        h.d_off = sr.d_lo; h.f_off = sr.f_lo; h.v_off = sr.v_lo;
+        for (int r = 0; r < m->n_gpus; r++) {                             // every GPU's slice of each exchanged vector
+            const ShardRange o2 = shard_range(f->h, m->n_gpus, r);
+            h.lo[l3m::kXAttn][r] = o2.head_lo * hd;
+            h.len[l3m::kXAttn][r] = (o2.head_hi - o2.head_lo) * hd;
+            h.lo[l3m::kXProj][r] = h.lo[l3m::kXDown][r] = o2.d_lo * L3M_TILE;
+            h.len[l3m::kXProj][r] = h.len[l3m::kXDown][r] = std::min(o2.d_hi * L3M_TILE, dim) - o2.d_lo * L3M_TILE;
+            h.lo[l3m::kXH][r] = o2.f_lo * L3M_TILE;
+            h.len[l3m::kXH][r] = std::min(o2.f_hi * L3M_TILE, ffn) - o2.f_lo * L3M_TILE;
+        }
+    }
     a.layers = g.layers;
     a.head = g.arena + off_head; a.dt_head = dt_head;
     a.embed = g.arena + off_embed; a.dt_embed = dt_embed; a.embed_row_bytes = (long long)emb_row;
@@ -507,8 +558,16 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     a.hx.count = a.hx.flag + 32;
     a.hx.abort_flag = (int *)(a.hx.flag + 16);
     a.hx.slots = (float *)(a.hx.flag + 64);
-    a.ctrl = m->ctrl_dev;
+    a.ctrl = m->ctrl_dev + g.rank;
     a.tokens = m->tokens_dev;
+    if (m->n_gpus > 1) {                                               // what the other GPUs write into (zeroed: epoch 0 never matches)
+        g.rx_bytes = (size_t)2 * (3 * dim + ffn) * sizeof(unsigned long long);
+        g.vote_bytes = (size_t)2 * l3m::kMaxShardGpus * 2 * sizeof(unsigned long long);
+        if (!cuda_ok(cudaMalloc(&g.rx, g.rx_bytes), "exchange buffers") || !cuda_ok(cudaMalloc(&g.vote, g.vote_bytes), "vote buffers"))
+            return false;
+        cudaMemset(g.rx, 0, g.rx_bytes);
+        cudaMemset(g.vote, 0, g.vote_bytes);
+    }
     if (!cuda_ok(cudaStreamCreateWithFlags(&g.stream, cudaStreamNonBlocking), "stream")) return false;
     if (!cuda_ok(cudaStreamCreateWithFlags(&g.side, cudaStreamNonBlocking), "stream")) return false;
     if (!cuda_ok(cudaMalloc(&g.args_dev, sizeof(l3m::DecodeArgs)), "args")) return false;
@@ -542,6 +601,36 @@ bool place_in_l2(l3m_model *m, Gpu &g, const l3m_opts &o, bool *over) {
         cudaStreamSetAttribute(g.stream, cudaStreamAttributeAccessPolicyWindow, &attr);
     }
     cudaGetLastError();   // the window is best effort
+    return true;
+}
+
+// Several GPUs: peer access both ways between every pair, then every GPU's arguments get every
+// GPU's receive buffers, vote buffer, logits history and abort word.
+bool connect_gpus(l3m_model *m) {
+    for (int i = 0; i < m->n_gpus; i++) {
+        cudaSetDevice(m->g[i].dev);
+        for (int j = 0; j < m->n_gpus; j++) {
+            if (i == j) continue;
+            cudaError_t e = cudaDeviceEnablePeerAccess(m->g[j].dev, 0);
+            if (e == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+            else if (!cuda_ok(e, "peer access")) return false;
+        }
+    }
+    for (int i = 0; i < m->n_gpus; i++) {
+        l3m::Shard &h = m->g[i].args.sh;
+        for (int j = 0; j < m->n_gpus; j++) {
+            const Gpu &o = m->g[j];
+            const int dim = m->dim;
+            unsigned long long *base = o.rx;                           // [kind][2 halves][length]
+            h.rx[j][l3m::kXAttn] = base;
+            h.rx[j][l3m::kXProj] = base + 2 * (size_t)dim;
+            h.rx[j][l3m::kXDown] = base + 4 * (size_t)dim;
+            h.rx[j][l3m::kXH] = base + 6 * (size_t)dim;
+            h.vote[j] = o.vote;
+            h.logits[j] = o.logits;
+            h.abort[j] = o.args.hx.abort_flag;
+        }
+    }
     return true;
 }
 
@@ -583,7 +672,7 @@ L3M_API int l3m_write_packed(const char *in, const char *out) {
     const int hd = (int)(h->dim / h->n_heads);
     Stage s;
     Streamed sw;
-    pack_streamed(&f, false, (int)h->n_heads, (int)h->n_kv_heads, hd, s, sw);
+    pack_streamed(&f, false, shard_range(h, 1, 0), hd, s, sw);
     std::vector<l3m_tensor> toc;
     for (uint32_t i = 0; i < h->n_tensors; i++)
         if (strncmp(f.toc[i].name, kPackedPrefix, strlen(kPackedPrefix))) toc.push_back(f.toc[i]);
@@ -623,7 +712,7 @@ L3M_API int l3m_write_packed(const char *in, const char *out) {
     if (l3m_file_open(&g, out)) return -1;
     Stage s2;
     Streamed sw2;
-    pack_streamed(&g, false, (int)g.h->n_heads, (int)g.h->n_kv_heads, hd, s2, sw2);
+    pack_streamed(&g, false, shard_range(g.h, 1, 0), hd, s2, sw2);
     l3m_file_close(&g);
     if (s2.buf != s.buf) { fprintf(stderr, "l3m: %s: the packed section does not read back as written\n", out); return -1; }
     return 0;
@@ -651,17 +740,29 @@ L3M_API l3m_model *l3m_load(const char *path, const l3m_opts *opts) {
         if (list[i] < 0 || list[i] >= devices) return fail(m, "bad GPU list: no such device");
         for (int j = 0; j < i; j++) if (list[j] == list[i]) return fail(m, "a GPU appears twice in the list");
     }
-    if (n > 1) return fail(m, "sharding one model over several GPUs in one process is not built; run one process per GPU");
+    if (n > l3m::kMaxShardGpus) return fail(m, "bad GPU list: at most 8 GPUs");
+    if (n > 1) {
+        // Every GPU must produce a slice of the dim and ffn vectors each layer (the exchange buffers'
+        // reuse rests on it), and every pair must reach the other's memory.
+        if (tiles_of(m->dim) < n || tiles_of(m->ffn) < n) return fail(m, "dim or ffn has fewer 16-row tiles than GPUs: use fewer GPUs");
+        for (int i = 0; i < n; i++)
+            for (int j = 0; j < n; j++) {
+                int can = 0;
+                if (i != j && (cudaDeviceCanAccessPeer(&can, list[i], list[j]) != cudaSuccess || !can))
+                    return fail(m, "a GPU of the list cannot access another's memory (no peer access between them)");
+            }
+    }
     m->n_gpus = n;
     cudaSetDevice(list[0]);
-    if (!cuda_ok(cudaHostAlloc((void **)&m->ctrl, sizeof(l3m::Ctrl), cudaHostAllocMapped), "control block") ||
-        !cuda_ok(cudaHostAlloc((void **)&m->tokens, (size_t)m->ctx * 4, cudaHostAllocMapped), "token ring"))
+    if (!cuda_ok(cudaHostAlloc((void **)&m->ctrl, sizeof(l3m::Ctrl) * kMaxGpus, cudaHostAllocMapped | cudaHostAllocPortable), "control block") ||
+        !cuda_ok(cudaHostAlloc((void **)&m->tokens, (size_t)m->ctx * 4, cudaHostAllocMapped | cudaHostAllocPortable), "token ring"))
         return fail(m, "host-mapped memory unavailable");
     cudaHostGetDevicePointer((void **)&m->ctrl_dev, m->ctrl, 0);
     cudaHostGetDevicePointer((void **)&m->tokens_dev, m->tokens, 0);
     bool over_any = false;
     for (int i = 0; i < n; i++) {
         m->g[i].dev = list[i];
+        m->g[i].rank = i;
         if (!build_gpu(m, m->g[i], o)) { l3m_free(m); return nullptr; }
         bool over;
         if (!place_in_l2(m, m->g[i], o, &over)) {
@@ -669,6 +770,7 @@ L3M_API l3m_model *l3m_load(const char *path, const l3m_opts *opts) {
         }
         m->weight_bytes += m->g[i].weight_bytes;
     }
+    if (n > 1 && !connect_gpus(m)) { l3m_free(m); return nullptr; }
     if (over_any) {
         char msg[256];
         snprintf(msg, sizeof msg, "the weights will not stay resident in the persisting L2 window on %d GPU%s: use more GPUs, "
@@ -701,7 +803,7 @@ L3M_API void l3m_free(l3m_model *m) {
             cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, g.prev_limit);
         }
         cudaFree(g.arena); cudaFree(g.kv); cudaFree(g.rope); cudaFree(g.layers); cudaFree(g.roles); cudaFree(g.args_dev); cudaFree(g.trace); cudaFree(g.hx);
-        cudaFree(g.prompt); cudaFree(g.logits); cudaFree(g.probs);
+        cudaFree(g.prompt); cudaFree(g.logits); cudaFree(g.probs); cudaFree(g.rx); cudaFree(g.vote);
         if (g.ev0) cudaEventDestroy(g.ev0);
         if (g.ev1) cudaEventDestroy(g.ev1);
         if (g.stream) cudaStreamDestroy(g.stream);
@@ -719,21 +821,41 @@ L3M_API int l3m_generate(l3m_model *m, const int32_t *prompt, int n_prompt, int 
     for (int i = 0; i < n_prompt; i++)
         if (prompt[i] < 0 || prompt[i] >= m->vocab) { fprintf(stderr, "l3m: token %d out of range\n", prompt[i]); return -1; }
     Gpu &g = m->g[0];
-    cudaSetDevice(g.dev);
-    memset((void *)m->ctrl, 0, sizeof *m->ctrl);
-    l3m::DecodeArgs a = g.args;
-    a.n_prompt = n_prompt;
-    a.max_new = max_new;
-    a.temp = temperature > 0 ? temperature : 0.0f;                     // NaN and <= 0: greedy (reference engine.c:301)
-    a.rng = seed * 0x9E3779B97F4A7C15ULL + 1;                           // reference engine.c:555
-    a.probs = g.probs;
+    memset((void *)m->ctrl, 0, sizeof(l3m::Ctrl) * kMaxGpus);
+    // Exchange epochs: every layer step and sampled position of this launch gets epochs no earlier
+    // launch used; before they would wrap, the (idle) exchange buffers are cleared and they restart.
+    const uint32_t span = (uint32_t)m->ctx * (uint32_t)(m->n_layers + 1) + 64;
+    if (m->n_gpus > 1 && m->epoch_next > 0x3F000000u - span) {
+        for (int i = 0; i < m->n_gpus; i++) {
+            cudaSetDevice(m->g[i].dev);
+            cudaMemset(m->g[i].rx, 0, m->g[i].rx_bytes);
+            cudaMemset(m->g[i].vote, 0, m->g[i].vote_bytes);
+            cudaDeviceSynchronize();
+        }
+        m->epoch_next = 1;
+    }
+    const uint32_t epoch0 = m->epoch_next;
+    m->epoch_next += span;
     const double t0 = now_ns();
-    cudaMemcpyAsync(g.prompt, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, g.stream);
-    cudaMemcpyAsync(g.args_dev, &a, sizeof a, cudaMemcpyHostToDevice, g.stream);
-    cudaMemsetAsync(g.hx, 0, g.hx_bytes, g.stream);                    // flag, count and abort word start at 0
-    cudaEventRecord(g.ev0, g.stream);
-    if (l3m_decode_launch(&a, g.args_dev, g.stream)) return -1;
-    cudaEventRecord(g.ev1, g.stream);
+    for (int i = m->n_gpus - 1; i >= 0; i--) {                          // GPU 0 last: its events time the call
+        Gpu &gi = m->g[i];
+        cudaSetDevice(gi.dev);
+        l3m::DecodeArgs a = gi.args;
+        a.n_prompt = n_prompt;
+        a.max_new = max_new;
+        a.temp = temperature > 0 ? temperature : 0.0f;                 // NaN and <= 0: greedy (reference engine.c:301)
+        a.rng = seed * 0x9E3779B97F4A7C15ULL + 1;                       // reference engine.c:555
+        a.probs = gi.probs;
+        a.sh.epoch0 = epoch0;
+        a.sh.all_logits = a.temp > 0.0f;                               // every GPU samples from the whole row
+        cudaMemcpyAsync(gi.prompt, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, gi.stream);
+        cudaMemcpyAsync(gi.args_dev, &a, sizeof a, cudaMemcpyHostToDevice, gi.stream);
+        cudaMemsetAsync(gi.hx, 0, gi.hx_bytes, gi.stream);              // flag, count and abort word start at 0
+        cudaEventRecord(gi.ev0, gi.stream);
+        if (l3m_decode_launch(&a, gi.args_dev, gi.stream)) return -1;
+        cudaEventRecord(gi.ev1, gi.stream);
+    }
+    cudaSetDevice(g.dev);
     int seen = 0, n_gen = 0, stopped = -1;
     if (on_token) {
         for (;;) {
@@ -758,10 +880,19 @@ L3M_API int l3m_generate(l3m_model *m, const int32_t *prompt, int n_prompt, int 
     }
     cudaError_t e = cudaStreamSynchronize(g.stream);
     const double t1 = now_ns();
+    for (int i = 1; i < m->n_gpus && e == cudaSuccess; i++) {
+        cudaSetDevice(m->g[i].dev);
+        e = cudaStreamSynchronize(m->g[i].stream);
+    }
+    cudaSetDevice(g.dev);
     if (!cuda_ok(e, "decode")) return -1;
-    if (!m->ctrl->done || m->ctrl->error) {
-        report_decode_error(m->ctrl);
-        return -1;
+    for (int i = 0; i < m->n_gpus; i++) {
+        const l3m::Ctrl *c = m->ctrl + i;
+        if (!c->done || c->error) {
+            if (m->n_gpus > 1) fprintf(stderr, "l3m: GPU %d of %d:\n", i, m->n_gpus);
+            report_decode_error(c);
+            return -1;
+        }
     }
     int last_pos;
     if (stopped >= 0) {
