@@ -163,6 +163,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gemv_stream_kernel(float *y
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();                                                       // the barriers are initialised
+    // Launched as a programmatic dependent: everything above overlaps the previous kernel's tail; no
+    // global memory is read before that kernel has completed (its writes, x or the tiles, visible).
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     // The producer: chunk c of this CTA's tiles into stage c % kStreamStages, once the compute warps
     // have released that stage (from the second round of the ring on).
     auto issue = [&](int c) {
@@ -181,6 +184,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gemv_stream_kernel(float *y
     const int early = min(total, kStreamStages);                           // the first ring needs no release
     if (warp == kStreamWarps)
         for (int c = 0; c < early; c++) issue(c);                          // the weights stream in while x is loaded
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");        // the next launch may start its prologue
     load_prep(DT, x, k, p);                                                // every thread; ends with __syncthreads
     if (warp == kStreamWarps) {
         for (int c = early; c < total; c++) issue(c);
@@ -360,6 +364,27 @@ __global__ void __launch_bounds__(kThreads) attend_kernel(float *out, const floa
 
 VecArg vec_arg(const l3m_vec *x) { return VecArg{x->f32, x->bf16, x->q8, x->scale, x->sum}; }
 
+// One streamed-matvec launch as a programmatic dependent launch: the kernel's prologue (shared-memory
+// barriers) may run while the previous work on the stream finishes; the kernel waits for that work
+// (griddepcontrol.wait) before it reads any global memory.
+template <class K>
+cudaError_t launch_stream(K kernel, int grid, size_t smem, cudaStream_t s, float *y, const uint8_t *t, int ntiles, int k, VecArg x,
+                          StreamPlan pl, int *tmo) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute at[1];
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kStreamThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, y, t, ntiles, k, x, pl, tmo);
+}
+
 // The kernels read tiles with 16-byte (and 4-byte) loads and x, y as 4-byte words: a misaligned
 // pointer would fault the caller's context, so it is refused before anything launches.
 bool misaligned_args(int dtype, const void *y, const void *tiles, const l3m_vec *x) {
@@ -480,21 +505,10 @@ L3M_API int l3m_gemv_dev(int exact, int dtype, float *y, const void *tiles, int 
         cudaError_t e = cudaSuccess;
         const uint8_t *t = (const uint8_t *)tiles;
         switch (dtype) {
-        case DT_BF16:
-            e = cudaFuncSetAttribute(gemv_stream_kernel<DT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (e == cudaSuccess) gemv_stream_kernel<DT_BF16><<<grid, kStreamThreads, smem, s>>>(y, t, ntiles, k, vec_arg(x), pl, tmo);
-            break;
-        case DT_Q8:
-            e = cudaFuncSetAttribute(gemv_stream_kernel<DT_Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (e == cudaSuccess) gemv_stream_kernel<DT_Q8><<<grid, kStreamThreads, smem, s>>>(y, t, ntiles, k, vec_arg(x), pl, tmo);
-            break;
-        case DT_Q4:
-            e = cudaFuncSetAttribute(gemv_stream_kernel<DT_Q4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (e == cudaSuccess) gemv_stream_kernel<DT_Q4><<<grid, kStreamThreads, smem, s>>>(y, t, ntiles, k, vec_arg(x), pl, tmo);
-            break;
-        default:
-            e = cudaFuncSetAttribute(gemv_stream_kernel<DT_MX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (e == cudaSuccess) gemv_stream_kernel<DT_MX><<<grid, kStreamThreads, smem, s>>>(y, t, ntiles, k, vec_arg(x), pl, tmo);
+        case DT_BF16: e = launch_stream(gemv_stream_kernel<DT_BF16>, grid, smem, s, y, t, ntiles, k, vec_arg(x), pl, tmo); break;
+        case DT_Q8: e = launch_stream(gemv_stream_kernel<DT_Q8>, grid, smem, s, y, t, ntiles, k, vec_arg(x), pl, tmo); break;
+        case DT_Q4: e = launch_stream(gemv_stream_kernel<DT_Q4>, grid, smem, s, y, t, ntiles, k, vec_arg(x), pl, tmo); break;
+        default: e = launch_stream(gemv_stream_kernel<DT_MX>, grid, smem, s, y, t, ntiles, k, vec_arg(x), pl, tmo); break;
         }
         if (e != cudaSuccess) return fail(e, "l3m_gemv_dev");
     } else {
