@@ -213,34 +213,43 @@ __device__ __forceinline__ void stage_init(const Smem &s) {
     __syncthreads();
 }
 
-// Tiles [t0, t1) of a matrix of dtype with k inputs: how many of the first ones fit in cap bytes
-// (0 for f32/bf16, which are read from global memory). Same value in every thread.
+// Tiles [t0, t1) of a matrix of dtype with k inputs: how many of the first ones fit in cap bytes at
+// staged_stride apart. Same value in every thread.
 __device__ __forceinline__ int stage_count(int dtype, int k, int t0, int t1, int cap) {
-    if (t1 <= t0 || !(dtype == DT_Q8 || dtype == DT_Q4 || dtype == DT_MX) || cap <= 0) return 0;
-    return min(t1 - t0, cap / (int)tile_bytes(dtype, k));
+    if (t1 <= t0 || cap <= 0) return 0;
+    return min(t1 - t0, cap / (int)staged_stride(dtype, k));
+}
+
+// One thread: copy bytes from src to the shared address dst, completing on the mbarrier bar, in
+// pieces of at most kStageChunk. cold: with an L2 evict-first policy.
+__device__ __noinline__ void bulk_copy(uint32_t dst, const uint8_t *src, uint32_t bytes, uint32_t bar, int cold) {
+    uint64_t policy = 0;
+    if (cold) asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+    for (uint32_t o = 0; o < bytes; o += kStageChunk) {
+        const uint32_t c = min(bytes - o, kStageChunk);
+        if (cold)
+            asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+                         ::"r"(dst + o), "l"(src + o), "r"(c), "r"(bar), "l"(policy) : "memory");
+        else
+            asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                         ::"r"(dst + o), "l"(src + o), "r"(c), "r"(bar) : "memory");
+    }
 }
 
 // Every thread, after a __syncthreads that ends every read of dst: start the copy of tiles
-// [t0, t0 + n) to dst (n = stage_count(...)); returns n. cold: with an L2 evict-first policy.
+// [t0, t0 + n) to dst (n = stage_count(...)); returns n. Quantised tiles go as one contiguous copy,
+// f32/bf16 tiles one copy each at the padded stride. cold: with an L2 evict-first policy.
 __device__ __forceinline__ int stage_issue(const Smem &s, int dtype, const uint8_t *tiles, int k, int t0, int t1, uint8_t *dst, int cap,
                                            int cold = 0) {
     const int n = stage_count(dtype, k, t0, t1, cap);
     if (n > 0 && threadIdx.x == kPrefetchThread) {
-        const size_t tb = tile_bytes(dtype, k);
-        const uint32_t bytes = (uint32_t)(n * tb), bar = smem_addr(s.wbar);
+        const size_t tb = tile_bytes(dtype, k), sst = staged_stride(dtype, k);
+        const uint32_t bar = smem_addr(s.wbar);
         const uint8_t *src = tiles + (size_t)t0 * tb;
-        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-        uint64_t policy = 0;
-        if (cold) asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
-        for (uint32_t o = 0; o < bytes; o += kStageChunk) {
-            const uint32_t c = min(bytes - o, kStageChunk);
-            if (cold)
-                asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
-                             ::"r"(smem_addr(dst + o)), "l"(src + o), "r"(c), "r"(bar), "l"(policy) : "memory");
-            else
-                asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                             ::"r"(smem_addr(dst + o)), "l"(src + o), "r"(c), "r"(bar) : "memory");
-        }
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"((uint32_t)(n * tb)) : "memory");
+        if (sst == tb) bulk_copy(smem_addr(dst), src, (uint32_t)(n * tb), bar, cold);
+        else
+            for (int i = 0; i < n; i++) bulk_copy(smem_addr(dst + i * sst), src + i * tb, (uint32_t)tb, bar, cold);
     }
     return n;
 }
@@ -747,8 +756,10 @@ __device__ __noinline__ int wait_word(const DecodeArgs &a, const uint32_t *p, ui
 // The head matvec over this CTA's vocabulary tiles of the final x in s.x (logits kept for
 // l3m_logits), this CTA's argmax -> hx.slots[cta] with an arrival on hx.count. host_stop: the
 // host's stop request (cluster 0, CTA 0 only). GPT2: the final LayerNorm.
+// staged, ns: the first ns of the CTA's tiles are resident in shared memory (helper CTAs).
 template <bool GPT2>
-__device__ __noinline__ void head_logits(const DecodeArgs &a, const Role &role, const Smem &s, int pos, int host_stop, int tslot) {
+__device__ __noinline__ void head_logits(const DecodeArgs &a, const Role &role, const Smem &s, int pos, int host_stop, int tslot,
+                                         const uint8_t *staged = nullptr, int ns = 0) {
     const int cta = blockIdx.x, tid = threadIdx.x, nth = blockDim.x;
     float best = -INFINITY;
     int best_i = -1;
@@ -758,7 +769,7 @@ __device__ __noinline__ void head_logits(const DecodeArgs &a, const Role &role, 
         trace(a, tslot, pos, a.n_layers, 3);
         prepare(a.dt_head, s.xb, a.dim, s.prep);
         trace(a, tslot, pos, a.n_layers, 4);
-        matvec_exact(a.dt_head, a.head, a.dim, role.voc0, role.voc1, s.prep, s.scratch, a.scratch_pairs, s.y);
+        matvec_exact(a.dt_head, a.head, a.dim, role.voc0, role.voc1, s.prep, s.scratch, a.scratch_pairs, s.y, staged, ns);
         trace(a, tslot, pos, a.n_layers, 5);
         float *lg = a.logits + (size_t)pos * a.vocab;
         const int g0 = (a.sh.v_off + role.voc0) * kTile, n = min((a.sh.v_off + role.voc1) * kTile, a.vocab) - g0;
@@ -858,28 +869,35 @@ __device__ __noinline__ void gpu_vote(const DecodeArgs &a, const Smem &s, uint32
 }
 
 // A CTA outside cluster 0: between sampled positions it sleeps on hx.flag; for each published x it
-// computes its vocabulary tiles. Ends when cluster 0 writes kHeadDone (or on a failed wait).
+// computes its vocabulary tiles. Its shared memory holds no layer state, so as many of its tiles as
+// fit in the whole staging area are copied in once, at launch, and stay there for every position;
+// the rest are pulled into L2 ahead of each use (cold: every tile, every position). Ends when
+// cluster 0 writes kHeadDone (or on a failed wait).
 template <bool GPT2>
-__device__ __noinline__ void head_helper(const DecodeArgs &a, const Role &role, const Smem &s) {
-    if (role.voc0 < role.voc1 && threadIdx.x == 0) {
-        const size_t th = tile_bytes(a.dt_head, a.dim);
-        prefetch_l2(a.head + role.voc0 * th, (size_t)(role.voc1 - role.voc0) * th);
-    }
+__device__ __noinline__ void head_helper(const DecodeArgs &a, const Role &role, const Smem &s, int cold) {
+    stage_init(s);
+    const int nres = cold ? 0 : stage_issue(s, a.dt_head, a.head, a.dim, role.voc0, role.voc1, s.w, a.w_bytes);   // cold: read each time
+    const size_t th = tile_bytes(a.dt_head, a.dim);
+    const int rest0 = role.voc0 + nres;
+    if (rest0 < role.voc1 && threadIdx.x == 0) prefetch_l2(a.head + rest0 * th, (size_t)(role.voc1 - rest0) * th);
+    bool landed = nres == 0;
     for (uint32_t e = 1;; e++) {
-        if (wait_word(a, a.hx.flag, e, true, -1, kWaitHeadFlag) <= 0) return;
+        if (wait_word(a, a.hx.flag, e, true, -1, kWaitHeadFlag) <= 0) break;
         const int pos = __float_as_int(ld_cg_f32(a.hx.x + a.dim));
         if ((a.dim & 3) == 0)
             for (int i = threadIdx.x * 4; i < a.dim; i += blockDim.x * 4) *(float4 *)(s.x + i) = __ldcg((const float4 *)(a.hx.x + i));
         else
             for (int i = threadIdx.x; i < a.dim; i += blockDim.x) s.x[i] = ld_cg_f32(a.hx.x + i);
         cp_async_wait_all();                                              // the final norm's weights
-        __syncthreads();
-        head_logits<GPT2>(a, role, s, pos, 0, -1);
-        if (role.voc0 < role.voc1 && threadIdx.x == 0) {                  // the next position reads the same tiles
-            const size_t th = tile_bytes(a.dt_head, a.dim);
-            prefetch_l2(a.head + role.voc0 * th, (size_t)(role.voc1 - role.voc0) * th);
+        if (!landed) {                                                    // the resident tiles (first position only)
+            stage_wait(a, s, 0, pos, -1);
+            landed = true;
         }
+        __syncthreads();
+        head_logits<GPT2>(a, role, s, pos, 0, -1, s.w, nres);
+        if (rest0 < role.voc1 && threadIdx.x == 0) prefetch_l2(a.head + rest0 * th, (size_t)(role.voc1 - rest0) * th);
     }
+    if (!landed) stage_wait(a, s, 0, -1, -1, true);                       // no copy outlives the CTA
 }
 
 // One instance per model family and cache mode, so that neither costs the other registers or
@@ -948,7 +966,7 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
     }
     if (cta >= kClusterCtas) {                                            // the other clusters: head tiles only
         cp_async_commit();
-        head_helper<GPT2>(a, role, s);
+        head_helper<GPT2>(a, role, s, COLD);
         cp_async_wait_all();
         return;
     }

@@ -401,7 +401,9 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     // query heads round-robin over the CTAs.
     const int Td = sr.d_hi - sr.d_lo, Tf = sr.f_hi - sr.f_lo, Tv = sr.v_hi - sr.v_lo, Tq = tiles_of(n_qkv_g);   // this GPU's tiles
     // Roles for a grid of gt CTAs; the shared-memory layout is sized for the largest share (gt = G).
-    auto make_roles = [&](int gt) {
+    // helpers_only: the head's tiles go to the helper clusters alone (when they can keep every one
+    // resident in shared memory), else to every CTA.
+    auto make_roles = [&](int gt, bool helpers_only = false) {
         std::vector<l3m::Role> rs(gt);
         for (int c = 0; c < gt; c++) {
             l3m::Role &r = rs[c];
@@ -413,7 +415,8 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
                 split(Tf, G, c, &r.ffn0, &r.ffn1);
                 split(Td, G, c, &r.dn0, &r.dn1);
             }
-            split(Tv, gt, c, &r.voc0, &r.voc1);
+            if (!helpers_only) split(Tv, gt, c, &r.voc0, &r.voc1);
+            else if (c >= G) split(Tv, gt - G, c - G, &r.voc0, &r.voc1);
         }
         return rs;
     };
@@ -539,14 +542,18 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
         return false;
     }
     a.grid = GT;
+    // The helper clusters keep their head tiles in shared memory (decode.cu head_helper): when all of
+    // them fit there, cluster 0 takes none and goes straight from the last layer to the token vote.
+    const int resident = a.w_bytes / (int)l3m::staged_stride(dt_head, dim);
+    const bool helpers_only = GT > G && !m->cold && (long long)resident * (GT - G) >= Tv;
     a.async_x = !getenv("L3M_CLUSTER_BARRIERS");                        // every CTA of cluster 0 must produce qkv rows
     {
-        std::vector<l3m::Role> rs0 = make_roles(GT);
+        std::vector<l3m::Role> rs0 = make_roles(GT, helpers_only);
         for (int c = 0; c < G; c++)
             if (rs0[c].qkv0 >= rs0[c].qkv1) a.async_x = 0;
     }
     {
-        std::vector<l3m::Role> roles = make_roles(GT);
+        std::vector<l3m::Role> roles = make_roles(GT, helpers_only);
         if (!cuda_ok(cudaMalloc(&g.roles, sizeof(l3m::Role) * GT), "roles")) return false;
         cudaMemcpy(g.roles, roles.data(), sizeof(l3m::Role) * GT, cudaMemcpyHostToDevice);
         a.roles = g.roles;

@@ -31,6 +31,12 @@ __host__ __device__ inline size_t tile_bytes(int dtype, int k) {
     if (dtype == DT_BF16) return (size_t)k * kTile * 2;
     return (size_t)(k / kQB) * block_bytes(dtype);
 }
+// Distance between consecutive tiles copied into shared memory. f32/bf16 tiles are copied one by
+// one, 64 bytes apart beyond their size: the two half-warps of a warp (two tiles, one output each
+// per lane) then read opposite halves of the banks.
+__host__ __device__ inline size_t staged_stride(int dtype, int k) {
+    return tile_bytes(dtype, k) + (dtype == DT_F32 || dtype == DT_BF16 ? 64 : 0);
+}
 
 // A prepared activation in shared memory.
 struct Prep {
@@ -269,9 +275,100 @@ __device__ void qmatvec(const uint8_t *tiles, const uint8_t *tilesB, int ntA, in
     }
 }
 
+// Shared-memory loads by address (the staged chains below): no side effects, so the compiler may
+// schedule them freely within the loop that uses them.
+__device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
+    uint32_t v;
+    asm("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ float lds_f32(uint32_t a) { return __uint_as_float(lds_u32(a)); }
+__device__ __forceinline__ float4 lds_f4(uint32_t a) {
+    float4 v;
+    asm("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
+    return v;
+}
+
+// One output's bf16 chain over a tile staged in shared memory (the reference's order, products exact
+// inside each fma): word q of the output at wa + 64 q holds inputs 2q (low half) and 2q + 1; x (fp32)
+// at xa. 16 inputs per step, the next step's loads in flight during this step's 16 fmas.
+__device__ __forceinline__ float chain_bf16_shared(uint32_t wa, uint32_t xa, int k) {
+    const int nw = k >> 1;
+    float acc = 0.0f;
+    int q = 0;
+    if (nw >= 8) {
+        uint32_t w[8];
+        float4 x[4];
+#pragma unroll
+        for (int j = 0; j < 8; j++) w[j] = lds_u32(wa + 64 * j);
+#pragma unroll
+        for (int j = 0; j < 4; j++) x[j] = lds_f4(xa + 16 * j);
+        for (; q + 8 <= nw; q += 8) {
+            const int qn = q + 16 <= nw ? q + 8 : q;
+            uint32_t wn[8];
+            float4 xn[4];
+#pragma unroll
+            for (int j = 0; j < 8; j++) wn[j] = lds_u32(wa + 64 * (qn + j));
+#pragma unroll
+            for (int j = 0; j < 4; j++) xn[j] = lds_f4(xa + 8 * qn + 16 * j);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                acc = __fmaf_rn(l3m_bits_f32(w[2 * j] << 16), x[j].x, acc);
+                acc = __fmaf_rn(l3m_bits_f32(w[2 * j] & 0xFFFF0000u), x[j].y, acc);
+                acc = __fmaf_rn(l3m_bits_f32(w[2 * j + 1] << 16), x[j].z, acc);
+                acc = __fmaf_rn(l3m_bits_f32(w[2 * j + 1] & 0xFFFF0000u), x[j].w, acc);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) w[j] = wn[j];
+#pragma unroll
+            for (int j = 0; j < 4; j++) x[j] = xn[j];
+        }
+    }
+    for (; q < nw; q++) {
+        const uint32_t v = lds_u32(wa + 64 * q);
+        acc = __fmaf_rn(l3m_bits_f32(v << 16), lds_f32(xa + 8 * q), acc);
+        acc = __fmaf_rn(l3m_bits_f32(v & 0xFFFF0000u), lds_f32(xa + 8 * q + 4), acc);
+    }
+    return acc;
+}
+
+// The same for an f32 tile (input i of the output at wa + 64 i): rounded products added up to
+// split, fmas after (the reference build's chain).
+__device__ __forceinline__ float chain_f32_shared(uint32_t wa, uint32_t xa, int k, int split) {
+    float acc = 0.0f;
+    int i = 0;
+    if (split >= 8) {
+        float w[8];
+        float4 x[2];
+#pragma unroll
+        for (int j = 0; j < 8; j++) w[j] = lds_f32(wa + 64 * j);
+        x[0] = lds_f4(xa);
+        x[1] = lds_f4(xa + 16);
+        for (; i + 8 <= split; i += 8) {
+            const int in = i + 16 <= split ? i + 8 : i;
+            float wn[8];
+            float4 xn[2];
+#pragma unroll
+            for (int j = 0; j < 8; j++) wn[j] = lds_f32(wa + 64 * (in + j));
+            xn[0] = lds_f4(xa + 4 * in);
+            xn[1] = lds_f4(xa + 4 * in + 16);
+            const float xv[8] = {x[0].x, x[0].y, x[0].z, x[0].w, x[1].x, x[1].y, x[1].z, x[1].w};
+#pragma unroll
+            for (int j = 0; j < 8; j++) acc = __fadd_rn(acc, __fmul_rn(w[j], xv[j]));
+#pragma unroll
+            for (int j = 0; j < 8; j++) w[j] = wn[j];
+            x[0] = xn[0];
+            x[1] = xn[1];
+        }
+    }
+    for (; i < split; i++) acc = __fadd_rn(acc, __fmul_rn(lds_f32(wa + 64 * i), lds_f32(xa + 4 * i)));
+    for (; i < k; i++) acc = __fmaf_rn(lds_f32(wa + 64 * i), lds_f32(xa + 4 * i), acc);
+    return acc;
+}
+
 // y = tiles[t0, t1) . x for one CTA, exact: y[o] for o in [0, 16 (t1 - t0)) (shared memory).
 // scratch holds scratch_pairs float2 (quantised dtypes; at least k/32). staged, ns: a copy of tiles
-// [t0, t0 + ns) in shared memory (quantised dtypes), read instead of global memory.
+// [t0, t0 + ns) in shared memory, staged_stride(dtype, k) bytes apart, read instead of global memory.
 static __device__ __noinline__ void matvec_exact(int dtype, const uint8_t *tiles, int k, int t0, int t1, const Prep p, float2 *scratch,
                                                  int scratch_pairs, float *y, const uint8_t *staged = nullptr, int ns = 0) {
     const int tid = threadIdx.x, nth = blockDim.x;
@@ -285,11 +382,18 @@ static __device__ __noinline__ void matvec_exact(int dtype, const uint8_t *tiles
     if (dtype == DT_Q4) { qmatvec<DT_Q4, true>(ta, tbb, nta, k, n, p, scratch, scratch_pairs, y); return; }
     if (dtype == DT_MX) { qmatvec<DT_MX, true>(ta, tbb, nta, k, n, p, scratch, scratch_pairs, y); return; }
     // f32 / bf16 (tiles [K][16] f32, [K/2][16][2] bf16): one thread per output walks its row in input
-    // order, the reference's chain.
+    // order, the reference's chain; lanes 0-15 and 16-31 of a warp take two tiles.
     const int split = fused_from(k);
+    const size_t sst = staged_stride(dtype, k);
+    const uint32_t xa = (uint32_t)__cvta_generic_to_shared(p.xf);
     for (int o = tid; o < n; o += nth) {
-        const uint8_t *tile = base + (size_t)(o >> 4) * tb;
-        const int c = o & 15;
+        const int t = o >> 4, c = o & 15;
+        if (t < ns) {
+            const uint32_t wa = (uint32_t)__cvta_generic_to_shared(staged + (size_t)t * sst) + 4 * c;
+            y[o] = dtype == DT_BF16 ? chain_bf16_shared(wa, xa, k) : chain_f32_shared(wa, xa, k, split);
+            continue;
+        }
+        const uint8_t *tile = base + (size_t)t * tb;
         float acc = 0.0f;
         if (dtype == DT_BF16) {
             const uint32_t *w = (const uint32_t *)tile + c;
