@@ -103,12 +103,14 @@ __device__ __noinline__ void scatter(const float *src, float *dst, int g0, int n
     const int tid = threadIdx.x, nth = blockDim.x, nr = (int)cl.num_blocks();
     if (((g0 | n) & 3) == 0) {
         const int n4 = n >> 2;
+        #pragma unroll 1
         for (int e = tid; e < n4 * nr; e += nth) {
             const int r = e % nr, j = e / nr;
             float4 *d = (float4 *)cl.map_shared_rank(dst + g0, (unsigned)r);
             d[j] = ((const float4 *)src)[j];
         }
     } else {
+        #pragma unroll 1
         for (int e = tid; e < n * nr; e += nth) {
             const int r = e % nr, j = e / nr;
             cl.map_shared_rank(dst + g0, (unsigned)r)[j] = src[j];
@@ -126,6 +128,7 @@ __device__ __noinline__ void scatter_tx(const float *src, float *dst, int g0, in
     const uint32_t ld = (uint32_t)__cvta_generic_to_shared(dst + g0), lb = (uint32_t)__cvta_generic_to_shared(bar);
     if (((g0 | n) & 3) == 0) {
         const int n4 = n >> 2;
+        #pragma unroll 1
         for (int e = tid; e < n4 * kClusterCtas; e += nth) {
             const int r = e % kClusterCtas, j = e / kClusterCtas;
             uint32_t ra, rb;
@@ -136,6 +139,7 @@ __device__ __noinline__ void scatter_tx(const float *src, float *dst, int g0, in
                          ::"r"(ra), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(rb) : "memory");
         }
     } else {
+        #pragma unroll 1
         for (int e = tid; e < n * kClusterCtas; e += nth) {
             const int r = e % kClusterCtas, j = e / kClusterCtas;
             uint32_t ra, rb;
@@ -147,9 +151,13 @@ __device__ __noinline__ void scatter_tx(const float *src, float *dst, int g0, in
     }
 }
 
+// Only the kernel's TRACE instances carry the stamps (the others have no code for them at all).
+template <bool TRACE>
 __device__ __forceinline__ void trace(const DecodeArgs &a, int slot, int pos, int l, int ev) {
-    if (a.trace && slot >= 0 && threadIdx.x == 0)
-        a.trace[(((size_t)slot * a.ctx + pos) * (a.n_layers + 1) + l) * kTraceEvents + ev] = (unsigned long long)clock64();
+    if constexpr (TRACE) {
+        if (slot >= 0 && threadIdx.x == 0)
+            a.trace[(((size_t)slot * a.ctx + pos) * (a.n_layers + 1) + l) * kTraceEvents + ev] = (unsigned long long)clock64();
+    }
 }
 
 // Pull a CTA's weight tiles into L2 ahead of use (cp.async.bulk.prefetch: no registers, no
@@ -183,7 +191,7 @@ __device__ void prefetch_layer(const DecodeArgs &a, const LayerDev &L, const Rol
 // The norm weights of layer L and the RoPE row of position pos, into shared memory (asynchronous;
 // the top of the next layer waits for them). GPT2: the LayerNorm biases too (GPT-2 family).
 template <bool GPT2>
-__device__ void stage_vectors(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s, int pos) {
+__device__ __noinline__ void stage_vectors(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s, int pos) {
     if (role.qkv0 < role.qkv1) {
         stage_f32(s.wa, L.attn_norm, a.dim);
         if (GPT2 && a.layernorm) stage_f32(s.wab, L.attn_norm_b, a.dim);
@@ -201,7 +209,6 @@ __device__ void stage_vectors(const DecodeArgs &a, const LayerDev &L, const Role
 // completion counted in bytes on one mbarrier) while the current phase, its barrier and the next
 // norm run; the matvec then reads shared memory. One copy is outstanding at a time: the phase that
 // consumes it waits for it, and the next copy is issued only after that phase's last read.
-constexpr uint32_t kStageChunk = 1u << 20;   // every stage is one copy (at most the staging area)
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -213,35 +220,27 @@ __device__ __forceinline__ void stage_init(const Smem &s) {
     __syncthreads();
 }
 
-// Tiles [t0, t1) of a matrix of dtype with k inputs: how many of the first ones fit in cap bytes at
-// staged_stride apart. Same value in every thread.
-__device__ __forceinline__ int stage_count(int dtype, int k, int t0, int t1, int cap) {
-    if (t1 <= t0 || cap <= 0) return 0;
-    return min(t1 - t0, cap / (int)staged_stride(dtype, k));
-}
-
-// One thread: copy bytes from src to the shared address dst, completing on the mbarrier bar, in
-// pieces of at most kStageChunk. cold: with an L2 evict-first policy.
+// One thread: one bulk copy of bytes (a multiple of 16, at most the staging area) from src to the
+// shared address dst, completing on the mbarrier bar. cold: with an L2 evict-first policy.
 __device__ __noinline__ void bulk_copy(uint32_t dst, const uint8_t *src, uint32_t bytes, uint32_t bar, int cold) {
-    uint64_t policy = 0;
-    if (cold) asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
-    for (uint32_t o = 0; o < bytes; o += kStageChunk) {
-        const uint32_t c = min(bytes - o, kStageChunk);
-        if (cold)
-            asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
-                         ::"r"(dst + o), "l"(src + o), "r"(c), "r"(bar), "l"(policy) : "memory");
-        else
-            asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                         ::"r"(dst + o), "l"(src + o), "r"(c), "r"(bar) : "memory");
+    if (cold) {
+        uint64_t policy;
+        asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+                     ::"r"(dst), "l"(src), "r"(bytes), "r"(bar), "l"(policy) : "memory");
+    } else {
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                     ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
     }
 }
 
 // Every thread, after a __syncthreads that ends every read of dst: start the copy of tiles
-// [t0, t0 + n) to dst (n = stage_count(...)); returns n. Quantised tiles go as one contiguous copy,
-// f32/bf16 tiles one copy each at the padded stride. cold: with an L2 evict-first policy.
-__device__ __forceinline__ int stage_issue(const Smem &s, int dtype, const uint8_t *tiles, int k, int t0, int t1, uint8_t *dst, int cap,
-                                           int cold = 0) {
-    const int n = stage_count(dtype, k, t0, t1, cap);
+// [t0, t0 + n) to dst, n = min(t1 - t0, cap) where cap is how many tiles fit (precomputed per matrix
+// by the host); returns n. Quantised tiles go as one contiguous copy, f32/bf16 tiles one copy each at
+// the padded stride. cold: with an L2 evict-first policy.
+__device__ __noinline__ int stage_issue(const Smem &s, int dtype, const uint8_t *tiles, int k, int t0, int t1, uint8_t *dst, int cap,
+                                       int cold = 0) {
+    const int n = t1 > t0 ? min(t1 - t0, cap) : 0;
     if (n > 0 && threadIdx.x == kPrefetchThread) {
         const size_t tb = tile_bytes(dtype, k), sst = staged_stride(dtype, k);
         const uint32_t bar = smem_addr(s.wbar);
@@ -331,6 +330,7 @@ __device__ __noinline__ void peer_send(const DecodeArgs &a, int k, const float *
     const int G = a.sh.n_gpus, me = a.sh.gpu;
     const uint64_t e = (uint64_t)(a.sh.epoch0 + step) << 32;
     const size_t half = (size_t)(step & 1u) * (size_t)xlen(a, k);
+    #pragma unroll 1
     for (int j = threadIdx.x; j < n * (G - 1); j += blockDim.x) {
         const int p = j / n, i = j - p * n, g = p < me ? p : p + 1;
         unsigned long long *dst = a.sh.rx[g][k] + half + g0 + i;
@@ -351,6 +351,7 @@ __device__ __noinline__ void peer_recv(const DecodeArgs &a, int k, float *dst, u
     for (int g = 0; g < G && !gave_up; g++) {
         if (g == me) continue;
         const int lo = a.sh.lo[k][g], hi = lo + a.sh.len[k][g];
+        #pragma unroll 1
         for (int i = lo + threadIdx.x; i < hi && !gave_up; i += blockDim.x) {
             for (;;) {
                 uint64_t w;
@@ -380,6 +381,7 @@ __device__ __noinline__ void peer_recv(const DecodeArgs &a, int k, float *dst, u
 template <bool GPT2>
 __device__ __noinline__ void embed_row(const DecodeArgs &a, int tok, int pos, float *x) {
     const uint8_t *row = a.embed + (size_t)tok * a.embed_row_bytes;
+    #pragma unroll 1
     for (int i = threadIdx.x; i < a.dim; i += blockDim.x) {
         float v;
         if (a.dt_embed == DT_F32) v = __ldg((const float *)row + i);
@@ -419,30 +421,25 @@ __device__ __forceinline__ const uint16_t *vcache(const DecodeArgs &a, const Lay
 
 // A head CTA's warps 1.. start the K/V copies of its attention (attend_prestage) while warp 0 runs
 // the serial part of the rmsnorm (GPT2: the LayerNorm).
-template <bool GPT2>
+template <bool GPT2, bool TRACE>
 __device__ __noinline__ void phase_qkv(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s, int ns, uint32_t par, int pos,
                                        int l, int tslot) {
-    if (role.head0 >= 0) {
-        const uint16_t *kc = kcache(a, L, role.head0), *vc = vcache(a, L, role.head0);
-        auto pre = [&](int t, int nt) { attend_prestage<true>(kc, vc, a.hd, a.vstride, pos, a.hd, s.kvbuf, s.vtbuf, a.attn_chunk, t, nt); };
-        if (GPT2 && a.layernorm) layernorm_side(s.x, s.wa, s.wab, a.dim, a.eps, s.xb, s.red, pre);
-        else rmsnorm_side(s.x, s.wa, a.dim, a.eps, s.xb, s.red, pre);
-    } else if (GPT2 && a.layernorm) {
-        layernorm_exact(s.x, s.wa, s.wab, a.dim, a.eps, s.xb, s.red);
-    } else {
-        rmsnorm_exact(s.x, s.wa, a.dim, a.eps, s.xb, s.tmp, s.red);
-    }
-    trace(a, tslot, pos, l, 16);
+    PreStage ps{};
+    if (role.head0 >= 0) ps = PreStage{kcache(a, L, role.head0), vcache(a, L, role.head0), a.hd, a.vstride, pos, a.hd, s.kvbuf, s.vtbuf, a.attn_chunk};
+    if (GPT2 && a.layernorm) layernorm_exact(s.x, s.wa, s.wab, a.dim, a.eps, s.xb, s.red, ps);
+    else rmsnorm_exact(s.x, s.wa, a.dim, a.eps, s.xb, s.red, ps);
+    trace<TRACE>(a, tslot, pos, l, 16);
     prepare(L.dt_qkv, s.xb, a.dim, s.prep);
-    trace(a, tslot, pos, l, 17);
+    trace<TRACE>(a, tslot, pos, l, 17);
     if (ns) stage_wait(a, s, par, pos, l);
-    trace(a, tslot, pos, l, 18);
+    trace<TRACE>(a, tslot, pos, l, 18);
     matvec_exact(L.dt_qkv, L.qkv, a.dim, role.qkv0, role.qkv1, s.prep, s.scratch, a.scratch_pairs, s.y, s.w + a.w_extra, ns);
-    trace(a, tslot, pos, l, 19);
+    trace<TRACE>(a, tslot, pos, l, 19);
     // This GPU's qkv rows: q of its heads, then k and v of its kv heads (biases of the same rows).
     const int g0 = role.qkv0 * kTile, n = min(role.qkv1 * kTile, a.sh.n_qkv_g) - g0, nq = a.sh.n_heads_g * a.hd, nk = a.sh.n_kv_g * a.hd;
     if (L.bq) {
         const int q0 = a.sh.head_lo * a.hd, k0 = a.sh.kv_lo * a.hd;
+        #pragma unroll 1
         for (int o = threadIdx.x; o < n; o += blockDim.x) {
             const int r = g0 + o;
             s.y[o] = __fadd_rn(s.y[o], __ldg(r < nq ? L.bq + q0 + r : r < nq + nk ? L.bk + k0 + (r - nq) : L.bv + k0 + (r - nq - nk)));
@@ -453,11 +450,13 @@ __device__ __noinline__ void phase_qkv(const DecodeArgs &a, const LayerDev &L, c
 
 // Phase A for query head h at position pos (xq complete): RoPE, this position's K/V row (stored by
 // the first head of each kv group this GPU holds), attention -> every CTA's xa[h*hd, (h+1)*hd).
+template <bool TRACE>
 __device__ __noinline__ void phase_attention(const DecodeArgs &a, const LayerDev &L, const Smem &s, int h, int pos, bool prestaged, int l,
                                              int tslot) {
     const int tid = threadIdx.x, nth = blockDim.x, hd = a.hd, hl = h - a.sh.head_lo, kvl = h / a.hpk - a.sh.kv_lo;
     const int nq = a.sh.n_heads_g * hd, nk = a.sh.n_kv_g * hd;
     float *y = s.y;                                                  // q, k, v of this head
+    #pragma unroll 1
     for (int i = tid; i < hd; i += nth) {
         y[i] = s.xq[hl * hd + i];
         y[hd + i] = s.xq[nq + kvl * hd + i];
@@ -470,6 +469,7 @@ __device__ __noinline__ void phase_attention(const DecodeArgs &a, const LayerDev
     }
     uint16_t *kc = (uint16_t *)kcache(a, L, h), *vc = (uint16_t *)vcache(a, L, h);
     const bool writer = h % a.hpk == 0 || h == a.sh.head_lo;
+    #pragma unroll 1
     for (int i = tid; i < hd; i += nth) {
         const uint16_t kb = l3m_f32_to_bf16(y[hd + i]), vb = l3m_f32_to_bf16(y[2 * hd + i]);
         s.kcur[i] = kb;
@@ -480,26 +480,28 @@ __device__ __noinline__ void phase_attention(const DecodeArgs &a, const LayerDev
         }
     }
     __syncthreads();
-    trace(a, tslot, pos, l, 14);
+    trace<TRACE>(a, tslot, pos, l, 14);
     attend_exact<true>(y, kc, vc, hd, a.vstride, s.kcur, s.vcur, pos, hd, s.scores, s.att, s.red, a.elist, a.eindex, s.kvbuf, s.vtbuf,
                        a.attn_chunk, prestaged);
-    trace(a, tslot, pos, l, 15);
+    trace<TRACE>(a, tslot, pos, l, 15);
     if (a.async_x) scatter_tx(s.att, s.xa, h * hd, hd, s.xbar + 1);
     else scatter(s.att, s.xa, h * hd, hd);
 }
 
 // Phase B: this CTA's tiles of wo over attn -> s.y (the caller scatters into xp; ns tiles staged at
 // offset w_extra).
+template <bool TRACE>
 __device__ __noinline__ void phase_wo(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s, int ns, uint32_t par, int pos,
                                       int l, int tslot) {
     prepare(L.dt_wo, s.xa, a.dim, s.prep);
-    trace(a, tslot, pos, l, 20);
+    trace<TRACE>(a, tslot, pos, l, 20);
     if (ns) stage_wait(a, s, par, pos, l);
-    trace(a, tslot, pos, l, 21);
+    trace<TRACE>(a, tslot, pos, l, 21);
     matvec_exact(L.dt_wo, L.wo, a.dim, role.wo0, role.wo1, s.prep, s.scratch, a.scratch_pairs, s.y, s.w + a.w_extra, ns);
-    trace(a, tslot, pos, l, 22);
+    trace<TRACE>(a, tslot, pos, l, 22);
     const int g0 = (a.sh.d_off + role.wo0) * kTile, n = min((a.sh.d_off + role.wo1) * kTile, a.dim) - g0;
     if (L.bo) {
+        #pragma unroll 1
         for (int o = threadIdx.x; o < n; o += blockDim.x) s.y[o] = __fadd_rn(s.y[o], __ldg(L.bo + g0 + o));
         __syncthreads();
     }
@@ -507,20 +509,21 @@ __device__ __noinline__ void phase_wo(const DecodeArgs &a, const LayerDev &L, co
 
 // Phase C: x += proj in every CTA; the ffn CTAs' tiles of up and gate -> s.y (up of the CTA's
 // tiles, then gate; ns tiles of up, or of the interleaved up/gate, staged at offset 0).
-template <bool GPT2>
+template <bool GPT2, bool TRACE>
 __device__ __noinline__ void phase_ffn(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s, int pos, int l, int tslot,
                                        int ns, uint32_t par) {
+    #pragma unroll 1
     for (int i = threadIdx.x; i < a.dim; i += blockDim.x) s.x[i] = __fadd_rn(s.x[i], s.xp[i]);
     __syncthreads();
     if (role.ffn0 >= role.ffn1) return;
     if (GPT2 && a.layernorm) layernorm_exact(s.x, s.wf, s.wfb, a.dim, a.eps, s.xb, s.red);
-    else rmsnorm_exact(s.x, s.wf, a.dim, a.eps, s.xb, s.tmp, s.red);
-    trace(a, tslot, pos, l, 7);
+    else rmsnorm_exact(s.x, s.wf, a.dim, a.eps, s.xb, s.red);
+    trace<TRACE>(a, tslot, pos, l, 7);
     const int nf = role.ffn1 - role.ffn0;
     prepare(L.dt_up, s.xb, a.dim, s.prep);
-    trace(a, tslot, pos, l, 26);
+    trace<TRACE>(a, tslot, pos, l, 26);
     if (ns) stage_wait(a, s, par, pos, l);
-    trace(a, tslot, pos, l, 12);
+    trace<TRACE>(a, tslot, pos, l, 12);
     if (GPT2 && a.gelu) {                                                 // GPT-2: up only
         matvec_exact(L.dt_up, L.up, a.dim, role.ffn0, role.ffn1, s.prep, s.scratch, a.scratch_pairs, s.y, s.w, ns);
     } else if (!L.gate) {                                                 // up and gate packed per CTA: one pass
@@ -530,7 +533,7 @@ __device__ __noinline__ void phase_ffn(const DecodeArgs &a, const LayerDev &L, c
         if (L.dt_gate != L.dt_up) prepare(L.dt_gate, s.xb, a.dim, s.prep);
         matvec_exact(L.dt_gate, L.gate, a.dim, role.ffn0, role.ffn1, s.prep, s.scratch, a.scratch_pairs, s.y + nf * kTile);
     }
-    trace(a, tslot, pos, l, 13);
+    trace<TRACE>(a, tslot, pos, l, 13);
 }
 
 // The SiLU gate of phase C's up/gate results in s.y -> s.tmp (the caller scatters into xh); GPT2:
@@ -538,6 +541,7 @@ __device__ __noinline__ void phase_ffn(const DecodeArgs &a, const LayerDev &L, c
 template <bool GPT2>
 __device__ __noinline__ void ffn_gate(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s) {
     const int nf = role.ffn1 - role.ffn0, g0 = (a.sh.f_off + role.ffn0) * kTile, n = min((a.sh.f_off + role.ffn1) * kTile, a.ffn) - g0;
+    #pragma unroll 1
     for (int o = threadIdx.x; o < n; o += blockDim.x) {
         const float up = L.b_up ? __fadd_rn(s.y[o], __ldg(L.b_up + g0 + o)) : s.y[o];
         s.tmp[o] = GPT2 && a.gelu ? gelu_tanh(up) : silu_mul(up, s.y[nf * kTile + o], a.elist, a.eindex);
@@ -547,16 +551,18 @@ __device__ __noinline__ void ffn_gate(const DecodeArgs &a, const LayerDev &L, co
 
 // Phase D: this CTA's tiles of down over h -> s.y (the caller scatters into xd; ns tiles staged at
 // offset 0).
+template <bool TRACE>
 __device__ __noinline__ void phase_down(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s, int ns, uint32_t par, int pos,
                                         int l, int tslot) {
     prepare(L.dt_down, s.xh, a.ffn, s.prep);
-    trace(a, tslot, pos, l, 23);
+    trace<TRACE>(a, tslot, pos, l, 23);
     if (ns) stage_wait(a, s, par, pos, l);
-    trace(a, tslot, pos, l, 24);
+    trace<TRACE>(a, tslot, pos, l, 24);
     matvec_exact(L.dt_down, L.down, a.ffn, role.dn0, role.dn1, s.prep, s.scratch, a.scratch_pairs, s.y, s.w, ns);
-    trace(a, tslot, pos, l, 25);
+    trace<TRACE>(a, tslot, pos, l, 25);
     const int g0 = (a.sh.d_off + role.dn0) * kTile, n = min((a.sh.d_off + role.dn1) * kTile, a.dim) - g0;
     if (L.b_down) {
+        #pragma unroll 1
         for (int o = threadIdx.x; o < n; o += blockDim.x) s.y[o] = __fadd_rn(s.y[o], __ldg(L.b_down + g0 + o));
         __syncthreads();
     }
@@ -695,6 +701,7 @@ __device__ __noinline__ int sample_token(const SampleIn &in, float *xs, float *t
             for (int b0 = 0; b0 < V; b0 += stage_n) {
                 const int n = min(stage_n, V - b0);
                 __syncthreads();
+                #pragma unroll 1
                 for (int i = tid; i < n; i += nth) stage[i] = ld_cg_f32(in.probs + b0 + i);
                 __syncthreads();
                 if (tid == 0) {
@@ -757,7 +764,7 @@ __device__ __noinline__ int wait_word(const DecodeArgs &a, const uint32_t *p, ui
 // l3m_logits), this CTA's argmax -> hx.slots[cta] with an arrival on hx.count. host_stop: the
 // host's stop request (cluster 0, CTA 0 only). GPT2: the final LayerNorm.
 // staged, ns: the first ns of the CTA's tiles are resident in shared memory (helper CTAs).
-template <bool GPT2>
+template <bool GPT2, bool TRACE>
 __device__ __noinline__ void head_logits(const DecodeArgs &a, const Role &role, const Smem &s, int pos, int host_stop, int tslot,
                                          const uint8_t *staged = nullptr, int ns = 0) {
     const int cta = blockIdx.x, tid = threadIdx.x, nth = blockDim.x;
@@ -765,14 +772,15 @@ __device__ __noinline__ void head_logits(const DecodeArgs &a, const Role &role, 
     int best_i = -1;
     if (role.voc0 < role.voc1) {
         if (GPT2 && a.layernorm) layernorm_exact(s.x, s.wh, s.whb, a.dim, a.eps, s.xb, s.red);
-        else rmsnorm_exact(s.x, s.wh, a.dim, a.eps, s.xb, s.tmp, s.red);
-        trace(a, tslot, pos, a.n_layers, 3);
+        else rmsnorm_exact(s.x, s.wh, a.dim, a.eps, s.xb, s.red);
+        trace<TRACE>(a, tslot, pos, a.n_layers, 3);
         prepare(a.dt_head, s.xb, a.dim, s.prep);
-        trace(a, tslot, pos, a.n_layers, 4);
+        trace<TRACE>(a, tslot, pos, a.n_layers, 4);
         matvec_exact(a.dt_head, a.head, a.dim, role.voc0, role.voc1, s.prep, s.scratch, a.scratch_pairs, s.y, staged, ns);
-        trace(a, tslot, pos, a.n_layers, 5);
+        trace<TRACE>(a, tslot, pos, a.n_layers, 5);
         float *lg = a.logits + (size_t)pos * a.vocab;
         const int g0 = (a.sh.v_off + role.voc0) * kTile, n = min((a.sh.v_off + role.voc1) * kTile, a.vocab) - g0;
+        #pragma unroll 1
         for (int o = tid; o < n; o += nth) {
             const float v = s.y[o];
             lg[g0 + o] = v;
@@ -782,6 +790,7 @@ __device__ __noinline__ void head_logits(const DecodeArgs &a, const Role &role, 
             for (int t = 0; t < a.sh.n_gpus; t++) {                       // temperature sampling every GPU does
                 if (t == a.sh.gpu || (t != 0 && !a.sh.all_logits)) continue;
                 float *pl = a.sh.logits[t] + (size_t)pos * a.vocab + g0;
+                #pragma unroll 1
                 for (int o = tid; o < n; o += nth) pl[o] = s.y[o];
             }
             __threadfence_system();                                       // before the arrival that the vote follows
@@ -876,7 +885,7 @@ __device__ __noinline__ void gpu_vote(const DecodeArgs &a, const Smem &s, uint32
 template <bool GPT2>
 __device__ __noinline__ void head_helper(const DecodeArgs &a, const Role &role, const Smem &s, int cold) {
     stage_init(s);
-    const int nres = cold ? 0 : stage_issue(s, a.dt_head, a.head, a.dim, role.voc0, role.voc1, s.w, a.w_bytes);   // cold: read each time
+    const int nres = cold ? 0 : stage_issue(s, a.dt_head, a.head, a.dim, role.voc0, role.voc1, s.w, a.st_head);   // cold: read each time
     const size_t th = tile_bytes(a.dt_head, a.dim);
     const int rest0 = role.voc0 + nres;
     if (rest0 < role.voc1 && threadIdx.x == 0) prefetch_l2(a.head + rest0 * th, (size_t)(role.voc1 - rest0) * th);
@@ -885,8 +894,10 @@ __device__ __noinline__ void head_helper(const DecodeArgs &a, const Role &role, 
         if (wait_word(a, a.hx.flag, e, true, -1, kWaitHeadFlag) <= 0) break;
         const int pos = __float_as_int(ld_cg_f32(a.hx.x + a.dim));
         if ((a.dim & 3) == 0)
+            #pragma unroll 1
             for (int i = threadIdx.x * 4; i < a.dim; i += blockDim.x * 4) *(float4 *)(s.x + i) = __ldcg((const float4 *)(a.hx.x + i));
         else
+            #pragma unroll 1
             for (int i = threadIdx.x; i < a.dim; i += blockDim.x) s.x[i] = ld_cg_f32(a.hx.x + i);
         cp_async_wait_all();                                              // the final norm's weights
         if (!landed) {                                                    // the resident tiles (first position only)
@@ -894,20 +905,141 @@ __device__ __noinline__ void head_helper(const DecodeArgs &a, const Role &role, 
             landed = true;
         }
         __syncthreads();
-        head_logits<GPT2>(a, role, s, pos, 0, -1, s.w, nres);
+        head_logits<GPT2, false>(a, role, s, pos, 0, -1, s.w, nres);
         if (rest0 < role.voc1 && threadIdx.x == 0) prefetch_l2(a.head + rest0 * th, (size_t)(role.voc1 - rest0) * th);
     }
     if (!landed) stage_wait(a, s, 0, -1, -1, true);                       // no copy outlives the CTA
 }
 
-// One instance per model family and cache mode, so that neither costs the other registers or
-// branches: GPT2 (LayerNorm, learned positions, GELU: the GPT-2 family's layers), COLD (every weight
-// copy with an L2 evict-first policy).
+// The weight-copy and exchange state carried from layer to layer: ns tiles of the outstanding copy,
+// its mbarrier phase parity wpar, and the exchanges' phase parity xpar (one phase per layer).
+struct LayerState {
+    int ns;
+    uint32_t wpar, xpar;
+};
+
+// One layer of position pos on cluster 0 (phases Q, A, B, C, D and the five exchanges), one
+// out-of-line function so that the layer's code is one contiguous run.
+template <bool GPT2, bool TRACE>
+__device__ __noinline__ void run_layer(const DecodeArgs &a, const LayerDev *layers, int l, const Role &role, const Smem &s, int pos, bool last,
+                                       int tslot, LayerState &st) {
+    const int tid = threadIdx.x;
+    const bool multi = a.sh.n_gpus > 1;
+    int ns = st.ns;
+    uint32_t wpar = st.wpar, xpar = st.xpar;
+    const LayerDev &L = layers[l];
+    cp_async_wait_all();                                          // this layer's norm weights and RoPE row
+    __syncthreads();
+    trace<TRACE>(a, tslot, pos, l, 0);
+    if (l + 1 == a.n_layers) {
+        if (last && role.voc0 < role.voc1 && tid == kPrefetchThread) {
+            const size_t th = tile_bytes(a.dt_head, a.dim);
+            prefetch_l2(a.head + role.voc0 * th, (size_t)(role.voc1 - role.voc0) * th);
+        }
+    }
+    if (role.head0 >= 0 && role.qkv0 >= role.qkv1)               // K/V copies land during Q (else started by phase_qkv)
+        attend_prestage<true>(kcache(a, L, role.head0), vcache(a, L, role.head0), a.hd, a.vstride, pos, a.hd, s.kvbuf, s.vtbuf,
+                              a.attn_chunk);
+    // Each phase: its matvec, the copy of the next phase's tiles (the staging area is free from
+    // here on), then the exchange.
+    if (role.qkv0 < role.qkv1) phase_qkv<GPT2, TRACE>(a, L, role, s, ns, wpar, pos, l, tslot);   // Q
+    if (ns) wpar ^= 1;
+    ns = stage_issue(s, L.dt_wo, L.wo, a.dim, role.wo0, role.wo1, s.w + a.w_extra, L.st_wo, a.cold);
+    trace<TRACE>(a, tslot, pos, l, 27);
+    if (role.qkv0 < role.qkv1) {
+        const int g0 = role.qkv0 * kTile, n = min(role.qkv1 * kTile, a.sh.n_qkv_g) - g0;
+        if (a.async_x) scatter_tx(s.y, s.xq, g0, n, s.xbar);
+        else scatter(s.y, s.xq, g0, n);
+    }
+    trace<TRACE>(a, tslot, pos, l, 1);
+    if (a.async_x) xwait(a, s, 0, xpar, xbytes(a, -1), pos, l);   // 1: qkv (this GPU's heads)
+    else cluster_sync();
+    trace<TRACE>(a, tslot, pos, l, 2);
+    const uint32_t step = layer_step(a, pos, l);
+    for (int h = role.head0; h >= 0 && h < a.sh.head_lo + a.sh.n_heads_g; h += kClusterCtas) {   // A
+        phase_attention<TRACE>(a, L, s, h, pos, h == role.head0, l, tslot);
+        if (multi) peer_send(a, kXAttn, s.att, h * a.hd, a.hd, step);
+    }
+    trace<TRACE>(a, tslot, pos, l, 3);
+    if (a.async_x) xwait(a, s, 1, xpar, xbytes(a, kXAttn), pos, l);     // 2: attn
+    else cluster_sync();
+    if (multi) peer_recv(a, kXAttn, s.xa, step, pos, l);
+    trace<TRACE>(a, tslot, pos, l, 4);
+    if (role.wo0 < role.wo1) phase_wo<TRACE>(a, L, role, s, ns, wpar, pos, l, tslot);   // B
+    if (ns) wpar ^= 1;
+    if (!L.gate && !(GPT2 && a.gelu)) ns = stage_issue(s, L.dt_up, L.up, a.dim, 2 * role.ffn0, 2 * role.ffn1, s.w, L.st_up, a.cold);
+    else ns = stage_issue(s, L.dt_up, L.up, a.dim, role.ffn0, role.ffn1, s.w, L.st_up, a.cold);
+    trace<TRACE>(a, tslot, pos, l, 28);
+    if (role.wo0 < role.wo1) {
+        const int g0 = (a.sh.d_off + role.wo0) * kTile, n = min((a.sh.d_off + role.wo1) * kTile, a.dim) - g0;
+        if (a.async_x) scatter_tx(s.y, s.xp, g0, n, s.xbar + 2);
+        else scatter(s.y, s.xp, g0, n);
+        if (multi) peer_send(a, kXProj, s.y, g0, n, step);
+    }
+    trace<TRACE>(a, tslot, pos, l, 5);
+    if (a.async_x) xwait(a, s, 2, xpar, xbytes(a, kXProj), pos, l);     // 3: proj
+    else cluster_sync();
+    if (multi) peer_recv(a, kXProj, s.xp, step, pos, l);
+    trace<TRACE>(a, tslot, pos, l, 6);
+    phase_ffn<GPT2, TRACE>(a, L, role, s, pos, l, tslot, ns, wpar);      // C
+    if (ns) wpar ^= 1;
+    ns = stage_issue(s, L.dt_down, L.down, a.ffn, role.dn0, role.dn1, s.w, L.st_down, a.cold);
+    trace<TRACE>(a, tslot, pos, l, 29);
+    if (role.ffn0 < role.ffn1) {
+        ffn_gate<GPT2>(a, L, role, s);
+        const int g0 = (a.sh.f_off + role.ffn0) * kTile, n = min((a.sh.f_off + role.ffn1) * kTile, a.ffn) - g0;
+        if (a.async_x) scatter_tx(s.tmp, s.xh, g0, n, s.xbar + 3);
+        else scatter(s.tmp, s.xh, g0, n);
+        if (multi) peer_send(a, kXH, s.tmp, g0, n, step);
+    }
+    // The next layer's norm weights (and the next position's RoPE row) while the rest runs.
+    if (l + 1 < a.n_layers) stage_vectors<GPT2>(a, layers[l + 1], role, s, pos);
+    else stage_vectors<GPT2>(a, layers[0], role, s, pos + 1);
+    trace<TRACE>(a, tslot, pos, l, 8);
+    if (a.async_x) xwait(a, s, 3, xpar, xbytes(a, kXH), pos, l);     // 4: h
+    else cluster_sync();
+    if (multi) peer_recv(a, kXH, s.xh, step, pos, l);
+    trace<TRACE>(a, tslot, pos, l, 9);
+    if (role.dn0 < role.dn1) phase_down<TRACE>(a, L, role, s, ns, wpar, pos, l, tslot);   // D
+    if (ns) wpar ^= 1;
+    {
+        const LayerDev &N = layers[l + 1 < a.n_layers ? l + 1 : 0];
+        ns = stage_issue(s, N.dt_qkv, N.qkv, a.dim, role.qkv0, role.qkv1, s.w + a.w_extra, N.st_qkv, a.cold);
+    }
+    trace<TRACE>(a, tslot, pos, l, 30);
+    if (role.dn0 < role.dn1) {
+        const int g0 = (a.sh.d_off + role.dn0) * kTile, n = min((a.sh.d_off + role.dn1) * kTile, a.dim) - g0;
+        if (a.async_x) scatter_tx(s.y, s.xd, g0, n, s.xbar + 4);
+        else scatter(s.y, s.xd, g0, n);
+        if (multi) peer_send(a, kXDown, s.y, g0, n, step);
+    }
+    trace<TRACE>(a, tslot, pos, l, 10);
+    if (a.async_x) {                                              // 5: down
+        xwait(a, s, 4, xpar, xbytes(a, kXDown), pos, l);
+        xpar ^= 1u;
+    } else {
+        cluster_sync();
+    }
+    if (multi) peer_recv(a, kXDown, s.xd, step, pos, l);
+#pragma unroll 1
+    for (int i = tid; i < a.dim; i += blockDim.x) s.x[i] = __fadd_rn(s.x[i], s.xd[i]);
+    __syncthreads();
+    trace<TRACE>(a, tslot, pos, l, 11);
+    st.ns = ns;
+    st.wpar = wpar;
+    st.xpar = xpar;
+}
+
+// One instance per model family, so that neither costs the other registers or branches: GPT2
+// (LayerNorm, learned positions, GELU: the GPT-2 family's layers); and per TRACE (the phase time
+// stamps), so that the untraced instance carries none of their code. The layer loop's code has to
+// stay inside the SM's instruction cache (between 96 and 128 KB on a B200: past that, every layer
+// fetches its code again from L2), which is why thread-strided loops are not unrolled.
 // The cluster shape is part of the kernel (__cluster_dims__), not only of the launch: a launch
 // attribute alone is dropped by some launch paths (a profiler's replay ran this kernel as clusters of
 // one CTA, which the entry check reports as kErrShape), while a compile-time shape holds for every
 // launch of the function.
-template <bool GPT2, bool COLD>
+template <bool GPT2, bool TRACE>
 __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeArgs *__restrict__ ap) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     // The arguments, this CTA's role, every layer's pointers and the carved shared-memory pointers
@@ -946,6 +1078,7 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
     {
         const uint32_t *src = (const uint32_t *)ap->layers;
         uint32_t *dst = (uint32_t *)(smem_raw + a.sm_layers);
+        #pragma unroll 1
         for (int i = threadIdx.x; i < a.n_layers * (int)(sizeof(LayerDev) / 4); i += blockDim.x) dst[i] = src[i];
     }
     const LayerDev *layers = (const LayerDev *)(smem_raw + a.sm_layers);
@@ -966,13 +1099,12 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
     }
     if (cta >= kClusterCtas) {                                            // the other clusters: head tiles only
         cp_async_commit();
-        head_helper<GPT2>(a, role, s, COLD);
+        head_helper<GPT2>(a, role, s, a.cold);
         cp_async_wait_all();
         return;
     }
     stage_vectors<GPT2>(a, layers[0], role, s, 0);
     stage_init(s);
-    uint32_t xpar = 0;                                                    // the exchanges' phase parity (one phase per layer)
     if (a.async_x && tid == 0) {
         const uint32_t bytes[5] = {xbytes(a, -1), xbytes(a, kXAttn), xbytes(a, kXProj), xbytes(a, kXH), xbytes(a, kXDown)};
         for (int k = 0; k < 5; k++) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(s.xbar + k)) : "memory");
@@ -981,10 +1113,9 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
             asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(s.xbar + k)), "r"(bytes[k]) : "memory");
     }
     // The staged-weight schedule: qkv and wo into [w_extra, w_bytes) (the attention buffers are live
-    // from the layer top to the end of attention), up/gate and down from offset 0. ns: tiles of the
-    // outstanding copy; wpar: its mbarrier phase parity.
-    uint32_t wpar = 0;
-    int ns = stage_issue(s, layers[0].dt_qkv, layers[0].qkv, a.dim, role.qkv0, role.qkv1, s.w + a.w_extra, a.w_bytes - a.w_extra, COLD);
+    // from the layer top to the end of attention), up/gate and down from offset 0.
+    LayerState st{0, 0, 0};
+    st.ns = stage_issue(s, layers[0].dt_qkv, layers[0].qkv, a.dim, role.qkv0, role.qkv1, s.w + a.w_extra, layers[0].st_qkv, a.cold);
     cluster_sync();                                                       // every CTA of the cluster has started
 
     for (pos = 0;; pos++) {
@@ -992,119 +1123,22 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
         if (pos < a.n_prompt) tok = a.prompt[pos];
         const bool stop_after = last && (n_gen >= a.max_new || pos + 1 >= a.ctx);   // reference engine.c:322, 352
         embed_row<GPT2>(a, tok, pos, s.x);
-        for (int l = 0; l < a.n_layers; l++) {
-            const LayerDev &L = layers[l];
-            cp_async_wait_all();                                          // this layer's norm weights and RoPE row
-            __syncthreads();
-            trace(a, tslot, pos, l, 0);
-            if (l + 1 == a.n_layers) {
-                if (last && role.voc0 < role.voc1 && tid == kPrefetchThread) {
-                    const size_t th = tile_bytes(a.dt_head, a.dim);
-                    prefetch_l2(a.head + role.voc0 * th, (size_t)(role.voc1 - role.voc0) * th);
-                }
-            }
-            if (role.head0 >= 0 && role.qkv0 >= role.qkv1)               // K/V copies land during Q (else started by phase_qkv)
-                attend_prestage<true>(kcache(a, L, role.head0), vcache(a, L, role.head0), a.hd, a.vstride, pos, a.hd, s.kvbuf, s.vtbuf,
-                                      a.attn_chunk);
-            // Each phase: its matvec, the copy of the next phase's tiles (the staging area is free from
-            // here on), then the exchange.
-            if (role.qkv0 < role.qkv1) phase_qkv<GPT2>(a, L, role, s, ns, wpar, pos, l, tslot);   // Q
-            if (ns) wpar ^= 1;
-            ns = stage_issue(s, L.dt_wo, L.wo, a.dim, role.wo0, role.wo1, s.w + a.w_extra, a.w_bytes - a.w_extra, COLD);
-            trace(a, tslot, pos, l, 27);
-            if (role.qkv0 < role.qkv1) {
-                const int g0 = role.qkv0 * kTile, n = min(role.qkv1 * kTile, a.sh.n_qkv_g) - g0;
-                if (a.async_x) scatter_tx(s.y, s.xq, g0, n, s.xbar);
-                else scatter(s.y, s.xq, g0, n);
-            }
-            trace(a, tslot, pos, l, 1);
-            if (a.async_x) xwait(a, s, 0, xpar, xbytes(a, -1), pos, l);   // 1: qkv (this GPU's heads)
-            else cluster_sync();
-            trace(a, tslot, pos, l, 2);
-            const uint32_t step = layer_step(a, pos, l);
-            for (int h = role.head0; h >= 0 && h < a.sh.head_lo + a.sh.n_heads_g; h += kClusterCtas) {   // A
-                phase_attention(a, L, s, h, pos, h == role.head0, l, tslot);
-                if (multi) peer_send(a, kXAttn, s.att, h * a.hd, a.hd, step);
-            }
-            trace(a, tslot, pos, l, 3);
-            if (a.async_x) xwait(a, s, 1, xpar, xbytes(a, kXAttn), pos, l);     // 2: attn
-            else cluster_sync();
-            if (multi) peer_recv(a, kXAttn, s.xa, step, pos, l);
-            trace(a, tslot, pos, l, 4);
-            if (role.wo0 < role.wo1) phase_wo(a, L, role, s, ns, wpar, pos, l, tslot);   // B
-            if (ns) wpar ^= 1;
-            if (!L.gate && !(GPT2 && a.gelu)) ns = stage_issue(s, L.dt_up, L.up, a.dim, 2 * role.ffn0, 2 * role.ffn1, s.w, a.w_bytes, COLD);
-            else ns = stage_issue(s, L.dt_up, L.up, a.dim, role.ffn0, role.ffn1, s.w, a.w_bytes, COLD);
-            trace(a, tslot, pos, l, 28);
-            if (role.wo0 < role.wo1) {
-                const int g0 = (a.sh.d_off + role.wo0) * kTile, n = min((a.sh.d_off + role.wo1) * kTile, a.dim) - g0;
-                if (a.async_x) scatter_tx(s.y, s.xp, g0, n, s.xbar + 2);
-                else scatter(s.y, s.xp, g0, n);
-                if (multi) peer_send(a, kXProj, s.y, g0, n, step);
-            }
-            trace(a, tslot, pos, l, 5);
-            if (a.async_x) xwait(a, s, 2, xpar, xbytes(a, kXProj), pos, l);     // 3: proj
-            else cluster_sync();
-            if (multi) peer_recv(a, kXProj, s.xp, step, pos, l);
-            trace(a, tslot, pos, l, 6);
-            phase_ffn<GPT2>(a, L, role, s, pos, l, tslot, ns, wpar);      // C
-            if (ns) wpar ^= 1;
-            ns = stage_issue(s, L.dt_down, L.down, a.ffn, role.dn0, role.dn1, s.w, a.w_bytes, COLD);
-            trace(a, tslot, pos, l, 29);
-            if (role.ffn0 < role.ffn1) {
-                ffn_gate<GPT2>(a, L, role, s);
-                const int g0 = (a.sh.f_off + role.ffn0) * kTile, n = min((a.sh.f_off + role.ffn1) * kTile, a.ffn) - g0;
-                if (a.async_x) scatter_tx(s.tmp, s.xh, g0, n, s.xbar + 3);
-                else scatter(s.tmp, s.xh, g0, n);
-                if (multi) peer_send(a, kXH, s.tmp, g0, n, step);
-            }
-            // The next layer's norm weights (and the next position's RoPE row) while the rest runs.
-            if (l + 1 < a.n_layers) stage_vectors<GPT2>(a, layers[l + 1], role, s, pos);
-            else stage_vectors<GPT2>(a, layers[0], role, s, pos + 1);
-            trace(a, tslot, pos, l, 8);
-            if (a.async_x) xwait(a, s, 3, xpar, xbytes(a, kXH), pos, l);     // 4: h
-            else cluster_sync();
-            if (multi) peer_recv(a, kXH, s.xh, step, pos, l);
-            trace(a, tslot, pos, l, 9);
-            if (role.dn0 < role.dn1) phase_down(a, L, role, s, ns, wpar, pos, l, tslot);   // D
-            if (ns) wpar ^= 1;
-            {
-                const LayerDev &N = layers[l + 1 < a.n_layers ? l + 1 : 0];
-                ns = stage_issue(s, N.dt_qkv, N.qkv, a.dim, role.qkv0, role.qkv1, s.w + a.w_extra, a.w_bytes - a.w_extra, COLD);
-            }
-            trace(a, tslot, pos, l, 30);
-            if (role.dn0 < role.dn1) {
-                const int g0 = (a.sh.d_off + role.dn0) * kTile, n = min((a.sh.d_off + role.dn1) * kTile, a.dim) - g0;
-                if (a.async_x) scatter_tx(s.y, s.xd, g0, n, s.xbar + 4);
-                else scatter(s.y, s.xd, g0, n);
-                if (multi) peer_send(a, kXDown, s.y, g0, n, step);
-            }
-            trace(a, tslot, pos, l, 10);
-            if (a.async_x) {                                              // 5: down
-                xwait(a, s, 4, xpar, xbytes(a, kXDown), pos, l);
-                xpar ^= 1u;
-            } else {
-                cluster_sync();
-            }
-            if (multi) peer_recv(a, kXDown, s.xd, step, pos, l);
-            for (int i = tid; i < a.dim; i += blockDim.x) s.x[i] = __fadd_rn(s.x[i], s.xd[i]);
-            __syncthreads();
-            trace(a, tslot, pos, l, 11);
-        }
+        for (int l = 0; l < a.n_layers; l++) run_layer<GPT2, TRACE>(a, layers, l, role, s, pos, last, tslot, st);
         if (!last) continue;                                              // the next position starts from its embedding
         ++tcount;
         // Publish x to every CTA of the launch (cluster 0's copies are identical), then this CTA's tiles.
         if (cta == 0 && a.grid > kClusterCtas) {
+            #pragma unroll 1
             for (int i = tid; i < a.dim; i += blockDim.x) a.hx.x[i] = s.x[i];
             if (tid == 0) a.hx.x[a.dim] = __int_as_float(pos);
             __syncthreads();
             if (tid == 0) asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.hx.flag), "r"(tcount) : "memory");
         }
-        trace(a, tslot, pos, a.n_layers, 0);
+        trace<TRACE>(a, tslot, pos, a.n_layers, 0);
         int host_stop = 0;
         if (cta == 0 && tid == 0) host_stop = ld_relaxed_sys_i32((const int *)&a.ctrl->stop_request);
-        head_logits<GPT2>(a, role, s, pos, host_stop, tslot);
-        trace(a, tslot, pos, a.n_layers, 1);
+        head_logits<GPT2, TRACE>(a, role, s, pos, host_stop, tslot);
+        trace<TRACE>(a, tslot, pos, a.n_layers, 1);
         // One cluster: every CTA sends (max, index, host stop, no abort seen) to every CTA's xt[4 + 4 cta],
         // and after the barrier each reduces the same 16 slots in CTA order. Several clusters: CTA 0
         // waits for every CTA's (max, index) in global memory (so every slice of the logits is written,
@@ -1117,6 +1151,7 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
         } else if (cta == 0) {
             const int r = wait_word(a, a.hx.count, tcount * (uint32_t)a.grid, false, pos, kWaitHeadCount);
             float *sl = s.tmp + 4;                                        // every slot at once, then a serial scan
+            #pragma unroll 1
             for (int i = tid; i < 3 * a.grid; i += blockDim.x) sl[i] = ld_cg_f32(a.hx.slots + i);
             __syncthreads();
             if (tid == 0) {
@@ -1160,7 +1195,7 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
             ok = false;
             break;
         }
-        trace(a, tslot, pos, a.n_layers, 2);
+        trace<TRACE>(a, tslot, pos, a.n_layers, 2);
         if (stop_after) break;                                            // logits kept, nothing sampled (uniform)
         if (a.temp > 0.0f) {                                              // every CTA of cluster 0, in step
             const SampleIn in{a.logits + (size_t)pos * a.vocab, a.probs, a.vocab, a.temp, gmax_all, a.elist, a.eindex};
@@ -1179,7 +1214,7 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
         // reaches after reading it here.
     }
     cp_async_wait_all();                                                  // no copy outlives the CTA
-    if (ns) stage_wait(a, s, wpar, pos, -1, true);
+    if (st.ns) stage_wait(a, s, st.wpar, pos, -1, true);
     cluster_sync();                                                       // no CTA leaves while others may write its memory
     if (cta == 0 && tid == 0) {
         asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.hx.flag), "r"(kHeadDone) : "memory");   // the helpers stop
@@ -1202,6 +1237,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) sample_kernel(const float *
     const int rank = (int)cg::this_cluster().block_rank(), tid = threadIdx.x;
     const int lo = (int)((long long)rank * vocab / kClusterCtas), hi = (int)((long long)(rank + 1) * vocab / kClusterCtas);
     float m = -INFINITY;
+    #pragma unroll 1
     for (int i = lo + tid; i < hi; i += blockDim.x) m = fmaxf(m, ld_cg_f32(logits + i));   // a NaN never wins
     for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if ((tid & 31) == 0) red[tid >> 5] = m;
@@ -1248,11 +1284,11 @@ cudaLaunchConfig_t cluster_config(int grid, int smem_bytes, cudaLaunchAttribute 
 
 using DecodeFn = void (*)(const l3m::DecodeArgs *);
 
-// The kernel instance for a's model family and cache mode.
+// The kernel instance for a's model family, traced or not.
 DecodeFn decode_instance(const l3m::DecodeArgs &a) {
-    const bool gpt2 = a.layernorm || a.gelu || a.pos_embed != nullptr;
-    if (gpt2) return a.cold ? l3m::decode_kernel<true, true> : l3m::decode_kernel<true, false>;
-    return a.cold ? l3m::decode_kernel<false, true> : l3m::decode_kernel<false, false>;
+    const bool gpt2 = a.layernorm || a.gelu || a.pos_embed != nullptr, traced = a.trace != nullptr;
+    if (gpt2) return traced ? l3m::decode_kernel<true, true> : l3m::decode_kernel<true, false>;
+    return traced ? l3m::decode_kernel<false, true> : l3m::decode_kernel<false, false>;
 }
 
 constexpr DecodeFn kDecodeInstances[4] = {l3m::decode_kernel<false, false>, l3m::decode_kernel<false, true>,
@@ -1268,6 +1304,10 @@ cudaError_t set_attributes(DecodeFn fn, int smem_bytes) {
 
 // a_dev: the arguments, already in device memory.
 extern "C" int l3m_decode_launch(const l3m::DecodeArgs *a, const l3m::DecodeArgs *a_dev, void *stream) {
+    if (!a_dev || !a->layers || !a->roles || !a->ctrl || !a->hx.abort_flag || !a->logits || !a->tokens) {   // never launch on an unset table
+        fprintf(stderr, "l3m: decode launch: a device table is not set\n");
+        return -1;
+    }
     const DecodeFn fn = decode_instance(*a);
     cudaError_t e = set_attributes(fn, a->smem_bytes);
     if (e == cudaSuccess) {

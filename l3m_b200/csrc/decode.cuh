@@ -12,6 +12,7 @@ struct alignas(16) LayerDev {
     const float *bq, *bk, *bv, *bo, *b_up, *b_down;   // NULL when absent
     uint16_t *kc, *vc;                  // K [n_kv][ctx][hd], V [n_kv][hd][vstride] bf16
     int dt_qkv, dt_wo, dt_gate, dt_up, dt_down;
+    int st_qkv, st_wo, st_up, st_down;  // how many tiles of each fit in its part of the staging area
 };
 
 // One CTA's share of every phase (output tiles are 16 rows; ranges are [lo, hi)). Query heads
@@ -122,17 +123,17 @@ struct DecodeArgs {
     int sm_layers;                      // a copy of layers[0 .. n_layers)
     int sm_xq, sm_xa, sm_xp, sm_xh, sm_xd, sm_xt;   // exchanged vectors: qkv, attn, proj, h, down; xt: the sampled token
                                                     // (next, stop, ok) and, one-cluster launch, each CTA c's slot at 4 + 4c
-    // Weight staging area (quantised tiles of the next matvec phase, copied in by cp.async.bulk):
+    // Weight staging area (the tiles of the next matvec phase, copied in by cp.async.bulk):
     // sm_w .. sm_w + w_bytes; its first w_extra bytes overlap the attention buffers (kvbuf, vt), so
     // the phases around attention (qkv, wo) use only [w_extra, w_bytes). sm_wbar: its mbarrier.
     int sm_w, w_bytes, w_extra, sm_wbar;
+    int st_head;                        // head tiles that fit in the whole staging area (helper CTAs)
     // Exchanges 1-5 of a layer through st.async + per-CTA mbarriers (sm_xbar: 5 of them) instead of
     // cluster barriers; set when every CTA of the cluster produces qkv rows, which orders every
     // buffer's next write after all its reads (see decode.cu).
     int async_x, sm_xbar;
     int cold;                           // reference --cold (engine.c:330-338 flushes the weights after each token):
-                                        // the launch takes the kernel's COLD instance, whose weight copies carry an
-                                        // L2 evict-first policy
+                                        // weight copies carry an L2 evict-first policy
     int vstride;                        // V cache: element i of position t at vc[i * vstride + t]
     int scratch_pairs, smem_bytes, attn_chunk;
 };

@@ -390,8 +390,6 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
         d.kc = g.kv + (size_t)l * (k_per + v_per);
         d.vc = d.kc + k_per;
     }
-    if (!cuda_ok(cudaMalloc(&g.layers, sizeof(l3m::LayerDev) * L), "layers")) return false;
-    cudaMemcpy(g.layers, layers.data(), sizeof(l3m::LayerDev) * L, cudaMemcpyHostToDevice);
 
     auto rope = rope_table(m->ctx, hd, m->f.h->rope_theta);
     if (!cuda_ok(cudaMalloc(&g.rope, rope.size() * sizeof(float2)), "rope")) return false;
@@ -444,7 +442,6 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
             h.len[l3m::kXH][r] = std::min(o2.f_hi * L3M_TILE, ffn) - o2.f_lo * L3M_TILE;
         }
     }
-    a.layers = g.layers;
     a.head = g.arena + off_head; a.dt_head = dt_head;
     a.embed = g.arena + off_embed; a.dt_embed = dt_embed; a.embed_row_bytes = (long long)emb_row;
     a.norm = A(off_norm);
@@ -533,6 +530,19 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     }
     a.w_bytes = (budget - a.sm_w) & ~127;
     a.smem_bytes = a.sm_w + a.w_bytes;
+    // How many tiles of each matrix fit in its part of the staging area (qkv and wo: the part past the
+    // attention buffers).
+    auto fit = [&](int dt, int k, int bytes) { return bytes / (int)l3m::staged_stride(dt, k); };
+    for (l3m::LayerDev &d : layers) {
+        d.st_qkv = fit(d.dt_qkv, dim, a.w_bytes - a.w_extra);
+        d.st_wo = fit(d.dt_wo, dim, a.w_bytes - a.w_extra);
+        d.st_up = fit(d.dt_up, dim, a.w_bytes);
+        d.st_down = fit(d.dt_down, ffn, a.w_bytes);
+    }
+    a.st_head = fit(dt_head, dim, a.w_bytes);
+    if (!cuda_ok(cudaMalloc(&g.layers, sizeof(l3m::LayerDev) * L), "layers")) return false;
+    cudaMemcpy(g.layers, layers.data(), sizeof(l3m::LayerDev) * L, cudaMemcpyHostToDevice);
+    a.layers = g.layers;
     if (o.verbose)
         fprintf(stderr, "l3m: shared memory %d B per CTA: vectors %d, scratch %d pairs, staging %d (attention buffers %d)\n", a.smem_bytes,
                 a.sm_scratch, a.scratch_pairs, a.w_bytes, a.w_extra);
@@ -544,8 +554,7 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     a.grid = GT;
     // The helper clusters keep their head tiles in shared memory (decode.cu head_helper): when all of
     // them fit there, cluster 0 takes none and goes straight from the last layer to the token vote.
-    const int resident = a.w_bytes / (int)l3m::staged_stride(dt_head, dim);
-    const bool helpers_only = GT > G && !m->cold && (long long)resident * (GT - G) >= Tv;
+    const bool helpers_only = GT > G && !m->cold && (long long)a.st_head * (GT - G) >= Tv;
     a.async_x = !getenv("L3M_CLUSTER_BARRIERS");                        // every CTA of cluster 0 must produce qkv rows
     {
         std::vector<l3m::Role> rs0 = make_roles(GT, helpers_only);
@@ -881,7 +890,10 @@ L3M_API int l3m_generate(l3m_model *m, const int32_t *prompt, int n_prompt, int 
                 }
             }
             if (done) break;
-            if (cudaEventQuery(g.ev1) == cudaSuccess && !m->ctrl->done) break;   // the kernel ended without finishing
+            // The kernel ended without finishing its loop, or failed (a CUDA error, reported below by
+            // the stream synchronisation): stop polling either way.
+            const cudaError_t q = cudaEventQuery(g.ev1);
+            if (q != cudaErrorNotReady && !m->ctrl->done) break;
             _mm_pause();
         }
     }

@@ -50,13 +50,16 @@ struct Prep {
 static __device__ __noinline__ void prepare(int dtype, const float *x, int n, const Prep p) {
     const int tid = threadIdx.x, nth = blockDim.x;
     if (dtype == DT_F32) {
+        #pragma unroll 1
         for (int i = tid; i < n; i += nth) p.xf[i] = x[i];
     } else if (dtype == DT_BF16) {
+        #pragma unroll 1
         for (int i = tid; i < n; i += nth) p.xf[i] = l3m_bf16_to_f32(l3m_f32_to_bf16(x[i]));
     } else {
         // 8 threads per 32-input block, 4 inputs each (x 16-byte aligned in shared memory); a warp takes
         // 4 blocks per step and every lane of it runs every step, so the shuffles always see the whole warp.
         const int j = tid & 7, sub = (tid & 31) >> 3, nblk = n / kQB;
+        #pragma unroll 1
         for (int b0 = (tid >> 5) * 4; b0 < nblk; b0 += (nth >> 5) * 4) {
             const int b = b0 + sub;
             const bool ok = b < nblk;
@@ -90,8 +93,10 @@ static __device__ __noinline__ void prepare(int dtype, const float *x, int n, co
 // commits, then waits with cp_async_wait_all + __syncthreads), else plain loads.
 __device__ __forceinline__ void stage_f32(float *dst, const float *src, int n) {
     if ((n & 3) == 0 && ((uintptr_t)src & 15) == 0 && ((uintptr_t)dst & 15) == 0) {
+        #pragma unroll 1
         for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4) cp_async16(dst + i, src + i);
     } else {
+        #pragma unroll 1
         for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = __ldg(src + i);
     }
 }
@@ -228,6 +233,7 @@ __device__ void qmatvec(const uint8_t *tiles, const uint8_t *tilesB, int ntA, in
         // item i = b * m4 + quad; this thread starts at i = tid and steps by nth
         int b = tid / m4, qd = tid - b * m4;
         const int db = nth / m4, dq = nth - db * m4;
+        #pragma unroll 1
         for (int i = tid; i < items; i += kQU * nth) {
             QLoad4 q[kQU];
             int bs[kQU], qs[kQU];
@@ -261,6 +267,7 @@ __device__ void qmatvec(const uint8_t *tiles, const uint8_t *tilesB, int ntA, in
             }
         }
         __syncthreads();
+        #pragma unroll 1
         for (int oo = tid; oo < m; oo += nth) {
             const float2 *r = scratch + oo;
             float acc = 0.0f;
@@ -291,39 +298,41 @@ __device__ __forceinline__ float4 lds_f4(uint32_t a) {
 
 // One output's bf16 chain over a tile staged in shared memory (the reference's order, products exact
 // inside each fma): word q of the output at wa + 64 q holds inputs 2q (low half) and 2q + 1; x (fp32)
-// at xa. 16 inputs per step, the next step's loads in flight during this step's 16 fmas.
+// at xa. 32 inputs per iteration in two halves, one half's loads in flight while the other computes.
+__device__ __forceinline__ void ld8w(uint32_t (&w)[8], float4 (&x)[4], uint32_t wa, uint32_t xa, int q) {
+#pragma unroll
+    for (int j = 0; j < 8; j++) w[j] = lds_u32(wa + 64 * (q + j));
+#pragma unroll
+    for (int j = 0; j < 4; j++) x[j] = lds_f4(xa + 8 * q + 16 * j);
+}
+__device__ __forceinline__ float fma8w(float acc, const uint32_t (&w)[8], const float4 (&x)[4]) {
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        acc = __fmaf_rn(l3m_bits_f32(w[2 * j] << 16), x[j].x, acc);
+        acc = __fmaf_rn(l3m_bits_f32(w[2 * j] & 0xFFFF0000u), x[j].y, acc);
+        acc = __fmaf_rn(l3m_bits_f32(w[2 * j + 1] << 16), x[j].z, acc);
+        acc = __fmaf_rn(l3m_bits_f32(w[2 * j + 1] & 0xFFFF0000u), x[j].w, acc);
+    }
+    return acc;
+}
 __device__ __forceinline__ float chain_bf16_shared(uint32_t wa, uint32_t xa, int k) {
-    const int nw = k >> 1;
+    const int nw = k >> 1, n16 = nw & ~15;
     float acc = 0.0f;
     int q = 0;
-    if (nw >= 8) {
-        uint32_t w[8];
-        float4 x[4];
-#pragma unroll
-        for (int j = 0; j < 8; j++) w[j] = lds_u32(wa + 64 * j);
-#pragma unroll
-        for (int j = 0; j < 4; j++) x[j] = lds_f4(xa + 16 * j);
-        for (; q + 8 <= nw; q += 8) {
-            const int qn = q + 16 <= nw ? q + 8 : q;
-            uint32_t wn[8];
-            float4 xn[4];
-#pragma unroll
-            for (int j = 0; j < 8; j++) wn[j] = lds_u32(wa + 64 * (qn + j));
-#pragma unroll
-            for (int j = 0; j < 4; j++) xn[j] = lds_f4(xa + 8 * qn + 16 * j);
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                acc = __fmaf_rn(l3m_bits_f32(w[2 * j] << 16), x[j].x, acc);
-                acc = __fmaf_rn(l3m_bits_f32(w[2 * j] & 0xFFFF0000u), x[j].y, acc);
-                acc = __fmaf_rn(l3m_bits_f32(w[2 * j + 1] << 16), x[j].z, acc);
-                acc = __fmaf_rn(l3m_bits_f32(w[2 * j + 1] & 0xFFFF0000u), x[j].w, acc);
-            }
-#pragma unroll
-            for (int j = 0; j < 8; j++) w[j] = wn[j];
-#pragma unroll
-            for (int j = 0; j < 4; j++) x[j] = xn[j];
+    if (n16) {
+        uint32_t wA[8], wB[8];
+        float4 xA[4], xB[4];
+        ld8w(wA, xA, wa, xa, 0);
+#pragma unroll 1
+        for (; q < n16; q += 16) {
+            ld8w(wB, xB, wa, xa, q + 8);
+            acc = fma8w(acc, wA, xA);
+            const int qn = q + 16 < n16 ? q + 16 : q;
+            ld8w(wA, xA, wa, xa, qn);
+            acc = fma8w(acc, wB, xB);
         }
     }
+#pragma unroll 1
     for (; q < nw; q++) {
         const uint32_t v = lds_u32(wa + 64 * q);
         acc = __fmaf_rn(l3m_bits_f32(v << 16), lds_f32(xa + 8 * q), acc);
@@ -333,71 +342,74 @@ __device__ __forceinline__ float chain_bf16_shared(uint32_t wa, uint32_t xa, int
 }
 
 // The same for an f32 tile (input i of the output at wa + 64 i): rounded products added up to
-// split, fmas after (the reference build's chain).
+// split, fmas after (the reference build's chain); 16 inputs per iteration in two halves.
+__device__ __forceinline__ void ld8f(float (&w)[8], float4 (&x)[2], uint32_t wa, uint32_t xa, int i) {
+#pragma unroll
+    for (int j = 0; j < 8; j++) w[j] = lds_f32(wa + 64 * (i + j));
+    x[0] = lds_f4(xa + 4 * i);
+    x[1] = lds_f4(xa + 4 * i + 16);
+}
+__device__ __forceinline__ float add8f(float acc, const float (&w)[8], const float4 (&x)[2]) {
+    const float xv[8] = {x[0].x, x[0].y, x[0].z, x[0].w, x[1].x, x[1].y, x[1].z, x[1].w};
+#pragma unroll
+    for (int j = 0; j < 8; j++) acc = __fadd_rn(acc, __fmul_rn(w[j], xv[j]));
+    return acc;
+}
 __device__ __forceinline__ float chain_f32_shared(uint32_t wa, uint32_t xa, int k, int split) {
     float acc = 0.0f;
     int i = 0;
-    if (split >= 8) {
-        float w[8];
-        float4 x[2];
-#pragma unroll
-        for (int j = 0; j < 8; j++) w[j] = lds_f32(wa + 64 * j);
-        x[0] = lds_f4(xa);
-        x[1] = lds_f4(xa + 16);
-        for (; i + 8 <= split; i += 8) {
-            const int in = i + 16 <= split ? i + 8 : i;
-            float wn[8];
-            float4 xn[2];
-#pragma unroll
-            for (int j = 0; j < 8; j++) wn[j] = lds_f32(wa + 64 * (in + j));
-            xn[0] = lds_f4(xa + 4 * in);
-            xn[1] = lds_f4(xa + 4 * in + 16);
-            const float xv[8] = {x[0].x, x[0].y, x[0].z, x[0].w, x[1].x, x[1].y, x[1].z, x[1].w};
-#pragma unroll
-            for (int j = 0; j < 8; j++) acc = __fadd_rn(acc, __fmul_rn(w[j], xv[j]));
-#pragma unroll
-            for (int j = 0; j < 8; j++) w[j] = wn[j];
-            x[0] = xn[0];
-            x[1] = xn[1];
+    const int s16 = split & ~15;
+    if (s16) {
+        float wA[8], wB[8];
+        float4 xA[2], xB[2];
+        ld8f(wA, xA, wa, xa, 0);
+#pragma unroll 1
+        for (; i < s16; i += 16) {
+            ld8f(wB, xB, wa, xa, i + 8);
+            acc = add8f(acc, wA, xA);
+            const int in = i + 16 < s16 ? i + 16 : i;
+            ld8f(wA, xA, wa, xa, in);
+            acc = add8f(acc, wB, xB);
         }
     }
+#pragma unroll 1
     for (; i < split; i++) acc = __fadd_rn(acc, __fmul_rn(lds_f32(wa + 64 * i), lds_f32(xa + 4 * i)));
+#pragma unroll 1
     for (; i < k; i++) acc = __fmaf_rn(lds_f32(wa + 64 * i), lds_f32(xa + 4 * i), acc);
     return acc;
 }
 
-// y = tiles[t0, t1) . x for one CTA, exact: y[o] for o in [0, 16 (t1 - t0)) (shared memory).
-// scratch holds scratch_pairs float2 (quantised dtypes; at least k/32). staged, ns: a copy of tiles
-// [t0, t0 + ns) in shared memory, staged_stride(dtype, k) bytes apart, read instead of global memory.
-static __device__ __noinline__ void matvec_exact(int dtype, const uint8_t *tiles, int k, int t0, int t1, const Prep p, float2 *scratch,
-                                                 int scratch_pairs, float *y, const uint8_t *staged = nullptr, int ns = 0) {
+// One out-of-line copy per quantised dtype (a layer runs only its own dtype's code).
+template <int DT>
+static __device__ __noinline__ void qmatvec_call(const uint8_t *tiles, const uint8_t *tilesB, int ntA, int k, int n_out, const Prep p,
+                                                 float2 *scratch, int scratch_pairs, float *y) {
+    qmatvec<DT, true>(tiles, tilesB, ntA, k, n_out, p, scratch, scratch_pairs, y);
+}
+
+// f32 / bf16 tiles ([K][16] f32, [K/2][16][2] bf16) [0, n/16) at base (the first ns staged), one
+// output per thread.
+template <int DT>
+static __device__ __noinline__ void matvec_wide(const uint8_t *base, int k, int n, const Prep p, float *y, const uint8_t *staged, int ns) {
     const int tid = threadIdx.x, nth = blockDim.x;
-    if (t1 <= t0) return;
-    const size_t tb = tile_bytes(dtype, k);
-    const uint8_t *base = tiles + (size_t)t0 * tb;
-    const int n = (t1 - t0) * kTile;
-    const uint8_t *ta = ns > 0 ? staged : base, *tbb = ns > 0 ? base + (size_t)ns * tb : base;
-    const int nta = ns > 0 ? ns : 1 << 30;
-    if (dtype == DT_Q8) { qmatvec<DT_Q8, true>(ta, tbb, nta, k, n, p, scratch, scratch_pairs, y); return; }
-    if (dtype == DT_Q4) { qmatvec<DT_Q4, true>(ta, tbb, nta, k, n, p, scratch, scratch_pairs, y); return; }
-    if (dtype == DT_MX) { qmatvec<DT_MX, true>(ta, tbb, nta, k, n, p, scratch, scratch_pairs, y); return; }
     // f32 / bf16 (tiles [K][16] f32, [K/2][16][2] bf16): one thread per output walks its row in input
     // order, the reference's chain; lanes 0-15 and 16-31 of a warp take two tiles.
     const int split = fused_from(k);
-    const size_t sst = staged_stride(dtype, k);
+    const size_t sst = staged_stride(DT, k), tb = tile_bytes(DT, k);
     const uint32_t xa = (uint32_t)__cvta_generic_to_shared(p.xf);
+#pragma unroll 1
     for (int o = tid; o < n; o += nth) {
         const int t = o >> 4, c = o & 15;
         if (t < ns) {
             const uint32_t wa = (uint32_t)__cvta_generic_to_shared(staged + (size_t)t * sst) + 4 * c;
-            y[o] = dtype == DT_BF16 ? chain_bf16_shared(wa, xa, k) : chain_f32_shared(wa, xa, k, split);
+            y[o] = DT == DT_BF16 ? chain_bf16_shared(wa, xa, k) : chain_f32_shared(wa, xa, k, split);
             continue;
         }
         const uint8_t *tile = base + (size_t)t * tb;
         float acc = 0.0f;
-        if (dtype == DT_BF16) {
+        if (DT == DT_BF16) {
             const uint32_t *w = (const uint32_t *)tile + c;
             int q = 0;
+#pragma unroll 1
             for (; q + 8 <= k / 2; q += 8) {
                 uint32_t v[8];
 #pragma unroll
@@ -408,6 +420,7 @@ static __device__ __noinline__ void matvec_exact(int dtype, const uint8_t *tiles
                     acc = __fmaf_rn(l3m_bits_f32(v[j] & 0xFFFF0000u), p.xf[2 * (q + j) + 1], acc);
                 }
             }
+#pragma unroll 1
             for (; q < k / 2; q++) {
                 const uint32_t v = ld_stream_u32(w + (size_t)q * kTile);
                 acc = __fmaf_rn(l3m_bits_f32(v << 16), p.xf[2 * q], acc);
@@ -417,6 +430,7 @@ static __device__ __noinline__ void matvec_exact(int dtype, const uint8_t *tiles
             const float *w = (const float *)tile + c;
 #pragma unroll 8
             for (int i = 0; i < split; i++) acc = __fadd_rn(acc, __fmul_rn(__ldg(w + (size_t)i * kTile), p.xf[i]));
+#pragma unroll 1
             for (int i = split; i < k; i++) acc = __fmaf_rn(__ldg(w + (size_t)i * kTile), p.xf[i], acc);
         }
         y[o] = acc;
@@ -424,63 +438,60 @@ static __device__ __noinline__ void matvec_exact(int dtype, const uint8_t *tiles
     __syncthreads();
 }
 
-// Sequential fp32 sum of v[0..n) in index order (v 16-byte aligned), by the calling thread: 32 values
-// per batch, the next batch loading while this one adds.
-// squares: add RN(v*v) instead of v.
-template <bool SQUARES>
-__device__ __forceinline__ float chain_sum(const float *v, int n, float acc) {
-    const float4 *v4 = (const float4 *)v;
-    const int nf = n & ~31;
-    if (nf) {
-        float4 r[8];
-#pragma unroll
-        for (int j = 0; j < 8; j++) r[j] = v4[j];
-        for (int i = 0; i < nf; i += 32) {
-            float4 nx[8];
-            const int in = i + 32 < nf ? i + 32 : i;
-#pragma unroll
-            for (int j = 0; j < 8; j++) nx[j] = v4[in / 4 + j];
-#pragma unroll
-            for (int j = 0; j < 8; j++) {
-                const float e[4] = {r[j].x, r[j].y, r[j].z, r[j].w};
-#pragma unroll
-                for (int h = 0; h < 4; h++) acc = __fadd_rn(acc, SQUARES ? __fmul_rn(e[h], e[h]) : e[h]);
-            }
-#pragma unroll
-            for (int j = 0; j < 8; j++) r[j] = nx[j];
-        }
-    }
-#pragma unroll 8
-    for (int i = nf; i < n; i++) acc = __fadd_rn(acc, SQUARES ? __fmul_rn(v[i], v[i]) : v[i]);
-    return acc;
+// y = tiles[t0, t1) . x for one CTA, exact: y[o] for o in [0, 16 (t1 - t0)) (shared memory).
+// scratch holds scratch_pairs float2 (quantised dtypes; at least k/32). staged, ns: a copy of tiles
+// [t0, t0 + ns) in shared memory, staged_stride(dtype, k) bytes apart, read instead of global memory.
+static __device__ __noinline__ void matvec_exact(int dtype, const uint8_t *tiles, int k, int t0, int t1, const Prep p, float2 *scratch,
+                                                 int scratch_pairs, float *y, const uint8_t *staged = nullptr, int ns = 0) {
+    if (t1 <= t0) return;
+    const size_t tb = tile_bytes(dtype, k);
+    const uint8_t *base = tiles + (size_t)t0 * tb;
+    const int n = (t1 - t0) * kTile;
+    const uint8_t *ta = ns > 0 ? staged : base, *tbb = ns > 0 ? base + (size_t)ns * tb : base;
+    const int nta = ns > 0 ? ns : 1 << 30;
+    if (dtype == DT_Q8) { qmatvec_call<DT_Q8>(ta, tbb, nta, k, n, p, scratch, scratch_pairs, y); return; }
+    if (dtype == DT_Q4) { qmatvec_call<DT_Q4>(ta, tbb, nta, k, n, p, scratch, scratch_pairs, y); return; }
+    if (dtype == DT_MX) { qmatvec_call<DT_MX>(ta, tbb, nta, k, n, p, scratch, scratch_pairs, y); return; }
+    if (dtype == DT_BF16) matvec_wide<DT_BF16>(base, k, n, p, y, staged, ns);
+    else matvec_wide<DT_F32>(base, k, n, p, y, staged, ns);
 }
 
+template <bool SQ>
+static __device__ __noinline__ float seq_sum(const float *v, int n);
+
 // ---- rmsnorm (reference src/ops.c:13-18). x 16-byte aligned, w in shared or global memory; red: one
-// float. The sum of squares is the reference's sequential chain, run by thread 0 from registers while
-// the other threads fetch w.
-constexpr int kNormPerThread = 8;
-struct NoSide { __device__ void operator()(int, int) const {} };
-// side(t, nt): work for threads 32.. (t = threadIdx.x - 32 of nt) while thread 0 runs the chain.
-template <class Side>
-__device__ __forceinline__ void rmsnorm_side(const float *x, const float *w, int n, float eps, float *y, float *red, const Side &side) {
+// float. The sum of squares is the reference's sequential chain, run by thread 0. ps (when ps.kc is
+// set): threads 32.. start attention's K/V copies
+// meanwhile (attend_prestage), so that they land while the chain runs.
+struct PreStage {
+    const uint16_t *kc, *vc;
+    int kstride, vstride, pos, hd;
+    uint16_t *kvbuf, *vtbuf;
+    int chunk;
+};
+template <bool VT>
+__device__ __noinline__ void attend_prestage(const uint16_t *kc, const uint16_t *vc, int kstride, int vstride, int pos, int hd,
+                                             uint16_t *kvbuf, uint16_t *vtbuf, int chunk, int tid = -1, int nth = 0);
+__device__ __forceinline__ void side_prestage(const PreStage &ps) {
+    if (ps.kc && threadIdx.x >= 32)
+        attend_prestage<true>(ps.kc, ps.vc, ps.kstride, ps.vstride, ps.pos, ps.hd, ps.kvbuf, ps.vtbuf, ps.chunk, threadIdx.x - 32, blockDim.x - 32);
+}
+static __device__ __noinline__ void rmsnorm_exact(const float *x, const float *w, int n, float eps, float *y, float *red,
+                                                  const PreStage ps = PreStage{}) {
     const int tid = threadIdx.x, nth = blockDim.x;
-    float wr[kNormPerThread];
-#pragma unroll
-    for (int j = 0; j < kNormPerThread; j++) wr[j] = tid + j * nth < n ? w[tid + j * nth] : 0.0f;
     if (tid == 0) {
         const int split = fused_from(n);
-        float ss = chain_sum<true>(x, split, 0.0f);
+        float ss = seq_sum<true>(x, split);
+#pragma unroll 1
         for (int i = split; i < n; i++) ss = __fmaf_rn(x[i], x[i], ss);
         *red = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
-    } else if (tid >= 32) {
-        side(tid - 32, nth - 32);
+    } else {
+        side_prestage(ps);
     }
     __syncthreads();
     const float sc = *red;
-#pragma unroll
-    for (int j = 0; j < kNormPerThread; j++)
-        if (tid + j * nth < n) y[tid + j * nth] = __fmul_rn(__fmul_rn(x[tid + j * nth], sc), wr[j]);
-    for (int i = tid + kNormPerThread * nth; i < n; i += nth) y[i] = __fmul_rn(__fmul_rn(x[i], sc), w[i]);
+#pragma unroll 1
+    for (int i = tid; i < n; i += nth) y[i] = __fmul_rn(__fmul_rn(x[i], sc), w[i]);
     __syncthreads();
 }
 
@@ -491,6 +502,7 @@ __device__ __forceinline__ float chain_var(const float *v, float mean, int n, in
     int i = 0;
     const float4 *v4 = (const float4 *)v;
     const int nf = split & ~3;
+#pragma unroll 1
     for (; i < nf; i += 4) {
         const float4 r = v4[i >> 2];
         const float e[4] = {r.x, r.y, r.z, r.w};
@@ -500,33 +512,31 @@ __device__ __forceinline__ float chain_var(const float *v, float mean, int n, in
             acc = __fadd_rn(acc, __fmul_rn(d, d));
         }
     }
+#pragma unroll 1
     for (; i < split; i++) { const float d = __fsub_rn(v[i], mean); acc = __fadd_rn(acc, __fmul_rn(d, d)); }
+#pragma unroll 1
     for (; i < n; i++) { const float d = __fsub_rn(v[i], mean); acc = __fmaf_rn(d, d, acc); }
     return acc;
 }
 
 // LayerNorm (reference src/ops.c:20-27): sequential mean, the variance chain above, s = 1/sqrt(var/n
-// + eps), y = fma((x - mean) * s, w, b). Thread 0 runs the chains; side(t, nt) as in rmsnorm_side.
-template <class Side>
-__device__ __forceinline__ void layernorm_side(const float *x, const float *w, const float *b, int n, float eps, float *y, float *red,
-                                               const Side &side) {
+// + eps), y = fma((x - mean) * s, w, b). Thread 0 runs the chains; ps as in rmsnorm_exact.
+static __device__ __noinline__ void layernorm_exact(const float *x, const float *w, const float *b, int n, float eps, float *y, float *red,
+                                                    const PreStage ps = PreStage{}) {
     const int tid = threadIdx.x, nth = blockDim.x;
     if (tid == 0) {
-        const float mean = __fdiv_rn(chain_sum<false>(x, n, 0.0f), (float)n);
+        const float mean = __fdiv_rn(seq_sum<false>(x, n), (float)n);
         const float var = chain_var(x, mean, n, fused_from(n));
         red[0] = mean;
         red[1] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(var, (float)n), eps)));
-    } else if (tid >= 32) {
-        side(tid - 32, nth - 32);
+    } else {
+        side_prestage(ps);
     }
     __syncthreads();
     const float mean = red[0], sc = red[1];
+#pragma unroll 1
     for (int i = tid; i < n; i += nth) y[i] = __fmaf_rn(__fmul_rn(__fsub_rn(x[i], mean), sc), w[i], b[i]);
     __syncthreads();
-}
-
-static __device__ __noinline__ void layernorm_exact(const float *x, const float *w, const float *b, int n, float eps, float *y, float *red) {
-    layernorm_side(x, w, b, n, eps, y, red, NoSide());
 }
 
 // GELU, tanh form (reference src/ops.c:53-56 as built: x + 0.044715 x^3 is one fma). tanhf is the
@@ -537,13 +547,9 @@ __device__ __forceinline__ float gelu_tanh(float v) {
     return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, tanhf(__fmul_rn(0.7978845608f, inner))));
 }
 
-static __device__ __noinline__ void rmsnorm_exact(const float *x, const float *w, int n, float eps, float *y, float *tmp, float *red) {
-    (void)tmp;
-    rmsnorm_side(x, w, n, eps, y, red, NoSide());
-}
-
 // ---- RoPE on one head in place (reference src/ops.c:29-40): cs[i] = {cos, sin} of pair i at this position.
 __device__ inline void rope_exact(float *v, int hd, const float2 *cs) {
+    #pragma unroll 1
     for (int i = threadIdx.x; i < hd / 2; i += blockDim.x) {
         const float2 c = cs[i];
         const float a = v[2 * i], b = v[2 * i + 1];
@@ -553,7 +559,9 @@ __device__ inline void rope_exact(float *v, int hd, const float2 *cs) {
     __syncthreads();
 }
 
-__device__ __forceinline__ float expf_libm(float x, const uint32_t *list, const uint32_t *index) {
+// One out-of-line copy for every caller (attention's softmax, the SiLU gate): code size matters more
+// than a call here.
+static __device__ __noinline__ float expf_libm(float x, const uint32_t *list, const uint32_t *index) {
     return l3m_expf_exact(x, list, index);
 }
 
@@ -583,7 +591,7 @@ __host__ __device__ constexpr int attn_vt_stride(int chunk) { return ((chunk + 1
 // own copies (cp_async_wait_all) before the barrier that precedes reading them.
 template <bool VT>
 __device__ __noinline__ void attend_prestage(const uint16_t *kc, const uint16_t *vc, int kstride, int vstride, int pos, int hd,
-                                             uint16_t *kvbuf, uint16_t *vtbuf, int chunk, int tid = -1, int nth = 0) {
+                                             uint16_t *kvbuf, uint16_t *vtbuf, int chunk, int tid, int nth) {
     if (tid < 0) { tid = threadIdx.x; nth = blockDim.x; }
     const int rs = hd + 8, h8 = hd / 8, vs = attn_vt_stride(chunk);
     const bool kvec = kstride % 8 == 0 && ((uintptr_t)kc & 15) == 0;
@@ -592,6 +600,7 @@ __device__ __noinline__ void attend_prestage(const uint16_t *kc, const uint16_t 
     {
         const int dr = nth / h8, dj = nth - dr * h8;
         int r = tid / h8, j = tid - r * h8;
+        #pragma unroll 1
         for (int e = tid; e < nk * h8; e += nth) {
             uint16_t *dst = kvbuf + r * rs + j * 8;
             const uint16_t *src = kc + (size_t)r * kstride + j * 8;
@@ -604,6 +613,7 @@ __device__ __noinline__ void attend_prestage(const uint16_t *kc, const uint16_t 
     if (VT) {
         const int p8 = (min(chunk, pos + 1) + 7) >> 3, di = nth / p8, dp = nth - di * p8;
         int i = tid / p8, pc = tid - i * p8;
+        #pragma unroll 1
         for (int e = tid; e < hd * p8; e += nth) {
             uint16_t *dst = vtbuf + i * vs + pc * 8;
             const uint16_t *src = vc + (size_t)i * vstride + pc * 8;
@@ -616,6 +626,167 @@ __device__ __noinline__ void attend_prestage(const uint16_t *kc, const uint16_t 
     cp_async_commit();
 }
 
+// K rows [c0, c0 + cnt) into kvbuf (row r at r * (hd + 8)); row pos from kcur. Asynchronous where
+// aligned (the caller commits, waits and synchronises).
+static __device__ __noinline__ void stage_k_rows(uint16_t *kvbuf, const uint16_t *kc, int kstride, const uint16_t *kcur, int pos, int hd, int c0, int cnt,
+                                          bool kvec) {
+    const int tid = threadIdx.x, nth = blockDim.x, rs = hd + 8, h8 = hd / 8;
+#pragma unroll 1
+    for (int e = tid; e < cnt * h8; e += nth) {
+        const int r = e / h8, i = (e - r * h8) * 8, t = c0 + r;
+        uint16_t *dst = kvbuf + r * rs + i;
+        if (t == pos) *(uint4 *)dst = *(const uint4 *)(kcur + i);
+        else if (kvec) cp_async16(dst, kc + (size_t)t * kstride + i);
+        else *(uint4 *)dst = ld_row8(kc + (size_t)t * kstride + i, false);
+    }
+    cp_async_commit();
+}
+
+// V of positions [c0, c0 + cnt) into shared memory. VT: vtbuf[i * vs + r], one 8-position piece per
+// copy (positions past pos in a piece are never read; position pos itself is patched from vcur by
+// the thread that reads its column, after the copies have landed). Else rows into kvbuf as K.
+template <bool VT>
+__device__ __noinline__ void stage_v_rows(uint16_t *kvbuf, uint16_t *vtbuf, const uint16_t *vc, int vstride, const uint16_t *vcur, int pos, int hd,
+                                          int c0, int cnt, int chunk, bool vvec) {
+    const int tid = threadIdx.x, nth = blockDim.x;
+    if (VT) {
+        const int p8 = (cnt + 7) >> 3, vs = attn_vt_stride(chunk);
+#pragma unroll 1
+        for (int e = tid; e < hd * p8; e += nth) {
+            const int i = e / p8, pc = e - i * p8;
+            uint16_t *dst = vtbuf + i * vs + pc * 8;
+            const uint16_t *src = vc + (size_t)i * vstride + c0 + pc * 8;
+            if (vvec) cp_async16(dst, src);
+            else *(uint4 *)dst = ld_row8(src, false);
+        }
+    } else {
+        stage_k_rows(kvbuf, vc, vstride, vcur, pos, hd, c0, cnt, vvec);
+        return;
+    }
+    cp_async_commit();
+}
+
+// Sequential fp32 sum of v[0..n) (v 16-byte aligned) in index order, by the calling thread; each term
+// squared first (rounded) with SQ. 32 values per step in two halves: one half's loads are in flight
+// while the other half adds (no register copies between steps).
+template <bool SQ>
+__device__ __forceinline__ float add16(float acc, const float4 (&r)[4]) {
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const float e[4] = {r[j].x, r[j].y, r[j].z, r[j].w};
+#pragma unroll
+        for (int h = 0; h < 4; h++) acc = __fadd_rn(acc, SQ ? __fmul_rn(e[h], e[h]) : e[h]);
+    }
+    return acc;
+}
+template <bool SQ>
+static __device__ __noinline__ float seq_sum(const float *v, int n) {
+    const float4 *v4 = (const float4 *)v;
+    const int n32 = n & ~31;
+    float acc = 0.0f;
+    int i = 0;
+    if (n32) {
+        float4 a[4], b[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) a[j] = v4[j];
+#pragma unroll 1
+        for (; i < n32; i += 32) {
+#pragma unroll
+            for (int j = 0; j < 4; j++) b[j] = v4[i / 4 + 4 + j];
+            acc = add16<SQ>(acc, a);
+            const int in = i + 32 < n32 ? i + 32 : i;
+#pragma unroll
+            for (int j = 0; j < 4; j++) a[j] = v4[in / 4 + j];
+            acc = add16<SQ>(acc, b);
+        }
+    }
+#pragma unroll 1
+    for (; i + 4 <= n; i += 4) {
+        const float4 t = v4[i / 4];
+        acc = __fadd_rn(acc, SQ ? __fmul_rn(t.x, t.x) : t.x);
+        acc = __fadd_rn(acc, SQ ? __fmul_rn(t.y, t.y) : t.y);
+        acc = __fadd_rn(acc, SQ ? __fmul_rn(t.z, t.z) : t.z);
+        acc = __fadd_rn(acc, SQ ? __fmul_rn(t.w, t.w) : t.w);
+    }
+#pragma unroll 1
+    for (; i < n; i++) acc = __fadd_rn(acc, SQ ? __fmul_rn(v[i], v[i]) : v[i]);
+    return acc;
+}
+
+// Attention's two chains, 16 steps per iteration in two halves (one half's loads in flight while the
+// other computes). A score: the sequential sum of rounded products q[i] * k[i] (k bf16, 8 per 16 bytes).
+__device__ __forceinline__ float dot8(float dot, const uint4 kv, const float4 q0, const float4 q1) {
+    dot = __fadd_rn(dot, __fmul_rn(q0.x, l3m_bits_f32(kv.x << 16)));
+    dot = __fadd_rn(dot, __fmul_rn(q0.y, l3m_bits_f32(kv.x & 0xFFFF0000u)));
+    dot = __fadd_rn(dot, __fmul_rn(q0.z, l3m_bits_f32(kv.y << 16)));
+    dot = __fadd_rn(dot, __fmul_rn(q0.w, l3m_bits_f32(kv.y & 0xFFFF0000u)));
+    dot = __fadd_rn(dot, __fmul_rn(q1.x, l3m_bits_f32(kv.z << 16)));
+    dot = __fadd_rn(dot, __fmul_rn(q1.y, l3m_bits_f32(kv.z & 0xFFFF0000u)));
+    dot = __fadd_rn(dot, __fmul_rn(q1.z, l3m_bits_f32(kv.w << 16)));
+    dot = __fadd_rn(dot, __fmul_rn(q1.w, l3m_bits_f32(kv.w & 0xFFFF0000u)));
+    return dot;
+}
+// row, q 16-byte aligned; hd a multiple of 8.
+__device__ __forceinline__ float score_dot(const uint16_t *row, const float *q, int hd) {
+    float dot = 0.0f;
+    int i = 0;
+    const int h16 = hd & ~15;
+    if (h16) {
+        uint4 kA = *(const uint4 *)row, kB;
+        float4 a0 = *(const float4 *)q, a1 = *(const float4 *)(q + 4), b0, b1;
+#pragma unroll 1
+        for (; i < h16; i += 16) {
+            kB = *(const uint4 *)(row + i + 8);
+            b0 = *(const float4 *)(q + i + 8);
+            b1 = *(const float4 *)(q + i + 12);
+            dot = dot8(dot, kA, a0, a1);
+            const int in = i + 16 < h16 ? i + 16 : i;
+            kA = *(const uint4 *)(row + in);
+            a0 = *(const float4 *)(q + in);
+            a1 = *(const float4 *)(q + in + 4);
+            dot = dot8(dot, kB, b0, b1);
+        }
+    }
+    if (i < hd) dot = dot8(dot, *(const uint4 *)(row + i), *(const float4 *)(q + i), *(const float4 *)(q + i + 4));
+    return dot;
+}
+// The value mix of one output element: acc = fma(p[r], v[r], acc) over positions in order, v a
+// transposed column (bf16, 8 positions per 16 bytes); col and p 16-byte aligned.
+__device__ __forceinline__ float vmix8(float acc, const uint4 v, const float4 p0, const float4 p1) {
+    acc = __fmaf_rn(p0.x, l3m_bits_f32(v.x << 16), acc); acc = __fmaf_rn(p0.y, l3m_bits_f32(v.x & 0xFFFF0000u), acc);
+    acc = __fmaf_rn(p0.z, l3m_bits_f32(v.y << 16), acc); acc = __fmaf_rn(p0.w, l3m_bits_f32(v.y & 0xFFFF0000u), acc);
+    acc = __fmaf_rn(p1.x, l3m_bits_f32(v.z << 16), acc); acc = __fmaf_rn(p1.y, l3m_bits_f32(v.z & 0xFFFF0000u), acc);
+    acc = __fmaf_rn(p1.z, l3m_bits_f32(v.w << 16), acc); acc = __fmaf_rn(p1.w, l3m_bits_f32(v.w & 0xFFFF0000u), acc);
+    return acc;
+}
+__device__ __forceinline__ float vmix_col(const uint16_t *col, const float *pp, int cnt, float acc) {
+    int r = 0;
+    const int c16 = cnt & ~15;
+    if (c16) {
+        uint4 vA = *(const uint4 *)col, vB;
+        float4 a0 = *(const float4 *)pp, a1 = *(const float4 *)(pp + 4), b0, b1;
+#pragma unroll 1
+        for (; r < c16; r += 16) {
+            vB = *(const uint4 *)(col + r + 8);
+            b0 = *(const float4 *)(pp + r + 8);
+            b1 = *(const float4 *)(pp + r + 12);
+            acc = vmix8(acc, vA, a0, a1);
+            const int rn = r + 16 < c16 ? r + 16 : r;
+            vA = *(const uint4 *)(col + rn);
+            a0 = *(const float4 *)(pp + rn);
+            a1 = *(const float4 *)(pp + rn + 4);
+            acc = vmix8(acc, vB, b0, b1);
+        }
+    }
+    if (r + 8 <= cnt) {
+        acc = vmix8(acc, *(const uint4 *)(col + r), *(const float4 *)(pp + r), *(const float4 *)(pp + r + 4));
+        r += 8;
+    }
+#pragma unroll 1
+    for (; r < cnt; r++) acc = __fmaf_rn(pp[r], l3m_bf16_to_f32(col[r]), acc);
+    return acc;
+}
+
 template <bool VT>
 __device__ __noinline__ void attend_exact(const float *q, const uint16_t *kc, const uint16_t *vc, int kstride, int vstride, const uint16_t *kcur,
                              const uint16_t *vcur, int pos, int hd, float *scores, float *out, float *red, const uint32_t *elist,
@@ -624,114 +795,59 @@ __device__ __noinline__ void attend_exact(const float *q, const uint16_t *kc, co
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
     const bool kvec = kstride % 8 == 0 && ((uintptr_t)kc & 15) == 0;
     const bool vvec = vstride % 8 == 0 && ((uintptr_t)vc & 15) == 0;
-    const int n = pos + 1, rs = hd + 8, h8 = hd / 8, vs = attn_vt_stride(chunk);
-    // V of positions [c0, c0 + cnt) into shared memory; aligned pieces as asynchronous copies that land
-    // while the caller goes on (cp_async_wait_all + __syncthreads before reading them).
-    auto stage_v = [&](int c0, int cnt) {
-        if (VT) {                                            // vtbuf[i * vs + r], one 8-position piece per copy
-            // Positions past pos in a piece are never read; position pos itself is patched from vcur
-            // by the thread that reads its column, after the copies have landed.
-            const int p8 = (cnt + 7) >> 3, di = nth / p8, dp = nth - di * p8;
-            int i = tid / p8, pc = tid - i * p8;
-            for (int e = tid; e < hd * p8; e += nth) {
-                uint16_t *dst = vtbuf + i * vs + pc * 8;
-                const uint16_t *src = vc + (size_t)i * vstride + c0 + pc * 8;
-                if (vvec) cp_async16(dst, src);
-                else *(uint4 *)dst = ld_row8(src, false);
-                pc += dp; i += di;
-                if (pc >= p8) { pc -= p8; i++; }
-            }
-        } else {                                             // kvbuf[r * rs + i], rows as in global memory
-            const int dr = nth / h8, dj = nth - dr * h8;
-            int r = tid / h8, j = tid - r * h8;
-            for (int e = tid; e < cnt * h8; e += nth) {
-                const int i = j * 8, t = c0 + r;
-                uint16_t *dst = kvbuf + r * rs + i;
-                if (t == pos) *(uint4 *)dst = *(const uint4 *)(vcur + i);
-                else if (vvec) cp_async16(dst, vc + (size_t)t * vstride + i);
-                else *(uint4 *)dst = ld_row8(vc + (size_t)t * vstride + i, false);
-                j += dj; r += dr;
-                if (j >= h8) { j -= h8; r++; }
-            }
-        }
-        cp_async_commit();
-    };
-    auto stage_k = [&](int c0, int cnt) {
-        const int dr = nth / h8, dj = nth - dr * h8;
-        int r = tid / h8, j = tid - r * h8;
-        for (int e = tid; e < cnt * h8; e += nth) {
-            const int i = j * 8, t = c0 + r;
-            uint16_t *dst = kvbuf + r * rs + i;
-            if (t == pos) *(uint4 *)dst = *(const uint4 *)(kcur + i);
-            else if (kvec) cp_async16(dst, kc + (size_t)t * kstride + i);
-            else *(uint4 *)dst = ld_row8(kc + (size_t)t * kstride + i, false);
-            j += dj; r += dr;
-            if (j >= h8) { j -= h8; r++; }
-        }
-        cp_async_commit();
-    };
+    const int n = pos + 1, rs = hd + 8, vs = attn_vt_stride(chunk);
     if (!prestaged) attend_prestage<VT>(kc, vc, kstride, vstride, pos, hd, kvbuf, vtbuf, chunk);
-    // Scores: one thread per row, from K rows staged in shared memory (coalesced copies).
+    // Scores: one thread per row, from K rows staged in shared memory (coalesced copies); each dot is
+    // the sequential sum of rounded products, 8 inputs per step with the next step's loads in flight.
     float m = -INFINITY;
+#pragma unroll 1
     for (int c0 = 0; c0 < n; c0 += chunk) {
         const int cnt = min(chunk, n - c0);
         if (c0 > 0) {
             __syncthreads();
-            stage_k(c0, cnt);
+            stage_k_rows(kvbuf, kc, kstride, kcur, pos, hd, c0, cnt, kvec);
         } else if (pos < cnt) {                              // the first chunk's rows < pos are prestaged
+#pragma unroll 1
             for (int i = tid * 8; i < hd; i += nth * 8) *(uint4 *)(kvbuf + pos * rs + i) = *(const uint4 *)(kcur + i);
         }
         cp_async_wait_all();
         __syncthreads();
+#pragma unroll 1
         for (int r = tid; r < cnt; r += nth) {
-            const uint16_t *row = kvbuf + r * rs;
-            float dot = 0.0f;
-            for (int i0 = 0; i0 < hd; i0 += 64) {
-                uint4 v[8];
-#pragma unroll
-                for (int j = 0; j < 8; j++)
-                    if (i0 + 8 * j < hd) v[j] = *(const uint4 *)(row + i0 + 8 * j);
-#pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    if (i0 + 8 * j >= hd) break;
-                    const uint32_t u[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-                    const float *qq = q + i0 + 8 * j;
-#pragma unroll
-                    for (int h = 0; h < 4; h++) {
-                        dot = __fadd_rn(dot, __fmul_rn(qq[2 * h], l3m_bits_f32(u[h] << 16)));
-                        dot = __fadd_rn(dot, __fmul_rn(qq[2 * h + 1], l3m_bits_f32(u[h] & 0xFFFF0000u)));
-                    }
-                }
-            }
+            const float dot = score_dot(kvbuf + r * rs, q, hd);
             const float sc = __fmul_rn(dot, scale);
             scores[c0 + r] = sc;
             m = fmaxf(m, sc);
         }
     }
     __syncthreads();
-    if (!VT) stage_v(0, min(chunk, n));                      // reuses the K buffer
+    if (!VT) stage_v_rows<VT>(kvbuf, vtbuf, vc, vstride, vcur, pos, hd, 0, min(chunk, n), chunk, vvec);   // reuses the K buffer
     // The reference takes the running maximum from scores[0] with a strict >: NaN scores after the
     // first are skipped (fmaxf drops them), a NaN first score stays. The maximum of the rest is order-free.
     m = warp_max_f32(m);
     if (lane == 0) red[warp] = m;
     __syncthreads();
     float mx = -INFINITY;
+#pragma unroll 1
     for (int w = 0; w < (nth >> 5); w++) mx = fmaxf(mx, red[w]);
     if (scores[0] != scores[0]) mx = scores[0];
+#pragma unroll 1
     for (int t = tid; t < n; t += nth) scores[t] = expf_libm(__fsub_rn(scores[t], mx), elist, eindex);
     __syncthreads();
-    if (tid == 0) red[32] = chain_sum<false>(scores, n, 0.0f);     // the sequential sum
+    if (tid == 0) red[32] = seq_sum<false>(scores, n);      // the sequential sum
     __syncthreads();
     const float sum = red[32];
+#pragma unroll 1
     for (int t = tid; t < n; t += nth) scores[t] = __fdiv_rn(scores[t], sum);
     cp_async_wait_all();
     __syncthreads();
     float acc = 0.0f;                                        // thread i < hd: output element i
+#pragma unroll 1
     for (int c0 = 0; c0 < n; c0 += chunk) {
         const int cnt = min(chunk, n - c0);
         if (c0 > 0) {
             __syncthreads();
-            stage_v(c0, cnt);
+            stage_v_rows<VT>(kvbuf, vtbuf, vc, vstride, vcur, pos, hd, c0, cnt, chunk, vvec);
             cp_async_wait_all();
             __syncthreads();
         }
@@ -739,40 +855,17 @@ __device__ __noinline__ void attend_exact(const float *q, const uint16_t *kc, co
             const float *pp = scores + c0;                   // c0 is a multiple of 8
             int r = 0;
             if (VT) {
-                uint16_t *col = vtbuf + tid * vs;            // 8 positions per 16-byte read, one batch ahead
+                uint16_t *col = vtbuf + tid * vs;
                 if (pos - c0 < cnt) col[pos - c0] = vcur[tid];
-                if (cnt >= 8) {
-                    uint4 v = *(const uint4 *)col;
-                    float4 p0 = *(const float4 *)pp, p1 = *(const float4 *)(pp + 4);
-                    for (; r + 8 <= cnt; r += 8) {
-                        const int rn = r + 16 <= cnt ? r + 8 : r;
-                        const uint4 vn = *(const uint4 *)(col + rn);
-                        const float4 q0 = *(const float4 *)(pp + rn), q1 = *(const float4 *)(pp + rn + 4);
-                        acc = __fmaf_rn(p0.x, l3m_bits_f32(v.x << 16), acc); acc = __fmaf_rn(p0.y, l3m_bits_f32(v.x & 0xFFFF0000u), acc);
-                        acc = __fmaf_rn(p0.z, l3m_bits_f32(v.y << 16), acc); acc = __fmaf_rn(p0.w, l3m_bits_f32(v.y & 0xFFFF0000u), acc);
-                        acc = __fmaf_rn(p1.x, l3m_bits_f32(v.z << 16), acc); acc = __fmaf_rn(p1.y, l3m_bits_f32(v.z & 0xFFFF0000u), acc);
-                        acc = __fmaf_rn(p1.z, l3m_bits_f32(v.w << 16), acc); acc = __fmaf_rn(p1.w, l3m_bits_f32(v.w & 0xFFFF0000u), acc);
-                        v = vn; p0 = q0; p1 = q1;
-                    }
-                }
-#pragma unroll 4
-                for (; r < cnt; r++) acc = __fmaf_rn(pp[r], l3m_bf16_to_f32(col[r]), acc);
+                acc = vmix_col(col, pp, cnt, acc);
             } else {
                 const uint16_t *col = kvbuf + tid;
-                for (; r + 8 <= cnt; r += 8) {
-                    const float4 p0 = *(const float4 *)(pp + r), p1 = *(const float4 *)(pp + r + 4);
-                    float vv[8];
-#pragma unroll
-                    for (int j = 0; j < 8; j++) vv[j] = l3m_bf16_to_f32(col[(r + j) * rs]);
-                    acc = __fmaf_rn(p0.x, vv[0], acc); acc = __fmaf_rn(p0.y, vv[1], acc);
-                    acc = __fmaf_rn(p0.z, vv[2], acc); acc = __fmaf_rn(p0.w, vv[3], acc);
-                    acc = __fmaf_rn(p1.x, vv[4], acc); acc = __fmaf_rn(p1.y, vv[5], acc);
-                    acc = __fmaf_rn(p1.z, vv[6], acc); acc = __fmaf_rn(p1.w, vv[7], acc);
-                }
+#pragma unroll 1
                 for (; r < cnt; r++) acc = __fmaf_rn(pp[r], l3m_bf16_to_f32(col[r * rs]), acc);
             }
         }
     }
+#pragma unroll 1
     for (int i = tid; i < hd; i += nth) out[i] = acc;
     __syncthreads();
 }
