@@ -282,17 +282,19 @@ __device__ void qmatvec(const uint8_t *tiles, const uint8_t *tilesB, int ntA, in
     }
 }
 
-// Shared-memory loads by address (the staged chains below): no side effects, so the compiler may
-// schedule them freely within the loop that uses them.
+// Shared-memory loads by shared-window address (the chains below), in program order with every other
+// memory access and barrier (volatile, memory clobber): the loops that use them already issue each
+// load where it must go, so the compiler has nothing to reorder, and it must not move one above the
+// barrier or store that makes its data ready. Arithmetic still schedules freely around them.
 __device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
     uint32_t v;
-    asm("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
     return v;
 }
 __device__ __forceinline__ float lds_f32(uint32_t a) { return __uint_as_float(lds_u32(a)); }
 __device__ __forceinline__ float4 lds_f4(uint32_t a) {
     float4 v;
-    asm("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a) : "memory");
     return v;
 }
 
@@ -666,13 +668,15 @@ __device__ __noinline__ void stage_v_rows(uint16_t *kvbuf, uint16_t *vtbuf, cons
     cp_async_commit();
 }
 
-// Sequential fp32 sum of v[0..n) (v 16-byte aligned) in index order, by the calling thread; each term
-// squared first (rounded) with SQ. 32 values per step in two halves: one half's loads are in flight
-// while the other half adds (no register copies between steps).
+// Sequential fp32 sum of v[0..n) (v in shared memory, 16-byte aligned) in index order, by the
+// calling thread; each term squared first (rounded) with SQ. 64 values per iteration in two halves:
+// one half's loads are in flight while the other half's 32 dependent adds run (about 150 cycles,
+// enough to cover a shared-memory load while bulk copies land in the same memory), and no register
+// copies between steps.
 template <bool SQ>
-__device__ __forceinline__ float add16(float acc, const float4 (&r)[4]) {
+__device__ __forceinline__ float add32(float acc, const float4 (&r)[8]) {
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
+    for (int j = 0; j < 8; j++) {
         const float e[4] = {r[j].x, r[j].y, r[j].z, r[j].w};
 #pragma unroll
         for (int h = 0; h < 4; h++) acc = __fadd_rn(acc, SQ ? __fmul_rn(e[h], e[h]) : e[h]);
@@ -681,40 +685,44 @@ __device__ __forceinline__ float add16(float acc, const float4 (&r)[4]) {
 }
 template <bool SQ>
 static __device__ __noinline__ float seq_sum(const float *v, int n) {
-    const float4 *v4 = (const float4 *)v;
-    const int n32 = n & ~31;
+    const uint32_t va = (uint32_t)__cvta_generic_to_shared(v);
+    const int n64 = n & ~63;
     float acc = 0.0f;
     int i = 0;
-    if (n32) {
-        float4 a[4], b[4];
+    if (n64) {
+        float4 a[8], b[8];
 #pragma unroll
-        for (int j = 0; j < 4; j++) a[j] = v4[j];
+        for (int j = 0; j < 8; j++) a[j] = lds_f4(va + 16 * j);
 #pragma unroll 1
-        for (; i < n32; i += 32) {
+        for (; i < n64; i += 64) {
 #pragma unroll
-            for (int j = 0; j < 4; j++) b[j] = v4[i / 4 + 4 + j];
-            acc = add16<SQ>(acc, a);
-            const int in = i + 32 < n32 ? i + 32 : i;
+            for (int j = 0; j < 8; j++) b[j] = lds_f4(va + 4 * i + 128 + 16 * j);
+            acc = add32<SQ>(acc, a);
+            const int in = i + 64 < n64 ? i + 64 : i;
 #pragma unroll
-            for (int j = 0; j < 4; j++) a[j] = v4[in / 4 + j];
-            acc = add16<SQ>(acc, b);
+            for (int j = 0; j < 8; j++) a[j] = lds_f4(va + 4 * in + 16 * j);
+            acc = add32<SQ>(acc, b);
         }
     }
 #pragma unroll 1
     for (; i + 4 <= n; i += 4) {
-        const float4 t = v4[i / 4];
+        const float4 t = lds_f4(va + 4 * i);
         acc = __fadd_rn(acc, SQ ? __fmul_rn(t.x, t.x) : t.x);
         acc = __fadd_rn(acc, SQ ? __fmul_rn(t.y, t.y) : t.y);
         acc = __fadd_rn(acc, SQ ? __fmul_rn(t.z, t.z) : t.z);
         acc = __fadd_rn(acc, SQ ? __fmul_rn(t.w, t.w) : t.w);
     }
 #pragma unroll 1
-    for (; i < n; i++) acc = __fadd_rn(acc, SQ ? __fmul_rn(v[i], v[i]) : v[i]);
+    for (; i < n; i++) {
+        const float t = lds_f32(va + 4 * i);
+        acc = __fadd_rn(acc, SQ ? __fmul_rn(t, t) : t);
+    }
     return acc;
 }
 
-// Attention's two chains, 16 steps per iteration in two halves (one half's loads in flight while the
-// other computes). A score: the sequential sum of rounded products q[i] * k[i] (k bf16, 8 per 16 bytes).
+// Attention's two chains, 32 steps per iteration in two halves (one half's loads in flight while the
+// other's 16 dependent steps run). A score: the sequential sum of rounded products q[i] * k[i] (k
+// bf16, 8 per 16 bytes); row, q in shared memory, 16-byte aligned; hd a multiple of 8.
 __device__ __forceinline__ float dot8(float dot, const uint4 kv, const float4 q0, const float4 q1) {
     dot = __fadd_rn(dot, __fmul_rn(q0.x, l3m_bits_f32(kv.x << 16)));
     dot = __fadd_rn(dot, __fmul_rn(q0.y, l3m_bits_f32(kv.x & 0xFFFF0000u)));
@@ -726,32 +734,49 @@ __device__ __forceinline__ float dot8(float dot, const uint4 kv, const float4 q0
     dot = __fadd_rn(dot, __fmul_rn(q1.w, l3m_bits_f32(kv.w & 0xFFFF0000u)));
     return dot;
 }
-// row, q 16-byte aligned; hd a multiple of 8.
+__device__ __forceinline__ uint4 lds_u4(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a) : "memory");
+    return v;
+}
+// 16 steps' operands: two 16-byte pieces of the bf16 vector at ra (+16) and four float4 at fa.
+struct Ops16 {
+    uint4 k0, k1;
+    float4 f0, f1, f2, f3;
+};
+__device__ __forceinline__ void ld16(Ops16 &o, uint32_t ra, uint32_t fa) {
+    o.k0 = lds_u4(ra);
+    o.k1 = lds_u4(ra + 16);
+    o.f0 = lds_f4(fa);
+    o.f1 = lds_f4(fa + 16);
+    o.f2 = lds_f4(fa + 32);
+    o.f3 = lds_f4(fa + 48);
+}
 __device__ __forceinline__ float score_dot(const uint16_t *row, const float *q, int hd) {
+    const uint32_t ra = (uint32_t)__cvta_generic_to_shared(row), qa = (uint32_t)__cvta_generic_to_shared(q);
     float dot = 0.0f;
     int i = 0;
-    const int h16 = hd & ~15;
-    if (h16) {
-        uint4 kA = *(const uint4 *)row, kB;
-        float4 a0 = *(const float4 *)q, a1 = *(const float4 *)(q + 4), b0, b1;
+    const int h32 = hd & ~31;
+    if (h32) {
+        Ops16 A, B;
+        ld16(A, ra, qa);
 #pragma unroll 1
-        for (; i < h16; i += 16) {
-            kB = *(const uint4 *)(row + i + 8);
-            b0 = *(const float4 *)(q + i + 8);
-            b1 = *(const float4 *)(q + i + 12);
-            dot = dot8(dot, kA, a0, a1);
-            const int in = i + 16 < h16 ? i + 16 : i;
-            kA = *(const uint4 *)(row + in);
-            a0 = *(const float4 *)(q + in);
-            a1 = *(const float4 *)(q + in + 4);
-            dot = dot8(dot, kB, b0, b1);
+        for (; i < h32; i += 32) {
+            ld16(B, ra + 2 * (i + 16), qa + 4 * (i + 16));
+            dot = dot8(dot, A.k0, A.f0, A.f1);
+            dot = dot8(dot, A.k1, A.f2, A.f3);
+            const int in = i + 32 < h32 ? i + 32 : i;
+            ld16(A, ra + 2 * in, qa + 4 * in);
+            dot = dot8(dot, B.k0, B.f0, B.f1);
+            dot = dot8(dot, B.k1, B.f2, B.f3);
         }
     }
-    if (i < hd) dot = dot8(dot, *(const uint4 *)(row + i), *(const float4 *)(q + i), *(const float4 *)(q + i + 4));
+#pragma unroll 1
+    for (; i < hd; i += 8) dot = dot8(dot, lds_u4(ra + 2 * i), lds_f4(qa + 4 * i), lds_f4(qa + 4 * i + 16));
     return dot;
 }
 // The value mix of one output element: acc = fma(p[r], v[r], acc) over positions in order, v a
-// transposed column (bf16, 8 positions per 16 bytes); col and p 16-byte aligned.
+// transposed column (bf16, 8 positions per 16 bytes); col and p in shared memory, 16-byte aligned.
 __device__ __forceinline__ float vmix8(float acc, const uint4 v, const float4 p0, const float4 p1) {
     acc = __fmaf_rn(p0.x, l3m_bits_f32(v.x << 16), acc); acc = __fmaf_rn(p0.y, l3m_bits_f32(v.x & 0xFFFF0000u), acc);
     acc = __fmaf_rn(p0.z, l3m_bits_f32(v.y << 16), acc); acc = __fmaf_rn(p0.w, l3m_bits_f32(v.y & 0xFFFF0000u), acc);
@@ -760,30 +785,27 @@ __device__ __forceinline__ float vmix8(float acc, const uint4 v, const float4 p0
     return acc;
 }
 __device__ __forceinline__ float vmix_col(const uint16_t *col, const float *pp, int cnt, float acc) {
+    const uint32_t ca = (uint32_t)__cvta_generic_to_shared(col), pa = (uint32_t)__cvta_generic_to_shared(pp);
     int r = 0;
-    const int c16 = cnt & ~15;
-    if (c16) {
-        uint4 vA = *(const uint4 *)col, vB;
-        float4 a0 = *(const float4 *)pp, a1 = *(const float4 *)(pp + 4), b0, b1;
+    const int c32 = cnt & ~31;
+    if (c32) {
+        Ops16 A, B;
+        ld16(A, ca, pa);
 #pragma unroll 1
-        for (; r < c16; r += 16) {
-            vB = *(const uint4 *)(col + r + 8);
-            b0 = *(const float4 *)(pp + r + 8);
-            b1 = *(const float4 *)(pp + r + 12);
-            acc = vmix8(acc, vA, a0, a1);
-            const int rn = r + 16 < c16 ? r + 16 : r;
-            vA = *(const uint4 *)(col + rn);
-            a0 = *(const float4 *)(pp + rn);
-            a1 = *(const float4 *)(pp + rn + 4);
-            acc = vmix8(acc, vB, b0, b1);
+        for (; r < c32; r += 32) {
+            ld16(B, ca + 2 * (r + 16), pa + 4 * (r + 16));
+            acc = vmix8(acc, A.k0, A.f0, A.f1);
+            acc = vmix8(acc, A.k1, A.f2, A.f3);
+            const int rn = r + 32 < c32 ? r + 32 : r;
+            ld16(A, ca + 2 * rn, pa + 4 * rn);
+            acc = vmix8(acc, B.k0, B.f0, B.f1);
+            acc = vmix8(acc, B.k1, B.f2, B.f3);
         }
     }
-    if (r + 8 <= cnt) {
-        acc = vmix8(acc, *(const uint4 *)(col + r), *(const float4 *)(pp + r), *(const float4 *)(pp + r + 4));
-        r += 8;
-    }
 #pragma unroll 1
-    for (; r < cnt; r++) acc = __fmaf_rn(pp[r], l3m_bf16_to_f32(col[r]), acc);
+    for (; r + 8 <= cnt; r += 8) acc = vmix8(acc, lds_u4(ca + 2 * r), lds_f4(pa + 4 * r), lds_f4(pa + 4 * r + 16));
+#pragma unroll 1
+    for (; r < cnt; r++) acc = __fmaf_rn(lds_f32(pa + 4 * r), l3m_bits_f32(lds_u32(ca + 2 * (r & ~1)) << (r & 1 ? 0 : 16) & 0xFFFF0000u), acc);
     return acc;
 }
 
