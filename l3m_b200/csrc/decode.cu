@@ -481,7 +481,7 @@ __device__ __noinline__ void phase_attention(const DecodeArgs &a, const LayerDev
     }
     __syncthreads();
     trace<TRACE>(a, tslot, pos, l, 14);
-    attend_exact<true>(y, kc, vc, hd, a.vstride, s.kcur, s.vcur, pos, hd, s.scores, s.att, s.red, a.elist, a.eindex, s.kvbuf, s.vtbuf,
+    attend_exact<true>(y, kc, vc, hd, a.vstride, s.kcur, s.vcur, pos, hd, s.scores, s.att, s.red, a.etab, s.kvbuf, s.vtbuf,
                        a.attn_chunk, prestaged);
     trace<TRACE>(a, tslot, pos, l, 15);
     if (a.async_x) scatter_tx(s.att, s.xa, h * hd, hd, s.xbar + 1);
@@ -544,7 +544,7 @@ __device__ __noinline__ void ffn_gate(const DecodeArgs &a, const LayerDev &L, co
     #pragma unroll 1
     for (int o = threadIdx.x; o < n; o += blockDim.x) {
         const float up = L.b_up ? __fadd_rn(s.y[o], __ldg(L.b_up + g0 + o)) : s.y[o];
-        s.tmp[o] = GPT2 && a.gelu ? gelu_tanh(up) : silu_mul(up, s.y[nf * kTile + o], a.elist, a.eindex);
+        s.tmp[o] = GPT2 && a.gelu ? gelu_tanh(up) : silu_mul(up, s.y[nf * kTile + o], a.etab);
     }
     __syncthreads();
 }
@@ -582,7 +582,7 @@ struct SampleIn {
     float *probs;                        // [vocab] scratch: the weights
     int vocab;
     float temp, gmax;
-    const uint32_t *elist, *eindex;      // libm expf exception list
+    const uint32_t *etab;                // libm expf exception set
 };
 
 __device__ __forceinline__ double rand01(unsigned long long &st) {
@@ -635,7 +635,7 @@ __device__ __noinline__ int sample_token(const SampleIn &in, float *xs, float *t
     int nan = 0;
     for (int i = i0; i < i1; i++) {
         const float d = __fdiv_rn(__fsub_rn(ld_cg_f32(in.logits + i), in.gmax), in.temp);
-        const float p = d < -16.0f ? 0.0f : l3m_expf_exact(d, in.elist, in.eindex);
+        const float p = d < -16.0f ? 0.0f : l3m_expf_exact(d, in.etab);
         in.probs[i] = p;
         if (p != p) nan = 1;
         else tsum += weight_units(p);
@@ -1198,7 +1198,7 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
         trace<TRACE>(a, tslot, pos, a.n_layers, 2);
         if (stop_after) break;                                            // logits kept, nothing sampled (uniform)
         if (a.temp > 0.0f) {                                              // every CTA of cluster 0, in step
-            const SampleIn in{a.logits + (size_t)pos * a.vocab, a.probs, a.vocab, a.temp, gmax_all, a.elist, a.eindex};
+            const SampleIn in{a.logits + (size_t)pos * a.vocab, a.probs, a.vocab, a.temp, gmax_all, a.etab};
             next = sample_token(in, s.xt + 4 + 4 * kClusterCtas, s.tmp, s.red, (float *)s.scratch, 2 * a.scratch_pairs, rng);
         }
         tok = next;
@@ -1231,8 +1231,7 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
 // One draw of the sampler on its own (tests): a single 16-CTA cluster over logits already on the
 // device; the maximum is found first (every CTA its slice, then an exchange).
 __global__ void __launch_bounds__(kDecodeThreads, 1) sample_kernel(const float *logits, float *probs, int vocab, float temp,
-                                                                  unsigned long long *rng_io, int *token, const uint32_t *elist,
-                                                                  const uint32_t *eindex) {
+                                                                  unsigned long long *rng_io, int *token, const uint32_t *etab) {
     __shared__ __align__(16) float xs[16 * kClusterCtas], xm[4 * kClusterCtas], tmp[4], red[64], stage[4096];
     const int rank = (int)cg::this_cluster().block_rank(), tid = threadIdx.x;
     const int lo = (int)((long long)rank * vocab / kClusterCtas), hi = (int)((long long)(rank + 1) * vocab / kClusterCtas);
@@ -1253,7 +1252,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) sample_kernel(const float *
     float gmax = -INFINITY;
     for (int c = 0; c < kClusterCtas; c++) gmax = fmaxf(gmax, xm[4 * c]);
     unsigned long long rng = *rng_io;
-    const SampleIn in{logits, probs, vocab, temp, gmax, elist, eindex};
+    const SampleIn in{logits, probs, vocab, temp, gmax, etab};
     const int t = sample_token(in, xs + 4, tmp, red, stage, 4096, rng);
     if (rank == 0 && tid == 0) { *token = t; *rng_io = rng; }
     cluster_sync();                                                       // no CTA leaves while others may write its memory
@@ -1338,7 +1337,7 @@ extern "C" int l3m_decode_smem_budget(void) {
     return budget;
 }
 
-extern "C" int l3m_expf_tables(const uint32_t **list, const uint32_t **index);
+extern "C" int l3m_expf_table(const uint32_t **table);
 extern "C" int l3m_error_msg(const char *msg);
 extern "C" int l3m_error_cuda(int e, const char *what);
 
@@ -1347,8 +1346,8 @@ extern "C" L3M_API int l3m_sample_dev(const float *logits, int vocab, float temp
                                       void *stream) {
     if (vocab <= 0 || !(temperature > 0.0f)) return l3m_error_msg("l3m_sample_dev: vocab > 0 and temperature > 0");
     if (!logits || !rng_state || !token || !scratch) return l3m_error_msg("l3m_sample_dev: logits, rng_state, token and scratch are required");
-    const uint32_t *list, *index;
-    if (l3m_expf_tables(&list, &index)) return -1;
+    const uint32_t *etab;
+    if (l3m_expf_table(&etab)) return -1;
     cudaError_t e = cudaFuncSetAttribute(l3m::sample_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e == cudaSuccess) {
         cudaLaunchConfig_t cfg = {};
@@ -1362,7 +1361,7 @@ extern "C" L3M_API int l3m_sample_dev(const float *logits, int vocab, float temp
         cfg.attrs = at;
         cfg.numAttrs = 1;
         e = cudaLaunchKernelEx(&cfg, l3m::sample_kernel, logits, scratch, vocab, temperature, (unsigned long long *)rng_state, (int *)token,
-                               list, index);
+                               etab);
     }
     return e == cudaSuccess ? 0 : l3m_error_cuda((int)e, "l3m_sample_dev");
 }

@@ -104,7 +104,7 @@ struct DecodeArgs {
     const float *pos_embed;             // [ctx][dim] learned positions (NULL: RoPE). Any of the three set: the
                                         // launch takes the kernel's GPT2 instance (only it reads them)
     const float2 *rope;                 // [ctx][hd/2] {cos, sin}
-    const uint32_t *elist, *eindex;     // libm expf exception list
+    const uint32_t *etab;               // libm expf exception set (hash table, expf_exact.h)
     const Role *roles;
     const int32_t *prompt;
     int n_prompt, max_new, eos, bos;

@@ -10,7 +10,7 @@
 #include <mutex>
 #include "../../include/l3m_kernels.h"
 
-extern "C" int l3m_expf_tables(const uint32_t **list, const uint32_t **index);
+extern "C" int l3m_expf_table(const uint32_t **table);
 
 namespace {
 

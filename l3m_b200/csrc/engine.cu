@@ -28,7 +28,7 @@
 extern "C" int l3m_decode_launch(const l3m::DecodeArgs *a, const l3m::DecodeArgs *a_dev, void *stream);
 extern "C" int l3m_decode_occupancy(int smem_bytes);
 extern "C" int l3m_decode_smem_budget(void);
-extern "C" int l3m_expf_tables(const uint32_t **list, const uint32_t **index);
+extern "C" int l3m_expf_table(const uint32_t **table);
 
 namespace {
 
@@ -451,7 +451,7 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     a.gelu = (m->flags & L3M_F_GELU) ? 1 : 0;
     a.pos_embed = (m->flags & L3M_F_LEARNED_POS) ? A(off_pos) : nullptr;
     a.rope = (m->flags & L3M_F_LEARNED_POS) ? nullptr : g.rope;
-    if (l3m_expf_tables(&a.elist, &a.eindex)) { fprintf(stderr, "l3m: %s\n", l3m_cuda_error()); return false; }
+    if (l3m_expf_table(&a.etab)) { fprintf(stderr, "l3m: %s\n", l3m_cuda_error()); return false; }
     a.trace_cta[0] = a.trace_cta[1] = -1;
     if (getenv("L3M_TRACE")) {                                         // phase time stamps of two CTAs: the first and the last
         a.trace_cta[0] = 0;

@@ -6,8 +6,9 @@
 // within about 2^-47 of a float rounding midpoint. The C library's expf is not always correctly
 // rounded; every input where the two differ lies within L3M_EXPF_WINDOW ulp of a midpoint (the
 // generator checks this over all 2^32 inputs). So: round the double result, and only when it falls
-// inside that window look the input up in a sorted exception list produced by running the C
-// library; a listed input takes the other float neighbour.
+// inside that window look the input up in the exceptions produced by running the C library (held
+// as an open-addressing hash set, so a lookup is usually one memory read); a listed input takes the
+// other float neighbour.
 //
 // Every operation is a single IEEE double operation (multiply, fused multiply-add, rint), so the
 // host and the device compute identical values. L3M_EXPF_HD marks functions for both compilers.
@@ -109,21 +110,55 @@ L3M_EXPF_HD float l3m_expf_candidate(float x, int *check, float *other) {
     return f;
 }
 
-// Binary search of a sorted list of input bit patterns; index[u >> 16] .. index[(u >> 16) + 1]
-// bounds the run sharing the top 16 bits.
-L3M_EXPF_HD int l3m_expf_listed(uint32_t u, const uint32_t *list, const uint32_t *index) {
-    uint32_t lo = index[u >> 16], hi = index[(u >> 16) + 1];
-    while (lo < hi) {
-        uint32_t mid = (lo + hi) >> 1, v = list[mid];
+// The exception set: 2^L3M_EXPF_HASH_BITS slots of input bit patterns, empty slots L3M_EXPF_EMPTY (a
+// NaN pattern, never listed), linear probing from l3m_expf_slot(u); the builder guarantees that every
+// probe sequence, for a listed input or not, ends within L3M_EXPF_PROBES slots.
+#define L3M_EXPF_HASH_BITS 19
+#define L3M_EXPF_SLOTS (1u << L3M_EXPF_HASH_BITS)
+#define L3M_EXPF_EMPTY 0xFFFFFFFFu
+#define L3M_EXPF_PROBES 64
+L3M_EXPF_HD uint32_t l3m_expf_slot(uint32_t u) { return (uint32_t)(u * 0x9E3779B1u) >> (32 - L3M_EXPF_HASH_BITS); }
+
+L3M_EXPF_HD int l3m_expf_listed(uint32_t u, const uint32_t *table) {
+    uint32_t i = l3m_expf_slot(u);
+    for (int p = 0; p < L3M_EXPF_PROBES; p++) {
+        const uint32_t v = table[i];
         if (v == u) return 1;
-        if (v < u) lo = mid + 1; else hi = mid;
+        if (v == L3M_EXPF_EMPTY) return 0;
+        i = (i + 1) & (L3M_EXPF_SLOTS - 1);
     }
     return 0;
 }
 
-L3M_EXPF_HD float l3m_expf_exact(float x, const uint32_t *list, const uint32_t *index) {
+#ifdef __CUDACC__
+#define L3M_EXPF_HOST static inline __host__
+#else
+#define L3M_EXPF_HOST static inline
+#endif
+// Host: fill table[L3M_EXPF_SLOTS] from the n listed inputs. Returns 0, or -1 when the set does not
+// fit (more inputs than half the slots, or a run of occupied slots reaching L3M_EXPF_PROBES).
+L3M_EXPF_HOST int l3m_expf_hash_build(const uint32_t *list, size_t n, uint32_t *table) {
+    if (n > L3M_EXPF_SLOTS / 2) return -1;
+    for (uint32_t i = 0; i < L3M_EXPF_SLOTS; i++) table[i] = L3M_EXPF_EMPTY;
+    for (size_t j = 0; j < n; j++) {
+        uint32_t i = l3m_expf_slot(list[j]);
+        while (table[i] != L3M_EXPF_EMPTY && table[i] != list[j]) i = (i + 1) & (L3M_EXPF_SLOTS - 1);
+        table[i] = list[j];
+    }
+    // Longest run of occupied slots (cyclic): every probe sequence ends at the empty slot after its run.
+    uint32_t run = 0, longest = 0, start = 0;
+    while (start < L3M_EXPF_SLOTS && table[start] != L3M_EXPF_EMPTY) start++;
+    for (uint32_t k = 1; k <= L3M_EXPF_SLOTS; k++) {
+        const uint32_t i = (start + k) & (L3M_EXPF_SLOTS - 1);
+        run = table[i] == L3M_EXPF_EMPTY ? 0 : run + 1;
+        if (run > longest) longest = run;
+    }
+    return longest + 1 < L3M_EXPF_PROBES ? 0 : -1;
+}
+
+L3M_EXPF_HD float l3m_expf_exact(float x, const uint32_t *table) {
     int check; float other;
     float f = l3m_expf_candidate(x, &check, &other);
-    if (check && l3m_expf_listed(l3m_f2u(x), list, index)) return other;
+    if (check && l3m_expf_listed(l3m_f2u(x), table)) return other;
     return f;
 }

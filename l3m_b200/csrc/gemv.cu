@@ -13,6 +13,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <vector>
 #include "ops.cuh"
 #include "../../include/l3m_kernels.h"
 
@@ -348,7 +349,7 @@ __global__ void __launch_bounds__(kThreads) prepare_kernel(int dtype, const floa
 }
 
 __global__ void __launch_bounds__(kThreads) attend_kernel(float *out, const float *q, const uint16_t *k, const uint16_t *v, int pos, int hd,
-                                                          int stride, const uint32_t *elist, const uint32_t *eindex) {
+                                                          int stride, const uint32_t *etab) {
     extern __shared__ __align__(16) unsigned char smem[];
     float *qs = (float *)smem, *o = qs + hd, *red = o + hd, *scores = red + 64;
     uint16_t *kcur = (uint16_t *)(scores + ((pos + 4) & ~3)), *vcur = kcur + hd, *kvbuf = vcur + hd;
@@ -358,7 +359,7 @@ __global__ void __launch_bounds__(kThreads) attend_kernel(float *out, const floa
         vcur[i] = v[(size_t)pos * stride + i];
     }
     __syncthreads();
-    attend_exact<false>(qs, k, v, stride, stride, kcur, vcur, pos, hd, scores, o, red, elist, eindex, kvbuf, nullptr, kAttnChunk, false);
+    attend_exact<false>(qs, k, v, stride, stride, kcur, vcur, pos, hd, scores, o, red, etab, kvbuf, nullptr, kAttnChunk, false);
     for (int i = threadIdx.x; i < hd; i += blockDim.x) out[i] = o[i];
 }
 
@@ -455,24 +456,22 @@ int grid_for(int ntiles) {
 // ---- expf exception list on the device (shared with the decode engine)
 #include "expf_exceptions.inc"
 
-extern "C" int l3m_expf_tables(const uint32_t **list, const uint32_t **index) {
+extern "C" int l3m_expf_table(const uint32_t **table) {
     static std::mutex mu;
-    static const uint32_t *d_list[64], *d_index[64];
+    static const uint32_t *d_table[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return fail_msg("no CUDA device");
     std::lock_guard<std::mutex> lock(mu);
-    if (!d_list[dev]) {
-        uint32_t *l = nullptr, *ix = nullptr;
-        cudaError_t e = cudaMalloc(&l, sizeof l3m_expf_list_host);
-        if (e == cudaSuccess) e = cudaMalloc(&ix, sizeof l3m_expf_index_host);
-        if (e == cudaSuccess) e = cudaMemcpy(l, l3m_expf_list_host, sizeof l3m_expf_list_host, cudaMemcpyHostToDevice);
-        if (e == cudaSuccess) e = cudaMemcpy(ix, l3m_expf_index_host, sizeof l3m_expf_index_host, cudaMemcpyHostToDevice);
-        if (e != cudaSuccess) return fail(e, "expf tables");
-        d_list[dev] = l;
-        d_index[dev] = ix;
+    if (!d_table[dev]) {
+        std::vector<uint32_t> h(L3M_EXPF_SLOTS);
+        if (l3m_expf_hash_build(l3m_expf_list_host, L3M_EXPF_LIST_N, h.data())) return fail_msg("expf exception set does not fit its table");
+        uint32_t *t = nullptr;
+        cudaError_t e = cudaMalloc(&t, h.size() * sizeof(uint32_t));
+        if (e == cudaSuccess) e = cudaMemcpy(t, h.data(), h.size() * sizeof(uint32_t), cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return fail(e, "expf table");
+        d_table[dev] = t;
     }
-    *list = d_list[dev];
-    *index = d_index[dev];
+    *table = d_table[dev];
     return 0;
 }
 
@@ -569,13 +568,13 @@ L3M_API int l3m_unpack_dev(int dtype, int8_t *q, float *d, const void *tiles, in
 L3M_API int l3m_attend_dev(float *out, const float *q, const uint16_t *k, const uint16_t *v, int pos, int head_dim, int stride, void *stream) {
     if (head_dim % 8 || head_dim <= 0 || pos < 0 || stride < head_dim) return fail_msg("l3m_attend_dev: bad arguments");
     if (!out || !q || !k || !v) return fail_msg("l3m_attend_dev: out, q, k and v are required");
-    const uint32_t *list, *index;
-    if (l3m_expf_tables(&list, &index)) return -1;
+    const uint32_t *etab;
+    if (l3m_expf_table(&etab)) return -1;
     size_t smem = (size_t)head_dim * 8 + 64 * 4 + (size_t)((pos + 4) & ~3) * 4 + (size_t)head_dim * 4 + 16 +
                   (size_t)kAttnChunk * (head_dim + 8) * 2;
     cudaError_t e = cudaFuncSetAttribute(attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return fail(e, "l3m_attend_dev");
-    attend_kernel<<<1, kThreads, smem, (cudaStream_t)stream>>>(out, q, k, v, pos, head_dim, stride, list, index);
+    attend_kernel<<<1, kThreads, smem, (cudaStream_t)stream>>>(out, q, k, v, pos, head_dim, stride, etab);
     e = cudaGetLastError();
     return e == cudaSuccess ? 0 : fail(e, "l3m_attend_dev");
 }

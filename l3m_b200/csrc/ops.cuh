@@ -563,8 +563,8 @@ __device__ inline void rope_exact(float *v, int hd, const float2 *cs) {
 
 // One out-of-line copy for every caller (attention's softmax, the SiLU gate): code size matters more
 // than a call here.
-static __device__ __noinline__ float expf_libm(float x, const uint32_t *list, const uint32_t *index) {
-    return l3m_expf_exact(x, list, index);
+static __device__ __noinline__ float expf_libm(float x, const uint32_t *tab) {
+    return l3m_expf_exact(x, tab);
 }
 
 // ---- one head of attention at position pos (reference src/ops.c:42-47, 58-73).
@@ -811,8 +811,8 @@ __device__ __forceinline__ float vmix_col(const uint16_t *col, const float *pp, 
 
 template <bool VT>
 __device__ __noinline__ void attend_exact(const float *q, const uint16_t *kc, const uint16_t *vc, int kstride, int vstride, const uint16_t *kcur,
-                             const uint16_t *vcur, int pos, int hd, float *scores, float *out, float *red, const uint32_t *elist,
-                             const uint32_t *eindex, uint16_t *kvbuf, uint16_t *vtbuf, int chunk, bool prestaged) {
+                             const uint16_t *vcur, int pos, int hd, float *scores, float *out, float *red, const uint32_t *etab,
+                             uint16_t *kvbuf, uint16_t *vtbuf, int chunk, bool prestaged) {
     const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31, warp = tid >> 5;
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
     const bool kvec = kstride % 8 == 0 && ((uintptr_t)kc & 15) == 0;
@@ -849,12 +849,15 @@ __device__ __noinline__ void attend_exact(const float *q, const uint16_t *kc, co
     m = warp_max_f32(m);
     if (lane == 0) red[warp] = m;
     __syncthreads();
-    float mx = -INFINITY;
+    float mx = -INFINITY;                                    // warp count a multiple of 4 (red 16-byte aligned)
 #pragma unroll 1
-    for (int w = 0; w < (nth >> 5); w++) mx = fmaxf(mx, red[w]);
+    for (int w = 0; w < (nth >> 5); w += 4) {
+        const float4 r = *(const float4 *)(red + w);
+        mx = fmaxf(mx, fmaxf(fmaxf(r.x, r.y), fmaxf(r.z, r.w)));
+    }
     if (scores[0] != scores[0]) mx = scores[0];
 #pragma unroll 1
-    for (int t = tid; t < n; t += nth) scores[t] = expf_libm(__fsub_rn(scores[t], mx), elist, eindex);
+    for (int t = tid; t < n; t += nth) scores[t] = expf_libm(__fsub_rn(scores[t], mx), etab);
     __syncthreads();
     if (tid == 0) red[32] = seq_sum<false>(scores, n);      // the sequential sum
     __syncthreads();
@@ -893,8 +896,8 @@ __device__ __noinline__ void attend_exact(const float *q, const uint16_t *kc, co
 }
 
 // SiLU gate (reference src/ops.c:49-51): h * (g / (1 + expf(-g))).
-__device__ __forceinline__ float silu_mul(float h, float g, const uint32_t *elist, const uint32_t *eindex) {
-    return __fmul_rn(h, __fdiv_rn(g, __fadd_rn(1.0f, expf_libm(-g, elist, eindex))));
+__device__ __forceinline__ float silu_mul(float h, float g, const uint32_t *etab) {
+    return __fmul_rn(h, __fdiv_rn(g, __fadd_rn(1.0f, expf_libm(-g, etab))));
 }
 
 }  // namespace l3m
