@@ -160,6 +160,17 @@ __device__ __forceinline__ void trace(const DecodeArgs &a, int slot, int pos, in
     }
 }
 
+// This CTA's share of the expf exception table into L2 with an evict-last policy (one thread; the
+// table's size is a multiple of 16 bytes per CTA share rounding, and its base 256-byte aligned).
+__device__ __noinline__ void prefetch_expf_table(const uint32_t *table, int cta, int ncta) {
+    const uint32_t units = L3M_EXPF_SLOTS * 4 / 16, u0 = (uint32_t)((uint64_t)units * cta / ncta), u1 = (uint32_t)((uint64_t)units * (cta + 1) / ncta);
+    if (u1 <= u0) return;
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"((const char *)table + 16ull * u0), "r"(16 * (u1 - u0)), "l"(pol)
+                 : "memory");
+}
+
 // Pull a CTA's weight tiles into L2 ahead of use (cp.async.bulk.prefetch: no registers, no
 // completion to wait for). Every tile range is 16-byte aligned and a multiple of 16 bytes.
 __device__ __forceinline__ void prefetch_l2(const void *p, size_t bytes) {
@@ -234,22 +245,26 @@ __device__ __noinline__ void bulk_copy(uint32_t dst, const uint8_t *src, uint32_
     }
 }
 
+// Thread kPrefetchThread: copy tiles [t0, t0 + n) of a matrix of dtype with k inputs to dst, completing
+// on the staging mbarrier. Quantised tiles go as one contiguous copy, f32/bf16 tiles one copy each at
+// the padded stride. cold: with an L2 evict-first policy.
+__device__ __noinline__ void stage_copy(const Smem &s, int dtype, const uint8_t *tiles, int k, int t0, int n, uint8_t *dst, int cold) {
+    const size_t tb = tile_bytes(dtype, k), sst = staged_stride(dtype, k);
+    const uint32_t bar = smem_addr(s.wbar);
+    const uint8_t *src = tiles + (size_t)t0 * tb;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"((uint32_t)(n * tb)) : "memory");
+    if (sst == tb) bulk_copy(smem_addr(dst), src, (uint32_t)(n * tb), bar, cold);
+    else
+        for (int i = 0; i < n; i++) bulk_copy(smem_addr(dst + i * sst), src + i * tb, (uint32_t)tb, bar, cold);
+}
+
 // Every thread, after a __syncthreads that ends every read of dst: start the copy of tiles
 // [t0, t0 + n) to dst, n = min(t1 - t0, cap) where cap is how many tiles fit (precomputed per matrix
-// by the host); returns n. Quantised tiles go as one contiguous copy, f32/bf16 tiles one copy each at
-// the padded stride. cold: with an L2 evict-first policy.
-__device__ __noinline__ int stage_issue(const Smem &s, int dtype, const uint8_t *tiles, int k, int t0, int t1, uint8_t *dst, int cap,
-                                       int cold = 0) {
+// by the host); returns n. Only the issuing thread leaves the caller's code.
+__device__ __forceinline__ int stage_issue(const Smem &s, int dtype, const uint8_t *tiles, int k, int t0, int t1, uint8_t *dst, int cap,
+                                           int cold = 0) {
     const int n = t1 > t0 ? min(t1 - t0, cap) : 0;
-    if (n > 0 && threadIdx.x == kPrefetchThread) {
-        const size_t tb = tile_bytes(dtype, k), sst = staged_stride(dtype, k);
-        const uint32_t bar = smem_addr(s.wbar);
-        const uint8_t *src = tiles + (size_t)t0 * tb;
-        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"((uint32_t)(n * tb)) : "memory");
-        if (sst == tb) bulk_copy(smem_addr(dst), src, (uint32_t)(n * tb), bar, cold);
-        else
-            for (int i = 0; i < n; i++) bulk_copy(smem_addr(dst + i * sst), src + i * tb, (uint32_t)tb, bar, cold);
-    }
+    if (n > 0 && threadIdx.x == kPrefetchThread) stage_copy(s, dtype, tiles, k, t0, n, dst, cold);
     return n;
 }
 
@@ -426,10 +441,9 @@ __device__ __noinline__ void phase_qkv(const DecodeArgs &a, const LayerDev &L, c
                                        int l, int tslot) {
     PreStage ps{};
     if (role.head0 >= 0) ps = PreStage{kcache(a, L, role.head0), vcache(a, L, role.head0), a.hd, a.vstride, pos, a.hd, s.kvbuf, s.vtbuf, a.attn_chunk};
-    if (GPT2 && a.layernorm) layernorm_exact(s.x, s.wa, s.wab, a.dim, a.eps, s.xb, s.red, ps);
-    else rmsnorm_exact(s.x, s.wa, a.dim, a.eps, s.xb, s.red, ps);
+    if (GPT2 && a.layernorm) layernorm_exact(s.x, s.wa, s.wab, a.dim, a.eps, s.xb, s.red, ps, L.dt_qkv, s.prep);
+    else rmsnorm_exact(s.x, s.wa, a.dim, a.eps, s.xb, s.red, ps, L.dt_qkv, s.prep);   // and prepare
     trace<TRACE>(a, tslot, pos, l, 16);
-    prepare(L.dt_qkv, s.xb, a.dim, s.prep);
     trace<TRACE>(a, tslot, pos, l, 17);
     if (ns) stage_wait(a, s, par, pos, l);
     trace<TRACE>(a, tslot, pos, l, 18);
@@ -455,28 +469,33 @@ __device__ __noinline__ void phase_attention(const DecodeArgs &a, const LayerDev
                                              int tslot) {
     const int tid = threadIdx.x, nth = blockDim.x, hd = a.hd, hl = h - a.sh.head_lo, kvl = h / a.hpk - a.sh.kv_lo;
     const int nq = a.sh.n_heads_g * hd, nk = a.sh.n_kv_g * hd;
-    float *y = s.y;                                                  // q, k, v of this head
-    #pragma unroll 1
-    for (int i = tid; i < hd; i += nth) {
-        y[i] = s.xq[hl * hd + i];
-        y[hd + i] = s.xq[nq + kvl * hd + i];
-        y[2 * hd + i] = s.xq[nq + nk + kvl * hd + i];
-    }
-    __syncthreads();
-    if (a.rope) {
-        rope_exact(y, hd, s.rope);
-        rope_exact(y + hd, hd, s.rope);
-    }
+    // q of this head (rotated) into y, k and v rows (rotated k) as bf16 into kcur / vcur and, by the
+    // writer, into the cache: one pass, thread i taking input pair i (reference src/ops.c:29-40).
+    float *y = s.y;
+    const float *qs = s.xq + hl * hd, *ks = s.xq + nq + kvl * hd, *vs = s.xq + nq + nk + kvl * hd;
     uint16_t *kc = (uint16_t *)kcache(a, L, h), *vc = (uint16_t *)vcache(a, L, h);
     const bool writer = h % a.hpk == 0 || h == a.sh.head_lo;
-    #pragma unroll 1
-    for (int i = tid; i < hd; i += nth) {
-        const uint16_t kb = l3m_f32_to_bf16(y[hd + i]), vb = l3m_f32_to_bf16(y[2 * hd + i]);
-        s.kcur[i] = kb;
-        s.vcur[i] = vb;
+#pragma unroll 1
+    for (int i = tid; i < hd / 2; i += nth) {
+        float q0 = qs[2 * i], q1 = qs[2 * i + 1], k0 = ks[2 * i], k1 = ks[2 * i + 1];
+        if (a.rope) {
+            const float2 c = s.rope[i];
+            const float rq0 = __fmaf_rn(q0, c.x, -__fmul_rn(q1, c.y)), rq1 = __fmaf_rn(q0, c.y, __fmul_rn(q1, c.x));
+            const float rk0 = __fmaf_rn(k0, c.x, -__fmul_rn(k1, c.y)), rk1 = __fmaf_rn(k0, c.y, __fmul_rn(k1, c.x));
+            q0 = rq0; q1 = rq1; k0 = rk0; k1 = rk1;
+        }
+        y[2 * i] = q0;
+        y[2 * i + 1] = q1;
+        const uint16_t kb0 = l3m_f32_to_bf16(k0), kb1 = l3m_f32_to_bf16(k1);
+        const uint16_t vb0 = l3m_f32_to_bf16(vs[2 * i]), vb1 = l3m_f32_to_bf16(vs[2 * i + 1]);
+        s.kcur[2 * i] = kb0;
+        s.kcur[2 * i + 1] = kb1;
+        s.vcur[2 * i] = vb0;
+        s.vcur[2 * i + 1] = vb1;
         if (writer) {
-            kc[(size_t)pos * hd + i] = kb;
-            vc[(size_t)i * a.vstride + pos] = vb;
+            *(uint32_t *)(kc + (size_t)pos * hd + 2 * i) = (uint32_t)kb0 | (uint32_t)kb1 << 16;
+            vc[(size_t)(2 * i) * a.vstride + pos] = vb0;
+            vc[(size_t)(2 * i + 1) * a.vstride + pos] = vb1;
         }
     }
     __syncthreads();
@@ -516,11 +535,10 @@ __device__ __noinline__ void phase_ffn(const DecodeArgs &a, const LayerDev &L, c
     for (int i = threadIdx.x; i < a.dim; i += blockDim.x) s.x[i] = __fadd_rn(s.x[i], s.xp[i]);
     __syncthreads();
     if (role.ffn0 >= role.ffn1) return;
-    if (GPT2 && a.layernorm) layernorm_exact(s.x, s.wf, s.wfb, a.dim, a.eps, s.xb, s.red);
-    else rmsnorm_exact(s.x, s.wf, a.dim, a.eps, s.xb, s.red);
+    if (GPT2 && a.layernorm) layernorm_exact(s.x, s.wf, s.wfb, a.dim, a.eps, s.xb, s.red, PreStage{}, L.dt_up, s.prep);
+    else rmsnorm_exact(s.x, s.wf, a.dim, a.eps, s.xb, s.red, PreStage{}, L.dt_up, s.prep);   // and prepare
     trace<TRACE>(a, tslot, pos, l, 7);
     const int nf = role.ffn1 - role.ffn0;
-    prepare(L.dt_up, s.xb, a.dim, s.prep);
     trace<TRACE>(a, tslot, pos, l, 26);
     if (ns) stage_wait(a, s, par, pos, l);
     trace<TRACE>(a, tslot, pos, l, 12);
@@ -771,10 +789,9 @@ __device__ __noinline__ void head_logits(const DecodeArgs &a, const Role &role, 
     float best = -INFINITY;
     int best_i = -1;
     if (role.voc0 < role.voc1) {
-        if (GPT2 && a.layernorm) layernorm_exact(s.x, s.wh, s.whb, a.dim, a.eps, s.xb, s.red);
-        else rmsnorm_exact(s.x, s.wh, a.dim, a.eps, s.xb, s.red);
+        if (GPT2 && a.layernorm) layernorm_exact(s.x, s.wh, s.whb, a.dim, a.eps, s.xb, s.red, PreStage{}, a.dt_head, s.prep);
+        else rmsnorm_exact(s.x, s.wh, a.dim, a.eps, s.xb, s.red, PreStage{}, a.dt_head, s.prep);   // and prepare
         trace<TRACE>(a, tslot, pos, a.n_layers, 3);
-        prepare(a.dt_head, s.xb, a.dim, s.prep);
         trace<TRACE>(a, tslot, pos, a.n_layers, 4);
         matvec_exact(a.dt_head, a.head, a.dim, role.voc0, role.voc1, s.prep, s.scratch, a.scratch_pairs, s.y, staged, ns);
         trace<TRACE>(a, tslot, pos, a.n_layers, 5);
@@ -1072,6 +1089,7 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
     if (threadIdx.x == 0) {
         sh_args = *ap;
         sh_role = ap->roles[blockIdx.x];
+        prefetch_expf_table(ap->etab, blockIdx.x, gridDim.x);
     }
     __syncthreads();
     const DecodeArgs &a = sh_args;

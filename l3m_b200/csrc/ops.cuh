@@ -47,43 +47,49 @@ struct Prep {
 };
 
 // ---- prepare (reference src/pack.c:101-122)
+// One quantisation step: the 8 lanes j = 0..7 of a warp's quarter hold the 4 values each of one
+// 32-input block b (lanes with ok false hold zeros and store nothing); every lane of the warp calls.
+__device__ __forceinline__ void quant_block4(const float4 v, int b, int j, bool ok, const Prep &p) {
+    const float a0 = fabsf(v.x), a1 = fabsf(v.y), a2 = fabsf(v.z), a3 = fabsf(v.w);
+    // a NaN never raises the maximum; the maximum of the rest is order-free
+    float m = fmaxf(fmaxf(a0 > 0.0f ? a0 : 0.0f, a1 > 0.0f ? a1 : 0.0f), fmaxf(a2 > 0.0f ? a2 : 0.0f, a3 > 0.0f ? a3 : 0.0f));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    const float inv = m > 0.0f ? __fdiv_rn(127.0f, m) : 0.0f;
+    const int q0 = (int8_t)__float2int_rn(__fmul_rn(v.x, inv)), q1 = (int8_t)__float2int_rn(__fmul_rn(v.y, inv));
+    const int q2 = (int8_t)__float2int_rn(__fmul_rn(v.z, inv)), q3 = (int8_t)__float2int_rn(__fmul_rn(v.w, inv));
+    int sm = q0 + q1 + q2 + q3;
+    sm += __shfl_xor_sync(0xffffffffu, sm, 4);
+    sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+    sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+    if (ok) {
+        ((uint32_t *)(p.q8 + b * kQB))[j] = (uint32_t)(q0 & 0xFF) | (uint32_t)(q1 & 0xFF) << 8 | (uint32_t)(q2 & 0xFF) << 16 | (uint32_t)(q3 & 0xFF) << 24;
+        if (j == 0) {
+            p.scale[b] = __fdiv_rn(m, 127.0f);
+            p.sum[b] = sm;
+        }
+    }
+}
+
 static __device__ __noinline__ void prepare(int dtype, const float *x, int n, const Prep p) {
     const int tid = threadIdx.x, nth = blockDim.x;
     if (dtype == DT_F32) {
-        #pragma unroll 1
+#pragma unroll 1
         for (int i = tid; i < n; i += nth) p.xf[i] = x[i];
     } else if (dtype == DT_BF16) {
-        #pragma unroll 1
+#pragma unroll 1
         for (int i = tid; i < n; i += nth) p.xf[i] = l3m_bf16_to_f32(l3m_f32_to_bf16(x[i]));
     } else {
         // 8 threads per 32-input block, 4 inputs each (x 16-byte aligned in shared memory); a warp takes
         // 4 blocks per step and every lane of it runs every step, so the shuffles always see the whole warp.
         const int j = tid & 7, sub = (tid & 31) >> 3, nblk = n / kQB;
-        #pragma unroll 1
+#pragma unroll 1
         for (int b0 = (tid >> 5) * 4; b0 < nblk; b0 += (nth >> 5) * 4) {
             const int b = b0 + sub;
             const bool ok = b < nblk;
             const float4 v = ok ? ((const float4 *)(x + b * kQB))[j] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            const float a0 = fabsf(v.x), a1 = fabsf(v.y), a2 = fabsf(v.z), a3 = fabsf(v.w);
-            // a NaN never raises the maximum; the maximum of the rest is order-free
-            float m = fmaxf(fmaxf(a0 > 0.0f ? a0 : 0.0f, a1 > 0.0f ? a1 : 0.0f), fmaxf(a2 > 0.0f ? a2 : 0.0f, a3 > 0.0f ? a3 : 0.0f));
-            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
-            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-            const float inv = m > 0.0f ? __fdiv_rn(127.0f, m) : 0.0f;
-            const int q0 = (int8_t)__float2int_rn(__fmul_rn(v.x, inv)), q1 = (int8_t)__float2int_rn(__fmul_rn(v.y, inv));
-            const int q2 = (int8_t)__float2int_rn(__fmul_rn(v.z, inv)), q3 = (int8_t)__float2int_rn(__fmul_rn(v.w, inv));
-            int sm = q0 + q1 + q2 + q3;
-            sm += __shfl_xor_sync(0xffffffffu, sm, 4);
-            sm += __shfl_xor_sync(0xffffffffu, sm, 2);
-            sm += __shfl_xor_sync(0xffffffffu, sm, 1);
-            if (ok) {
-                ((uint32_t *)(p.q8 + b * kQB))[j] = (uint32_t)(q0 & 0xFF) | (uint32_t)(q1 & 0xFF) << 8 | (uint32_t)(q2 & 0xFF) << 16 | (uint32_t)(q3 & 0xFF) << 24;
-                if (j == 0) {
-                    p.scale[b] = __fdiv_rn(m, 127.0f);
-                    p.sum[b] = sm;
-                }
-            }
+            quant_block4(v, b, j, ok, p);
         }
     }
     __syncthreads();
@@ -478,9 +484,42 @@ __device__ __forceinline__ void side_prestage(const PreStage &ps) {
     if (ps.kc && threadIdx.x >= 32)
         attend_prestage<true>(ps.kc, ps.vc, ps.kstride, ps.vstride, ps.pos, ps.hd, ps.kvbuf, ps.vtbuf, ps.chunk, threadIdx.x - 32, blockDim.x - 32);
 }
-static __device__ __noinline__ void rmsnorm_exact(const float *x, const float *w, int n, float eps, float *y, float *red,
-                                                  const PreStage ps = PreStage{}) {
+// The normalised vector's epilogue: y[i] = f(i) for i < n, and when pdt >= 0 the activation that a
+// matrix of dtype pdt multiplies (prepare's output, from the same y values) in the same pass. f(i)
+// is computed from 4 consecutive elements at a time when n is a multiple of 32 (quantised: 8 lanes per
+// block, as prepare), else one element at a time.
+template <class F>
+__device__ __forceinline__ void norm_out(int n, float *y, int pdt, const Prep &p, const F &f) {
     const int tid = threadIdx.x, nth = blockDim.x;
+    if (pdt >= DT_Q8 && n % kQB == 0) {
+        const int j = tid & 7, sub = (tid & 31) >> 3, nblk = n / kQB;
+#pragma unroll 1
+        for (int b0 = (tid >> 5) * 4; b0 < nblk; b0 += (nth >> 5) * 4) {
+            const int b = b0 + sub;
+            const bool ok = b < nblk;
+            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (ok) {
+                const int i = b * kQB + 4 * j;
+                v = make_float4(f(i), f(i + 1), f(i + 2), f(i + 3));
+                *(float4 *)(y + i) = v;
+            }
+            quant_block4(v, b, j, ok, p);
+        }
+    } else {
+#pragma unroll 1
+        for (int i = tid; i < n; i += nth) {
+            const float v = f(i);
+            y[i] = v;
+            if (pdt == DT_F32) p.xf[i] = v;
+            else if (pdt == DT_BF16) p.xf[i] = l3m_bf16_to_f32(l3m_f32_to_bf16(v));
+        }
+    }
+}
+
+// pdt, p: also prepare the output for a matrix of dtype pdt (-1: do not).
+static __device__ __noinline__ void rmsnorm_exact(const float *x, const float *w, int n, float eps, float *y, float *red, const PreStage ps = PreStage{},
+                                                  int pdt = -1, const Prep p = Prep{}) {
+    const int tid = threadIdx.x;
     if (tid == 0) {
         const int split = fused_from(n);
         float ss = seq_sum<true>(x, split);
@@ -492,8 +531,7 @@ static __device__ __noinline__ void rmsnorm_exact(const float *x, const float *w
     }
     __syncthreads();
     const float sc = *red;
-#pragma unroll 1
-    for (int i = tid; i < n; i += nth) y[i] = __fmul_rn(__fmul_rn(x[i], sc), w[i]);
+    norm_out(n, y, pdt, p, [&](int i) { return __fmul_rn(__fmul_rn(x[i], sc), w[i]); });
     __syncthreads();
 }
 
@@ -524,8 +562,8 @@ __device__ __forceinline__ float chain_var(const float *v, float mean, int n, in
 // LayerNorm (reference src/ops.c:20-27): sequential mean, the variance chain above, s = 1/sqrt(var/n
 // + eps), y = fma((x - mean) * s, w, b). Thread 0 runs the chains; ps as in rmsnorm_exact.
 static __device__ __noinline__ void layernorm_exact(const float *x, const float *w, const float *b, int n, float eps, float *y, float *red,
-                                                    const PreStage ps = PreStage{}) {
-    const int tid = threadIdx.x, nth = blockDim.x;
+                                                    const PreStage ps = PreStage{}, int pdt = -1, const Prep p = Prep{}) {
+    const int tid = threadIdx.x;
     if (tid == 0) {
         const float mean = __fdiv_rn(seq_sum<false>(x, n), (float)n);
         const float var = chain_var(x, mean, n, fused_from(n));
@@ -536,8 +574,7 @@ static __device__ __noinline__ void layernorm_exact(const float *x, const float 
     }
     __syncthreads();
     const float mean = red[0], sc = red[1];
-#pragma unroll 1
-    for (int i = tid; i < n; i += nth) y[i] = __fmaf_rn(__fmul_rn(__fsub_rn(x[i], mean), sc), w[i], b[i]);
+    norm_out(n, y, pdt, p, [&](int i) { return __fmaf_rn(__fmul_rn(__fsub_rn(x[i], mean), sc), w[i], b[i]); });
     __syncthreads();
 }
 
