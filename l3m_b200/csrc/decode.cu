@@ -764,7 +764,7 @@ __device__ __noinline__ int wait_word(const DecodeArgs &a, const uint32_t *p, ui
             const uint32_t v = ld_acquire_u32(p);
             if (done_ok && v == kHeadDone) { r = 0; break; }
             if (v >= want && v != kHeadDone) { r = 1; break; }
-            __nanosleep(done_ok ? 256 : 64);
+            __nanosleep(32);
             if ((spins & 255) == 255) {
                 if (globaltimer_ns() - t0 > a.hx.timeout_ns) { record_abort(a, kErrTimeout, pos, -1, wait); break; }
                 if (aborted(a)) break;
@@ -899,8 +899,8 @@ __device__ __noinline__ void gpu_vote(const DecodeArgs &a, const Smem &s, uint32
 // fit in the whole staging area are copied in once, at launch, and stay there for every position;
 // the rest are pulled into L2 ahead of each use (cold: every tile, every position). Ends when
 // cluster 0 writes kHeadDone (or on a failed wait).
-template <bool GPT2>
-__device__ __noinline__ void head_helper(const DecodeArgs &a, const Role &role, const Smem &s, int cold) {
+template <bool GPT2, bool TRACE>
+__device__ __noinline__ void head_helper(const DecodeArgs &a, const Role &role, const Smem &s, int cold, int tslot) {
     stage_init(s);
     const int nres = cold ? 0 : stage_issue(s, a.dt_head, a.head, a.dim, role.voc0, role.voc1, s.w, a.st_head);   // cold: read each time
     const size_t th = tile_bytes(a.dt_head, a.dim);
@@ -922,7 +922,9 @@ __device__ __noinline__ void head_helper(const DecodeArgs &a, const Role &role, 
             landed = true;
         }
         __syncthreads();
-        head_logits<GPT2, false>(a, role, s, pos, 0, -1, s.w, nres);
+        trace<TRACE>(a, tslot, pos, a.n_layers, 0);
+        head_logits<GPT2, TRACE>(a, role, s, pos, 0, tslot, s.w, nres);
+        trace<TRACE>(a, tslot, pos, a.n_layers, 1);
         if (rest0 < role.voc1 && threadIdx.x == 0) prefetch_l2(a.head + rest0 * th, (size_t)(role.voc1 - rest0) * th);
     }
     if (!landed) stage_wait(a, s, 0, -1, -1, true);                       // no copy outlives the CTA
@@ -1117,7 +1119,7 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
     }
     if (cta >= kClusterCtas) {                                            // the other clusters: head tiles only
         cp_async_commit();
-        head_helper<GPT2>(a, role, s, a.cold);
+        head_helper<GPT2, TRACE>(a, role, s, a.cold, tslot);
         cp_async_wait_all();
         return;
     }
@@ -1168,20 +1170,29 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
             scatter(s.tmp, s.xt, 4 + 4 * cta, 4);
         } else if (cta == 0) {
             const int r = wait_word(a, a.hx.count, tcount * (uint32_t)a.grid, false, pos, kWaitHeadCount);
-            float *sl = s.tmp + 4;                                        // every slot at once, then a serial scan
-            #pragma unroll 1
-            for (int i = tid; i < 3 * a.grid; i += blockDim.x) sl[i] = ld_cg_f32(a.hx.slots + i);
-            __syncthreads();
-            if (tid == 0) {
-                float gmax = -INFINITY;
-                int next = 0;
-                for (int c = 0; c < a.grid; c++) {
-                    if (sl[3 * c] > gmax) { gmax = sl[3 * c]; next = __float_as_int(sl[3 * c + 1]); }
+            // Warp 0 reduces the slots: the first CTA (in CTA order, the vocabulary order) with the
+            // largest maximum; a slot whose maximum is not above -inf (an empty or all-NaN slice) never
+            // wins, and with no winner the token is 0 (the serial rule gmax = -inf; if (m > gmax) ...).
+            if (tid < 32) {
+                float bm = -INFINITY;
+                int bc = a.grid;
+#pragma unroll 1
+                for (int c = tid; c < a.grid; c += 32) {                  // increasing c: strict > keeps the first
+                    const float m = ld_cg_f32(a.hx.slots + 3 * c);
+                    if (m > bm) { bm = m; bc = c; }
                 }
-                s.tmp[0] = __int_as_float(next);
-                s.tmp[1] = sl[2];
-                s.tmp[2] = __int_as_float(r > 0 && !*(volatile int *)a.hx.abort_flag ? 1 : 0);
-                s.tmp[3] = gmax;
+#pragma unroll
+                for (int o = 16; o; o >>= 1) {
+                    const float om = __shfl_xor_sync(0xffffffffu, bm, o);
+                    const int oc = __shfl_xor_sync(0xffffffffu, bc, o);
+                    if (om > bm || (om == bm && oc < bc)) { bm = om; bc = oc; }
+                }
+                if (tid == 0) {
+                    s.tmp[0] = __int_as_float(bc < a.grid ? __float_as_int(ld_cg_f32(a.hx.slots + 3 * bc + 1)) : 0);
+                    s.tmp[1] = ld_cg_f32(a.hx.slots + 2);
+                    s.tmp[2] = __int_as_float(r > 0 && !*(volatile int *)a.hx.abort_flag ? 1 : 0);
+                    s.tmp[3] = bm;
+                }
             }
             __syncthreads();
             scatter(s.tmp, s.xt, 0, 4);

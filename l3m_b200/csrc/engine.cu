@@ -399,8 +399,8 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     // query heads round-robin over the CTAs.
     const int Td = sr.d_hi - sr.d_lo, Tf = sr.f_hi - sr.f_lo, Tv = sr.v_hi - sr.v_lo, Tq = tiles_of(n_qkv_g);   // this GPU's tiles
     // Roles for a grid of gt CTAs; the shared-memory layout is sized for the largest share (gt = G).
-    // helpers_only: the head's tiles go to the helper clusters alone (when they can keep every one
-    // resident in shared memory), else to every CTA.
+    // helpers_only: the head's tiles go to the helper clusters alone (they keep as many as fit resident
+    // in shared memory), else to every CTA.
     auto make_roles = [&](int gt, bool helpers_only = false) {
         std::vector<l3m::Role> rs(gt);
         for (int c = 0; c < gt; c++) {
@@ -453,9 +453,9 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     a.rope = (m->flags & L3M_F_LEARNED_POS) ? nullptr : g.rope;
     if (l3m_expf_table(&a.etab)) { fprintf(stderr, "l3m: %s\n", l3m_cuda_error()); return false; }
     a.trace_cta[0] = a.trace_cta[1] = -1;
-    if (getenv("L3M_TRACE")) {                                         // phase time stamps of two CTAs: the first and the last
+    if (getenv("L3M_TRACE")) {                                         // phase time stamps of two CTAs: the first and a helper
         a.trace_cta[0] = 0;
-        a.trace_cta[1] = G - 1;
+        a.trace_cta[1] = GT > G ? G : G - 1;                            // a helper's head, when there are helpers
         g.trace_bytes = (size_t)2 * m->ctx * (L + 1) * l3m::kTraceEvents * sizeof(unsigned long long);
         if (!cuda_ok(cudaMalloc(&g.trace, g.trace_bytes), "trace")) return false;
         cudaMemset(g.trace, 0, g.trace_bytes);
@@ -552,9 +552,10 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
         return false;
     }
     a.grid = GT;
-    // The helper clusters keep their head tiles in shared memory (decode.cu head_helper): when all of
-    // them fit there, cluster 0 takes none and goes straight from the last layer to the token vote.
-    const bool helpers_only = GT > G && !m->cold && (long long)a.st_head * (GT - G) >= Tv;
+    // The helper clusters keep their head tiles in shared memory (decode.cu head_helper), so unless the
+    // weights are read cold, cluster 0 takes none and goes straight from the last layer to the token
+    // vote (its own tiles would come from L2 and finish last).
+    const bool helpers_only = GT > G && !m->cold;
     a.async_x = !getenv("L3M_CLUSTER_BARRIERS");                        // every CTA of cluster 0 must produce qkv rows
     {
         std::vector<l3m::Role> rs0 = make_roles(GT, helpers_only);

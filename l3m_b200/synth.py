@@ -10,6 +10,7 @@ Weights follow the recipe of the benchmark configurations: N(0, 0.02) fp32 tenso
 order from numpy.random.default_rng(seed), norm gains 1.0, a byte-level tokenizer (256 bytes, <s>,
 </s>, empty pieces up to vocab), then quantised per 32-element block by the file dtype.
 """
+import os
 import struct
 from dataclasses import dataclass, field
 from pathlib import Path
@@ -238,10 +239,12 @@ def make(name, out_dir, ctx=None, stop_tokens=False, seed=0):
         shape["ctx"] = ctx
     out = Path(out_dir) / f"{name}-ctx{shape['ctx']}{'-stop' if stop_tokens else ''}-s{seed}.l3m"
     if not out.exists():
+        # Several processes (the ranks of one job) may build the same file at once: each writes its own
+        # temporary file and moves it into place atomically (the contents are identical).
         out.parent.mkdir(parents=True, exist_ok=True)
-        tmp = out.with_suffix(".tmp")
+        tmp = out.with_suffix(f".{os.getpid()}.tmp")
         write(llama(**shape, seed=seed, stop_tokens=stop_tokens), dtype, head_dtype, tmp)
-        tmp.rename(out)
+        os.replace(tmp, out)
     return out
 
 

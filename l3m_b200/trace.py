@@ -4,9 +4,9 @@
 
 Runs one greedy generation (the bench workload: the config's context, a 4-token prompt, the rest
 generated) of a synthetic model through ``l3m_b200.Model`` with tracing on, then prints for the two
-traced CTAs (the first and the last of cluster 0) the median time, over layers and over the
-positions from 50 on, of every traced event after the layer's start, then the layer and token
-periods and the head phase. Times are SM cycles converted at the clock the header records (the
+traced CTAs (CTA 0 of the layer cluster, and the first helper CTA, or the last CTA of the layer
+cluster when the launch has no helpers) the median time, over layers and over the positions from 50
+on, of every traced event after the layer's start, the layer and token periods, and the head step. Times are SM cycles converted at the clock the header records (the
 maximum SM clock; the bench's clock samples show the part runs there under this load).
 """
 import argparse
@@ -26,7 +26,7 @@ LAYER_EVENTS = {
     23: "D   prepare", 24: "D   weight copy waited", 25: "D   matvec", 30: "D   next copy issued", 10: "D   exchanged",
     11: "    barrier 5, x += down (layer end)",
 }
-HEAD_EVENTS = {3: "rmsnorm", 4: "prepare", 5: "matvec", 1: "argmax slots", 2: "token agreed"}
+HEAD_EVENTS = {3: "rmsnorm + prepare", 4: "-", 5: "matvec", 1: "argmax slot", 2: "token agreed"}
 
 
 def summarize(path, first=50):
@@ -45,12 +45,15 @@ def summarize(path, first=50):
                 rows.append((np.median((tt[:, :L, ev] - tt[:, :L, 0])[ok]), name))
         for v, name in sorted(rows):
             lines.append(f"   {v:8.0f}  {name}")
-        lay = tt[:, 1:L, 0] - tt[:, :L - 1, 0]
-        tok = np.diff(tt[:, 0, 0])
-        lines.append(f"   layer period {np.median(lay):.0f} ns, token period {np.median(tok):.0f} ns")
         h = tt[:, L]
-        parts = [f"{HEAD_EVENTS[e]} {np.median(h[:, e] - h[:, p]):.0f}" for p, e in ((0, 3), (3, 4), (4, 5), (5, 1), (1, 2))]
-        lines.append("   head (ns): " + ", ".join(parts))
+        if (tt[:, :L, 0] > 0).any():                                    # a CTA of the layer cluster
+            lay = tt[:, 1:L, 0] - tt[:, :L - 1, 0]
+            tok = np.diff(tt[:, 0, 0])
+            lines.append(f"   layer period {np.median(lay):.0f} ns, token period {np.median(tok):.0f} ns")
+            lines.append(f"   head (ns): x published to token agreed {np.median(h[:, 2] - h[:, 0]):.0f}")
+        else:                                                           # a helper: its head step from the published x
+            parts = [f"{HEAD_EVENTS[e]} {np.median(h[:, e] - h[:, p]):.0f}" for p, e in ((0, 3), (3, 4), (4, 5), (5, 1))]
+            lines.append("   head step (ns): " + ", ".join(parts))
     return "\n".join(lines)
 
 
