@@ -246,6 +246,25 @@ def combine_ranks(dist, t_dev, t_wall, positions):
     return tmax[0].item(), tmax[1].item(), tsum[2].item()
 
 
+def residency_line(path, ctx, prompt, max_new, warm_value, steps=2):
+    """The same decode with the weights evicted from L2 before every position (the reference's --cold,
+    src/engine.c:330-338: the flush is not token time), device-timed, beside the warm number."""
+    import l3m_b200
+    m = l3m_b200.Model(str(path), ctx=ctx, force=True, cold=True)
+    m.generate(prompt, max_new, temperature=0)
+    m.perf()
+    dev, pos = 0.0, 0
+    for _ in range(steps):
+        m.generate(prompt, max_new, temperature=0)
+        dev += m.device_ns()
+        pos += int(m.perf()["tokens"])
+    m.close()
+    cold = pos / (dev * 1e-9)
+    return {"warm_tok_s": warm_value, "cold_tok_s": round(cold, 1), "cold_over_warm": round(cold / warm_value, 3),
+            "cold": "weights evicted from L2 before every position by streaming 1.5 x L2 of scratch through the layer "
+                    "cluster's shared memory; the flush time is excluded, as the reference's --cold"}
+
+
 def bench_ours(a):
     rank, world, local = rank_env()
     import l3m_b200
@@ -262,7 +281,7 @@ def bench_ours(a):
     # One batch-1 stream on all `world` GPUs: rank 0 loads the model split over GPUs 0..world-1 and
     # drives every GPU (one host thread per model, as the reference's one process per model); the
     # other ranks only join the barriers and report no work.
-    dev_ns, wall_ns, positions, toks = [], [], 0, []
+    dev_ns, wall_ns, positions, toks, waits = [], [], 0, [], []
     if rank == 0:
         m = l3m_b200.Model(path, cpus=list(range(world)), ctx=ctx, force=True)
         flush = L2Flush()
@@ -278,9 +297,10 @@ def bench_ours(a):
             t0 = time.perf_counter_ns()
             toks = m.generate(prompt, max_new, temperature=0, on_token=sink.append)
             wall_ns.append(time.perf_counter_ns() - t0)
+            dev_ns.append(m.device_ns())
             p = m.perf()
-            dev_ns.append(p["ns_compute"] * p["tokens"])
             positions += int(p["tokens"])
+            waits.append(p["ns_wait"])
     n_gen = len(toks)
     t_dev, t_wall, total = combine_ranks(dist, sum(dev_ns), sum(wall_ns), positions)
     if dist:
@@ -315,7 +335,10 @@ def bench_ours(a):
                      "algorithmic_bytes_per_launch": alg},
         "gpu_launches": a.steps,
         "clocks": clk.summary(),
+        "ns_wait_per_token": round(float(np.mean(waits)), 1) if waits else None,
     }
+    if not a.no_cold and world == 1:
+        out["residency"] = residency_line(path, ctx, prompt, max_new, out["value"])
     if not a.no_matvec and world == 1:
         out["matvec"] = matvec_line()
     if not a.no_cpu and world == 1:
@@ -367,6 +390,7 @@ def main():
     ap.add_argument("--config", default="SmolLM2-135M-q8_0", choices=list(synth.CONFIGS))
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-matvec", action="store_true", help="skip the matvec line of the decode bench")
+    ap.add_argument("--no-cold", action="store_true", help="skip the cold-residency measurement of the decode bench")
     ap.add_argument("--positions", type=int, default=0,
                     help="forward passes per step (default: the whole context); small values make a profiling case")
     ap.add_argument("--sweep", action="store_true", help="the matvec sweep instead of decode (one JSON line per case)")

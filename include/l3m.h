@@ -22,15 +22,15 @@ typedef struct {
     int        reference;  // 1 = the fp32 reference path (no activation quantisation), on the GPU
     int        force;      // 1 = load even if the weights will not stay resident in the persisting L2 window
     int        verbose;    // print each GPU's shard sizes against its L2 budget, on stderr
-    int        cold;       // 1 = no persisting L2 window: the weights compete for L2 (per-token eviction not built)
+    int        cold;       // 1 = the weights are evicted from L2 before every position (time excluded), no persisting window
 } l3m_opts;
 
 // Field order and types are the reference's (src/l3m.h:21-29).
 typedef struct {
     double tokens;         // forward passes since the previous read, prompt included
     double ns_token;       // wall time per token
-    double ns_compute;     // per token, device time inside the decode kernel
-    double ns_wait;        // per token, device time spent waiting on exchanges (0 when not measured)
+    double ns_compute;     // per token, ns_token - ns_wait
+    double ns_wait;        // per token, time the layer cluster's CTAs spend in exchange and token waits (their average)
     double bytes_token;    // weight bytes streamed per token, summed over the GPUs (padding included)
     double l2_bytes;       // L2 cache summed over the GPUs
     double l3_miss, dram_bytes, energy_j, llc_occupancy;   // NAN: CPU counters, not measured on GPUs
@@ -60,6 +60,9 @@ L3M_API int          l3m_eos(const l3m_model *m);
 L3M_API const char  *l3m_chatml(const l3m_model *m, int32_t *im_start);
 
 L3M_API int          l3m_perf_read(l3m_model *m, l3m_perf *out);   // since the previous read; -1 if nothing ran
+// Extension (not in the reference's API): device time of the decode launches since the previous
+// l3m_perf_read (CUDA events around each launch, cold flushes excluded), ns.
+L3M_API double       l3m_device_ns(const l3m_model *m);
 
 L3M_API int          l3m_parse_cpus(const char *list, int *cpus, int max);   // "0-7,12" -> count, -1 on error
 L3M_API void         l3m_print_hw(FILE *out);                        // the GPUs, their L2 and persisting budgets

@@ -69,6 +69,7 @@ def lib():
         "l3m_eos": (i, [vp]),
         "l3m_chatml": (C.c_char_p, [vp, C.POINTER(C.c_int32)]),
         "l3m_perf_read": (i, [vp, C.POINTER(Perf)]),
+        "l3m_device_ns": (C.c_double, [vp]),
         "l3m_parse_cpus": (i, [C.c_char_p, C.POINTER(C.c_int), i]),
         "l3m_row_bytes": (sz, [i, i]),
         "l3m_tile_bytes": (sz, [i, i]),
@@ -217,6 +218,11 @@ class Model:
         """The logits of the last position run (during on_token: of the token just produced)."""
         with self._using() as ptr:
             return np.ctypeslib.as_array(self._lib.l3m_logits(ptr), shape=(self.vocab,)).copy()
+
+    def device_ns(self):
+        """Device time (ns) of the decode launches since the previous perf() call, cold flushes excluded."""
+        with self._using() as ptr:
+            return self._lib.l3m_device_ns(ptr)
 
     def perf(self):
         """Per-token counters since the previous call; NaN where unavailable."""

@@ -905,7 +905,7 @@ __device__ __noinline__ void head_helper(const DecodeArgs &a, const Role &role, 
     const int nres = cold ? 0 : stage_issue(s, a.dt_head, a.head, a.dim, role.voc0, role.voc1, s.w, a.st_head);   // cold: read each time
     const size_t th = tile_bytes(a.dt_head, a.dim);
     const int rest0 = role.voc0 + nres;
-    if (rest0 < role.voc1 && threadIdx.x == 0) prefetch_l2(a.head + rest0 * th, (size_t)(role.voc1 - rest0) * th);
+    if (!cold && rest0 < role.voc1 && threadIdx.x == 0) prefetch_l2(a.head + rest0 * th, (size_t)(role.voc1 - rest0) * th);
     bool landed = nres == 0;
     for (uint32_t e = 1;; e++) {
         if (wait_word(a, a.hx.flag, e, true, -1, kWaitHeadFlag) <= 0) break;
@@ -925,9 +925,31 @@ __device__ __noinline__ void head_helper(const DecodeArgs &a, const Role &role, 
         trace<TRACE>(a, tslot, pos, a.n_layers, 0);
         head_logits<GPT2, TRACE>(a, role, s, pos, 0, tslot, s.w, nres);
         trace<TRACE>(a, tslot, pos, a.n_layers, 1);
-        if (rest0 < role.voc1 && threadIdx.x == 0) prefetch_l2(a.head + rest0 * th, (size_t)(role.voc1 - rest0) * th);
+        if (!cold && rest0 < role.voc1 && threadIdx.x == 0) prefetch_l2(a.head + rest0 * th, (size_t)(role.voc1 - rest0) * th);
     }
     if (!landed) stage_wait(a, s, 0, -1, -1, true);                       // no copy outlives the CTA
+}
+
+// Cold mode (reference src/engine.c:330-338): this CTA's share of the scratch buffer, cold_chunk bytes per
+// copy into the attention-buffer part of the staging area (the bytes are never read), rounds of up to
+// kFlushCopies copies on the staging mbarrier. The scratch, 1.5 x L2 over the cluster, displaces the
+// weights from L2 before the next position starts.
+constexpr int kFlushCopies = 8;
+__device__ __noinline__ void cold_flush(const DecodeArgs &a, const Smem &s, int cta, uint32_t &wpar) {
+    const unsigned long long share = a.cold_bytes / kClusterCtas, base = share * (unsigned long long)cta;
+    const uint32_t chunk = (uint32_t)a.cold_chunk, bar = smem_addr(s.wbar);
+    for (unsigned long long off = 0; off < share; off += (unsigned long long)kFlushCopies * chunk) {
+        const int n = (int)min((unsigned long long)kFlushCopies, (share - off) / chunk);
+        if (threadIdx.x == kPrefetchThread) {
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"((uint32_t)n * chunk) : "memory");
+            for (int i = 0; i < n; i++) bulk_copy(smem_addr(s.w), a.cold_buf + base + off + (unsigned long long)i * chunk, chunk, bar, 0);
+        }
+        stage_wait(a, s, wpar, -1, -1, true);
+        wpar ^= 1;
+        // Every thread has seen this round complete before the next one is armed; a recorded failure
+        // ends the flush in every thread alike.
+        if (__syncthreads_or(threadIdx.x == 0 && aborted(a))) break;
+    }
 }
 
 // The weight-copy and exchange state carried from layer to layer: ns tiles of the outstanding copy,
@@ -935,6 +957,7 @@ __device__ __noinline__ void head_helper(const DecodeArgs &a, const Role &role, 
 struct LayerState {
     int ns;
     uint32_t wpar, xpar;
+    unsigned long long wait_cyc;        // SM cycles spent in exchange and token waits (thread 0's count)
 };
 
 // One layer of position pos on cluster 0 (phases Q, A, B, C, D and the five exchanges), one
@@ -971,8 +994,10 @@ __device__ __noinline__ void run_layer(const DecodeArgs &a, const LayerDev *laye
         else scatter(s.y, s.xq, g0, n);
     }
     trace<TRACE>(a, tslot, pos, l, 1);
+    long long w0 = clock64();
     if (a.async_x) xwait(a, s, 0, xpar, xbytes(a, -1), pos, l);   // 1: qkv (this GPU's heads)
     else cluster_sync();
+    st.wait_cyc += clock64() - w0;
     trace<TRACE>(a, tslot, pos, l, 2);
     const uint32_t step = layer_step(a, pos, l);
     for (int h = role.head0; h >= 0 && h < a.sh.head_lo + a.sh.n_heads_g; h += kClusterCtas) {   // A
@@ -980,9 +1005,11 @@ __device__ __noinline__ void run_layer(const DecodeArgs &a, const LayerDev *laye
         if (multi) peer_send(a, kXAttn, s.att, h * a.hd, a.hd, step);
     }
     trace<TRACE>(a, tslot, pos, l, 3);
+    w0 = clock64();
     if (a.async_x) xwait(a, s, 1, xpar, xbytes(a, kXAttn), pos, l);     // 2: attn
     else cluster_sync();
     if (multi) peer_recv(a, kXAttn, s.xa, step, pos, l);
+    st.wait_cyc += clock64() - w0;
     trace<TRACE>(a, tslot, pos, l, 4);
     if (role.wo0 < role.wo1) phase_wo<TRACE>(a, L, role, s, ns, wpar, pos, l, tslot);   // B
     if (ns) wpar ^= 1;
@@ -996,9 +1023,11 @@ __device__ __noinline__ void run_layer(const DecodeArgs &a, const LayerDev *laye
         if (multi) peer_send(a, kXProj, s.y, g0, n, step);
     }
     trace<TRACE>(a, tslot, pos, l, 5);
+    w0 = clock64();
     if (a.async_x) xwait(a, s, 2, xpar, xbytes(a, kXProj), pos, l);     // 3: proj
     else cluster_sync();
     if (multi) peer_recv(a, kXProj, s.xp, step, pos, l);
+    st.wait_cyc += clock64() - w0;
     trace<TRACE>(a, tslot, pos, l, 6);
     phase_ffn<GPT2, TRACE>(a, L, role, s, pos, l, tslot, ns, wpar);      // C
     if (ns) wpar ^= 1;
@@ -1015,15 +1044,19 @@ __device__ __noinline__ void run_layer(const DecodeArgs &a, const LayerDev *laye
     if (l + 1 < a.n_layers) stage_vectors<GPT2>(a, layers[l + 1], role, s, pos);
     else stage_vectors<GPT2>(a, layers[0], role, s, pos + 1);
     trace<TRACE>(a, tslot, pos, l, 8);
+    w0 = clock64();
     if (a.async_x) xwait(a, s, 3, xpar, xbytes(a, kXH), pos, l);     // 4: h
     else cluster_sync();
     if (multi) peer_recv(a, kXH, s.xh, step, pos, l);
+    st.wait_cyc += clock64() - w0;
     trace<TRACE>(a, tslot, pos, l, 9);
     if (role.dn0 < role.dn1) phase_down<TRACE>(a, L, role, s, ns, wpar, pos, l, tslot);   // D
     if (ns) wpar ^= 1;
-    {
+    if (l + 1 < a.n_layers || !a.cold) {                          // cold: the next position's first copy follows its flush
         const LayerDev &N = layers[l + 1 < a.n_layers ? l + 1 : 0];
         ns = stage_issue(s, N.dt_qkv, N.qkv, a.dim, role.qkv0, role.qkv1, s.w + a.w_extra, N.st_qkv, a.cold);
+    } else {
+        ns = 0;
     }
     trace<TRACE>(a, tslot, pos, l, 30);
     if (role.dn0 < role.dn1) {
@@ -1033,6 +1066,7 @@ __device__ __noinline__ void run_layer(const DecodeArgs &a, const LayerDev *laye
         if (multi) peer_send(a, kXDown, s.y, g0, n, step);
     }
     trace<TRACE>(a, tslot, pos, l, 10);
+    w0 = clock64();
     if (a.async_x) {                                              // 5: down
         xwait(a, s, 4, xpar, xbytes(a, kXDown), pos, l);
         xpar ^= 1u;
@@ -1040,6 +1074,7 @@ __device__ __noinline__ void run_layer(const DecodeArgs &a, const LayerDev *laye
         cluster_sync();
     }
     if (multi) peer_recv(a, kXDown, s.xd, step, pos, l);
+    st.wait_cyc += clock64() - w0;
 #pragma unroll 1
     for (int i = tid; i < a.dim; i += blockDim.x) s.x[i] = __fadd_rn(s.x[i], s.xd[i]);
     __syncthreads();
@@ -1107,6 +1142,8 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
     const Smem &s = sh_s;
     const Role &role = sh_role;
     const int cta = blockIdx.x, tid = threadIdx.x;
+    const long long cyc0 = clock64();                                     // CTA 0 keeps these for the statistics
+    const unsigned long long gt0 = globaltimer_ns();
     const bool multi = a.sh.n_gpus > 1;
     const int tslot = a.trace_cta[0] == cta ? 0 : a.trace_cta[1] == cta ? 1 : -1;
     int n_gen = 0, tok = 0, pos = 0;
@@ -1134,14 +1171,22 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
     }
     // The staged-weight schedule: qkv and wo into [w_extra, w_bytes) (the attention buffers are live
     // from the layer top to the end of attention), up/gate and down from offset 0.
-    LayerState st{0, 0, 0};
-    st.ns = stage_issue(s, layers[0].dt_qkv, layers[0].qkv, a.dim, role.qkv0, role.qkv1, s.w + a.w_extra, layers[0].st_qkv, a.cold);
+    LayerState st{0, 0, 0, 0};
+    if (!a.cold) st.ns = stage_issue(s, layers[0].dt_qkv, layers[0].qkv, a.dim, role.qkv0, role.qkv1, s.w + a.w_extra, layers[0].st_qkv);
+    unsigned long long cold_ns = 0;
     cluster_sync();                                                       // every CTA of the cluster has started
 
     for (pos = 0;; pos++) {
         const bool last = pos >= a.n_prompt - 1;
         if (pos < a.n_prompt) tok = a.prompt[pos];
         const bool stop_after = last && (n_gen >= a.max_new || pos + 1 >= a.ctx);   // reference engine.c:322, 352
+        if (a.cold) {                                                     // evict the weights; not token time
+            const unsigned long long f0 = globaltimer_ns();
+            cold_flush(a, s, cta, st.wpar);
+            cluster_sync();
+            if (tid == 0) cold_ns += globaltimer_ns() - f0;
+            st.ns = stage_issue(s, layers[0].dt_qkv, layers[0].qkv, a.dim, role.qkv0, role.qkv1, s.w + a.w_extra, layers[0].st_qkv, 1);
+        }
         embed_row<GPT2>(a, tok, pos, s.x);
         for (int l = 0; l < a.n_layers; l++) run_layer<GPT2, TRACE>(a, layers, l, role, s, pos, last, tslot, st);
         if (!last) continue;                                              // the next position starts from its embedding
@@ -1197,6 +1242,7 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
             __syncthreads();
             scatter(s.tmp, s.xt, 0, 4);
         }
+        const long long w6 = clock64();
         cluster_sync();                                                   // 6: the sampled token
         if (a.grid == kClusterCtas) {
             float gmax = -INFINITY;
@@ -1215,6 +1261,7 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
             if (cta == 0) gpu_vote(a, s, tcount, pos);
             cluster_sync();
         }
+        st.wait_cyc += clock64() - w6;
         int next = __float_as_int(s.xt[0]);
         const int stop_req = __float_as_int(s.xt[1]);
         const float gmax_all = s.xt[3];
@@ -1244,9 +1291,18 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
     }
     cp_async_wait_all();                                                  // no copy outlives the CTA
     if (st.ns) stage_wait(a, s, st.wpar, pos, -1, true);
+    if (tid == 0) a.hx.stats[cta] = st.wait_cyc;
     cluster_sync();                                                       // no CTA leaves while others may write its memory
     if (cta == 0 && tid == 0) {
         asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.hx.flag), "r"(kHeadDone) : "memory");   // the helpers stop
+        unsigned long long wsum = 0;
+        for (int c = 0; c < kClusterCtas; c++) wsum += ((volatile unsigned long long *)a.hx.stats)[c];
+        a.ctrl->wait_cyc = wsum;
+        a.ctrl->cold_ns = cold_ns;
+        a.ctrl->cyc0 = (unsigned long long)cyc0;
+        a.ctrl->gt0 = gt0;
+        a.ctrl->cyc1 = (unsigned long long)clock64();
+        a.ctrl->gt1 = globaltimer_ns();
         const int err = *(volatile int *)a.hx.abort_flag;
         a.ctrl->final_pos = pos;
         a.ctrl->n_gen = n_gen;

@@ -33,6 +33,11 @@ struct Ctrl {
     volatile int32_t where[4];       // the first failure: CTA, position, layer, wait (kWait*); for kErrShape
                                      // the launch shape seen: CTAs per cluster, clusters, grid, block
     volatile int32_t pad[2];
+    // Launch statistics, written once when the loop ends: the exchange and token waits of the layer
+    // cluster's CTAs (SM cycles, summed over its CTAs), the cold flushes' time (ns, excluded from token
+    // time as the reference's --cold), and CTA 0's SM clock and global timer at the launch's start and
+    // end (the cycles-to-time ratio of this launch).
+    volatile unsigned long long wait_cyc, cold_ns, cyc0, cyc1, gt0, gt1;
 };
 
 constexpr int kDecodeThreads = 256;   // 8 warps per CTA
@@ -49,6 +54,7 @@ struct HeadX {
     uint32_t *count;                    // arrivals: grid per sampled position
     float *slots;                       // [grid][2] (max, index bits)
     int *abort_flag;                    // [0]: first error code of any CTA; [1..4]: where (as Ctrl::where)
+    unsigned long long *stats;          // [kClusterCtas]: each layer-cluster CTA's wait cycles at the end
     unsigned long long timeout_ns;
 };
 constexpr uint32_t kHeadDone = 0xFFFFFFFFu;
@@ -132,8 +138,12 @@ struct DecodeArgs {
     // cluster barriers; set when every CTA of the cluster produces qkv rows, which orders every
     // buffer's next write after all its reads (see decode.cu).
     int async_x, sm_xbar;
-    int cold;                           // reference --cold (engine.c:330-338 flushes the weights after each token):
-                                        // weight copies carry an L2 evict-first policy
+    int cold;                           // reference --cold (engine.c:330-338): before every position the layer cluster
+                                        // streams cold_bytes (1.5 x L2) of scratch through its shared memory, evicting the
+                                        // weights from L2 (timed apart); weight copies carry an L2 evict-first policy
+    const uint8_t *cold_buf;
+    unsigned long long cold_bytes;      // a multiple of kClusterCtas x cold_chunk
+    int cold_chunk;                     // bytes per flush copy (a multiple of 16, at most w_extra)
     int vstride;                        // V cache: element i of position t at vc[i * vstride + t]
     int scratch_pairs, smem_bytes, attn_chunk;
 };

@@ -65,6 +65,7 @@ struct Gpu {
     float *probs = nullptr;                                            // [vocab] sampling weights
     unsigned long long *rx = nullptr, *vote = nullptr;                 // receive buffers and votes from other GPUs
     size_t rx_bytes = 0, vote_bytes = 0;
+    uint8_t *cold = nullptr;                                           // cold mode: the scratch streamed before each position
     l3m::DecodeArgs args{};
     size_t l2_bytes = 0, persist_max = 0, window_max = 0, prev_limit = 0;
     bool limit_set = false;
@@ -87,7 +88,7 @@ struct l3m_model {
     int32_t *tokens_dev = nullptr;
     std::vector<float> host_logits;
     int logits_pos = -1, cached_pos = -2;
-    double tok_count = 0, ns = 0, dev_ns = 0;
+    double tok_count = 0, ns = 0, dev_ns = 0, wait_ns = 0, cold_ns = 0;   // since the last l3m_perf_read
     size_t weight_bytes = 0;
     const l3m_kernels *kk = nullptr;
     char desc[256] = {0};
@@ -568,13 +569,21 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
         cudaMemcpy(g.roles, roles.data(), sizeof(l3m::Role) * GT, cudaMemcpyHostToDevice);
         a.roles = g.roles;
     }
-    g.hx_bytes = (size_t)(dim + 4) * 4 + 256 + (size_t)3 * GT * 4;
+    g.hx_bytes = (size_t)(dim + 4) * 4 + 256 + (size_t)3 * GT * 4 + 8 + l3m::kClusterCtas * 8;
     if (!cuda_ok(cudaMalloc(&g.hx, g.hx_bytes), "head exchange")) return false;
     a.hx.x = (float *)g.hx;
     a.hx.flag = (uint32_t *)((char *)g.hx + (size_t)(dim + 4) * 4);
     a.hx.count = a.hx.flag + 32;
     a.hx.abort_flag = (int *)(a.hx.flag + 16);
     a.hx.slots = (float *)(a.hx.flag + 64);
+    a.hx.stats = (unsigned long long *)(((uintptr_t)(a.hx.slots + 3 * GT) + 7) & ~(uintptr_t)7);
+    if (m->cold) {                                                     // 1.5 x L2, in whole copies per CTA of the cluster
+        a.cold_chunk = std::min(a.w_extra, 64 << 10) & ~15;
+        const unsigned long long unit = (unsigned long long)G * a.cold_chunk;
+        a.cold_bytes = (g.l2_bytes * 3 / 2 + unit - 1) / unit * unit;
+        if (a.cold_chunk < 4096 || !cuda_ok(cudaMalloc(&g.cold, a.cold_bytes), "cold-mode scratch")) return false;
+        a.cold_buf = g.cold;
+    }
     a.ctrl = m->ctrl_dev + g.rank;
     a.tokens = m->tokens_dev;
     if (m->n_gpus > 1) {                                               // what the other GPUs write into (zeroed: epoch 0 never matches)
@@ -819,7 +828,7 @@ L3M_API void l3m_free(l3m_model *m) {
             cudaCtxResetPersistingL2Cache();
             cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, g.prev_limit);
         }
-        cudaFree(g.arena); cudaFree(g.kv); cudaFree(g.rope); cudaFree(g.layers); cudaFree(g.roles); cudaFree(g.args_dev); cudaFree(g.trace); cudaFree(g.hx);
+        cudaFree(g.arena); cudaFree(g.kv); cudaFree(g.rope); cudaFree(g.layers); cudaFree(g.roles); cudaFree(g.args_dev); cudaFree(g.trace); cudaFree(g.hx); cudaFree(g.cold);
         cudaFree(g.prompt); cudaFree(g.logits); cudaFree(g.probs); cudaFree(g.rx); cudaFree(g.vote);
         if (g.ev0) cudaEventDestroy(g.ev0);
         if (g.ev1) cudaEventDestroy(g.ev1);
@@ -937,9 +946,16 @@ L3M_API int l3m_generate(l3m_model *m, const int32_t *prompt, int n_prompt, int 
     }
     float ms = 0;
     cudaEventElapsedTime(&ms, g.ev0, g.ev1);
+    // GPU 0's launch statistics: the layer cluster's wait cycles (averaged over its CTAs, the reference's
+    // average over ranks) at this launch's cycles-to-time ratio, and the cold flushes' time.
+    const l3m::Ctrl *c0 = m->ctrl;
+    const double cyc = (double)(c0->cyc1 - c0->cyc0), gt = (double)(c0->gt1 - c0->gt0);
+    const double ns_per_cyc = cyc > 0 && gt > 0 ? gt / cyc : 0.0;
     m->tok_count += last_pos + 1;
     m->ns += t1 - t0;
     m->dev_ns += ms * 1e6;
+    m->wait_ns += (double)c0->wait_cyc / l3m::kClusterCtas * ns_per_cyc;
+    m->cold_ns += (double)c0->cold_ns;
     return n_gen;
 }
 
@@ -971,20 +987,25 @@ L3M_API const char *l3m_decode(const l3m_model *m, int32_t tok, int *len) {
     return (const char *)l3m_tokenizer_decode(&m->f.tok, tok, len);
 }
 
+// The reference's accounting (src/engine.c:578-593): token time excludes the cold flushes; ns_wait is
+// the time the workers (here the layer cluster's CTAs, averaged) spent in exchange and token waits;
+// ns_compute is the rest.
 L3M_API int l3m_perf_read(l3m_model *m, l3m_perf *out) {
     memset(out, 0, sizeof *out);
     out->l3_miss = out->dram_bytes = out->energy_j = out->llc_occupancy = NAN;
-    const double tokens = m->tok_count, ns = m->ns, dev = m->dev_ns;
-    m->tok_count = m->ns = m->dev_ns = 0;
+    const double tokens = m->tok_count, ns = std::max(0.0, m->ns - m->cold_ns), wait = m->wait_ns;
+    m->tok_count = m->ns = m->dev_ns = m->wait_ns = m->cold_ns = 0;
     if (tokens <= 0) return -1;
     out->tokens = tokens;
     out->ns_token = ns / tokens;
-    out->ns_compute = std::min(dev / tokens, out->ns_token);
-    out->ns_wait = out->ns_token - out->ns_compute;          // outside the kernel: launch and host
+    out->ns_wait = std::min(wait / tokens, out->ns_token);
+    out->ns_compute = out->ns_token - out->ns_wait;
     out->bytes_token = (double)m->weight_bytes;
     for (int i = 0; i < m->n_gpus; i++) out->l2_bytes += (double)m->g[i].l2_bytes;
     return 0;
 }
+
+L3M_API double l3m_device_ns(const l3m_model *m) { return std::max(0.0, m->dev_ns - m->cold_ns); }
 
 L3M_API int l3m_parse_cpus(const char *list, int *cpus, int max) {
     int n = 0;
