@@ -64,7 +64,11 @@ L3M_API void   l3m_vec_prepare(l3m_vec *v, int dtype, const float *x, int n, voi
 
 // ---- device entry points (no counterpart in the reference: the GPU-resident forms of the above)
 
-// y = tiles . x on the device. exact 1: the sm100a table's order; 0: sm100a-fast.
+// y = tiles . x on the device. exact bit 0: 1 the sm100a table's order, 0 sm100a-fast. exact bit 1
+// (L3M_GEMV_CONST_TILES): the caller guarantees that no work issued earlier on the stream writes the
+// tiles (model weights), so the streamed kernel may start reading them before that work has finished
+// (x and y keep the stream order); successive calls then overlap.
+#define L3M_GEMV_CONST_TILES 2
 L3M_API int l3m_gemv_dev(int exact, int dtype, float *y, const void *tiles, int ntiles, int k, const l3m_vec *x, void *stream);
 // The exact quantised matvec (the same y as l3m_gemv_dev with exact = 1, bit for bit) for callers
 // that must not allocate device memory, such as a host whose framework owns the device's memory

@@ -615,8 +615,10 @@ bool place_in_l2(l3m_model *m, Gpu &g, const l3m_opts &o, bool *over) {
     if (m->cold || !g.persist_max || !g.window_max) return true;
     cudaSetDevice(g.dev);
     size_t setaside = std::min(g.weight_bytes, g.persist_max);
-    if (cudaDeviceGetLimit(&g.prev_limit, cudaLimitPersistingL2CacheSize) == cudaSuccess &&
-        cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, setaside) == cudaSuccess) {
+    // The window is best effort (the decode is correct without it), but a failure to set it is reported.
+    cudaError_t e = cudaDeviceGetLimit(&g.prev_limit, cudaLimitPersistingL2CacheSize);
+    if (e == cudaSuccess) e = cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, setaside);
+    if (e == cudaSuccess) {
         g.limit_set = true;
         cudaStreamAttrValue attr = {};
         attr.accessPolicyWindow.base_ptr = g.arena;
@@ -624,9 +626,15 @@ bool place_in_l2(l3m_model *m, Gpu &g, const l3m_opts &o, bool *over) {
         attr.accessPolicyWindow.hitRatio = (float)std::min(1.0, (double)setaside / attr.accessPolicyWindow.num_bytes);
         attr.accessPolicyWindow.hitProp = cudaAccessPropertyPersisting;
         attr.accessPolicyWindow.missProp = cudaAccessPropertyStreaming;
-        cudaStreamSetAttribute(g.stream, cudaStreamAttributeAccessPolicyWindow, &attr);
+        e = cudaStreamSetAttribute(g.stream, cudaStreamAttributeAccessPolicyWindow, &attr);
     }
-    cudaGetLastError();   // the window is best effort
+    if (e != cudaSuccess) {
+        fprintf(stderr, "l3m: gpu %d: persisting L2 window not set (%s); the weights compete for L2\n", g.dev, cudaGetErrorString(e));
+        cudaGetLastError();
+    } else if (o.verbose) {
+        fprintf(stderr, "l3m: gpu %d: persisting L2 window over %.2f MiB of weights, %.2f MiB set aside\n", g.dev,
+                std::min(g.weight_bytes, g.window_max) / MiB, setaside / MiB);
+    }
     return true;
 }
 

@@ -92,8 +92,9 @@ constexpr int kStreamThreads = 32 * (kStreamWarps + 1);
 constexpr int kStreamStages = 4;
 constexpr int kStreamChunk = 32768;                 // target weight bytes per chunk
 constexpr int kStreamScratch = 48 * 1024;           // bytes of per-wave (scale product, dot) pairs
+constexpr int kConstTiles = 2;                      // l3m_gemv_dev flag: no earlier work on the stream writes the tiles
 
-struct StreamPlan { int G, U, piece, stage_bytes, scratch_pairs; };
+struct StreamPlan { int G, U, piece, stage_bytes, scratch_pairs, early; };   // early: start the weight copies before the grid dependency
 
 __host__ __device__ inline int stream_unit_bytes(int dtype) { return dtype == DT_BF16 ? 1024 : block_bytes(dtype); }
 
@@ -113,6 +114,7 @@ StreamPlan stream_plan(int dtype, int k, int tiles_per_cta) {
     pl.piece = pl.U * bb + 64;
     pl.stage_bytes = g * pl.piece;
     pl.scratch_pairs = dtype == DT_BF16 ? 0 : g * nb * kTile;
+    pl.early = 0;
     return pl;
 }
 
@@ -164,9 +166,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gemv_stream_kernel(float *y
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();                                                       // the barriers are initialised
-    // Launched as a programmatic dependent: everything above overlaps the previous kernel's tail; no
-    // global memory is read before that kernel has completed (its writes, x or the tiles, visible).
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // Launched as a programmatic dependent: everything above overlaps the previous kernel's tail. Unless
+    // the caller declared the tiles constant (pl.early), no global memory is read before that kernel
+    // has completed (its writes, x or the tiles, visible); with constant tiles the first ring of weight
+    // copies starts at once and only x waits.
+    if (!pl.early) asm volatile("griddepcontrol.wait;" ::: "memory");
     // The producer: chunk c of this CTA's tiles into stage c % kStreamStages, once the compute warps
     // have released that stage (from the second round of the ring on).
     auto issue = [&](int c) {
@@ -185,6 +189,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gemv_stream_kernel(float *y
     const int early = min(total, kStreamStages);                           // the first ring needs no release
     if (warp == kStreamWarps)
         for (int c = 0; c < early; c++) issue(c);                          // the weights stream in while x is loaded
+    if (pl.early) asm volatile("griddepcontrol.wait;" ::: "memory");       // x may be the previous launch's output
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");        // the next launch may start its prologue
     load_prep(DT, x, k, p);                                                // every thread; ends with __syncthreads
     if (warp == kStreamWarps) {
@@ -219,7 +224,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gemv_stream_kernel(float *y
             for (int i = tid; i < items; i += 32 * kStreamWarps) {
                 const int u = i / per_u, rem = i - u * per_u, g = rem >> 2, r4 = rem & 3, b = b0 + u;
                 QLoad4 q;
-                qload4<DT, true>(q, buf + (size_t)g * pl.piece + (size_t)u * bb, r4);
+                qload4_shared<DT>(q, smem_u32(buf + (size_t)g * pl.piece + (size_t)u * bb), r4);
                 const uint4 x0 = *(const uint4 *)(xw + 8 * b), x1 = *(const uint4 *)(xw + 8 * b + 4);
                 const uint32_t xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
                 const float sx = p.scale[b];
@@ -252,6 +257,125 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gemv_stream_kernel(float *y
             if (tid < ng * kTile) y[(size_t)(g0 + (tid >> 4)) * kTile + (tid & 15)] = *(volatile int *)&fail ? __int_as_float(0x7FC00000) : acc;
             acc = 0.0f;
         }
+    }
+}
+
+// ---- Warp-streamed exact matvec (q8_0, q4_0, mxfp4; k a multiple of 32). One CTA per SM takes a
+// contiguous run of tiles [t0, t1), in waves of G tiles whose (scale product, dot) pairs fit the
+// scratch. The tiles are cut into pieces of kWarpPieceBlocks 32-input blocks (one contiguous range of
+// a tile); warp w takes pieces w, w + 8, ... and streams them through its own ring of kWarpStages
+// shared-memory buffers: its lane 0 issues one cp.async.bulk per piece (this CTA's shared memory, no
+// multicast), completing on that buffer's mbarrier, and refills the buffer as soon as the warp has
+// read it. So no warp waits for another while the weights stream. Each lane computes one item per
+// piece (4 rows x 1 block: the exact integer dots with dp4a) and leaves {RN(sx*d), (float)dot} in the
+// wave's scratch; after one CTA barrier per wave, one thread per output runs acc = fma(RN(sx*d), dot,
+// acc) over the blocks in order: the scalar kernel's rounding sequence (src/kernels_scalar.c:30-75).
+constexpr int kWarpWarps = 8, kWarpThreads = 32 * kWarpWarps;
+constexpr int kWarpStages = 4;
+constexpr int kWarpPieceBlocks = 8;                 // 4 row groups x 8 blocks: one item per lane
+constexpr size_t kWarpScratchCap = 64 * 1024;       // (scale product, dot) pairs of a wave
+
+__host__ __device__ inline int warp_piece_bytes(int dtype) { return kWarpPieceBlocks * block_bytes(dtype); }   // a multiple of 16
+
+size_t warp_fixed_bytes(int dtype, int k) {                            // the activation and the buffer rings
+    return ((prep_smem(k) + 127) & ~(size_t)127) + (size_t)kWarpWarps * kWarpStages * warp_piece_bytes(dtype);
+}
+size_t smem_optin();
+int stream_sms();
+// The wave size for a quantised matvec of ntiles tiles of k inputs: the most tiles (at most 16, one
+// output per thread, and at most one CTA's share) whose pairs fit kWarpScratchCap beside the fixed
+// parts within the opt-in shared memory; 0 when the kernel does not take the shape.
+int warp_plan_G(int dtype, int k, int ntiles) {
+    if (dtype < DT_Q8 || k % kQB || ntiles <= 0) return 0;
+    const size_t fixed = warp_fixed_bytes(dtype, k), optin = smem_optin(), per_tile = (size_t)(k / kQB) * kTile * sizeof(float2);
+    if (fixed + 1024 >= optin) return 0;
+    const size_t scratch = std::min(kWarpScratchCap, optin - 1024 - fixed);
+    const int grid = std::min(ntiles, stream_sms()), per_cta = (ntiles + grid - 1) / grid;
+    return (int)std::min<size_t>((size_t)std::min(16, per_cta), scratch / per_tile);
+}
+
+template <int DT>
+__global__ void __launch_bounds__(kWarpThreads, 1) gemv_warp_kernel(float *y, const uint8_t *tiles, int ntiles, int k, VecArg x, int G, int early,
+                                                                     int *timeouts) {
+    extern __shared__ __align__(16) unsigned char smem_w[];
+    __shared__ __align__(8) unsigned long long full[kWarpWarps][kWarpStages];
+    __shared__ int fail;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int bb = block_bytes(DT), nb = k / kQB, ppt = (nb + kWarpPieceBlocks - 1) / kWarpPieceBlocks, pbytes = warp_piece_bytes(DT);
+    const size_t tb = (size_t)nb * bb;
+    Prep p = carve_prep(smem_w, k);
+    unsigned char *ring = smem_w + ((prep_smem(k) + 127) & ~(size_t)127);   // 16-byte aligned (bulk copy destinations)
+    float2 *scratch = (float2 *)(ring + (size_t)kWarpWarps * kWarpStages * pbytes);
+    const int t0 = (int)((long long)blockIdx.x * ntiles / gridDim.x), t1 = (int)((long long)(blockIdx.x + 1) * ntiles / gridDim.x);
+    const int nt = t1 - t0, total = nt * ppt;                               // pieces of this CTA, tile-major
+    if (G < 1) return;                                                     // the host never launches this (uniform)
+    if (tid == 0) {
+        fail = 0;
+        for (int w = 0; w < kWarpWarps; w++)
+            for (int i = 0; i < kWarpStages; i++) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&full[w][i])) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();                                                       // the barriers are initialised
+    // A programmatic dependent: unless the tiles are declared constant, no global memory is read before
+    // the previous kernel on the stream has completed; with constant tiles only x waits.
+    if (!early) asm volatile("griddepcontrol.wait;" ::: "memory");
+    // This warp's j-th piece (CTA piece warp + 8 j) into its buffer j % kWarpStages.
+    auto issue = [&](int j) {
+        const int i = warp + kWarpWarps * j;
+        if (i >= total || lane != 0) return;
+        const int tl = i / ppt, b0 = (i - tl * ppt) * kWarpPieceBlocks, nbk = min(kWarpPieceBlocks, nb - b0);
+        const uint32_t bar = smem_u32(&full[warp][j % kWarpStages]);
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"((uint32_t)(nbk * bb)) : "memory");
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                     ::"r"(smem_u32(ring + (size_t)(warp * kWarpStages + j % kWarpStages) * pbytes)),
+                     "l"(tiles + (size_t)(t0 + tl) * tb + (size_t)b0 * bb), "r"((uint32_t)(nbk * bb)), "r"(bar) : "memory");
+    };
+    for (int j = 0; j < kWarpStages; j++) issue(j);                        // the weights stream in while x is loaded
+    if (early) asm volatile("griddepcontrol.wait;" ::: "memory");          // x may be the previous launch's output
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    load_prep(DT, x, k, p);                                                // every thread; ends with __syncthreads
+    const uint32_t *xw = (const uint32_t *)p.q8;
+    const int r4 = lane & 3, u = lane >> 2;                                 // this lane's item in a piece: rows 4 r4.., block u
+    int j = 0;
+    for (int tw0 = 0; tw0 < nt; tw0 += G) {
+        const int tw1 = min(nt, tw0 + G), n_out = (tw1 - tw0) * kTile;
+        for (;; j++) {                                                      // this warp's pieces of the wave
+            const int i = warp + kWarpWarps * j;
+            if (i >= total || i / ppt >= tw1) break;
+            const int st = j % kWarpStages, tl = i / ppt, b0 = (i - tl * ppt) * kWarpPieceBlocks, nbk = min(kWarpPieceBlocks, nb - b0);
+            mbar_wait(smem_u32(&full[warp][st]), (uint32_t)(j / kWarpStages) & 1u, &fail, timeouts);
+            if (u < nbk) {
+                const int b = b0 + u;
+                QLoad4 q;
+                qload4_shared<DT>(q, smem_u32(ring + (size_t)(warp * kWarpStages + st) * pbytes + (size_t)u * bb), r4);
+                const uint4 x0 = *(const uint4 *)(xw + 8 * b), x1 = *(const uint4 *)(xw + 8 * b + 4);
+                const uint32_t xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                const float sx = p.scale[b];
+                const int32_t xs = p.sum[b];
+                float4 r0, r1;
+                r0.x = __fmul_rn(sx, qscale4<DT>(q.d, 0)); r0.y = __int2float_rn(qdot4<DT>(q, 0, xv, xs));
+                r0.z = __fmul_rn(sx, qscale4<DT>(q.d, 1)); r0.w = __int2float_rn(qdot4<DT>(q, 1, xv, xs));
+                r1.x = __fmul_rn(sx, qscale4<DT>(q.d, 2)); r1.y = __int2float_rn(qdot4<DT>(q, 2, xv, xs));
+                r1.z = __fmul_rn(sx, qscale4<DT>(q.d, 3)); r1.w = __int2float_rn(qdot4<DT>(q, 3, xv, xs));
+                float4 *dst = (float4 *)(scratch + (size_t)b * n_out + (tl - tw0) * kTile + 4 * r4);
+                dst[0] = r0;
+                dst[1] = r1;
+            }
+            __syncwarp();                                                   // every lane has read the buffer
+            issue(j + kWarpStages);                                         // refill it (possibly with the next wave's piece)
+        }
+        __syncthreads();                                                    // every pair of the wave written
+        if (tid < n_out) {
+            const float2 *r = scratch + tid;
+            float acc = 0.0f;
+#pragma unroll 8
+            for (int b = 0; b < nb; b++) {
+                const float2 v = r[(size_t)b * n_out];
+                acc = __fmaf_rn(v.x, v.y, acc);
+            }
+            y[(size_t)(t0 + tw0) * kTile + tid] = *(volatile int *)&fail ? __int_as_float(0x7FC00000) : acc;
+        }
+        __syncthreads();                                                    // read before the next wave writes
     }
 }
 
@@ -364,6 +488,25 @@ __global__ void __launch_bounds__(kThreads) attend_kernel(float *out, const floa
 }
 
 VecArg vec_arg(const l3m_vec *x) { return VecArg{x->f32, x->bf16, x->q8, x->scale, x->sum}; }
+
+// One warp-streamed matvec launch, a programmatic dependent launch like launch_stream's.
+template <class K>
+cudaError_t launch_warp(K kernel, int grid, size_t smem, cudaStream_t s, float *y, const uint8_t *t, int ntiles, int k, VecArg x, int G,
+                        int early, int *tmo) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute at[1];
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kWarpThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, y, t, ntiles, k, x, G, early, tmo);
+}
 
 // One streamed-matvec launch as a programmatic dependent launch: the kernel's prologue (shared-memory
 // barriers) may run while the previous work on the stream finishes; the kernel waits for that work
@@ -494,12 +637,25 @@ L3M_API int l3m_gemv_dev(int exact, int dtype, float *y, const void *tiles, int 
     if (stream_timeouts(&tmo)) return -1;
     cudaStream_t s = (cudaStream_t)stream;
     static const bool stream_off = getenv("L3M_GEMV_STREAM") && !strcmp(getenv("L3M_GEMV_STREAM"), "0");
-    if (!exact && dtype <= DT_BF16) {
+    if (!(exact & 1) && dtype <= DT_BF16) {
         gemv_fast_kernel<<<grid_for((ntiles + 15) / 16), kThreads, 0, s>>>(dtype, y, (const uint8_t *)tiles, ntiles, k, vec_arg(x));
+    } else if (const int G = warp_plan_G(dtype, k, ntiles); !stream_off && G > 0 && ((uintptr_t)tiles & 15) == 0) {
+        const int grid = std::min(ntiles, stream_sms());
+        const size_t smem = warp_fixed_bytes(dtype, k) + (size_t)G * (k / kQB) * kTile * sizeof(float2);
+        const int early = (exact & kConstTiles) ? 1 : 0;
+        const uint8_t *t = (const uint8_t *)tiles;
+        cudaError_t e = cudaSuccess;
+        switch (dtype) {
+        case DT_Q8: e = launch_warp(gemv_warp_kernel<DT_Q8>, grid, smem, s, y, t, ntiles, k, vec_arg(x), G, early, tmo); break;
+        case DT_Q4: e = launch_warp(gemv_warp_kernel<DT_Q4>, grid, smem, s, y, t, ntiles, k, vec_arg(x), G, early, tmo); break;
+        default: e = launch_warp(gemv_warp_kernel<DT_MX>, grid, smem, s, y, t, ntiles, k, vec_arg(x), G, early, tmo); break;
+        }
+        if (e != cudaSuccess) return fail(e, "l3m_gemv_dev");
     } else if (!stream_off && dtype >= DT_BF16 && k % kQB == 0 && ((uintptr_t)tiles & 15) == 0 && stream_plan(dtype, k, 16).G &&
                stream_smem(k, stream_plan(dtype, k, 16)) + 1024 <= smem_optin()) {
         const int grid = std::min(ntiles, stream_sms());
-        const StreamPlan pl = stream_plan(dtype, k, (ntiles + grid - 1) / grid);
+        StreamPlan pl = stream_plan(dtype, k, (ntiles + grid - 1) / grid);
+        pl.early = (exact & kConstTiles) ? 1 : 0;
         const size_t smem = stream_smem(k, pl);
         cudaError_t e = cudaSuccess;
         const uint8_t *t = (const uint8_t *)tiles;

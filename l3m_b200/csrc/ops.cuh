@@ -146,6 +146,38 @@ __device__ __forceinline__ void qload4(QLoad4 &q, const uint8_t *blk, int r4) {
     }
 }
 
+__device__ __forceinline__ uint4 lds_u4_ord(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint32_t lds_u32_ord(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint2 lds_u2_ord(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a) : "memory");
+    return v;
+}
+// qload4 from a block at shared-window address blk (shared-space loads, in program order).
+template <int DT>
+__device__ __forceinline__ void qload4_shared(QLoad4 &q, uint32_t blk, int r4) {
+    if (DT == DT_Q8) {
+        const uint32_t g = blk + 32 + 16 * r4;
+#pragma unroll
+        for (int j = 0; j < 8; j++) q.w[j] = lds_u4_ord(g + 64 * j);
+        q.d = lds_u2_ord(blk + 8 * r4);
+    } else {
+        const uint32_t g = blk + (DT == DT_MX ? 16 : 32) + 16 * r4;
+#pragma unroll
+        for (int j = 0; j < 4; j++) q.w[j] = lds_u4_ord(g + 64 * j);
+        if (DT == DT_MX) q.d = make_uint2(lds_u32_ord(blk + 4 * r4), 0);
+        else q.d = lds_u2_ord(blk + 8 * r4);
+    }
+}
+
 __device__ __forceinline__ uint32_t u4_at(const uint4 &v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
 
 // Exact integer dot of row c (0..3) of a QLoad4 with the block's prepared activation words xw[0..7],

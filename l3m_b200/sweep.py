@@ -9,7 +9,9 @@ tile layout with the sweep's value distributions: q8_0 int8 uniform in [-127, 12
 uniform with e8m0 scales uniform in [118, 130]; bf16 weights N(0, 0.02). x ~ N(0,1) is prepared on
 the device (l3m_vec_prepare_dev). Each case runs l3m_gemv_dev (the C ABI, device pointers) in two
 regimes; `iters` launches are captured into a CUDA graph, which is replayed once warm and once
-timed with CUDA events (so the GPU time per launch is measured, not the host's launch rate):
+timed with CUDA events (so the GPU time per launch is measured, not the host's launch rate). The
+tiles are declared constant (L3M_GEMV_CONST_TILES, as model weights are), so a launch may start
+streaming them while the previous one finishes; --ordered measures without that:
 
   hbm  R copies of the matrix, at least 2.5x the L2 in total, used round robin: every launch reads
        its tiles from HBM;
@@ -68,7 +70,10 @@ def l2_copy_gbs(torch, iters=200):
     return 2 * a.numel() * 4 * iters / (e0.elapsed_time(e1) * 1e-3) / 1e9
 
 
-def run(dtypes, shapes, iters, exact, out, echo=True):
+CONST_TILES = 2   # l3m_gemv_dev flag: the tiles are constant (include/l3m_kernels.h, L3M_GEMV_CONST_TILES)
+
+
+def run(dtypes, shapes, iters, exact, out, echo=True, const_tiles=True):
     import torch
     from . import Vec, lib
     L = lib()
@@ -102,7 +107,8 @@ def run(dtypes, shapes, iters, exact, out, echo=True):
             for regime in ("hbm", "l2"):
                 def launch(i, st):
                     p = base + (i % reps) * stride if regime == "hbm" else base
-                    if L.l3m_gemv_dev(exact, dt, C.c_void_p(y.data_ptr()), C.c_void_p(p), m // 16, k, C.byref(v), st):
+                    if L.l3m_gemv_dev(exact | (CONST_TILES if const_tiles else 0), dt, C.c_void_p(y.data_ptr()), C.c_void_p(p), m // 16,
+                                      k, C.byref(v), st):
                         raise RuntimeError(L.l3m_cuda_error().decode())
                 for i in range(min(20, reps) if regime == "hbm" else 20):
                     launch(i, sp)
@@ -124,7 +130,7 @@ def run(dtypes, shapes, iters, exact, out, echo=True):
                 us = e0.elapsed_time(e1) * 1e3 / iters
                 del g
                 gbs = nbytes / (us * 1e-6) / 1e9
-                row = {"dtype": name, "m": m, "k": k, "regime": regime, "table": "exact" if exact else "fast",
+                row = {"dtype": name, "m": m, "k": k, "regime": regime, "table": "exact" if exact else "fast", "const_tiles": bool(const_tiles),
                        "bytes": nbytes, "us_per_launch": round(us, 3), "gbs": round(gbs, 1),
                        "frac_hbm": round(gbs / hbm_peak, 4), "frac_l2_copy": round(gbs / l2_ref, 4),
                        "hbm_peak": hbm_peak, "hbm_peak_kind": peak_kind, "l2_copy_gbs": round(l2_ref, 1), "copies": reps}
@@ -145,10 +151,12 @@ def main():
     ap.add_argument("--iters", type=int, default=200)
     ap.add_argument("--exact", type=int, default=1)
     ap.add_argument("--json", default="")
+    ap.add_argument("--ordered", action="store_true",
+                    help="do not declare the tiles constant: each launch reads its tiles only after the previous one ends")
     a = ap.parse_args()
     shapes = [tuple(int(v) for v in s.split("x")) for s in a.shapes.split(",")]
     with open(a.json, "w") if a.json else open("/dev/null", "w") as out:
-        rows = run(a.dtypes.split(","), shapes, a.iters, a.exact, out)
+        rows = run(a.dtypes.split(","), shapes, a.iters, a.exact, out, const_tiles=not a.ordered)
     print("\n| dtype | M x K | MB | HBM: us | GB/s | of HBM peak | L2: us | GB/s |")
     print("|---|---|---|---|---|---|---|---|")
     by = {(r["dtype"], r["m"], r["k"], r["regime"]): r for r in rows}
