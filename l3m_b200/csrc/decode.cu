@@ -51,6 +51,7 @@ struct Smem {
     unsigned long long *wbar;            // its mbarrier
     unsigned long long *xbar;            // exchanges 1-5 (async_x)
     Prep prep;
+    Prep pa, ph;                         // q8 exchanges: the activations of wo and down as received
 };
 
 __device__ __forceinline__ Smem carve(unsigned char *base, const DecodeArgs &a) {
@@ -87,6 +88,8 @@ __device__ __forceinline__ Smem carve(unsigned char *base, const DecodeArgs &a) 
     s.prep.scale = (float *)(base + a.sm_scale);
     s.prep.sum = (int32_t *)(base + a.sm_sum);
     s.prep.xf = (float *)(base + a.sm_xf);
+    s.pa = Prep{(int8_t *)(base + a.sm_pa_q8), (float *)(base + a.sm_pa_scale), (int32_t *)(base + a.sm_pa_sum), s.prep.xf};
+    s.ph = Prep{(int8_t *)(base + a.sm_ph_q8), (float *)(base + a.sm_ph_scale), (int32_t *)(base + a.sm_ph_sum), s.prep.xf};
     return s;
 }
 
@@ -334,9 +337,52 @@ __device__ __noinline__ void xwait(const DecodeArgs &a, const Smem &s, int k, ui
 // reading step s.
 __device__ __forceinline__ uint32_t layer_step(const DecodeArgs &a, int pos, int l) { return (uint32_t)pos * (uint32_t)a.n_layers + (uint32_t)l; }
 __device__ __forceinline__ int xlen(const DecodeArgs &a, int k) { return k == kXH ? a.ffn : a.dim; }
-// The bytes of exchange k (-1: qkv) that this GPU's own CTAs deliver to each of its CTAs.
+// The bytes of exchange k (-1: qkv) that this GPU's own CTAs deliver to each of its CTAs: 4 per value,
+// or per 32-value block 40 (q8 bytes, scale, sum) for the q8 exchanges.
 __device__ __forceinline__ uint32_t xbytes(const DecodeArgs &a, int k) {
-    return 4u * (uint32_t)(k < 0 ? a.sh.n_qkv_g : a.sh.len[k][a.sh.gpu]);
+    const uint32_t n = (uint32_t)(k < 0 ? a.sh.n_qkv_g : a.sh.len[k][a.sh.gpu]);
+    if ((k == kXAttn && a.qx_attn) || (k == kXH && a.qx_h)) return n / kQB * 40u;
+    return 4u * n;
+}
+
+// The q8 form of an exchange: src[0, n) (n a multiple of 32, this CTA's values g0.., g0 a multiple of
+// 32) quantised by warp 0 into stage (the prepare step, block by block), then every block's 32 bytes,
+// scale and sum stored into every CTA's dst at block g0 / 32 with st.async, completing on bar.
+__device__ __noinline__ void scatter_q8(const float *src, int g0, int n, const Prep &stage, const Prep &dst, unsigned long long *bar) {
+    const int tid = threadIdx.x, nblk = n / kQB, b0 = g0 / kQB;
+    if (tid < 32) {
+        const int j = tid & 7, sub = tid >> 3;
+#pragma unroll 1
+        for (int bq = 0; bq < nblk; bq += 4) {
+            const int b = bq + sub;
+            const bool ok = b < nblk;
+            const float4 v = ok ? ((const float4 *)(src + b * kQB))[j] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            quant_block4(v, b, j, ok, stage);
+        }
+    }
+    __syncthreads();
+    const uint32_t lb = (uint32_t)__cvta_generic_to_shared(bar);
+    const uint32_t dq = (uint32_t)__cvta_generic_to_shared(dst.q8 + g0), ds = (uint32_t)__cvta_generic_to_shared(dst.scale + b0),
+                   dm = (uint32_t)__cvta_generic_to_shared(dst.sum + b0);
+    // per rank and block: two 16-byte pieces of q8, the scale, the sum
+#pragma unroll 1
+    for (int e = tid; e < 4 * nblk * kClusterCtas; e += blockDim.x) {
+        const int r = e % kClusterCtas, item = e / kClusterCtas, b = item >> 2, part = item & 3;
+        uint32_t rb;
+        asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rb) : "r"(lb), "r"(r));
+        if (part < 2) {
+            const uint4 v = *(const uint4 *)(stage.q8 + b * kQB + 16 * part);
+            uint32_t ra;
+            asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(dq + b * kQB + 16 * part), "r"(r));
+            asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];"
+                         ::"r"(ra), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(rb) : "memory");
+        } else {
+            const uint32_t w = part == 2 ? __float_as_uint(stage.scale[b]) : (uint32_t)stage.sum[b];
+            uint32_t ra;
+            asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"((part == 2 ? ds : dm) + 4 * b), "r"(r));
+            asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(ra), "r"(w), "r"(rb) : "memory");
+        }
+    }
 }
 
 // This CTA's part src[0, n) of exchanged vector k (elements [g0, g0 + n)) into every other GPU's
@@ -503,7 +549,8 @@ __device__ __noinline__ void phase_attention(const DecodeArgs &a, const LayerDev
     attend_exact<true>(y, kc, vc, hd, a.vstride, s.kcur, s.vcur, pos, hd, s.scores, s.att, s.red, a.etab, s.kvbuf, s.vtbuf,
                        a.attn_chunk, prestaged);
     trace<TRACE>(a, tslot, pos, l, 15);
-    if (a.async_x) scatter_tx(s.att, s.xa, h * hd, hd, s.xbar + 1);
+    if (a.qx_attn) scatter_q8(s.att, h * hd, hd, s.prep, s.pa, s.xbar + 1);   // prep is free during phase A
+    else if (a.async_x) scatter_tx(s.att, s.xa, h * hd, hd, s.xbar + 1);
     else scatter(s.att, s.xa, h * hd, hd);
 }
 
@@ -512,11 +559,11 @@ __device__ __noinline__ void phase_attention(const DecodeArgs &a, const LayerDev
 template <bool TRACE>
 __device__ __noinline__ void phase_wo(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s, int ns, uint32_t par, int pos,
                                       int l, int tslot) {
-    prepare(L.dt_wo, s.xa, a.dim, s.prep);
+    if (!a.qx_attn) prepare(L.dt_wo, s.xa, a.dim, s.prep);              // else exchange 2 delivered it prepared
     trace<TRACE>(a, tslot, pos, l, 20);
     if (ns) stage_wait(a, s, par, pos, l);
     trace<TRACE>(a, tslot, pos, l, 21);
-    matvec_exact(L.dt_wo, L.wo, a.dim, role.wo0, role.wo1, s.prep, s.scratch, a.scratch_pairs, s.y, s.w + a.w_extra, ns);
+    matvec_exact(L.dt_wo, L.wo, a.dim, role.wo0, role.wo1, a.qx_attn ? s.pa : s.prep, s.scratch, a.scratch_pairs, s.y, s.w + a.w_extra, ns);
     trace<TRACE>(a, tslot, pos, l, 22);
     const int g0 = (a.sh.d_off + role.wo0) * kTile, n = min((a.sh.d_off + role.wo1) * kTile, a.dim) - g0;
     if (L.bo) {
@@ -572,11 +619,11 @@ __device__ __noinline__ void ffn_gate(const DecodeArgs &a, const LayerDev &L, co
 template <bool TRACE>
 __device__ __noinline__ void phase_down(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s, int ns, uint32_t par, int pos,
                                         int l, int tslot) {
-    prepare(L.dt_down, s.xh, a.ffn, s.prep);
+    if (!a.qx_h) prepare(L.dt_down, s.xh, a.ffn, s.prep);               // else exchange 4 delivered it prepared
     trace<TRACE>(a, tslot, pos, l, 23);
     if (ns) stage_wait(a, s, par, pos, l);
     trace<TRACE>(a, tslot, pos, l, 24);
-    matvec_exact(L.dt_down, L.down, a.ffn, role.dn0, role.dn1, s.prep, s.scratch, a.scratch_pairs, s.y, s.w, ns);
+    matvec_exact(L.dt_down, L.down, a.ffn, role.dn0, role.dn1, a.qx_h ? s.ph : s.prep, s.scratch, a.scratch_pairs, s.y, s.w, ns);
     trace<TRACE>(a, tslot, pos, l, 25);
     const int g0 = (a.sh.d_off + role.dn0) * kTile, n = min((a.sh.d_off + role.dn1) * kTile, a.dim) - g0;
     if (L.b_down) {
@@ -1036,7 +1083,8 @@ __device__ __noinline__ void run_layer(const DecodeArgs &a, const LayerDev *laye
     if (role.ffn0 < role.ffn1) {
         ffn_gate<GPT2>(a, L, role, s);
         const int g0 = (a.sh.f_off + role.ffn0) * kTile, n = min((a.sh.f_off + role.ffn1) * kTile, a.ffn) - g0;
-        if (a.async_x) scatter_tx(s.tmp, s.xh, g0, n, s.xbar + 3);
+        if (a.qx_h) scatter_q8(s.tmp, g0, n, s.pa, s.ph, s.xbar + 3);    // pa is free again once phase B is done
+        else if (a.async_x) scatter_tx(s.tmp, s.xh, g0, n, s.xbar + 3);
         else scatter(s.tmp, s.xh, g0, n);
         if (multi) peer_send(a, kXH, s.tmp, g0, n, step);
     }

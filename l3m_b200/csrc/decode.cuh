@@ -138,6 +138,12 @@ struct DecodeArgs {
     // cluster barriers; set when every CTA of the cluster produces qkv rows, which orders every
     // buffer's next write after all its reads (see decode.cu).
     int async_x, sm_xbar;
+    // Exchanges 2 (attention output) and 4 (gate output) as prepared q8 blocks instead of floats: the
+    // producer quantises its own whole blocks and stores them, with their scales and sums, straight into
+    // every CTA's activation for wo (sm_pa_*) or down (sm_ph_*), so phases B and D need no prepare. Set
+    // when single-GPU, async exchanges, the matrix quantised, and every producer's outputs whole blocks.
+    int qx_attn, qx_h;
+    int sm_pa_q8, sm_pa_scale, sm_pa_sum, sm_ph_q8, sm_ph_scale, sm_ph_sum;
     int cold;                           // reference --cold (engine.c:330-338): before every position the layer cluster
                                         // streams cold_bytes (1.5 x L2) of scratch through its shared memory, evicting the
                                         // weights from L2 (timed apart); weight copies carry an L2 evict-first policy

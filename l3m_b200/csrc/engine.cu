@@ -485,6 +485,12 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     a.sm_scale = take(nb * 4);
     a.sm_sum = take(nb * 4);
     a.sm_xf = take(mx * 4);
+    a.sm_pa_q8 = take(dim);                                            // the q8 exchanges' receive buffers
+    a.sm_pa_scale = take((dim / 32 + 1) * 4);
+    a.sm_pa_sum = take((dim / 32 + 1) * 4);
+    a.sm_ph_q8 = take(ffn);
+    a.sm_ph_scale = take((ffn / 32 + 1) * 4);
+    a.sm_ph_sum = take((ffn / 32 + 1) * 4);
     a.sm_y = take(max_tiles * L3M_TILE * 4);
     a.sm_scores = take(m->ctx * 4);
     a.sm_kv = take(2 * hd * 2);
@@ -562,6 +568,23 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
         std::vector<l3m::Role> rs0 = make_roles(GT, helpers_only);
         for (int c = 0; c < G; c++)
             if (rs0[c].qkv0 >= rs0[c].qkv1) a.async_x = 0;
+        // The q8 exchanges need whole blocks from every producer: a head's hd outputs, each ffn CTA's
+        // rows; and quantised wo / down in every layer (the activation is then the q8 prepare's).
+        const bool q8 = a.async_x && m->n_gpus == 1 && !getenv("L3M_FLOAT_EXCHANGES");
+        bool wo_q = true, down_q = true;
+        for (const l3m::LayerDev &d : layers) {
+            wo_q = wo_q && d.dt_wo >= l3m::DT_Q8;
+            down_q = down_q && d.dt_down >= l3m::DT_Q8;
+        }
+        bool ffn_blocks = ffn % 32 == 0;
+        for (int c = 0; c < G; c++) {
+            const l3m::Role &r = rs0[c];
+            if (r.ffn0 >= r.ffn1) continue;
+            const int g0 = r.ffn0 * L3M_TILE, n = std::min(r.ffn1 * L3M_TILE, ffn) - g0;
+            if (g0 % 32 || n % 32) ffn_blocks = false;
+        }
+        a.qx_attn = q8 && wo_q && hd % 32 == 0 && dim % 32 == 0;
+        a.qx_h = q8 && down_q && ffn_blocks;
     }
     {
         std::vector<l3m::Role> roles = make_roles(GT, helpers_only);

@@ -71,9 +71,12 @@ def main():
     m = l3m_b200.Model(str(path), ctx=ctx, force=True)
     prompt = synth.prompt(4, seed=1, vocab=32000)
     for _ in range(2):                                   # the second run is the one summarized
+        m.perf()
         m.generate(prompt, ctx - len(prompt), temperature=0)
+    dev = m.device_ns()
     p = m.perf()
-    print(f"{a.config}: {1e9 / p['ns_compute']:.1f} tok/s (device), {1e9 / p['ns_token']:.1f} tok/s (wall)")
+    print(f"{a.config}: {p['tokens'] * 1e9 / dev:.1f} tok/s (device), {1e9 / p['ns_token']:.1f} tok/s (wall), "
+          f"ns_wait {p['ns_wait']:.0f} per token")
     print(summarize(a.out))
     return 0
 
