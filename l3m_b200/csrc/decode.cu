@@ -345,43 +345,42 @@ __device__ __forceinline__ uint32_t xbytes(const DecodeArgs &a, int k) {
     return 4u * n;
 }
 
-// The q8 form of an exchange: src[0, n) (n a multiple of 32, this CTA's values g0.., g0 a multiple of
-// 32) quantised by warp 0 into stage (the prepare step, block by block), then every block's 32 bytes,
-// scale and sum stored into every CTA's dst at block g0 / 32 with st.async, completing on bar.
-__device__ __noinline__ void scatter_q8(const float *src, int g0, int n, const Prep &stage, const Prep &dst, unsigned long long *bar) {
-    const int tid = threadIdx.x, nblk = n / kQB, b0 = g0 / kQB;
-    if (tid < 32) {
-        const int j = tid & 7, sub = tid >> 3;
+// The q8 form of an exchange: src[0, n) (n a multiple of 32; this CTA's values g0.., g0 a multiple of
+// 32), one warp per 32-value block: each lane takes one value, the block's maximum and sum come from
+// warp shuffles (the prepare step's arithmetic, reference src/pack.c:101-122), the 32 bytes are packed
+// by shuffles, and lane r (r < 16) stores the first 16 bytes and the scale into CTA r, lane 16 + r the
+// last 16 bytes and the sum, with st.async completing on bar. src must be ready in shared memory.
+__device__ __noinline__ void scatter_q8(const float *src, int g0, int n, const Prep &dst, unsigned long long *bar) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nblk = n / kQB, r = lane & 15, half = lane >> 4;
+    uint32_t rb;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rb) : "r"((uint32_t)__cvta_generic_to_shared(bar)), "r"(r));
 #pragma unroll 1
-        for (int bq = 0; bq < nblk; bq += 4) {
-            const int b = bq + sub;
-            const bool ok = b < nblk;
-            const float4 v = ok ? ((const float4 *)(src + b * kQB))[j] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            quant_block4(v, b, j, ok, stage);
-        }
-    }
-    __syncthreads();
-    const uint32_t lb = (uint32_t)__cvta_generic_to_shared(bar);
-    const uint32_t dq = (uint32_t)__cvta_generic_to_shared(dst.q8 + g0), ds = (uint32_t)__cvta_generic_to_shared(dst.scale + b0),
-                   dm = (uint32_t)__cvta_generic_to_shared(dst.sum + b0);
-    // per rank and block: two 16-byte pieces of q8, the scale, the sum
-#pragma unroll 1
-    for (int e = tid; e < 4 * nblk * kClusterCtas; e += blockDim.x) {
-        const int r = e % kClusterCtas, item = e / kClusterCtas, b = item >> 2, part = item & 3;
-        uint32_t rb;
-        asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rb) : "r"(lb), "r"(r));
-        if (part < 2) {
-            const uint4 v = *(const uint4 *)(stage.q8 + b * kQB + 16 * part);
-            uint32_t ra;
-            asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(dq + b * kQB + 16 * part), "r"(r));
-            asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];"
-                         ::"r"(ra), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(rb) : "memory");
-        } else {
-            const uint32_t w = part == 2 ? __float_as_uint(stage.scale[b]) : (uint32_t)stage.sum[b];
-            uint32_t ra;
-            asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"((part == 2 ? ds : dm) + 4 * b), "r"(r));
-            asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(ra), "r"(w), "r"(rb) : "memory");
-        }
+    for (int b = warp; b < nblk; b += (int)(blockDim.x >> 5)) {
+        const float v = src[b * kQB + lane];
+        const float av = fabsf(v);
+        float m = av > 0.0f ? av : 0.0f;                                  // a NaN never raises the maximum
+#pragma unroll
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        const float inv = m > 0.0f ? __fdiv_rn(127.0f, m) : 0.0f;
+        const int q = (int8_t)__float2int_rn(__fmul_rn(v, inv));
+        int sm = q;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+        uint32_t w = (uint32_t)(q & 0xFF) << (8 * (lane & 3));              // byte lane & 3 of word lane >> 2
+        w |= __shfl_xor_sync(0xffffffffu, w, 1);
+        w |= __shfl_xor_sync(0xffffffffu, w, 2);
+        uint32_t wv[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) wv[k] = __shfl_sync(0xffffffffu, w, 16 * half + 4 * k);
+        const int bg = g0 / kQB + b;
+        uint32_t ra, rs;
+        asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"((uint32_t)__cvta_generic_to_shared(dst.q8 + bg * kQB + 16 * half)), "r"(r));
+        asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];"
+                     ::"r"(ra), "r"(wv[0]), "r"(wv[1]), "r"(wv[2]), "r"(wv[3]), "r"(rb) : "memory");
+        const uint32_t sw = half ? (uint32_t)sm : __float_as_uint(__fdiv_rn(m, 127.0f));
+        const void *sd = half ? (const void *)(dst.sum + bg) : (const void *)(dst.scale + bg);
+        asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rs) : "r"((uint32_t)__cvta_generic_to_shared(sd)), "r"(r));
+        asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(rs), "r"(sw), "r"(rb) : "memory");
     }
 }
 
@@ -549,7 +548,7 @@ __device__ __noinline__ void phase_attention(const DecodeArgs &a, const LayerDev
     attend_exact<true>(y, kc, vc, hd, a.vstride, s.kcur, s.vcur, pos, hd, s.scores, s.att, s.red, a.etab, s.kvbuf, s.vtbuf,
                        a.attn_chunk, prestaged);
     trace<TRACE>(a, tslot, pos, l, 15);
-    if (a.qx_attn) scatter_q8(s.att, h * hd, hd, s.prep, s.pa, s.xbar + 1);   // prep is free during phase A
+    if (a.qx_attn) scatter_q8(s.att, h * hd, hd, s.pa, s.xbar + 1);
     else if (a.async_x) scatter_tx(s.att, s.xa, h * hd, hd, s.xbar + 1);
     else scatter(s.att, s.xa, h * hd, hd);
 }
@@ -1083,7 +1082,7 @@ __device__ __noinline__ void run_layer(const DecodeArgs &a, const LayerDev *laye
     if (role.ffn0 < role.ffn1) {
         ffn_gate<GPT2>(a, L, role, s);
         const int g0 = (a.sh.f_off + role.ffn0) * kTile, n = min((a.sh.f_off + role.ffn1) * kTile, a.ffn) - g0;
-        if (a.qx_h) scatter_q8(s.tmp, g0, n, s.pa, s.ph, s.xbar + 3);    // pa is free again once phase B is done
+        if (a.qx_h) scatter_q8(s.tmp, g0, n, s.ph, s.xbar + 3);
         else if (a.async_x) scatter_tx(s.tmp, s.xh, g0, n, s.xbar + 3);
         else scatter(s.tmp, s.xh, g0, n);
         if (multi) peer_send(a, kXH, s.tmp, g0, n, step);
