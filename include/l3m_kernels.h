@@ -77,8 +77,8 @@ L3M_API int l3m_gemv_dev(int exact, int dtype, float *y, const void *tiles, int 
 // fixed 4 MiB device buffer inside this library: q8_0/q4_0/mxfp4 only, at most 524,288 block
 // results per call (ntiles*16*k/32), larger calls return -1 and launch nothing. The buffer is
 // shared by all calls on a device, so overlapping calls (two streams or threads) race and must be
-// serialised. The first call on each device looks the buffer up; make it before any stream capture.
-// The address found is kept for the process's life, so do not reset a device this entry has used.
+// serialised. The first call on each device looks the buffer's address up and keeps it for the
+// process's life, so do not reset a device this entry has used.
 // Pointers must be 4-byte aligned (refused with -1 otherwise).
 L3M_API int l3m_gemv_splitk_dev(int dtype, float *y, const void *tiles, int ntiles, int k, const l3m_vec *x, void *stream);
 // One draw of the reference's temperature sampler (src/engine.c:98-101, 283-287, 370-384, one

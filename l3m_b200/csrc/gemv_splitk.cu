@@ -18,8 +18,7 @@
 //  - the scratch is one buffer per device and per process: calls that overlap on one device (two
 //    streams, two host threads) race on it and must be serialised by the caller;
 //  - the first call on each device looks up the buffer's address (cudaGetSymbolAddress, which may
-//    load this library's device code); make that first call before any stream capture;
-//  - that address is kept for the life of the process: it belongs to the device's context of the
+//    load this library's device code); that address is kept for the life of the process: it belongs to the device's context of the
 //    first call, so a device reset (cudaDeviceReset, or a reset of the primary context) while this
 //    library is loaded leaves it stale; do not reset a device that this entry point has used;
 //  - misaligned pointers (tiles, y, and x's q8, scale and sum must be 4-byte aligned) are refused

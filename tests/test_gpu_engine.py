@@ -130,6 +130,36 @@ def test_cold_matches_warm(gpu, models):
     assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
 
 
+def test_cold_flush_is_not_token_time(gpu, models):
+    """Cold mode evicts the weights before every position and, as the reference's --cold, leaves the
+    flush out of the counters: for this 2-layer model the device time per token stays within 1.5x of a
+    warm run's, while the flush (1.5 x L2 streamed per position, about 80 us) would more than double it."""
+    path = models[("gqa", "q8_0")]
+    out = {}
+    for cold in (False, True):
+        m = l3m_b200.Model(path, force=True, cold=cold)
+        m.generate(PROMPT, 24, temperature=0)
+        m.perf()
+        m.generate(PROMPT, 24, temperature=0)
+        dev = m.device_ns()
+        p = m.perf()
+        assert p["tokens"] == len(PROMPT) + 24 and dev > 0
+        assert 0 <= p["ns_wait"] <= p["ns_token"] and p["ns_compute"] == pytest.approx(p["ns_token"] - p["ns_wait"])
+        out[cold] = (dev / p["tokens"], p["ns_token"])
+        m.close()
+    assert out[True][0] < 1.5 * out[False][0], out
+
+
+@pytest.mark.parametrize("name,dt", [("gqa", "q8_0"), ("mha40", "q4_0"), ("gpt2s", "mxfp4")])
+def test_float_and_q8_exchanges_agree(gpu, models, monkeypatch, name, dt):
+    """The attention and gate outputs travel between CTAs either as floats (each receiver prepares
+    them) or as prepared q8 blocks from their producer: the same tokens and logits."""
+    _, t0, l0 = gpu_run(models[(name, dt)], PROMPT, 24)
+    monkeypatch.setenv("L3M_FLOAT_EXCHANGES", "1")
+    _, t1, l1 = gpu_run(models[(name, dt)], PROMPT, 24)
+    assert t0 == t1 and np.array_equal(l0.view(np.uint32), l1.view(np.uint32))
+
+
 def test_max_new_zero_gives_prompt_logits(gpu, oracle, models):
     path = models[("gqa", "q8_0")]
     m = l3m_b200.Model(path, force=True)

@@ -55,6 +55,21 @@ def test_splitk_equals_exact_gemv_twice(gpu, oracle, cuda, dtype, k, ntiles):
     cuda.free()
 
 
+@pytest.mark.parametrize("dtype,k,ntiles", [(2, 768, 2000), (3, 4096, 256), (4, 288, 18)])
+def test_const_tiles_flag_gives_the_same_y(gpu, oracle, cuda, dtype, k, ntiles):
+    """l3m_gemv_dev with the tiles declared constant (bit 1 of exact: the kernel may read them before
+    earlier work on the stream ends) computes the same y, on back-to-back calls."""
+    rng = np.random.default_rng(77 + dtype)
+    dt, dv, want = device_case(gpu, oracle, cuda, rng, dtype, k, ntiles)
+    m = ntiles * 16
+    y1, y2 = cuda.empty(4 * m), cuda.empty(4 * m)
+    for y in (y1, y2, y1):
+        assert gpu.l3m_gemv_dev(1 | 2, dtype, y, dt, ntiles, k, C.byref(dv), None) == 0, gpu.l3m_cuda_error()
+    a, b = cuda.get(y1, np.zeros(m, np.float32)), cuda.get(y2, np.zeros(m, np.float32))
+    assert np.array_equal(a.view(np.uint32), want.view(np.uint32)) and np.array_equal(b.view(np.uint32), want.view(np.uint32))
+    cuda.free()
+
+
 def test_splitk_rejects_what_it_cannot_hold(gpu, oracle, cuda):
     rng = np.random.default_rng(5)
     dt, dv, _ = device_case(gpu, oracle, cuda, rng, 2, 288, 1)
