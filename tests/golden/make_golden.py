@@ -1,7 +1,7 @@
 """Regenerate the golden fixtures in this directory from the reference (fpedd/l3m) itself.
 
 Run where the reference checkout and its compiled library exist (oracle/_ref, built by
-oracle/Makefile):  python tests/golden/make_golden.py [REFERENCE_CHECKOUT]
+oracle/Makefile):  python tests/golden/make_golden.py [REFERENCE_CHECKOUT] [--configs]
 
   ggml.json       ggml block bytes for the reference's own known-answer inputs (its
                   tests/unit/test_export.py:19-59), recomputed with its exporter and checked
@@ -12,6 +12,12 @@ oracle/Makefile):  python tests/golden/make_golden.py [REFERENCE_CHECKOUT]
                   kernel table on 1 and 3 cores (L3M_ISA=scalar), and its fp32 reference path;
                   and its sampled tokens (temperature 0.8 seed 7, 1.7 seed 123) on 1 core and
                   on the reference path.
+  configs.npz     the five BASELINE configs at full size (l3m_b200.synth.make, the bench's files and
+                  workload: the config's context, the bench's 4-token prompt, greedy to the end of the
+                  context): the reference's greedy tokens (scalar table, 8 cores: the same logits as
+                  one core) and a 16-byte sha256 prefix of every position's fp32 logits row, read in
+                  its on_token callback (its l3m_logits holds the position that produced the token)
+                  and after the call. `--configs` regenerates only this file.
 """
 import ctypes as C
 import hashlib
@@ -26,7 +32,8 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-_ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("L3M_REF_SRC")
+_args = [a for a in sys.argv[1:] if not a.startswith("--")]
+_ref = _args[0] if _args else os.environ.get("L3M_REF_SRC")
 if not _ref:
     sys.exit("usage: make_golden.py <reference checkout> (or set L3M_REF_SRC)")
 REF = Path(_ref)
@@ -130,14 +137,51 @@ def run_ref_sampled(lib, path, cores, reference, temp, seed):
     return toks
 
 
-def main():
-    (HERE / "ggml.json").write_text(json.dumps(ggml_golden(), indent=1))
+def row_digest(row):
+    """The first 16 bytes of the sha256 of one fp32 logits row (little-endian floats)."""
+    return np.frombuffer(hashlib.sha256(np.ascontiguousarray(row, dtype="<f4").tobytes()).digest()[:16], np.uint8)
+
+
+def config_streams(lib, cores=8):
+    """Greedy token stream and per-position logits digests of the reference on each BASELINE config."""
+    out = {}
+    cb_t = C.CFUNCTYPE(C.c_int, C.c_int32, C.c_void_p)
+    prompt = synth.prompt(4, seed=1, vocab=32000)
+    with tempfile.TemporaryDirectory() as tmp:
+        for name, (_, _, _, ctx) in synth.CONFIGS.items():
+            path = synth.make(name, tmp)
+            cpus = (C.c_int * cores)(*range(cores))
+            m = lib.l3m_load(os.fsencode(str(path)), C.byref(Opts(cpus=cpus, n_cpus=cores, ctx=ctx, force=1)))
+            assert m
+            V = lib.l3m_vocab(m)
+            toks, dig = [], []
+            cb = cb_t(lambda t, u: toks.append(t) or dig.append(row_digest(np.ctypeslib.as_array(lib.l3m_logits(m), shape=(V,)))) or 1)
+            pr = (C.c_int32 * len(prompt))(*prompt)
+            lib.l3m_generate(m, pr, len(prompt), ctx - len(prompt), 0.0, 0, cb, None)
+            dig.append(row_digest(np.ctypeslib.as_array(lib.l3m_logits(m), shape=(V,))))
+            lib.l3m_free(m)
+            out[f"{name}-tokens"] = np.array(toks, np.int32)
+            out[f"{name}-digests"] = np.stack(dig)
+            print(name, len(toks), "tokens")
+    return out
+
+
+def ref_lib():
     os.environ["L3M_ISA"] = "scalar"
     lib = C.CDLL(str(ROOT / "oracle/_ref/libl3m.so"))
     lib.l3m_load.restype, lib.l3m_load.argtypes = C.c_void_p, [C.c_char_p, C.POINTER(Opts)]
     lib.l3m_generate.argtypes = [C.c_void_p, C.POINTER(C.c_int32), C.c_int, C.c_int, C.c_float, C.c_uint64, C.c_void_p, C.c_void_p]
     lib.l3m_logits.restype, lib.l3m_logits.argtypes = C.POINTER(C.c_float), [C.c_void_p]
     lib.l3m_vocab.argtypes = lib.l3m_free.argtypes = [C.c_void_p]
+    return lib
+
+
+def main():
+    if "--configs" in sys.argv:
+        np.savez_compressed(HERE / "configs.npz", **config_streams(ref_lib()))
+        return
+    (HERE / "ggml.json").write_text(json.dumps(ggml_golden(), indent=1))
+    lib = ref_lib()
     hashes, arrays = {}, {}
     with tempfile.TemporaryDirectory() as tmp:
         for name, shape in SPECS.items():
@@ -171,6 +215,7 @@ def main():
                     arrays[f"{name}-{label}-{lab}-logits"] = lg
     (HERE / "models.json").write_text(json.dumps({"prompt": PROMPT, "steps": STEPS, "sha256": hashes}, indent=1))
     np.savez_compressed(HERE / "engine.npz", **arrays)
+    np.savez_compressed(HERE / "configs.npz", **config_streams(lib))
     print("wrote", ", ".join(p.name for p in HERE.iterdir() if p.suffix in (".json", ".npz")))
 
 

@@ -50,3 +50,33 @@ def test_config_stream_bit_exact(gpu, oracle_streams, name):
     assert toks == want_tokens
     bad = np.nonzero((lg.view(np.uint32) != want_logits.view(np.uint32)).any(axis=1))[0]
     assert bad.size == 0, f"first differing position {bad[0]}, max |diff| {np.abs(lg - want_logits).max()}"
+
+
+GOLDEN = np.load(os.path.join(os.path.dirname(__file__), "golden", "configs.npz"))
+
+
+def row_digest(row):
+    """tests/golden/make_golden.py's digest: the first 16 bytes of the sha256 of the fp32 row."""
+    import hashlib
+    return np.frombuffer(hashlib.sha256(np.ascontiguousarray(row, dtype="<f4").tobytes()).digest()[:16], np.uint8)
+
+
+@pytest.mark.parametrize("name", list(synth.CONFIGS))
+def test_config_stream_matches_reference_run(gpu, tmp_path_factory, name):
+    """Each config at full size and on the bench's own workload (its file, its context, the 4-token
+    prompt, greedy to the end of the context) against a recorded run of the reference itself
+    (tests/golden/configs.npz: its scalar table's tokens and a digest of every position's logits
+    row): the same tokens and every logits row bit-identical."""
+    _, _, _, ctx = synth.CONFIGS[name]
+    path = synth.make(name, tmp_path_factory.mktemp("bench_files"))
+    want_tokens, want_dig = GOLDEN[f"{name}-tokens"].tolist(), GOLDEN[f"{name}-digests"]
+    m = l3m_b200.Model(path, ctx=ctx, force=True)
+    dig = []
+    toks = m.generate(PROMPT, ctx - len(PROMPT), temperature=0, on_token=lambda t: dig.append(row_digest(m.logits)) or True)
+    dig.append(row_digest(m.logits))
+    m.close()
+    assert toks == want_tokens
+    got = np.stack(dig)
+    assert got.shape == want_dig.shape
+    bad = np.nonzero((got != want_dig).any(axis=1))[0]
+    assert bad.size == 0, f"{bad.size} logits rows differ, the first at position {bad[0]}"
