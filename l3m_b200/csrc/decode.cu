@@ -1028,11 +1028,15 @@ __device__ __noinline__ void run_layer(const DecodeArgs &a, const LayerDev *laye
     if (role.head0 >= 0 && role.qkv0 >= role.qkv1)               // K/V copies land during Q (else started by phase_qkv)
         attend_prestage<true>(kcache(a, L, role.head0), vcache(a, L, role.head0), a.hd, a.vstride, pos, a.hd, s.kvbuf, s.vtbuf,
                               a.attn_chunk);
-    // Each phase: its matvec, the copy of the next phase's tiles (the staging area is free from
-    // here on), then the exchange.
+    // Each phase: its matvec, its exchange, and the copy of the next phase's tiles (the staging area
+    // is free once the matvec has read it). A copy landing in a CTA's shared memory delays the
+    // exchange stores arriving there, so no copy is in flight while an exchange's stores are: the
+    // wo and up/gate copies start once their exchange has arrived (each has the next phase's
+    // prelude, 3 to 5 us, to land in); the next layer's qkv copy, which has only the norm (weights
+    // from HBM when the model is larger than L2), starts right after the down exchange's stores;
+    // the down copy is issued before the gate, which outlasts it.
     if (role.qkv0 < role.qkv1) phase_qkv<GPT2, TRACE>(a, L, role, s, ns, wpar, pos, l, tslot);   // Q
     if (ns) wpar ^= 1;
-    ns = stage_issue(s, L.dt_wo, L.wo, a.dim, role.wo0, role.wo1, s.w + a.w_extra, L.st_wo, a.cold);
     trace<TRACE>(a, tslot, pos, l, 27);
     if (role.qkv0 < role.qkv1) {
         const int g0 = role.qkv0 * kTile, n = min(role.qkv1 * kTile, a.sh.n_qkv_g) - g0;
@@ -1044,6 +1048,7 @@ __device__ __noinline__ void run_layer(const DecodeArgs &a, const LayerDev *laye
     if (a.async_x) xwait(a, s, 0, xpar, xbytes(a, -1), pos, l);   // 1: qkv (this GPU's heads)
     else cluster_sync();
     st.wait_cyc += clock64() - w0;
+    ns = stage_issue(s, L.dt_wo, L.wo, a.dim, role.wo0, role.wo1, s.w + a.w_extra, L.st_wo, a.cold);
     trace<TRACE>(a, tslot, pos, l, 2);
     const uint32_t step = layer_step(a, pos, l);
     for (int h = role.head0; h >= 0 && h < a.sh.head_lo + a.sh.n_heads_g; h += kClusterCtas) {   // A
@@ -1059,8 +1064,6 @@ __device__ __noinline__ void run_layer(const DecodeArgs &a, const LayerDev *laye
     trace<TRACE>(a, tslot, pos, l, 4);
     if (role.wo0 < role.wo1) phase_wo<TRACE>(a, L, role, s, ns, wpar, pos, l, tslot);   // B
     if (ns) wpar ^= 1;
-    if (!L.gate && !(GPT2 && a.gelu)) ns = stage_issue(s, L.dt_up, L.up, a.dim, 2 * role.ffn0, 2 * role.ffn1, s.w, L.st_up, a.cold);
-    else ns = stage_issue(s, L.dt_up, L.up, a.dim, role.ffn0, role.ffn1, s.w, L.st_up, a.cold);
     trace<TRACE>(a, tslot, pos, l, 28);
     if (role.wo0 < role.wo1) {
         const int g0 = (a.sh.d_off + role.wo0) * kTile, n = min((a.sh.d_off + role.wo1) * kTile, a.dim) - g0;
@@ -1074,6 +1077,8 @@ __device__ __noinline__ void run_layer(const DecodeArgs &a, const LayerDev *laye
     else cluster_sync();
     if (multi) peer_recv(a, kXProj, s.xp, step, pos, l);
     st.wait_cyc += clock64() - w0;
+    if (!L.gate && !(GPT2 && a.gelu)) ns = stage_issue(s, L.dt_up, L.up, a.dim, 2 * role.ffn0, 2 * role.ffn1, s.w, L.st_up, a.cold);
+    else ns = stage_issue(s, L.dt_up, L.up, a.dim, role.ffn0, role.ffn1, s.w, L.st_up, a.cold);
     trace<TRACE>(a, tslot, pos, l, 6);
     phase_ffn<GPT2, TRACE>(a, L, role, s, pos, l, tslot, ns, wpar);      // C
     if (ns) wpar ^= 1;
@@ -1099,18 +1104,18 @@ __device__ __noinline__ void run_layer(const DecodeArgs &a, const LayerDev *laye
     trace<TRACE>(a, tslot, pos, l, 9);
     if (role.dn0 < role.dn1) phase_down<TRACE>(a, L, role, s, ns, wpar, pos, l, tslot);   // D
     if (ns) wpar ^= 1;
-    if (l + 1 < a.n_layers || !a.cold) {                          // cold: the next position's first copy follows its flush
-        const LayerDev &N = layers[l + 1 < a.n_layers ? l + 1 : 0];
-        ns = stage_issue(s, N.dt_qkv, N.qkv, a.dim, role.qkv0, role.qkv1, s.w + a.w_extra, N.st_qkv, a.cold);
-    } else {
-        ns = 0;
-    }
     trace<TRACE>(a, tslot, pos, l, 30);
     if (role.dn0 < role.dn1) {
         const int g0 = (a.sh.d_off + role.dn0) * kTile, n = min((a.sh.d_off + role.dn1) * kTile, a.dim) - g0;
         if (a.async_x) scatter_tx(s.y, s.xd, g0, n, s.xbar + 4);
         else scatter(s.y, s.xd, g0, n);
         if (multi) peer_send(a, kXDown, s.y, g0, n, step);
+    }
+    if (l + 1 < a.n_layers || !a.cold) {                          // cold: the next position's first copy follows its flush
+        const LayerDev &N = layers[l + 1 < a.n_layers ? l + 1 : 0];
+        ns = stage_issue(s, N.dt_qkv, N.qkv, a.dim, role.qkv0, role.qkv1, s.w + a.w_extra, N.st_qkv, a.cold);
+    } else {
+        ns = 0;
     }
     trace<TRACE>(a, tslot, pos, l, 10);
     w0 = clock64();

@@ -454,8 +454,13 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     a.rope = (m->flags & L3M_F_LEARNED_POS) ? nullptr : g.rope;
     if (l3m_expf_table(&a.etab)) { fprintf(stderr, "l3m: %s\n", l3m_cuda_error()); return false; }
     a.trace_cta[0] = a.trace_cta[1] = -1;
-    if (getenv("L3M_TRACE")) {                                         // phase time stamps of two CTAs: the first and a helper
-        a.trace_cta[0] = 0;
+    if (getenv("L3M_TRACE")) {                                         // phase time stamps of two CTAs: a layer CTA and a helper
+        const char *tc = getenv("L3M_TRACE_CTA");                      // which layer CTA (default the first)
+        a.trace_cta[0] = tc ? atoi(tc) : 0;
+        if (a.trace_cta[0] < 0 || a.trace_cta[0] >= l3m::kClusterCtas) {
+            fprintf(stderr, "l3m: L3M_TRACE_CTA must be a CTA of the layer cluster, 0..%d\n", l3m::kClusterCtas - 1);
+            return false;
+        }
         a.trace_cta[1] = GT > G ? G : G - 1;                            // a helper's head, when there are helpers
         g.trace_bytes = (size_t)2 * m->ctx * (L + 1) * l3m::kTraceEvents * sizeof(unsigned long long);
         if (!cuda_ok(cudaMalloc(&g.trace, g.trace_bytes), "trace")) return false;

@@ -1,6 +1,6 @@
 """Per-phase timing of the decode kernel, from the cycle stamps it writes when L3M_TRACE is set.
 
-    python -m l3m_b200.trace [--config SmolLM2-135M-q8_0] [--out /tmp/l3m_trace.bin]
+    python -m l3m_b200.trace [--config SmolLM2-135M-q8_0] [--out /tmp/l3m_trace.bin] [--ctas 0-15]
 
 Runs one greedy generation (the bench workload: the config's context, a 4-token prompt, the rest
 generated) of a synthetic model through ``l3m_b200.Model`` with tracing on, then prints for the two
@@ -8,6 +8,12 @@ traced CTAs (CTA 0 of the layer cluster, and the first helper CTA, or the last C
 cluster when the launch has no helpers) the median time, over layers and over the positions from 50
 on, of every traced event after the layer's start, the layer and token periods, and the head step. Times are SM cycles converted at the clock the header records (the
 maximum SM clock; the bench's clock samples show the part runs there under this load).
+
+With ``--ctas`` (a range of the layer cluster's CTAs) it traces each of those CTAs in turn
+(``L3M_TRACE_CTA``, one load and two generations per CTA) and prints one column per CTA: the median
+time of every layer event after that CTA's own layer start. The SM cycle counters of different SMs
+are not aligned, so columns compare durations, not instants: every CTA passes an exchange barrier
+when the last bytes land, so the CTA with the shortest barrier wait is the one the others wait for.
 """
 import argparse
 import os
@@ -18,12 +24,12 @@ import numpy as np
 # Event ids as stamped in csrc/decode.cu (per position and layer; the head uses layer index n_layers).
 LAYER_EVENTS = {
     16: "Q   rmsnorm (head CTAs: K/V copies issued meanwhile)", 17: "Q   prepare", 18: "Q   weight copy waited", 19: "Q   matvec",
-    27: "Q   next copy issued", 1: "Q   exchanged", 2: "    barrier 1",
+    27: "Q   bias", 1: "Q   exchanged", 2: "    barrier 1, wo copy issued",
     14: "A   RoPE + K/V row", 15: "A   attention", 3: "A   exchanged", 4: "    barrier 2",
-    20: "B   prepare", 21: "B   weight copy waited", 22: "B   matvec", 28: "B   next copy issued", 5: "B   exchanged", 6: "    barrier 3",
+    20: "B   prepare", 21: "B   weight copy waited", 22: "B   matvec", 28: "B   bias", 5: "B   exchanged", 6: "    barrier 3, up/gate copy issued",
     7: "C   x += proj, rmsnorm", 26: "C   prepare", 12: "C   weight copy waited", 13: "C   up/gate matvec", 29: "C   next copy issued",
     8: "C   SiLU gate exchanged", 9: "    barrier 4",
-    23: "D   prepare", 24: "D   weight copy waited", 25: "D   matvec", 30: "D   next copy issued", 10: "D   exchanged",
+    23: "D   prepare", 24: "D   weight copy waited", 25: "D   matvec", 30: "D   bias", 10: "D   exchanged, next qkv copy issued",
     11: "    barrier 5, x += down (layer end)",
 }
 HEAD_EVENTS = {3: "rmsnorm + prepare", 4: "-", 5: "matvec", 1: "argmax slot", 2: "token agreed"}
@@ -57,13 +63,55 @@ def summarize(path, first=50):
     return "\n".join(lines)
 
 
+def medians(path, first=50):
+    """{event: median ns after the layer start} of the traced layer CTA (slot 0)."""
+    raw = open(path, "rb").read()
+    ctx, L, _, last, _, _, E, khz = (int(v) for v in np.frombuffer(raw[:32], np.int32))
+    tt = (np.frombuffer(raw[32:], np.uint64).reshape(2, ctx, L + 1, E).astype(np.float64) / (khz / 1e6))[0, first:last]
+    out = {}
+    for ev in LAYER_EVENTS:
+        ok = (tt[:, :L, ev] > 0) & (tt[:, :L, 0] > 0)
+        if ok.any():
+            out[ev] = float(np.median((tt[:, :L, ev] - tt[:, :L, 0])[ok]))
+    out["period"] = float(np.median(tt[:, 1:L, 0] - tt[:, :L - 1, 0]))
+    return out
+
+
+def per_cta(config, ctas, out, models):
+    """One column per layer CTA (see the module docstring)."""
+    import l3m_b200
+    from l3m_b200 import synth
+    _, _, _, ctx = synth.CONFIGS[config]
+    path = synth.make(config, models)
+    prompt = synth.prompt(4, seed=1, vocab=32000)
+    cols = {}
+    for c in ctas:
+        os.environ["L3M_TRACE_CTA"] = str(c)
+        m = l3m_b200.Model(str(path), ctx=ctx, force=True)
+        for _ in range(2):
+            m.generate(prompt, ctx - len(prompt), temperature=0)
+        m.close()
+        cols[c] = medians(out)
+    order = sorted(LAYER_EVENTS, key=lambda e: cols[ctas[0]].get(e, 1e18))
+    lines = [f"{config}: median ns after each CTA's layer start", "event".ljust(44) + "".join(f"{c:>7d}" for c in ctas)]
+    for ev in order:
+        lines.append(LAYER_EVENTS[ev][:43].ljust(44) + "".join(f"{cols[c][ev]:7.0f}" if ev in cols[c] else "      -" for c in ctas))
+    lines.append("layer period".ljust(44) + "".join(f"{cols[c]['period']:7.0f}" for c in ctas))
+    return "\n".join(lines)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--config", default="SmolLM2-135M-q8_0")
     ap.add_argument("--out", default="/tmp/l3m_trace.bin")
     ap.add_argument("--models", default="/tmp/l3m_bench")
+    ap.add_argument("--ctas", default=None, help="a range of layer CTAs, e.g. 0-15: one column each")
     a = ap.parse_args()
     os.environ["L3M_TRACE"] = a.out
+    if a.ctas:
+        lo, _, hi = a.ctas.partition("-")
+        print(per_cta(a.config, list(range(int(lo), int(hi or lo) + 1)), a.out, a.models))
+        return 0
     import l3m_b200
     from l3m_b200 import synth
     _, _, _, ctx = synth.CONFIGS[a.config]
