@@ -88,8 +88,8 @@ __device__ __forceinline__ Smem carve(unsigned char *base, const DecodeArgs &a) 
     s.prep.scale = (float *)(base + a.sm_scale);
     s.prep.sum = (int32_t *)(base + a.sm_sum);
     s.prep.xf = (float *)(base + a.sm_xf);
-    s.pa = Prep{(int8_t *)(base + a.sm_pa_q8), (float *)(base + a.sm_pa_scale), (int32_t *)(base + a.sm_pa_sum), s.prep.xf};
-    s.ph = Prep{(int8_t *)(base + a.sm_ph_q8), (float *)(base + a.sm_ph_scale), (int32_t *)(base + a.sm_ph_sum), s.prep.xf};
+    s.pa = Prep{(int8_t *)(base + a.sm_pa_q8), (float *)(base + a.sm_pa_scale), (int32_t *)(base + a.sm_pa_sum), (float *)(base + a.sm_xa)};
+    s.ph = Prep{(int8_t *)(base + a.sm_ph_q8), (float *)(base + a.sm_ph_scale), (int32_t *)(base + a.sm_ph_sum), (float *)(base + a.sm_xh)};
     return s;
 }
 
@@ -126,7 +126,9 @@ __device__ __noinline__ void scatter(const float *src, float *dst, int g0, int n
 // The same with st.async: each 16- (or 4-) byte store completes its bytes on the receiving CTA's
 // mbarrier bar (this CTA's address of it, mapped per rank), so the receivers wait for their bytes
 // instead of a cluster barrier, and the sender does not wait for its stores to land.
-__device__ __noinline__ void scatter_tx(const float *src, float *dst, int g0, int n, unsigned long long *bar) {
+__device__ __forceinline__ float round_bf16(float v, bool r) { return r ? l3m_bf16_to_f32(l3m_f32_to_bf16(v)) : v; }
+// rb: each value rounded to bf16 first (the bf16 prepare's rounding).
+__device__ __noinline__ void scatter_tx(const float *src, float *dst, int g0, int n, unsigned long long *bar, bool rb = false) {
     const int tid = threadIdx.x, nth = blockDim.x;
     const uint32_t ld = (uint32_t)__cvta_generic_to_shared(dst + g0), lb = (uint32_t)__cvta_generic_to_shared(bar);
     if (((g0 | n) & 3) == 0) {
@@ -134,22 +136,23 @@ __device__ __noinline__ void scatter_tx(const float *src, float *dst, int g0, in
         #pragma unroll 1
         for (int e = tid; e < n4 * kClusterCtas; e += nth) {
             const int r = e % kClusterCtas, j = e / kClusterCtas;
-            uint32_t ra, rb;
+            uint32_t ra, rbar;
             asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(ld + 16 * j), "r"(r));
-            asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rb) : "r"(lb), "r"(r));
+            asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbar) : "r"(lb), "r"(r));
             const float4 v = ((const float4 *)src)[j];
             asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];"
-                         ::"r"(ra), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(rb) : "memory");
+                         ::"r"(ra), "f"(round_bf16(v.x, rb)), "f"(round_bf16(v.y, rb)), "f"(round_bf16(v.z, rb)), "f"(round_bf16(v.w, rb)),
+                         "r"(rbar) : "memory");
         }
     } else {
         #pragma unroll 1
         for (int e = tid; e < n * kClusterCtas; e += nth) {
             const int r = e % kClusterCtas, j = e / kClusterCtas;
-            uint32_t ra, rb;
+            uint32_t ra, rbar;
             asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(ld + 4 * j), "r"(r));
-            asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rb) : "r"(lb), "r"(r));
-            asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(ra), "r"(__float_as_uint(src[j])), "r"(rb)
-                         : "memory");
+            asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbar) : "r"(lb), "r"(r));
+            asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];"
+                         ::"r"(ra), "r"(__float_as_uint(round_bf16(src[j], rb))), "r"(rbar) : "memory");
         }
     }
 }
@@ -341,7 +344,7 @@ __device__ __forceinline__ int xlen(const DecodeArgs &a, int k) { return k == kX
 // or per 32-value block 40 (q8 bytes, scale, sum) for the q8 exchanges.
 __device__ __forceinline__ uint32_t xbytes(const DecodeArgs &a, int k) {
     const uint32_t n = (uint32_t)(k < 0 ? a.sh.n_qkv_g : a.sh.len[k][a.sh.gpu]);
-    if ((k == kXAttn && a.qx_attn) || (k == kXH && a.qx_h)) return n / kQB * 40u;
+    if ((k == kXAttn && a.qx_attn == kXQ8) || (k == kXH && a.qx_h == kXQ8)) return n / kQB * 40u;
     return 4u * n;
 }
 
@@ -548,8 +551,8 @@ __device__ __noinline__ void phase_attention(const DecodeArgs &a, const LayerDev
     attend_exact<true>(y, kc, vc, hd, a.vstride, s.kcur, s.vcur, pos, hd, s.scores, s.att, s.red, a.etab, s.kvbuf, s.vtbuf,
                        a.attn_chunk, prestaged);
     trace<TRACE>(a, tslot, pos, l, 15);
-    if (a.qx_attn) scatter_q8(s.att, h * hd, hd, s.pa, s.xbar + 1);
-    else if (a.async_x) scatter_tx(s.att, s.xa, h * hd, hd, s.xbar + 1);
+    if (a.qx_attn == kXQ8) scatter_q8(s.att, h * hd, hd, s.pa, s.xbar + 1);
+    else if (a.async_x) scatter_tx(s.att, s.xa, h * hd, hd, s.xbar + 1, a.qx_attn == kXPrepBF16);
     else scatter(s.att, s.xa, h * hd, hd);
 }
 
@@ -558,11 +561,12 @@ __device__ __noinline__ void phase_attention(const DecodeArgs &a, const LayerDev
 template <bool TRACE>
 __device__ __noinline__ void phase_wo(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s, int ns, uint32_t par, int pos,
                                       int l, int tslot) {
-    if (!a.qx_attn) prepare(L.dt_wo, s.xa, a.dim, s.prep);              // else exchange 2 delivered it prepared
+    if (a.qx_attn == kXFloat) prepare(L.dt_wo, s.xa, a.dim, s.prep);     // else exchange 2 delivered it prepared
     trace<TRACE>(a, tslot, pos, l, 20);
     if (ns) stage_wait(a, s, par, pos, l);
     trace<TRACE>(a, tslot, pos, l, 21);
-    matvec_exact(L.dt_wo, L.wo, a.dim, role.wo0, role.wo1, a.qx_attn ? s.pa : s.prep, s.scratch, a.scratch_pairs, s.y, s.w + a.w_extra, ns);
+    matvec_exact(L.dt_wo, L.wo, a.dim, role.wo0, role.wo1, a.qx_attn != kXFloat ? s.pa : s.prep, s.scratch, a.scratch_pairs, s.y,
+                 s.w + a.w_extra, ns);
     trace<TRACE>(a, tslot, pos, l, 22);
     const int g0 = (a.sh.d_off + role.wo0) * kTile, n = min((a.sh.d_off + role.wo1) * kTile, a.dim) - g0;
     if (L.bo) {
@@ -618,11 +622,11 @@ __device__ __noinline__ void ffn_gate(const DecodeArgs &a, const LayerDev &L, co
 template <bool TRACE>
 __device__ __noinline__ void phase_down(const DecodeArgs &a, const LayerDev &L, const Role &role, const Smem &s, int ns, uint32_t par, int pos,
                                         int l, int tslot) {
-    if (!a.qx_h) prepare(L.dt_down, s.xh, a.ffn, s.prep);               // else exchange 4 delivered it prepared
+    if (a.qx_h == kXFloat) prepare(L.dt_down, s.xh, a.ffn, s.prep);      // else exchange 4 delivered it prepared
     trace<TRACE>(a, tslot, pos, l, 23);
     if (ns) stage_wait(a, s, par, pos, l);
     trace<TRACE>(a, tslot, pos, l, 24);
-    matvec_exact(L.dt_down, L.down, a.ffn, role.dn0, role.dn1, a.qx_h ? s.ph : s.prep, s.scratch, a.scratch_pairs, s.y, s.w, ns);
+    matvec_exact(L.dt_down, L.down, a.ffn, role.dn0, role.dn1, a.qx_h != kXFloat ? s.ph : s.prep, s.scratch, a.scratch_pairs, s.y, s.w, ns);
     trace<TRACE>(a, tslot, pos, l, 25);
     const int g0 = (a.sh.d_off + role.dn0) * kTile, n = min((a.sh.d_off + role.dn1) * kTile, a.dim) - g0;
     if (L.b_down) {
@@ -793,44 +797,14 @@ __device__ __noinline__ int sample_token(const SampleIn &in, float *xs, float *t
     return t == 0x7FFFFFFF ? V - 1 : t;
 }
 
-__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t *p) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-// Thread 0 waits until *p >= want (or, with done_ok, *p == kHeadDone), sleeping between polls; the
-// whole CTA learns the outcome: 1 reached, 0 done, -1 timeout or another CTA's abort.
-__device__ __noinline__ int wait_word(const DecodeArgs &a, const uint32_t *p, uint32_t want, bool done_ok, int pos, int wait) {
-    __shared__ int res;
-    if (threadIdx.x == 0) {
-        const uint64_t t0 = globaltimer_ns();
-        int r = -1;
-        for (int spins = 0;; spins++) {
-            const uint32_t v = ld_acquire_u32(p);
-            if (done_ok && v == kHeadDone) { r = 0; break; }
-            if (v >= want && v != kHeadDone) { r = 1; break; }
-            __nanosleep(32);
-            if ((spins & 255) == 255) {
-                if (globaltimer_ns() - t0 > a.hx.timeout_ns) { record_abort(a, kErrTimeout, pos, -1, wait); break; }
-                if (aborted(a)) break;
-            }
-        }
-        res = r;
-    }
-    __syncthreads();
-    const int r = res;
-    __syncthreads();
-    return r;
-}
-
 // The head matvec over this CTA's vocabulary tiles of the final x in s.x (logits kept for
-// l3m_logits), this CTA's argmax -> hx.slots[cta] with an arrival on hx.count. host_stop: the
-// host's stop request (cluster 0, CTA 0 only). GPT2: the final LayerNorm.
+// l3m_logits), this CTA's (max, index) in s.tmp[0..1] and, with several clusters, posted as its slot
+// word for the tcount-th sampled position (a release store after the barrier that ends the logits
+// stores). host_stop: the host's stop request (cluster 0, CTA 0 only). GPT2: the final LayerNorm.
 // staged, ns: the first ns of the CTA's tiles are resident in shared memory (helper CTAs).
 template <bool GPT2, bool TRACE>
 __device__ __noinline__ void head_logits(const DecodeArgs &a, const Role &role, const Smem &s, int pos, int host_stop, int tslot,
-                                         const uint8_t *staged = nullptr, int ns = 0) {
+                                         uint32_t tcount, const uint8_t *staged = nullptr, int ns = 0) {
     const int cta = blockIdx.x, tid = threadIdx.x, nth = blockDim.x;
     float best = -INFINITY;
     int best_i = -1;
@@ -876,15 +850,70 @@ __device__ __noinline__ void head_logits(const DecodeArgs &a, const Role &role, 
             if (v > m || (v == m && vi >= 0 && (mi < 0 || vi < mi))) { m = v; mi = vi; }
         }
         if (mi < 0) mi = (a.sh.v_off + role.voc0) * kTile;                   // an empty or all-NaN slice
-        s.tmp[0] = m;                                                         // also kept here for a one-cluster launch
+        s.tmp[0] = m;                                                         // for a one-cluster launch
         s.tmp[1] = __int_as_float(mi);
         s.tmp[2] = __int_as_float(host_stop);
-        a.hx.slots[3 * cta] = m;
-        a.hx.slots[3 * cta + 1] = __int_as_float(mi);
-        a.hx.slots[3 * cta + 2] = __int_as_float(host_stop);
-        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.hx.count) : "memory");
+        if (a.grid > kClusterCtas && cta >= a.slot_lo) {
+            const unsigned long long w = (unsigned long long)(head_epoch(tcount) << 24 | (uint32_t)mi) << 32 | __float_as_uint(m);
+            asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(a.hx.slots + cta), "l"(w) : "memory");
+        }
     }
     __syncthreads();
+}
+
+// Thread 0 of a helper: the next published position (epoch e of the x words): 1 and *pos, 0 when
+// generation has ended (kHeadDone), -1 on the time limit or another CTA's abort. Sleeps between polls
+// (the helpers wait through every layer of every position). The whole CTA learns the outcome.
+__device__ __noinline__ int wait_published(const DecodeArgs &a, uint32_t e, int *pos) {
+    __shared__ int res, where;
+    if (threadIdx.x == 0) {
+        const unsigned long long *p = a.hx.xw + a.dim;
+        const uint64_t t0 = globaltimer_ns();
+        int r = -1;
+        for (int spins = 0;; spins++) {
+            unsigned long long v;
+            asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+            if ((uint32_t)(v >> 32) == e) {
+                r = (uint32_t)v == kHeadDone ? 0 : 1;
+                where = (int)(uint32_t)v;
+                break;
+            }
+            __nanosleep(32);
+            if ((spins & 255) == 255) {
+                if (globaltimer_ns() - t0 > a.hx.timeout_ns) { record_abort(a, kErrTimeout, -1, -1, kWaitHeadFlag); break; }
+                if (aborted(a)) break;
+            }
+        }
+        res = r;
+    }
+    __syncthreads();
+    const int r = res;
+    *pos = where;
+    __syncthreads();
+    return r;
+}
+
+// Every thread: x[i] = the value of x word i once it carries epoch e (its own bounded wait: the words
+// are written without a fence, so each may land after the position word). False on a failure.
+__device__ __noinline__ bool read_published_x(const DecodeArgs &a, uint32_t e, float *x, int pos) {
+    bool ok = true;
+#pragma unroll 1
+    for (int i = threadIdx.x; i < a.dim && ok; i += blockDim.x) {
+        unsigned long long v;
+        uint64_t t0 = 0;
+        for (int spins = 0;; spins++) {
+            asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(a.hx.xw + i) : "memory");
+            if ((uint32_t)(v >> 32) == e) break;
+            if (spins == 0) {
+                t0 = globaltimer_ns();
+            } else if ((spins & 63) == 0) {
+                if (aborted(a)) { ok = false; break; }
+                if (globaltimer_ns() - t0 > a.hx.timeout_ns) { record_abort(a, kErrTimeout, pos, -1, kWaitHeadFlag); ok = false; break; }
+            }
+        }
+        x[i] = __uint_as_float((uint32_t)v);
+    }
+    return __syncthreads_and(ok);
 }
 
 // Several GPUs: CTA 0 of each has its GPU's agreed (max, index, host stop, ok) in xt[0..3]. Its thread 0
@@ -940,7 +969,7 @@ __device__ __noinline__ void gpu_vote(const DecodeArgs &a, const Smem &s, uint32
     scatter(s.tmp, s.xt, 0, 4);
 }
 
-// A CTA outside cluster 0: between sampled positions it sleeps on hx.flag; for each published x it
+// A CTA outside cluster 0: between sampled positions it sleeps on the position word; for each published x it
 // computes its vocabulary tiles. Its shared memory holds no layer state, so as many of its tiles as
 // fit in the whole staging area are copied in once, at launch, and stay there for every position;
 // the rest are pulled into L2 ahead of each use (cold: every tile, every position). Ends when
@@ -954,14 +983,9 @@ __device__ __noinline__ void head_helper(const DecodeArgs &a, const Role &role, 
     if (!cold && rest0 < role.voc1 && threadIdx.x == 0) prefetch_l2(a.head + rest0 * th, (size_t)(role.voc1 - rest0) * th);
     bool landed = nres == 0;
     for (uint32_t e = 1;; e++) {
-        if (wait_word(a, a.hx.flag, e, true, -1, kWaitHeadFlag) <= 0) break;
-        const int pos = __float_as_int(ld_cg_f32(a.hx.x + a.dim));
-        if ((a.dim & 3) == 0)
-            #pragma unroll 1
-            for (int i = threadIdx.x * 4; i < a.dim; i += blockDim.x * 4) *(float4 *)(s.x + i) = __ldcg((const float4 *)(a.hx.x + i));
-        else
-            #pragma unroll 1
-            for (int i = threadIdx.x; i < a.dim; i += blockDim.x) s.x[i] = ld_cg_f32(a.hx.x + i);
+        int pos;
+        if (wait_published(a, e, &pos) <= 0) break;
+        if (!read_published_x(a, e, s.x, pos)) break;
         cp_async_wait_all();                                              // the final norm's weights
         if (!landed) {                                                    // the resident tiles (first position only)
             stage_wait(a, s, 0, pos, -1);
@@ -969,7 +993,7 @@ __device__ __noinline__ void head_helper(const DecodeArgs &a, const Role &role, 
         }
         __syncthreads();
         trace<TRACE>(a, tslot, pos, a.n_layers, 0);
-        head_logits<GPT2, TRACE>(a, role, s, pos, 0, tslot, s.w, nres);
+        head_logits<GPT2, TRACE>(a, role, s, pos, 0, tslot, e, s.w, nres);
         trace<TRACE>(a, tslot, pos, a.n_layers, 1);
         if (!cold && rest0 < role.voc1 && threadIdx.x == 0) prefetch_l2(a.head + rest0 * th, (size_t)(role.voc1 - rest0) * th);
     }
@@ -1087,8 +1111,8 @@ __device__ __noinline__ void run_layer(const DecodeArgs &a, const LayerDev *laye
     if (role.ffn0 < role.ffn1) {
         ffn_gate<GPT2>(a, L, role, s);
         const int g0 = (a.sh.f_off + role.ffn0) * kTile, n = min((a.sh.f_off + role.ffn1) * kTile, a.ffn) - g0;
-        if (a.qx_h) scatter_q8(s.tmp, g0, n, s.ph, s.xbar + 3);
-        else if (a.async_x) scatter_tx(s.tmp, s.xh, g0, n, s.xbar + 3);
+        if (a.qx_h == kXQ8) scatter_q8(s.tmp, g0, n, s.ph, s.xbar + 3);
+        else if (a.async_x) scatter_tx(s.tmp, s.xh, g0, n, s.xbar + 3, a.qx_h == kXPrepBF16);
         else scatter(s.tmp, s.xh, g0, n);
         if (multi) peer_send(a, kXH, s.tmp, g0, n, step);
     }
@@ -1243,55 +1267,77 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
         for (int l = 0; l < a.n_layers; l++) run_layer<GPT2, TRACE>(a, layers, l, role, s, pos, last, tslot, st);
         if (!last) continue;                                              // the next position starts from its embedding
         ++tcount;
-        // Publish x to every CTA of the launch (cluster 0's copies are identical), then this CTA's tiles.
+        // Publish x to every CTA of the launch (cluster 0's copies are identical) as epoch words, no
+        // fence: each word carries its own epoch. Then this CTA's tiles, if it has any.
         if (cta == 0 && a.grid > kClusterCtas) {
             #pragma unroll 1
-            for (int i = tid; i < a.dim; i += blockDim.x) a.hx.x[i] = s.x[i];
-            if (tid == 0) a.hx.x[a.dim] = __int_as_float(pos);
-            __syncthreads();
-            if (tid == 0) asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.hx.flag), "r"(tcount) : "memory");
+            for (int i = tid; i <= a.dim; i += blockDim.x) {
+                const uint32_t v = i < a.dim ? __float_as_uint(s.x[i]) : (uint32_t)pos;
+                asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(a.hx.xw + i), "l"((unsigned long long)tcount << 32 | v) : "memory");
+            }
         }
         trace<TRACE>(a, tslot, pos, a.n_layers, 0);
         int host_stop = 0;
         if (cta == 0 && tid == 0) host_stop = ld_relaxed_sys_i32((const int *)&a.ctrl->stop_request);
-        head_logits<GPT2, TRACE>(a, role, s, pos, host_stop, tslot);
+        if (a.grid == kClusterCtas || cta >= a.slot_lo) head_logits<GPT2, TRACE>(a, role, s, pos, host_stop, tslot, tcount);
         trace<TRACE>(a, tslot, pos, a.n_layers, 1);
         // One cluster: every CTA sends (max, index, host stop, no abort seen) to every CTA's xt[4 + 4 cta],
         // and after the barrier each reduces the same 16 slots in CTA order. Several clusters: CTA 0
-        // waits for every CTA's (max, index) in global memory (so every slice of the logits is written,
-        // also when nothing is sampled), reduces them in CTA order (vocabulary order, reference
-        // engine.c:299-300) and hands the result to cluster 0, so all 16 decide alike.
+        // waits for every posted slot word (one thread each, acquire: every slice of the logits is
+        // written before its slot, also when nothing is sampled), reduces them in CTA order (the
+        // vocabulary order, reference engine.c:299-300): the first CTA with the largest maximum; a slot
+        // whose maximum is not above -inf (an empty or all-NaN slice) never wins, and with no winner
+        // the token is 0 (the serial rule gmax = -inf; if (m > gmax) ...). The result goes to cluster
+        // 0, so all 16 decide alike.
         if (a.grid == kClusterCtas) {
             if (tid == 0) s.tmp[3] = __int_as_float(*(volatile int *)a.hx.abort_flag == 0 ? 1 : 0);
             __syncthreads();
             scatter(s.tmp, s.xt, 4 + 4 * cta, 4);
         } else if (cta == 0) {
-            const int r = wait_word(a, a.hx.count, tcount * (uint32_t)a.grid, false, pos, kWaitHeadCount);
-            // Warp 0 reduces the slots: the first CTA (in CTA order, the vocabulary order) with the
-            // largest maximum; a slot whose maximum is not above -inf (an empty or all-NaN slice) never
-            // wins, and with no winner the token is 0 (the serial rule gmax = -inf; if (m > gmax) ...).
-            if (tid < 32) {
-                float bm = -INFINITY;
-                int bc = a.grid;
+            const uint32_t e8 = head_epoch(tcount);
+            float bm = -INFINITY;
+            int bc = a.grid, bi = 0;
+            bool good = true;
 #pragma unroll 1
-                for (int c = tid; c < a.grid; c += 32) {                  // increasing c: strict > keeps the first
-                    const float m = ld_cg_f32(a.hx.slots + 3 * c);
-                    if (m > bm) { bm = m; bc = c; }
+            for (int c = a.slot_lo + tid; c < a.grid && good; c += blockDim.x) {   // increasing c: strict > keeps the first
+                unsigned long long w;
+                uint64_t t0 = 0;
+                for (int spins = 0;; spins++) {
+                    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(a.hx.slots + c) : "memory");
+                    if ((uint32_t)(w >> 56) == e8) break;
+                    if (spins == 0) {
+                        t0 = globaltimer_ns();
+                    } else if ((spins & 63) == 0) {
+                        if (aborted(a)) { good = false; break; }
+                        if (globaltimer_ns() - t0 > a.hx.timeout_ns) { record_abort(a, kErrTimeout, pos, -1, kWaitHeadCount); good = false; break; }
+                    }
                 }
+                const float m = __uint_as_float((uint32_t)w);
+                if (good && m > bm) { bm = m; bc = c; bi = (int)((w >> 32) & 0xFFFFFFu); }
+            }
+            trace<TRACE>(a, tslot, pos, a.n_layers, 6);
 #pragma unroll
-                for (int o = 16; o; o >>= 1) {
-                    const float om = __shfl_xor_sync(0xffffffffu, bm, o);
-                    const int oc = __shfl_xor_sync(0xffffffffu, bc, o);
-                    if (om > bm || (om == bm && oc < bc)) { bm = om; bc = oc; }
+            for (int o = 16; o; o >>= 1) {
+                const float om = __shfl_xor_sync(0xffffffffu, bm, o);
+                const int oc = __shfl_xor_sync(0xffffffffu, bc, o), oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (om > bm || (om == bm && oc < bc)) { bm = om; bc = oc; bi = oi; }
+            }
+            const int nw = (int)(blockDim.x >> 5);                        // 8 warps: 24 of red's 64 words
+            if ((tid & 31) == 0) { s.red[tid >> 5] = bm; ((int *)s.red)[nw + (tid >> 5)] = bc; ((int *)s.red)[2 * nw + (tid >> 5)] = bi; }
+            const bool all_good = __syncthreads_and(good);
+            if (tid == 0) {
+                for (int w = 1; w < nw; w++) {
+                    const float om = s.red[w];
+                    const int oc = ((int *)s.red)[nw + w];
+                    if (om > bm || (om == bm && oc < bc)) { bm = om; bc = oc; bi = ((int *)s.red)[2 * nw + w]; }
                 }
-                if (tid == 0) {
-                    s.tmp[0] = __int_as_float(bc < a.grid ? __float_as_int(ld_cg_f32(a.hx.slots + 3 * bc + 1)) : 0);
-                    s.tmp[1] = ld_cg_f32(a.hx.slots + 2);
-                    s.tmp[2] = __int_as_float(r > 0 && !*(volatile int *)a.hx.abort_flag ? 1 : 0);
-                    s.tmp[3] = bm;
-                }
+                s.tmp[0] = __int_as_float(bc < a.grid ? bi : 0);
+                s.tmp[1] = __int_as_float(host_stop);
+                s.tmp[2] = __int_as_float(all_good && !*(volatile int *)a.hx.abort_flag ? 1 : 0);
+                s.tmp[3] = bm;
             }
             __syncthreads();
+            trace<TRACE>(a, tslot, pos, a.n_layers, 7);
             scatter(s.tmp, s.xt, 0, 4);
         }
         const long long w6 = clock64();
@@ -1346,7 +1392,8 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
     if (tid == 0) a.hx.stats[cta] = st.wait_cyc;
     cluster_sync();                                                       // no CTA leaves while others may write its memory
     if (cta == 0 && tid == 0) {
-        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.hx.flag), "r"(kHeadDone) : "memory");   // the helpers stop
+        if (a.grid > kClusterCtas)                                        // the helpers stop
+            asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(a.hx.xw + a.dim), "l"((unsigned long long)(tcount + 1) << 32 | kHeadDone) : "memory");
         unsigned long long wsum = 0;
         for (int c = 0; c < kClusterCtas; c++) wsum += ((volatile unsigned long long *)a.hx.stats)[c];
         a.ctrl->wait_cyc = wsum;

@@ -45,31 +45,40 @@ constexpr int kMaxShardGpus = 8;      // GPUs one model can be split over
 constexpr int kClusterCtas = 16;      // one thread-block cluster runs the whole model
 constexpr int kTraceEvents = 32;      // stamps per (position, layer); see the trace() calls in decode.cu
 
-// The head phase runs on every CTA of the launch (several clusters): cluster 0 publishes x in
-// global memory with a release flag, every CTA computes its vocabulary tiles and adds (max, index)
-// with an arrival count that cluster 0 waits for. Waits are bounded by timeout_ns.
+// The head phase runs on the helper clusters (and, in cold mode, on cluster 0 too): cluster 0 publishes
+// x, every CTA with vocabulary tiles posts its (max, index), and CTA 0 reduces the posted slots. Waits
+// are bounded by timeout_ns.
+// The head's exchange between cluster 0 and the helper clusters, as self-validating 8-byte words (no
+// flag, no count, no fence between data and signal): xw[i] = {tcount << 32 | bits of x[i]}, the
+// final residual of the tcount-th sampled position, and xw[dim] = {tcount << 32 | position}, or
+// kHeadDone as the position when generation ends; slots[c] = {head_epoch(tcount) << 56 | index << 32
+// | bits of max}, CTA c's argmax (index < 2^24), written with a release so that the CTA's logits are
+// visible first. The buffer is zeroed before every launch and tcount starts at 1, so no stale word
+// carries a current epoch.
 struct HeadX {
-    float *x;                           // [dim] the final residual of the sampled position
-    uint32_t *flag;                     // tcount of the published x; kHeadDone when generation ends
-    uint32_t *count;                    // arrivals: grid per sampled position
-    float *slots;                       // [grid][2] (max, index bits)
+    unsigned long long *xw;             // [dim + 1]
+    unsigned long long *slots;          // [grid]; posted by CTAs slot_lo.. only
     int *abort_flag;                    // [0]: first error code of any CTA; [1..4]: where (as Ctrl::where)
     unsigned long long *stats;          // [kClusterCtas]: each layer-cluster CTA's wait cycles at the end
     unsigned long long timeout_ns;
 };
 constexpr uint32_t kHeadDone = 0xFFFFFFFFu;
+// The slot words' 8-bit epoch: 1..255, consecutive sampled positions always differ and none is 0.
+__host__ __device__ inline uint32_t head_epoch(uint32_t tcount) { return 1u + (tcount - 1u) % 255u; }
 // Error codes: a wait on another CTA gave up; a wait on a weight copy gave up; the launch does not
 // have the shape the kernel was built for (cluster size, cluster count, grid, block); a sampled token
 // outside the vocabulary.
 enum { kErrNone = 0, kErrTimeout = 1, kErrStageTimeout = 2, kErrShape = 3, kErrToken = 4 };
-// Which wait gave up (Ctrl::where[3]): exchanges 1-5 of a layer, the weight copy, the head job flag
-// (helper clusters), the head arrival count (CTA 0).
+// Which wait gave up (Ctrl::where[3]): exchanges 1-5 of a layer, the weight copy, the published x
+// (helper clusters), the posted argmax slots (CTA 0).
 enum { kWaitQkv = 1, kWaitAttn = 2, kWaitProj = 3, kWaitH = 4, kWaitDown = 5, kWaitStage = 8, kWaitHeadFlag = 9, kWaitHeadCount = 10,
        kWaitPeerAttn = 12, kWaitPeerProj = 13, kWaitPeerH = 14, kWaitPeerDown = 15, kWaitPeerToken = 16 };
 
 // The vectors GPUs exchange each layer when a model is split over several (the reference's four
 // all-gathers per layer, src/engine.c:254-274): attention output, wo output, gate output, down output.
 enum { kXAttn = 0, kXProj = 1, kXH = 2, kXDown = 3, kXKinds = 4 };
+// Forms of exchanges 2 and 4 (DecodeArgs::qx_attn, qx_h).
+enum { kXFloat = 0, kXQ8 = 1, kXPrepF32 = 2, kXPrepBF16 = 3 };
 
 // This GPU's share of an output-channel split over n_gpus GPUs (the reference's split over ranks,
 // src/engine.c:467-476, at tile granularity, then over the CTAs of the GPU): query heads
@@ -96,6 +105,8 @@ struct Shard {
 
 struct DecodeArgs {
     int dim, hd, ffn, vocab, ctx, n_heads, n_kv, hpk, n_layers, n_qkv, grid;   // n_qkv = (n_heads + 2 n_kv) hd; grid: all CTAs
+    int slot_lo;                        // several clusters: the first CTA that posts a head slot (the
+                                        // layer cluster posts none when the helpers take the whole head)
     HeadX hx;
     Shard sh;
     float eps;
@@ -138,10 +149,12 @@ struct DecodeArgs {
     // cluster barriers; set when every CTA of the cluster produces qkv rows, which orders every
     // buffer's next write after all its reads (see decode.cu).
     int async_x, sm_xbar;
-    // Exchanges 2 (attention output) and 4 (gate output) as prepared q8 blocks instead of floats: the
-    // producer quantises its own whole blocks and stores them, with their scales and sums, straight into
-    // every CTA's activation for wo (sm_pa_*) or down (sm_ph_*), so phases B and D need no prepare. Set
-    // when single-GPU, async exchanges, the matrix quantised, and every producer's outputs whole blocks.
+    // The form of exchanges 2 (attention output) and 4 (gate output), kX*: floats that phases B and D
+    // prepare for wo / down; or, single-GPU with async exchanges, the activation already prepared by its
+    // producer: q8 blocks with their scales and sums (the matrix quantised in every layer, every
+    // producer's outputs whole blocks) stored into every CTA's sm_pa_* / sm_ph_*, or floats as the
+    // matrix's prepare makes them (the same float dtype in every layer: bf16-rounded, or as they are)
+    // stored into xa / xh. Either way phases B and D run no prepare.
     int qx_attn, qx_h;
     int sm_pa_q8, sm_pa_scale, sm_pa_sum, sm_ph_q8, sm_ph_scale, sm_ph_sum;
     int cold;                           // reference --cold (engine.c:330-338): before every position the layer cluster

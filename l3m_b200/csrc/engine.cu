@@ -319,6 +319,7 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     // cross-cluster waits; for profilers that do not keep every cluster of a launch resident).
     if (const char *nc = getenv("L3M_CLUSTERS")) GT = std::max(G, std::min(GT, atoi(nc) * G));
     if (hd > l3m::kDecodeThreads) { fprintf(stderr, "l3m: head_dim %d above %d is not built\n", hd, l3m::kDecodeThreads); return false; }
+    if (V >= (1 << 24)) { fprintf(stderr, "l3m: a vocabulary of %d entries is not built (the head exchange holds indices below 2^24)\n", V); return false; }
 
     // Streamed weights first (one contiguous range for the persisting window), then the rest.
     Stage s;
@@ -573,9 +574,10 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
         std::vector<l3m::Role> rs0 = make_roles(GT, helpers_only);
         for (int c = 0; c < G; c++)
             if (rs0[c].qkv0 >= rs0[c].qkv1) a.async_x = 0;
-        // The q8 exchanges need whole blocks from every producer: a head's hd outputs, each ffn CTA's
-        // rows; and quantised wo / down in every layer (the activation is then the q8 prepare's).
-        const bool q8 = a.async_x && m->n_gpus == 1 && !getenv("L3M_FLOAT_EXCHANGES");
+        // Prepared exchanges (one GPU, st.async exchanges; L3M_FLOAT_EXCHANGES=1 keeps plain floats). The
+        // q8 form needs whole blocks from every producer: a head's hd outputs, each ffn CTA's rows; and
+        // quantised wo / down in every layer (the activation is then the q8 prepare's).
+        const bool prepared = a.async_x && m->n_gpus == 1 && !getenv("L3M_FLOAT_EXCHANGES");
         bool wo_q = true, down_q = true;
         for (const l3m::LayerDev &d : layers) {
             wo_q = wo_q && d.dt_wo >= l3m::DT_Q8;
@@ -588,8 +590,17 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
             const int g0 = r.ffn0 * L3M_TILE, n = std::min(r.ffn1 * L3M_TILE, ffn) - g0;
             if (g0 % 32 || n % 32) ffn_blocks = false;
         }
-        a.qx_attn = q8 && wo_q && hd % 32 == 0 && dim % 32 == 0;
-        a.qx_h = q8 && down_q && ffn_blocks;
+        // Float matrices: the producers round to the matrix's prepare form, when every layer's matrix is
+        // that same float dtype.
+        auto float_form = [&](bool is_wo) {
+            const int d0 = is_wo ? layers[0].dt_wo : layers[0].dt_down;
+            if (d0 != l3m::DT_F32 && d0 != l3m::DT_BF16) return (int)l3m::kXFloat;
+            for (const l3m::LayerDev &d : layers)
+                if ((is_wo ? d.dt_wo : d.dt_down) != d0) return (int)l3m::kXFloat;
+            return d0 == l3m::DT_BF16 ? (int)l3m::kXPrepBF16 : (int)l3m::kXPrepF32;
+        };
+        a.qx_attn = !prepared ? l3m::kXFloat : wo_q && hd % 32 == 0 && dim % 32 == 0 ? l3m::kXQ8 : float_form(true);
+        a.qx_h = !prepared ? l3m::kXFloat : down_q && ffn_blocks ? l3m::kXQ8 : float_form(false);
     }
     {
         std::vector<l3m::Role> roles = make_roles(GT, helpers_only);
@@ -597,14 +608,17 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
         cudaMemcpy(g.roles, roles.data(), sizeof(l3m::Role) * GT, cudaMemcpyHostToDevice);
         a.roles = g.roles;
     }
-    g.hx_bytes = (size_t)(dim + 4) * 4 + 256 + (size_t)3 * GT * 4 + 8 + l3m::kClusterCtas * 8;
-    if (!cuda_ok(cudaMalloc(&g.hx, g.hx_bytes), "head exchange")) return false;
-    a.hx.x = (float *)g.hx;
-    a.hx.flag = (uint32_t *)((char *)g.hx + (size_t)(dim + 4) * 4);
-    a.hx.count = a.hx.flag + 32;
-    a.hx.abort_flag = (int *)(a.hx.flag + 16);
-    a.hx.slots = (float *)(a.hx.flag + 64);
-    a.hx.stats = (unsigned long long *)(((uintptr_t)(a.hx.slots + 3 * GT) + 7) & ~(uintptr_t)7);
+    {                                                                  // x words, abort word, slots, statistics
+        const size_t x_bytes = ((size_t)(dim + 1) * 8 + 255) & ~(size_t)255, slot_bytes = ((size_t)GT * 8 + 255) & ~(size_t)255;
+        g.hx_bytes = x_bytes + 256 + slot_bytes + l3m::kClusterCtas * 8;
+        if (!cuda_ok(cudaMalloc(&g.hx, g.hx_bytes), "head exchange")) return false;
+        char *b = (char *)g.hx;
+        a.hx.xw = (unsigned long long *)b;
+        a.hx.abort_flag = (int *)(b + x_bytes);
+        a.hx.slots = (unsigned long long *)(b + x_bytes + 256);
+        a.hx.stats = (unsigned long long *)(b + x_bytes + 256 + slot_bytes);
+    }
+    a.slot_lo = helpers_only ? G : 0;
     if (m->cold) {                                                     // 1.5 x L2, in whole copies per CTA of the cluster
         a.cold_chunk = std::min(a.w_extra, 64 << 10) & ~15;
         const unsigned long long unit = (unsigned long long)G * a.cold_chunk;
@@ -707,7 +721,7 @@ void report_decode_error(const l3m::Ctrl *c) {
                 l3m::kDecodeThreads, e);
     } else {
         static const char *waits[] = {"?", "exchange 1 (qkv)", "exchange 2 (attention)", "exchange 3 (wo)", "exchange 4 (ffn gate)",
-                                      "exchange 5 (down)", "?", "?", "a weight copy", "the head job flag", "the head arrivals"};
+                                      "exchange 5 (down)", "?", "?", "a weight copy", "the published x", "the posted head slots"};
         const int w = c->where[3];
         const char *what = e == l3m::kErrTimeout ? "a wait on another CTA gave up" : e == l3m::kErrStageTimeout ? "a weight copy wait gave up"
                            : e == l3m::kErrToken ? "a sampled token outside the vocabulary" : "unknown error";
@@ -912,7 +926,7 @@ L3M_API int l3m_generate(l3m_model *m, const int32_t *prompt, int n_prompt, int 
         a.sh.all_logits = a.temp > 0.0f;                               // every GPU samples from the whole row
         cudaMemcpyAsync(gi.prompt, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, gi.stream);
         cudaMemcpyAsync(gi.args_dev, &a, sizeof a, cudaMemcpyHostToDevice, gi.stream);
-        cudaMemsetAsync(gi.hx, 0, gi.hx_bytes, gi.stream);              // flag, count and abort word start at 0
+        cudaMemsetAsync(gi.hx, 0, gi.hx_bytes, gi.stream);              // no head word carries an epoch; abort word 0
         cudaEventRecord(gi.ev0, gi.stream);
         if (l3m_decode_launch(&a, gi.args_dev, gi.stream)) return -1;
         cudaEventRecord(gi.ev1, gi.stream);

@@ -119,24 +119,28 @@ L3M_EXPF_HD float l3m_expf_candidate(float x, int *check, float *other) {
 #define L3M_EXPF_PROBES 64
 L3M_EXPF_HD uint32_t l3m_expf_slot(uint32_t u) { return (uint32_t)(u * 0x9E3779B1u) >> (32 - L3M_EXPF_HASH_BITS); }
 
-// One slot. On the device with an L2 evict-last policy: the table is prefetched into L2 with the same
-// policy when a decode launch starts, so the rare lookups stay in L2 while the weights stream past.
-L3M_EXPF_HD uint32_t l3m_expf_slot_load(const uint32_t *table, uint32_t i) {
+// One slot. On the device with an L2 evict-last policy (pol): the table is prefetched into L2 with the
+// same policy when a decode launch starts, so the rare lookups stay in L2 while the weights stream past.
+L3M_EXPF_HD uint32_t l3m_expf_slot_load(const uint32_t *table, uint32_t i, uint64_t pol) {
 #ifdef __CUDA_ARCH__
-    uint64_t pol;
     uint32_t v;
-    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
     asm volatile("ld.global.nc.L2::cache_hint.u32 %0, [%1], %2;" : "=r"(v) : "l"(table + i), "l"(pol));
     return v;
 #else
+    (void)pol;
     return table[i];
 #endif
 }
 
 L3M_EXPF_HD int l3m_expf_listed(uint32_t u, const uint32_t *table) {
     uint32_t i = l3m_expf_slot(u);
-    for (int p = 0; p < L3M_EXPF_PROBES; p++) {
-        const uint32_t v = l3m_expf_slot_load(table, i);
+    uint64_t pol = 0;
+#ifdef __CUDA_ARCH__
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+#pragma unroll 1
+#endif
+    for (int p = 0; p < L3M_EXPF_PROBES; p++) {                // kept rolled: the first probe almost always ends it
+        const uint32_t v = l3m_expf_slot_load(table, i, pol);
         if (v == u) return 1;
         if (v == L3M_EXPF_EMPTY) return 0;
         i = (i + 1) & (L3M_EXPF_SLOTS - 1);

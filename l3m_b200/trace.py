@@ -57,6 +57,10 @@ def summarize(path, first=50):
             tok = np.diff(tt[:, 0, 0])
             lines.append(f"   layer period {np.median(lay):.0f} ns, token period {np.median(tok):.0f} ns")
             lines.append(f"   head (ns): x published to token agreed {np.median(h[:, 2] - h[:, 0]):.0f}")
+            if (h[:, 6] > 0).any():                                     # several clusters: where CTA 0 waits
+                parts = [f"{name} {np.median(h[:, e] - h[:, p]):.0f}" for p, e, name in
+                         ((0, 1, "own slot"), (1, 6, "every arrival seen"), (6, 7, "slots reduced"), (7, 2, "token agreed"))]
+                lines.append("   head steps (ns): " + ", ".join(parts))
         else:                                                           # a helper: its head step from the published x
             parts = [f"{HEAD_EVENTS[e]} {np.median(h[:, e] - h[:, p]):.0f}" for p, e in ((0, 3), (3, 4), (4, 5), (5, 1))]
             lines.append("   head step (ns): " + ", ".join(parts))

@@ -150,10 +150,12 @@ def test_cold_flush_is_not_token_time(gpu, models):
     assert out[True][0] < 1.5 * out[False][0], out
 
 
-@pytest.mark.parametrize("name,dt", [("gqa", "q8_0"), ("mha40", "q4_0"), ("gpt2s", "mxfp4")])
-def test_float_and_q8_exchanges_agree(gpu, models, monkeypatch, name, dt):
+@pytest.mark.parametrize("name,dt", [("gqa", "q8_0"), ("mha40", "q4_0"), ("gpt2s", "mxfp4"), ("gqa", "bf16"), ("mha40", "f32"),
+                                     ("gpt2s", "bf16")])
+def test_prepared_and_float_exchanges_agree(gpu, models, monkeypatch, name, dt):
     """The attention and gate outputs travel between CTAs either as floats (each receiver prepares
-    them) or as prepared q8 blocks from their producer: the same tokens and logits."""
+    them) or already prepared by their producer (q8 blocks for quantised wo / down, bf16-rounded or
+    plain floats for bf16 / f32 ones): the same tokens and logits."""
     _, t0, l0 = gpu_run(models[(name, dt)], PROMPT, 24)
     monkeypatch.setenv("L3M_FLOAT_EXCHANGES", "1")
     _, t1, l1 = gpu_run(models[(name, dt)], PROMPT, 24)
