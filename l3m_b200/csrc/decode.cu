@@ -126,9 +126,11 @@ __device__ __noinline__ void scatter(const float *src, float *dst, int g0, int n
 // The same with st.async: each 16- (or 4-) byte store completes its bytes on the receiving CTA's
 // mbarrier bar (this CTA's address of it, mapped per rank), so the receivers wait for their bytes
 // instead of a cluster barrier, and the sender does not wait for its stores to land.
-__device__ __forceinline__ float round_bf16(float v, bool r) { return r ? l3m_bf16_to_f32(l3m_f32_to_bf16(v)) : v; }
-// rb: each value rounded to bf16 first (the bf16 prepare's rounding).
-__device__ __noinline__ void scatter_tx(const float *src, float *dst, int g0, int n, unsigned long long *bar, bool rb = false) {
+template <bool RB>
+__device__ __forceinline__ float round_bf16(float v) { return RB ? l3m_bf16_to_f32(l3m_f32_to_bf16(v)) : v; }
+// RB: each value rounded to bf16 first (the bf16 prepare's rounding); one instance each.
+template <bool RB = false>
+__device__ __noinline__ void scatter_tx(const float *src, float *dst, int g0, int n, unsigned long long *bar) {
     const int tid = threadIdx.x, nth = blockDim.x;
     const uint32_t ld = (uint32_t)__cvta_generic_to_shared(dst + g0), lb = (uint32_t)__cvta_generic_to_shared(bar);
     if (((g0 | n) & 3) == 0) {
@@ -141,7 +143,7 @@ __device__ __noinline__ void scatter_tx(const float *src, float *dst, int g0, in
             asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbar) : "r"(lb), "r"(r));
             const float4 v = ((const float4 *)src)[j];
             asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];"
-                         ::"r"(ra), "f"(round_bf16(v.x, rb)), "f"(round_bf16(v.y, rb)), "f"(round_bf16(v.z, rb)), "f"(round_bf16(v.w, rb)),
+                         ::"r"(ra), "f"(round_bf16<RB>(v.x)), "f"(round_bf16<RB>(v.y)), "f"(round_bf16<RB>(v.z)), "f"(round_bf16<RB>(v.w)),
                          "r"(rbar) : "memory");
         }
     } else {
@@ -152,7 +154,7 @@ __device__ __noinline__ void scatter_tx(const float *src, float *dst, int g0, in
             asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(ld + 4 * j), "r"(r));
             asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbar) : "r"(lb), "r"(r));
             asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];"
-                         ::"r"(ra), "r"(__float_as_uint(round_bf16(src[j], rb))), "r"(rbar) : "memory");
+                         ::"r"(ra), "r"(__float_as_uint(round_bf16<RB>(src[j]))), "r"(rbar) : "memory");
         }
     }
 }
@@ -552,7 +554,8 @@ __device__ __noinline__ void phase_attention(const DecodeArgs &a, const LayerDev
                        a.attn_chunk, prestaged);
     trace<TRACE>(a, tslot, pos, l, 15);
     if (a.qx_attn == kXQ8) scatter_q8(s.att, h * hd, hd, s.pa, s.xbar + 1);
-    else if (a.async_x) scatter_tx(s.att, s.xa, h * hd, hd, s.xbar + 1, a.qx_attn == kXPrepBF16);
+    else if (a.async_x && a.qx_attn == kXPrepBF16) scatter_tx<true>(s.att, s.xa, h * hd, hd, s.xbar + 1);
+    else if (a.async_x) scatter_tx(s.att, s.xa, h * hd, hd, s.xbar + 1);
     else scatter(s.att, s.xa, h * hd, hd);
 }
 
@@ -893,25 +896,40 @@ __device__ __noinline__ int wait_published(const DecodeArgs &a, uint32_t e, int 
     return r;
 }
 
-// Every thread: x[i] = the value of x word i once it carries epoch e (its own bounded wait: the words
-// are written without a fence, so each may land after the position word). False on a failure.
+// Every thread: x[i] = the value of x word i once it carries epoch e (the words are written without a
+// fence, so each may land after the position word). Each thread issues the loads of up to 4 of its
+// words at once (dim <= 1024 costs one round trip), then re-polls only words that are not there yet,
+// with its own bounded wait. False on a failure.
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
 __device__ __noinline__ bool read_published_x(const DecodeArgs &a, uint32_t e, float *x, int pos) {
+    const int nth = blockDim.x;
     bool ok = true;
 #pragma unroll 1
-    for (int i = threadIdx.x; i < a.dim && ok; i += blockDim.x) {
-        unsigned long long v;
-        uint64_t t0 = 0;
-        for (int spins = 0;; spins++) {
-            asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(a.hx.xw + i) : "memory");
-            if ((uint32_t)(v >> 32) == e) break;
-            if (spins == 0) {
-                t0 = globaltimer_ns();
-            } else if ((spins & 63) == 0) {
-                if (aborted(a)) { ok = false; break; }
-                if (globaltimer_ns() - t0 > a.hx.timeout_ns) { record_abort(a, kErrTimeout, pos, -1, kWaitHeadFlag); ok = false; break; }
+    for (int i0 = threadIdx.x; i0 < a.dim && ok; i0 += 4 * nth) {
+        unsigned long long v[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+            if (i0 + u * nth < a.dim) v[u] = ld_relaxed_u64(a.hx.xw + i0 + u * nth);
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int i = i0 + u * nth;
+            if (i >= a.dim || !ok) continue;
+            uint64_t t0 = 0;
+            for (int spins = 0; (uint32_t)(v[u] >> 32) != e; spins++) {
+                if (spins == 0) {
+                    t0 = globaltimer_ns();
+                } else if ((spins & 63) == 0) {
+                    if (aborted(a)) { ok = false; break; }
+                    if (globaltimer_ns() - t0 > a.hx.timeout_ns) { record_abort(a, kErrTimeout, pos, -1, kWaitHeadFlag); ok = false; break; }
+                }
+                v[u] = ld_relaxed_u64(a.hx.xw + i);
             }
+            x[i] = __uint_as_float((uint32_t)v[u]);
         }
-        x[i] = __uint_as_float((uint32_t)v);
     }
     return __syncthreads_and(ok);
 }
@@ -1112,7 +1130,8 @@ __device__ __noinline__ void run_layer(const DecodeArgs &a, const LayerDev *laye
         ffn_gate<GPT2>(a, L, role, s);
         const int g0 = (a.sh.f_off + role.ffn0) * kTile, n = min((a.sh.f_off + role.ffn1) * kTile, a.ffn) - g0;
         if (a.qx_h == kXQ8) scatter_q8(s.tmp, g0, n, s.ph, s.xbar + 3);
-        else if (a.async_x) scatter_tx(s.tmp, s.xh, g0, n, s.xbar + 3, a.qx_h == kXPrepBF16);
+        else if (a.async_x && a.qx_h == kXPrepBF16) scatter_tx<true>(s.tmp, s.xh, g0, n, s.xbar + 3);
+        else if (a.async_x) scatter_tx(s.tmp, s.xh, g0, n, s.xbar + 3);
         else scatter(s.tmp, s.xh, g0, n);
         if (multi) peer_send(a, kXH, s.tmp, g0, n, step);
     }
