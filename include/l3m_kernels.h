@@ -98,6 +98,10 @@ L3M_API int l3m_block_dots_dev(int dtype, int32_t *dots, const void *tiles, int 
 L3M_API int l3m_unpack_dev(int dtype, int8_t *q, float *d, const void *tiles, int ntiles, int k, void *stream);
 // One head of causal attention over a bf16 KV cache (reference src/ops.h:14-16), device pointers.
 L3M_API int l3m_attend_dev(float *out, const float *q, const uint16_t *k, const uint16_t *v, int pos, int head_dim, int stride, void *stream);
+// y[i] = expf(x[i]) for i < n on the device, bit for bit the host C library's expf (the function the
+// reference's softmax, SiLU and sampler call, src/ops.c:45, 50; the kernels above use the same code).
+// x, y: device memory.
+L3M_API int l3m_expf_dev(const float *x, float *y, int n, void *stream);
 // The last CUDA error this library saw, as text ("" if none).
 L3M_API const char *l3m_cuda_error(void);
 

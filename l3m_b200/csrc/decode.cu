@@ -1221,7 +1221,7 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kDecodeTh
     if (threadIdx.x == 0) {
         sh_args = *ap;
         sh_role = ap->roles[blockIdx.x];
-        prefetch_expf_table(ap->etab, blockIdx.x, gridDim.x);
+        if (ap->etab) prefetch_expf_table(ap->etab, blockIdx.x, gridDim.x);
     }
     __syncthreads();
     const DecodeArgs &a = sh_args;

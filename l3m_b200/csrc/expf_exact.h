@@ -1,17 +1,19 @@
 // expf that returns, bit for bit, what the host C library's expf returns, written once for both
 // the host (the build-time generator) and the device (the decode kernels).
 //
-// Method: e^x is evaluated in double precision (x = k ln2 + r, |r| <= ln2/2, degree-12 Taylor
-// polynomial, scaled by 2^k) and rounded to float. That is correctly rounded except when e^x lies
-// within about 2^-47 of a float rounding midpoint. The C library's expf is not always correctly
-// rounded; every input where the two differ lies within L3M_EXPF_WINDOW ulp of a midpoint (the
-// generator checks this over all 2^32 inputs). So: round the double result, and only when it falls
-// inside that window look the input up in the exceptions produced by running the C library (held
-// as an open-addressing hash set, so a lookup is usually one memory read); a listed input takes the
-// other float neighbour.
+// Method: the table-driven evaluation that glibc's expf publishes (since glibc 2.28; ARM's optimized
+// routines), restated in double precision: z = x N/ln2 (N = 32) split as k + r with the shift trick,
+// |r| <= 1/2; e^x = 2^(k/N) 2^(r/N) with 2^((k mod N)/N) from a 32-entry table of correctly rounded
+// doubles scaled by 2^floor(k/N), and 2^(r/N) - 1 by a cubic; the double result rounded to float. The
+// first step is one fused multiply-add (as x86-64 builds of the C library with FMA evaluate it). On
+// this method the C library and this code agree on every input (the generator checks all 2^32 at build
+// time). For a C library that differs, the same check collects the inputs where it does: each must lie
+// within L3M_EXPF_WINDOW ulp of a float rounding midpoint of the double result, and those inputs, held
+// as an open-addressing hash set, take the other float neighbour. With an empty set (this method's own
+// library) the kernels get no table and never look anything up.
 //
-// Every operation is a single IEEE double operation (multiply, fused multiply-add, rint), so the
-// host and the device compute identical values. L3M_EXPF_HD marks functions for both compilers.
+// Every operation is a single IEEE double operation (multiply, add, fused multiply-add, conversion), so
+// the host and the device compute identical values. L3M_EXPF_HD marks functions for both compilers.
 #pragma once
 #include <stdint.h>
 
@@ -60,30 +62,59 @@ L3M_EXPF_HD double l3m_mul(double a, double b) {
     return a * b;
 #endif
 }
-L3M_EXPF_HD double l3m_rint(double a) { return rint(a); }
+L3M_EXPF_HD double l3m_sub(double a, double b) {
+#ifdef __CUDA_ARCH__
+    return __dsub_rn(a, b);
+#else
+    return a - b;
+#endif
+}
+L3M_EXPF_HD uint64_t l3m_d2u(double d) {
+#ifdef __CUDA_ARCH__
+    return (uint64_t)__double_as_longlong(d);
+#else
+    uint64_t u; memcpy(&u, &d, 8); return u;
+#endif
+}
 
-// e^x in double for finite x in [-104, 89].
+// 2^(i/32), i = 0..31, each the double nearest to it.
+#define L3M_EXP2_TAB {                                                                                    \
+    0x1.0000000000000p+0, 0x1.059b0d3158574p+0, 0x1.0b5586cf9890fp+0, 0x1.11301d0125b51p+0,                \
+    0x1.172b83c7d517bp+0, 0x1.1d4873168b9aap+0, 0x1.2387a6e756238p+0, 0x1.29e9df51fdee1p+0,                \
+    0x1.306fe0a31b715p+0, 0x1.371a7373aa9cbp+0, 0x1.3dea64c123422p+0, 0x1.44e086061892dp+0,                \
+    0x1.4bfdad5362a27p+0, 0x1.5342b569d4f82p+0, 0x1.5ab07dd485429p+0, 0x1.6247eb03a5585p+0,                \
+    0x1.6a09e667f3bcdp+0, 0x1.71f75e8ec5f74p+0, 0x1.7a11473eb0187p+0, 0x1.82589994cce13p+0,                \
+    0x1.8ace5422aa0dbp+0, 0x1.93737b0cdc5e5p+0, 0x1.9c49182a3f090p+0, 0x1.a5503b23e255dp+0,                \
+    0x1.ae89f995ad3adp+0, 0x1.b7f76f2fb5e47p+0, 0x1.c199bdd85529cp+0, 0x1.cb720dcef9069p+0,                \
+    0x1.d5818dcfba487p+0, 0x1.dfc97337b9b5fp+0, 0x1.ea4afa2a490dap+0, 0x1.f50765b6e4540p+0}
+static const double l3m_exp2_tab_host[32] = L3M_EXP2_TAB;
+#ifdef __CUDACC__
+static __device__ const double l3m_exp2_tab_dev[32] = L3M_EXP2_TAB;
+#endif
+L3M_EXPF_HD double l3m_exp2_tab(int i) {
+#ifdef __CUDA_ARCH__
+    return __ldg(&l3m_exp2_tab_dev[i]);
+#else
+    return l3m_exp2_tab_host[i];
+#endif
+}
+
+// e^x in double for finite x in [-0x1.9fe368p6, 0x1.62e42ep6] (the float results from 0 to the
+// largest float): the method above.
 L3M_EXPF_HD double l3m_exp_double(float xf) {
-    double x = (double)xf;
-    double k = l3m_rint(l3m_mul(x, 1.4426950408889634));            // 1/ln2
-    const double L1 = 0x1.62e42fefa3800p-1, L2 = 0x1.ef35793c7673p-45;   // ln2 = L1 + L2, L1 with trailing zeros
-    double r = l3m_fma(-k, L1, x);
-    r = l3m_fma(-k, L2, r);
-    double p = 1.0 / 479001600.0;                                     // 1/12!
-    p = l3m_fma(p, r, 1.0 / 39916800.0);
-    p = l3m_fma(p, r, 1.0 / 3628800.0);
-    p = l3m_fma(p, r, 1.0 / 362880.0);
-    p = l3m_fma(p, r, 1.0 / 40320.0);
-    p = l3m_fma(p, r, 1.0 / 5040.0);
-    p = l3m_fma(p, r, 1.0 / 720.0);
-    p = l3m_fma(p, r, 1.0 / 120.0);
-    p = l3m_fma(p, r, 1.0 / 24.0);
-    p = l3m_fma(p, r, 1.0 / 6.0);
-    p = l3m_fma(p, r, 0.5);
-    p = l3m_fma(p, r, 1.0);
-    p = l3m_fma(p, r, 1.0);
-    int ki = (int)k;                                                  // |k| <= 150: 2^k is a normal double
-    return l3m_mul(p, l3m_u2d((uint64_t)(ki + 1023) << 52));
+    const double InvLn2N = 0x1.71547652b82fep+0 * 32, Shift = 0x1.8p+52;   // 32/ln2; 1.5 * 2^52
+    const double C0 = 0x1.c6af84b912394p-5 / 32 / 32 / 32, C1 = 0x1.ebfce50fac4f3p-3 / 32 / 32, C2 = 0x1.62e42ff0c52d6p-1 / 32;
+    const double x = (double)xf;
+    double kd = l3m_fma(InvLn2N, x, Shift);                          // k in kd's low mantissa bits, rounded to nearest even
+    const uint64_t ki = l3m_d2u(kd);
+    kd = l3m_sub(kd, Shift);
+    const double r = l3m_fma(InvLn2N, x, -kd);                       // |r| <= 1/2
+    const int64_t k = (int64_t)(ki << 12) >> 12;                     // the 52-bit field, sign-extended
+    const double s = l3m_u2d(l3m_d2u(l3m_exp2_tab((int)(k & 31))) + ((uint64_t)(k >> 5) << 52));   // 2^(k/32), a normal double
+    const double z = l3m_fma(C0, r, C1), r2 = l3m_mul(r, r);
+    double y = l3m_fma(C2, r, 1.0);
+    y = l3m_fma(z, r2, y);
+    return l3m_mul(y, s);
 }
 
 // Correctly rounded candidate and whether the exception list must be consulted. *other is the float
@@ -92,8 +123,8 @@ L3M_EXPF_HD float l3m_expf_candidate(float x, int *check, float *other) {
     *check = 0;
     *other = 0.0f;
     if (x != x) return x + x;                      // NaN
-    if (x > 89.0f) return l3m_u2f(0x7F800000u);    // overflow: +inf
-    if (x < -104.0f) return 0.0f;                  // underflow: +0
+    if (x > 0x1.62e42ep6f) return l3m_u2f(0x7F800000u);    // overflow: +inf
+    if (x < -0x1.9fe368p6f) return 0.0f;           // underflow: +0
     double y = l3m_exp_double(x);
     float f = (float)y;                            // round to nearest even (subnormals included)
     uint32_t fu = l3m_f2u(f);
@@ -174,9 +205,10 @@ L3M_EXPF_HOST int l3m_expf_hash_build(const uint32_t *list, size_t n, uint32_t *
     return longest + 1 < L3M_EXPF_PROBES ? 0 : -1;
 }
 
+// table: the exception set, or null when it is empty (nothing to look up).
 L3M_EXPF_HD float l3m_expf_exact(float x, const uint32_t *table) {
     int check; float other;
     float f = l3m_expf_candidate(x, &check, &other);
-    if (check && l3m_expf_listed(l3m_f2u(x), table)) return other;
+    if (check && table && l3m_expf_listed(l3m_f2u(x), table)) return other;
     return f;
 }

@@ -605,6 +605,10 @@ extern "C" int l3m_expf_table(const uint32_t **table) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return fail_msg("no CUDA device");
     std::lock_guard<std::mutex> lock(mu);
+    if (L3M_EXPF_LIST_N == 0) {                                      // the C library follows the method: nothing to look up
+        *table = nullptr;
+        return 0;
+    }
     if (!d_table[dev]) {
         std::vector<uint32_t> h(L3M_EXPF_SLOTS);
         if (l3m_expf_hash_build(l3m_expf_list_host, L3M_EXPF_LIST_N, h.data())) return fail_msg("expf exception set does not fit its table");
@@ -618,6 +622,10 @@ extern "C" int l3m_expf_table(const uint32_t **table) {
     return 0;
 }
 
+__global__ void expf_kernel(const float *__restrict__ x, float *__restrict__ y, int n, const uint32_t *etab) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) y[i] = l3m_expf_exact(x[i], etab);
+}
+
 // Error text for the other entry-point files of this library (not exported).
 extern "C" int l3m_error_msg(const char *msg) { return fail_msg(msg); }
 extern "C" int l3m_error_cuda(int e, const char *what) { return fail((cudaError_t)e, what); }
@@ -625,6 +633,17 @@ extern "C" int l3m_error_cuda(int e, const char *what) { return fail((cudaError_
 extern "C" {
 
 L3M_API const char *l3m_cuda_error(void) { return g_err; }
+
+L3M_API int l3m_expf_dev(const float *x, float *y, int n, void *stream) {
+    if (n < 0 || (n > 0 && (!x || !y))) return fail_msg("l3m_expf_dev: bad arguments");
+    const uint32_t *etab;
+    if (l3m_expf_table(&etab)) return -1;
+    if (n == 0) return 0;
+    const int blocks = std::min((n + 255) / 256, 148 * 8);
+    expf_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(x, y, n, etab);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : fail(e, "l3m_expf_dev");
+}
 
 L3M_API int l3m_gemv_dev(int exact, int dtype, float *y, const void *tiles, int ntiles, int k, const l3m_vec *x, void *stream) {
     if (dtype < 0 || dtype >= L3M_DT_COUNT || ntiles < 0 || k <= 0) return fail_msg("l3m_gemv_dev: bad arguments");

@@ -77,4 +77,4 @@ void o_gelu(float *x, int n);
 float o_expf(float x);
 // The correctly rounded double evaluation used to build the GPU's exception list: returns the
 // double approximation of e^x; see oracle_expf.c.
-double o_exp_double(float x);
+void o_expf_n(const float *x, float *y, int n);

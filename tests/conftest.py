@@ -78,7 +78,7 @@ def load_oracle():
         "o_unpack": (None, [i, vp, vp, vp, i, i]),
         "o_rmsnorm": (None, [vp, vp, vp, i, C.c_float]), "o_rope": (None, [vp, i, i, i, C.c_float]),
         "o_silu_mul": (None, [vp, vp, i]), "o_attend": (None, [vp, vp, vp, vp, i, i, i]),
-        "o_expf": (C.c_float, [C.c_float]), "o_exp_double": (C.c_double, [C.c_float]),
+        "o_expf": (C.c_float, [C.c_float]), "o_expf_n": (None, [C.c_void_p, C.c_void_p, C.c_int]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(lib, name)

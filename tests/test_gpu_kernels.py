@@ -201,6 +201,29 @@ def test_attend_exact(gpu, oracle):
                 assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), (hd, pos, qscale)
 
 
+def test_expf_matches_c_library(gpu, oracle, cuda):
+    """The device expf (softmax, SiLU gate, sampler weights) equals the host C library's expf, which
+    the reference calls (src/ops.c:45, 50), bit for bit: one float in every 509 bit patterns over the
+    whole 32-bit space (NaNs, infinities, subnormals and the over/underflow edges among them), and
+    every 97th float in [-1, 1] plus the edges of the range where expf is finite and
+    nonzero. The build already checks the same arithmetic on the host for all 2^32 inputs."""
+    import l3m_b200
+    lib = l3m_b200.lib()
+    sweep = np.arange(0, 2**32, 509, dtype=np.uint64).astype(np.uint32)
+    near = np.arange(0, 0x3F800001, 97, dtype=np.uint32)
+    edges = np.array([0x42B17217, 0x42B17218, 0x42B17219, 0xC2CFF1B4, 0xC2CFF1B5, 0xC2CFF1B3, 0xC2AEAC4F, 0xC2AEAC50, 0x7F800000,
+                      0xFF800000, 0x7FC00000, 0x00000001, 0x80000001, 0x33800000, 0xB3800000], np.uint32)
+    x = np.concatenate([sweep, near, near | 0x80000000, edges]).view(np.float32)
+    want = np.empty_like(x)
+    oracle.o_expf_n(P(x), P(want), x.size)
+    dx, dy = cuda.put(x), cuda.empty(x.nbytes)
+    assert lib.l3m_expf_dev(dx, dy, x.size, None) == 0
+    got = cuda.get(dy, np.empty_like(x))
+    same = (got.view(np.uint32) == want.view(np.uint32)) | (np.isnan(got) & np.isnan(want))
+    bad = np.nonzero(~same)[0]
+    assert bad.size == 0, f"{bad.size} differ, first x bits 0x{x.view(np.uint32)[bad[0]]:08x}"
+
+
 SWEEP = [(288, 288), (768, 288), (2048, 768), (4096, 4096), (32000, 768)]
 
 

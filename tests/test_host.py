@@ -73,6 +73,8 @@ def test_device_entries_refuse_bad_arguments(lib):
         (lambda: lib.l3m_sample_dev(p, 0, 1.0, p, p, p, None), "vocab > 0"),
         (lambda: lib.l3m_sample_dev(p, 10, 0.0, p, p, p, None), "temperature > 0"),
         (lambda: lib.l3m_sample_dev(p, 10, 1.0, None, p, p, None), "required"),
+        (lambda: lib.l3m_expf_dev(None, p, 5, None), "bad arguments"),
+        (lambda: lib.l3m_expf_dev(p, p, -1, None), "bad arguments"),
     ]
     for call, text in cases:
         assert call() == -1
