@@ -49,7 +49,7 @@ struct Gpu {
     cudaStream_t stream = nullptr, side = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     uint8_t *arena = nullptr;
-    size_t arena_bytes = 0, weight_bytes = 0;
+    size_t arena_bytes = 0, weight_bytes = 0, held_bytes = 0;
     uint16_t *kv = nullptr;
     size_t kv_bytes = 0;
     float2 *rope = nullptr;
@@ -188,10 +188,71 @@ struct Streamed {
     int dt_head = 0;
     struct Entry { std::string name; size_t off, rows; int dtype, k; };
     std::vector<Entry> entries;                  // every packed matrix, for the writer
+    size_t widened = 0;                          // bytes added by widening q4_0 / mxfp4 matrices to q8_0
 };
 constexpr const char *kPackedPrefix = "b200v1.";
 
-size_t pack_rows(Stage &s, Rows &r, const l3m_file *f, const std::string &name, Streamed &out, bool ref, int *dtype) {
+// q4_0 and mxfp4 tiles rewritten as q8_0 tiles with the same block dots and scales, so the decode
+// kernel multiplies them with q8_0's one dp4a per 4 inputs instead of unpacking nibbles. A q8_0 byte
+// is the weight + 128 (offset 128): a q4_0 code c (the reference's dot uses c with offset 8) becomes
+// c + 120, and an mxfp4 code's doubled e2m1 value v (offset 16 on v + 16) becomes v + 128, so
+// sum(byte * x) - 128 * sum(x) is the reference's integer dot exactly. Scales: q4_0's f16 as they
+// are; mxfp4's 2^(e - 128) as the f16 holding exactly that value, which exists for e in [104, 143]
+// (mxfp4_fits checks a matrix first). Source block: scales, then byte j of group g of row c at
+// (g*16 + c)*4 + j holding inputs 8g+j (low nibble) and 8g+4+j (high nibble); q8_0 block: 16 f16
+// scales, then input i of row c at (i/4*16 + c)*4 + i%4 (reference src/pack.c).
+bool mxfp4_fits(const uint8_t *src, size_t ntiles, int k) {
+    const size_t blocks = ntiles * (size_t)(k / L3M_QBLOCK);
+    for (size_t b = 0; b < blocks; b++)
+        for (int c = 0; c < L3M_TILE; c++) {
+            const int e = src[b * 272 + c];
+            if (e < 104 || e > 143) return false;
+        }
+    return true;
+}
+void widen_to_q8(int dtype, const uint8_t *src, uint8_t *dst, size_t ntiles, int k) {
+    const int sb = dtype == L3M_MXFP4 ? 16 : 32, in_b = sb + 256;
+    uint8_t val[16];
+    for (int n = 0; n < 16; n++) val[n] = (uint8_t)(dtype == L3M_MXFP4 ? l3m_mxfp4_value(n) + 128 : n + 120);
+    for (size_t b = 0; b < ntiles * (size_t)(k / L3M_QBLOCK); b++) {
+        const uint8_t *in = src + b * in_b;
+        uint8_t *out = dst + b * 544;
+        if (dtype == L3M_MXFP4) {
+            for (int c = 0; c < L3M_TILE; c++) {                               // 2^p, p = e - 128 in [-24, 15]
+                const int p = (int)in[c] - 128;
+                const uint16_t h = (uint16_t)(p >= -14 ? (p + 15) << 10 : 1 << (p + 24));
+                memcpy(out + 2 * c, &h, 2);
+            }
+        } else {
+            memcpy(out, in, 32);
+        }
+        uint8_t *w = out + 32;
+        for (int g = 0; g < 4; g++)
+            for (int c = 0; c < L3M_TILE; c++)
+                for (int j = 0; j < 4; j++) {
+                    const uint8_t v = in[sb + (g * L3M_TILE + c) * 4 + j];
+                    const int i0 = 8 * g + j, i1 = 8 * g + 4 + j;
+                    w[(i0 / 4 * L3M_TILE + c) * 4 + i0 % 4] = val[v & 15];
+                    w[(i1 / 4 * L3M_TILE + c) * 4 + i1 % 4] = val[v >> 4];
+                }
+    }
+}
+
+// Which q4_0 / mxfp4 matrices the decode kernel gets as q8_0 tiles: only where a CTA's whole share of
+// the widened tiles fits the part of the staging area that matrix is copied into (else the kernel
+// would read the rest from global memory, slower than unpacking nibbles from shared memory).
+struct Widen {
+    bool on = false;
+    long cap_qkv_wo = 0, cap_rest = 0;   // staging bytes for qkv / wo, and for up(+gate) / down / the head
+    int head_ctas = 1;                   // the CTAs the head's tiles are split over
+};
+
+// widen: q4_0 and mxfp4 matrices go to the device as q8_0 tiles (widen_to_q8; an mxfp4 matrix only
+// when every scale has an f16 form) when per_cta tiles of them fit in cap bytes; *dtype is then
+// L3M_Q8_0 and out.widened counts the extra bytes. The writer's entries keep the file's layout.
+size_t pack_rows(Stage &s, Rows &r, const l3m_file *f, const std::string &name, Streamed &out, bool ref, const Widen &wd, long cap,
+                 int per_cta, int *dtype) {
+    const bool widen = wd.on && (long)per_cta * (r.k / L3M_QBLOCK) * (long)l3m_tile_bytes(L3M_Q8_0, L3M_QBLOCK) <= cap;
     const size_t rows = (size_t)tiles_of((int)r.ptr.size()) * L3M_TILE, tb = l3m_tile_bytes(r.dtype, r.k);
     *dtype = r.dtype;
     const l3m_tensor *pt = ref ? nullptr : l3m_file_tensor(f, (kPackedPrefix + name).c_str());
@@ -201,6 +262,16 @@ size_t pack_rows(Stage &s, Rows &r, const l3m_file *f, const std::string &name, 
     else
         off = pack(s, r);
     out.entries.push_back({name, off, rows, r.dtype, r.k});
+    const size_t nt = rows / L3M_TILE;
+    if (widen && rows && (r.dtype == L3M_Q4_0 || (r.dtype == L3M_MXFP4 && mxfp4_fits(s.buf.data() + off, nt, r.k)))) {
+        const size_t bytes = nt * tb, wide = nt * l3m_tile_bytes(L3M_Q8_0, r.k);
+        const std::vector<uint8_t> packed(s.buf.begin() + off, s.buf.begin() + off + bytes);
+        s.buf.resize(off);                                                          // the packed copy was the last put
+        off = s.reserve(wide);
+        widen_to_q8(r.dtype, packed.data(), s.buf.data() + off, nt, r.k);
+        out.widened += wide - bytes;
+        *dtype = L3M_Q8_0;
+    }
     return off;
 }
 
@@ -234,12 +305,13 @@ void add_rows(Rows &r, const l3m_file *f, const l3m_tensor *t, int lo, int hi, b
     }
 }
 
-void pack_streamed(const l3m_file *f, bool ref, const ShardRange &sr, int hd, Stage &s, Streamed &out) {
+void pack_streamed(const l3m_file *f, bool ref, const ShardRange &sr, int hd, Stage &s, Streamed &out, const Widen &wide = Widen{}) {
     const int L = (int)f->h->n_layers;
     const bool packed_ok = sr.whole && !ref;                                        // the file's b200v1 section is for one GPU
     for (auto *v : {&out.off_qkv, &out.off_wo, &out.off_up, &out.off_gate, &out.off_down}) v->assign(L, 0);
     for (auto *v : {&out.dt_qkv, &out.dt_wo, &out.dt_up, &out.dt_gate, &out.dt_down}) v->assign(L, 0);
     const int T = L3M_TILE, ftiles = sr.f_hi - sr.f_lo;
+    auto share = [](int tiles) { return (tiles + l3m::kClusterCtas - 1) / l3m::kClusterCtas; };   // a layer CTA's largest share
     for (int l = 0; l < L; l++) {
         const std::string b = "blk." + std::to_string(l) + ".";
         const l3m_tensor *wq = l3m_file_blk(f, l, "wq"), *wk = l3m_file_blk(f, l, "wk"), *wv = l3m_file_blk(f, l, "wv");
@@ -248,19 +320,19 @@ void pack_streamed(const l3m_file *f, bool ref, const ShardRange &sr, int hd, St
         add_rows(r, f, wk, sr.kv_lo * hd, sr.kv_hi * hd, ref);
         add_rows(r, f, wv, sr.kv_lo * hd, sr.kv_hi * hd, ref);
         if (r.ptr.empty()) r.k = (int)wq->shape[1], r.dtype = ref ? L3M_F32 : (int)wq->dtype;
-        out.off_qkv[l] = pack_rows(s, r, f, b + "qkv", out, !packed_ok, &out.dt_qkv[l]);
+        out.off_qkv[l] = pack_rows(s, r, f, b + "qkv", out, !packed_ok, wide, wide.cap_qkv_wo, share(tiles_of((int)r.ptr.size())), &out.dt_qkv[l]);
         {
             Rows ro;
             const l3m_tensor *wo = l3m_file_blk(f, l, "wo");
             add_rows(ro, f, wo, sr.d_lo * T, std::min(sr.d_hi * T, (int)wo->shape[0]), ref);
-            out.off_wo[l] = pack_rows(s, ro, f, b + "wo", out, !packed_ok, &out.dt_wo[l]);
+            out.off_wo[l] = pack_rows(s, ro, f, b + "wo", out, !packed_ok, wide, wide.cap_qkv_wo, share(tiles_of((int)ro.ptr.size())), &out.dt_wo[l]);
         }
         const l3m_tensor *wu = l3m_file_blk(f, l, "w_up"), *wg = l3m_file_blk(f, l, "w_gate");
         const int ffn_hi = std::min(sr.f_hi * T, (int)wu->shape[0]);
         if (!wg) {                                                                  // GELU MLP: up only
             Rows ru;
             add_rows(ru, f, wu, sr.f_lo * T, ffn_hi, ref);
-            out.off_up[l] = pack_rows(s, ru, f, b + "up", out, !packed_ok, &out.dt_up[l]);
+            out.off_up[l] = pack_rows(s, ru, f, b + "up", out, !packed_ok, wide, wide.cap_rest, share(ftiles), &out.dt_up[l]);
             out.off_gate[l] = (size_t)-1;
             out.dt_gate[l] = out.dt_up[l];
         } else if (ref || wu->dtype == wg->dtype) {
@@ -271,25 +343,84 @@ void pack_streamed(const l3m_file *f, bool ref, const ShardRange &sr, int hd, St
                 split(ftiles, l3m::kClusterCtas, c, &t0, &t1);
                 for (const l3m_tensor *t : {wu, wg}) add_rows(ru, f, t, (sr.f_lo + t0) * T, (sr.f_lo + t1) * T, ref);
             }
-            out.off_up[l] = pack_rows(s, ru, f, b + "upgate16", out, !packed_ok, &out.dt_up[l]);
+            out.off_up[l] = pack_rows(s, ru, f, b + "upgate16", out, !packed_ok, wide, wide.cap_rest, 2 * share(ftiles), &out.dt_up[l]);
             out.off_gate[l] = (size_t)-1;
             out.dt_gate[l] = out.dt_up[l];
         } else {
             Rows ru, rg;
             add_rows(ru, f, wu, sr.f_lo * T, ffn_hi, ref);
             add_rows(rg, f, wg, sr.f_lo * T, ffn_hi, ref);
-            out.off_up[l] = pack_rows(s, ru, f, b + "up", out, !packed_ok, &out.dt_up[l]);
-            out.off_gate[l] = pack_rows(s, rg, f, b + "gate", out, !packed_ok, &out.dt_gate[l]);
+            out.off_up[l] = pack_rows(s, ru, f, b + "up", out, !packed_ok, wide, wide.cap_rest, share(ftiles), &out.dt_up[l]);
+            out.off_gate[l] = pack_rows(s, rg, f, b + "gate", out, !packed_ok, Widen{}, 0, 0, &out.dt_gate[l]);   // read from global memory
         }
         Rows rd;
         const l3m_tensor *wd = l3m_file_blk(f, l, "w_down");
         add_rows(rd, f, wd, sr.d_lo * T, std::min(sr.d_hi * T, (int)wd->shape[0]), ref);
-        out.off_down[l] = pack_rows(s, rd, f, b + "down", out, !packed_ok, &out.dt_down[l]);
+        out.off_down[l] = pack_rows(s, rd, f, b + "down", out, !packed_ok, wide, wide.cap_rest, share(tiles_of((int)rd.ptr.size())), &out.dt_down[l]);
     }
     const l3m_tensor *head = l3m_file_tensor(f, (f->h->flags & L3M_F_TIED) ? "embed" : "lm_head");
     Rows rh;
     add_rows(rh, f, head, sr.v_lo * T, std::min(sr.v_hi * T, (int)head->shape[0]), ref);
-    out.off_head = pack_rows(s, rh, f, "head", out, !packed_ok, &out.dt_head);
+    out.off_head = pack_rows(s, rh, f, "head", out, !packed_ok, wide, wide.cap_rest, (tiles_of((int)rh.ptr.size()) + wide.head_ctas - 1) / wide.head_ctas, &out.dt_head);
+}
+
+// The decode kernel's shared-memory layout for these sizes: every vector's offset in a, the scratch, the
+// start of the weight staging area (sm_w) with the attention buffers at its start (w_extra bytes).
+// Returns the bytes in use before the staging area's weights; the area itself is the rest of the SM's
+// budget. max_tiles, pairs: the largest per-CTA share of a phase (tiles; scratch pairs).
+struct LayoutSizes { int dim, ffn, hd, ctx, L, n_qkv, vstride, max_tiles, pairs; bool ln; };
+int smem_layout(l3m::DecodeArgs &a, const LayoutSizes &z) {
+    const int dim = z.dim, ffn = z.ffn, hd = z.hd, mx = std::max(dim, ffn), nb = (mx + 31) / 32, G = l3m::kClusterCtas;
+    int off = 0;
+    auto take = [&](int bytes) { int o2 = off; off = align16(off + bytes); return o2; };
+    a.sm_x = take(dim * 4);
+    a.sm_xb = take(mx * 4);
+    a.sm_tmp = take(mx * 4);
+    a.sm_q8 = take(mx);
+    a.sm_scale = take(nb * 4);
+    a.sm_sum = take(nb * 4);
+    a.sm_xf = take(mx * 4);
+    a.sm_pa_q8 = take(dim);                                            // the q8 exchanges' receive buffers
+    a.sm_pa_scale = take((dim / 32 + 1) * 4);
+    a.sm_pa_sum = take((dim / 32 + 1) * 4);
+    a.sm_ph_q8 = take(ffn);
+    a.sm_ph_scale = take((ffn / 32 + 1) * 4);
+    a.sm_ph_sum = take((ffn / 32 + 1) * 4);
+    a.sm_y = take(z.max_tiles * L3M_TILE * 4);
+    a.sm_scores = take(z.ctx * 4);
+    a.sm_kv = take(2 * hd * 2);
+    a.sm_att = take(hd * 4);
+    a.sm_red = take(64 * 4);
+    a.sm_wa = take(dim * 4);
+    a.sm_wf = take(dim * 4);
+    a.sm_wh = take(dim * 4);
+    a.sm_wab = take(z.ln ? dim * 4 : 0);
+    a.sm_wfb = take(z.ln ? dim * 4 : 0);
+    a.sm_whb = take(z.ln ? dim * 4 : 0);
+    a.sm_rope = take(hd / 2 * 8);
+    a.sm_layers = take(z.L * (int)sizeof(l3m::LayerDev));
+    a.attn_chunk = std::min(z.ctx, 256);
+    a.vstride = z.vstride;
+    a.sm_xq = take(z.n_qkv * 4);
+    a.sm_xa = take(dim * 4);
+    a.sm_xp = take(dim * 4);
+    a.sm_xh = take(ffn * 4);
+    a.sm_xd = take(dim * 4);
+    a.sm_xt = take((4 + 16 * G) * 4);                                  // token, argmax slots, 3 sampling exchanges
+    a.sm_wbar = take(16);
+    a.sm_xbar = take(5 * 8);
+    // Scratch: the (scale product, dot) pairs of the largest per-CTA phase of a layer, so each runs in
+    // one pass (the head runs in several).
+    a.scratch_pairs = z.pairs;
+    a.sm_scratch = take(z.pairs * 8);
+    // The weight staging area takes the rest; the attention buffers are its first bytes.
+    off = (off + 127) & ~127;
+    a.sm_w = off;
+    a.sm_kvbuf = take(a.attn_chunk * (hd + 8) * 2);
+    a.sm_vt = take(hd * l3m::attn_vt_stride(a.attn_chunk) * 2);
+    off = (off + 127) & ~127;
+    a.w_extra = off - a.sm_w;
+    return off;
 }
 
 // Build everything one GPU holds and fill its decode arguments.
@@ -326,9 +457,24 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     std::vector<l3m::LayerDev> layers(L);
     Streamed sw;
     const ShardRange sr = shard_range(f->h, m->n_gpus, g.rank);
-    pack_streamed(f, ref, sr, hd, s, sw);
     const int n_qkv = (m->n_heads + 2 * m->n_kv) * hd;
     const int heads_g = sr.head_hi - sr.head_lo, kv_g = sr.kv_hi - sr.kv_lo, n_qkv_g = (heads_g + 2 * kv_g) * hd;
+    Widen wd;                                                            // the staging capacities, from the layout alone
+    if (!ref) {
+        const int Tq = tiles_of(n_qkv_g), Td = sr.d_hi - sr.d_lo, Tf = sr.f_hi - sr.f_lo, Tv = sr.v_hi - sr.v_lo, mx = std::max(dim, ffn);
+        auto share = [&](int t) { return (t + G - 1) / G; };              // the largest of the split's parts
+        const int max_t = std::max({tiles_of(3 * hd), share(Tq), 2 * share(Tf), share(Td), share(Tv)});
+        const int pr = std::max({(mx / 32) * L3M_TILE, share(Tq) * L3M_TILE * (dim / 32), share(Td) * L3M_TILE * (dim / 32),
+                                 2 * share(Tf) * L3M_TILE * (dim / 32), share(Td) * L3M_TILE * (ffn / 32)});
+        l3m::DecodeArgs probe{};
+        smem_layout(probe, LayoutSizes{dim, ffn, hd, m->ctx, L, n_qkv, (m->ctx + 7) & ~7, max_t, pr, (m->flags & L3M_F_LAYERNORM) != 0});
+        const long w_bytes = ((long)l3m_decode_smem_budget() - probe.sm_w) & ~127L;
+        wd.on = !getenv("L3M_NO_WIDEN");
+        wd.cap_qkv_wo = std::max(0L, w_bytes - probe.w_extra);
+        wd.cap_rest = std::max(0L, w_bytes);
+        wd.head_ctas = GT > G && !m->cold ? GT - G : GT;
+    }
+    pack_streamed(f, ref, sr, hd, s, sw, wd);
     const std::vector<size_t> &off_qkv = sw.off_qkv, &off_wo = sw.off_wo, &off_gate = sw.off_gate, &off_up = sw.off_up, &off_down = sw.off_down;
     for (int l = 0; l < L; l++) {
         layers[l].dt_qkv = sw.dt_qkv[l]; layers[l].dt_wo = sw.dt_wo[l]; layers[l].dt_up = sw.dt_up[l];
@@ -336,7 +482,8 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     }
     const int dt_head = sw.dt_head;
     const size_t off_head = sw.off_head;
-    g.weight_bytes = s.buf.size();
+    g.weight_bytes = s.buf.size() - sw.widened;                         // the model's bytes, as the reference counts them
+    g.held_bytes = s.buf.size();                                         // what the arena holds (widened matrices included)
     const l3m_tensor *emb = l3m_file_tensor(f, "embed");
     int dt_embed = (int)emb->dtype;
     size_t emb_row = l3m_row_bytes(dt_embed, dim), off_embed;
@@ -481,61 +628,13 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
     a.hx.timeout_ns = (unsigned long long)(tmo ? atof(tmo) : 5000.0) * 1000000ull;
 
     // Shared memory layout.
-    const int mx = std::max(dim, ffn), nb = (mx + 31) / 32;
-    int off = 0;
-    auto take = [&](int bytes) { int o2 = off; off = align16(off + bytes); return o2; };
-    a.sm_x = take(dim * 4);
-    a.sm_xb = take(mx * 4);
-    a.sm_tmp = take(mx * 4);
-    a.sm_q8 = take(mx);
-    a.sm_scale = take(nb * 4);
-    a.sm_sum = take(nb * 4);
-    a.sm_xf = take(mx * 4);
-    a.sm_pa_q8 = take(dim);                                            // the q8 exchanges' receive buffers
-    a.sm_pa_scale = take((dim / 32 + 1) * 4);
-    a.sm_pa_sum = take((dim / 32 + 1) * 4);
-    a.sm_ph_q8 = take(ffn);
-    a.sm_ph_scale = take((ffn / 32 + 1) * 4);
-    a.sm_ph_sum = take((ffn / 32 + 1) * 4);
-    a.sm_y = take(max_tiles * L3M_TILE * 4);
-    a.sm_scores = take(m->ctx * 4);
-    a.sm_kv = take(2 * hd * 2);
-    a.sm_att = take(hd * 4);
-    a.sm_red = take(64 * 4);
-    a.sm_wa = take(dim * 4);
-    a.sm_wf = take(dim * 4);
-    a.sm_wh = take(dim * 4);
+    const int mx = std::max(dim, ffn);
     const bool ln = (m->flags & L3M_F_LAYERNORM) != 0;                   // LayerNorm biases: GPT-2 family only
-    a.sm_wab = take(ln ? dim * 4 : 0);
-    a.sm_wfb = take(ln ? dim * 4 : 0);
-    a.sm_whb = take(ln ? dim * 4 : 0);
-    a.sm_rope = take(hd / 2 * 8);
-    a.sm_layers = take(L * (int)sizeof(l3m::LayerDev));
-    a.attn_chunk = std::min(m->ctx, 256);
-    a.vstride = vstride;
-    a.sm_xq = take(n_qkv * 4);
-    a.sm_xa = take(dim * 4);
-    a.sm_xp = take(dim * 4);
-    a.sm_xh = take(ffn * 4);
-    a.sm_xd = take(dim * 4);
-    a.sm_xt = take((4 + 16 * G) * 4);                                  // token, argmax slots, 3 sampling exchanges
-    a.sm_wbar = take(16);
-    a.sm_xbar = take(5 * 8);
-    // Scratch: the (scale product, dot) pairs of the largest per-CTA phase of a layer, so each runs in
-    // one pass (the head runs in several).
     int pairs = (mx / 32) * L3M_TILE;
     for (const l3m::Role &r : make_roles(G))
         pairs = std::max({pairs, (r.qkv1 - r.qkv0) * L3M_TILE * (dim / 32), (r.wo1 - r.wo0) * L3M_TILE * (dim / 32),
                           2 * (r.ffn1 - r.ffn0) * L3M_TILE * (dim / 32), (r.dn1 - r.dn0) * L3M_TILE * (ffn / 32)});
-    a.scratch_pairs = pairs;
-    a.sm_scratch = take(pairs * 8);
-    // The weight staging area takes the rest; the attention buffers are its first bytes.
-    off = (off + 127) & ~127;
-    a.sm_w = off;
-    a.sm_kvbuf = take(a.attn_chunk * (hd + 8) * 2);
-    a.sm_vt = take(hd * l3m::attn_vt_stride(a.attn_chunk) * 2);
-    off = (off + 127) & ~127;
-    a.w_extra = off - a.sm_w;
+    const int off = smem_layout(a, LayoutSizes{dim, ffn, hd, m->ctx, L, n_qkv, vstride, max_tiles, pairs, ln});
     const int budget = l3m_decode_smem_budget();
     if (off > budget) {
         fprintf(stderr, "l3m: dim %d / ffn %d / ctx %d need more shared memory than a B200 SM has for this kernel\n", dim, ffn, m->ctx);
@@ -656,7 +755,7 @@ bool place_in_l2(l3m_model *m, Gpu &g, const l3m_opts &o, bool *over) {
     if (*over && !o.force) return false;
     if (m->cold || !g.persist_max || !g.window_max) return true;
     cudaSetDevice(g.dev);
-    size_t setaside = std::min(g.weight_bytes, g.persist_max);
+    size_t setaside = std::min(g.held_bytes, g.persist_max);
     // The window is best effort (the decode is correct without it), but a failure to set it is reported.
     cudaError_t e = cudaDeviceGetLimit(&g.prev_limit, cudaLimitPersistingL2CacheSize);
     if (e == cudaSuccess) e = cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, setaside);
@@ -664,7 +763,7 @@ bool place_in_l2(l3m_model *m, Gpu &g, const l3m_opts &o, bool *over) {
         g.limit_set = true;
         cudaStreamAttrValue attr = {};
         attr.accessPolicyWindow.base_ptr = g.arena;
-        attr.accessPolicyWindow.num_bytes = std::min(g.weight_bytes, g.window_max);
+        attr.accessPolicyWindow.num_bytes = std::min(g.held_bytes, g.window_max);
         attr.accessPolicyWindow.hitRatio = (float)std::min(1.0, (double)setaside / attr.accessPolicyWindow.num_bytes);
         attr.accessPolicyWindow.hitProp = cudaAccessPropertyPersisting;
         attr.accessPolicyWindow.missProp = cudaAccessPropertyStreaming;
@@ -675,7 +774,7 @@ bool place_in_l2(l3m_model *m, Gpu &g, const l3m_opts &o, bool *over) {
         cudaGetLastError();
     } else if (o.verbose) {
         fprintf(stderr, "l3m: gpu %d: persisting L2 window over %.2f MiB of weights, %.2f MiB set aside\n", g.dev,
-                std::min(g.weight_bytes, g.window_max) / MiB, setaside / MiB);
+                std::min(g.held_bytes, g.window_max) / MiB, setaside / MiB);
     }
     return true;
 }
