@@ -162,6 +162,29 @@ def test_prepared_and_float_exchanges_agree(gpu, models, monkeypatch, name, dt):
     assert t0 == t1 and np.array_equal(l0.view(np.uint32), l1.view(np.uint32))
 
 
+@pytest.mark.parametrize("name,dt", [("gqa", "q4_0"), ("mha40", "q4_0"), ("gqa", "mxfp4"), ("gpt2s", "mxfp4")])
+def test_widened_and_file_layouts_agree(gpu, models, monkeypatch, name, dt):
+    """q4_0 and mxfp4 matrices multiplied as widened q8_0 tiles (the default where they fit) or in
+    their file layout (L3M_NO_WIDEN): the same tokens and logits, bit for bit."""
+    _, t0, l0 = gpu_run(models[(name, dt)], PROMPT, 24)
+    monkeypatch.setenv("L3M_NO_WIDEN", "1")
+    _, t1, l1 = gpu_run(models[(name, dt)], PROMPT, 24)
+    assert t0 == t1 and np.array_equal(l0.view(np.uint32), l1.view(np.uint32))
+
+
+def test_mxfp4_scales_without_an_f16_form(gpu, oracle, tmp_path):
+    """An mxfp4 model whose block scales 2^(e-128) have no exact f16 (weights about 2^-30: e < 104)
+    keeps its matrices in the mxfp4 layout and stays bit-exact with the oracle."""
+    m = synth.llama(dim=64, n_layers=2, n_heads=4, n_kv_heads=2, ffn_dim=128, vocab=300, ctx=96, tied=False, seed=5,
+                    std=2.0 ** -30, stop_tokens=False)
+    path = tmp_path / "tiny-mxfp4.l3m"
+    synth.write(m, "mxfp4", "mxfp4", path)
+    want = OracleRun(oracle, path, PROMPT, 16)
+    _, toks, lg = gpu_run(path, PROMPT, 16)
+    assert toks == want.tokens
+    assert np.array_equal(lg.view(np.uint32), want.logits.view(np.uint32))
+
+
 def test_max_new_zero_gives_prompt_logits(gpu, oracle, models):
     path = models[("gqa", "q8_0")]
     m = l3m_b200.Model(path, force=True)
