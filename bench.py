@@ -15,6 +15,8 @@ l3m_generate call. tok/s counts forward passes, prompt included, as the referenc
              on_token), host wall clock around each call
   roofline   HBM: algorithmic bytes per launch (weights once per token + KV reads and writes) over
              the kernel's duration, against MEASURED_PEAKS.json
+  chain_bound  the second bound of this latency-bound kernel: the launch's dependent fp32 chain steps
+             (the reference's sequential sums, kept exact) x the measured cycles of one such step
   cpu_baseline  the reference itself (oracle/_ref/l3m bench, built from its sources) on this host's cores
 
 The L2 is flushed (a 256 MiB write) between timed steps. --impl reference times the reference's
@@ -115,6 +117,41 @@ def algorithmic_bytes(name, positions):
     w = synth.weight_bytes(name)
     kv = sum(2 * L * (p + 1) * kvd * 2 + 2 * L * kvd * 2 for p in range(positions))
     return positions * w + kv, positions
+
+
+def chain_steps(name, positions, n_prompt):
+    """Dependent fp32 steps on one launch's critical path (Llama family, the kernels' exact chains),
+    summed over its forward passes: per layer the attention norm's sum of squares (dim steps), the
+    qkv, wo, up/gate and down matvecs' chains over blocks (k/32 steps for quantised matrices, k for
+    bf16/f32), one score's chain (head_dim), the softmax's sequential sum and the V mix (pos + 1 each),
+    the ffn norm (dim); on every sampled position the final norm and the head's chain. Exchanges,
+    barriers and loads come on top: this is a floor, not a model of the kernel."""
+    shape, dtype, head_dtype, _ = synth.CONFIGS[name]
+    dim, ffn, L, hd = shape["dim"], shape["ffn_dim"], shape["n_layers"], shape["dim"] // shape["n_heads"]
+    mv = lambda dt, k: k if dt in ("bf16", "f32") else k // 32
+    per_layer = 2 * dim + 2 * mv(dtype, dim) + mv(dtype, dim) + mv(dtype, ffn) + hd
+    total = 0
+    for pos in range(positions):
+        total += L * (per_layer + 2 * (pos + 1))
+        if pos >= n_prompt - 1:
+            total += dim + mv(head_dtype, dim)
+    return total
+
+
+def chain_line(lib, name, positions, n_prompt, launch_s, clocks):
+    """The chain-latency bound beside the HBM roofline: chain_steps x the measured cycles of one
+    dependent fp32 step (l3m_chain_cycles_dev, timed here) at the median SM clock sampled during the
+    timed region; frac = that time / the launch's device time."""
+    cyc = C.c_double()
+    if lib.l3m_chain_cycles_dev(65536, C.byref(cyc)) != 0:
+        return {"unavailable": lib.l3m_cuda_error().decode()}
+    steps = chain_steps(name, positions, n_prompt)
+    mhz = clocks.get("sm_mhz") or clocks.get("sm_max_mhz") or 1965.0
+    bound_s = steps * cyc.value / (mhz * 1e6)
+    return {"steps_per_launch": steps, "cycles_per_step": round(cyc.value, 3), "sm_mhz": mhz, "bound_ms": round(bound_s * 1e3, 3),
+            "launch_ms": round(launch_s * 1e3, 3), "frac": round(bound_s / launch_s, 4),
+            "note": "dependent fp32 chain steps of one launch (norms, matvec block chains, attention score, softmax sum and V mix, "
+                    "head) x the measured latency of one step; exchanges and loads not counted"}
 
 
 def measured_peaks():
@@ -337,6 +374,7 @@ def bench_ours(a):
                      "traffic_note": traffic["note"] if traffic else "not measured for this config",
                      "peak_kind": peak_kind,
                      "algorithmic_bytes_per_launch": alg},
+        "chain_bound": chain_line(l3m_b200.lib(), name, per_launch_pos, len(prompt), launch_s, clk.summary()),
         "gpu_launches": a.steps,
         "clocks": clk.summary(),
         "ns_wait_per_token": round(float(np.mean(waits)), 1) if waits else None,

@@ -102,6 +102,10 @@ L3M_API int l3m_attend_dev(float *out, const float *q, const uint16_t *k, const 
 // reference's softmax, SiLU and sampler call, src/ops.c:45, 50; the kernels above use the same code).
 // x, y: device memory.
 L3M_API int l3m_expf_dev(const float *x, float *y, int n, void *stream);
+// Diagnostics: the SM cycles per step of a dependent fp32 fma chain (operands in registers), timed
+// on the current device over `steps` steps (64 .. 2^24) by one warp; synchronous. The decode's
+// chain-latency bound is its dependent steps per token times this.
+L3M_API int l3m_chain_cycles_dev(int steps, double *cycles_per_step);
 // The last CUDA error this library saw, as text ("" if none).
 L3M_API const char *l3m_cuda_error(void);
 

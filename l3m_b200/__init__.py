@@ -86,6 +86,7 @@ def lib():
         "l3m_unpack_dev": (i, [i, vp, vp, vp, i, i, vp]),
         "l3m_attend_dev": (i, [vp, vp, vp, vp, i, i, i, vp]),
         "l3m_expf_dev": (i, [vp, vp, i, vp]),
+        "l3m_chain_cycles_dev": (i, [i, C.POINTER(C.c_double)]),
         "l3m_cuda_error": (C.c_char_p, []),
         "l3m_write_packed": (i, [C.c_char_p, C.c_char_p]),
     }

@@ -622,6 +622,24 @@ extern "C" int l3m_expf_table(const uint32_t **table) {
     return 0;
 }
 
+// The latency of one step of a dependent fp32 chain (acc = fma(acc, a, b), operands in registers),
+// timed by the SM's cycle counter: the per-step cost of the sequential sums and fma chains that bound
+// the decode. The read of acc before the second stamp waits for the chain's last step.
+__device__ long long g_chain_cycles;
+__device__ float g_chain_sink;
+__global__ void chain_kernel(int steps, float a, float b) {
+    float acc = 0.0f;
+    const long long t0 = clock64();
+#pragma unroll 8
+    for (int i = 0; i < steps; i++) acc = __fmaf_rn(acc, a, b);
+    if (__float_as_uint(acc) == 0x7FC00001u) g_chain_sink = acc;
+    const long long t1 = clock64();
+    if (threadIdx.x == 0) {
+        g_chain_cycles = t1 - t0;
+        g_chain_sink = acc;
+    }
+}
+
 __global__ void expf_kernel(const float *__restrict__ x, float *__restrict__ y, int n, const uint32_t *etab) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) y[i] = l3m_expf_exact(x[i], etab);
 }
@@ -633,6 +651,19 @@ extern "C" int l3m_error_cuda(int e, const char *what) { return fail((cudaError_
 extern "C" {
 
 L3M_API const char *l3m_cuda_error(void) { return g_err; }
+
+L3M_API int l3m_chain_cycles_dev(int steps, double *cycles_per_step) {
+    if (steps < 64 || steps > (1 << 24) || !cycles_per_step) return fail_msg("l3m_chain_cycles_dev: bad arguments (steps in [64, 2^24])");
+    long long cyc = 0;
+    for (int run = 0; run < 2; run++) {                               // the second run, warm
+        chain_kernel<<<1, 32>>>(steps, 0.999f, 0.001f);
+        cudaError_t e = cudaDeviceSynchronize();
+        if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&cyc, g_chain_cycles, sizeof cyc);
+        if (e != cudaSuccess) return fail(e, "l3m_chain_cycles_dev");
+    }
+    *cycles_per_step = (double)cyc / steps;
+    return 0;
+}
 
 L3M_API int l3m_expf_dev(const float *x, float *y, int n, void *stream) {
     if (n < 0 || (n > 0 && (!x || !y))) return fail_msg("l3m_expf_dev: bad arguments");

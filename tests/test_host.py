@@ -75,6 +75,7 @@ def test_device_entries_refuse_bad_arguments(lib):
         (lambda: lib.l3m_sample_dev(p, 10, 1.0, None, p, p, None), "required"),
         (lambda: lib.l3m_expf_dev(None, p, 5, None), "bad arguments"),
         (lambda: lib.l3m_expf_dev(p, p, -1, None), "bad arguments"),
+        (lambda: lib.l3m_chain_cycles_dev(8, C.byref(C.c_double())), "bad arguments"),
     ]
     for call, text in cases:
         assert call() == -1
