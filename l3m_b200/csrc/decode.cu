@@ -81,7 +81,7 @@ __device__ __forceinline__ Smem carve(unsigned char *base, const DecodeArgs &a) 
     s.kvbuf = (uint16_t *)(base + a.sm_kvbuf);
     s.vtbuf = (uint16_t *)(base + a.sm_vt);
     s.scratch = (float2 *)(base + a.sm_scratch);
-    s.w = base + a.sm_w;
+    s.w = base + (blockIdx.x >= kClusterCtas ? a.sm_w_head : a.sm_w);
     s.wbar = (unsigned long long *)(base + a.sm_wbar);
     s.xbar = (unsigned long long *)(base + a.sm_xbar);
     s.prep.q8 = (int8_t *)(base + a.sm_q8);

@@ -135,6 +135,7 @@ struct DecodeArgs {
     int trace_cta[2];
     // shared memory layout, byte offsets
     int sm_x, sm_xb, sm_tmp, sm_q8, sm_scale, sm_sum, sm_xf, sm_y, sm_scores, sm_kv, sm_att, sm_red, sm_kvbuf, sm_vt, sm_scratch;
+    int sm_w_head;                      // a helper CTA's resident head tiles start here (it uses nothing after)
     int sm_wa, sm_wf, sm_wh, sm_rope;   // this layer's norm weights, the final norm, this position's RoPE row
     int sm_wab, sm_wfb, sm_whb;         // the same norms' LayerNorm biases
     int sm_layers;                      // a copy of layers[0 .. n_layers)

@@ -243,7 +243,8 @@ void widen_to_q8(int dtype, const uint8_t *src, uint8_t *dst, size_t ntiles, int
 // would read the rest from global memory, slower than unpacking nibbles from shared memory).
 struct Widen {
     bool on = false;
-    long cap_qkv_wo = 0, cap_rest = 0;   // staging bytes for qkv / wo, and for up(+gate) / down / the head
+    long cap_qkv_wo = 0, cap_rest = 0;   // staging bytes for qkv / wo, and for up(+gate) / down
+    long cap_head = 0;                   // a helper CTA's resident head tiles
     int head_ctas = 1;                   // the CTAs the head's tiles are split over
 };
 
@@ -361,7 +362,7 @@ void pack_streamed(const l3m_file *f, bool ref, const ShardRange &sr, int hd, St
     const l3m_tensor *head = l3m_file_tensor(f, (f->h->flags & L3M_F_TIED) ? "embed" : "lm_head");
     Rows rh;
     add_rows(rh, f, head, sr.v_lo * T, std::min(sr.v_hi * T, (int)head->shape[0]), ref);
-    out.off_head = pack_rows(s, rh, f, "head", out, !packed_ok, wide, wide.cap_rest, (tiles_of((int)rh.ptr.size()) + wide.head_ctas - 1) / wide.head_ctas, &out.dt_head);
+    out.off_head = pack_rows(s, rh, f, "head", out, !packed_ok, wide, wide.cap_head, (tiles_of((int)rh.ptr.size()) + wide.head_ctas - 1) / wide.head_ctas, &out.dt_head);
 }
 
 // The decode kernel's shared-memory layout for these sizes: every vector's offset in a, the scratch, the
@@ -373,6 +374,9 @@ int smem_layout(l3m::DecodeArgs &a, const LayoutSizes &z) {
     const int dim = z.dim, ffn = z.ffn, hd = z.hd, mx = std::max(dim, ffn), nb = (mx + 31) / 32, G = l3m::kClusterCtas;
     int off = 0;
     auto take = [&](int bytes) { int o2 = off; off = align16(off + bytes); return o2; };
+    // First what a helper CTA (the head alone) uses, so that its resident head tiles can start at
+    // sm_w_head: x, the norm's output and prepared activation, outputs, reductions, the final norm's
+    // weights, the layer table (every CTA copies it at entry), the staging barrier, the scratch.
     a.sm_x = take(dim * 4);
     a.sm_xb = take(mx * 4);
     a.sm_tmp = take(mx * 4);
@@ -380,25 +384,33 @@ int smem_layout(l3m::DecodeArgs &a, const LayoutSizes &z) {
     a.sm_scale = take(nb * 4);
     a.sm_sum = take(nb * 4);
     a.sm_xf = take(mx * 4);
+    a.sm_y = take(z.max_tiles * L3M_TILE * 4);
+    a.sm_red = take(64 * 4);
+    a.sm_wh = take(dim * 4);
+    a.sm_whb = take(z.ln ? dim * 4 : 0);
+    a.sm_layers = take(z.L * (int)sizeof(l3m::LayerDev));
+    a.sm_wbar = take(16);
+    // Scratch: the (scale product, dot) pairs of the largest per-CTA phase of a layer, so each runs in
+    // one pass (the head runs in several).
+    a.scratch_pairs = z.pairs;
+    a.sm_scratch = take(z.pairs * 8);
+    off = (off + 127) & ~127;
+    a.sm_w_head = off;
+    // Then what only the layer cluster uses.
     a.sm_pa_q8 = take(dim);                                            // the q8 exchanges' receive buffers
     a.sm_pa_scale = take((dim / 32 + 1) * 4);
     a.sm_pa_sum = take((dim / 32 + 1) * 4);
     a.sm_ph_q8 = take(ffn);
     a.sm_ph_scale = take((ffn / 32 + 1) * 4);
     a.sm_ph_sum = take((ffn / 32 + 1) * 4);
-    a.sm_y = take(z.max_tiles * L3M_TILE * 4);
     a.sm_scores = take(z.ctx * 4);
     a.sm_kv = take(2 * hd * 2);
     a.sm_att = take(hd * 4);
-    a.sm_red = take(64 * 4);
     a.sm_wa = take(dim * 4);
     a.sm_wf = take(dim * 4);
-    a.sm_wh = take(dim * 4);
     a.sm_wab = take(z.ln ? dim * 4 : 0);
     a.sm_wfb = take(z.ln ? dim * 4 : 0);
-    a.sm_whb = take(z.ln ? dim * 4 : 0);
     a.sm_rope = take(hd / 2 * 8);
-    a.sm_layers = take(z.L * (int)sizeof(l3m::LayerDev));
     a.attn_chunk = std::min(z.ctx, 256);
     a.vstride = z.vstride;
     a.sm_xq = take(z.n_qkv * 4);
@@ -407,12 +419,7 @@ int smem_layout(l3m::DecodeArgs &a, const LayoutSizes &z) {
     a.sm_xh = take(ffn * 4);
     a.sm_xd = take(dim * 4);
     a.sm_xt = take((4 + 16 * G) * 4);                                  // token, argmax slots, 3 sampling exchanges
-    a.sm_wbar = take(16);
     a.sm_xbar = take(5 * 8);
-    // Scratch: the (scale product, dot) pairs of the largest per-CTA phase of a layer, so each runs in
-    // one pass (the head runs in several).
-    a.scratch_pairs = z.pairs;
-    a.sm_scratch = take(z.pairs * 8);
     // The weight staging area takes the rest; the attention buffers are its first bytes.
     off = (off + 127) & ~127;
     a.sm_w = off;
@@ -472,6 +479,7 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
         wd.on = !getenv("L3M_NO_WIDEN");
         wd.cap_qkv_wo = std::max(0L, w_bytes - probe.w_extra);
         wd.cap_rest = std::max(0L, w_bytes);
+        wd.cap_head = std::max(0L, ((long)l3m_decode_smem_budget() - probe.sm_w_head) & ~127L);
         wd.head_ctas = GT > G && !m->cold ? GT - G : GT;
     }
     pack_streamed(f, ref, sr, hd, s, sw, wd);
@@ -651,7 +659,7 @@ bool build_gpu(l3m_model *m, Gpu &g, const l3m_opts &o) {
         d.st_up = fit(d.dt_up, dim, a.w_bytes);
         d.st_down = fit(d.dt_down, ffn, a.w_bytes);
     }
-    a.st_head = fit(dt_head, dim, a.w_bytes);
+    a.st_head = fit(dt_head, dim, (budget - a.sm_w_head) & ~127);     // a helper's: from sm_w_head on
     if (!cuda_ok(cudaMalloc(&g.layers, sizeof(l3m::LayerDev) * L), "layers")) return false;
     cudaMemcpy(g.layers, layers.data(), sizeof(l3m::LayerDev) * L, cudaMemcpyHostToDevice);
     a.layers = g.layers;
