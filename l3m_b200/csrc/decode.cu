@@ -1,14 +1,16 @@
 // The decode kernel: one launch runs a whole l3m_generate call (prompt feed and greedy sampling) on
-// one GPU as a single thread-block cluster of kClusterCtas CTAs. Replaces the reference's pinned
-// thread pool and its four barriers per layer (src/engine.c:230-281, src/pool.c:111-123).
+// one GPU: one thread-block cluster of kClusterCtas CTAs (cluster 0) runs the layers, and the other
+// clusters of the launch (the helpers, as many as the GPU holds) run the head. Replaces the
+// reference's pinned thread pool and its four barriers per layer (src/engine.c:230-281,
+// src/pool.c:111-123).
 //
 // Every CTA keeps the residual x in its shared memory. Each matrix is split into contiguous runs of
 // 16-row tiles over the CTAs (the reference's split over ranks, src/engine.c:88-91). A CTA writes
 // its slice of every produced vector straight into the shared memory of all CTAs of the cluster
 // (distributed shared memory) with st.async, each store completing its bytes on the receiver's
-// mbarrier for that exchange, so an exchange costs a few hundred nanoseconds and no global-memory
-// round trip (when some CTA has no qkv rows, hardware cluster barriers order the exchanges
-// instead). Per layer:
+// mbarrier for that exchange, so an exchange needs no global-memory round trip and no cluster
+// barrier (when some CTA has no qkv rows, hardware cluster barriers order the exchanges instead).
+// Per layer:
 //   Q  qkv CTAs:  rmsnorm, their tiles of the q/k/v rows                   -> qkv      exchange 1
 //   A  head CTAs: RoPE, KV row, attention (K/V copies started during Q)   -> attn     exchange 2
 //   B  wo CTAs:   matvec                                                  -> proj     exchange 3
@@ -16,15 +18,16 @@
 //   D  down CTAs: matvec                                                  -> down     exchange 5
 //   all:          x += down
 // After the last prompt position each position ends with the head matvec (logits kept for
-// l3m_logits) on every CTA of the launch, a per-CTA argmax, and the same global argmax in every CTA
-// of cluster 0, in CTA order. Each exchanged vector has one buffer: its next write comes after every
-// reader has finished with it. The quantised weight tiles of the next matvec phase are copied into
-// shared memory by the tensor memory accelerator while the current phase runs; each layer's norm
-// weights and RoPE row are copied into shared memory while the previous layer runs.
+// l3m_logits) on the helper clusters (on every CTA in cold mode), a per-CTA argmax posted as one
+// slot word, and the same global argmax in every CTA of cluster 0, in CTA order. Each exchanged
+// vector has one buffer: its next write comes after every reader has finished with it. The weight
+// tiles of the next matvec phase are copied into shared memory by the tensor memory accelerator
+// (bulk copies, this CTA's own memory) where no exchange is in flight; each layer's norm weights and
+// RoPE row are copied into shared memory while the previous layer runs.
 //
 // Waits. Cluster barriers are reached the same number of times by every CTA of the cluster. Every
-// other wait (an exchange's mbarrier, a weight copy's mbarrier, the head job flag and arrival count
-// in global memory) polls with a time limit; a wait that gives up records an error code and where it
+// other wait (an exchange's mbarrier, a weight copy's mbarrier, the head's x and slot words in
+// global memory) polls with a time limit; a wait that gives up records an error code and where it
 // was (CTA, position, layer, which wait) in the abort word, and every later wait of the launch stops
 // as soon as it sees that word set, so the launch ends at the next sampled position instead of
 // running every remaining wait to its limit. At entry every CTA checks that the launch has the shape
